@@ -1,0 +1,287 @@
+"""Serving benchmark: output tokens/s of the whole box on Llama-3-8B (bf16, TP = number of GPUs).
+
+Workload (synthetic, random-init weights of the architecture): a saturating request stream
+(arrival rate above the service rate, modelled as all requests queued at t = 0 and the queue
+refilled from the same seeded stream), prompts uniform in [128, 2048] tokens with ids uniform
+over the vocabulary, 256 output tokens per request, greedy sampling, EOS ignored, paged KV cache
+with block size 16 in bf16.
+
+One *step* is one ``LLMEngine.step()`` (one continuous-batching iteration: chunked prefill
+plus every running decode, sampling, H2D of the step's inputs from pinned memory and D2H of the
+sampled ids). Before the W warm-up steps the engine is filled (untimed) until its running set
+reaches ``max_num_seqs``; then exactly K steps are timed, bracketed by barrier + synchronize.
+
+Reported:
+  value      output tokens of the K steps / device time (sum over steps of the CUDA-event span of
+             each step's device work), max over ranks
+  e2e.value  the same tokens / host wall-clock time of the K public-API ``step()`` calls (includes
+             scheduling, host preparation, H2D and D2H), max over ranks
+
+Launch: ``python bench.py`` (1 GPU) or
+``python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "output tok/s (whole box, max over ranks) + p50 TTFT/TPOT, Llama-3-8B/70B TP"
+BASELINE_TOK_S = 95.0  # published Llama-3-8B FP8 decode tok/s on 1x B200 (kernel/blackwell README:96)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=300)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="llama-3-8b")
+    p.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the number)")
+    p.add_argument("--num-requests", type=int, default=1024)
+    p.add_argument("--prompt-min", type=int, default=128)
+    p.add_argument("--prompt-max", type=int, default=2048)
+    p.add_argument("--output-len", type=int, default=256)
+    p.add_argument("--max-num-seqs", type=int, default=256)
+    p.add_argument("--max-batched-tokens", type=int, default=8192)
+    p.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--no-fill", action="store_true")
+    return p.parse_args()
+
+
+def reference_unavailable(args):
+    print(json.dumps({
+        "impl": "reference",
+        "unavailable": "bhangun/gollek is a Java 25/Quarkus Maven project with no Python package (pip: "
+                       "'Neither setup.py nor pyproject.toml found'), no JDK/Maven on the box, and its CUDA "
+                       "kernels ship only as absent prebuilt .so files",
+        "n_gpus": args.gpus,
+    }))
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class Stream:
+    """Deterministic synthetic request stream (identical on every rank)."""
+
+    def __init__(self, vocab, pmin, pmax, out_len, seed=0):
+        self.rng = np.random.default_rng(seed)
+        self.vocab, self.pmin, self.pmax, self.out_len = vocab, pmin, pmax, out_len
+        self.n = 0
+
+    def next(self):
+        L = int(self.rng.integers(self.pmin, self.pmax + 1))
+        ids = self.rng.integers(0, self.vocab, size=L).tolist()
+        self.n += 1
+        return f"req-{self.n}", ids
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from gollek_b200 import ops
+    from gollek_b200.config import EngineConfig, preset
+    from gollek_b200.engine.engine import LLMEngine
+    from gollek_b200.engine.sequence import SamplingParams
+    from gollek_b200.parallel.dist import NcclComm, init_distributed
+    from gollek_b200.utils.timing import StepTimer
+
+    di = init_distributed(timeout_s=300)
+    if di.world_size != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={di.world_size}")
+    torch.cuda.set_device(di.local_rank)
+    mcfg = preset(args.model)
+    if args.layers:
+        mcfg.num_hidden_layers = args.layers
+    ec = EngineConfig(model=args.model, device="cuda", dtype="bfloat16", tensor_parallel_size=di.world_size,
+                      block_size=16, max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_batched_tokens,
+                      max_model_len=args.prompt_max + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
+                      enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm)
+    comm = NcclComm(di.rank, di.world_size) if di.world_size > 1 else None
+    eng = LLMEngine(ec, model_cfg=mcfg, comm=comm)
+    stream = Stream(mcfg.vocab_size, args.prompt_min, args.prompt_max, args.output_len)
+    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
+
+    def refill():
+        while len(eng.scheduler.waiting) < max(args.max_num_seqs, 64):
+            rid, ids = stream.next()
+            eng.add_request(rid, ids, SamplingParams(**vars(sp)))
+
+    for _ in range(args.num_requests):
+        rid, ids = stream.next()
+        eng.add_request(rid, ids, SamplingParams(**vars(sp)))
+    if not args.no_graphs:
+        eng.runner.capture_all()
+    # fill (untimed): ramp the running set to max_num_seqs
+    if not args.no_fill:
+        guard = 0
+        while len(eng.scheduler.running) < args.max_num_seqs and guard < 10000:
+            refill()
+            eng.step()
+            guard += 1
+    for _ in range(args.warmup):
+        refill()
+        eng.step()
+
+    timer = StepTimer()
+    eng.runner.timer = timer
+    eng.runner.h2d_bytes = eng.runner.d2h_bytes = 0
+    clocks = ClockSampler(di.local_rank)
+    tokens = 0
+    token_log = []  # (request_id, time) of tokens produced in the window
+    if di.world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ops.LAUNCHES.reset()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    t0 = time.perf_counter()
+    first_seen = {}
+    for _ in range(args.steps):
+        refill()
+        for sq in eng.scheduler.running:
+            if sq.scheduled_time is not None and sq.request_id not in first_seen:
+                first_seen[sq.request_id] = sq.scheduled_time
+        outs = eng.step()
+        for sq in eng.scheduler.running:
+            if sq.scheduled_time is not None and sq.request_id not in first_seen:
+                first_seen[sq.request_id] = sq.scheduled_time
+        tokens += len(outs)
+        now = time.perf_counter()
+        token_log.extend((o.request_id, now, len(o.output_token_ids)) for o in outs)
+    t1 = time.perf_counter()
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = ops.LAUNCHES.reset()
+    if di.world_size > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    window_ms = ev0.elapsed_time(ev1)
+    busy_ms = timer.total_ms()
+    host_ms = (t1 - t0) * 1e3
+    vals = torch.tensor([busy_ms, host_ms, window_ms], dtype=torch.float64, device="cuda")
+    if di.world_size > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    busy_ms, host_ms, window_ms = vals.tolist()
+
+    # latency metrics from in-window tokens (host timestamps of step completion)
+    per_req = {}
+    for rid, t, n in token_log:
+        per_req.setdefault(rid, []).append((t, n))
+    ttft, tpot = [], []
+    for rid, lst in per_req.items():
+        ts = [t for t, _ in lst]
+        if len(ts) >= 2:
+            tpot.append((ts[-1] - ts[0]) / (len(ts) - 1))
+        if lst[0][1] == 1:  # first output token landed in the window: service TTFT from admission
+            s = first_seen.get(rid)
+            if s is not None:
+                ttft.append(lst[0][0] - s)
+
+    value = tokens / (busy_ms / 1e3)
+    e2e = tokens / (host_ms / 1e3)
+    steps = args.steps
+    h2d = eng.runner.h2d_bytes / steps
+    d2h = eng.runner.d2h_bytes / steps
+    res = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "output tokens/s",
+        "n_gpus": di.world_size,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(busy_ms / steps, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": round(value / BASELINE_TOK_S, 2),
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform random token ids)",
+        "impl": "ours",
+        "config": {
+            "model": "Llama-3-8B" + (f" ({mcfg.num_hidden_layers} layers: INVALID debug run)" if args.layers else ""),
+            "global_batch": args.max_num_seqs,
+            "seq_len": f"prompt U[{args.prompt_min},{args.prompt_max}] + {args.output_len} out",
+            "parallelism": f"tp{di.world_size}",
+            "requests": f"saturating stream, first {args.num_requests} queued at t0, refilled",
+            "max_num_batched_tokens": args.max_batched_tokens,
+            "kv_block_size": 16,
+            "l2": "inputs larger than L2 (16 GB of weights streamed per step)",
+            "comm": args.comm if di.world_size > 1 else "none",
+            "timing": "value: sum of per-step CUDA-event spans (first H2D .. D2H) over K engine steps; "
+                      "e2e: host wall clock of the same K LLMEngine.step() calls; both max over ranks",
+        },
+        "window_ms": round(window_ms, 2),
+        "ttft_p50_ms": round(1e3 * float(np.median(ttft)), 2) if ttft else None,
+        "tpot_p50_ms": round(1e3 * float(np.median(tpot)), 2) if tpot else None,
+        "e2e": {"value": round(e2e, 2), "unit": "output tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if di.rank == 0:
+        print(json.dumps(res))
+    eng.runner.graphs.clear()
+    if di.world_size > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

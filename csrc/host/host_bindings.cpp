@@ -1,0 +1,19 @@
+// Python bindings of the host C++ runtime (module gollek_b200_host).
+#include <torch/extension.h>
+
+torch::Tensor quantize_q8_0(torch::Tensor x);
+torch::Tensor dequantize_q8_0(torch::Tensor raw, int64_t n);
+torch::Tensor quantize_q4_k(torch::Tensor x);
+torch::Tensor dequantize_q4_k(torch::Tensor raw, int64_t n);
+void register_block_allocator(pybind11::module& m);
+void register_forelen(pybind11::module& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "gollek_b200 host runtime";
+  m.def("quantize_q8_0", &quantize_q8_0);
+  m.def("dequantize_q8_0", &dequantize_q8_0);
+  m.def("quantize_q4_k", &quantize_q4_k);
+  m.def("dequantize_q4_k", &dequantize_q4_k);
+  register_block_allocator(m);
+  register_forelen(m);
+}

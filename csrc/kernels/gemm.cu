@@ -1,0 +1,362 @@
+// K5/K8: bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   C[M, N'] = epilogue( A[M, K] · B[N, K]^T )      A, B bf16 K-major (nn.Linear layout), fp32 accumulate
+//
+// Persistent, warp-specialised CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: one elected lane streams 128x64 A tiles and BNx64 B tiles
+//               (128-byte swizzle) into a STAGES-deep shared-memory ring (mbarrier tx counts).
+//   warp 1      MMA issuer: one elected lane issues tcgen05.mma (M=128, N=BN, K=16) into a
+//               double-buffered TMEM accumulator (2 x BN fp32 columns) and releases smem
+//               stages / publishes finished accumulators with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from the TMEM lane quarter the warp
+//               may access, apply the fused epilogue, store bf16 to global. Runs concurrently
+//               with the next tile's main loop (the other TMEM buffer).
+// Fused epilogues: none, +residual (o_proj / down_proj residual add), SwiGLU
+// (gate/up rows interleaved in groups of 64 so one tile holds matching gate and up columns;
+// output width N/2).
+//
+// Reference ops replaced: gollek_cuda_matmul / gollek_blackwell_matmul
+// (kernel/cuda/gollek-kernel-cuda/…/cuda/binding/CudaBinding.java:59,282-288) and silu_ffn
+// (…/CudaBinding.java:64,390-395), CPU math CudaCpuFallback.java:61-117,261-290.
+//
+// Every mbarrier wait is bounded (globaltimer deadline); on timeout the CTA records a status bit,
+// stops issuing, drains its own in-flight copies/MMAs (bounded) and frees its TMEM before returning.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "../common/common.cuh"
+#include "../common/tma_host.h"
+
+using namespace gollek;
+
+namespace {
+
+enum Epi : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2 };
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+};
+
+GOLLEK_DEVICE uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: no legitimate wait inside one GEMM comes close
+
+// Bounded, abortable mbarrier wait. Returns false on timeout (status recorded) or abort.
+GOLLEK_DEVICE bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t* status, volatile int* abort_flag) {
+  for (int i = 0; i < 256; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      report_status(status, kStatusMbarTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+// Drain wait used only on the abort path (no abort check, still bounded).
+GOLLEK_DEVICE void drain_bar(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) break;
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
+                     int M, int N, int K, uint32_t* status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;   // [2]
+  uint64_t* tempty = tfull + 2;       // [2]
+  uint64_t* done_bar = tempty + 2;    // [1] abort-path drain of the MMA pipe
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* consumed = abort_flag + 1;  // k-blocks consumed by the MMA warp (abort drain)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+  constexpr uint32_t idesc = make_idesc_bf16(Cfg::BM, BN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    *consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * Cfg::BM, n0 = (tile / num_m) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(&empty[stage], phase ^ 1, status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, kb * Cfg::BK, m0, &full[stage]);
+          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, kb * Cfg::BK, n0, &full[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // wait (bounded) for our own loads still in flight before the CTA may exit
+        for (int i = max(*consumed, issued - STAGES); i < issued; ++i)
+          drain_bar(&full[i % STAGES], (i / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      int used = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_bar(&tempty[acc], acc_phase ^ 1, status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!wait_bar(&full[stage], phase, status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tcgen05_fence_after();
+          const uint64_t a_desc = make_smem_desc_sw128(smem_u32(sA + stage * Cfg::A_BYTES));
+          const uint64_t b_desc = make_smem_desc_sw128(smem_u32(sB + stage * Cfg::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzled row = +2 in the encoded address
+            umma_f16_ss(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          *consumed = ++used;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        umma_commit(done_bar);
+        drain_bar(done_bar, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int lg = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!wait_bar(&tfull[acc], acc_phase, status, abort_flag)) break;
+      tcgen05_fence_after();
+      const int m0 = (tile % num_m) * Cfg::BM, n0 = (tile / num_m) * BN;
+      const int row = m0 + lg * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * BN;
+      if constexpr (EPI == kEpiSwiglu) {
+        const int out_n = N / 2;
+#pragma unroll 1
+        for (int p = 0; p < BN / 128; ++p) {
+#pragma unroll 1
+          for (int h = 0; h < 64; h += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(tbase + p * 128 + h, g);
+            tmem_ld_32x32b_x32(tbase + p * 128 + 64 + h, u);
+            tmem_ld_wait();
+            const int col = n0 / 2 + p * 64 + h;
+            if (row < M) {
+              __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (col + 8 * j + 8 <= out_n) {
+                  float v[8];
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    v[e] = silu(__uint_as_float(g[8 * j + e])) * __uint_as_float(u[8 * j + e]);
+                  *reinterpret_cast<uint4*>(dst + 8 * j) = float_to_bf16x8(v);
+                }
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (row < M) {
+            __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (col + 8 * j + 8 <= N) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[8 * j + e]);
+                if constexpr (EPI == kEpiResidual) {
+                  float rr[8];
+                  bf16x8_to_float(*reinterpret_cast<const uint4*>(R + (int64_t)row * ldr + col + 8 * j), rr);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) v[e] += rr[e];
+                }
+                *reinterpret_cast<uint4*>(dst + 8 * j) = float_to_bf16x8(v);
+              }
+            }
+          }
+        }
+      }
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tcgen05_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN, int EPI>
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const torch::Tensor* res,
+                 uint32_t* status, int grid_limit) {
+  using Cfg = GemmCfg<BN>;
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, a.stride(0), Cfg::BM,
+                                Cfg::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, b.stride(0), BN, Cfg::BK,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = gemm_bf16_kernel<BN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_set = true;
+  }
+  const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
+  int grid = std::min(tiles, num_sms());
+  if (grid_limit > 0) grid = std::min(grid, grid_limit);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  kern<<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+                                         res ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr,
+                                         res ? res->stride(0) : 0, M, N, K, status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int pick_bn(int M, int N, int epi) {
+  const int num_m = (M + 127) / 128;
+  const int sms = num_sms();
+  if (epi == kEpiSwiglu) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
+  if (num_m * ((N + 255) / 256) >= sms) return 256;
+  if (num_m * ((N + 127) / 128) >= sms / 2) return 128;
+  return 64;
+}
+
+}  // namespace
+
+// out[M, N] (or [M, N/2] for SwiGLU) = epi(a[M, K] @ b[N, K]^T). bn = 0 picks the tile width.
+void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
+                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
+              "gemm: bf16 tensors");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: shape mismatch");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: K-major operands");
+  TORCH_CHECK(a.size(1) % 8 == 0, "gemm: K must be a multiple of 8");
+  const int M = a.size(0), N = b.size(0);
+  if (M == 0) return;
+  TORCH_CHECK(out.stride(0) % 8 == 0, "gemm: output row pitch must keep 16-byte alignment");
+  if (epi == kEpiSwiglu) {
+    TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "gemm swiglu: N must be a multiple of 128, out [M, N/2]");
+  } else {
+    TORCH_CHECK(out.size(1) == N && N % 8 == 0, "gemm: out [M, N] with N % 8 == 0");
+  }
+  const torch::Tensor* res = nullptr;
+  if (epi == kEpiResidual) {
+    TORCH_CHECK(residual.has_value() && residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
+                    residual->stride(0) % 8 == 0,
+                "gemm residual: bf16 row-major residual required");
+    res = &residual.value();
+  }
+  uint32_t* st = status.has_value() ? reinterpret_cast<uint32_t*>(status->data_ptr()) : nullptr;
+  if (bn == 0) bn = pick_bn(M, N, (int)epi);
+  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  const int gl = (int)grid_limit;
+#define GOLLEK_GEMM_CASE(BNV, EPIV) \
+  if (bn == BNV && epi == EPIV) return launch_gemm<BNV, EPIV>(a, b, out, res, st, gl);
+  GOLLEK_GEMM_CASE(256, kEpiNone)
+  GOLLEK_GEMM_CASE(128, kEpiNone)
+  GOLLEK_GEMM_CASE(64, kEpiNone)
+  GOLLEK_GEMM_CASE(256, kEpiResidual)
+  GOLLEK_GEMM_CASE(128, kEpiResidual)
+  GOLLEK_GEMM_CASE(64, kEpiResidual)
+  GOLLEK_GEMM_CASE(256, kEpiSwiglu)
+  GOLLEK_GEMM_CASE(128, kEpiSwiglu)
+#undef GOLLEK_GEMM_CASE
+  TORCH_CHECK(false, "gemm: unsupported tile width ", bn, " / epilogue ", epi);
+}

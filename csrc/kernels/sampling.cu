@@ -1,0 +1,304 @@
+// K11: batched token sampling (sm_100a), one CTA per row, no sort.
+//
+//   argmax            greedy fast path (ties -> lowest token id)
+//   apply_penalties   repetition (HF divide/multiply) over every listed token, frequency (x count)
+//                     and presence (if count > 0) over generated ones; (row, token, count) triples
+//   sample            temperature -> top-k (radix select of the k-th largest logit) -> min-p
+//                     (closed-form threshold) -> top-p (radix search of the probability-mass
+//                     threshold among survivors) -> exponential race (Gumbel-max) with a
+//                     counter-based hash RNG, so the draw is reproducible from (seed, step).
+//
+// Reference sampler order: runner/safetensor/gollek-safetensor-engine/…/generation/TokenSampler.java:62-208
+// and the llama.cpp chain in runner/llamacpp/gollek-runner-llamacpp/…/LlamaHandles.java:174-203.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "../common/common.cuh"
+
+using namespace gollek;
+
+namespace {
+
+constexpr int kSampThreads = 1024;
+
+template <typename T>
+GOLLEK_DEVICE float to_f(T v);
+template <>
+GOLLEK_DEVICE float to_f<float>(float v) { return v; }
+template <>
+GOLLEK_DEVICE float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+GOLLEK_DEVICE uint32_t ord_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// 32-bit integer hash (xor-shift-multiply finaliser, constants 0x7feb352d / 0x846ca68b).
+GOLLEK_DEVICE uint32_t hash32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+struct ArgMax {
+  float v;
+  int i;
+};
+GOLLEK_DEVICE ArgMax better(ArgMax a, ArgMax b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+GOLLEK_DEVICE ArgMax warp_argmax(ArgMax a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax b;
+    b.v = __shfl_xor_sync(0xffffffffu, a.v, o);
+    b.i = __shfl_xor_sync(0xffffffffu, a.i, o);
+    a = better(a, b);
+  }
+  return a;
+}
+GOLLEK_DEVICE ArgMax block_argmax(ArgMax a, ArgMax* sh) {
+  a = warp_argmax(a);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = a;
+  __syncthreads();
+  if (w == 0) {
+    ArgMax b = (l < (int)(blockDim.x >> 5)) ? sh[l] : ArgMax{-INFINITY, 0x7fffffff};
+    b = warp_argmax(b);
+    if (l == 0) sh[0] = b;
+  }
+  __syncthreads();
+  ArgMax r = sh[0];
+  __syncthreads();
+  return r;
+}
+GOLLEK_DEVICE float block_sum(float v, float* sh) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    float b = (l < (int)(blockDim.x >> 5)) ? sh[l] : 0.f;
+    b = warp_sum(b);
+    if (l == 0) sh[0] = b;
+  }
+  __syncthreads();
+  float r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) argmax_kernel(int64_t* __restrict__ out, const T* __restrict__ logits,
+                                                              int V, int64_t stride) {
+  __shared__ ArgMax sh[32];
+  const T* row = logits + (int64_t)blockIdx.x * stride;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{to_f(row[i]), i});
+  best = block_argmax(best, sh);
+  if (threadIdx.x == 0) out[blockIdx.x] = best.i == 0x7fffffff ? 0 : best.i;
+}
+
+// triples: [n, 3] int32 (row, token, count); logits updated in place (fp32).
+__global__ void penalties_kernel(float* __restrict__ logits, int64_t stride, const int* __restrict__ triples, int n,
+                                 const float* __restrict__ rep, const float* __restrict__ freq,
+                                 const float* __restrict__ pres) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int r = triples[3 * i], tok = triples[3 * i + 1], cnt = triples[3 * i + 2];
+  float* p = logits + (int64_t)r * stride + tok;
+  float v = *p;
+  const float rp = rep[r];
+  v = v > 0.f ? v / rp : v * rp;
+  v -= freq[r] * (float)cnt + (cnt > 0 ? pres[r] : 0.f);
+  *p = v;
+}
+
+// Radix select: largest key K such that #{keys >= K} >= k (i.e. the k-th largest key).
+template <typename T>
+GOLLEK_DEVICE uint32_t radix_kth_largest(const T* row, int V, int k, uint32_t* hist, uint32_t* sh_u) {
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const uint32_t key = ord_key(to_f(row[i]));
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, bin = 0;
+      for (bin = 255; bin >= 0; --bin) {
+        if (cum + (int)hist[bin] >= remaining) break;
+        cum += hist[bin];
+      }
+      if (bin < 0) bin = 0;
+      sh_u[0] = (uint32_t)bin;
+      sh_u[1] = (uint32_t)(remaining - cum);
+    }
+    __syncthreads();
+    prefix |= sh_u[0] << shift;
+    mask |= 255u << shift;
+    remaining = (int)sh_u[1];
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Radix search of the mass threshold: largest key K such that sum_{key >= K} w >= target,
+// over elements with key >= floor_key, where w = exp2((x - m) * inv_t_log2).
+template <typename T>
+GOLLEK_DEVICE uint32_t radix_mass_threshold(const T* row, int V, uint32_t floor_key, float m, float inv_t_log2,
+                                            float target, float* hist_f, uint32_t* sh_u, float* sh_f) {
+  uint32_t prefix = 0, mask = 0;
+  float above = 0.f;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist_f[i] = 0.f;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float x = to_f(row[i]);
+      const uint32_t key = ord_key(x);
+      if (key >= floor_key && (key & mask) == prefix)
+        atomicAdd(&hist_f[(key >> shift) & 255u], exp2f((x - m) * inv_t_log2));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float cum = above;
+      int bin;
+      for (bin = 255; bin >= 0; --bin) {
+        if (cum + hist_f[bin] >= target) break;
+        cum += hist_f[bin];
+      }
+      if (bin < 0) bin = 0;
+      sh_u[0] = (uint32_t)bin;
+      sh_f[0] = cum;
+    }
+    __syncthreads();
+    prefix |= sh_u[0] << shift;
+    mask |= 255u << shift;
+    above = sh_f[0];
+    __syncthreads();
+  }
+  return prefix;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSampThreads) sample_kernel(int64_t* __restrict__ out, const T* __restrict__ logits,
+                                                              int V, int64_t stride, const float* __restrict__ temps,
+                                                              const int* __restrict__ top_ks,
+                                                              const float* __restrict__ top_ps,
+                                                              const float* __restrict__ min_ps,
+                                                              const int64_t* __restrict__ seeds,
+                                                              const int64_t* __restrict__ offsets) {
+  __shared__ ArgMax sha[32];
+  __shared__ float shf[33];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh_u[2];
+  const int b = blockIdx.x;
+  const T* row = logits + (int64_t)b * stride;
+  const float t = temps[b];
+  // 1) max
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{to_f(row[i]), i});
+  best = block_argmax(best, sha);
+  if (t <= 0.f) {
+    if (threadIdx.x == 0) out[b] = best.i == 0x7fffffff ? 0 : best.i;
+    return;
+  }
+  const float m = best.v;
+  const float inv_t_log2 = 1.4426950408889634f / t;
+  uint32_t floor_key = 0;
+  // 2) top-k
+  const int k = top_ks[b];
+  if (k > 0 && k < V) floor_key = max(floor_key, radix_kth_largest(row, V, k, hist, sh_u));
+  // 3) min-p: p_i >= min_p * p_max  <=>  x_i >= m + t * ln(min_p)
+  const float mp = min_ps[b];
+  if (mp > 0.f) floor_key = max(floor_key, ord_key(m + t * __logf(mp)));
+  // 4) top-p over the survivors (renormalised)
+  const float tp = top_ps[b];
+  if (tp < 1.f) {
+    float z = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float x = to_f(row[i]);
+      if (ord_key(x) >= floor_key) z += exp2f((x - m) * inv_t_log2);
+    }
+    z = block_sum(z, shf);
+    floor_key = max(floor_key, radix_mass_threshold(row, V, floor_key, m, inv_t_log2, tp * z,
+                                                    reinterpret_cast<float*>(hist), sh_u, shf));
+  }
+  // 5) exponential race among survivors: argmax x/t + Gumbel(u)
+  const uint32_t seed_mix = hash32((uint32_t)seeds[b] ^ hash32((uint32_t)offsets[b] + 0x9E3779B9u));
+  ArgMax pick{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float x = to_f(row[i]);
+    if (ord_key(x) < floor_key) continue;
+    const uint32_t h = hash32(seed_mix ^ hash32((uint32_t)i));
+    const float u = ((float)(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
+    const float g = -__logf(-__logf(u));
+    pick = better(pick, ArgMax{(x - m) / t + g, i});
+  }
+  pick = block_argmax(pick, sha);
+  if (threadIdx.x == 0) out[b] = pick.i == 0x7fffffff ? best.i : pick.i;
+}
+
+}  // namespace
+
+void argmax_out(torch::Tensor out, torch::Tensor logits) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "argmax: [B, V] logits");
+  TORCH_CHECK(out.scalar_type() == at::kLong, "argmax: int64 output");
+  const int B = logits.size(0), V = logits.size(1);
+  if (B == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (logits.scalar_type() == at::kFloat)
+    argmax_kernel<float><<<B, kSampThreads, 0, stream>>>(out.data_ptr<int64_t>(), logits.data_ptr<float>(), V,
+                                                         logits.stride(0));
+  else if (logits.scalar_type() == at::kBFloat16)
+    argmax_kernel<__nv_bfloat16><<<B, kSampThreads, 0, stream>>>(
+        out.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, logits.stride(0));
+  else
+    TORCH_CHECK(false, "argmax: fp32 or bf16 logits");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void apply_penalties_(torch::Tensor logits, torch::Tensor triples, torch::Tensor rep, torch::Tensor freq,
+                      torch::Tensor pres) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "penalties: fp32 logits");
+  TORCH_CHECK(triples.scalar_type() == at::kInt && triples.is_contiguous(), "penalties: int32 triples");
+  const int n = triples.size(0);
+  if (n == 0) return;
+  penalties_kernel<<<(n + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), triples.data_ptr<int>(), n, rep.data_ptr<float>(),
+      freq.data_ptr<float>(), pres.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sample_out(torch::Tensor out, torch::Tensor logits, torch::Tensor temps, torch::Tensor top_ks,
+                torch::Tensor top_ps, torch::Tensor min_ps, torch::Tensor seeds, torch::Tensor offsets) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "sample: [B, V] logits");
+  TORCH_CHECK(temps.scalar_type() == at::kFloat && top_ps.scalar_type() == at::kFloat &&
+                  min_ps.scalar_type() == at::kFloat && top_ks.scalar_type() == at::kInt &&
+                  seeds.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong,
+              "sample: parameter dtypes");
+  const int B = logits.size(0), V = logits.size(1);
+  if (B == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+#define GOLLEK_SAMPLE_ARGS                                                                                  \
+  out.data_ptr<int64_t>(), lp, V, logits.stride(0), temps.data_ptr<float>(), top_ks.data_ptr<int>(),      \
+      top_ps.data_ptr<float>(), min_ps.data_ptr<float>(), seeds.data_ptr<int64_t>(), offsets.data_ptr<int64_t>()
+  if (logits.scalar_type() == at::kFloat) {
+    const float* lp = logits.data_ptr<float>();
+    sample_kernel<float><<<B, kSampThreads, 0, stream>>>(GOLLEK_SAMPLE_ARGS);
+  } else if (logits.scalar_type() == at::kBFloat16) {
+    const __nv_bfloat16* lp = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+    sample_kernel<__nv_bfloat16><<<B, kSampThreads, 0, stream>>>(GOLLEK_SAMPLE_ARGS);
+  } else {
+    TORCH_CHECK(false, "sample: fp32 or bf16 logits");
+  }
+#undef GOLLEK_SAMPLE_ARGS
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,233 @@
+"""The serving engine: request intake → continuous-batching steps → outputs.
+
+``LLMEngine`` is the synchronous core (``add_request`` / ``step`` / ``generate``); it owns the
+model shard, the paged KV pool, the scheduler and the model runner. ``LLM`` is the
+user-facing convenience wrapper (``LLM("llama-3-8b").generate(prompts, params)``).
+
+Plays the role of the reference's engine stack (inference/gollek-engine/…/engine/inference/
+PlatformInferenceService.java:74-103 → DefaultInferenceEngine.java:94-143 →
+DefaultInferenceOrchestrator.java:122-200) together with its runtime continuous batcher
+(inference/gollek-runtime-inference/…/batch/ContinuousBatchScheduler.java:383-468) and the
+llama.cpp runner's decode loop (runner/llamacpp/gollek-runner-llamacpp/…/InferenceLogicExecutor.java:105-149).
+"""
+from __future__ import annotations
+
+import os
+import time
+import uuid
+from typing import Callable, Dict, Iterable, List, Optional, Sequence as Seq, Union
+
+import torch
+
+from ..config import EngineConfig, ModelConfig, PRESETS, preset
+from ..models.llama import LlamaModel, TPComm
+from ..native import host_ext
+from .kv_cache import KVCacheManager, allocate_kv_cache, num_blocks_from_memory
+from .model_runner import ModelRunner
+from .scheduler import Scheduler
+from .sequence import RequestOutput, SamplingParams, Sequence, SeqStatus
+from ..utils.metrics import EngineMetrics
+
+
+def _dtype(name: str) -> torch.dtype:
+    return {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16, "float32": torch.float32,
+            "fp32": torch.float32, "float16": torch.float16}[name]
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, model_cfg: Optional[ModelConfig] = None,
+                 weights: Optional[Callable[[str], torch.Tensor]] = None, comm: Optional[TPComm] = None,
+                 tokenizer=None, num_blocks: Optional[int] = None):
+        self.cfg = cfg
+        self.comm = comm or TPComm()
+        dev = cfg.device
+        if dev == "cuda":
+            dev = f"cuda:{torch.cuda.current_device()}" if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(dev)
+        self.dtype = _dtype(cfg.dtype) if self.device.type == "cuda" else torch.float32
+        self.tokenizer = tokenizer
+        # ---- model
+        if model_cfg is None:
+            model_cfg, weights, tok = load_model_source(cfg.model)
+            self.tokenizer = self.tokenizer or tok
+        self.model_cfg = model_cfg
+        self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm)
+        if weights is None:
+            self.model.init_random(cfg.seed)
+        else:
+            self.model.load_weights(weights)
+        # ---- KV cache
+        bpb = self.model.kv_bytes_per_block(cfg.block_size)
+        nb = num_blocks or cfg.num_gpu_blocks
+        if nb is None:
+            if self.device.type == "cuda":
+                nb = num_blocks_from_memory(bpb, self.model.weight_bytes(), self.device, cfg.gpu_memory_utilization)
+            else:
+                nb = 1024
+        if self.comm.size > 1 and self.device.type == "cuda":
+            t = torch.tensor([nb], device=self.device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            nb = int(t)
+        self.num_blocks = nb
+        self.kv_cache = allocate_kv_cache(self.model.kv_cache_shape(nb, cfg.block_size), self.dtype, self.device)
+        self.kv = KVCacheManager(nb, cfg.block_size, cfg.enable_prefix_caching)
+        predictor = None
+        if cfg.scheduling_policy == "wait":
+            predictor = host_ext().LengthPredictor(64, 1.0, float(cfg.max_model_len), 0.05, 8)
+        self.scheduler = Scheduler(cfg, self.kv, predictor)
+        self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
+        self.seqs: Dict[str, Sequence] = {}
+        self.metrics = EngineMetrics()
+        self.eos_token_id = model_cfg.eos_token_id
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, request_id: Optional[str], prompt: Union[str, List[int]],
+                    params: Optional[SamplingParams] = None, lora_id: int = 0,
+                    arrival_time: Optional[float] = None, priority: int = 0) -> str:
+        request_id = request_id or uuid.uuid4().hex
+        if request_id in self.seqs:
+            raise ValueError(f"duplicate request id {request_id}")
+        params = (params or SamplingParams()).validate()
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise ValueError("text prompt given but the model has no tokenizer")
+            ids = self.tokenizer.encode(prompt)
+        else:
+            ids = list(prompt)
+        if not ids:
+            raise ValueError("empty prompt")
+        if max(ids) >= self.model_cfg.vocab_size or min(ids) < 0:
+            raise ValueError("prompt token id out of range")
+        room = self.cfg.max_model_len - len(ids)
+        if room < 1:
+            raise ValueError("prompt too long for max_model_len")
+        params.max_tokens = min(params.max_tokens, room)
+        seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
+        self.scheduler.add(seq)
+        self.seqs[request_id] = seq
+        self.metrics.on_arrival()
+        return request_id
+
+    def abort_request(self, request_id: str) -> bool:
+        seq = self.scheduler.abort(request_id)
+        self.seqs.pop(request_id, None)
+        return seq is not None
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ------------------------------------------------------------------ stepping
+    def _check_stop(self, seq: Sequence, tok: int) -> Optional[SeqStatus]:
+        p = seq.params
+        n_out = len(seq.output_token_ids)
+        if n_out >= p.min_tokens:
+            if not p.ignore_eos and tok == self.eos_token_id:
+                seq.stop_reason = tok
+                return SeqStatus.FINISHED_STOPPED
+            if tok in p.stop_token_ids:
+                seq.stop_reason = tok
+                return SeqStatus.FINISHED_STOPPED
+            if p.stop and self.tokenizer is not None:
+                seq.output_text = self.tokenizer.decode(seq.output_token_ids)
+                for s in p.stop:
+                    idx = seq.output_text.find(s)
+                    if idx >= 0:
+                        seq.output_text = seq.output_text[:idx]
+                        seq.stop_reason = s
+                        return SeqStatus.FINISHED_STOPPED
+        if n_out >= p.max_tokens or seq.num_tokens >= self.cfg.max_model_len:
+            return SeqStatus.FINISHED_LENGTH
+        return None
+
+    def step(self) -> List[RequestOutput]:
+        """One scheduler iteration: schedule, run the model, append tokens, retire finished."""
+        sched = self.scheduler.schedule()
+        if sched.empty:
+            return []
+        t0 = time.perf_counter()
+        sampled = self.runner.execute(sched)
+        now = time.perf_counter()
+        outputs: List[RequestOutput] = []
+        k = 0
+        n_new = 0
+        for c in sched.chunks:
+            seq = c.seq
+            seq.num_computed_tokens = c.start + c.num_tokens
+            self.kv.commit_full_blocks(seq)
+            if not c.sample:
+                continue
+            tok = int(sampled[k])
+            k += 1
+            seq.output_token_ids.append(tok)
+            seq.token_times.append(now)
+            n_new += 1
+            if seq.first_token_time is None:
+                seq.first_token_time = now
+            status = self._check_stop(seq, tok)
+            finished = status is not None
+            if finished:
+                seq.finish_time = now
+                self.scheduler.finish(seq, status)
+                self.seqs.pop(seq.request_id, None)
+                self.metrics.on_finish(seq)
+            text = ""
+            if self.tokenizer is not None and finished:
+                text = seq.output_text or self.tokenizer.decode(seq.output_token_ids)
+            outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, [tok],
+                                         finished, status.value if status else None, text))
+        self.metrics.on_step(now - t0, sched.num_tokens, n_new, len(self.scheduler.running),
+                             len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
+        return outputs
+
+    def generate(self, prompts: Seq[Union[str, List[int]]], params: Union[SamplingParams, List[SamplingParams], None] = None,
+                 lora_ids: Optional[List[int]] = None) -> List[RequestOutput]:
+        ids = []
+        for i, p in enumerate(prompts):
+            sp = params[i] if isinstance(params, list) else (params or SamplingParams())
+            sp = SamplingParams(**vars(sp))
+            ids.append(self.add_request(f"gen-{uuid.uuid4().hex[:8]}-{i}", p, sp,
+                                        lora_id=lora_ids[i] if lora_ids else 0))
+        final: Dict[str, RequestOutput] = {}
+        while self.has_unfinished():
+            for o in self.step():
+                if o.finished:
+                    final[o.request_id] = o
+        return [final[i] for i in ids]
+
+
+def load_model_source(source: str):
+    """Resolve a preset name, a safetensors checkpoint (file or directory) or a GGUF file.
+
+    Returns (ModelConfig, weight getter or None for random init, tokenizer or None).
+    """
+    from ..loaders.safetensors import SafetensorsCheckpoint
+    from ..utils.tokenizer import load_tokenizer
+    if source in PRESETS:
+        from ..utils.tokenizer import ByteTokenizer
+        cfg = preset(source)
+        return cfg, None, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id)
+    if source.endswith(".gguf"):
+        from ..loaders.gguf import load_llama_gguf
+        cfg, w, f = load_llama_gguf(source, torch.float32)
+        from ..utils.tokenizer import GGUFTokenizer
+        tok = GGUFTokenizer.from_metadata(f.metadata)
+        return cfg, w.__getitem__, tok
+    if os.path.isdir(source) or source.endswith(".safetensors"):
+        d = source if os.path.isdir(source) else os.path.dirname(source)
+        import json
+        with open(os.path.join(d, "config.json")) as fh:
+            cfg = ModelConfig.from_hf(json.load(fh))
+        ck = SafetensorsCheckpoint(source)
+        return cfg, ck.get, load_tokenizer(d)
+    raise ValueError(f"unknown model source {source!r}")
+
+
+class LLM:
+    """Offline convenience API: ``LLM(model).generate(prompts, SamplingParams(...))``."""
+
+    def __init__(self, model: str = "tiny-llama", **kwargs):
+        cfg = EngineConfig.load(**{"model": model, **kwargs})
+        self.engine = LLMEngine(cfg)
+
+    def generate(self, prompts, params: Optional[SamplingParams] = None, lora_ids=None) -> List[RequestOutput]:
+        return self.engine.generate(prompts, params, lora_ids)

@@ -1,0 +1,287 @@
+"""Executes one scheduler step on the device.
+
+Host side: the native ``SeqTables.build_batch`` writes positions, slot mapping, padded block
+tables, KV lengths and query offsets for the step straight into pinned int32 buffers; token
+ids go into a pinned buffer too. One async H2D copy per buffer, the forward, the sampler,
+then one D2H read of the sampled ids (the only synchronisation of the step).
+
+Pure-decode steps of a captured batch size replay a CUDA graph of the whole forward +
+greedy argmax (static device buffers, padded rows write no KV and are ignored), which removes
+the per-kernel launch cost that dominates small-batch decode.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..config import EngineConfig
+from ..models.llama import AttnMetadata, LlamaModel
+from .kv_cache import KVCacheManager
+from .scheduler import SchedulerOutput
+from .sequence import Sequence
+
+
+class _Pinned:
+    """Reusable pinned host staging buffers for one step."""
+
+    def __init__(self, max_tokens: int, max_seqs: int, max_blocks: int, pin: bool):
+        kw = dict(pin_memory=pin)
+        self.input_ids = torch.zeros(max_tokens, dtype=torch.int32, **kw)
+        self.positions = torch.zeros(max_tokens, dtype=torch.int32, **kw)
+        self.slots = torch.zeros(max_tokens, dtype=torch.int32, **kw)
+        self.block_tables = torch.zeros(max_seqs, max_blocks, dtype=torch.int32, **kw)
+        self.seq_lens = torch.zeros(max_seqs, dtype=torch.int32, **kw)
+        self.query_start = torch.zeros(max_seqs + 1, dtype=torch.int32, **kw)
+        self.seq_ids = torch.zeros(max_seqs, dtype=torch.int64)
+        self.start = torch.zeros(max_seqs, dtype=torch.int32)
+        self.n_new = torch.zeros(max_seqs, dtype=torch.int32)
+        self.logits_idx = torch.zeros(max_seqs, dtype=torch.int64, **kw)
+        self.sampled = torch.zeros(max_seqs, dtype=torch.int64, **kw)
+
+
+class _DecodeGraph:
+    def __init__(self, bs: int):
+        self.bs = bs
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.input_ids = None
+        self.positions = None
+        self.slots = None
+        self.block_tables = None
+        self.seq_lens = None
+        self.out_ids = None
+        self.logits = None
+        self.launches = 0
+
+
+class ModelRunner:
+    def __init__(self, model: LlamaModel, cfg: EngineConfig, kv_cache: Optional[torch.Tensor],
+                 kv: KVCacheManager):
+        self.model = model
+        self.cfg = cfg
+        self.kv_cache = kv_cache
+        self.kv = kv
+        self.device = model.device
+        self.is_cuda = self.device.type == "cuda"
+        self.block_size = cfg.block_size
+        self.max_blocks = (cfg.max_model_len + cfg.block_size - 1) // cfg.block_size
+        max_tokens = cfg.max_num_batched_tokens + cfg.max_num_seqs
+        self.host = _Pinned(max_tokens, cfg.max_num_seqs, self.max_blocks, self.is_cuda)
+        self.graphs: Dict[int, _DecodeGraph] = {}
+        self.graph_pool = None
+        self.step_counter = 0
+        self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
+        self.timer = None  # optional StepTimer (device span of every step, for benchmarks)
+        self.h2d_bytes = 0  # host->device bytes copied by execute() (inputs of every step)
+        self.d2h_bytes = 0  # device->host bytes read back (sampled token ids)
+
+    # ------------------------------------------------------------------ batch preparation
+    def _fill_host(self, out: SchedulerOutput) -> Tuple[int, int, List[Sequence], List[int]]:
+        chunks = out.chunks
+        n = len(chunks)
+        h = self.host
+        ids = h.input_ids.numpy()
+        t = 0
+        sample_rows: List[int] = []
+        sample_seqs: List[Sequence] = []
+        for i, c in enumerate(chunks):
+            h.seq_ids[i] = c.seq.seq_id
+            h.start[i] = c.start
+            h.n_new[i] = c.num_tokens
+            toks = c.seq.tokens(c.start, c.start + c.num_tokens)
+            ids[t:t + c.num_tokens] = toks
+            t += c.num_tokens
+            if c.sample:
+                sample_rows.append(t - 1)
+                sample_seqs.append(c.seq)
+        T = self.kv.tables.build_batch(h.seq_ids[:n], h.start[:n], h.n_new[:n], h.positions, h.slots,
+                                       h.block_tables[:n], h.seq_lens[:n], h.query_start[: n + 1])
+        assert T == t
+        h.logits_idx[: len(sample_rows)] = torch.tensor(sample_rows, dtype=torch.int64)
+        return n, T, sample_seqs, sample_rows
+
+    def _decode_splits(self, nd: int, max_len: int) -> int:
+        return ops.decode_splits(nd, self.model.Hk, max_len, self.num_sms, self.block_size)
+
+    # ------------------------------------------------------------------ execution
+    @torch.inference_mode()
+    def execute(self, out: SchedulerOutput) -> List[int]:
+        """Run one step; returns the sampled token for every chunk with ``sample`` set (in order)."""
+        self.step_counter += 1
+        n, T, sample_seqs, sample_rows = self._fill_host(out)
+        if self.timer is not None:
+            self.timer.begin()
+        try:
+            return self._execute(out, n, T, sample_seqs, sample_rows)
+        finally:
+            if self.timer is not None:
+                self.timer.end()
+
+    def _execute(self, out: SchedulerOutput, n: int, T: int, sample_seqs: List[Sequence],
+                 sample_rows: List[int]) -> List[int]:
+        nd = len(out.decode)
+        h = self.host
+        dev = self.device
+        all_greedy = all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
+        if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0
+                and self._graph_for(nd) is not None):
+            return self._replay_decode(nd)
+        nb = int(max(1, (int(h.seq_lens[:n].max()) + self.block_size - 1) // self.block_size))
+        self.h2d_bytes += 4 * (3 * T + n * self.max_blocks + n + (n - nd + 1)) + 8 * max(1, len(sample_rows))
+        self.d2h_bytes += 8 * len(sample_rows)
+        input_ids = h.input_ids[:T].to(dev, non_blocking=True)
+        positions = h.positions[:T].to(dev, non_blocking=True)
+        slots = h.slots[:T].to(dev, non_blocking=True)
+        bt = h.block_tables[:n].to(dev, non_blocking=True)[:, :nb]  # contiguous pinned rows; sliced on device
+        lens = h.seq_lens[:n].to(dev, non_blocking=True)
+        meta = AttnMetadata(positions=positions, slot_mapping=slots, num_decode=nd)
+        if nd > 0:
+            meta.decode_block_tables = bt[:nd]
+            meta.decode_seq_lens = lens[:nd]
+            meta.decode_splits = self._decode_splits(nd, int(h.seq_lens[:nd].max()))
+        if n > nd:
+            qs = h.query_start[nd: n + 1] - h.query_start[nd]
+            meta.num_prefill_tokens = T - nd
+            meta.prefill_block_tables = bt[nd:]
+            meta.prefill_seq_lens = lens[nd:]
+            meta.prefill_query_start = qs.to(dev, non_blocking=True)
+            if self.is_cuda:
+                meta.prefill_tiles = ops.prefill_tiles(qs.tolist()).to(dev, non_blocking=True)
+        ns = len(sample_rows)
+        if ns == 0:
+            meta.logits_indices = h.logits_idx[:1].to(dev, non_blocking=True)
+            self.model.forward(input_ids, meta, self.kv_cache)
+            return []
+        meta.logits_indices = h.logits_idx[:ns].to(dev, non_blocking=True)
+        logits = self.model.forward(input_ids, meta, self.kv_cache)
+        ids = self.sample(logits, sample_seqs)
+        return ids
+
+    def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
+        dev = logits.device
+        ns = len(seqs)
+        if all(s.params.greedy and not s.params.needs_penalties for s in seqs):
+            out = ops.argmax(logits)
+        else:
+            lf = logits.float()
+            if any(s.params.needs_penalties for s in seqs):
+                trip = []
+                for r, s in enumerate(seqs):
+                    if not s.params.needs_penalties:
+                        continue
+                    ou, oc = np.unique(np.asarray(s.output_token_ids, dtype=np.int64), return_counts=True)
+                    cnt = dict(zip(ou.tolist(), oc.tolist()))
+                    toks = set(cnt)
+                    if s.params.repetition_penalty != 1.0:
+                        toks |= set(s.prompt_token_ids)
+                    trip.extend((r, int(tok), int(cnt.get(tok, 0))) for tok in sorted(toks))
+                if trip:
+                    tri = torch.tensor(trip, dtype=torch.int32).to(dev)
+                    rep = torch.tensor([s.params.repetition_penalty for s in seqs], dtype=torch.float32).to(dev)
+                    fr = torch.tensor([s.params.frequency_penalty for s in seqs], dtype=torch.float32).to(dev)
+                    pr = torch.tensor([s.params.presence_penalty for s in seqs], dtype=torch.float32).to(dev)
+                    ops.apply_penalties(lf, tri, rep, fr, pr)
+            temps = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32).to(dev)
+            tks = torch.tensor([s.params.top_k for s in seqs], dtype=torch.int32).to(dev)
+            tps = torch.tensor([s.params.top_p for s in seqs], dtype=torch.float32).to(dev)
+            mps = torch.tensor([s.params.min_p for s in seqs], dtype=torch.float32).to(dev)
+            seeds = torch.tensor([(s.params.seed if s.params.seed is not None else s.seq_id * 7919 + self.cfg.seed)
+                                  for s in seqs], dtype=torch.int64).to(dev)
+            offs = torch.tensor([len(s.output_token_ids) for s in seqs], dtype=torch.int64).to(dev)
+            out = ops.sample(lf, temps, tks, tps, mps, seeds, offs)
+        if self.is_cuda:
+            self.host.sampled[:ns].copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return self.host.sampled[:ns].tolist()
+        return out.tolist()
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def _bucket(self, nd: int) -> Optional[int]:
+        for b in self.cfg.cuda_graph_batch_sizes:
+            if b >= nd and b <= self.cfg.max_num_seqs:
+                return b
+        return None
+
+    def _graph_for(self, nd: int) -> Optional[_DecodeGraph]:
+        b = self._bucket(nd)
+        if b is None:
+            return None
+        g = self.graphs.get(b)
+        if g is None:
+            g = self._capture(b)
+        return g
+
+    def _decode_meta(self, g: _DecodeGraph) -> AttnMetadata:
+        splits = self._decode_splits(g.bs, self.cfg.max_model_len)
+        meta = AttnMetadata(positions=g.positions, slot_mapping=g.slots, num_decode=g.bs,
+                            decode_block_tables=g.block_tables, decode_seq_lens=g.seq_lens,
+                            decode_splits=splits)
+        if splits > 1:
+            meta.decode_workspace = g.workspace
+        meta.logits_indices = None
+        return meta
+
+    def _capture(self, bs: int) -> _DecodeGraph:
+        dev = self.device
+        g = _DecodeGraph(bs)
+        g.input_ids = torch.zeros(bs, dtype=torch.int32, device=dev)
+        g.positions = torch.zeros(bs, dtype=torch.int32, device=dev)
+        g.slots = torch.full((bs,), -1, dtype=torch.int32, device=dev)
+        g.block_tables = torch.zeros(bs, self.max_blocks, dtype=torch.int32, device=dev)
+        g.seq_lens = torch.ones(bs, dtype=torch.int32, device=dev)
+        splits = self._decode_splits(bs, self.cfg.max_model_len)
+        g.workspace = torch.empty(bs * self.model.H * max(1, splits) * (self.model.D + 2),
+                                  dtype=torch.float32, device=dev)
+        meta = self._decode_meta(g)
+        # warm up (lazy kernel attributes, allocator) outside capture
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                logits = self.model.forward(g.input_ids, meta, self.kv_cache)
+                ops.argmax(logits)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        n0 = ops.LAUNCHES.n
+        with torch.cuda.graph(graph, pool=self.graph_pool):
+            g.logits = self.model.forward(g.input_ids, meta, self.kv_cache)
+            g.out_ids = ops.argmax(g.logits)
+        g.launches = ops.LAUNCHES.n - n0
+        ops.LAUNCHES.n = n0
+        g.graph = graph
+        self.graphs[bs] = g
+        return g
+
+    def _replay_decode(self, nd: int) -> List[int]:
+        g = self._graph_for(nd)
+        h = self.host
+        bs = g.bs
+        self.h2d_bytes += 4 * bs * (4 + self.max_blocks)
+        self.d2h_bytes += 8 * bs
+        # pad rows: slot -1 (no KV write), length 1, block 0
+        if nd < bs:
+            h.positions[nd:bs] = 0
+            h.slots[nd:bs] = -1
+            h.seq_lens[nd:bs] = 1
+            h.block_tables[nd:bs] = 0
+            h.input_ids[nd:bs] = 0
+        g.input_ids.copy_(h.input_ids[:bs], non_blocking=True)
+        g.positions.copy_(h.positions[:bs], non_blocking=True)
+        g.slots.copy_(h.slots[:bs], non_blocking=True)
+        g.seq_lens.copy_(h.seq_lens[:bs], non_blocking=True)
+        g.block_tables.copy_(h.block_tables[:bs], non_blocking=True)
+        g.graph.replay()
+        ops.LAUNCHES.add(g.launches)
+        self.host.sampled[:bs].copy_(g.out_ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return self.host.sampled[:nd].tolist()
+
+    def capture_all(self, sizes=None) -> None:
+        for b in sizes or self.cfg.cuda_graph_batch_sizes:
+            if b <= self.cfg.max_num_seqs and b not in self.graphs:
+                self._capture(b)

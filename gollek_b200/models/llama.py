@@ -1,0 +1,285 @@
+"""Serving graph of the Llama family (Llama-2/3, Mistral) and Mixtral (top-k MoE).
+
+One instance runs on one GPU (one process per GPU); under tensor parallelism it holds the
+rank's Megatron-style shard: QKV and gate/up column-parallel (whole heads / FFN slices),
+o_proj and down_proj row-parallel followed by an all-reduce, lm_head vocab-parallel
+followed by an all-gather; embedding and norms replicated. Weights are fused at load time:
+``w_qkv = [q; k; v]`` rows and ``w_gate_up`` = gate/up rows interleaved in groups of 64 so
+the GEMM's SwiGLU epilogue emits ``silu(gate) * up`` directly.
+
+Per layer (decode or mixed chunked-prefill step):
+  fused_add_rms_norm → GEMM(qkv) → rope_kv_write (RoPE + paged KV write) →
+  paged attention (decode kernel for the q_len = 1 sequences, prefill kernel for the rest) →
+  GEMM(o) [→ all-reduce] → fused_add_rms_norm → GEMM(gate_up, SwiGLU) → GEMM(down) [→ all-reduce]
+
+Replaces the reference's per-layer flow (kernel/cuda/gollek-kernel-cuda/…/cuda/runner/
+CudaRunner.java:475-569 and runner/safetensor/gollek-safetensor-engine/…/engine/forward/
+DirectForwardPass.java:221-321) and its MoE loop (…/generation/moe/MoeForwardPass.java:39-128).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, Dict, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from .reference import rope_cos_sin
+
+
+@dataclass
+class AttnMetadata:
+    """Per-step batch description built by the model runner.
+
+    Tokens are ordered: the ``num_decode`` single-token (decode) sequences first, then the
+    prefill / chunked-prefill sequences.
+    """
+    positions: torch.Tensor            # [T] int32
+    slot_mapping: torch.Tensor         # [T] int32
+    num_decode: int
+    decode_block_tables: Optional[torch.Tensor] = None   # [nd, max_blocks] int32
+    decode_seq_lens: Optional[torch.Tensor] = None       # [nd] int32
+    decode_splits: int = 1
+    decode_workspace: Optional[torch.Tensor] = None
+    num_prefill_tokens: int = 0
+    prefill_block_tables: Optional[torch.Tensor] = None  # [np, max_blocks] int32
+    prefill_seq_lens: Optional[torch.Tensor] = None      # [np] int32
+    prefill_query_start: Optional[torch.Tensor] = None   # [np + 1] int32 (relative)
+    prefill_tiles: Optional[torch.Tensor] = None         # [ntiles, 2] int32
+    logits_indices: Optional[torch.Tensor] = None        # [B_out] int64 rows for the lm_head
+
+    @property
+    def num_tokens(self) -> int:
+        return self.num_decode + self.num_prefill_tokens
+
+
+class TPComm:
+    """Collectives used by the model under tensor parallelism (no-ops at tp_size 1)."""
+
+    def __init__(self, rank: int = 0, size: int = 1):
+        self.rank, self.size = rank, size
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        return t
+
+    def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
+        return t
+
+
+def _pad_rows(w: torch.Tensor, rows: int) -> torch.Tensor:
+    if w.shape[0] == rows:
+        return w
+    out = torch.zeros(rows, *w.shape[1:], dtype=w.dtype, device=w.device)
+    out[: w.shape[0]] = w
+    return out
+
+
+def _pad_cols(w: torch.Tensor, cols: int) -> torch.Tensor:
+    if w.shape[1] == cols:
+        return w
+    out = torch.zeros(w.shape[0], cols, dtype=w.dtype, device=w.device)
+    out[:, : w.shape[1]] = w
+    return out
+
+
+class LlamaModel:
+    """Llama / Mixtral decoder for serving (one TP rank)."""
+
+    def __init__(self, cfg: ModelConfig, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                 comm: Optional[TPComm] = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.comm = comm or TPComm()
+        tp, r = self.comm.size, self.comm.rank
+        if cfg.num_attention_heads % tp:
+            raise ValueError("num_attention_heads must be divisible by the TP size")
+        self.H = cfg.num_attention_heads // tp
+        if cfg.num_key_value_heads >= tp:
+            if cfg.num_key_value_heads % tp:
+                raise ValueError("num_key_value_heads must be divisible by the TP size")
+            self.Hk = cfg.num_key_value_heads // tp
+            self.kv_head0 = r * self.Hk
+        else:  # replicate KV heads across ranks
+            self.Hk = 1
+            self.kv_head0 = r * cfg.num_key_value_heads // tp
+        self.D = cfg.head_dim
+        f_shard = cfg.intermediate_size // tp
+        if cfg.intermediate_size % tp:
+            raise ValueError("intermediate_size must be divisible by the TP size")
+        self.F = f_shard
+        self.F_pad = (f_shard + ops.SWIGLU_GROUP - 1) // ops.SWIGLU_GROUP * ops.SWIGLU_GROUP
+        if cfg.vocab_size % tp:
+            raise ValueError("vocab_size must be divisible by the TP size")
+        self.V_local = cfg.vocab_size // tp
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.cos_sin = rope_cos_sin(cfg, max(cfg.max_position_embeddings, 8192), device=self.device)
+        self.layers: List[Dict[str, torch.Tensor]] = []
+        self.embed: Optional[torch.Tensor] = None
+        self.norm: Optional[torch.Tensor] = None
+        self.lm_head: Optional[torch.Tensor] = None
+        self.lora = None  # optional MultiLoRA hook (gollek_b200.engine.lora)
+
+    # ------------------------------------------------------------------ weights
+    def load_weights(self, get: Callable[[str], torch.Tensor]) -> None:
+        """Shard and fuse HF-named weights. ``get(name)`` returns a (CPU or GPU) tensor."""
+        cfg, tp, r = self.cfg, self.comm.size, self.comm.rank
+        H, Hk, D = self.H, self.Hk, self.D
+        dev, dt = self.device, self.dtype
+
+        def t(name):
+            return get(name).to(device=dev, dtype=dt)
+
+        self.embed = t("model.embed_tokens.weight").contiguous()
+        self.norm = t("model.norm.weight").contiguous()
+        head_name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
+        self.lm_head = t(head_name)[r * self.V_local:(r + 1) * self.V_local].contiguous()
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = f"model.layers.{i}."
+            q = t(p + "self_attn.q_proj.weight")[r * H * D:(r + 1) * H * D]
+            k = t(p + "self_attn.k_proj.weight")[self.kv_head0 * D:(self.kv_head0 + Hk) * D]
+            v = t(p + "self_attn.v_proj.weight")[self.kv_head0 * D:(self.kv_head0 + Hk) * D]
+            o = t(p + "self_attn.o_proj.weight")[:, r * H * D:(r + 1) * H * D]
+            L = {
+                "in_norm": t(p + "input_layernorm.weight").contiguous(),
+                "post_norm": t(p + "post_attention_layernorm.weight").contiguous(),
+                "w_qkv": torch.cat([q, k, v], 0).contiguous(),
+                "w_o": o.contiguous(),
+            }
+            if cfg.is_moe:
+                pe = p + "block_sparse_moe."
+                L["router"] = t(pe + "gate.weight").contiguous()
+                experts = []
+                for e in range(cfg.num_local_experts):
+                    g = t(pe + f"experts.{e}.w1.weight")[r * self.F:(r + 1) * self.F]
+                    u = t(pe + f"experts.{e}.w3.weight")[r * self.F:(r + 1) * self.F]
+                    d = t(pe + f"experts.{e}.w2.weight")[:, r * self.F:(r + 1) * self.F]
+                    experts.append((
+                        ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad)).contiguous(),
+                        _pad_cols(d, self.F_pad).contiguous()))
+                L["experts"] = experts
+            else:
+                g = t(p + "mlp.gate_proj.weight")[r * self.F:(r + 1) * self.F]
+                u = t(p + "mlp.up_proj.weight")[r * self.F:(r + 1) * self.F]
+                d = t(p + "mlp.down_proj.weight")[:, r * self.F:(r + 1) * self.F]
+                L["w_gate_up"] = ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad)).contiguous()
+                L["w_down"] = _pad_cols(d, self.F_pad).contiguous()
+            self.layers.append(L)
+
+    def init_random(self, seed: int = 0, std: float = 0.02) -> None:
+        """Random-init this rank's shard directly on the device (benchmarks; no checkpoint)."""
+        cfg = self.cfg
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + self.comm.rank)
+        dev, dt = self.device, self.dtype
+
+        def rnd(*shape):
+            x = torch.empty(*shape, dtype=dt, device=dev)
+            x.normal_(0.0, std, generator=g)
+            return x
+
+        h = cfg.hidden_size
+        self.embed = rnd(cfg.vocab_size, h)
+        self.norm = torch.ones(h, dtype=dt, device=dev)
+        self.lm_head = rnd(self.V_local, h)
+        self.layers = []
+        for _ in range(cfg.num_hidden_layers):
+            L = {
+                "in_norm": torch.ones(h, dtype=dt, device=dev),
+                "post_norm": torch.ones(h, dtype=dt, device=dev),
+                "w_qkv": rnd((self.H + 2 * self.Hk) * self.D, h),
+                "w_o": rnd(h, self.H * self.D),
+            }
+            if cfg.is_moe:
+                L["router"] = rnd(cfg.num_local_experts, h)
+                L["experts"] = [(rnd(2 * self.F_pad, h), rnd(h, self.F_pad)) for _ in range(cfg.num_local_experts)]
+            else:
+                L["w_gate_up"] = rnd(2 * self.F_pad, h)
+                L["w_down"] = rnd(h, self.F_pad)
+            self.layers.append(L)
+
+    def weight_bytes(self) -> int:
+        n = sum(x.numel() * x.element_size() for x in (self.embed, self.norm, self.lm_head))
+        for L in self.layers:
+            for k, v in L.items():
+                if k == "experts":
+                    n += sum(a.numel() * a.element_size() + b.numel() * b.element_size() for a, b in v)
+                else:
+                    n += v.numel() * v.element_size()
+        return n
+
+    # ------------------------------------------------------------------ KV cache
+    def kv_cache_shape(self, num_blocks: int, block_size: int = 16) -> tuple:
+        return (self.cfg.num_hidden_layers, num_blocks, 2, self.Hk, block_size, self.D)
+
+    def kv_bytes_per_block(self, block_size: int = 16) -> int:
+        return self.cfg.num_hidden_layers * 2 * self.Hk * block_size * self.D * torch.finfo(self.dtype).bits // 8
+
+    # ------------------------------------------------------------------ forward
+    def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata) -> torch.Tensor:
+        out = torch.empty_like(q)
+        nd = meta.num_decode
+        if nd > 0:
+            ops.paged_decode_attention(q[:nd], cache, meta.decode_block_tables, meta.decode_seq_lens, self.scale,
+                                       meta.decode_splits, out=out[:nd], workspace=meta.decode_workspace)
+        if meta.num_prefill_tokens > 0:
+            ops.paged_prefill_attention(q[nd:], cache, meta.prefill_block_tables, meta.prefill_seq_lens,
+                                        meta.prefill_query_start, self.scale, tiles=meta.prefill_tiles,
+                                        out=out[nd:])
+        return out
+
+    def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:
+        cfg = self.cfg
+        logits = ops.linear(x, L["router"]).float()
+        probs = torch.softmax(logits, -1)
+        topw, topi = probs.topk(cfg.num_experts_per_tok, -1)
+        topw = (topw / topw.sum(-1, keepdim=True)).to(torch.float32)
+        out = torch.zeros(x.shape[0], cfg.hidden_size, dtype=torch.float32, device=x.device)
+        for e, (w_gu, w_d) in enumerate(L["experts"]):
+            sel = (topi == e)
+            rows = sel.any(-1).nonzero().flatten()
+            if rows.numel() == 0:
+                continue
+            xe = x.index_select(0, rows).contiguous()
+            ye = ops.linear(ops.linear_swiglu(xe, w_gu), w_d).float()
+            we = (topw * sel).sum(-1).index_select(0, rows)
+            out.index_add_(0, rows, ye * we[:, None])
+        return out.to(x.dtype)
+
+    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor]) -> torch.Tensor:
+        """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP)."""
+        cfg = self.cfg
+        eps = cfg.rms_norm_eps
+        h = ops.embedding(input_ids, self.embed)
+        residual = h  # the embedding output buffer becomes the residual stream (updated in place)
+        x = h
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                x = ops.rms_norm(h, L["in_norm"], eps)
+            else:
+                x = ops.fused_add_rms_norm(h, residual, L["in_norm"], eps)
+            qkv = ops.linear(x, L["w_qkv"])
+            if self.lora is not None:
+                qkv = self.lora.apply(li, "qkv", x, qkv)
+            cache = kv_cache[li] if kv_cache is not None else None
+            q = ops.rope_kv_write(qkv, meta.positions, self.cos_sin, cache, meta.slot_mapping,
+                                  self.H, self.Hk, self.D)
+            a = self._attention(q, cache, meta).view(q.shape[0], self.H * self.D)
+            h = ops.linear(a, L["w_o"])
+            if self.lora is not None:
+                h = self.lora.apply(li, "o", a, h)
+            h = self.comm.all_reduce(h)
+            x = ops.fused_add_rms_norm(h, residual, L["post_norm"], eps)
+            if cfg.is_moe:
+                h = self._moe(x, L)
+            else:
+                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"])
+            h = self.comm.all_reduce(h)
+        x = ops.fused_add_rms_norm(h, residual, self.norm, eps)
+        if meta.logits_indices is not None:
+            x = x.index_select(0, meta.logits_indices)
+        logits = ops.linear(x, self.lm_head)
+        return self.comm.all_gather_last(logits)

@@ -1,0 +1,213 @@
+"""Hot-op entry points.
+
+Every function dispatches on the device of its inputs: CUDA tensors go to the sm_100a
+kernels of ``gollek_b200_C`` (``csrc/kernels``), CPU tensors to the plain-PyTorch
+restatement in ``gollek_b200.ops.reference`` (the numerics oracle). There is no silent
+fallback: a CUDA tensor with the extension missing raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ..native import cuda_ext
+
+EPI_NONE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+SWIGLU_GROUP = 64
+
+
+class _LaunchCounter:
+    """Counts sm_100a kernel launches issued through this module (graph replays add their
+    captured count via ``add``); the benchmark reports it for its timed region."""
+
+    def __init__(self):
+        self.n = 0
+
+    def add(self, k: int = 1) -> None:
+        self.n += k
+
+    def reset(self) -> int:
+        n, self.n = self.n, 0
+        return n
+
+
+LAUNCHES = _LaunchCounter()
+
+
+def _C(k: int = 1):
+    LAUNCHES.add(k)
+    return cuda_ext()
+
+
+def _cpu(result: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+    """CPU path: honour a caller-provided output buffer."""
+    if out is None:
+        return result
+    out.copy_(result)
+    return out
+
+
+# ----------------------------------------------------------------------------- norms
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return _cpu(ref.rms_norm(x, w, eps), out)
+    out = torch.empty_like(x) if out is None else out
+    _C().rms_norm(out, x, w, float(eps))
+    return out
+
+
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """residual += x (in place); returns rms_norm(residual) * w."""
+    if not x.is_cuda:
+        return _cpu(ref.fused_add_rms_norm(x, residual, w, eps), out)
+    out = torch.empty_like(x) if out is None else out
+    _C().fused_add_rms_norm(out, x, residual, w, float(eps))
+    return out
+
+
+# ----------------------------------------------------------------------------- rope + kv
+def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
+                  kv_cache: Optional[torch.Tensor], slot_mapping: Optional[torch.Tensor],
+                  num_heads: int, num_kv_heads: int, head_dim: int,
+                  q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not qkv.is_cuda:
+        return _cpu(ref.rope_kv_write(qkv, positions, cos_sin, kv_cache, slot_mapping,
+                                      num_heads, num_kv_heads, head_dim), q_out)
+    T = qkv.shape[0]
+    q_out = torch.empty(T, num_heads, head_dim, dtype=qkv.dtype, device=qkv.device) if q_out is None else q_out
+    _C().rope_kv_write(q_out, qkv, positions, cos_sin, kv_cache, slot_mapping,
+                       num_heads, num_kv_heads, head_dim)
+    return q_out
+
+
+# ----------------------------------------------------------------------------- attention
+def decode_splits(num_seqs: int, num_kv_heads: int, max_seq_len: int, num_sms: int = 148,
+                  block_size: int = 16) -> int:
+    """Split-KV factor for the decode kernel: fill ~2 waves of CTAs, keep >= 8 blocks per split."""
+    ctas = max(1, num_seqs * num_kv_heads)
+    if ctas >= 2 * num_sms:
+        return 1
+    want = (2 * num_sms + ctas - 1) // ctas
+    max_by_len = max(1, (max_seq_len + block_size - 1) // block_size // 8)
+    return int(max(1, min(want, max_by_len, 32)))
+
+
+def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                           seq_lens: torch.Tensor, scale: float, num_splits: int = 1,
+                           out: Optional[torch.Tensor] = None,
+                           workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One query token per sequence: q [B, H, D]."""
+    if not q.is_cuda:
+        B = q.shape[0]
+        qsl = torch.arange(B + 1, dtype=torch.int32)
+        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, qsl, scale), out)
+    out = torch.empty_like(q) if out is None else out
+    if num_splits > 1 and workspace is None:
+        B, H, D = q.shape
+        workspace = torch.empty(B * H * num_splits * (D + 2), dtype=torch.float32, device=q.device)
+    _C(2 if num_splits > 1 else 1).paged_decode_attention(out, q, kv_cache, block_tables, seq_lens, float(scale),
+                                                          int(num_splits), workspace)
+    return out
+
+
+def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
+    """(sequence, query offset) pairs of the 64-row query tiles the prefill kernel runs."""
+    tiles = []
+    for b in range(len(query_start) - 1):
+        ql = query_start[b + 1] - query_start[b]
+        for off in range(0, ql, block_m):
+            tiles.append((b, off))
+    return torch.tensor(tiles, dtype=torch.int32).view(-1, 2)
+
+
+def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                            seq_lens: torch.Tensor, query_start: torch.Tensor, scale: float,
+                            tiles: Optional[torch.Tensor] = None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new)."""
+    if not q.is_cuda:
+        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale), out)
+    out = torch.empty_like(q) if out is None else out
+    if tiles is None:
+        tiles = prefill_tiles(query_start.tolist()).to(q.device)
+    _C().paged_prefill_attention(out, q, kv_cache, block_tables, seq_lens, query_start, tiles, float(scale))
+    return out
+
+
+# ----------------------------------------------------------------------------- GEMM
+def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None, bn: int = 0) -> torch.Tensor:
+    """a [M, K] @ w[N, K]^T (+ residual), bf16 in/out, fp32 accumulate (tcgen05 on GPU)."""
+    if not a.is_cuda:
+        return _cpu(ref.gemm(a, w, residual), out)
+    M, N = a.shape[0], w.shape[0]
+    out = torch.empty(M, N, dtype=a.dtype, device=a.device) if out is None else out
+    epi = EPI_RESIDUAL if residual is not None else EPI_NONE
+    _C().gemm_bf16(out, a, w, residual, epi, bn, None, 0)
+    return out
+
+
+def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  bn: int = 0) -> torch.Tensor:
+    """silu(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``."""
+    if not a.is_cuda:
+        return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP), out)
+    M, N = a.shape[0], w_gate_up.shape[0]
+    out = torch.empty(M, N // 2, dtype=a.dtype, device=a.device) if out is None else out
+    _C().gemm_bf16(out, a, w_gate_up, None, EPI_SWIGLU, bn, None, 0)
+    return out
+
+
+interleave_gate_up = ref.interleave_gate_up
+
+
+def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return _cpu(ref.silu_mul(x), out)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device) if out is None else out
+    _C().silu_mul(out, x)
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not table.is_cuda:
+        return _cpu(ref.embedding(ids, table), out)
+    out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device) if out is None else out
+    _C().embedding(out, ids, table)
+    return out
+
+
+# ----------------------------------------------------------------------------- sampling
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not logits.is_cuda:
+        return _cpu(logits.float().argmax(-1), out)
+    out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device) if out is None else out
+    _C().argmax(out, logits)
+    return out
+
+
+def apply_penalties(logits: torch.Tensor, triples: torch.Tensor, repetition: torch.Tensor,
+                    frequency: torch.Tensor, presence: torch.Tensor) -> torch.Tensor:
+    """In-place penalties on fp32 logits from unique (row, token, count) triples."""
+    if not logits.is_cuda:
+        return ref.apply_penalties_triples(logits, triples, repetition, frequency, presence)
+    _C().apply_penalties(logits, triples, repetition, frequency, presence)
+    return logits
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           min_p: torch.Tensor, seeds: torch.Tensor, offsets: torch.Tensor,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not logits.is_cuda:
+        return _cpu(ref.sample(logits, temperature, top_k, top_p, min_p, seeds, offsets), out)
+    out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device) if out is None else out
+    _C().sample(out, logits, temperature, top_k, top_p, min_p, seeds, offsets)
+    return out
+
+
+def attention_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

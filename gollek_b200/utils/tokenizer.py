@@ -1,0 +1,135 @@
+"""Tokenizers: Hugging Face ``tokenizer.json``, GGUF-embedded vocabularies, and a byte fallback.
+
+The reference ships BPE / HF-BPE / SentencePiece / WordPiece tokenizers and a GGUF
+metadata tokenizer (core/gollek-tokenizer-core/…/tokenizer/impl/*.java; runner/gguf/
+gollek-gguf-tokenizer/…/GGUFTokenizer.java:1-335) plus a streaming decoder. Here the HF path
+uses the ``tokenizers`` library, GGUF vocabularies get a greedy longest-match SentencePiece-style
+encoder over the stored pieces (scores break ties), and random-init presets use a byte-level
+tokenizer so text requests still work end to end.
+"""
+from __future__ import annotations
+
+import json
+import os
+from typing import Dict, List, Optional
+
+
+class ByteTokenizer:
+    """UTF-8 bytes mapped to ids 3..258 (0 = pad, 1 = bos, 2 = eos)."""
+    offset = 3
+
+    def __init__(self, vocab_size: int = 32000, eos_token_id: int = 2):
+        self.vocab_size = vocab_size
+        self.eos_token_id = eos_token_id
+
+    def encode(self, text: str) -> List[int]:
+        return [b + self.offset for b in text.encode("utf-8")]
+
+    def decode(self, ids: List[int]) -> str:
+        bs = bytes(i - self.offset for i in ids if self.offset <= i < self.offset + 256)
+        return bs.decode("utf-8", errors="replace")
+
+    def apply_chat_template(self, messages: List[dict]) -> str:
+        return default_chat_template(messages)
+
+
+class HFTokenizer:
+    def __init__(self, path: str):
+        from tokenizers import Tokenizer
+        self.tok = Tokenizer.from_file(path)
+        self.vocab_size = self.tok.get_vocab_size()
+        self.chat_template: Optional[str] = None
+        cfg = os.path.join(os.path.dirname(path), "tokenizer_config.json")
+        if os.path.exists(cfg):
+            with open(cfg) as f:
+                self.chat_template = json.load(f).get("chat_template")
+
+    def encode(self, text: str) -> List[int]:
+        return self.tok.encode(text, add_special_tokens=True).ids
+
+    def decode(self, ids: List[int]) -> str:
+        return self.tok.decode(ids, skip_special_tokens=True)
+
+    def apply_chat_template(self, messages: List[dict]) -> str:
+        if self.chat_template:
+            try:
+                import jinja2
+                return jinja2.Template(self.chat_template).render(messages=messages, add_generation_prompt=True,
+                                                                  bos_token="", eos_token="")
+            except Exception:
+                pass
+        return default_chat_template(messages)
+
+
+class GGUFTokenizer:
+    """Vocabulary from ``tokenizer.ggml.tokens`` (+ scores); SentencePiece-style greedy encode."""
+
+    def __init__(self, tokens: List[str], scores: Optional[List[float]] = None, bos: int = 1, eos: int = 2):
+        self.tokens = tokens
+        self.vocab_size = len(tokens)
+        self.scores = scores or [0.0] * len(tokens)
+        self.bos, self.eos_token_id = bos, eos
+        self.index: Dict[str, int] = {}
+        for i, t in enumerate(tokens):
+            if t not in self.index or self.scores[i] > self.scores[self.index[t]]:
+                self.index[t] = i
+        self.max_len = max((len(t) for t in tokens), default=1)
+        self.byte_ids = {}
+        for i, t in enumerate(tokens):
+            if len(t) == 6 and t.startswith("<0x") and t.endswith(">"):
+                try:
+                    self.byte_ids[int(t[3:5], 16)] = i
+                except ValueError:
+                    pass
+
+    @staticmethod
+    def from_metadata(meta: dict) -> "GGUFTokenizer":
+        return GGUFTokenizer(meta.get("tokenizer.ggml.tokens", []), meta.get("tokenizer.ggml.scores"),
+                             int(meta.get("tokenizer.ggml.bos_token_id", 1)), int(meta.get("tokenizer.ggml.eos_token_id", 2)))
+
+    def encode(self, text: str) -> List[int]:
+        s = "▁" + text.replace(" ", "▁")
+        ids, i = [], 0
+        while i < len(s):
+            for L in range(min(self.max_len, len(s) - i), 0, -1):
+                piece = s[i:i + L]
+                if piece in self.index:
+                    ids.append(self.index[piece])
+                    i += L
+                    break
+            else:
+                for b in s[i].encode("utf-8"):
+                    ids.append(self.byte_ids.get(b, 0))
+                i += 1
+        return ids
+
+    def decode(self, ids: List[int]) -> str:
+        out = bytearray()
+        inv_bytes = {v: k for k, v in self.byte_ids.items()}
+        for i in ids:
+            if i in inv_bytes:
+                out.append(inv_bytes[i])
+            elif 0 <= i < len(self.tokens):
+                out += self.tokens[i].replace("▁", " ").encode("utf-8")
+        return out.decode("utf-8", errors="replace").lstrip(" ")
+
+    def apply_chat_template(self, messages: List[dict]) -> str:
+        return default_chat_template(messages)
+
+
+def default_chat_template(messages: List[dict]) -> str:
+    parts = []
+    for m in messages:
+        content = m.get("content", "")
+        if isinstance(content, list):
+            content = "".join(c.get("text", "") for c in content if isinstance(c, dict))
+        parts.append(f"<|{m.get('role', 'user')}|>\n{content}\n")
+    parts.append("<|assistant|>\n")
+    return "".join(parts)
+
+
+def load_tokenizer(directory: str):
+    p = os.path.join(directory, "tokenizer.json")
+    if os.path.exists(p):
+        return HFTokenizer(p)
+    return None

@@ -1,0 +1,180 @@
+"""sm_100a kernels against the plain-PyTorch fp32 restatements (gollek_b200.ops.reference)."""
+import math
+
+import pytest
+import torch
+
+from gollek_b200 import ops
+from gollek_b200.ops import reference as R
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _g(seed=0):
+    return torch.Generator(device=DEV).manual_seed(seed)
+
+
+def bf(x):
+    return x.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("T,d", [(1, 256), (7, 4096), (33, 8192), (5, 1024)])
+def test_rms_norm(T, d):
+    x = bf(torch.randn(T, d, device=DEV, generator=_g(1)))
+    w = bf(torch.randn(d, device=DEV, generator=_g(2)))
+    torch.testing.assert_close(ops.rms_norm(x, w, 1e-5).float(), R.rms_norm(x.float(), w.float(), 1e-5),
+                               rtol=2e-2, atol=2e-2)
+    res = bf(torch.randn(T, d, device=DEV, generator=_g(3)))
+    res_ref = res.clone()
+    y = ops.fused_add_rms_norm(x, res, w, 1e-5)
+    yr = R.fused_add_rms_norm(x, res_ref, w, 1e-5)
+    torch.testing.assert_close(res, res_ref, rtol=0, atol=0)
+    torch.testing.assert_close(y.float(), yr.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("H,Hk,D", [(32, 8, 128), (8, 2, 32), (4, 1, 128)])
+def test_rope_kv_write(H, Hk, D):
+    from gollek_b200.config import preset
+    from gollek_b200.models.reference import rope_cos_sin
+    cfg = preset("tiny-llama", head_dim=D, rope_theta=500000.0)
+    T, NB, bs = 37, 8, 16
+    qkv = bf(torch.randn(T, (H + 2 * Hk) * D, device=DEV, generator=_g(4)))
+    pos = torch.randint(0, 4000, (T,), device=DEV, generator=_g(5)).int()
+    slots = torch.randperm(NB * bs, device=DEV, generator=_g(6))[:T].int()
+    slots[3] = -1
+    cs = rope_cos_sin(cfg, 4096, device=DEV)
+    c1 = torch.zeros(NB, 2, Hk, bs, D, dtype=torch.bfloat16, device=DEV)
+    c2 = c1.clone()
+    q1 = ops.rope_kv_write(qkv, pos, cs, c1, slots, H, Hk, D)
+    q2 = R.rope_kv_write(qkv.float(), pos, cs, c2, slots, H, Hk, D)
+    torch.testing.assert_close(q1.float(), q2.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(c1.float(), c2.float(), rtol=2e-2, atol=2e-2)
+
+
+def _paged_setup(B, Hk, D, lens, NB=None, bs=16, seed=0):
+    g = _g(seed)
+    max_blocks = max((l + bs - 1) // bs for l in lens)
+    NB = NB or B * max_blocks + 3
+    cache = bf(torch.randn(NB, 2, Hk, bs, D, device=DEV, generator=g))
+    perm = torch.randperm(NB, device=DEV, generator=g)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32, device=DEV)
+    k = 0
+    for b, l in enumerate(lens):
+        n = (l + bs - 1) // bs
+        bt[b, :n] = perm[k:k + n].int()
+        k += n
+    return cache, bt, torch.tensor(lens, dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("H,Hk,D", [(32, 8, 128), (4, 1, 128), (8, 2, 32), (64, 8, 128)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_decode_attention(H, Hk, D, splits):
+    lens = [1, 17, 100, 513, 40]
+    B = len(lens)
+    cache, bt, sl = _paged_setup(B, Hk, D, lens, seed=7)
+    q = bf(torch.randn(B, H, D, device=DEV, generator=_g(8)))
+    scale = 1 / math.sqrt(D)
+    out = ops.paged_decode_attention(q, cache, bt, sl, scale, num_splits=splits)
+    qsl = torch.arange(B + 1, dtype=torch.int32)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl, scale)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("H,Hk,D", [(32, 8, 128), (8, 2, 32), (8, 8, 64)])
+def test_paged_prefill_attention(H, Hk, D):
+    # (prefix already cached, new tokens) per sequence
+    specs = [(0, 70), (33, 20), (128, 1), (5, 130)]
+    lens = [p + n for p, n in specs]
+    B = len(specs)
+    cache, bt, sl = _paged_setup(B, Hk, D, lens, seed=9)
+    qs = [0]
+    for _, n in specs:
+        qs.append(qs[-1] + n)
+    T = qs[-1]
+    q = bf(torch.randn(T, H, D, device=DEV, generator=_g(10)))
+    qsl = torch.tensor(qs, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(D)
+    out = ops.paged_prefill_attention(q, cache, bt, sl, qsl, scale)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl.cpu(), scale)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (77, 384, 256), (128, 4096, 4096), (300, 6144, 4096),
+                                   (2048, 1024, 512), (16, 32000, 256)])
+@pytest.mark.parametrize("bn", [0, 64, 128, 256])
+def test_gemm(M, N, K, bn):
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(11)) * 0.5)
+    b = bf(torch.randn(N, K, device=DEV, generator=_g(12)) * 0.05)
+    y = ops.linear(a, b, bn=bn)
+    ref = a.float() @ b.float().t()
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2 * max(1.0, ref.abs().max().item() / 4))
+
+
+def test_gemm_residual():
+    M, N, K = 200, 512, 384
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(13)))
+    b = bf(torch.randn(N, K, device=DEV, generator=_g(14)) * 0.05)
+    r = bf(torch.randn(M, N, device=DEV, generator=_g(15)))
+    y = ops.linear(a, b, residual=r)
+    torch.testing.assert_close(y.float(), a.float() @ b.float().t() + r.float(), rtol=2e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("M,F,K", [(5, 704, 256), (300, 1792, 4096), (64, 14336, 4096)])
+def test_gemm_swiglu(M, F, K):
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(16)))
+    wg = bf(torch.randn(F, K, device=DEV, generator=_g(17)) * 0.03)
+    wu = bf(torch.randn(F, K, device=DEV, generator=_g(18)) * 0.03)
+    w = ops.interleave_gate_up(wg, wu).contiguous()
+    y = ops.linear_swiglu(a, w)
+    ref = torch.nn.functional.silu(a.float() @ wg.float().t()) * (a.float() @ wu.float().t())
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=3e-2)
+
+
+def test_embedding_and_silu():
+    table = bf(torch.randn(1000, 256, device=DEV, generator=_g(19)))
+    ids = torch.randint(0, 1000, (50,), device=DEV, generator=_g(20)).int()
+    torch.testing.assert_close(ops.embedding(ids, table), table[ids.long()])
+    x = bf(torch.randn(9, 512, device=DEV, generator=_g(21)))
+    torch.testing.assert_close(ops.silu_mul(x).float(), R.silu_mul(x.float()), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("V", [1000, 32000, 128256])
+def test_argmax(V):
+    logits = bf(torch.randn(33, V, device=DEV, generator=_g(22)))
+    out = ops.argmax(logits)
+    lf = logits.float()
+    ref = torch.stack([torch.nonzero(r == r.max())[0, 0] for r in lf])
+    assert torch.equal(out.cpu(), ref.cpu())
+
+
+def test_sampler_matches_reference():
+    B, V = 24, 32000
+    logits = torch.randn(B, V, device=DEV, generator=_g(23)) * 3
+    g = torch.Generator().manual_seed(0)
+    temps = torch.rand(B, generator=g) * 1.5
+    temps[0] = 0.0
+    top_k = torch.randint(0, 100, (B,), generator=g).int()
+    top_p = torch.rand(B, generator=g) * 0.5 + 0.5
+    top_p[1] = 1.0
+    min_p = torch.rand(B, generator=g) * 0.1
+    min_p[2] = 0.0
+    seeds = torch.randint(0, 2 ** 31, (B,), generator=g)
+    offs = torch.randint(0, 1000, (B,), generator=g)
+    out = ops.sample(logits, temps.to(DEV), top_k.to(DEV), top_p.to(DEV), min_p.to(DEV), seeds.to(DEV), offs.to(DEV))
+    ref = R.sample(logits.cpu(), temps, top_k, top_p, min_p, seeds, offs)
+    agree = (out.cpu() == ref).float().mean().item()
+    assert agree >= 0.95, agree
+
+
+def test_penalties():
+    B, V = 4, 500
+    logits = torch.randn(B, V, device=DEV, generator=_g(24))
+    l2 = logits.clone().cpu()
+    trip = torch.tensor([[0, 5, 2], [0, 7, 0], [2, 9, 1], [3, 499, 3]], dtype=torch.int32)
+    rep = torch.tensor([1.3, 1.0, 1.1, 0.9])
+    fr = torch.tensor([0.5, 0.0, 0.2, 0.1])
+    pr = torch.tensor([0.3, 0.0, 0.1, 0.0])
+    ops.apply_penalties(logits, trip.to(DEV), rep.to(DEV), fr.to(DEV), pr.to(DEV))
+    R.apply_penalties_triples(l2, trip, rep, fr, pr)
+    torch.testing.assert_close(logits.cpu(), l2)
