@@ -1,0 +1,160 @@
+"""Per-kernel timing at Llama-3-8B serving shapes against the measured B200 roofline.
+
+Every number: median of CUDA-event timings on the launching stream after warm-up, with a
+256 MB buffer written between iterations to flush the 126 MB L2. Fractions are of the measured
+peaks in MEASURED_PEAKS.json (HBM copy GB/s, cuBLAS bf16 TFLOP/s burst). cuBLAS (torch.matmul)
+timings are printed beside our GEMMs as a reference point only.
+
+    python benchmarks/kernel_bench.py [--only gemm,attn,norm] [--json out.jsonl]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, REPO)
+
+from gollek_b200 import ops  # noqa: E402
+from gollek_b200.utils.timing import time_cuda  # noqa: E402
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "of measured"
+    return 6650.0, 1590.0, "of fallback"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,attn,norm,sample")
+    ap.add_argument("--json", default=None)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    only = set(args.only.split(","))
+    hbm, tflops, tag = peaks()
+    dev = "cuda"
+    torch.manual_seed(0)
+    rows = []
+    flush = 256 << 20
+
+    def rec(name, ms, flops=0.0, nbytes=0.0, extra=None):
+        r = {"kernel": name, "ms": round(ms, 4)}
+        if flops:
+            r["tflops"] = round(flops / ms / 1e9, 1)
+            r["frac_compute"] = round(flops / ms / 1e9 / tflops, 3)
+        if nbytes:
+            r["gbs"] = round(nbytes / ms / 1e6, 1)
+            r["frac_hbm"] = round(nbytes / ms / 1e6 / hbm, 3)
+        if flops or nbytes:
+            t_roof = max(flops / (tflops * 1e12), nbytes / (hbm * 1e9)) * 1e3
+            r["frac_roofline"] = round(t_roof / ms, 3)
+        if extra:
+            r.update(extra)
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+
+    if "gemm" in only:
+        shapes = [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up_swiglu", 28672, 4096),
+                  ("down", 4096, 14336), ("lm_head", 128256, 4096)]
+        for M in (64, 256, 1024, 8192):
+            for name, N, K in shapes:
+                if name == "lm_head" and M > 256:
+                    continue
+                a = torch.randn(M, K, device=dev).bfloat16()
+                w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+                sw = name.endswith("swiglu")
+                out = torch.empty(M, N // 2 if sw else N, device=dev, dtype=torch.bfloat16)
+                fn = (lambda: ops.linear_swiglu(a, w, out=out)) if sw else (lambda: ops.linear(a, w, out=out))
+                ms = time_cuda(fn, iters=args.iters, flush_bytes=flush)
+                flops = 2.0 * M * N * K
+                nbytes = 2.0 * (M * K + N * K + M * (N // 2 if sw else N))
+                cub = time_cuda(lambda: torch.matmul(a, w.t()), iters=args.iters, flush_bytes=flush)
+                bn = ops.cuda_ext().gemm_pick_bn(M, N, 2 if sw else 0)
+                rec(f"gemm_{name}_M{M}", ms, flops, nbytes, {"shape": [M, N, K], "bn": bn,
+                                                              "cublas_ms": round(cub, 4)})
+    if "attn" in only:
+        Hq, Hk, D, bs = 32, 8, 128, 16
+        for B, ctx in ((256, 1200), (64, 4096), (8, 2048), (1, 8192)):
+            nblk = (ctx + bs - 1) // bs
+            NB = B * nblk
+            cache = torch.randn(NB, 2, Hk, bs, D, device=dev).bfloat16()
+            bt = torch.randperm(NB, device=dev).int().view(B, nblk)
+            sl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+            q = torch.randn(B, Hq, D, device=dev).bfloat16()
+            splits = ops.decode_splits(B, Hk, ctx)
+            ws = torch.empty(B * Hq * splits * (D + 2), device=dev)
+            out = torch.empty_like(q)
+            ms = time_cuda(lambda: ops.paged_decode_attention(q, cache, bt, sl, 1 / math.sqrt(D), splits, out=out,
+                                                              workspace=ws), iters=args.iters, flush_bytes=flush)
+            nbytes = B * ctx * Hk * D * 2 * 2
+            flops = 4.0 * B * ctx * Hq * D
+            rec(f"attn_decode_B{B}_ctx{ctx}", ms, flops, nbytes, {"splits": splits})
+        for nseq, L in ((4, 2048), (8, 1024), (1, 8192)):
+            T = nseq * L
+            nblk = L // bs
+            NB = nseq * nblk
+            cache = torch.randn(NB, 2, Hk, bs, D, device=dev).bfloat16()
+            bt = torch.arange(NB, device=dev).int().view(nseq, nblk)
+            sl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
+            qs = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+            q = torch.randn(T, Hq, D, device=dev).bfloat16()
+            tiles = ops.prefill_tiles(qs.tolist()).to(dev)
+            out = torch.empty_like(q)
+            ms = time_cuda(lambda: ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D), tiles=tiles,
+                                                               out=out), iters=args.iters, flush_bytes=flush)
+            flops = 4.0 * nseq * (L * L / 2) * Hq * D
+            nbytes = 2.0 * (2 * T * Hq * D + 2 * T * Hk * D)
+            rec(f"attn_prefill_{nseq}x{L}", ms, flops, nbytes)
+    if "norm" in only:
+        d = 4096
+        for T in (256, 8192):
+            x = torch.randn(T, d, device=dev).bfloat16()
+            r = torch.randn(T, d, device=dev).bfloat16()
+            w = torch.ones(d, device=dev).bfloat16()
+            out = torch.empty_like(x)
+            ms = time_cuda(lambda: ops.fused_add_rms_norm(x, r, w, 1e-5, out=out), iters=args.iters, flush_bytes=flush)
+            rec(f"fused_add_rms_norm_T{T}", ms, 0, 2.0 * 4 * T * d)
+            from gollek_b200.config import preset
+            from gollek_b200.models.reference import rope_cos_sin
+            cs = rope_cos_sin(preset("llama-3-8b"), 8192, device=dev)
+            qkv = torch.randn(T, 6144, device=dev).bfloat16()
+            pos = torch.arange(T, device=dev).int() % 8000
+            cache = torch.zeros(T // 16 + 1, 2, 8, 16, 128, device=dev).bfloat16()
+            slots = torch.arange(T, device=dev).int()
+            qo = torch.empty(T, 32, 128, device=dev).bfloat16()
+            ms = time_cuda(lambda: ops.rope_kv_write(qkv, pos, cs, cache, slots, 32, 8, 128, q_out=qo),
+                           iters=args.iters, flush_bytes=flush)
+            rec(f"rope_kv_write_T{T}", ms, 0, 2.0 * (T * 6144 + T * 4096 + T * 2048))
+    if "sample" in only:
+        for B in (256,):
+            V = 128256
+            logits = torch.randn(B, V, device=dev).bfloat16()
+            out = torch.empty(B, dtype=torch.int64, device=dev)
+            ms = time_cuda(lambda: ops.argmax(logits, out=out), iters=args.iters, flush_bytes=flush)
+            rec(f"argmax_B{B}_V{V}", ms, 0, 2.0 * B * V)
+            lf = logits.float()
+            t = torch.full((B,), 0.8, device=dev)
+            k = torch.full((B,), 50, dtype=torch.int32, device=dev)
+            p = torch.full((B,), 0.9, device=dev)
+            mp = torch.zeros(B, device=dev)
+            sd = torch.arange(B, device=dev)
+            off = torch.zeros(B, dtype=torch.int64, device=dev)
+            ms = time_cuda(lambda: ops.sample(lf, t, k, p, mp, sd, off, out=out), iters=args.iters, flush_bytes=flush)
+            rec(f"sample_topk_topp_B{B}_V{V}", ms, 0, 4.0 * B * V)
+    if args.json:
+        with open(args.json, "w") as f:
+            for r in rows:
+                f.write(json.dumps(r) + "\n")
+    print(f"# peaks: HBM {hbm} GB/s, bf16 {tflops} TFLOP/s ({tag})")
+
+
+if __name__ == "__main__":
+    main()

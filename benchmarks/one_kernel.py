@@ -1,0 +1,65 @@
+"""Run one hot kernel a few times on one shape (small, self-terminating case for ncu captures).
+
+    python benchmarks/one_kernel.py gemm --M 8192 --N 28672 --K 4096 [--swiglu] [--reps 3]
+    python benchmarks/one_kernel.py decode --B 256 --ctx 1200
+    python benchmarks/one_kernel.py prefill --nseq 4 --L 2048
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from gollek_b200 import ops  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kind", choices=["gemm", "decode", "prefill"])
+    ap.add_argument("--M", type=int, default=8192)
+    ap.add_argument("--N", type=int, default=28672)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--bn", type=int, default=0)
+    ap.add_argument("--swiglu", action="store_true")
+    ap.add_argument("--B", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=1200)
+    ap.add_argument("--nseq", type=int, default=4)
+    ap.add_argument("--L", type=int, default=2048)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    dev = "cuda"
+    if a.kind == "gemm":
+        x = torch.randn(a.M, a.K, device=dev).bfloat16()
+        w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
+        for _ in range(a.reps):
+            (ops.linear_swiglu(x, w, bn=a.bn) if a.swiglu else ops.linear(x, w, bn=a.bn))
+    elif a.kind == "decode":
+        Hq, Hk, D, bs = 32, 8, 128, 16
+        nblk = (a.ctx + bs - 1) // bs
+        cache = torch.randn(a.B * nblk, 2, Hk, bs, D, device=dev).bfloat16()
+        bt = torch.randperm(a.B * nblk, device=dev).int().view(a.B, nblk)
+        sl = torch.full((a.B,), a.ctx, dtype=torch.int32, device=dev)
+        q = torch.randn(a.B, Hq, D, device=dev).bfloat16()
+        for _ in range(a.reps):
+            ops.paged_decode_attention(q, cache, bt, sl, 1 / math.sqrt(D), ops.decode_splits(a.B, Hk, a.ctx))
+    else:
+        Hq, Hk, D, bs = 32, 8, 128, 16
+        T = a.nseq * a.L
+        nblk = a.L // bs
+        cache = torch.randn(a.nseq * nblk, 2, Hk, bs, D, device=dev).bfloat16()
+        bt = torch.arange(a.nseq * nblk, device=dev).int().view(a.nseq, nblk)
+        sl = torch.full((a.nseq,), a.L, dtype=torch.int32, device=dev)
+        qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
+        q = torch.randn(T, Hq, D, device=dev).bfloat16()
+        for _ in range(a.reps):
+            ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D))
+    torch.cuda.synchronize()
+    print("ok")
+
+
+if __name__ == "__main__":
+    main()

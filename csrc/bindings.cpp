@@ -1,25 +1,224 @@
 // Python bindings of the sm_100a kernels (module gollek_b200_C).
+//
+// All torch-tensor validation happens here (compiled by the host compiler); the .cu files
+// only see raw pointers, strides and the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
-void rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
-void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w, double eps);
+#include "kernels/launchers.h"
+
+using namespace gollek;
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16(const torch::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+void check_i32(const torch::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kInt, name, " must be int32");
+}
+void check_same_device(const torch::Tensor& a, const torch::Tensor& b) {
+  TORCH_CHECK(a.device() == b.device(), "tensors on different devices");
+}
+
+void rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  check_bf16(w, "w");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 && w.is_contiguous(), "rms_norm: row-major 2-D");
+  TORCH_CHECK(out.sizes() == x.sizes() && w.numel() == x.size(1), "rms_norm: shape mismatch");
+  launch_rms_norm(out.data_ptr(), x.data_ptr(), nullptr, w.data_ptr(), x.size(0), x.size(1), x.stride(0),
+                  out.stride(0), (float)eps, cur_stream());
+}
+
+void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w,
+                            double eps) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  TORCH_CHECK(residual.is_contiguous() && residual.sizes() == x.sizes(), "residual must be contiguous [T, d]");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 && w.is_contiguous(), "rms_norm: row-major 2-D");
+  TORCH_CHECK(out.sizes() == x.sizes() && w.numel() == x.size(1), "rms_norm: shape mismatch");
+  launch_rms_norm(out.data_ptr(), x.data_ptr(), residual.data_ptr(), w.data_ptr(), x.size(0), x.size(1),
+                  x.stride(0), out.stride(0), (float)eps, cur_stream());
+}
+
 void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
                        c10::optional<torch::Tensor> cache, c10::optional<torch::Tensor> slots, int64_t H, int64_t Hk,
-                       int64_t D);
-void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table);
-void silu_mul_out(torch::Tensor out, torch::Tensor x);
+                       int64_t D) {
+  check_bf16(qkv, "qkv");
+  check_bf16(q_out, "q_out");
+  check_i32(positions, "positions");
+  check_cuda(cos_sin, "cos_sin");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == D,
+              "cos_sin must be fp32 [max_pos, head_dim]");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (H + 2 * Hk) * D, "qkv shape mismatch");
+  TORCH_CHECK(qkv.stride(0) % 8 == 0, "qkv row pitch must keep 16-byte alignment");
+  const int T = qkv.size(0);
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == (int64_t)T * H * D, "q_out must be contiguous [T, H, D]");
+  TORCH_CHECK(positions.numel() >= T, "positions too short");
+  void* cp = nullptr;
+  const int* sp = nullptr;
+  int bs = 16;
+  if (cache.has_value() && slots.has_value()) {
+    check_bf16(*cache, "kv_cache");
+    check_i32(*slots, "slots");
+    TORCH_CHECK(cache->dim() == 5 && cache->size(1) == 2 && cache->size(2) == Hk && cache->size(4) == D,
+                "kv cache must be [blocks, 2, Hk, block_size, D]");
+    TORCH_CHECK(cache->is_contiguous() && slots->numel() >= T, "cache contiguous, enough slots");
+    cp = cache->data_ptr();
+    sp = slots->data_ptr<int>();
+    bs = cache->size(3);
+  }
+  launch_rope_kv_write(q_out.data_ptr(), qkv.data_ptr(), positions.data_ptr<int>(), cos_sin.data_ptr<float>(), cp,
+                       sp, T, H, Hk, D, bs, qkv.stride(0), (int)cos_sin.size(0), cur_stream());
+}
+
+void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
+  check_bf16(table, "table");
+  check_bf16(out, "out");
+  check_i32(ids, "ids");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && out.size(0) == ids.size(0) &&
+                  out.size(1) == table.size(1),
+              "embedding: shapes");
+  launch_embedding(out.data_ptr(), ids.data_ptr<int>(), table.data_ptr(), ids.size(0), table.size(1), table.size(0),
+                   cur_stream());
+}
+
+void silu_mul_out(torch::Tensor out, torch::Tensor x) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && out.size(1) * 2 == x.size(1), "silu_mul: shapes");
+  launch_silu_mul(out.data_ptr(), x.data_ptr(), x.size(0), x.size(1) / 2, cur_stream());
+}
+
 void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                                 torch::Tensor seq_lens, double scale, int64_t num_splits,
-                                c10::optional<torch::Tensor> workspace);
+                                c10::optional<torch::Tensor> workspace) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(cache, "kv_cache");
+  check_i32(block_tables, "block_tables");
+  check_i32(seq_lens, "seq_lens");
+  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2), "q must be [B, H, D] with packed heads");
+  TORCH_CHECK(out.is_contiguous() && out.sizes() == q.sizes(), "out must be contiguous like q");
+  TORCH_CHECK(cache.is_contiguous() && cache.dim() == 5 && cache.size(4) == q.size(2), "cache [NB, 2, Hk, bs, D]");
+  TORCH_CHECK(block_tables.stride(1) == 1 && block_tables.size(0) >= q.size(0) && seq_lens.numel() >= q.size(0),
+              "block_tables [B, max_blocks] row-major");
+  const int B = q.size(0), H = q.size(1), D = q.size(2);
+  num_splits = std::max<int64_t>(1, num_splits);
+  float* po = nullptr;
+  float* pml = nullptr;
+  if (num_splits > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->is_cuda() && workspace->scalar_type() == at::kFloat &&
+                    workspace->numel() >= (int64_t)B * H * num_splits * (D + 2),
+                "decode attention: fp32 workspace too small for split-KV");
+    po = workspace->data_ptr<float>();
+    pml = po + (int64_t)B * H * num_splits * D;
+  }
+  launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(), block_tables.data_ptr<int>(),
+                      block_tables.stride(0), seq_lens.data_ptr<int>(), B, H, cache.size(2), D, cache.size(3),
+                      (int)num_splits, (float)scale, po, pml, cur_stream());
+}
+
 void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
-                                 torch::Tensor seq_lens, torch::Tensor query_start, torch::Tensor tiles, double scale);
+                                 torch::Tensor seq_lens, torch::Tensor query_start, torch::Tensor tiles,
+                                 double scale) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(cache, "kv_cache");
+  check_i32(block_tables, "block_tables");
+  check_i32(seq_lens, "seq_lens");
+  check_i32(query_start, "query_start");
+  check_i32(tiles, "tiles");
+  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2), "q must be [T, H, D]");
+  TORCH_CHECK(out.dim() == 3 && out.stride(2) == 1 && out.stride(1) == out.size(2) && out.sizes() == q.sizes(),
+              "out must be [T, H, D]");
+  TORCH_CHECK(cache.is_contiguous() && cache.dim() == 5 && cache.size(4) == q.size(2), "cache [NB, 2, Hk, bs, D]");
+  TORCH_CHECK(block_tables.stride(1) == 1 && tiles.is_contiguous() && query_start.is_contiguous(), "metadata layout");
+  launch_paged_prefill(out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), cache.data_ptr(),
+                       block_tables.data_ptr<int>(), block_tables.stride(0), seq_lens.data_ptr<int>(),
+                       query_start.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), q.size(1), cache.size(2),
+                       q.size(2), cache.size(3), (float)scale, cur_stream());
+}
+
 void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
-                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit);
-void argmax_out(torch::Tensor out, torch::Tensor logits);
+                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(out, "out");
+  check_same_device(a, b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: shape mismatch");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: K-major operands, row-major out");
+  const int M = a.size(0), N = b.size(0), K = a.size(1);
+  TORCH_CHECK(out.size(0) == M, "gemm: out rows");
+  if (epi == kEpiSwiglu) {
+    TORCH_CHECK(out.size(1) == N / 2, "gemm swiglu: out [M, N/2]");
+  } else {
+    TORCH_CHECK(out.size(1) == N, "gemm: out [M, N]");
+  }
+  const void* rp = nullptr;
+  int64_t ldr = 0;
+  if (epi == kEpiResidual) {
+    TORCH_CHECK(residual.has_value(), "gemm residual: residual tensor required");
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->stride(1) == 1 && residual->size(0) == M && residual->size(1) == N, "residual [M, N]");
+    rp = residual->data_ptr();
+    ldr = residual->stride(0);
+  }
+  uint32_t* st = nullptr;
+  if (status.has_value()) {
+    check_cuda(*status, "status");
+    st = reinterpret_cast<uint32_t*>(status->data_ptr());
+  }
+  launch_gemm_bf16(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), rp, ldr, M,
+                   N, K, (int)epi, (int)bn, st, (int)grid_limit, cur_stream());
+}
+
+void argmax_out(torch::Tensor out, torch::Tensor logits) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "argmax: [B, V] logits");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.numel() >= logits.size(0), "argmax: int64 output");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16, "argmax: fp32/bf16");
+  launch_argmax(out.data_ptr<int64_t>(), logits.data_ptr(), logits.scalar_type() == at::kBFloat16, logits.size(0),
+                logits.size(1), logits.stride(0), cur_stream());
+}
+
 void apply_penalties_(torch::Tensor logits, torch::Tensor triples, torch::Tensor rep, torch::Tensor freq,
-                      torch::Tensor pres);
+                      torch::Tensor pres) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "penalties: fp32 logits");
+  check_i32(triples, "triples");
+  TORCH_CHECK(triples.is_contiguous() && (triples.numel() == 0 || triples.size(1) == 3), "triples [n, 3]");
+  launch_penalties(logits.data_ptr<float>(), logits.stride(0), triples.data_ptr<int>(), triples.size(0),
+                   rep.data_ptr<float>(), freq.data_ptr<float>(), pres.data_ptr<float>(), cur_stream());
+}
+
 void sample_out(torch::Tensor out, torch::Tensor logits, torch::Tensor temps, torch::Tensor top_ks,
-                torch::Tensor top_ps, torch::Tensor min_ps, torch::Tensor seeds, torch::Tensor offsets);
+                torch::Tensor top_ps, torch::Tensor min_ps, torch::Tensor seeds, torch::Tensor offsets) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: [B, V] logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16, "sample: fp32/bf16");
+  TORCH_CHECK(temps.scalar_type() == at::kFloat && top_ps.scalar_type() == at::kFloat &&
+                  min_ps.scalar_type() == at::kFloat && top_ks.scalar_type() == at::kInt &&
+                  seeds.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong &&
+                  out.scalar_type() == at::kLong,
+              "sample: parameter dtypes");
+  launch_sample(out.data_ptr<int64_t>(), logits.data_ptr(), logits.scalar_type() == at::kBFloat16, logits.size(0),
+                logits.size(1), logits.stride(0), temps.data_ptr<float>(), top_ks.data_ptr<int>(),
+                top_ps.data_ptr<float>(), min_ps.data_ptr<float>(), seeds.data_ptr<int64_t>(),
+                offsets.data_ptr<int64_t>(), cur_stream());
+}
+
+}  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "gollek_b200 sm_100a kernels";
@@ -31,6 +230,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attention", &paged_decode_attention_out, "paged decode attention (K3)");
   m.def("paged_prefill_attention", &paged_prefill_attention_out, "paged prefill attention (K4)");
   m.def("gemm_bf16", &gemm_bf16_out, "tcgen05 bf16 GEMM with fused epilogues (K5/K8)");
+  m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
+  m.def("num_sms", &device_num_sms);
   m.def("argmax", &argmax_out, "greedy argmax (K11)");
   m.def("apply_penalties", &apply_penalties_, "repetition/frequency/presence penalties (K11)");
   m.def("sample", &sample_out, "top-k/min-p/top-p sampling (K11)");

@@ -13,6 +13,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <stdexcept>
+#include <string>
+
 #define GOLLEK_DEVICE __device__ __forceinline__
 
 #ifndef GOLLEK_SPIN_LIMIT
@@ -301,9 +304,10 @@ GOLLEK_DEVICE bool wait_flag_geq(const uint32_t* flag, uint32_t target, uint32_t
 
 }  // namespace gollek
 
-#define GOLLEK_CUDA_CHECK(expr)                                                               \
-  do {                                                                                        \
-    cudaError_t _e = (expr);                                                                  \
-    TORCH_CHECK(_e == cudaSuccess, "CUDA error: ", cudaGetErrorString(_e), " at ", __FILE__, \
-                ":", __LINE__);                                                               \
+#define GOLLEK_CUDA_CHECK(expr)                                                                   \
+  do {                                                                                            \
+    cudaError_t _e = (expr);                                                                      \
+    if (_e != cudaSuccess)                                                                        \
+      throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(_e) + " at " +   \
+                               __FILE__ + ":" + std::to_string(__LINE__));                       \
   } while (0)

@@ -4,9 +4,9 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include <torch/extension.h>
-
 #include <mutex>
+#include <stdexcept>
+#include <string>
 
 namespace gollek {
 
@@ -21,8 +21,8 @@ inline EncodeTiledFn get_encode_tiled() {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
-                "cannot resolve cuTensorMapEncodeTiled from the CUDA driver");
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cannot resolve cuTensorMapEncodeTiled from the CUDA driver");
     fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
@@ -33,8 +33,8 @@ inline EncodeTiledFn get_encode_tiled() {
 inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows,
                                 uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols,
                                 CUtensorMapSwizzle swizzle) {
-  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
-  TORCH_CHECK((ld * elem_bytes) % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base address must be 16-byte aligned");
+  if ((ld * elem_bytes) % 16 != 0) throw std::runtime_error("TMA row pitch must be a multiple of 16 bytes");
   CUtensorMap m;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * (uint64_t)elem_bytes};
@@ -43,7 +43,7 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
   CUresult r = get_encode_tiled()(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
   return m;
 }
 

@@ -13,10 +13,8 @@
 // Reference semantics: core/optimization/gollek-plugin-paged-attention/…/PagedAttentionCpuFallback.java:37-124
 // (decode), runner/safetensor/gollek-safetensor-engine/…/attention/PagedAttentionVectorAPI.java:20-127
 // (online softmax over blocks, GQA, causal). KV layout per layer: [blocks, 2, Hk, block_size, D].
-#include <ATen/cuda/CUDAContext.h>
-#include <torch/extension.h>
-
 #include "../common/common.cuh"
+#include "launchers.h"
 
 using namespace gollek;
 
@@ -458,52 +456,37 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
 }
 
 template <int D, int G>
-void launch_decode(torch::Tensor& out, const torch::Tensor& q, const torch::Tensor& cache, const torch::Tensor& bt,
-                   const torch::Tensor& lens, int num_splits, float scale_log2, float* po, float* pml,
-                   cudaStream_t stream) {
-  const int B = q.size(0), Hk = cache.size(2), BS = cache.size(3);
-  TORCH_CHECK(BS == 16, "decode attention is built for block_size 16");
+void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cache, const int* bt, int bt_stride,
+                     const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po, float* pml,
+                     cudaStream_t s) {
   dim3 grid(B, Hk, num_splits);
-  paged_decode_kernel<D, G, 16><<<grid, kDecodeWarps * 32, 0, stream>>>(
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), po, pml,
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(cache.data_ptr()),
-      bt.data_ptr<int>(), bt.stride(0), lens.data_ptr<int>(), Hk, num_splits, scale_log2, q.stride(0));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  paged_decode_kernel<D, G, 16><<<grid, kDecodeWarps * 32, 0, s>>>(
+      reinterpret_cast<__nv_bfloat16*>(out), po, pml, reinterpret_cast<const __nv_bfloat16*>(q),
+      reinterpret_cast<const __nv_bfloat16*>(cache), bt, bt_stride, lens, Hk, num_splits, scale_log2, q_stride);
+  check_launch("paged_decode_attention");
   if (num_splits > 1) {
-    decode_combine_kernel<D><<<B * Hk * G, D, 0, stream>>>(reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), po,
-                                                           pml, num_splits);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    decode_combine_kernel<D><<<B * Hk * G, D, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml, num_splits);
+    check_launch("paged_decode_attention combine");
   }
 }
 
 }  // namespace
 
-// Split-KV partial buffers live in `workspace` (fp32, >= B*H*S*(D+2) floats) when num_splits > 1.
-void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
-                                torch::Tensor seq_lens, double scale, int64_t num_splits,
-                                c10::optional<torch::Tensor> workspace) {
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "bf16 inputs");
-  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2), "q must be [B, H, D] with packed heads");
-  TORCH_CHECK(out.is_contiguous() && cache.is_contiguous(), "out/cache contiguous");
-  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt, "int32 metadata");
-  const int B = q.size(0), H = q.size(1), D = q.size(2), Hk = cache.size(2);
-  TORCH_CHECK(H % Hk == 0, "H must be a multiple of Hk");
+namespace gollek {
+
+void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, const int* block_tables,
+                         int bt_stride, const int* seq_lens, int B, int H, int Hk, int D, int block_size,
+                         int num_splits, float scale, float* part_o, float* part_ml, cudaStream_t s) {
+  throw_if(block_size != 16, "decode attention is built for block_size 16");
+  throw_if(H % Hk != 0, "H must be a multiple of Hk");
+  throw_if(num_splits > 1 && (part_o == nullptr || part_ml == nullptr), "split-KV decode needs a workspace");
   if (B == 0) return;
   const int G = H / Hk;
-  num_splits = std::max<int64_t>(1, num_splits);
-  float* po = nullptr;
-  float* pml = nullptr;
-  if (num_splits > 1) {
-    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
-                    workspace->numel() >= (int64_t)B * H * num_splits * (D + 2),
-                "decode attention: fp32 workspace too small for split-KV");
-    po = workspace->data_ptr<float>();
-    pml = po + (int64_t)B * H * num_splits * D;
-  }
-  const float sl = (float)scale * kLog2e;
-  auto stream = at::cuda::getCurrentCUDAStream();
-#define GOLLEK_DECODE_CASE(DD, GG) \
-  if (D == DD && G == GG) return launch_decode<DD, GG>(out, q, cache, block_tables, seq_lens, num_splits, sl, po, pml, stream);
+  const float sl = scale * kLog2e;
+#define GOLLEK_DECODE_CASE(DD, GG)                                                                            \
+  if (D == DD && G == GG)                                                                                     \
+    return launch_decode_t<DD, GG>(out, q, q_stride, cache, block_tables, bt_stride, seq_lens, B, Hk, num_splits, \
+                                   sl, part_o, part_ml, s);
   GOLLEK_DECODE_CASE(128, 1)
   GOLLEK_DECODE_CASE(128, 2)
   GOLLEK_DECODE_CASE(128, 4)
@@ -516,40 +499,34 @@ void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tenso
   GOLLEK_DECODE_CASE(32, 4)
   GOLLEK_DECODE_CASE(32, 8)
 #undef GOLLEK_DECODE_CASE
-  TORCH_CHECK(false, "decode attention: unsupported head_dim/group ", D, "/", G);
+  throw_if(true, "decode attention: unsupported head_dim/group " + std::to_string(D) + "/" + std::to_string(G));
 }
 
-void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
-                                 torch::Tensor seq_lens, torch::Tensor query_start, torch::Tensor tiles,
-                                 double scale) {
-  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && cache.scalar_type() == at::kBFloat16, "bf16 inputs");
-  TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2), "q must be [T, H, D]");
-  TORCH_CHECK(out.dim() == 3 && out.stride(2) == 1 && out.stride(1) == out.size(2), "out must be [T, H, D]");
-  TORCH_CHECK(tiles.scalar_type() == at::kInt && query_start.scalar_type() == at::kInt, "int32 metadata");
-  TORCH_CHECK(cache.is_contiguous(), "cache contiguous");
-  const int H = q.size(1), D = q.size(2), Hk = cache.size(2), BS = cache.size(3);
-  const int ntiles = tiles.size(0);
+void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
+                          const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
+                          const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
+                          cudaStream_t s) {
+  throw_if(H % Hk != 0, "H must be a multiple of Hk");
   if (ntiles == 0) return;
-  const float sl = (float)scale * kLog2e;
-  auto stream = at::cuda::getCurrentCUDAStream();
+  const float sl = scale * kLog2e;
   dim3 grid(ntiles, H);
-#define GOLLEK_PREFILL_CASE(DD)                                                                                     \
-  if (D == DD) {                                                                                                  \
-    const size_t smem = (size_t)(kPfBM + 4 * kPfBN) * DD * 2;                                                    \
-    auto kern = paged_prefill_kernel<DD>;                                                                         \
-    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));        \
-    kern<<<grid, kPfThreads, smem, stream>>>(                                                                     \
-        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),                                          \
-        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),                                        \
-        reinterpret_cast<const __nv_bfloat16*>(cache.data_ptr()), block_tables.data_ptr<int>(),                   \
-        block_tables.stride(0), seq_lens.data_ptr<int>(), query_start.data_ptr<int>(), tiles.data_ptr<int>(), H, \
-        Hk, BS, sl);                                                                                              \
-    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                               \
-    return;                                                                                                       \
+#define GOLLEK_PREFILL_CASE(DD)                                                                               \
+  if (D == DD) {                                                                                            \
+    const size_t smem = (size_t)(kPfBM + 4 * kPfBN) * DD * 2;                                              \
+    auto kern = paged_prefill_kernel<DD>;                                                                   \
+    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));  \
+    kern<<<grid, kPfThreads, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(out), out_stride,                  \
+                                        reinterpret_cast<const __nv_bfloat16*>(q), q_stride,                \
+                                        reinterpret_cast<const __nv_bfloat16*>(cache), block_tables,        \
+                                        bt_stride, seq_lens, query_start, tiles, H, Hk, block_size, sl);    \
+    check_launch("paged_prefill_attention");                                                                \
+    return;                                                                                                 \
   }
   GOLLEK_PREFILL_CASE(128)
   GOLLEK_PREFILL_CASE(64)
   GOLLEK_PREFILL_CASE(32)
 #undef GOLLEK_PREFILL_CASE
-  TORCH_CHECK(false, "prefill attention: unsupported head_dim ", D);
+  throw_if(true, "prefill attention: unsupported head_dim " + std::to_string(D));
 }
+
+}  // namespace gollek

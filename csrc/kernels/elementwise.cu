@@ -7,10 +7,8 @@
 // Reference math: RMSNorm kernel/cuda/gollek-kernel-cuda/…/cuda/binding/CudaCpuFallback.java:181-211,
 // SiLU·up :261-290, RoPE runner/safetensor/gollek-safetensor-engine/…/attention/RopeFrequencyCache.java:49-107,
 // paged KV write …/attention/FlashAttentionKernel.java:166-194.
-#include <ATen/cuda/CUDAContext.h>
-#include <torch/extension.h>
-
 #include "../common/common.cuh"
+#include "launchers.h"
 
 using namespace gollek;
 
@@ -72,28 +70,6 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* _
       orow[idx] = float_to_bf16x8(v[i]);
     }
   }
-}
-
-template <bool ADD>
-void launch_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor* residual, torch::Tensor w, double eps) {
-  const int T = x.size(0), d = x.size(1);
-  TORCH_CHECK(d % 8 == 0 && d <= 8 * 4 * kNormThreads, "rms_norm: hidden size must be a multiple of 8, <= 8192");
-  TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "rms_norm: rows must be contiguous");
-  TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "rms_norm: row stride must keep 16-byte alignment");
-  if (T == 0) return;
-  auto stream = at::cuda::getCurrentCUDAStream();
-  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
-  auto* rp = residual ? reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()) : nullptr;
-  auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
-  const int nvec = d / 8;
-  if (nvec <= kNormThreads)
-    rms_norm_kernel<1, ADD><<<T, kNormThreads, 0, stream>>>(o, xp, rp, wp, d, x.stride(0), out.stride(0), eps);
-  else if (nvec <= 2 * kNormThreads)
-    rms_norm_kernel<2, ADD><<<T, kNormThreads, 0, stream>>>(o, xp, rp, wp, d, x.stride(0), out.stride(0), eps);
-  else
-    rms_norm_kernel<4, ADD><<<T, kNormThreads, 0, stream>>>(o, xp, rp, wp, d, x.stride(0), out.stride(0), eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -171,78 +147,61 @@ __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
   *reinterpret_cast<uint4*>(out + (int64_t)t * d + i * 8) = float_to_bf16x8(o);
 }
 
-void check_bf16_cuda(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
-}
-
 }  // namespace
 
-void rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps) {
-  check_bf16_cuda(x, "x");
-  check_bf16_cuda(out, "out");
-  check_bf16_cuda(w, "w");
-  launch_rms_norm<false>(out, x, nullptr, w, eps);
-}
+namespace gollek {
 
-void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w,
-                            double eps) {
-  check_bf16_cuda(x, "x");
-  check_bf16_cuda(residual, "residual");
-  TORCH_CHECK(residual.is_contiguous(), "residual must be contiguous");
-  launch_rms_norm<true>(out, x, &residual, w, eps);
-}
-
-void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
-                       c10::optional<torch::Tensor> cache, c10::optional<torch::Tensor> slots, int64_t H,
-                       int64_t Hk, int64_t D) {
-  check_bf16_cuda(qkv, "qkv");
-  TORCH_CHECK(qkv.stride(1) == 1 && qkv.size(1) == (H + 2 * Hk) * D, "qkv shape mismatch");
-  TORCH_CHECK(positions.scalar_type() == at::kInt && cos_sin.scalar_type() == at::kFloat, "positions int32, cos_sin fp32");
-  TORCH_CHECK(D % 16 == 0 && cos_sin.size(1) == D, "head_dim must be a multiple of 16 and match cos_sin");
-  TORCH_CHECK(q_out.is_contiguous(), "q_out must be contiguous");
-  const int T = qkv.size(0);
+void launch_rms_norm(void* out, const void* x, void* residual, const void* w, int T, int d, int64_t x_stride,
+                     int64_t out_stride, float eps, cudaStream_t s) {
+  throw_if(d % 8 != 0 || d > 8 * 4 * kNormThreads, "rms_norm: hidden size must be a multiple of 8, <= 8192");
+  throw_if(x_stride % 8 != 0 || out_stride % 8 != 0, "rms_norm: row stride must keep 16-byte alignment");
   if (T == 0) return;
-  __nv_bfloat16* cp = nullptr;
-  const int* sp = nullptr;
-  int bs = 16;
-  if (cache.has_value() && slots.has_value()) {
-    check_bf16_cuda(*cache, "kv_cache");
-    TORCH_CHECK(cache->dim() == 5 && cache->size(1) == 2 && cache->size(2) == Hk && cache->size(4) == D,
-                "kv cache must be [blocks, 2, Hk, block_size, D]");
-    TORCH_CHECK(cache->is_contiguous() && slots->scalar_type() == at::kInt, "cache contiguous, slots int32");
-    cp = reinterpret_cast<__nv_bfloat16*>(cache->data_ptr());
-    sp = slots->data_ptr<int>();
-    bs = cache->size(3);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto* rp = reinterpret_cast<__nv_bfloat16*>(residual);
+  auto* wp = reinterpret_cast<const __nv_bfloat16*>(w);
+  const int nvec = d / 8;
+#define GOLLEK_NORM(V)                                                                                        \
+  if (rp) rms_norm_kernel<V, true><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps);   \
+  else rms_norm_kernel<V, false><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps);
+  if (nvec <= kNormThreads) {
+    GOLLEK_NORM(1)
+  } else if (nvec <= 2 * kNormThreads) {
+    GOLLEK_NORM(2)
+  } else {
+    GOLLEK_NORM(4)
   }
-  auto stream = at::cuda::getCurrentCUDAStream();
-  rope_kv_write_kernel<<<T, 128, 0, stream>>>(
-      reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
-      positions.data_ptr<int>(), cos_sin.data_ptr<float>(), cp, sp, H, Hk, D, bs, qkv.stride(0),
-      (int)cos_sin.size(0));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+#undef GOLLEK_NORM
+  check_launch("rms_norm");
 }
 
-void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
-  check_bf16_cuda(table, "table");
-  TORCH_CHECK(ids.scalar_type() == at::kInt && table.is_contiguous() && out.is_contiguous(), "embedding args");
-  const int T = ids.size(0), d = table.size(1);
-  TORCH_CHECK(d % 8 == 0, "embedding dim must be a multiple of 8");
+void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
+                          const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
+                          int max_pos, cudaStream_t s) {
+  throw_if(D % 16 != 0, "rope_kv_write: head_dim must be a multiple of 16");
   if (T == 0) return;
-  embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ids.data_ptr<int>(),
-      reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), d, (int)table.size(0));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  rope_kv_write_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(q_out),
+                                         reinterpret_cast<const __nv_bfloat16*>(qkv), positions, cos_sin,
+                                         reinterpret_cast<__nv_bfloat16*>(cache), slots, H, Hk, D, block_size,
+                                         qkv_stride, max_pos);
+  check_launch("rope_kv_write");
 }
 
-void silu_mul_out(torch::Tensor out, torch::Tensor x) {
-  check_bf16_cuda(x, "x");
-  TORCH_CHECK(x.is_contiguous() && out.is_contiguous(), "silu_mul: contiguous tensors");
-  const int T = x.size(0), d = x.size(1) / 2;
-  TORCH_CHECK(d % 8 == 0, "silu_mul: width must be a multiple of 16");
+void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s) {
+  throw_if(d % 8 != 0, "embedding: dim must be a multiple of 8");
+  if (T == 0) return;
+  embedding_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ids,
+                                     reinterpret_cast<const __nv_bfloat16*>(table), d, vocab);
+  check_launch("embedding");
+}
+
+void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s) {
+  throw_if(d % 8 != 0, "silu_mul: width must be a multiple of 16");
   if (T == 0) return;
   dim3 grid((d / 8 + 127) / 128, T);
-  silu_mul_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), d);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  silu_mul_kernel<<<grid, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out),
+                                       reinterpret_cast<const __nv_bfloat16*>(x), d);
+  check_launch("silu_mul");
 }
+
+}  // namespace gollek

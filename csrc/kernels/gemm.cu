@@ -21,17 +21,13 @@
 //
 // Every mbarrier wait is bounded (globaltimer deadline); on timeout the CTA records a status bit,
 // stops issuing, drains its own in-flight copies/MMAs (bounded) and frees its TMEM before returning.
-#include <ATen/cuda/CUDAContext.h>
-#include <torch/extension.h>
-
 #include "../common/common.cuh"
 #include "../common/tma_host.h"
+#include "launchers.h"
 
 using namespace gollek;
 
 namespace {
-
-enum Epi : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2 };
 
 template <int BN>
 struct GemmCfg {
@@ -283,31 +279,30 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int BN, int EPI>
-void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const torch::Tensor* res,
-                 uint32_t* status, int grid_limit) {
+void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
+                   int64_t ldr, int M, int N, int K, uint32_t* status, int grid_limit, cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
-  const int M = a.size(0), K = a.size(1), N = b.size(0);
-  CUtensorMap ta = make_tmap_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, a.stride(0), Cfg::BM,
-                                Cfg::BK, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = make_tmap_2d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, b.stride(0), BN, Cfg::BK,
+  CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, BN, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   auto kern = gemm_bf16_kernel<BN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_set = true;
-  }
+  GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
   const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
   int grid = std::min(tiles, num_sms());
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
-  auto stream = at::cuda::getCurrentCUDAStream();
-  kern<<<grid, 192, Cfg::SMEM, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
-                                         res ? reinterpret_cast<const __nv_bfloat16*>(res->data_ptr()) : nullptr,
-                                         res ? res->stride(0) : 0, M, N, K, status);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
+                                     reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, status);
+  check_launch("gemm_bf16");
 }
 
-int pick_bn(int M, int N, int epi) {
+}  // namespace
+
+namespace gollek {
+
+int device_num_sms() { return num_sms(); }
+
+int gemm_pick_bn(int M, int N, int epi) {
   const int num_m = (M + 127) / 128;
   const int sms = num_sms();
   if (epi == kEpiSwiglu) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
@@ -316,39 +311,20 @@ int pick_bn(int M, int N, int epi) {
   return 64;
 }
 
-}  // namespace
-
-// out[M, N] (or [M, N/2] for SwiGLU) = epi(a[M, K] @ b[N, K]^T). bn = 0 picks the tile width.
-void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
-                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit) {
-  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors");
-  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
-                  out.scalar_type() == at::kBFloat16,
-              "gemm: bf16 tensors");
-  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: shape mismatch");
-  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: K-major operands");
-  TORCH_CHECK(a.size(1) % 8 == 0, "gemm: K must be a multiple of 8");
-  const int M = a.size(0), N = b.size(0);
+void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
+                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, uint32_t* status,
+                      int grid_limit, cudaStream_t s) {
+  throw_if(K % 8 != 0, "gemm: K must be a multiple of 8");
+  throw_if(ldc % 8 != 0, "gemm: output row pitch must keep 16-byte alignment");
   if (M == 0) return;
-  TORCH_CHECK(out.stride(0) % 8 == 0, "gemm: output row pitch must keep 16-byte alignment");
-  if (epi == kEpiSwiglu) {
-    TORCH_CHECK(N % 128 == 0 && out.size(1) == N / 2, "gemm swiglu: N must be a multiple of 128, out [M, N/2]");
-  } else {
-    TORCH_CHECK(out.size(1) == N && N % 8 == 0, "gemm: out [M, N] with N % 8 == 0");
-  }
-  const torch::Tensor* res = nullptr;
-  if (epi == kEpiResidual) {
-    TORCH_CHECK(residual.has_value() && residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
-                    residual->stride(0) % 8 == 0,
-                "gemm residual: bf16 row-major residual required");
-    res = &residual.value();
-  }
-  uint32_t* st = status.has_value() ? reinterpret_cast<uint32_t*>(status->data_ptr()) : nullptr;
-  if (bn == 0) bn = pick_bn(M, N, (int)epi);
+  if (epi == kEpiSwiglu) throw_if(N % 128 != 0, "gemm swiglu: N must be a multiple of 128");
+  else throw_if(N % 8 != 0, "gemm: N must be a multiple of 8");
+  if (epi == kEpiResidual) throw_if(residual == nullptr || ldr % 8 != 0, "gemm residual: bf16 residual required");
+  if (bn == 0) bn = gemm_pick_bn(M, N, epi);
   if (epi == kEpiSwiglu && bn < 128) bn = 128;
-  const int gl = (int)grid_limit;
 #define GOLLEK_GEMM_CASE(BNV, EPIV) \
-  if (bn == BNV && epi == EPIV) return launch_gemm<BNV, EPIV>(a, b, out, res, st, gl);
+  if (bn == BNV && epi == EPIV)     \
+    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, residual, ldr, M, N, K, status, grid_limit, s);
   GOLLEK_GEMM_CASE(256, kEpiNone)
   GOLLEK_GEMM_CASE(128, kEpiNone)
   GOLLEK_GEMM_CASE(64, kEpiNone)
@@ -358,5 +334,7 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
   GOLLEK_GEMM_CASE(256, kEpiSwiglu)
   GOLLEK_GEMM_CASE(128, kEpiSwiglu)
 #undef GOLLEK_GEMM_CASE
-  TORCH_CHECK(false, "gemm: unsupported tile width ", bn, " / epilogue ", epi);
+  throw_if(true, "gemm: unsupported tile width " + std::to_string(bn) + " / epilogue " + std::to_string(epi));
 }
+
+}  // namespace gollek

@@ -1,0 +1,57 @@
+// Host launchers of the sm_100a kernels. The .cu files include only CUDA headers (fast nvcc
+// builds); argument checking against torch tensors lives in csrc/bindings.cpp. Launchers throw
+// std::runtime_error (surfaced as RuntimeError in Python) on invalid arguments or launch errors.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace gollek {
+
+inline void throw_if(bool bad, const std::string& msg) {
+  if (bad) throw std::runtime_error(msg);
+}
+inline void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---- elementwise (K1, K2, K13)
+void launch_rms_norm(void* out, const void* x, void* residual, const void* w, int T, int d, int64_t x_stride,
+                     int64_t out_stride, float eps, cudaStream_t s);
+void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
+                          const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
+                          int max_pos, cudaStream_t s);
+void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s);
+void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
+
+// ---- attention (K3, K4)
+void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, const int* block_tables,
+                         int bt_stride, const int* seq_lens, int B, int H, int Hk, int D, int block_size,
+                         int num_splits, float scale, float* part_o, float* part_ml, cudaStream_t s);
+void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
+                          const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
+                          const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
+                          cudaStream_t s);
+
+// ---- GEMM (K5, K8)
+enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2 };
+int gemm_pick_bn(int M, int N, int epi);
+void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
+                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, uint32_t* status,
+                      int grid_limit, cudaStream_t s);
+
+// ---- sampling (K11)
+void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s);
+void launch_penalties(float* logits, int64_t stride, const int* triples, int n, const float* rep, const float* freq,
+                      const float* pres, cudaStream_t s);
+void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, const float* temps,
+                   const int* top_ks, const float* top_ps, const float* min_ps, const int64_t* seeds,
+                   const int64_t* offsets, cudaStream_t s);
+
+int device_num_sms();
+
+}  // namespace gollek

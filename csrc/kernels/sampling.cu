@@ -10,10 +10,8 @@
 //
 // Reference sampler order: runner/safetensor/gollek-safetensor-engine/…/generation/TokenSampler.java:62-208
 // and the llama.cpp chain in runner/llamacpp/gollek-runner-llamacpp/…/LlamaHandles.java:174-203.
-#include <ATen/cuda/CUDAContext.h>
-#include <torch/extension.h>
-
 #include "../common/common.cuh"
+#include "launchers.h"
 
 using namespace gollek;
 
@@ -248,57 +246,36 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(int64_t* __restric
 
 }  // namespace
 
-void argmax_out(torch::Tensor out, torch::Tensor logits) {
-  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "argmax: [B, V] logits");
-  TORCH_CHECK(out.scalar_type() == at::kLong, "argmax: int64 output");
-  const int B = logits.size(0), V = logits.size(1);
+namespace gollek {
+
+void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s) {
   if (B == 0) return;
-  auto stream = at::cuda::getCurrentCUDAStream();
-  if (logits.scalar_type() == at::kFloat)
-    argmax_kernel<float><<<B, kSampThreads, 0, stream>>>(out.data_ptr<int64_t>(), logits.data_ptr<float>(), V,
-                                                         logits.stride(0));
-  else if (logits.scalar_type() == at::kBFloat16)
-    argmax_kernel<__nv_bfloat16><<<B, kSampThreads, 0, stream>>>(
-        out.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, logits.stride(0));
+  if (is_bf16)
+    argmax_kernel<__nv_bfloat16><<<B, kSampThreads, 0, s>>>(out, reinterpret_cast<const __nv_bfloat16*>(logits), V,
+                                                            stride);
   else
-    TORCH_CHECK(false, "argmax: fp32 or bf16 logits");
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+    argmax_kernel<float><<<B, kSampThreads, 0, s>>>(out, reinterpret_cast<const float*>(logits), V, stride);
+  check_launch("argmax");
 }
 
-void apply_penalties_(torch::Tensor logits, torch::Tensor triples, torch::Tensor rep, torch::Tensor freq,
-                      torch::Tensor pres) {
-  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "penalties: fp32 logits");
-  TORCH_CHECK(triples.scalar_type() == at::kInt && triples.is_contiguous(), "penalties: int32 triples");
-  const int n = triples.size(0);
+void launch_penalties(float* logits, int64_t stride, const int* triples, int n, const float* rep, const float* freq,
+                      const float* pres, cudaStream_t s) {
   if (n == 0) return;
-  penalties_kernel<<<(n + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), logits.stride(0), triples.data_ptr<int>(), n, rep.data_ptr<float>(),
-      freq.data_ptr<float>(), pres.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  penalties_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, stride, triples, n, rep, freq, pres);
+  check_launch("apply_penalties");
 }
 
-void sample_out(torch::Tensor out, torch::Tensor logits, torch::Tensor temps, torch::Tensor top_ks,
-                torch::Tensor top_ps, torch::Tensor min_ps, torch::Tensor seeds, torch::Tensor offsets) {
-  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "sample: [B, V] logits");
-  TORCH_CHECK(temps.scalar_type() == at::kFloat && top_ps.scalar_type() == at::kFloat &&
-                  min_ps.scalar_type() == at::kFloat && top_ks.scalar_type() == at::kInt &&
-                  seeds.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong,
-              "sample: parameter dtypes");
-  const int B = logits.size(0), V = logits.size(1);
+void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, const float* temps,
+                   const int* top_ks, const float* top_ps, const float* min_ps, const int64_t* seeds,
+                   const int64_t* offsets, cudaStream_t s) {
   if (B == 0) return;
-  auto stream = at::cuda::getCurrentCUDAStream();
-#define GOLLEK_SAMPLE_ARGS                                                                                  \
-  out.data_ptr<int64_t>(), lp, V, logits.stride(0), temps.data_ptr<float>(), top_ks.data_ptr<int>(),      \
-      top_ps.data_ptr<float>(), min_ps.data_ptr<float>(), seeds.data_ptr<int64_t>(), offsets.data_ptr<int64_t>()
-  if (logits.scalar_type() == at::kFloat) {
-    const float* lp = logits.data_ptr<float>();
-    sample_kernel<float><<<B, kSampThreads, 0, stream>>>(GOLLEK_SAMPLE_ARGS);
-  } else if (logits.scalar_type() == at::kBFloat16) {
-    const __nv_bfloat16* lp = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
-    sample_kernel<__nv_bfloat16><<<B, kSampThreads, 0, stream>>>(GOLLEK_SAMPLE_ARGS);
-  } else {
-    TORCH_CHECK(false, "sample: fp32 or bf16 logits");
-  }
-#undef GOLLEK_SAMPLE_ARGS
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (is_bf16)
+    sample_kernel<__nv_bfloat16><<<B, kSampThreads, 0, s>>>(out, reinterpret_cast<const __nv_bfloat16*>(logits), V,
+                                                            stride, temps, top_ks, top_ps, min_ps, seeds, offsets);
+  else
+    sample_kernel<float><<<B, kSampThreads, 0, s>>>(out, reinterpret_cast<const float*>(logits), V, stride, temps,
+                                                    top_ks, top_ps, min_ps, seeds, offsets);
+  check_launch("sample");
 }
+
+}  // namespace gollek

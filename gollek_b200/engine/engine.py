@@ -179,6 +179,29 @@ class LLMEngine:
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
         return outputs
 
+    def embed(self, token_lists: List[List[int]]) -> List[List[float]]:
+        """Mean-pooled, L2-normalised final hidden states (one prefill pass per input, KV blocks
+        borrowed from the pool and returned). Must run between steps (the async front calls it on
+        the engine thread)."""
+        from .scheduler import ScheduledChunk, SchedulerOutput
+        vecs: List[List[float]] = []
+        for ids in token_lists:
+            if not ids:
+                raise ValueError("empty embedding input")
+            ids = list(ids)[: self.cfg.max_model_len - 1]
+            seq = Sequence(f"embed-{uuid.uuid4().hex[:8]}", ids, SamplingParams(max_tokens=1))
+            self.kv.add(seq)
+            try:
+                if not self.kv.ensure(seq, len(ids)):
+                    raise RuntimeError("KV cache full: retry the embedding request later")
+                out = SchedulerOutput(prefill=[ScheduledChunk(seq, 0, len(ids), False)])
+                hid = self.runner.run_hidden(out).float().mean(0)
+                hid = hid / hid.norm().clamp_min(1e-12)
+                vecs.append(hid.cpu().tolist())
+            finally:
+                self.kv.free(seq)
+        return vecs
+
     def generate(self, prompts: Seq[Union[str, List[int]]], params: Union[SamplingParams, List[SamplingParams], None] = None,
                  lora_ids: Optional[List[int]] = None) -> List[RequestOutput]:
         ids = []

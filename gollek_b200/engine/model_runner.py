@@ -160,6 +160,22 @@ class ModelRunner:
         ids = self.sample(logits, sample_seqs)
         return ids
 
+    @torch.inference_mode()
+    def run_hidden(self, out: SchedulerOutput) -> torch.Tensor:
+        """Prefill-only forward of ``out`` returning final hidden states [T, hidden] (embeddings)."""
+        n, T, _, _ = self._fill_host(out)
+        h = self.host
+        dev = self.device
+        nb = int(max(1, (int(h.seq_lens[:n].max()) + self.block_size - 1) // self.block_size))
+        bt = h.block_tables[:n].to(dev)[:, :nb]
+        qs = h.query_start[: n + 1].clone()
+        meta = AttnMetadata(positions=h.positions[:T].to(dev), slot_mapping=h.slots[:T].to(dev), num_decode=0,
+                            num_prefill_tokens=T, prefill_block_tables=bt, prefill_seq_lens=h.seq_lens[:n].to(dev),
+                            prefill_query_start=qs.to(dev))
+        if self.is_cuda:
+            meta.prefill_tiles = ops.prefill_tiles(qs.tolist()).to(dev)
+        return self.model.forward(h.input_ids[:T].to(dev), meta, self.kv_cache, hidden_only=True)
+
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
         dev = logits.device
         ns = len(seqs)

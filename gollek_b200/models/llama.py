@@ -249,8 +249,10 @@ class LlamaModel:
             out.index_add_(0, rows, ye * we[:, None])
         return out.to(x.dtype)
 
-    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor]) -> torch.Tensor:
-        """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP)."""
+    def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
+                hidden_only: bool = False) -> torch.Tensor:
+        """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP), or with
+        ``hidden_only`` the final-norm hidden states of every token [T, hidden]."""
         cfg = self.cfg
         eps = cfg.rms_norm_eps
         h = ops.embedding(input_ids, self.embed)
@@ -279,6 +281,8 @@ class LlamaModel:
                 h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"])
             h = self.comm.all_reduce(h)
         x = ops.fused_add_rms_norm(h, residual, self.norm, eps)
+        if hidden_only:
+            return x
         if meta.logits_indices is not None:
             x = x.index_select(0, meta.logits_indices)
         logits = ops.linear(x, self.lm_head)

@@ -1,0 +1,485 @@
+"""HTTP API: OpenAI-compatible routes plus the gollek platform routes.
+
+OpenAI surface (runner/safetensor/gollek-safetensor-api/…/OpenAiCompatibleResource.java:32-462):
+  POST /v1/chat/completions (JSON, or SSE ``chat.completion.chunk`` frames + ``[DONE]`` when
+  ``stream``), POST /v1/chat/completions/stream, POST /v1/completions, GET /v1/models[/{id}],
+  POST /v1/embeddings. Defaults as the reference: temperature 0.7, top_p 0.95, top_k 50,
+  max_tokens 2048 (capped by the model length).
+gollek surface (inference/gollek-api-rest/…/api/rest/InferenceResource.java:46-266):
+  POST /v1/infer/completions → {requestId, content, model, tokensUsed, durationMs, timestamp}
+  POST /v1/infer/async → {jobId}; GET /v1/infer/async/{jobId}; POST /v1/infer/stream (SSE of
+  {index, content, isFinal}); POST /v1/infer/batch; POST /v1/infer/embeddings;
+  DELETE /v1/infer/{requestId}. The same routes are served under /v1/inference/* (the path the
+  reference SDK calls, sdk/gollek-sdk-java-remote/…/GollekClient.java:96) and POST
+  /api/v1/inference (the path its bench script posts to, scripts/bench-multilora-zipf.sh:33).
+Operations: GET /health, /q/health[/live|/ready], /metrics (Prometheus), /v1/system, /v1/providers,
+optional API-key auth (``Authorization: Bearer`` or ``X-API-Key``; ui/gollek-server-api/…/
+SecurityFilter.java), bulkhead / circuit breaker / per-key rate limit / request timeout.
+Token counts are real (the reference estimates chars/4, OpenAiCompatibleResource.java:372).
+"""
+from __future__ import annotations
+
+import asyncio
+import json
+import time
+import uuid
+from datetime import datetime, timezone
+from typing import Any, Dict, List, Optional, Union
+
+from fastapi import FastAPI, Header, HTTPException, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+from pydantic import BaseModel, Field
+
+from ..engine.sequence import SamplingParams
+from .async_engine import AsyncEngine, EngineDeadError
+from .resilience import Bulkhead, BulkheadFull, CircuitBreaker, CircuitOpen, RateLimited, RateLimiter
+
+
+# ----------------------------------------------------------------------------- schemas
+class ChatMessage(BaseModel):
+    role: str = "user"
+    content: Union[str, List[Dict[str, Any]], None] = ""
+    name: Optional[str] = None
+
+
+class ChatRequest(BaseModel):
+    model: Optional[str] = None
+    messages: List[ChatMessage]
+    max_tokens: Optional[int] = None
+    max_completion_tokens: Optional[int] = None
+    temperature: Optional[float] = None
+    top_p: Optional[float] = None
+    top_k: Optional[int] = None
+    min_p: Optional[float] = None
+    stop: Union[str, List[str], None] = None
+    stream: bool = False
+    seed: Optional[int] = None
+    presence_penalty: Optional[float] = None
+    frequency_penalty: Optional[float] = None
+    repetition_penalty: Optional[float] = None
+    n: int = 1
+    user: Optional[str] = None
+    adapter_id: Optional[str] = None
+
+
+class CompletionRequest(BaseModel):
+    model: Optional[str] = None
+    prompt: Union[str, List[int], List[str], List[List[int]]] = ""
+    max_tokens: Optional[int] = 16
+    temperature: Optional[float] = None
+    top_p: Optional[float] = None
+    top_k: Optional[int] = None
+    min_p: Optional[float] = None
+    stop: Union[str, List[str], None] = None
+    stream: bool = False
+    seed: Optional[int] = None
+    presence_penalty: Optional[float] = None
+    frequency_penalty: Optional[float] = None
+    repetition_penalty: Optional[float] = None
+    ignore_eos: bool = False
+    n: int = 1
+    adapter_id: Optional[str] = None
+
+
+class EmbeddingRequest(BaseModel):
+    model: Optional[str] = None
+    input: Union[str, List[str], List[int], List[List[int]]]
+
+
+class InferMessage(BaseModel):
+    role: str = "user"
+    content: Optional[str] = ""
+
+
+class InferRequest(BaseModel):
+    model: Optional[str] = None
+    messages: List[InferMessage] = Field(default_factory=list)
+    prompt: Optional[str] = None
+    parameters: Dict[str, Any] = Field(default_factory=dict)
+    timeout: int = 0
+    priority: int = 0
+    requestId: Optional[str] = None
+
+
+# ----------------------------------------------------------------------------- helpers
+def _now() -> int:
+    return int(time.time())
+
+
+def _param(p: Dict[str, Any], *names, default=None):
+    for n in names:
+        if n in p and p[n] is not None:
+            return p[n]
+    return default
+
+
+class ServerState:
+    def __init__(self, aengine: AsyncEngine, model_name: str, api_keys: Optional[List[str]] = None,
+                 rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
+                 max_concurrent: int = 1024, max_queue: int = 4096):
+        self.ae = aengine
+        self.model_name = model_name
+        self.api_keys = set(api_keys or [])
+        self.bulkhead = Bulkhead(max_concurrent, max_queue)
+        self.breaker = CircuitBreaker()
+        self.limiter = RateLimiter(rate, burst)
+        self.timeout = request_timeout
+        self.jobs: Dict[str, Dict[str, Any]] = {}
+        self.adapters: Dict[str, int] = {}  # adapter name -> engine LoRA id
+
+    @property
+    def engine(self):
+        return self.ae.engine
+
+    @property
+    def tokenizer(self):
+        return self.engine.tokenizer
+
+    def max_len(self) -> int:
+        return self.engine.cfg.max_model_len
+
+    def lora_id(self, name: Optional[str]) -> int:
+        if not name:
+            return 0
+        lm = getattr(self.engine, "lora_manager", None)
+        if lm is None or name not in lm.name_to_id:
+            raise HTTPException(404, f"unknown adapter {name!r}")
+        return lm.name_to_id[name]
+
+
+def build_sampling(st: ServerState, d: Dict[str, Any], defaults: Dict[str, Any]) -> SamplingParams:
+    stop = _param(d, "stop", default=[]) or []
+    if isinstance(stop, str):
+        stop = [stop]
+    sp = SamplingParams(
+        temperature=float(_param(d, "temperature", default=defaults["temperature"])),
+        top_p=float(_param(d, "top_p", "topP", default=defaults["top_p"])),
+        top_k=int(_param(d, "top_k", "topK", default=defaults["top_k"])),
+        min_p=float(_param(d, "min_p", "minP", default=0.0)),
+        repetition_penalty=float(_param(d, "repetition_penalty", "repeat_penalty", "repetitionPenalty",
+                                        default=defaults.get("repetition_penalty", 1.0))),
+        frequency_penalty=float(_param(d, "frequency_penalty", "frequencyPenalty", default=0.0)),
+        presence_penalty=float(_param(d, "presence_penalty", "presencePenalty", default=0.0)),
+        max_tokens=int(_param(d, "max_tokens", "max_completion_tokens", "maxTokens",
+                              default=defaults["max_tokens"])),
+        stop=list(stop),
+        seed=_param(d, "seed"),
+        ignore_eos=bool(_param(d, "ignore_eos", default=False)),
+    )
+    try:
+        return sp.validate()
+    except ValueError as e:
+        raise HTTPException(400, str(e))
+
+
+OPENAI_DEFAULTS = dict(temperature=0.7, top_p=0.95, top_k=50, max_tokens=2048, repetition_penalty=1.0)
+
+
+def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
+               rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0) -> FastAPI:
+    st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
+    gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
+    app = FastAPI(title="gollek-b200", version="0.1")
+    app.state.server = st
+
+    # -------------------------------------------------------------- middleware
+    @app.middleware("http")
+    async def auth_and_limits(request: Request, call_next):
+        path = request.url.path
+        open_paths = ("/health", "/q/health", "/metrics", "/docs", "/openapi.json")
+        if st.api_keys and not path.startswith(open_paths):
+            key = request.headers.get("x-api-key")
+            auth = request.headers.get("authorization", "")
+            if auth.lower().startswith("bearer "):
+                key = auth[7:].strip()
+            if key not in st.api_keys:
+                return JSONResponse({"error": {"message": "invalid or missing API key", "type": "unauthorized"}},
+                                    status_code=401)
+        try:
+            st.limiter.check(request.headers.get("x-api-key") or request.client.host if request.client else "anon")
+        except RateLimited as e:
+            return JSONResponse({"error": {"message": str(e), "type": "rate_limited"}}, status_code=429)
+        return await call_next(request)
+
+    # -------------------------------------------------------------- core runner
+    async def run_full(prompt, sp: SamplingParams, rid: Optional[str] = None, lora_id: int = 0,
+                       priority: int = 0, timeout: Optional[float] = None):
+        try:
+            st.breaker.before()
+        except CircuitOpen as e:
+            raise HTTPException(503, str(e))
+        try:
+            async with st.bulkhead:
+                last = None
+
+                async def consume():
+                    nonlocal last
+                    async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, priority=priority):
+                        last = out
+
+                await asyncio.wait_for(consume(), timeout=timeout or st.timeout)
+            st.breaker.record(True)
+            return last
+        except BulkheadFull as e:
+            raise HTTPException(429, str(e))
+        except asyncio.TimeoutError:
+            st.breaker.record(False)
+            raise HTTPException(504, "request timed out")
+        except EngineDeadError as e:
+            st.breaker.record(False)
+            raise HTTPException(503, str(e))
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+
+    def detok(ids: List[int]) -> str:
+        return st.tokenizer.decode(ids) if st.tokenizer is not None else " ".join(map(str, ids))
+
+    def chat_prompt(messages) -> Union[str, List[int]]:
+        if st.tokenizer is None:
+            raise HTTPException(400, "model has no tokenizer for chat messages")
+        msgs = [m if isinstance(m, dict) else m.model_dump() for m in messages]
+        tmpl = getattr(st.tokenizer, "apply_chat_template", None)
+        return tmpl(msgs) if tmpl else "\n".join(str(m.get("content", "")) for m in msgs)
+
+    async def sse_stream(prompt, sp, rid, lora_id, frame, final_frame, done_marker=True):
+        prev = ""
+
+        async def gen():
+            nonlocal prev
+            try:
+                async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id):
+                    text = detok(out.output_token_ids)
+                    if out.finished and out.text:
+                        text = out.text
+                    delta = text[len(prev):] if text.startswith(prev) else text
+                    prev = text
+                    yield "data: " + json.dumps(frame(delta, out)) + "\n\n"
+                    if out.finished:
+                        yield "data: " + json.dumps(final_frame(out)) + "\n\n"
+                if done_marker:
+                    yield "data: [DONE]\n\n"
+            except (EngineDeadError, ValueError) as e:
+                yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+
+        return StreamingResponse(gen(), media_type="text/event-stream")
+
+    # -------------------------------------------------------------- health / ops
+    @app.get("/health")
+    @app.get("/q/health")
+    @app.get("/q/health/live")
+    async def health():
+        ok = st.ae.healthy
+        return JSONResponse({"status": "UP" if ok else "DOWN", "checks": [{"name": "engine", "status": "UP" if ok else "DOWN"}]},
+                            status_code=200 if ok else 503)
+
+    @app.get("/q/health/ready")
+    async def ready():
+        ok = st.ae.healthy and not st.ae.draining
+        return JSONResponse({"status": "UP" if ok else "DOWN"}, status_code=200 if ok else 503)
+
+    @app.get("/metrics")
+    async def metrics():
+        return PlainTextResponse(st.engine.metrics.prometheus())
+
+    @app.get("/v1/system")
+    async def system():
+        import torch
+        e = st.engine
+        info = {"model": st.model_name, "device": str(e.device), "dtype": str(e.dtype),
+                "tensor_parallel_size": e.comm.size, "kv_blocks": e.num_blocks, "block_size": e.cfg.block_size,
+                "max_model_len": e.cfg.max_model_len, "metrics": e.metrics.snapshot()}
+        if torch.cuda.is_available():
+            info["gpu"] = torch.cuda.get_device_name(e.device)
+        return info
+
+    @app.get("/v1/providers")
+    async def providers():
+        return {"providers": [{"id": "gollek-b200", "type": "local", "formats": ["safetensors", "gguf"],
+                               "healthy": st.ae.healthy, "models": [st.model_name]}]}
+
+    # -------------------------------------------------------------- OpenAI
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": st.model_name, "object": "model", "created": _now(),
+                                            "owned_by": "gollek-b200", "max_model_len": st.max_len()}]}
+
+    @app.get("/v1/models/{model_id}")
+    async def model(model_id: str):
+        if model_id != st.model_name:
+            raise HTTPException(404, f"model {model_id} not found")
+        return {"id": st.model_name, "object": "model", "created": _now(), "owned_by": "gollek-b200"}
+
+    @app.post("/v1/completions")
+    async def completions(req: CompletionRequest):
+        if req.n != 1:
+            raise HTTPException(400, "only n=1 is supported")
+        sp = build_sampling(st, req.model_dump(), {**OPENAI_DEFAULTS, "max_tokens": req.max_tokens or 16})
+        lora = st.lora_id(req.adapter_id)
+        prompts = req.prompt
+        if isinstance(prompts, list) and prompts and isinstance(prompts[0], (str, list)):
+            batch = prompts
+        else:
+            batch = [prompts]
+        cid = "cmpl-" + uuid.uuid4().hex
+        if req.stream:
+            if len(batch) != 1:
+                raise HTTPException(400, "streaming supports a single prompt")
+            frame = lambda d, o: {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name,  # noqa: E731
+                                  "choices": [{"index": 0, "text": d, "finish_reason": o.finish_reason, "logprobs": None}]}
+            final = lambda o: {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name,  # noqa: E731
+                               "choices": [], "usage": {"prompt_tokens": len(o.prompt_token_ids),
+                                                        "completion_tokens": len(o.output_token_ids),
+                                                        "total_tokens": len(o.prompt_token_ids) + len(o.output_token_ids)}}
+            return await sse_stream(batch[0], sp, cid, lora, frame, final)
+        outs = await asyncio.gather(*[run_full(p, SamplingParams(**vars(sp)), lora_id=lora) for p in batch])
+        choices, pt, ct = [], 0, 0
+        for i, o in enumerate(outs):
+            choices.append({"index": i, "text": o.text or detok(o.output_token_ids), "finish_reason": o.finish_reason,
+                            "logprobs": None})
+            pt += len(o.prompt_token_ids)
+            ct += len(o.output_token_ids)
+        return {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name, "choices": choices,
+                "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
+
+    async def _chat(req: ChatRequest, force_stream: bool = False):
+        if req.n != 1:
+            raise HTTPException(400, "only n=1 is supported")
+        d = req.model_dump()
+        d["max_tokens"] = req.max_tokens or req.max_completion_tokens
+        sp = build_sampling(st, d, OPENAI_DEFAULTS)
+        lora = st.lora_id(req.adapter_id)
+        prompt = chat_prompt(req.messages)
+        cid = "chatcmpl-" + uuid.uuid4().hex
+        if req.stream or force_stream:
+            first = {"sent": False}
+
+            def frame(delta, o):
+                dd = {"content": delta}
+                if not first["sent"]:
+                    dd["role"] = "assistant"
+                    first["sent"] = True
+                return {"id": cid, "object": "chat.completion.chunk", "created": _now(), "model": st.model_name,
+                        "choices": [{"index": 0, "delta": dd, "finish_reason": o.finish_reason}]}
+
+            final = lambda o: {"id": cid, "object": "chat.completion.chunk", "created": _now(), "model": st.model_name,  # noqa: E731
+                               "choices": [], "usage": {"prompt_tokens": len(o.prompt_token_ids),
+                                                        "completion_tokens": len(o.output_token_ids),
+                                                        "total_tokens": len(o.prompt_token_ids) + len(o.output_token_ids)}}
+            return await sse_stream(prompt, sp, cid, lora, frame, final)
+        o = await run_full(prompt, sp, lora_id=lora)
+        pt, ct = len(o.prompt_token_ids), len(o.output_token_ids)
+        return {"id": cid, "object": "chat.completion", "created": _now(), "model": st.model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": o.text or detok(o.output_token_ids)},
+                             "finish_reason": o.finish_reason}],
+                "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: ChatRequest):
+        return await _chat(req)
+
+    @app.post("/v1/chat/completions/stream")
+    async def chat_stream(req: ChatRequest):
+        return await _chat(req, force_stream=True)
+
+    async def _embed(inputs) -> List[List[float]]:
+        if isinstance(inputs, str):
+            inputs = [inputs]
+        elif inputs and isinstance(inputs[0], int):
+            inputs = [inputs]
+        toks = []
+        for x in inputs:
+            if isinstance(x, str):
+                if st.tokenizer is None:
+                    raise HTTPException(400, "model has no tokenizer")
+                toks.append(st.tokenizer.encode(x))
+            else:
+                toks.append(list(x))
+        return await st.ae.call(lambda eng: eng.embed(toks))
+
+    @app.post("/v1/embeddings")
+    async def embeddings(req: EmbeddingRequest):
+        vecs = await _embed(req.input)
+        n = sum(len(v) for v in vecs)
+        return {"object": "list", "model": st.model_name,
+                "data": [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)],
+                "usage": {"prompt_tokens": n, "total_tokens": n}}
+
+    # -------------------------------------------------------------- gollek platform routes
+    def infer_prompt(req: InferRequest):
+        if req.prompt is not None and not req.messages:
+            return req.prompt
+        return chat_prompt([m.model_dump() for m in req.messages])
+
+    async def infer_completions(req: InferRequest, x_request_id: Optional[str] = Header(None)):
+        return await _infer(req, x_request_id)
+
+    async def _infer(req: InferRequest, x_request_id: Optional[str] = None):
+        rid = req.requestId or x_request_id or uuid.uuid4().hex
+        sp = build_sampling(st, req.parameters, gollek_defaults)
+        lora = st.lora_id(_param(req.parameters, "adapter_id", "adapterId", "lora"))
+        t0 = time.perf_counter()
+        o = await run_full(infer_prompt(req), sp, rid, lora, req.priority, timeout=req.timeout / 1000 if req.timeout else None)
+        return {"requestId": rid, "content": o.text or detok(o.output_token_ids), "model": req.model or st.model_name,
+                "tokensUsed": len(o.prompt_token_ids) + len(o.output_token_ids),
+                "durationMs": int((time.perf_counter() - t0) * 1e3),
+                "timestamp": datetime.now(timezone.utc).isoformat(), "finishReason": o.finish_reason}
+
+    async def infer_async(req: InferRequest):
+        jid = req.requestId or uuid.uuid4().hex
+        st.jobs[jid] = {"jobId": jid, "status": "PENDING", "result": None, "error": None}
+
+        async def run():
+            st.jobs[jid]["status"] = "RUNNING"
+            try:
+                st.jobs[jid]["result"] = await _infer(req)
+                st.jobs[jid]["status"] = "COMPLETED"
+            except HTTPException as e:
+                st.jobs[jid].update(status="FAILED", error=e.detail)
+            except Exception as e:  # report, don't crash the server
+                st.jobs[jid].update(status="FAILED", error=repr(e))
+
+        asyncio.get_running_loop().create_task(run())
+        return JSONResponse({"jobId": jid, "status": "PENDING"}, status_code=202)
+
+    async def infer_async_status(job_id: str):
+        if job_id not in st.jobs:
+            raise HTTPException(404, "unknown job")
+        return st.jobs[job_id]
+
+    async def infer_stream(req: InferRequest):
+        rid = req.requestId or uuid.uuid4().hex
+        sp = build_sampling(st, req.parameters, gollek_defaults)
+        lora = st.lora_id(_param(req.parameters, "adapter_id", "adapterId", "lora"))
+        counter = {"i": 0}
+
+        def frame(delta, o):
+            counter["i"] += 1
+            return {"requestId": rid, "index": counter["i"] - 1, "content": delta, "isFinal": bool(o.finished)}
+
+        final = lambda o: {"requestId": rid, "index": counter["i"], "content": "", "isFinal": True,  # noqa: E731
+                           "finishReason": o.finish_reason, "tokensUsed": len(o.prompt_token_ids) + len(o.output_token_ids)}
+        return await sse_stream(infer_prompt(req), sp, rid, lora, frame, final, done_marker=False)
+
+    async def infer_batch(reqs: List[InferRequest]):
+        return await asyncio.gather(*[_infer(r) for r in reqs])
+
+    async def infer_embeddings(req: InferRequest):
+        texts = [m.content or "" for m in req.messages] or [req.prompt or ""]
+        vecs = await _embed(texts)
+        return {"model": req.model or st.model_name, "embeddings": vecs}
+
+    async def infer_cancel(request_id: str):
+        await st.ae.abort(request_id)
+        return {"requestId": request_id, "status": "CANCELLED"}
+
+    for base in ("/v1/infer", "/v1/inference"):
+        app.post(base + "/completions")(infer_completions)
+        app.post(base + "/async")(infer_async)
+        app.get(base + "/async/{job_id}")(infer_async_status)
+        app.post(base + "/stream")(infer_stream)
+        app.post(base + "/batch")(infer_batch)
+        app.post(base + "/embeddings")(infer_embeddings)
+        app.delete(base + "/{request_id}")(infer_cancel)
+    app.post("/api/v1/inference")(infer_completions)
+    app.post("/v1/inference")(infer_completions)
+    return app

@@ -18,18 +18,28 @@ def _engine(cfg, w, graphs=True, **kw):
     return LLMEngine(ec, model_cfg=cfg, weights=w.__getitem__, num_blocks=256)
 
 
+def _near_argmax(ref: ReferenceDecoder, prompt, tokens, tol: float) -> float:
+    """Fraction of GPU-chosen tokens whose fp32-oracle logit (same history) is within ``tol`` of the max."""
+    logits = ref.forward(torch.tensor(prompt + tokens))[len(prompt) - 1: len(prompt) - 1 + len(tokens)]
+    chosen = logits[torch.arange(len(tokens)), torch.tensor(tokens)]
+    return float(((logits.max(-1).values - chosen) <= tol).float().mean())
+
+
 def test_tiny_llama_greedy_tokens(tiny_cfg, tiny_weights):
-    """Config 1 shape (4 layers, d 256, GQA 8/2, hd 32): 32-token prompt, 32 greedy tokens, block 16."""
+    """Config 1 shape (4 layers, d 256, GQA 8/2, hd 32): 32-token prompt, 32 greedy tokens, block 16.
+
+    bf16 rounding flips near-ties of this random model (top-2 logit gaps go down to 0.004), so the
+    check is: the first token matches the fp32 oracle and every GPU token is the oracle's argmax
+    (within 0.03 logits, ~10% of the logit std) given the GPU's own history."""
     prompt = torch.randint(0, tiny_cfg.vocab_size, (32,), generator=torch.Generator().manual_seed(0)).tolist()
     ref = ReferenceDecoder(tiny_cfg, tiny_weights)
-    ref_tokens, ref_logits = ref.greedy(prompt, 32)
+    ref_tokens, ref_logits = ref.greedy(prompt, 4)
     for graphs in (False, True):
         eng = _engine(tiny_cfg, tiny_weights, graphs=graphs)
         out = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=32, ignore_eos=True))[0]
-        # bf16 compute: require the first 8 tokens exact and >= 75% overall agreement
-        agree = sum(a == b for a, b in zip(out.output_token_ids, ref_tokens)) / 32
-        assert out.output_token_ids[:8] == ref_tokens[:8]
-        assert agree >= 0.75, agree
+        assert len(out.output_token_ids) == 32
+        assert out.output_token_ids[0] == ref_tokens[0]
+        assert _near_argmax(ref, prompt, out.output_token_ids, 0.03) == 1.0
 
 
 def test_batched_mixed_steps_match_single(tiny_cfg, tiny_weights):
