@@ -102,7 +102,7 @@ void silu_mul_out(torch::Tensor out, torch::Tensor x) {
 
 void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                                 torch::Tensor seq_lens, double scale, int64_t num_splits,
-                                c10::optional<torch::Tensor> workspace) {
+                                c10::optional<torch::Tensor> workspace, bool tensor_cores) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(cache, "kv_cache");
@@ -124,7 +124,8 @@ void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tenso
     po = workspace->data_ptr<float>();
     pml = po + (int64_t)B * H * num_splits * D;
   }
-  launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(), block_tables.data_ptr<int>(),
+  launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(),
+                      tensor_cores ? (int)cache.size(0) : 0, block_tables.data_ptr<int>(),
                       block_tables.stride(0), seq_lens.data_ptr<int>(), B, H, cache.size(2), D, cache.size(3),
                       (int)num_splits, (float)scale, po, pml, cur_stream());
 }
@@ -151,7 +152,8 @@ void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tens
 }
 
 void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
-                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit) {
+                   int64_t epi, int64_t bn, c10::optional<torch::Tensor> status, int64_t grid_limit,
+                   int64_t splits, c10::optional<torch::Tensor> workspace) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_bf16(out, "out");
@@ -179,8 +181,28 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
     check_cuda(*status, "status");
     st = reinterpret_cast<uint32_t*>(status->data_ptr());
   }
+  int bn_i = (int)bn, sp = (int)splits;
+  if (bn_i == 0) {
+    int auto_sp = 1;
+    gemm_plan(M, N, K, (int)epi, bn_i, auto_sp);
+    if (sp <= 0) sp = auto_sp;
+  }
+  if (sp <= 0) sp = 1;
+  float* part = nullptr;
+  if (sp > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->is_cuda() && workspace->scalar_type() == at::kFloat &&
+                    workspace->numel() >= (int64_t)sp * M * N,
+                "gemm: split-K ", sp, " needs an fp32 workspace of ", (int64_t)sp * M * N, " elements");
+    part = workspace->data_ptr<float>();
+  }
   launch_gemm_bf16(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), rp, ldr, M,
-                   N, K, (int)epi, (int)bn, st, (int)grid_limit, cur_stream());
+                   N, K, (int)epi, bn_i, sp, part, st, (int)grid_limit, cur_stream());
+}
+
+std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  int bn = 0, sp = 1;
+  gemm_plan((int)M, (int)N, (int)K, (int)epi, bn, sp);
+  return {bn, sp};
 }
 
 void argmax_out(torch::Tensor out, torch::Tensor logits) {
@@ -231,6 +253,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_prefill_attention", &paged_prefill_attention_out, "paged prefill attention (K4)");
   m.def("gemm_bf16", &gemm_bf16_out, "tcgen05 bf16 GEMM with fused epilogues (K5/K8)");
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
+  m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
   m.def("num_sms", &device_num_sms);
   m.def("argmax", &argmax_out, "greedy argmax (K11)");
   m.def("apply_penalties", &apply_penalties_, "repetition/frequency/presence penalties (K11)");

@@ -14,6 +14,7 @@
 // (decode), runner/safetensor/gollek-safetensor-engine/…/attention/PagedAttentionVectorAPI.java:20-127
 // (online softmax over blocks, GQA, causal). KV layout per layer: [blocks, 2, Hk, block_size, D].
 #include "../common/common.cuh"
+#include "../common/tma_host.h"
 #include "launchers.h"
 
 using namespace gollek;
@@ -38,7 +39,19 @@ struct DecodeCfg {
 };
 
 constexpr int kDecodeWarps = 4;
+constexpr int kDecodeStages = 3;  // per-warp ring depth (blocks in flight per warp)
 
+// Bounded wait for the per-warp ring barriers (no legitimate wait comes near the limit).
+GOLLEK_DEVICE bool ring_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  for (uint32_t i = 0; i < (1u << 24); ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  report_status(status, kStatusMbarTimeout);
+  return false;
+}
+
+// Each warp owns a kDecodeStages-deep shared-memory ring; its lane 0 streams the warp's paged
+// blocks (K tile and V tile, BS*D bf16 each, contiguous in the cache) with cp.async.bulk and the
+// whole warp consumes them. Warps take blocks blk_begin + warp, + 4, ... of this CTA's split.
 template <int D, int G, int BS>
 __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     __nv_bfloat16* __restrict__ out,            // [B, H, D]          (num_splits == 1)
@@ -47,17 +60,48 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q,        // [B, H, D] rows at q_stride
     const __nv_bfloat16* __restrict__ cache,    // [NB, 2, Hk, BS, D]
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens, int Hk,
-    int num_splits, float scale_log2, int64_t q_stride) {
+    int num_splits, float scale_log2, int64_t q_stride, uint32_t* status) {
   using C = DecodeCfg<D, G, BS>;
+  constexpr int TILE = BS * D;                         // elements of one K (or V) tile
+  constexpr uint32_t TILE_BYTES = TILE * 2;
+  extern __shared__ __align__(128) uint8_t dsmem[];
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int H = Hk * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = lane % C::CH, tsub = lane / C::CH;
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(dsmem) + (size_t)warp * kDecodeStages * 2 * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsmem + (size_t)kDecodeWarps * kDecodeStages * 2 * TILE_BYTES) +
+                   warp * kDecodeStages;
+  float* sm_o = reinterpret_cast<float*>(bars - warp * kDecodeStages + kDecodeWarps * kDecodeStages);
+  float* sm_m = sm_o + kDecodeWarps * G * D;
+  float* sm_l = sm_m + kDecodeWarps * G;
+
   const int L = seq_lens[b];
   const int nblocks = (L + BS - 1) / BS;
   const int per = (nblocks + num_splits - 1) / num_splits;
   const int blk_begin = split * per;
   const int blk_end = min(nblocks, blk_begin + per);
+  const int nmine = blk_begin + warp < blk_end ? (blk_end - blk_begin - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+  const int* bt = block_tables + (int64_t)b * bt_stride;
+
+  if (lane == 0) {
+    for (int st = 0; st < kDecodeStages; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  auto issue = [&](int j) {  // lane 0 only
+    const int st = j % kDecodeStages;
+    const int64_t pb = bt[blk_begin + warp + kDecodeWarps * j];
+    const __nv_bfloat16* kb = cache + ((pb * 2 + 0) * Hk + kh) * (int64_t)TILE;
+    const __nv_bfloat16* vb = cache + ((pb * 2 + 1) * Hk + kh) * (int64_t)TILE;
+    mbar_arrive_expect_tx(&bars[st], 2 * TILE_BYTES);
+    bulk_g2s(ring + st * 2 * TILE, kb, TILE_BYTES, &bars[st]);
+    bulk_g2s(ring + st * 2 * TILE + TILE, vb, TILE_BYTES, &bars[st]);
+  };
+  int issued = 0;
+  if (lane == 0) {
+    for (; issued < min(kDecodeStages, nmine); ++issued) issue(issued);
+  }
 
   // query chunk for this lane, pre-scaled into the log2 domain
   float qv[G][8];
@@ -76,24 +120,21 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
   }
-  const int* bt = block_tables + (int64_t)b * bt_stride;
-  const int64_t head_stride = (int64_t)BS * D;           // one (block, kv, head) tile
-  for (int blk = blk_begin + warp; blk < blk_end; blk += kDecodeWarps) {
-    const int64_t pb = bt[blk];
-    const __nv_bfloat16* kbase = cache + ((pb * 2 + 0) * Hk + kh) * head_stride;
-    const __nv_bfloat16* vbase = cache + ((pb * 2 + 1) * Hk + kh) * head_stride;
-    uint4 kr[C::NI], vr[C::NI];
-#pragma unroll
-    for (int i = 0; i < C::NI; ++i) {
-      const int t = i * C::TPI + tsub;
-      kr[i] = __ldg(reinterpret_cast<const uint4*>(kbase + t * D + c * 8));
+  bool ok = true;
+  int j = 0;
+  for (; j < nmine; ++j) {
+    const int st = j % kDecodeStages;
+    if (!ring_wait(&bars[st], (j / kDecodeStages) & 1, status)) {
+      ok = false;
+      break;
     }
+    const __nv_bfloat16* kt = ring + st * 2 * TILE;
+    const __nv_bfloat16* vt = kt + TILE;
+    const int tok0 = (blk_begin + warp + kDecodeWarps * j) * BS;
+    uint4 kr[C::NI];
 #pragma unroll
-    for (int i = 0; i < C::NI; ++i) {
-      const int t = i * C::TPI + tsub;
-      vr[i] = __ldg(reinterpret_cast<const uint4*>(vbase + t * D + c * 8));
-    }
-    // scores s[g][i] for token i*TPI + tsub
+    for (int i = 0; i < C::NI; ++i)
+      kr[i] = *reinterpret_cast<const uint4*>(kt + (i * C::TPI + tsub) * D + c * 8);
     float s[G][C::NI];
 #pragma unroll
     for (int i = 0; i < C::NI; ++i) {
@@ -107,7 +148,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
         s[g][i] = d0;
       }
     }
-    // reduce over the CH lanes that hold one token row
 #pragma unroll
     for (int o = C::CH / 2; o > 0; o >>= 1) {
 #pragma unroll
@@ -115,7 +155,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
 #pragma unroll
         for (int i = 0; i < C::NI; ++i) s[g][i] += __shfl_xor_sync(0xffffffffu, s[g][i], o);
     }
-    const int tok0 = blk * BS;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float bm = -INFINITY;
@@ -143,7 +182,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
 #pragma unroll
     for (int i = 0; i < C::NI; ++i) {
       float vf[8];
-      bf16x8_to_float(vr[i], vf);
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(vt + (i * C::TPI + tsub) * D + c * 8), vf);
       const bool valid = tok0 + i * C::TPI + tsub < L;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -152,7 +191,18 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
         for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, valid ? vf[e] : 0.f, acc[g][e]);
       }
     }
+    __syncwarp();  // every lane has read stage st before it is refilled
+    if (lane == 0 && issued < nmine) {
+      fence_proxy_async_smem();
+      issue(issued);
+      ++issued;
+    }
   }
+  if (!ok && lane == 0) {
+    // bounded drain of our own copies still in flight before the CTA may exit
+    for (int jj = j; jj < issued; ++jj) ring_wait(&bars[jj % kDecodeStages], (jj / kDecodeStages) & 1, nullptr);
+  }
+  __syncwarp();
   // combine the lanes holding different token subsets (same chunk c)
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -164,20 +214,18 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     }
   }
   // cross-warp merge through shared memory
-  __shared__ float sm_m[kDecodeWarps][G], sm_l[kDecodeWarps][G];
-  __shared__ __align__(16) float sm_o[kDecodeWarps][G][D];
   if (lane < C::CH) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sm_o[warp][g][c * 8 + e] = acc[g][e];
+      for (int e = 0; e < 8; ++e) sm_o[(warp * G + g) * D + c * 8 + e] = acc[g][e];
     }
   }
   if (lane == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      sm_m[warp][g] = m[g];
-      sm_l[warp][g] = l[g];
+      sm_m[warp * G + g] = m[g];
+      sm_l[warp * G + g] = l[g];
     }
   }
   __syncthreads();
@@ -185,13 +233,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     const int g = idx / D, d = idx % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, sm_m[w][g]);
+    for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, sm_m[w * G + g]);
     float Lsum = 0.f, O = 0.f;
 #pragma unroll
     for (int w = 0; w < kDecodeWarps; ++w) {
-      const float f = (sm_m[w][g] == -INFINITY) ? 0.f : exp2f(sm_m[w][g] - M);
-      Lsum += sm_l[w][g] * f;
-      O += sm_o[w][g][d] * f;
+      const float mw = sm_m[w * G + g];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      Lsum += sm_l[w * G + g] * f;
+      O += sm_o[(w * G + g) * D + d] * f;
     }
     const int h = kh * G + g;
     if (num_splits == 1) {
@@ -205,6 +254,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
       }
     }
   }
+}
+
+template <int D, int G, int BS>
+constexpr size_t decode_smem_bytes() {
+  return (size_t)kDecodeWarps * kDecodeStages * 2 * BS * D * 2 + kDecodeWarps * kDecodeStages * 8 +
+         (size_t)kDecodeWarps * G * D * 4 + 2 * kDecodeWarps * G * 4;
 }
 
 // Combine split-KV partials: out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
@@ -455,14 +510,264 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
   }
 }
 
+// =============================================================================================
+// K3 (tensor-core variant, head_dim 128): the G query heads of one KV group form the M = 16 rows
+// of mma.sync m16n8k16 (rows >= G are zero), the 16 tokens of a paged block are N, so one block
+// costs 32 MMAs per warp instead of ~1000 CUDA-core instructions. K/V tiles arrive by 2-D TMA
+// (box 64 dims x 16 tokens, 128-byte swizzle, two boxes per tile) into a per-warp 3-stage ring;
+// ldmatrix reads them conflict-free.
+// =============================================================================================
+constexpr int kTcStages = 3;
+constexpr int kTcTileBytes = 16 * 128 * 2;            // one K (or V) tile of a paged block
+constexpr int kTcStageBytes = 2 * kTcTileBytes;       // K + V
+
+GOLLEK_DEVICE uint32_t sw128_off(int row, int chunk16) {  // byte offset inside a [rows][128 dims] bf16 tile
+  const int box = chunk16 >> 3, cc = chunk16 & 7;
+  return box * 2048 + row * 128 + ((cc ^ (row & 7)) << 4);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
+    const __grid_constant__ CUtensorMap tmap,      // cache rows [NB*2*Hk*16, 128] bf16
+    __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
+    const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
+    const int* __restrict__ seq_lens, int Hk, int num_splits, float scale_log2, int64_t q_stride,
+    uint32_t* status) {
+  static_assert(G >= 1 && G <= 16, "GQA group must fit the 16 MMA rows");
+  constexpr int D = 128, BS = 16;
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = dsm_raw + ((1024 - (smem_u32(dsm_raw) & 1023)) & 1023);
+  const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  const int H = Hk * G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = dsm + warp * kTcStages * kTcStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + kDecodeWarps * kTcStages * kTcStageBytes) + warp * kTcStages;
+  float* sm_o = reinterpret_cast<float*>(dsm + kDecodeWarps * kTcStages * kTcStageBytes + kDecodeWarps * kTcStages * 8);
+  float* sm_m = sm_o + kDecodeWarps * G * D;
+  float* sm_l = sm_m + kDecodeWarps * G;
+
+  const int L = seq_lens[b];
+  const int nblocks = (L + BS - 1) / BS;
+  const int per = (nblocks + num_splits - 1) / num_splits;
+  const int blk_begin = split * per;
+  const int blk_end = min(nblocks, blk_begin + per);
+  const int nmine = blk_begin + warp < blk_end ? (blk_end - blk_begin - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
+  const int* bt = block_tables + (int64_t)b * bt_stride;
+
+  if (lane == 0) {
+    prefetch_tmap(&tmap);
+    for (int st = 0; st < kTcStages; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  auto issue = [&](int j) {  // lane 0 only
+    const int st = j % kTcStages;
+    const int pb = bt[blk_begin + warp + kDecodeWarps * j];
+    const int rk = ((pb * 2 + 0) * Hk + kh) * BS, rv = ((pb * 2 + 1) * Hk + kh) * BS;
+    uint8_t* dst = ring + st * kTcStageBytes;
+    mbar_arrive_expect_tx(&bars[st], kTcStageBytes);
+    tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
+    tma_load_2d(dst + 2048, &tmap, 64, rk, &bars[st]);
+    tma_load_2d(dst + kTcTileBytes, &tmap, 0, rv, &bars[st]);
+    tma_load_2d(dst + kTcTileBytes + 2048, &tmap, 64, rv, &bars[st]);
+  };
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < min(kTcStages, nmine); ++issued) issue(issued);
+
+  // Q as the A operand: rows = heads of this group (zero beyond G), K = 128 dims (8 k-steps)
+  const int r = lane >> 2, cq = (lane & 3) * 2;
+  uint32_t qf[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const __nv_bfloat16* q0 = q + (int64_t)b * q_stride + (int64_t)(kh * G) * D + ks * 16 + cq;
+    qf[ks][0] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D) : 0u;
+    qf[ks][1] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D) : 0u;
+    qf[ks][2] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D + 8) : 0u;
+    qf[ks][3] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D + 8) : 0u;
+  }
+  float o[16][4];
+#pragma unroll
+  for (int jn = 0; jn < 16; ++jn)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[jn][e] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  const int mi = lane >> 3, rr = lane & 7;
+  bool ok = true;
+  int j = 0;
+  for (; j < nmine; ++j) {
+    const int st = j % kTcStages;
+    if (!ring_wait(&bars[st], (j / kTcStages) & 1, status)) {
+      ok = false;
+      break;
+    }
+    const uint32_t kt = smem_u32(ring + st * kTcStageBytes);
+    const uint32_t vt = kt + kTcTileBytes;
+    // S = Q K^T : 16 x 16 (two n-tiles of 8 tokens)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t bfr[4];
+      const int tok = (mi >> 1) * 8 + rr, ch = 2 * ks + (mi & 1);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
+                   : "r"(kt + sw128_off(tok, ch)));
+      mma_bf16_16816(sc[0], qf[ks], bfr);
+      mma_bf16_16816(sc[1], qf[ks], bfr + 2);
+    }
+    const int tok0 = (blk_begin + warp + kDecodeWarps * j) * BS;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = tok0 + nt * 8 + cq + (e & 1);
+        const float v = t < L ? sc[nt][e] * scale_log2 : -INFINITY;
+        sc[nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    }
+    float mnew[2], corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mnew[h] = fmaxf(mrow[h], mx[h]);
+      const float ms = mnew[h] == -INFINITY ? 0.f : mnew[h];
+      corr[h] = exp2f(mrow[h] - ms);
+      mrow[h] = mnew[h];
+      mnew[h] = ms;
+      lrow[h] *= corr[h];
+    }
+#pragma unroll
+    for (int jn = 0; jn < 16; ++jn) {
+      o[jn][0] *= corr[0];
+      o[jn][1] *= corr[0];
+      o[jn][2] *= corr[1];
+      o[jn][3] *= corr[1];
+    }
+    uint32_t pf[4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = exp2f(sc[nt][0] - mnew[0]), p1 = exp2f(sc[nt][1] - mnew[0]);
+      const float p2 = exp2f(sc[nt][2] - mnew[1]), p3 = exp2f(sc[nt][3] - mnew[1]);
+      lrow[0] += p0 + p1;
+      lrow[1] += p2 + p3;
+      pf[nt * 2 + 0] = pack_bf16x2(p0, p1);
+      pf[nt * 2 + 1] = pack_bf16x2(p2, p3);
+    }
+    // O += P V : 16 x 128 (16 n-tiles of 8 dims), one k-step of 16 tokens
+#pragma unroll
+    for (int jd = 0; jd < 8; ++jd) {
+      uint32_t bfr[4];
+      const int tok = (mi & 1) * 8 + rr, ch = 2 * jd + (mi >> 1);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
+                   : "r"(vt + sw128_off(tok, ch)));
+      mma_bf16_16816(o[2 * jd], pf, bfr);
+      mma_bf16_16816(o[2 * jd + 1], pf, bfr + 2);
+    }
+    __syncwarp();
+    if (lane == 0 && issued < nmine) {
+      fence_proxy_async_smem();
+      issue(issued);
+      ++issued;
+    }
+  }
+  if (!ok && lane == 0)
+    for (int jj = j; jj < issued; ++jj) ring_wait(&bars[jj % kTcStages], (jj / kTcStages) & 1, nullptr);
+  __syncwarp();
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 1);
+    lrow[h] += __shfl_xor_sync(0xffffffffu, lrow[h], 2);
+  }
+  // per-warp partials to shared memory (rows r, r + 8 that are real heads)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int g = r + 8 * h;
+    if (g < G) {
+#pragma unroll
+      for (int jn = 0; jn < 16; ++jn) {
+        sm_o[(warp * G + g) * D + jn * 8 + cq] = o[jn][2 * h];
+        sm_o[(warp * G + g) * D + jn * 8 + cq + 1] = o[jn][2 * h + 1];
+      }
+      if ((lane & 3) == 0) {
+        sm_m[warp * G + g] = mrow[h];
+        sm_l[warp * G + g] = lrow[h];
+      }
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, sm_m[w * G + g]);
+    float Lsum = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecodeWarps; ++w) {
+      const float mw = sm_m[w * G + g];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      Lsum += sm_l[w * G + g] * f;
+      O += sm_o[(w * G + g) * D + d] * f;
+    }
+    const int hq = kh * G + g;
+    if (num_splits == 1) {
+      out[((int64_t)b * H + hq) * D + d] = __float2bfloat16(Lsum > 0.f ? O / Lsum : 0.f);
+    } else {
+      const int64_t pi = ((int64_t)b * H + hq) * num_splits + split;
+      part_o[pi * D + d] = O;
+      if (d == 0) {
+        part_ml[pi * 2 + 0] = M;
+        part_ml[pi * 2 + 1] = Lsum;
+      }
+    }
+  }
+}
+
+template <int G>
+constexpr size_t decode_tc_smem_bytes() {
+  return 1024 + (size_t)kDecodeWarps * kTcStages * kTcStageBytes + kDecodeWarps * kTcStages * 8 +
+         (size_t)kDecodeWarps * G * 128 * 4 + 2 * kDecodeWarps * G * 4;
+}
+
+template <int G>
+void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks, const int* bt,
+                      int bt_stride, const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po,
+                      float* pml, cudaStream_t s) {
+  const uint64_t rows = (uint64_t)num_blocks * 2 * Hk * 16;
+  CUtensorMap tm = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, 128, 16, 64,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  constexpr size_t smem = decode_tc_smem_bytes<G>();
+  auto kern = paged_decode_tc_kernel<G>;
+  GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid(B, Hk, num_splits);
+  kern<<<grid, kDecodeWarps * 32, smem, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), po, pml,
+                                              reinterpret_cast<const __nv_bfloat16*>(q), bt, bt_stride, lens, Hk,
+                                              num_splits, scale_log2, q_stride, nullptr);
+  check_launch("paged_decode_attention (tensor cores)");
+  if (num_splits > 1) {
+    decode_combine_kernel<128><<<B * Hk * G, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml,
+                                                          num_splits);
+    check_launch("paged_decode_attention combine");
+  }
+}
+
 template <int D, int G>
 void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cache, const int* bt, int bt_stride,
                      const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po, float* pml,
                      cudaStream_t s) {
   dim3 grid(B, Hk, num_splits);
-  paged_decode_kernel<D, G, 16><<<grid, kDecodeWarps * 32, 0, s>>>(
+  constexpr size_t smem = decode_smem_bytes<D, G, 16>();
+  auto kern = paged_decode_kernel<D, G, 16>;
+  GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<grid, kDecodeWarps * 32, smem, s>>>(
       reinterpret_cast<__nv_bfloat16*>(out), po, pml, reinterpret_cast<const __nv_bfloat16*>(q),
-      reinterpret_cast<const __nv_bfloat16*>(cache), bt, bt_stride, lens, Hk, num_splits, scale_log2, q_stride);
+      reinterpret_cast<const __nv_bfloat16*>(cache), bt, bt_stride, lens, Hk, num_splits, scale_log2, q_stride,
+      nullptr);
   check_launch("paged_decode_attention");
   if (num_splits > 1) {
     decode_combine_kernel<D><<<B * Hk * G, D, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml, num_splits);
@@ -474,15 +779,27 @@ void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cac
 
 namespace gollek {
 
-void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, const int* block_tables,
-                         int bt_stride, const int* seq_lens, int B, int H, int Hk, int D, int block_size,
-                         int num_splits, float scale, float* part_o, float* part_ml, cudaStream_t s) {
+void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
+                         const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
+                         int block_size, int num_splits, float scale, float* part_o, float* part_ml,
+                         cudaStream_t s) {
   throw_if(block_size != 16, "decode attention is built for block_size 16");
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(num_splits > 1 && (part_o == nullptr || part_ml == nullptr), "split-KV decode needs a workspace");
   if (B == 0) return;
   const int G = H / Hk;
   const float sl = scale * kLog2e;
+  if (D == 128 && num_blocks > 0) {
+#define GOLLEK_DECODE_TC(GG) \
+  if (G == GG) return launch_decode_tc<GG>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, B, Hk, \
+                                           num_splits, sl, part_o, part_ml, s);
+    GOLLEK_DECODE_TC(1)
+    GOLLEK_DECODE_TC(2)
+    GOLLEK_DECODE_TC(4)
+    GOLLEK_DECODE_TC(8)
+    GOLLEK_DECODE_TC(16)
+#undef GOLLEK_DECODE_TC
+  }
 #define GOLLEK_DECODE_CASE(DD, GG)                                                                            \
   if (D == DD && G == GG)                                                                                     \
     return launch_decode_t<DD, GG>(out, q, q_stride, cache, block_tables, bt_stride, seq_lens, B, Hk, num_splits, \

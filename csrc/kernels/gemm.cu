@@ -25,6 +25,8 @@
 #include "../common/tma_host.h"
 #include "launchers.h"
 
+#include <algorithm>
+
 using namespace gollek;
 
 namespace {
@@ -75,7 +77,8 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
-                     int M, int N, int K, uint32_t* status) {
+                     int M, int N, int K, int group_m, int splits, float* __restrict__ partial,
+                     uint32_t* status) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -95,7 +98,23 @@ __global__ void __launch_bounds__(192, 1)
   const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  const int num_units = num_tiles * splits;
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+  const int kb_per = (num_kb + splits - 1) / splits;
+  // work unit -> (m0, n0, k-block range). Units are split-major so CTAs running at the same time
+  // share a K slice of A; tiles follow a grouped raster (group_m M-tiles swept across all N tiles)
+  // so a slab of A stays resident in L2 while B streams.
+  auto unit_coords = [&](int u, int& m0, int& n0, int& kb0, int& kb1) {
+    const int ks = u / num_tiles, tile = u % num_tiles;
+    const int gsz = group_m * num_n;
+    const int g = tile / gsz, r = tile % gsz;
+    const int first_m = g * group_m;
+    const int gm = min(num_m - first_m, group_m);
+    m0 = (first_m + r % gm) * Cfg::BM;
+    n0 = (r / gm) * BN;
+    kb0 = ks * kb_per;
+    kb1 = min(num_kb, kb0 + kb_per);
+  };
   constexpr uint32_t idesc = make_idesc_bf16(Cfg::BM, BN);
 
   if (threadIdx.x == 0) {
@@ -132,9 +151,10 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * Cfg::BM, n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int m0, n0, kb0, kb1;
+        unit_coords(u, m0, n0, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, status, abort_flag)) {
             ok = false;
             break;
@@ -163,7 +183,9 @@ __global__ void __launch_bounds__(192, 1)
       int local = 0;
       int used = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+        int m0, n0, kb0, kb1;
+        unit_coords(u, m0, n0, kb0, kb1);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!wait_bar(&tempty[acc], acc_phase ^ 1, status, abort_flag)) {
@@ -172,7 +194,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         tcgen05_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&full[stage], phase, status, abort_flag)) {
             ok = false;
             break;
@@ -183,7 +205,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
             // +32 bytes along K inside the 128-byte swizzled row = +2 in the encoded address
-            umma_f16_ss(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+            umma_f16_ss(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           *consumed = ++used;
@@ -204,15 +226,33 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      int m0, n0, kb0, kb1;
+      unit_coords(u, m0, n0, kb0, kb1);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!wait_bar(&tfull[acc], acc_phase, status, abort_flag)) break;
       tcgen05_fence_after();
-      const int m0 = (tile % num_m) * Cfg::BM, n0 = (tile / num_m) * BN;
       const int row = m0 + lg * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * BN;
-      if constexpr (EPI == kEpiSwiglu) {
+      if (splits > 1) {
+        // split-K: raw fp32 partial sums; the reduce kernel applies the epilogue
+        float* prow = partial + ((int64_t)(u / num_tiles) * M + row) * N;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (row < M) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (col + 4 * j + 4 <= N)
+                *reinterpret_cast<uint4*>(prow + col + 4 * j) =
+                    make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          }
+        }
+      } else if constexpr (EPI == kEpiSwiglu) {
         const int out_n = N / 2;
 #pragma unroll 1
         for (int p = 0; p < BN / 128; ++p) {
@@ -278,9 +318,50 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Split-K reduction: out = epilogue(sum_s partial[s]) for one 8-column group per thread.
+template <int EPI>
+__global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ C, int64_t ldc, const float* __restrict__ partial,
+                                     const __nv_bfloat16* __restrict__ R, int64_t ldr, int M, int N, int splits) {
+  const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
+  const int groups = out_n / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)M * groups) return;
+  const int row = idx / groups, col = (idx % groups) * 8;
+  float v[8];
+  if constexpr (EPI == kEpiSwiglu) {
+    const int gc = (col / 64) * 128 + col % 64;  // gate column of the interleaved weight rows
+    float g[8] = {0}, u[8] = {0};
+    for (int s = 0; s < splits; ++s) {
+      const float* p = partial + ((int64_t)s * M + row) * N;
+      const float4 g0 = *reinterpret_cast<const float4*>(p + gc), g1 = *reinterpret_cast<const float4*>(p + gc + 4);
+      const float4 u0 = *reinterpret_cast<const float4*>(p + gc + 64), u1 = *reinterpret_cast<const float4*>(p + gc + 68);
+      g[0] += g0.x; g[1] += g0.y; g[2] += g0.z; g[3] += g0.w; g[4] += g1.x; g[5] += g1.y; g[6] += g1.z; g[7] += g1.w;
+      u[0] += u0.x; u[1] += u0.y; u[2] += u0.z; u[3] += u0.w; u[4] += u1.x; u[5] += u1.y; u[6] += u1.z; u[7] += u1.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = silu(g[e]) * u[e];
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float* p = partial + ((int64_t)s * M + row) * N + col;
+      const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    if constexpr (EPI == kEpiResidual) {
+      float rr[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(R + (int64_t)row * ldr + col), rr);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += rr[e];
+    }
+  }
+  *reinterpret_cast<uint4*>(C + (int64_t)row * ldc + col) = float_to_bf16x8(v);
+}
+
 template <int BN, int EPI>
 void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
-                   int64_t ldr, int M, int N, int K, uint32_t* status, int grid_limit, cudaStream_t s) {
+                   int64_t ldr, int M, int N, int K, int splits, float* partial, uint32_t* status, int grid_limit,
+                   cudaStream_t s) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -288,12 +369,25 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   auto kern = gemm_bf16_kernel<BN, EPI>;
   GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-  const int tiles = ((M + Cfg::BM - 1) / Cfg::BM) * ((N + BN - 1) / BN);
-  int grid = std::min(tiles, num_sms());
+  const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
+  const int tiles = num_m * ((N + BN - 1) / BN);
+  // grouped raster: a ~32 MB slab of A (group_m M-tiles) stays L2-resident while B streams
+  const int64_t a_tile_bytes = (int64_t)Cfg::BM * K * 2;
+  const int group_m = (int)std::max<int64_t>(1, std::min<int64_t>(num_m, (32ll << 20) / a_tile_bytes));
+  int grid = std::min(tiles * splits, num_sms());
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
   kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
-                                     reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, status);
+                                     reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
+                                     partial, status);
   check_launch("gemm_bf16");
+  if (splits > 1) {
+    const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
+    const int64_t threads = (int64_t)M * (out_n / 8);
+    splitk_reduce_kernel<EPI><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<__nv_bfloat16*>(out), ldc, partial, reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N,
+        splits);
+    check_launch("gemm_bf16 split-K reduce");
+  }
 }
 
 }  // namespace
@@ -311,20 +405,50 @@ int gemm_pick_bn(int M, int N, int epi) {
   return 64;
 }
 
+// Tile width and split-K factor for one GEMM. Small-M (decode) GEMMs use wide tiles (fewer
+// re-reads of A) and split K across CTAs so every SM streams part of the weight matrix.
+void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits) {
+  const int num_m = (M + 127) / 128;
+  const int sms = num_sms();
+  const int num_kb = (K + 63) / 64;
+  // Measured at Llama-3-8B decode shapes (M = 64..256): wide tiles + split-K (fp32 partials and a
+  // reduce pass) lost to narrow tiles without split, so split-K is opt-in (explicit splits > 1).
+  (void)K;
+  (void)num_kb;
+  (void)sms;
+  (void)num_m;
+  splits = 1;
+  if (bn == 0) bn = gemm_pick_bn(M, N, epi);
+  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+}
+
+int gemm_splits(int M, int N, int K, int epi) {
+  int bn = 0, sp = 1;
+  gemm_plan(M, N, K, epi, bn, sp);
+  return sp;
+}
+
 void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
-                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, uint32_t* status,
-                      int grid_limit, cudaStream_t s) {
+                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, int splits,
+                      float* partial, uint32_t* status, int grid_limit, cudaStream_t s) {
   throw_if(K % 8 != 0, "gemm: K must be a multiple of 8");
   throw_if(ldc % 8 != 0, "gemm: output row pitch must keep 16-byte alignment");
   if (M == 0) return;
   if (epi == kEpiSwiglu) throw_if(N % 128 != 0, "gemm swiglu: N must be a multiple of 128");
   else throw_if(N % 8 != 0, "gemm: N must be a multiple of 8");
   if (epi == kEpiResidual) throw_if(residual == nullptr || ldr % 8 != 0, "gemm residual: bf16 residual required");
-  if (bn == 0) bn = gemm_pick_bn(M, N, epi);
+  if (bn == 0) {
+    int sp = 1;
+    gemm_plan(M, N, K, epi, bn, sp);
+    if (splits <= 0) splits = sp;
+  }
+  if (splits <= 0) splits = 1;
   if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  throw_if(splits > 1 && partial == nullptr, "gemm: split-K needs an fp32 workspace");
 #define GOLLEK_GEMM_CASE(BNV, EPIV) \
   if (bn == BNV && epi == EPIV)     \
-    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, residual, ldr, M, N, K, status, grid_limit, s);
+    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, residual, ldr, M, N, K, splits, partial, status, \
+                                    grid_limit, s);
   GOLLEK_GEMM_CASE(256, kEpiNone)
   GOLLEK_GEMM_CASE(128, kEpiNone)
   GOLLEK_GEMM_CASE(64, kEpiNone)

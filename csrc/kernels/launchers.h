@@ -29,9 +29,11 @@ void launch_embedding(void* out, const int* ids, const void* table, int T, int d
 void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
 
 // ---- attention (K3, K4)
-void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, const int* block_tables,
-                         int bt_stride, const int* seq_lens, int B, int H, int Hk, int D, int block_size,
-                         int num_splits, float scale, float* part_o, float* part_ml, cudaStream_t s);
+// num_blocks > 0 enables the tensor-core path for head_dim 128 (needs the cache extent for its TMA map).
+void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
+                         const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
+                         int block_size, int num_splits, float scale, float* part_o, float* part_ml,
+                         cudaStream_t s);
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
@@ -40,9 +42,12 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
 // ---- GEMM (K5, K8)
 enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2 };
 int gemm_pick_bn(int M, int N, int epi);
+void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
+int gemm_splits(int M, int N, int K, int epi);
+// splits: 0 = automatic (with bn = 0), 1 = none; partial: fp32 [splits, M, N] workspace when splits > 1.
 void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
-                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, uint32_t* status,
-                      int grid_limit, cudaStream_t s);
+                      const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, int splits,
+                      float* partial, uint32_t* status, int grid_limit, cudaStream_t s);
 
 // ---- sampling (K11)
 void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s);

@@ -1,0 +1,207 @@
+"""Command-line interface: ``python -m gollek_b200 <command>``.
+
+Commands follow the reference CLI (ui/gollek-cli/…/cli/commands/RunCommand.java:45-324 and
+siblings: run, chat, batch, list, show, convert, quantize, serve, providers, stats):
+
+  run       one-shot generation            chat      interactive chat loop
+  batch     JSONL prompts → JSONL outputs  serve     HTTP server (OpenAI + gollek routes)
+  convert   safetensors → GGUF (F32/F16/Q8_0/Q4_K)
+  quantize  GGUF → GGUF at another type, or safetensors → block-scaled FP8 safetensors
+  show      model config and tensor table  list      presets and models under $GOLLEK_HOME
+  bench     serving benchmark (bench.py)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+
+def _engine(args):
+    from .config import EngineConfig
+    from .engine.engine import LLMEngine
+    over = dict(model=args.model)
+    if getattr(args, "device", None):
+        over["device"] = args.device
+    if getattr(args, "max_model_len", None):
+        over["max_model_len"] = args.max_model_len
+    if getattr(args, "device", None) == "cpu":
+        over["dtype"] = "float32"
+        over["use_cuda_graphs"] = False
+    cfg = EngineConfig.load(getattr(args, "config", None), **over)
+    return LLMEngine(cfg)
+
+
+def _params(args):
+    from .engine.sequence import SamplingParams
+    return SamplingParams(temperature=args.temperature, top_p=args.top_p, top_k=args.top_k,
+                          max_tokens=args.max_tokens, seed=args.seed).validate()
+
+
+def cmd_run(args):
+    eng = _engine(args)
+    t0 = time.perf_counter()
+    out = eng.generate([args.prompt], _params(args))[0]
+    dt = time.perf_counter() - t0
+    text = out.text or (eng.tokenizer.decode(out.output_token_ids) if eng.tokenizer else str(out.output_token_ids))
+    print(text)
+    if args.stats:
+        n = len(out.output_token_ids)
+        print(f"\n[{n} tokens in {dt:.2f}s, {n / dt:.1f} tok/s, finish={out.finish_reason}]", file=sys.stderr)
+
+
+def cmd_chat(args):
+    eng = _engine(args)
+    history = []
+    print("chat (empty line or Ctrl-D to quit)")
+    for line in sys.stdin:
+        line = line.rstrip("\n")
+        if not line:
+            break
+        history.append({"role": "user", "content": line})
+        prompt = eng.tokenizer.apply_chat_template(history)
+        out = eng.generate([prompt], _params(args))[0]
+        text = out.text or eng.tokenizer.decode(out.output_token_ids)
+        history.append({"role": "assistant", "content": text})
+        print(text, flush=True)
+
+
+def cmd_batch(args):
+    eng = _engine(args)
+    prompts = [json.loads(l)["prompt"] for l in open(args.input) if l.strip()]
+    outs = eng.generate(prompts, _params(args))
+    with open(args.output, "w") as f:
+        for p, o in zip(prompts, outs):
+            text = o.text or (eng.tokenizer.decode(o.output_token_ids) if eng.tokenizer else "")
+            f.write(json.dumps({"prompt": p, "text": text, "tokens": o.output_token_ids,
+                                "finish_reason": o.finish_reason}) + "\n")
+    print(f"wrote {len(outs)} results to {args.output}")
+
+
+def cmd_serve(args):
+    from .server.__main__ import main as serve_main
+    serve_main(sys.argv[2:])
+
+
+def cmd_convert(args):
+    import torch
+    from .config import ModelConfig
+    from .loaders import gguf as G
+    from .loaders.safetensors import SafetensorsCheckpoint
+    with open(os.path.join(args.src, "config.json")) as f:
+        cfg = ModelConfig.from_hf(json.load(f))
+    ck = SafetensorsCheckpoint(args.src)
+    w = {k: ck.get(k).float() for k in ck.keys()}
+    t = G.TYPE_BY_NAME[args.type.upper()]
+    emb = G.TYPE_BY_NAME[args.embed_type.upper()] if args.embed_type else None
+    G.write_llama_gguf(args.dst, cfg, w, t, embed_type=emb)
+    print(f"wrote {args.dst} ({args.type})")
+
+
+def cmd_quantize(args):
+    from .loaders import gguf as G
+    if args.src.endswith(".gguf"):
+        cfg, w, f = G.load_llama_gguf(args.src)
+        G.write_llama_gguf(args.dst, cfg, w, G.TYPE_BY_NAME[args.type.upper()])
+        print(f"wrote {args.dst} ({args.type})")
+    else:
+        from .quant.fp8 import quantize_checkpoint_fp8
+        quantize_checkpoint_fp8(args.src, args.dst)
+        print(f"wrote {args.dst} (fp8 e4m3, 128x128 block scales)")
+
+
+def cmd_show(args):
+    if args.model.endswith(".gguf"):
+        from .loaders.gguf import GGUFFile, GGML_TYPES, config_from_gguf
+        f = GGUFFile(args.model)
+        print(json.dumps(vars(config_from_gguf(f.metadata)), default=str, indent=1))
+        for n, ti in list(f.tensors.items())[: args.max_tensors]:
+            print(f"{n:48s} {GGML_TYPES[ti.ggml_type][0]:6s} {list(ti.shape)}")
+        return
+    from .engine.engine import load_model_source
+    cfg, _, _ = load_model_source(args.model)
+    print(json.dumps(vars(cfg), default=str, indent=1))
+    print(f"parameters: {cfg.num_params() / 1e9:.2f} B")
+
+
+def cmd_list(args):
+    from .config import PRESETS
+    print("presets:")
+    for k, v in PRESETS.items():
+        print(f"  {k:16s} {v.num_params() / 1e9:7.2f} B params  {v.architecture}")
+    home = os.environ.get("GOLLEK_HOME", os.path.expanduser("~/.gollek"))
+    mdir = os.path.join(home, "models")
+    if os.path.isdir(mdir):
+        print(f"local models ({mdir}):")
+        for n in sorted(os.listdir(mdir)):
+            print("  " + n)
+
+
+def cmd_bench(args):
+    import subprocess
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.exit(subprocess.call([sys.executable, os.path.join(here, "bench.py")] + args.rest))
+
+
+def build_parser():
+    p = argparse.ArgumentParser(prog="gollek_b200")
+    sub = p.add_subparsers(dest="cmd", required=True)
+
+    def gen_opts(sp):
+        sp.add_argument("--model", "-m", default="tiny-llama")
+        sp.add_argument("--config", default=None)
+        sp.add_argument("--device", default=None)
+        sp.add_argument("--max-model-len", type=int, default=None)
+        sp.add_argument("--max-tokens", type=int, default=128)
+        sp.add_argument("--temperature", type=float, default=0.7)
+        sp.add_argument("--top-p", type=float, default=0.95)
+        sp.add_argument("--top-k", type=int, default=40)
+        sp.add_argument("--seed", type=int, default=None)
+
+    r = sub.add_parser("run")
+    gen_opts(r)
+    r.add_argument("prompt")
+    r.add_argument("--stats", action="store_true")
+    r.set_defaults(fn=cmd_run)
+    c = sub.add_parser("chat")
+    gen_opts(c)
+    c.set_defaults(fn=cmd_chat)
+    b = sub.add_parser("batch")
+    gen_opts(b)
+    b.add_argument("input")
+    b.add_argument("output")
+    b.set_defaults(fn=cmd_batch)
+    s = sub.add_parser("serve", add_help=False)
+    s.set_defaults(fn=cmd_serve)
+    cv = sub.add_parser("convert")
+    cv.add_argument("src")
+    cv.add_argument("dst")
+    cv.add_argument("--type", default="F16", choices=["F32", "F16", "BF16", "Q8_0", "Q4_K"])
+    cv.add_argument("--embed-type", default=None)
+    cv.set_defaults(fn=cmd_convert)
+    q = sub.add_parser("quantize")
+    q.add_argument("src")
+    q.add_argument("dst")
+    q.add_argument("--type", default="Q4_K")
+    q.set_defaults(fn=cmd_quantize)
+    sh = sub.add_parser("show")
+    sh.add_argument("model")
+    sh.add_argument("--max-tensors", type=int, default=40)
+    sh.set_defaults(fn=cmd_show)
+    ls = sub.add_parser("list")
+    ls.set_defaults(fn=cmd_list)
+    be = sub.add_parser("bench")
+    be.add_argument("rest", nargs=argparse.REMAINDER)
+    be.set_defaults(fn=cmd_bench)
+    return p
+
+
+def main(argv=None):
+    args = build_parser().parse_args(argv)
+    args.fn(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -99,8 +99,9 @@ def decode_splits(num_seqs: int, num_kv_heads: int, max_seq_len: int, num_sms: i
 def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                            seq_lens: torch.Tensor, scale: float, num_splits: int = 1,
                            out: Optional[torch.Tensor] = None,
-                           workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """One query token per sequence: q [B, H, D]."""
+                           workspace: Optional[torch.Tensor] = None, tensor_cores: bool = True) -> torch.Tensor:
+    """One query token per sequence: q [B, H, D]. head_dim 128 runs the tensor-core kernel
+    (``tensor_cores=False`` selects the CUDA-core kernel, used for other head sizes)."""
     if not q.is_cuda:
         B = q.shape[0]
         qsl = torch.arange(B + 1, dtype=torch.int32)
@@ -110,7 +111,7 @@ def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables
         B, H, D = q.shape
         workspace = torch.empty(B * H * num_splits * (D + 2), dtype=torch.float32, device=q.device)
     _C(2 if num_splits > 1 else 1).paged_decode_attention(out, q, kv_cache, block_tables, seq_lens, float(scale),
-                                                          int(num_splits), workspace)
+                                                          int(num_splits), workspace, bool(tensor_cores))
     return out
 
 
@@ -139,6 +140,30 @@ def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_table
 
 
 # ----------------------------------------------------------------------------- GEMM
+_PLAN_CACHE: dict = {}
+
+
+def gemm_plan(M: int, N: int, K: int, epi: int = EPI_NONE) -> tuple:
+    """(tile width, split-K factor) the tcgen05 GEMM uses for this shape."""
+    key = (M, N, K, epi)
+    p = _PLAN_CACHE.get(key)
+    if p is None:
+        p = tuple(cuda_ext().gemm_plan(M, N, K, epi))
+        _PLAN_CACHE[key] = p
+    return p
+
+
+def _gemm(out, a, w, residual, epi, bn):
+    M, K = a.shape
+    N = w.shape[0]
+    splits, ws = 1, None
+    if bn == 0:
+        bn, splits = gemm_plan(M, N, K, epi)
+    if splits > 1:  # fp32 partial sums, reduced (with the epilogue) by a second kernel
+        ws = torch.empty(splits * M * N, dtype=torch.float32, device=a.device)
+    _C(2 if splits > 1 else 1).gemm_bf16(out, a, w, residual, epi, bn, None, 0, splits, ws)
+
+
 def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None, bn: int = 0) -> torch.Tensor:
     """a [M, K] @ w[N, K]^T (+ residual), bf16 in/out, fp32 accumulate (tcgen05 on GPU)."""
@@ -147,7 +172,7 @@ def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
     M, N = a.shape[0], w.shape[0]
     out = torch.empty(M, N, dtype=a.dtype, device=a.device) if out is None else out
     epi = EPI_RESIDUAL if residual is not None else EPI_NONE
-    _C().gemm_bf16(out, a, w, residual, epi, bn, None, 0)
+    _gemm(out, a, w, residual, epi, bn)
     return out
 
 
@@ -158,7 +183,7 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.
         return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP), out)
     M, N = a.shape[0], w_gate_up.shape[0]
     out = torch.empty(M, N // 2, dtype=a.dtype, device=a.device) if out is None else out
-    _C().gemm_bf16(out, a, w_gate_up, None, EPI_SWIGLU, bn, None, 0)
+    _gemm(out, a, w_gate_up, None, EPI_SWIGLU, bn)
     return out
 
 

@@ -178,3 +178,49 @@ def test_penalties():
     ops.apply_penalties(logits, trip.to(DEV), rep.to(DEV), fr.to(DEV), pr.to(DEV))
     R.apply_penalties_triples(l2, trip, rep, fr, pr)
     torch.testing.assert_close(logits.cpu(), l2)
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("splits", [2, 3, 8])
+def test_gemm_split_k(epi, splits):
+    M, N, K = 200, 1024, 4096
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(30)) * 0.5)
+    w = bf(torch.randn(N, K, device=DEV, generator=_g(31)) * 0.02)
+    r = bf(torch.randn(M, N, device=DEV, generator=_g(32)))
+    out = torch.empty(M, N // 2 if epi == 2 else N, dtype=torch.bfloat16, device=DEV)
+    ws = torch.empty(splits * M * N, dtype=torch.float32, device=DEV)
+    ops.cuda_ext().gemm_bf16(out, a, w, r if epi == 1 else None, epi, 256, None, 0, splits, ws)
+    y = a.float() @ w.float().t()
+    if epi == 1:
+        y = y + r.float()
+    elif epi == 2:
+        y = R.gemm_swiglu(a.float(), w.float())
+    torch.testing.assert_close(out.float(), y, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 4096, 14336), (64, 6144, 4096), (256, 28672, 4096)])
+def test_gemm_auto_plan_decode_shapes(M, N, K):
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(33)) * 0.5)
+    w = bf(torch.randn(N, K, device=DEV, generator=_g(34)) * 0.02)
+    bn, splits = ops.gemm_plan(M, N, K)
+    y = ops.linear(a, w)
+    torch.testing.assert_close(y.float(), a.float() @ w.float().t(), rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("splits", [1, 4])
+@pytest.mark.parametrize("tc", [True, False])
+def test_paged_decode_attention_hd128(G, splits, tc):
+    if not tc and G == 16:
+        pytest.skip("the CUDA-core decode kernel is instantiated for groups up to 8")
+    Hk, D = 2, 128
+    H = Hk * G
+    lens = [1, 16, 17, 300, 1029, 64]
+    B = len(lens)
+    cache, bt, sl = _paged_setup(B, Hk, D, lens, seed=40 + G)
+    q = bf(torch.randn(B, H, D, device=DEV, generator=_g(41)))
+    scale = 1 / math.sqrt(D)
+    out = ops.paged_decode_attention(q, cache, bt, sl, scale, num_splits=splits, tensor_cores=tc)
+    qsl = torch.arange(B + 1, dtype=torch.int32)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl, scale)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
