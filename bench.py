@@ -52,7 +52,7 @@ def parse():
     p.add_argument("--output-len", type=int, default=256)
     p.add_argument("--max-num-seqs", type=int, default=256)
     p.add_argument("--max-batched-tokens", type=int, default=8192)
-    p.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--no-fill", action="store_true")
     return p.parse_args()
@@ -152,7 +152,15 @@ def main():
                       block_size=16, max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_batched_tokens,
                       max_model_len=args.prompt_max + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
                       enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm)
-    comm = NcclComm(di.rank, di.world_size) if di.world_size > 1 else None
+    comm = None
+    if di.world_size > 1:
+        if args.comm == "fused":
+            from gollek_b200.parallel.dist import cpu_group
+            from gollek_b200.parallel.symm import FusedTPComm
+            comm = FusedTPComm(di.rank, di.world_size, max_tokens=args.max_batched_tokens + args.max_num_seqs,
+                               hidden=mcfg.hidden_size, cpu_group=cpu_group())
+        else:
+            comm = NcclComm(di.rank, di.world_size)
     eng = LLMEngine(ec, model_cfg=mcfg, comm=comm)
     stream = Stream(mcfg.vocab_size, args.prompt_min, args.prompt_max, args.output_len)
     sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)

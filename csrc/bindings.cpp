@@ -3,6 +3,7 @@
 // All torch-tensor validation happens here (compiled by the host compiler); the .cu files
 // only see raw pointers, strides and the current CUDA stream.
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "kernels/launchers.h"
@@ -240,9 +241,60 @@ void sample_out(torch::Tensor out, torch::Tensor logits, torch::Tensor temps, to
                 offsets.data_ptr<int64_t>(), cur_stream());
 }
 
+// ---------------------------------------------------------------- symmetric heap + TP collectives
+torch::Tensor symm_alloc_tensor(int64_t bytes, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = symm_alloc((size_t)bytes);
+  return torch::from_blob(p, {bytes}, [](void* q) { symm_free(q); },
+                          torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+}
+
+pybind11::bytes symm_handle_py(torch::Tensor region) {
+  auto h = symm_ipc_handle(region.data_ptr());
+  return pybind11::bytes(reinterpret_cast<const char*>(h.data()), h.size());
+}
+
+uint64_t symm_open_py(pybind11::bytes handle) {
+  std::string s = handle;
+  std::vector<uint8_t> h(s.begin(), s.end());
+  return reinterpret_cast<uint64_t>(symm_open_peer(h));
+}
+
+void symm_close_py(uint64_t p) { symm_close_peer(reinterpret_cast<void*>(p)); }
+
+int64_t symm_status_py(torch::Tensor region) { return (int64_t)symm_read_status(region.data_ptr()); }
+
+void tp_ar_rmsnorm_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int64_t p1, int64_t g, int64_t parity,
+                      bool one_shot, torch::Tensor residual, torch::Tensor w, torch::Tensor x_out, double eps,
+                      double timeout_s, int64_t grid) {
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  check_bf16(x_out, "x_out");
+  TORCH_CHECK(residual.is_contiguous() && x_out.is_contiguous() && residual.sizes() == x_out.sizes(),
+              "residual / x_out must be contiguous [T, d]");
+  launch_tp_ar_rmsnorm(bases, (int)rank, p0, p1, g, (int)parity, one_shot, residual.data_ptr(), w.data_ptr(),
+                       x_out.data_ptr(), residual.size(0), residual.size(1), (float)eps, timeout_s, (int)grid,
+                       cur_stream());
+}
+
+void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int64_t p1, int64_t parity,
+                     torch::Tensor out, double timeout_s, int64_t grid) {
+  check_bf16(out, "out");
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  launch_tp_allreduce(bases, (int)rank, p0, p1, (int)parity, out.data_ptr(), out.numel(), timeout_s, (int)grid,
+                      cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("symm_alloc", &symm_alloc_tensor, "allocate a zeroed IPC-shareable device region (uint8 tensor)");
+  m.def("symm_ipc_handle", &symm_handle_py);
+  m.def("symm_open_peer", &symm_open_py);
+  m.def("symm_close_peer", &symm_close_py);
+  m.def("symm_status", &symm_status_py);
+  m.def("tp_allreduce_add_rmsnorm", &tp_ar_rmsnorm_py, "fused TP all-reduce + residual add + RMSNorm over P2P");
+  m.def("tp_allreduce", &tp_allreduce_py, "TP all-reduce over P2P");
   m.doc() = "gollek_b200 sm_100a kernels";
   m.def("rms_norm", &rms_norm_out, "RMSNorm (K1)");
   m.def("fused_add_rms_norm", &fused_add_rms_norm_out, "residual add + RMSNorm (K1)");

@@ -1,0 +1,328 @@
+// Symmetric device heap over CUDA IPC + fused tensor-parallel collectives over NVLink P2P (sm_100a).
+//
+// Heap: each rank cudaMalloc's one region of identical size; IPC handles are exchanged by the
+// host (gloo) and every peer region is mapped with cudaIpcOpenMemHandle, so a kernel can load
+// from / store to any rank's region through NVLink/NVSwitch. A small header at the start of
+// each region holds the barrier flags, an arrive counter, the epoch and a status word.
+//
+// tp_allreduce_add_rmsnorm (C1/C4 in the design): for the row-parallel projections (o_proj,
+// down_proj) each rank's GEMM writes its partial [T, d] directly into its own symmetric
+// "partial" buffer (two of them, alternating per call). One persistent kernel then
+//   A) start barrier: every rank is past its previous call (so no peer still reads a buffer
+//      this call overwrites);
+//   1) reduce-scatter by rows: rank r sums the N partials of its row chunk with P2P loads,
+//      adds the residual rows, and writes the new residual rows to its "gather" buffer;
+//   B) barrier: every rank finished phase 1 (last CTA to arrive signals all peers);
+//   2) all-gather + RMSNorm: every rank reads each row from its owner's gather buffer (P2P),
+//      stores it as the new residual and writes x = rmsnorm(residual) * w.
+// (one_shot = true skips the scatter: every rank sums all N partials for all rows, one barrier;
+// the latency-optimal choice for decode-sized T.)
+//
+// Flags carry a per-call epoch (monotonic), so nothing is reset between calls. All waits are
+// bounded by a globaltimer deadline; on timeout a status bit is set and the kernel finishes
+// without the missing data (the host checks the status word and raises). No multicast and no
+// TMA on peer memory: plain ld/st.global over NVLink.
+#include "../common/common.cuh"
+#include "../kernels/launchers.h"
+
+#include <vector>
+
+namespace gollek {
+
+// Header at the start of every rank's region (peers write into it).
+struct SymmHeader {
+  uint32_t flag_a[16];   // flag_a[src] = epoch when rank src entered call `epoch`
+  uint32_t flag_b[16];   // flag_b[src] = epoch when rank src finished phase 1
+  uint32_t arrive;       // local CTA arrive counter for barrier B
+  uint32_t epoch;        // last completed call
+  uint32_t status;       // kStatus* bits
+  uint32_t pad[29];
+};
+static_assert(sizeof(SymmHeader) == 256, "header size");
+
+constexpr int kArThreads = 512;
+
+GOLLEK_DEVICE uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait until flag >= target (wrap-safe), bounded by `limit_ns`.
+GOLLEK_DEVICE bool wait_geq(const uint32_t* flag, uint32_t target, uint64_t limit_ns) {
+  if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+  const uint64_t t0 = gtimer();
+  while ((int32_t)(ld_acquire_sys(flag) - target) < 0) {
+    if (gtimer() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+struct ArArgs {
+  uint8_t* bases[8];          // every rank's region base (own included)
+  int64_t partial_off[2];     // byte offsets of the two partial buffers in a region
+  int64_t gather_off;         // byte offset of the gather buffer
+  int rank, world;
+  int T, d;
+  int parity;                 // which partial buffer this call reads
+  int one_shot;
+  float eps;
+  uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __nv_bfloat16* __restrict__ residual,
+                                                                    const __nv_bfloat16* __restrict__ w,
+                                                                    __nv_bfloat16* __restrict__ x_out) {
+  SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
+  __shared__ uint32_t s_epoch;
+  __shared__ float red[kArThreads / 32];
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  // ---- barrier A
+  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+    __threadfence_system();
+    SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[threadIdx.x]);
+    st_release_sys(&peer->flag_a[a.rank], epoch);
+  }
+  if (threadIdx.x < a.world) {
+    if (!wait_geq(&me->flag_a[threadIdx.x], epoch, a.timeout_ns)) {
+      atomicOr(&me->status, kStatusPeerTimeout);
+      s_ok = 0;
+    }
+  }
+  __syncthreads();
+  const int nvec = a.d / 8;
+  const int world = a.world;
+  if (!a.one_shot) {
+    // ---- phase 1: reduce my row chunk into my gather buffer
+    const int chunk = (a.T + world - 1) / world;
+    const int r0 = a.rank * chunk, r1 = min(a.T, r0 + chunk);
+    __nv_bfloat16* gmine = reinterpret_cast<__nv_bfloat16*>(a.bases[a.rank] + a.gather_off);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)(r1 - r0) * nvec;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int row = r0 + (int)(i / nvec), v = (int)(i % nvec);
+      const int64_t off = (int64_t)row * a.d + v * 8;
+      float acc[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), acc);
+      for (int p = 0; p < world; ++p) {
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
+        float t[8];
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(src + off), t);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += t[e];
+      }
+      *reinterpret_cast<uint4*>(gmine + off) = float_to_bf16x8(acc);
+    }
+    // ---- barrier B: last local CTA signals every peer
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const uint32_t prev = atomicAdd(&me->arrive, 1u);
+      if (prev == gridDim.x - 1) {
+        me->arrive = 0;
+        for (int p = 0; p < world; ++p) {
+          SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[p]);
+          st_release_sys(&peer->flag_b[a.rank], epoch);
+        }
+      }
+    }
+    if (threadIdx.x < world) {
+      if (!wait_geq(&me->flag_b[threadIdx.x], epoch, a.timeout_ns)) {
+        atomicOr(&me->status, kStatusPeerTimeout);
+        s_ok = 0;
+      }
+    }
+    __syncthreads();
+  }
+  // ---- phase 2: gather rows (or reduce all rows, one-shot) + RMSNorm, one row per CTA iteration
+  const int chunk = (a.T + world - 1) / world;
+  for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
+    const int64_t base = (int64_t)row * a.d;
+    float ss = 0.f;
+    // each thread owns up to 2 vectors of the row (d <= 8192)
+    float vals[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int v = threadIdx.x + k * kArThreads;
+      if (v < nvec) {
+        const int64_t off = base + v * 8;
+        if (a.one_shot) {
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), vals[k]);
+          for (int p = 0; p < world; ++p) {
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
+            float t[8];
+            bf16x8_to_float(*reinterpret_cast<const uint4*>(src + off), t);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vals[k][e] += t[e];
+          }
+          uint4 packed = float_to_bf16x8(vals[k]);
+          bf16x8_to_float(packed, vals[k]);
+          *reinterpret_cast<uint4*>(residual + off) = packed;
+        } else {
+          const int owner = min(row / chunk, world - 1);
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[owner] + a.gather_off);
+          const uint4 u = *reinterpret_cast<const uint4*>(src + off);
+          *reinterpret_cast<uint4*>(residual + off) = u;
+          bf16x8_to_float(u, vals[k]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += vals[k][e] * vals[k][e];
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kArThreads / 32 ? red[threadIdx.x] : 0.f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float rs = rsqrtf(red[0] / (float)a.d + a.eps);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int v = threadIdx.x + k * kArThreads;
+      if (v < nvec) {
+        float wf[8];
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(w + v * 8), wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vals[k][e] = vals[k][e] * rs * wf[e];
+        *reinterpret_cast<uint4*>(x_out + base + v * 8) = float_to_bf16x8(vals[k]);
+      }
+    }
+  }
+  // ---- epilogue: the call is complete on this rank once every CTA got here; CTA 0 records it
+  if (a.one_shot) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t prev = atomicAdd(&me->arrive, 1u);
+      if (prev == gridDim.x - 1) {
+        me->arrive = 0;
+        me->epoch = epoch;
+      }
+    }
+  } else if (blockIdx.x == 0 && threadIdx.x == 0) {
+    me->epoch = epoch;  // every CTA read the epoch before barrier B completed
+  }
+}
+
+// Plain all-reduce (sum) of the partial buffer into `out` (no residual / norm), one-shot.
+__global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(ArArgs a, __nv_bfloat16* __restrict__ out,
+                                                                  int64_t nvec_total) {
+  SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+    __threadfence_system();
+    SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[threadIdx.x]);
+    st_release_sys(&peer->flag_a[a.rank], epoch);
+  }
+  if (threadIdx.x < a.world && !wait_geq(&me->flag_a[threadIdx.x], epoch, a.timeout_ns))
+    atomicOr(&me->status, kStatusPeerTimeout);
+  __syncthreads();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec_total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < a.world; ++p) {
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
+      float t[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(src + i * 8), t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += t[e];
+    }
+    *reinterpret_cast<uint4*>(out + i * 8) = float_to_bf16x8(acc);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&me->arrive, 1u);
+    if (prev == gridDim.x - 1) {
+      me->arrive = 0;
+      me->epoch = epoch;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------- host side
+void* symm_alloc(size_t bytes) {
+  void* p = nullptr;
+  GOLLEK_CUDA_CHECK(cudaMalloc(&p, bytes));
+  GOLLEK_CUDA_CHECK(cudaMemset(p, 0, bytes));
+  return p;
+}
+
+void symm_free(void* p) { cudaFree(p); }
+
+std::vector<uint8_t> symm_ipc_handle(void* p) {
+  cudaIpcMemHandle_t h;
+  GOLLEK_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(&h);
+  return std::vector<uint8_t>(b, b + sizeof(h));
+}
+
+void* symm_open_peer(const std::vector<uint8_t>& handle) {
+  throw_if(handle.size() != sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  GOLLEK_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+
+void symm_close_peer(void* p) { cudaIpcCloseMemHandle(p); }
+
+static ArArgs make_args(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int64_t g, int T,
+                        int d, int parity, bool one_shot, float eps, double timeout_s) {
+  ArArgs a{};
+  throw_if(bases.size() > 8 || bases.empty(), "tp collectives support 1..8 ranks");
+  for (size_t i = 0; i < bases.size(); ++i) a.bases[i] = reinterpret_cast<uint8_t*>(bases[i]);
+  a.partial_off[0] = p0;
+  a.partial_off[1] = p1;
+  a.gather_off = g;
+  a.rank = rank;
+  a.world = (int)bases.size();
+  a.T = T;
+  a.d = d;
+  a.parity = parity;
+  a.one_shot = one_shot ? 1 : 0;
+  a.eps = eps;
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  return a;
+}
+
+void launch_tp_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int64_t g,
+                          int parity, bool one_shot, void* residual, const void* w, void* x_out, int T, int d,
+                          float eps, double timeout_s, int grid, cudaStream_t s) {
+  throw_if(d % 8 != 0 || d > 16 * kArThreads, "tp all-reduce: hidden size must be a multiple of 8, <= 8192");
+  if (T == 0) return;
+  ArArgs a = make_args(bases, rank, p0, p1, g, T, d, parity, one_shot, eps, timeout_s);
+  tp_ar_rmsnorm_kernel<<<grid, kArThreads, 0, s>>>(a, reinterpret_cast<__nv_bfloat16*>(residual),
+                                                   reinterpret_cast<const __nv_bfloat16*>(w),
+                                                   reinterpret_cast<__nv_bfloat16*>(x_out));
+  check_launch("tp_allreduce_add_rmsnorm");
+}
+
+void launch_tp_allreduce(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int parity, void* out,
+                         int64_t numel, double timeout_s, int grid, cudaStream_t s) {
+  throw_if(numel % 8 != 0, "tp all-reduce: element count must be a multiple of 8");
+  if (numel == 0) return;
+  ArArgs a = make_args(bases, rank, p0, p1, 0, 0, 0, parity, true, 0.f, timeout_s);
+  tp_allreduce_kernel<<<grid, kArThreads, 0, s>>>(a, reinterpret_cast<__nv_bfloat16*>(out), numel / 8);
+  check_launch("tp_allreduce");
+}
+
+uint32_t symm_read_status(void* base) {
+  uint32_t st = 0;
+  GOLLEK_CUDA_CHECK(cudaMemcpy(&st, reinterpret_cast<uint8_t*>(base) + offsetof(SymmHeader, status), 4,
+                               cudaMemcpyDeviceToHost));
+  return st;
+}
+
+}  // namespace gollek

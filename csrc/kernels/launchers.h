@@ -8,6 +8,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace gollek {
 
@@ -58,5 +59,18 @@ void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V,
                    const int64_t* offsets, cudaStream_t s);
 
 int device_num_sms();
+
+// ---- symmetric heap + tensor-parallel collectives (csrc/comm/symm.cu)
+void* symm_alloc(size_t bytes);
+void symm_free(void* p);
+std::vector<uint8_t> symm_ipc_handle(void* p);
+void* symm_open_peer(const std::vector<uint8_t>& handle);
+void symm_close_peer(void* p);
+uint32_t symm_read_status(void* base);
+void launch_tp_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int64_t g,
+                          int parity, bool one_shot, void* residual, const void* w, void* x_out, int T, int d,
+                          float eps, double timeout_s, int grid, cudaStream_t s);
+void launch_tp_allreduce(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int parity, void* out,
+                         int64_t numel, double timeout_s, int grid, cudaStream_t s);
 
 }  // namespace gollek

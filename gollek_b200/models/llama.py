@@ -56,13 +56,29 @@ class AttnMetadata:
 
 
 class TPComm:
-    """Collectives used by the model under tensor parallelism (no-ops at tp_size 1)."""
+    """Collectives used by the model under tensor parallelism (no-ops at tp_size 1).
+
+    ``allreduce_add_rmsnorm`` is the one collective on the layer path: it follows each
+    row-parallel GEMM (o_proj, down_proj) and folds in the residual add and the next RMSNorm.
+    Implementations: this base class (single GPU), ``parallel.dist.NcclComm`` (NCCL all-reduce +
+    the fused norm kernel; the baseline) and ``parallel.symm.FusedTPComm`` (one P2P kernel).
+    """
+
+    fused_ar = False
 
     def __init__(self, rank: int = 0, size: int = 1):
         self.rank, self.size = rank, size
 
+    def partial_buffer(self, T: int) -> Optional[torch.Tensor]:
+        """Where the next row-parallel GEMM should write its partial output (None = allocate)."""
+        return None
+
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         return t
+
+    def allreduce_add_rmsnorm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                              eps: float) -> torch.Tensor:
+        return ops.fused_add_rms_norm(self.all_reduce(h), residual, w, eps)
 
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
         return t
@@ -255,32 +271,33 @@ class LlamaModel:
         ``hidden_only`` the final-norm hidden states of every token [T, hidden]."""
         cfg = self.cfg
         eps = cfg.rms_norm_eps
+        T = input_ids.shape[0]
         h = ops.embedding(input_ids, self.embed)
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
-        x = h
+        n = len(self.layers)
+        x = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
         for li, L in enumerate(self.layers):
-            if li == 0:
-                x = ops.rms_norm(h, L["in_norm"], eps)
-            else:
-                x = ops.fused_add_rms_norm(h, residual, L["in_norm"], eps)
             qkv = ops.linear(x, L["w_qkv"])
             if self.lora is not None:
-                qkv = self.lora.apply(li, "qkv", x, qkv)
+                self.lora.apply(li, "qkv", x, qkv)
             cache = kv_cache[li] if kv_cache is not None else None
             q = ops.rope_kv_write(qkv, meta.positions, self.cos_sin, cache, meta.slot_mapping,
                                   self.H, self.Hk, self.D)
-            a = self._attention(q, cache, meta).view(q.shape[0], self.H * self.D)
-            h = ops.linear(a, L["w_o"])
+            a = self._attention(q, cache, meta).view(T, self.H * self.D)
+            h = ops.linear(a, L["w_o"], out=self.comm.partial_buffer(T))
             if self.lora is not None:
-                h = self.lora.apply(li, "o", a, h)
-            h = self.comm.all_reduce(h)
-            x = ops.fused_add_rms_norm(h, residual, L["post_norm"], eps)
+                self.lora.apply(li, "o", a, h)
+            x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
             if cfg.is_moe:
                 h = self._moe(x, L)
+                buf = self.comm.partial_buffer(T)
+                if buf is not None:
+                    buf.copy_(h)
+                    h = buf
             else:
-                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"])
-            h = self.comm.all_reduce(h)
-        x = ops.fused_add_rms_norm(h, residual, self.norm, eps)
+                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"], out=self.comm.partial_buffer(T))
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
+            x = self.comm.allreduce_add_rmsnorm(h, residual, nxt, eps)
         if hidden_only:
             return x
         if meta.logits_indices is not None:

@@ -35,6 +35,7 @@ CUDA_SOURCES = [
     "kernels/attention.cu",
     "kernels/gemm.cu",
     "kernels/sampling.cu",
+    "comm/symm.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

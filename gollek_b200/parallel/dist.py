@@ -81,7 +81,8 @@ def shutdown() -> None:
 
 
 class NcclComm(TPComm):
-    """Tensor-parallel collectives through NCCL (the baseline path)."""
+    """Tensor-parallel collectives through NCCL (the baseline path): NCCL all-reduce followed by
+    the fused residual-add + RMSNorm kernel."""
 
     def __init__(self, rank: int, size: int, group=None):
         super().__init__(rank, size)
@@ -97,6 +98,10 @@ class NcclComm(TPComm):
         if self.size == 1:
             return t
         B, v = t.shape
-        buf = torch.empty(self.size, B, v, dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(buf, t.contiguous(), group=self.group)
-        return buf.permute(1, 0, 2).reshape(B, self.size * v)
+        if t.is_cuda:
+            buf = torch.empty(self.size, B, v, dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(buf, t.contiguous(), group=self.group)
+            return buf.permute(1, 0, 2).reshape(B, self.size * v)
+        parts = [torch.empty_like(t) for _ in range(self.size)]
+        dist.all_gather(parts, t.contiguous(), group=self.group)
+        return torch.cat(parts, dim=1)

@@ -1,0 +1,52 @@
+"""Per-rank body of the 2-GPU collective tests (spawned processes, NCCL + symmetric heap)."""
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def run_collectives(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+        from gollek_b200 import ops
+        from gollek_b200.parallel.dist import cpu_group, init_distributed
+        from gollek_b200.parallel.symm import FusedTPComm
+        init_distributed(backend="nccl", timeout_s=60)
+        d = 4096
+        comm = FusedTPComm(rank, world, max_tokens=1024, hidden=d, cpu_group=cpu_group(), one_shot_max_tokens=16)
+        errs = []
+        for T in (1, 7, 16, 300, 1024):
+            for rep in range(3):  # consecutive calls exercise the buffer parity and epochs
+                g = torch.Generator(device="cuda").manual_seed(1000 * T + 10 * rep + rank)
+                h = (torch.randn(T, d, device="cuda", generator=g) * 0.5).bfloat16()
+                gs = torch.Generator(device="cuda").manual_seed(7 * T + rep)
+                res = torch.randn(T, d, device="cuda", generator=gs).bfloat16()
+                w = (torch.rand(d, device="cuda", generator=gs) + 0.5).bfloat16()
+                # NCCL oracle
+                h_ref = h.clone()
+                dist.all_reduce(h_ref)
+                res_ref = res.clone()
+                x_ref = ops.fused_add_rms_norm(h_ref, res_ref, w, 1e-5)
+                x = comm.allreduce_add_rmsnorm(h, res, w, 1e-5)
+                torch.cuda.synchronize()
+                # relative to magnitude: the fused kernel rounds the fp32 sum once, NCCL + norm twice
+                errs.append((T, rep, float(((x.float() - x_ref.float()).abs() / (1 + x_ref.float().abs())).max()),
+                             float(((res.float() - res_ref.float()).abs() / (1 + res_ref.float().abs())).max())))
+            # plain all-reduce
+            t = (torch.randn(T, d, device="cuda", generator=g)).bfloat16()
+            t_ref = t.clone()
+            dist.all_reduce(t_ref)
+            comm.all_reduce(t)
+            torch.cuda.synchronize()
+            errs.append((T, "ar", float(((t.float() - t_ref.float()).abs() / (1 + t_ref.float().abs())).max()), 0.0))
+        comm.check()
+        result_q.put((rank, errs, None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+        result_q.put((rank, None, traceback.format_exc()))
