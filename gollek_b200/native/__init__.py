@@ -36,6 +36,7 @@ CUDA_SOURCES = [
     "kernels/gemm.cu",
     "kernels/sampling.cu",
     "comm/symm.cu",
+    "kernels/noalloc.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",
