@@ -285,9 +285,40 @@ void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int6
                       cur_stream());
 }
 
+void lora_shrink_py(torch::Tensor V, torch::Tensor x, torch::Tensor A, torch::Tensor seg_ptr, torch::Tensor tok_idx,
+                    torch::Tensor seg_slot) {
+  check_cuda(V, "V");
+  TORCH_CHECK(V.scalar_type() == at::kFloat && V.stride(1) == 1, "lora: V fp32 [T, R]");
+  check_bf16(x, "x");
+  check_bf16(A, "A");
+  check_i32(seg_ptr, "seg_ptr");
+  check_i32(tok_idx, "tok_idx");
+  check_i32(seg_slot, "seg_slot");
+  TORCH_CHECK(A.dim() == 3 && A.is_contiguous() && A.size(2) == x.size(1) && x.stride(1) == 1, "lora: A [slots, R, K]");
+  TORCH_CHECK(V.size(1) >= A.size(1), "lora: V narrower than R");
+  launch_lora_shrink(V.data_ptr<float>(), V.stride(0), x.data_ptr(), x.stride(0), A.data_ptr(), A.size(1), A.size(2),
+                     seg_ptr.data_ptr<int>(), tok_idx.data_ptr<int>(), seg_slot.data_ptr<int>(), seg_slot.numel(),
+                     cur_stream());
+}
+
+void lora_expand_py(torch::Tensor Y, torch::Tensor V, torch::Tensor B, int64_t n1, int64_t n2, torch::Tensor scales,
+                    torch::Tensor seg_ptr, torch::Tensor tok_idx, torch::Tensor seg_slot) {
+  check_bf16(Y, "Y");
+  check_cuda(V, "V");
+  check_bf16(B, "B");
+  TORCH_CHECK(V.scalar_type() == at::kFloat && V.is_contiguous(), "lora: V fp32 contiguous");
+  TORCH_CHECK(B.dim() == 3 && B.is_contiguous() && B.size(1) == Y.size(1) && Y.stride(1) == 1, "lora: B [slots, N, r]");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat, "lora: fp32 scales");
+  launch_lora_expand(Y.data_ptr(), Y.stride(0), V.data_ptr<float>(), V.size(1), B.data_ptr(), B.size(1), B.size(2),
+                     (int)n1, (int)n2, scales.data_ptr<float>(), seg_ptr.data_ptr<int>(), tok_idx.data_ptr<int>(),
+                     seg_slot.data_ptr<int>(), seg_slot.numel(), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("lora_shrink", &lora_shrink_py, "multi-LoRA shrink V += x A^T per adapter segment (K10)");
+  m.def("lora_expand", &lora_expand_py, "multi-LoRA expand Y += s V B^T per adapter segment (K10)");
   m.def("symm_alloc", &symm_alloc_tensor, "allocate a zeroed IPC-shareable device region (uint8 tensor)");
   m.def("symm_ipc_handle", &symm_handle_py);
   m.def("symm_open_peer", &symm_open_py);

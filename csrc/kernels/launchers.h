@@ -60,6 +60,13 @@ void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V,
 
 int device_num_sms();
 
+// ---- multi-LoRA (K10)
+void launch_lora_shrink(float* V, int ldv, const void* x, int64_t ldx, const void* A, int R, int K,
+                        const int* seg_ptr, const int* tok_idx, const int* seg_slot, int num_segs, cudaStream_t s);
+void launch_lora_expand(void* Y, int64_t ldy, const float* V, int ldv, const void* B, int N, int rank, int n1,
+                        int n2, const float* scales, const int* seg_ptr, const int* tok_idx, const int* seg_slot,
+                        int num_segs, cudaStream_t s);
+
 // ---- symmetric heap + tensor-parallel collectives (csrc/comm/symm.cu)
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);

@@ -75,6 +75,10 @@ class LLMEngine:
         if cfg.scheduling_policy == "wait":
             predictor = host_ext().LengthPredictor(64, 1.0, float(cfg.max_model_len), 0.05, 8)
         self.scheduler = Scheduler(cfg, self.kv, predictor)
+        self.lora_manager = None
+        if cfg.enable_lora:
+            from .lora import LoRAManager
+            self.lora_manager = LoRAManager(self.model, cfg.max_loras, cfg.max_lora_rank)
         self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
         self.seqs: Dict[str, Sequence] = {}
         self.metrics = EngineMetrics()
@@ -102,11 +106,22 @@ class LLMEngine:
         if room < 1:
             raise ValueError("prompt too long for max_model_len")
         params.max_tokens = min(params.max_tokens, room)
+        if lora_id and (self.lora_manager is None or lora_id not in self.lora_manager.adapters):
+            raise ValueError(f"unknown LoRA adapter id {lora_id}")
         seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
         self.scheduler.add(seq)
         self.seqs[request_id] = seq
         self.metrics.on_arrival()
         return request_id
+
+    def add_lora(self, name: str, path: Optional[str] = None, seed: Optional[int] = None, rank: int = 16) -> int:
+        """Register a PEFT adapter directory (or a random adapter when ``path`` is None); returns its id."""
+        if self.lora_manager is None:
+            raise RuntimeError("engine was created without enable_lora")
+        if path is not None:
+            return self.lora_manager.load_peft(path, name)
+        return self.lora_manager.random_adapter(name, seed if seed is not None else len(self.lora_manager.adapters),
+                                                rank=rank)
 
     def abort_request(self, request_id: str) -> bool:
         seq = self.scheduler.abort(request_id)

@@ -125,8 +125,15 @@ class ModelRunner:
         nd = len(out.decode)
         h = self.host
         dev = self.device
+        lora = self.model.lora
+        if lora is not None:
+            ids = []
+            for c in out.chunks:
+                ids.extend([c.seq.lora_id] * c.num_tokens)
+            lora.set_batch(ids)
+        lora_active = lora is not None and lora.active
         all_greedy = all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
-        if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0
+        if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0 and not lora_active
                 and self._graph_for(nd) is not None):
             return self._replay_decode(nd)
         nb = int(max(1, (int(h.seq_lens[:n].max()) + self.block_size - 1) // self.block_size))

@@ -37,6 +37,7 @@ CUDA_SOURCES = [
     "kernels/sampling.cu",
     "comm/symm.cu",
     "kernels/noalloc.cu",
+    "kernels/lora.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",
