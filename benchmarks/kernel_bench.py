@@ -149,6 +149,20 @@ def main():
             off = torch.zeros(B, dtype=torch.int64, device=dev)
             ms = time_cuda(lambda: ops.sample(lf, t, k, p, mp, sd, off, out=out), iters=args.iters, flush_bytes=flush)
             rec(f"sample_topk_topp_B{B}_V{V}", ms, 0, 4.0 * B * V)
+    if "gguf" in only:
+        from gollek_b200.native import host_ext
+        from gollek_b200.quant.gguf_weights import QWeight
+        h = host_ext()
+        for name, N, K in (("qkv", 6144, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336)):
+            w = torch.randn(N * K) * 0.02
+            for qtype, q in ((12, h.quantize_q4_k), (8, h.quantize_q8_0)):
+                qw = QWeight(q(w).to(dev), N, K, qtype)
+                for M in (1, 4, 16, 64, 256):
+                    x = torch.randn(M, K, device=dev).bfloat16()
+                    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                    ms = time_cuda(lambda: ops.linear(x, qw, out=out), iters=args.iters, flush_bytes=flush)
+                    rec(f"gguf_{'q4k' if qtype == 12 else 'q8_0'}_{name}_M{M}", ms, 2.0 * M * N * K,
+                        qw.nbytes() + 2.0 * M * (K + N))
     if args.json:
         with open(args.json, "w") as f:
             for r in rows:

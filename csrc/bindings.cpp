@@ -314,9 +314,39 @@ void lora_expand_py(torch::Tensor Y, torch::Tensor V, torch::Tensor B, int64_t n
                      seg_slot.data_ptr<int>(), seg_slot.numel(), cur_stream());
 }
 
+void gguf_gemv_py(torch::Tensor y, torch::Tensor x, torch::Tensor W, int64_t qtype, int64_t N, int64_t K, bool swiglu) {
+  check_bf16(y, "y");
+  check_bf16(x, "x");
+  check_cuda(W, "W");
+  TORCH_CHECK(W.scalar_type() == at::kByte && W.is_contiguous(), "gguf: raw uint8 weight blocks");
+  TORCH_CHECK(x.stride(1) == 1 && y.stride(1) == 1 && x.size(1) == K, "gguf gemv: shapes");
+  TORCH_CHECK(x.stride(0) % 8 == 0, "gguf gemv: x row pitch must keep 16-byte alignment");
+  launch_gguf_gemv(y.data_ptr(), y.stride(0), x.data_ptr(), x.stride(0), W.data_ptr(), (int)qtype, (int)N, (int)K,
+                   x.size(0), swiglu, cur_stream());
+}
+
+void gguf_dequant_py(torch::Tensor out, torch::Tensor W, int64_t qtype) {
+  check_bf16(out, "out");
+  check_cuda(W, "W");
+  TORCH_CHECK(W.scalar_type() == at::kByte && W.is_contiguous() && out.is_contiguous(), "gguf dequant: layout");
+  launch_gguf_dequant(out.data_ptr(), W.data_ptr(), (int)qtype, out.numel(), cur_stream());
+}
+
+void embedding_q8_0_py(torch::Tensor out, torch::Tensor ids, torch::Tensor table, int64_t vocab) {
+  check_bf16(out, "out");
+  check_i32(ids, "ids");
+  check_cuda(table, "table");
+  TORCH_CHECK(out.is_contiguous(), "embedding: contiguous out");
+  launch_embedding_q8_0(out.data_ptr(), ids.data_ptr<int>(), table.data_ptr(), ids.size(0), out.size(1), (int)vocab,
+                        cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gguf_gemv", &gguf_gemv_py, "Q4_K / Q8_0 GEMV for up to 16 tokens (K9)");
+  m.def("gguf_dequant", &gguf_dequant_py, "Q4_K / Q8_0 -> bf16 (K9)");
+  m.def("embedding_q8_0", &embedding_q8_0_py, "embedding gather from a Q8_0 table (K9/K13)");
   m.def("lora_shrink", &lora_shrink_py, "multi-LoRA shrink V += x A^T per adapter segment (K10)");
   m.def("lora_expand", &lora_expand_py, "multi-LoRA expand Y += s V B^T per adapter segment (K10)");
   m.def("symm_alloc", &symm_alloc_tensor, "allocate a zeroed IPC-shareable device region (uint8 tensor)");

@@ -1,0 +1,285 @@
+// K9: GGUF-quantized weights on the GPU (sm_100a): Q4_K / Q8_0 GEMV and dequantization.
+//
+// Weights stay in their ggml block format in HBM ([N rows] x [K/256 Q4_K blocks of 144 B] or
+// [K/32 Q8_0 blocks of 34 B]) and are decoded in registers.
+//   q4k_gemv   y[m, n] = sum_k x[m, k] W[n, k] for up to 16 tokens (decode): one warp per row group,
+//              lane l decodes 8 weights of sub-block l/4 of every super-block (one 8-byte load of
+//              packed nibbles + the 6-bit scale/min of that sub-block) and applies them to every
+//              token; optional SwiGLU epilogue over gate/up rows interleaved in groups of 64.
+//   q8_0_gemv  same for Q8_0 (lm_head / embeddings of Q4_K_M-style checkpoints).
+//   dequant_*  whole-matrix dequantization to bf16 (prefill: followed by the tcgen05 GEMM).
+// Block layouts: ggml spec (see csrc/host/gguf_quant.cpp); the reference decodes these only on
+// the CPU (runner/gguf/gollek-gguf-loader/…/gguf/quant/Dequantizer.java, GGUFVectorOps.java:73-88).
+#include "../common/common.cuh"
+#include "launchers.h"
+
+#include <algorithm>
+
+using namespace gollek;
+
+namespace {
+
+constexpr int kGemvMaxTok = 16;
+constexpr int kGemvWarps = 8;
+
+GOLLEK_DEVICE void q4k_scale_min(int j, const uint8_t* sc12, float& sc, float& mn) {
+  uint8_t s, m;
+  if (j < 4) {
+    s = sc12[j] & 63;
+    m = sc12[j + 4] & 63;
+  } else {
+    s = (sc12[j + 4] & 0xF) | ((sc12[j - 4] >> 6) << 4);
+    m = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
+  }
+  sc = (float)s;
+  mn = (float)m;
+}
+
+GOLLEK_DEVICE float h2f(const uint8_t* p) {
+  __half h;
+  *reinterpret_cast<uint16_t*>(&h) = *reinterpret_cast<const uint16_t*>(p);
+  return __half2float(h);
+}
+
+// Decode the 8 Q4_K weights lane `lane` owns in one 144-byte super-block.
+GOLLEK_DEVICE void q4k_decode8(const uint8_t* blk, int lane, float* w) {
+  const int j = lane >> 2, part = lane & 3;
+  const float d = h2f(blk), dmin = h2f(blk + 2);
+  float sc, mn;
+  q4k_scale_min(j, blk + 4, sc, mn);
+  const float a = d * sc, b = dmin * mn;
+  const uint2 q = *reinterpret_cast<const uint2*>(blk + 16 + 32 * (j >> 1) + part * 8);
+  const uint32_t qq[2] = {q.x, q.y};
+  const int shift = (j & 1) ? 4 : 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const uint32_t byte = (qq[e >> 2] >> (8 * (e & 3))) & 0xFF;
+    w[e] = a * (float)((byte >> shift) & 0xF) - b;
+  }
+}
+
+template <int NT, bool SWIGLU>
+__global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                                   const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                   const uint8_t* __restrict__ W, int N, int K,
+                                                                   int M) {
+  // each warp owns a pair of rows: (n, n + 64) in SwiGLU mode (gate, up), (2i, 2i+1) otherwise
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x * kGemvWarps + warp;
+  int r0, r1;
+  if (SWIGLU) {
+    const int grp = pair / 64, within = pair % 64;
+    r0 = grp * 128 + within;
+    r1 = r0 + 64;
+  } else {
+    r0 = 2 * pair;
+    r1 = r0 + 1;
+  }
+  if (r0 >= N) return;
+  const bool has1 = r1 < N;
+  const int nblk = K / 256;
+  const int64_t row_bytes = (int64_t)nblk * 144;
+  const uint8_t* w0 = W + (int64_t)r0 * row_bytes;
+  const uint8_t* w1 = W + (int64_t)(has1 ? r1 : r0) * row_bytes;
+  float acc0[NT], acc1[NT];
+#pragma unroll
+  for (int m = 0; m < NT; ++m) acc0[m] = acc1[m] = 0.f;
+  const int koff = (lane >> 2) * 32 + (lane & 3) * 8;
+  for (int b = 0; b < nblk; ++b) {
+    float wa[8], wb[8];
+    q4k_decode8(w0 + b * 144, lane, wa);
+    q4k_decode8(w1 + b * 144, lane, wb);
+#pragma unroll
+    for (int m = 0; m < NT; ++m) {
+      if (m < M) {
+        float xv[8];
+        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 256 + koff)), xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          acc0[m] = fmaf(wa[e], xv[e], acc0[m]);
+          acc1[m] = fmaf(wb[e], xv[e], acc1[m]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < NT; ++m) {
+    if (m < M) {
+      const float s0 = warp_sum(acc0[m]);
+      const float s1 = warp_sum(acc1[m]);
+      if (lane == 0) {
+        if (SWIGLU) {
+          const int on = (r0 / 128) * 64 + r0 % 128;
+          y[(int64_t)m * ldy + on] = __float2bfloat16(silu(s0) * s1);
+        } else {
+          y[(int64_t)m * ldy + r0] = __float2bfloat16(s0);
+          if (has1) y[(int64_t)m * ldy + r1] = __float2bfloat16(s1);
+        }
+      }
+    }
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kGemvWarps * 32) q8_0_gemv_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                                    const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                    const uint8_t* __restrict__ W, int N, int K,
+                                                                    int M) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kGemvWarps + warp;
+  if (row >= N) return;
+  const int nblk = K / 32;
+  const uint8_t* wr = W + (int64_t)row * nblk * 34;
+  float acc[NT];
+#pragma unroll
+  for (int m = 0; m < NT; ++m) acc[m] = 0.f;
+  // lane handles 8 weights: block b = i / 4, quarter = i % 4, for i = lane, lane + 32, ...
+  for (int i = lane; i < nblk * 4; i += 32) {
+    const int b = i >> 2, qtr = i & 3;
+    const uint8_t* blk = wr + b * 34;
+    const float d = h2f(blk);
+    // Q8_0 blocks are 34 bytes, so only 2-byte alignment is guaranteed: load 4 x u16
+    const uint16_t* q16 = reinterpret_cast<const uint16_t*>(blk + 2 + qtr * 8);
+    float w[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint16_t v = q16[e];
+      w[2 * e] = d * (float)(int8_t)(v & 0xFF);
+      w[2 * e + 1] = d * (float)(int8_t)(v >> 8);
+    }
+#pragma unroll
+    for (int m = 0; m < NT; ++m) {
+      if (m < M) {
+        float xv[8];
+        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 32 + qtr * 8)), xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m] = fmaf(w[e], xv[e], acc[m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < NT; ++m) {
+    if (m < M) {
+      const float s = warp_sum(acc[m]);
+      if (lane == 0) y[(int64_t)m * ldy + row] = __float2bfloat16(s);
+    }
+  }
+}
+
+// One 256-weight super-block per warp-iteration: lane l writes its 8 decoded weights.
+__global__ void dequant_q4k_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ W,
+                                   int64_t nblocks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t b = wid; b < nblocks; b += nw) {
+    float w[8];
+    q4k_decode8(W + b * 144, lane, w);
+    const int koff = (lane >> 2) * 32 + (lane & 3) * 8;
+    *reinterpret_cast<uint4*>(out + b * 256 + koff) = float_to_bf16x8(w);
+  }
+}
+
+__global__ void dequant_q8_0_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ W,
+                                    int64_t nblocks) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one quarter block (8 weights)
+  if (i >= nblocks * 4) return;
+  const int64_t b = i >> 2;
+  const int qtr = i & 3;
+  const uint8_t* blk = W + b * 34;
+  const float d = h2f(blk);
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = d * (float)(int8_t)blk[2 + qtr * 8 + e];
+  *reinterpret_cast<uint4*>(out + b * 32 + qtr * 8) = float_to_bf16x8(w);
+}
+
+// Embedding rows gathered from a Q8_0 table.
+__global__ void embedding_q8_0_kernel(__nv_bfloat16* __restrict__ out, const int* __restrict__ ids,
+                                      const uint8_t* __restrict__ table, int d, int vocab) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  const uint8_t* row = table + (int64_t)id * (d / 32) * 34;
+  for (int i = threadIdx.x; i < d / 8; i += blockDim.x) {
+    const uint8_t* blk = row + (i >> 2) * 34;
+    const float dd = h2f(blk);
+    float w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = dd * (float)(int8_t)blk[2 + (i & 3) * 8 + e];
+    *reinterpret_cast<uint4*>(out + (int64_t)t * d + i * 8) = float_to_bf16x8(w);
+  }
+}
+
+}  // namespace
+
+namespace gollek {
+
+void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const void* W, int qtype, int N, int K,
+                      int M, bool swiglu, cudaStream_t s) {
+  throw_if(M < 1 || M > kGemvMaxTok, "gguf gemv: 1..16 tokens");
+  throw_if(qtype == 12 && K % 256 != 0, "Q4_K: K must be a multiple of 256");
+  throw_if(qtype == 8 && K % 32 != 0, "Q8_0: K must be a multiple of 32");
+  throw_if(swiglu && (qtype != 12 || N % 128 != 0), "gguf gemv swiglu: Q4_K with N % 128 == 0");
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y);
+  const auto* wp = reinterpret_cast<const uint8_t*>(W);
+  if (qtype == 12) {
+    const int pairs = (N + 1) / 2;
+    const int grid = (pairs + kGemvWarps - 1) / kGemvWarps;
+#define GOLLEK_Q4K(NT)                                                                                          \
+  if (M <= NT) {                                                                                              \
+    if (swiglu) q4k_gemv_kernel<NT, true><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);   \
+    else q4k_gemv_kernel<NT, false><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);         \
+    check_launch("q4k_gemv");                                                                                 \
+    return;                                                                                                   \
+  }
+    GOLLEK_Q4K(1)
+    GOLLEK_Q4K(4)
+    GOLLEK_Q4K(8)
+    GOLLEK_Q4K(16)
+#undef GOLLEK_Q4K
+  } else if (qtype == 8) {
+    const int grid = (N + kGemvWarps - 1) / kGemvWarps;
+#define GOLLEK_Q8(NT)                                                                                 \
+  if (M <= NT) {                                                                                    \
+    q8_0_gemv_kernel<NT><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);          \
+    check_launch("q8_0_gemv");                                                                      \
+    return;                                                                                         \
+  }
+    GOLLEK_Q8(1)
+    GOLLEK_Q8(4)
+    GOLLEK_Q8(8)
+    GOLLEK_Q8(16)
+#undef GOLLEK_Q8
+  }
+  throw_if(true, "gguf gemv: unsupported ggml type " + std::to_string(qtype));
+}
+
+void launch_gguf_dequant(void* out, const void* W, int qtype, int64_t numel, cudaStream_t s) {
+  const auto* wp = reinterpret_cast<const uint8_t*>(W);
+  auto* op = reinterpret_cast<__nv_bfloat16*>(out);
+  if (qtype == 12) {
+    throw_if(numel % 256 != 0, "Q4_K dequant: size");
+    const int64_t nb = numel / 256;
+    const int grid = (int)std::min<int64_t>((nb + 7) / 8, 148 * 16);
+    dequant_q4k_kernel<<<grid, 256, 0, s>>>(op, wp, nb);
+  } else if (qtype == 8) {
+    throw_if(numel % 32 != 0, "Q8_0 dequant: size");
+    const int64_t nq = numel / 8;
+    dequant_q8_0_kernel<<<(unsigned)((nq + 255) / 256), 256, 0, s>>>(op, wp, numel / 32);
+  } else {
+    throw_if(true, "gguf dequant: unsupported ggml type " + std::to_string(qtype));
+  }
+  check_launch("gguf_dequant");
+}
+
+void launch_embedding_q8_0(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s) {
+  throw_if(d % 32 != 0, "Q8_0 embedding: dim must be a multiple of 32");
+  if (T == 0) return;
+  embedding_q8_0_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ids,
+                                         reinterpret_cast<const uint8_t*>(table), d, vocab);
+  check_launch("embedding_q8_0");
+}
+
+}  // namespace gollek

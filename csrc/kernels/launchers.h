@@ -60,6 +60,12 @@ void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V,
 
 int device_num_sms();
 
+// ---- GGUF quantized weights (K9); qtype = ggml type id (8 = Q8_0, 12 = Q4_K)
+void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const void* W, int qtype, int N, int K,
+                      int M, bool swiglu, cudaStream_t s);
+void launch_gguf_dequant(void* out, const void* W, int qtype, int64_t numel, cudaStream_t s);
+void launch_embedding_q8_0(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s);
+
 // ---- multi-LoRA (K10)
 void launch_lora_shrink(float* V, int ldv, const void* x, int64_t ldx, const void* A, int R, int K,
                         const int* seg_ptr, const int* tok_idx, const int* seg_slot, int num_segs, cudaStream_t s);

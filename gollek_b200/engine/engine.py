@@ -48,7 +48,7 @@ class LLMEngine:
         self.tokenizer = tokenizer
         # ---- model
         if model_cfg is None:
-            model_cfg, weights, tok = load_model_source(cfg.model)
+            model_cfg, weights, tok = load_model_source(cfg.model, keep_quantized=cfg.quantization == "gguf")
             self.tokenizer = self.tokenizer or tok
         self.model_cfg = model_cfg
         self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm)
@@ -233,7 +233,7 @@ class LLMEngine:
         return [final[i] for i in ids]
 
 
-def load_model_source(source: str):
+def load_model_source(source: str, keep_quantized: bool = False):
     """Resolve a preset name, a safetensors checkpoint (file or directory) or a GGUF file.
 
     Returns (ModelConfig, weight getter or None for random init, tokenizer or None).
@@ -246,7 +246,7 @@ def load_model_source(source: str):
         return cfg, None, ByteTokenizer(cfg.vocab_size, cfg.eos_token_id)
     if source.endswith(".gguf"):
         from ..loaders.gguf import load_llama_gguf
-        cfg, w, f = load_llama_gguf(source, torch.float32)
+        cfg, w, f = load_llama_gguf(source, torch.float32, keep_quantized=keep_quantized)
         from ..utils.tokenizer import GGUFTokenizer
         tok = GGUFTokenizer.from_metadata(f.metadata)
         return cfg, w.__getitem__, tok

@@ -393,8 +393,10 @@ def load_llama_gguf(path: str, dtype: torch.dtype = torch.float32,
         hf = gguf_to_hf_name(name)
         is_q = hf.endswith("q_proj.weight")
         is_k = hf.endswith("k_proj.weight")
-        if keep_quantized and ti.ggml_type in (GGML_Q8_0, GGML_Q4_K) and len(ti.shape) == 2 \
-                and hf != "model.embed_tokens.weight":
+        keep = keep_quantized and ti.ggml_type in (GGML_Q8_0, GGML_Q4_K) and len(ti.shape) == 2
+        if hf == "model.embed_tokens.weight" and ti.ggml_type != GGML_Q8_0:
+            keep = False  # the quantized embedding gather supports Q8_0 tables
+        if keep:
             raw = f.raw(name).clone()
             if is_q or is_k:  # blocks run along K, so the Q/K row permutation moves whole byte rows
                 rows = raw.view(ti.shape[0], -1)

@@ -145,8 +145,26 @@ class LlamaModel:
         H, Hk, D = self.H, self.Hk, self.D
         dev, dt = self.device, self.dtype
 
+        from ..quant.gguf_weights import QWeight, cat_rows, interleave_rows
+
         def t(name):
-            return get(name).to(device=dev, dtype=dt)
+            v = get(name)
+            if type(v).__name__ == "QuantizedWeight":  # GGUF blocks stay quantized on the device
+                return QWeight.from_quantized(v).to(dev)
+            return v.to(device=dev, dtype=dt)
+
+        def cat(ws):
+            return cat_rows(ws) if isinstance(ws[0], QWeight) else torch.cat(ws, 0)
+
+        def gate_up(g, u):
+            if isinstance(g, QWeight):
+                if self.F_pad != self.F:
+                    raise ValueError("quantized FFN width must be a multiple of 64 per TP rank")
+                return interleave_rows(g, u)
+            return ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad))
+
+        def down(d):
+            return d if isinstance(d, QWeight) else _pad_cols(d, self.F_pad)
 
         self.embed = t("model.embed_tokens.weight").contiguous()
         self.norm = t("model.norm.weight").contiguous()
@@ -162,7 +180,7 @@ class LlamaModel:
             L = {
                 "in_norm": t(p + "input_layernorm.weight").contiguous(),
                 "post_norm": t(p + "post_attention_layernorm.weight").contiguous(),
-                "w_qkv": torch.cat([q, k, v], 0).contiguous(),
+                "w_qkv": cat([q, k, v]).contiguous(),
                 "w_o": o.contiguous(),
             }
             if cfg.is_moe:
@@ -173,16 +191,14 @@ class LlamaModel:
                     g = t(pe + f"experts.{e}.w1.weight")[r * self.F:(r + 1) * self.F]
                     u = t(pe + f"experts.{e}.w3.weight")[r * self.F:(r + 1) * self.F]
                     d = t(pe + f"experts.{e}.w2.weight")[:, r * self.F:(r + 1) * self.F]
-                    experts.append((
-                        ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad)).contiguous(),
-                        _pad_cols(d, self.F_pad).contiguous()))
+                    experts.append((gate_up(g, u).contiguous(), down(d).contiguous()))
                 L["experts"] = experts
             else:
                 g = t(p + "mlp.gate_proj.weight")[r * self.F:(r + 1) * self.F]
                 u = t(p + "mlp.up_proj.weight")[r * self.F:(r + 1) * self.F]
                 d = t(p + "mlp.down_proj.weight")[:, r * self.F:(r + 1) * self.F]
-                L["w_gate_up"] = ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad)).contiguous()
-                L["w_down"] = _pad_cols(d, self.F_pad).contiguous()
+                L["w_gate_up"] = gate_up(g, u).contiguous()
+                L["w_down"] = down(d).contiguous()
             self.layers.append(L)
 
     def init_random(self, seed: int = 0, std: float = 0.02) -> None:
@@ -218,13 +234,16 @@ class LlamaModel:
             self.layers.append(L)
 
     def weight_bytes(self) -> int:
-        n = sum(x.numel() * x.element_size() for x in (self.embed, self.norm, self.lm_head))
+        def nb(x):
+            return x.nbytes() if hasattr(x, "qtype") else x.numel() * x.element_size()
+
+        n = sum(nb(x) for x in (self.embed, self.norm, self.lm_head))
         for L in self.layers:
             for k, v in L.items():
                 if k == "experts":
-                    n += sum(a.numel() * a.element_size() + b.numel() * b.element_size() for a, b in v)
+                    n += sum(nb(a) + nb(b) for a, b in v)
                 else:
-                    n += v.numel() * v.element_size()
+                    n += nb(v)
         return n
 
     # ------------------------------------------------------------------ KV cache

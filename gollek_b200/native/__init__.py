@@ -38,6 +38,7 @@ CUDA_SOURCES = [
     "comm/symm.cu",
     "kernels/noalloc.cu",
     "kernels/lora.cu",
+    "kernels/gguf.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

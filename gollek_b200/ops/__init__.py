@@ -164,9 +164,56 @@ def _gemm(out, a, w, residual, epi, bn):
     _C(2 if splits > 1 else 1).gemm_bf16(out, a, w, residual, epi, bn, None, 0, splits, ws)
 
 
+GGUF_GEMV_MAX_TOKENS = 4
+GGUF_CHUNK_BYTES = 48 << 20  # bf16 scratch per chunk: stays resident in the 126 MB L2
+
+
+def _qlinear(a: torch.Tensor, w, out: Optional[torch.Tensor], swiglu: bool) -> torch.Tensor:
+    """Matmul with a GGUF-quantized weight.
+
+    <= GGUF_GEMV_MAX_TOKENS rows: fused dequant GEMV (weights decoded in registers).
+    More rows: the weight is dequantized in row chunks of <= 48 MB of bf16 into a scratch buffer
+    that stays in L2, and each chunk is multiplied by the tcgen05 GEMM right away, so HBM sees
+    the quantized bytes once plus the activations.
+    """
+    M = a.shape[0]
+    N = w.N
+    n_out = N // 2 if swiglu else N
+    if not a.is_cuda:
+        wd = w.dequantize().to(a.dtype)
+        y = ref.gemm_swiglu(a, wd, SWIGLU_GROUP) if swiglu else ref.gemm(a, wd)
+        return _cpu(y, out)
+    out = torch.empty(M, n_out, dtype=a.dtype, device=a.device) if out is None else out
+    if M <= GGUF_GEMV_MAX_TOKENS and (not swiglu or w.qtype == 12):
+        _C().gguf_gemv(out, a, w.raw, w.qtype, N, w.K, swiglu)
+        return out
+    rows = max(128, GGUF_CHUNK_BYTES // (2 * w.K) // 128 * 128)
+    scratch = torch.empty(min(rows, N), w.K, dtype=torch.bfloat16, device=a.device)
+    ext = cuda_ext()
+    for n0 in range(0, N, rows):
+        n1 = min(N, n0 + rows)
+        wd = scratch[: n1 - n0]
+        _C().gguf_dequant(wd, w.raw[n0:n1], w.qtype)
+        if swiglu:
+            _gemm(out[:, n0 // 2: n1 // 2], a, wd, None, EPI_SWIGLU, 0)
+        else:
+            _gemm(out[:, n0:n1], a, wd, None, EPI_NONE, 0)
+    return out
+
+
+def _is_q(w) -> bool:
+    return type(w).__name__ == "QWeight"
+
+
 def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None, bn: int = 0) -> torch.Tensor:
-    """a [M, K] @ w[N, K]^T (+ residual), bf16 in/out, fp32 accumulate (tcgen05 on GPU)."""
+    """a [M, K] @ w[N, K]^T (+ residual), bf16 in/out, fp32 accumulate (tcgen05 on GPU).
+    ``w`` may be a GGUF-quantized ``QWeight`` (see gollek_b200.quant.gguf_weights)."""
+    if _is_q(w):
+        y = _qlinear(a, w, out, False)
+        if residual is not None:
+            y.add_(residual)
+        return y
     if not a.is_cuda:
         return _cpu(ref.gemm(a, w, residual), out)
     M, N = a.shape[0], w.shape[0]
@@ -179,6 +226,8 @@ def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
 def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.Tensor] = None,
                   bn: int = 0) -> torch.Tensor:
     """silu(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``."""
+    if _is_q(w_gate_up):
+        return _qlinear(a, w_gate_up, out, True)
     if not a.is_cuda:
         return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP), out)
     M, N = a.shape[0], w_gate_up.shape[0]
@@ -199,6 +248,14 @@ def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tenso
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if _is_q(table):
+        if not table.raw.is_cuda:
+            return _cpu(table.dequantize()[ids.long()].to(torch.float32), out)
+        if table.qtype != 8:
+            return embedding(ids, table.dequantize(), out)
+        out = torch.empty(ids.shape[0], table.K, dtype=torch.bfloat16, device=table.device) if out is None else out
+        _C().embedding_q8_0(out, ids, table.raw, table.N)
+        return out
     if not table.is_cuda:
         return _cpu(ref.embedding(ids, table), out)
     out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device) if out is None else out
