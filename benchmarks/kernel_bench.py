@@ -163,6 +163,18 @@ def main():
                     ms = time_cuda(lambda: ops.linear(x, qw, out=out), iters=args.iters, flush_bytes=flush)
                     rec(f"gguf_{'q4k' if qtype == 12 else 'q8_0'}_{name}_M{M}", ms, 2.0 * M * N * K,
                         qw.nbytes() + 2.0 * M * (K + N))
+    if "fp8" in only:
+        from gollek_b200.quant import fp8 as F8
+        # Llama-3-70B per-rank shapes at TP=8 (hidden 8192, 64/8 heads, ffn 28672)
+        for name, N, K in (("qkv", 1280, 8192), ("o_proj", 8192, 1024), ("gate_up", 7168, 8192), ("down", 8192, 3584)):
+            w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+            fw = F8.quantize_weight(w)
+            for M in (64, 1024, 8192):
+                x = torch.randn(M, K, device=dev).bfloat16()
+                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                ms = time_cuda(lambda: ops.linear(x, fw, out=out), iters=args.iters, flush_bytes=flush)
+                rec(f"fp8_{name}_tp8_M{M}", ms, 2.0 * M * N * K, N * K + 2.0 * M * (K + N),
+                    {"splits": ops.cuda_ext().gemm_fp8_splits(M, N, K, 0)})
     if args.json:
         with open(args.json, "w") as f:
             for r in rows:

@@ -341,9 +341,59 @@ void embedding_q8_0_py(torch::Tensor out, torch::Tensor ids, torch::Tensor table
                         cur_stream());
 }
 
+void gemm_fp8_py(torch::Tensor out, torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, int64_t epi,
+                 int64_t splits, c10::optional<torch::Tensor> workspace) {
+  check_bf16(out, "out");
+  check_cuda(a, "a");
+  check_cuda(b, "b");
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "fp8: e4m3 operands");
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sb.scalar_type() == at::kFloat && sa.is_contiguous() &&
+                  sb.is_contiguous(),
+              "fp8: fp32 contiguous scales");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1 && a.size(1) == b.size(1), "fp8: shapes");
+  const int M = a.size(0), N = b.size(0), K = a.size(1);
+  TORCH_CHECK(sa.numel() >= (int64_t)M * (K / 128) && sb.numel() >= (int64_t)((N + 127) / 128) * (K / 128),
+              "fp8: scale tensors too small");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == (epi == kEpiSwiglu ? N / 2 : N), "fp8: out shape");
+  int sp = (int)splits;
+  if (sp <= 0) sp = gemm_fp8_splits(M, N, K, (int)epi);
+  float* part = nullptr;
+  if (sp > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
+                    workspace->numel() >= (int64_t)sp * M * N,
+                "fp8 gemm: split-K ", sp, " needs an fp32 workspace of ", (int64_t)sp * M * N, " elements");
+    part = workspace->data_ptr<float>();
+  }
+  launch_gemm_fp8(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), sa.data_ptr<float>(), b.data_ptr(),
+                  b.stride(0), sb.data_ptr<float>(), M, N, K, (int)epi, sp, part, nullptr, cur_stream());
+}
+
+void act_quant_fp8_py(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
+  check_bf16(x, "x");
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.is_contiguous() && scale.scalar_type() == at::kFloat,
+              "act quant: e4m3 out, fp32 scales");
+  TORCH_CHECK(x.stride(1) == 1, "act quant: row-major x");
+  launch_act_quant_fp8(q.data_ptr(), scale.data_ptr<float>(), x.data_ptr(), x.stride(0), x.size(0), x.size(1),
+                       cur_stream());
+}
+
+void weight_quant_fp8_py(torch::Tensor q, torch::Tensor scale, torch::Tensor w) {
+  check_bf16(w, "w");
+  TORCH_CHECK(w.is_contiguous() && q.is_contiguous() && q.scalar_type() == at::kFloat8_e4m3fn, "weight quant: layout");
+  launch_weight_quant_fp8(q.data_ptr(), scale.data_ptr<float>(), w.data_ptr(), w.size(0), w.size(1), cur_stream());
+}
+
+int64_t gemm_fp8_splits_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  return gemm_fp8_splits((int)M, (int)N, (int)K, (int)epi);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemm_fp8", &gemm_fp8_py, "block-scaled FP8 GEMM on tcgen05 (K6)");
+  m.def("gemm_fp8_splits", &gemm_fp8_splits_py);
+  m.def("act_quant_fp8", &act_quant_fp8_py, "1x128 per-token-group FP8 quantisation (K7)");
+  m.def("weight_quant_fp8", &weight_quant_fp8_py, "128x128 block FP8 weight quantisation");
   m.def("gguf_gemv", &gguf_gemv_py, "Q4_K / Q8_0 GEMV for up to 16 tokens (K9)");
   m.def("gguf_dequant", &gguf_dequant_py, "Q4_K / Q8_0 -> bf16 (K9)");
   m.def("embedding_q8_0", &embedding_q8_0_py, "embedding gather from a Q8_0 table (K9/K13)");

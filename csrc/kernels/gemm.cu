@@ -396,6 +396,22 @@ namespace gollek {
 
 int device_num_sms() { return num_sms(); }
 
+void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* residual, int64_t ldr, int M, int N,
+                   int splits, int epi, cudaStream_t s) {
+  const int out_n = epi == kEpiSwiglu ? N / 2 : N;
+  const int64_t threads = (int64_t)M * (out_n / 8);
+  const unsigned grid = (unsigned)((threads + 255) / 256);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  auto* r = reinterpret_cast<const __nv_bfloat16*>(residual);
+  if (epi == kEpiSwiglu)
+    splitk_reduce_kernel<kEpiSwiglu><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
+  else if (epi == kEpiResidual)
+    splitk_reduce_kernel<kEpiResidual><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
+  else
+    splitk_reduce_kernel<kEpiNone><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
+  check_launch("split-K reduce");
+}
+
 int gemm_pick_bn(int M, int N, int epi) {
   const int num_m = (M + 127) / 128;
   const int sms = num_sms();

@@ -60,6 +60,16 @@ void launch_sample(int64_t* out, const void* logits, bool is_bf16, int B, int V,
 
 int device_num_sms();
 
+// ---- block-scaled FP8 (K6, K7)
+void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const float* sa, const void* b, int64_t ldb,
+                     const float* sb, int M, int N, int K, int epi, int splits, float* partial, uint32_t* status,
+                     cudaStream_t s);
+int gemm_fp8_splits(int M, int N, int K, int epi);
+void launch_act_quant_fp8(void* q, float* scale, const void* x, int64_t ldx, int M, int K, cudaStream_t s);
+void launch_weight_quant_fp8(void* q, float* scale, const void* w, int N, int K, cudaStream_t s);
+void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* residual, int64_t ldr, int M, int N,
+                   int splits, int epi, cudaStream_t s);
+
 // ---- GGUF quantized weights (K9); qtype = ggml type id (8 = Q8_0, 12 = Q4_K)
 void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const void* W, int qtype, int N, int K,
                       int M, bool swiglu, cudaStream_t s);

@@ -53,9 +53,11 @@ class LLMEngine:
         self.model_cfg = model_cfg
         self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm)
         if weights is None:
-            self.model.init_random(cfg.seed)
+            self.model.init_random(cfg.seed, fp8=cfg.quantization == "fp8")
         else:
             self.model.load_weights(weights)
+            if cfg.quantization == "fp8":
+                self.model.quantize_fp8()
         # ---- KV cache
         bpb = self.model.kv_bytes_per_block(cfg.block_size)
         nb = num_blocks or cfg.num_gpu_blocks

@@ -201,7 +201,7 @@ class LlamaModel:
                 L["w_down"] = down(d).contiguous()
             self.layers.append(L)
 
-    def init_random(self, seed: int = 0, std: float = 0.02) -> None:
+    def init_random(self, seed: int = 0, std: float = 0.02, fp8: bool = False) -> None:
         """Random-init this rank's shard directly on the device (benchmarks; no checkpoint)."""
         cfg = self.cfg
         g = torch.Generator(device=self.device)
@@ -231,11 +231,31 @@ class LlamaModel:
             else:
                 L["w_gate_up"] = rnd(2 * self.F_pad, h)
                 L["w_down"] = rnd(h, self.F_pad)
+            if fp8:  # quantise this layer now so bf16 copies of all layers never coexist
+                from ..quant.fp8 import quantize_weight
+                for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+                    if k in L:
+                        L[k] = quantize_weight(L[k])
+                if "experts" in L:
+                    L["experts"] = [(quantize_weight(a), quantize_weight(b)) for a, b in L["experts"]]
             self.layers.append(L)
+
+    def quantize_fp8(self) -> None:
+        """Convert the linear weights (qkv, o, gate/up, down; experts too) to block-scaled FP8, layer by
+        layer so the bf16 copies are released as it goes. Embedding, norms and lm_head stay bf16."""
+        from ..quant.fp8 import quantize_weight
+        for L in self.layers:
+            for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+                if k in L and isinstance(L[k], torch.Tensor):
+                    L[k] = quantize_weight(L[k])
+            if "experts" in L:
+                L["experts"] = [(quantize_weight(a), quantize_weight(b)) for a, b in L["experts"]]
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
 
     def weight_bytes(self) -> int:
         def nb(x):
-            return x.nbytes() if hasattr(x, "qtype") else x.numel() * x.element_size()
+            return x.nbytes() if hasattr(x, "nbytes") and callable(x.nbytes) else x.numel() * x.element_size()
 
         n = sum(nb(x) for x in (self.embed, self.norm, self.lm_head))
         for L in self.layers:

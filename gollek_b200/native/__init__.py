@@ -39,6 +39,7 @@ CUDA_SOURCES = [
     "kernels/noalloc.cu",
     "kernels/lora.cu",
     "kernels/gguf.cu",
+    "kernels/gemm_fp8.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

@@ -205,10 +205,42 @@ def _is_q(w) -> bool:
     return type(w).__name__ == "QWeight"
 
 
+def _is_fp8(w) -> bool:
+    return type(w).__name__ == "FP8Weight"
+
+
+def linear_fp8(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, swiglu: bool = False) -> torch.Tensor:
+    """bf16 activations × block-scaled FP8 weight: quantise a per (token, 128 group), FP8 GEMM."""
+    from ..quant import fp8 as F8
+    M = a.shape[0]
+    n_out = w.N // 2 if swiglu else w.N
+    if not a.is_cuda:
+        xq, sa = F8.quantize_act(a)
+        y = F8.reference_gemm(xq, sa, w)
+        if swiglu:
+            y = y.view(M, -1, 2, SWIGLU_GROUP)
+            y = (torch.nn.functional.silu(y[:, :, 0]) * y[:, :, 1]).reshape(M, -1)
+        return _cpu(y.to(a.dtype), out)
+    out = torch.empty(M, n_out, dtype=torch.bfloat16, device=a.device) if out is None else out
+    xq, sa = F8.quantize_act(a)
+    LAUNCHES.add(1)
+    epi = EPI_SWIGLU if swiglu else EPI_NONE
+    ext = cuda_ext()
+    splits = ext.gemm_fp8_splits(M, w.N, w.K, epi)
+    ws = torch.empty(splits * M * w.N, dtype=torch.float32, device=a.device) if splits > 1 else None
+    _C(2 if splits > 1 else 1).gemm_fp8(out, xq, sa, w.q, w.scale, epi, splits, ws)
+    return out
+
+
 def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None, bn: int = 0) -> torch.Tensor:
     """a [M, K] @ w[N, K]^T (+ residual), bf16 in/out, fp32 accumulate (tcgen05 on GPU).
     ``w`` may be a GGUF-quantized ``QWeight`` (see gollek_b200.quant.gguf_weights)."""
+    if _is_fp8(w):
+        y = linear_fp8(a, w, out)
+        if residual is not None:
+            y.add_(residual)
+        return y
     if _is_q(w):
         y = _qlinear(a, w, out, False)
         if residual is not None:
@@ -228,6 +260,8 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.
     """silu(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``."""
     if _is_q(w_gate_up):
         return _qlinear(a, w_gate_up, out, True)
+    if _is_fp8(w_gate_up):
+        return linear_fp8(a, w_gate_up, out, swiglu=True)
     if not a.is_cuda:
         return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP), out)
     M, N = a.shape[0], w_gate_up.shape[0]
