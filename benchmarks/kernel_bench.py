@@ -106,13 +106,15 @@ def main():
             sl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
             qs = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
             q = torch.randn(T, Hq, D, device=dev).bfloat16()
-            tiles = ops.prefill_tiles(qs.tolist()).to(dev)
             out = torch.empty_like(q)
-            ms = time_cuda(lambda: ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D), tiles=tiles,
-                                                               out=out), iters=args.iters, flush_bytes=flush)
             flops = 4.0 * nseq * (L * L / 2) * Hq * D
             nbytes = 2.0 * (2 * T * Hq * D + 2 * T * Hk * D)
-            rec(f"attn_prefill_{nseq}x{L}", ms, flops, nbytes)
+            for tc in (True, False):
+                tiles = ops.prefill_tiles(qs.tolist(), ops.prefill_block_m(D, tc)).to(dev)
+                ms = time_cuda(lambda: ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D), tiles=tiles,
+                                                                   out=out, tensor_cores=tc),
+                               iters=args.iters, flush_bytes=flush)
+                rec(f"attn_prefill_{'tcgen05' if tc else 'mmasync'}_{nseq}x{L}", ms, flops, nbytes)
     if "norm" in only:
         d = 4096
         for T in (256, 8192):

@@ -35,6 +35,10 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
                          cudaStream_t s);
+void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
+                             const void* cache, int num_blocks, const int* block_tables, int bt_stride,
+                             const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
+                             int Hk, float scale, cudaStream_t s);
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,

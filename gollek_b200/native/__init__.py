@@ -40,6 +40,7 @@ CUDA_SOURCES = [
     "kernels/lora.cu",
     "kernels/gguf.cu",
     "kernels/gemm_fp8.cu",
+    "kernels/attention_tc.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

@@ -115,6 +115,11 @@ def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables
     return out
 
 
+def prefill_block_m(head_dim: int, tensor_cores: bool = True) -> int:
+    """Query rows per CTA of the prefill kernel (128 on the tcgen05 path, 64 on the mma.sync path)."""
+    return 128 if (tensor_cores and head_dim == 128) else 64
+
+
 def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
     """(sequence, query offset) pairs of the 64-row query tiles the prefill kernel runs."""
     tiles = []
@@ -128,14 +133,17 @@ def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
 def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                             seq_lens: torch.Tensor, query_start: torch.Tensor, scale: float,
                             tiles: Optional[torch.Tensor] = None,
-                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new)."""
+                            out: Optional[torch.Tensor] = None, tensor_cores: bool = True) -> torch.Tensor:
+    """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new).
+    head_dim 128 runs on tcgen05/TMEM (128-row query tiles); other sizes on mma.sync (64 rows).
+    ``tiles`` must have been built with ``prefill_block_m`` rows per tile."""
     if not q.is_cuda:
         return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale), out)
     out = torch.empty_like(q) if out is None else out
     if tiles is None:
-        tiles = prefill_tiles(query_start.tolist()).to(q.device)
-    _C().paged_prefill_attention(out, q, kv_cache, block_tables, seq_lens, query_start, tiles, float(scale))
+        tiles = prefill_tiles(query_start.tolist(), prefill_block_m(q.shape[2], tensor_cores)).to(q.device)
+    _C().paged_prefill_attention(out, q, kv_cache, block_tables, seq_lens, query_start, tiles, float(scale),
+                                 bool(tensor_cores))
     return out
 
 

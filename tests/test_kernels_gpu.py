@@ -100,6 +100,34 @@ def test_paged_prefill_attention(H, Hk, D):
     torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("H,Hk", [(32, 8), (4, 1), (64, 8), (8, 8)])
+@pytest.mark.parametrize("tensor_cores", [True, False])
+def test_paged_prefill_attention_d128(H, Hk, tensor_cores):
+    """head_dim 128: the tcgen05 kernel (128-row query tiles, several 128-key KV tiles, cached
+    prefixes not on tile boundaries) and the mma.sync kernel against the fp32 oracle."""
+    specs = [(0, 70), (33, 20), (128, 1), (5, 130), (300, 400), (1000, 260), (0, 129)]
+    lens = [p + n for p, n in specs]
+    B = len(specs)
+    D = 128
+    cache, bt, sl = _paged_setup(B, Hk, D, lens, seed=19)
+    qs = [0]
+    for _, n in specs:
+        qs.append(qs[-1] + n)
+    T = qs[-1]
+    q = bf(torch.randn(T, H, D, device=DEV, generator=_g(20)))
+    qsl = torch.tensor(qs, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(D)
+    out = ops.paged_prefill_attention(q, cache, bt, sl, qsl, scale, tensor_cores=tensor_cores)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl.cpu(), scale)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+    # a second call into a view of a larger buffer (the engine's decode-then-prefill layout)
+    big = torch.full((T + 3, H, D), float("nan"), device=DEV, dtype=torch.bfloat16)
+    qb = torch.zeros(T + 3, H, D, device=DEV, dtype=torch.bfloat16)
+    qb[3:] = q
+    ops.paged_prefill_attention(qb[3:], cache, bt, sl, qsl, scale, out=big[3:], tensor_cores=tensor_cores)
+    torch.testing.assert_close(big[3:].float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (77, 384, 256), (128, 4096, 4096), (300, 6144, 4096),
                                    (2048, 1024, 512), (16, 32000, 256)])
 @pytest.mark.parametrize("bn", [0, 64, 128, 256])
