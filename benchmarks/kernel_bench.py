@@ -177,6 +177,26 @@ def main():
                 ms = time_cuda(lambda: ops.linear(x, fw, out=out), iters=args.iters, flush_bytes=flush)
                 rec(f"fp8_{name}_tp8_M{M}", ms, 2.0 * M * N * K, N * K + 2.0 * M * (K + N),
                     {"splits": ops.cuda_ext().gemm_fp8_splits(M, N, K, 0)})
+    if "moe" in only:
+        # Mixtral-8x7B MoE layer (H 4096, F 14336, 8 experts, top-2): all experts on one GPU, and the
+        # one-expert shard a rank holds under EP=8 (its partial sum; the all-reduce is not included)
+        H, F, E, k = 4096, 14336, 8, 2
+        router = (torch.randn(E, H, device=dev) * 0.02).bfloat16()
+        for e_loc in (8, 1):
+            gu = (torch.randn(e_loc * 2 * F, H, device=dev) * 0.02).bfloat16()
+            dn = (torch.randn(e_loc * H, F, device=dev) * 0.02).bfloat16()
+            for T in (64, 256, 2048, 8192):
+                x = torch.randn(T, H, device=dev).bfloat16()
+                out = torch.empty_like(x)
+                ms = time_cuda(lambda: ops.fused_moe(x, router, gu, dn, k, e0=0, e_loc=e_loc, out=out),
+                               iters=args.iters, flush_bytes=flush)
+                with torch.no_grad():
+                    ids, _ = ops.moe_route_ref(x[:min(T, 4096)].float(), router.float(), k)
+                rows = T * k * e_loc / E  # expected routed rows on these experts (uniform router)
+                active = min(e_loc, len(set(ids.flatten().tolist()) & set(range(e_loc))) or e_loc)
+                flops = 2.0 * rows * 3 * H * F
+                nbytes = active * 3.0 * H * F * 2 + 2.0 * 2 * T * H + 2.0 * rows * (2 * H + F)
+                rec(f"moe_mixtral_{'all8' if e_loc == 8 else 'ep8_shard'}_T{T}", ms, flops, nbytes)
     if args.json:
         with open(args.json, "w") as f:
             for r in rows:

@@ -207,6 +207,40 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
                    N, K, (int)epi, bn_i, sp, part, st, (int)grid_limit, cur_stream());
 }
 
+// MoE layer (K12 + grouped tcgen05 GEMMs). w_gu: [e_loc * 2F, H] gate/up rows interleaved in groups
+// of 64 per expert; w_down: [e_loc * H, F]. ws: int32 [moe_ws_ints] zero-filled once at allocation
+// (the plan kernel re-zeroes its counters after every use). ids/dest [T*topk] int32, wts fp32,
+// xp/yp [cap, H] and hp [cap, F] bf16 scratch with cap = moe_capacity_rows(T, topk, e_loc).
+void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, torch::Tensor w_gu,
+                     torch::Tensor w_down, torch::Tensor ws, torch::Tensor ids, torch::Tensor wts, torch::Tensor dest,
+                     torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, int64_t topk, bool renorm, int64_t e0,
+                     int64_t e_loc) {
+  for (auto* t : {&out, &x, &router, &w_gu, &w_down, &xp, &hp, &yp}) check_bf16(*t, "moe operand");
+  check_same_device(x, w_gu);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "moe: x/out row-major [T, H]");
+  const int T = x.size(0), H = x.size(1), E = router.size(0);
+  TORCH_CHECK(router.dim() == 2 && router.size(1) == H && router.is_contiguous(), "moe: router [E, H]");
+  TORCH_CHECK(w_down.dim() == 2 && w_down.size(0) == e_loc * H && w_down.is_contiguous(), "moe: w_down [e_loc*H, F]");
+  const int F = w_down.size(1);
+  TORCH_CHECK(w_gu.dim() == 2 && w_gu.size(0) == e_loc * 2 * F && w_gu.size(1) == H && w_gu.is_contiguous(),
+              "moe: w_gu [e_loc*2F, H]");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == H, "moe: out [T, H]");
+  const int cap = moe_capacity_rows(T, (int)topk, (int)e_loc);
+  TORCH_CHECK(xp.is_contiguous() && xp.size(0) >= cap && xp.size(1) == H, "moe: xp [cap, H]");
+  TORCH_CHECK(yp.is_contiguous() && yp.size(0) >= cap && yp.size(1) == H, "moe: yp [cap, H]");
+  TORCH_CHECK(hp.is_contiguous() && hp.size(0) >= cap && hp.size(1) == F, "moe: hp [cap, F]");
+  TORCH_CHECK(ws.scalar_type() == at::kInt && ws.is_cuda() && ws.numel() >= moe_ws_ints(T, (int)topk, (int)e_loc),
+              "moe: int32 workspace too small");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && dest.scalar_type() == at::kInt && wts.scalar_type() == at::kFloat &&
+                  ids.numel() >= (int64_t)T * topk && dest.numel() >= (int64_t)T * topk &&
+                  wts.numel() >= (int64_t)T * topk,
+              "moe: ids/dest int32 and wts fp32 of T*topk");
+  launch_moe_forward(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), router.data_ptr(), w_gu.data_ptr(),
+                     w_down.data_ptr(), ws.data_ptr<int>(), ids.data_ptr<int>(), wts.data_ptr<float>(),
+                     dest.data_ptr<int>(), xp.data_ptr(), hp.data_ptr(), yp.data_ptr(), T, H, F, E, (int)topk,
+                     renorm ? 1 : 0, (int)e0, (int)e_loc, nullptr, cur_stream());
+}
+
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
   int bn = 0, sp = 1;
   gemm_plan((int)M, (int)N, (int)K, (int)epi, bn, sp);
@@ -425,6 +459,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
   m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
   m.def("num_sms", &device_num_sms);
+  m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)");
+  m.def("moe_capacity_rows", &moe_capacity_rows);
+  m.def("moe_ws_ints", &moe_ws_ints);
   m.def("argmax", &argmax_out, "greedy argmax (K11)");
   m.def("apply_penalties", &apply_penalties_, "repetition/frequency/presence penalties (K11)");
   m.def("sample", &sample_out, "top-k/min-p/top-p sampling (K11)");

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
                      int M, int N, int K, int group_m, int splits, float* __restrict__ partial,
-                     uint32_t* status) {
+                     uint32_t* status, const int* __restrict__ tile_group, const int* __restrict__ num_m_dev) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -95,7 +95,10 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* consumed = abort_flag + 1;  // k-blocks consumed by the MMA warp (abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
+  // Grouped mode (MoE experts): A rows are grouped per expert, each group padded to BM rows;
+  // tile_group[m-tile] names the expert whose B rows [g*N, g*N+N) multiply that M tile, and the
+  // number of valid M tiles is read from device memory (no host round trip).
+  const int num_m = tile_group ? min(*num_m_dev, (M + Cfg::BM - 1) / Cfg::BM) : (M + Cfg::BM - 1) / Cfg::BM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_units = num_tiles * splits;
@@ -161,7 +164,8 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, kb * Cfg::BK, m0, &full[stage]);
-          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, kb * Cfg::BK, n0, &full[stage]);
+          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, kb * Cfg::BK,
+                      tile_group ? n0 + tile_group[m0 / Cfg::BM] * N : n0, &full[stage]);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -361,11 +365,11 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ C, int64_t ldc,
 template <int BN, int EPI>
 void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
                    int64_t ldr, int M, int N, int K, int splits, float* partial, uint32_t* status, int grid_limit,
-                   cudaStream_t s) {
+                   cudaStream_t s, const int* tile_group = nullptr, const int* num_m_dev = nullptr, int groups = 1) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, ldb, BN, Cfg::BK,
+  CUtensorMap tb = make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)N * groups, K, ldb, BN, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   auto kern = gemm_bf16_kernel<BN, EPI>;
   GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
@@ -378,7 +382,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
   kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
-                                     partial, status);
+                                     partial, status, tile_group, num_m_dev);
   check_launch("gemm_bf16");
   if (splits > 1) {
     const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
@@ -475,6 +479,36 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
   GOLLEK_GEMM_CASE(128, kEpiSwiglu)
 #undef GOLLEK_GEMM_CASE
   throw_if(true, "gemm: unsupported tile width " + std::to_string(bn) + " / epilogue " + std::to_string(epi));
+}
+
+void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, int M_cap,
+                         int N, int K, int groups, int epi, int bn, const int* tile_group, const int* num_m_dev,
+                         uint32_t* status, cudaStream_t s) {
+  throw_if(K % 8 != 0, "grouped gemm: K must be a multiple of 8");
+  throw_if(ldc % 8 != 0, "grouped gemm: output row pitch must keep 16-byte alignment");
+  throw_if(M_cap % 128 != 0, "grouped gemm: row capacity must be a multiple of 128");
+  throw_if(tile_group == nullptr || num_m_dev == nullptr, "grouped gemm: tile map required");
+  throw_if(epi == kEpiResidual, "grouped gemm: residual epilogue not supported");
+  if (M_cap == 0) return;
+  if (epi == kEpiSwiglu) throw_if(N % 128 != 0, "grouped gemm swiglu: N must be a multiple of 128");
+  else throw_if(N % 8 != 0, "grouped gemm: N must be a multiple of 8");
+  if (bn == 0) {
+    // typical live M tiles: one per expert at decode, capacity/128 when every expert is full
+    const int m_tiles = std::max(groups, std::min(M_cap / 128, groups * 2));
+    bn = (m_tiles * ((N + 255) / 256) >= num_sms() || epi == kEpiSwiglu) ? 256 : 128;
+  }
+  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+#define GOLLEK_GG_CASE(BNV, EPIV) \
+  if (bn == BNV && epi == EPIV)   \
+    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, nullptr, 0, M_cap, N, K, 1, nullptr, status, 0, s, \
+                                    tile_group, num_m_dev, groups);
+  GOLLEK_GG_CASE(256, kEpiNone)
+  GOLLEK_GG_CASE(128, kEpiNone)
+  GOLLEK_GG_CASE(64, kEpiNone)
+  GOLLEK_GG_CASE(256, kEpiSwiglu)
+  GOLLEK_GG_CASE(128, kEpiSwiglu)
+#undef GOLLEK_GG_CASE
+  throw_if(true, "grouped gemm: unsupported tile width " + std::to_string(bn));
 }
 
 }  // namespace gollek

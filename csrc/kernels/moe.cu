@@ -1,0 +1,235 @@
+// K12: MoE routing and token permutation, plus the expert combine (sm_100a).
+//
+//   moe_route    one warp per token: router logits x·Wrᵀ (fp32 accumulate, E ≤ 64), softmax,
+//                top-k (k ≤ 8, ties to the lower expert id), optional renormalisation of the k
+//                weights (Mixtral), per-local-expert token counts (atomics).
+//   moe_plan     one thread: per-expert row offsets in the permuted buffer, each expert's rows
+//                padded to the 128-row GEMM tile, the M-tile → expert map for the grouped GEMM
+//                and the live M-tile count; re-zeroes the counters for the next call.
+//   moe_gather   one warp per (token, choice) routed to a local expert: claims a row of its
+//                expert's segment and copies the token's hidden vector there.
+//   moe_combine  out[t] = Σ_j w[t,j] · Y[dest[t,j]] over the choices that were local (fp32 sum).
+//
+// The grouped expert GEMMs between gather and combine run on the tcgen05 GEMM (gemm.cu) in
+// grouped mode. Nothing here synchronises with the host, so a MoE layer can be captured in a
+// CUDA graph. Under expert parallelism each rank owns experts [e0, e0 + e_loc) of the replicated
+// activations and ``out`` is its partial sum; the tensor-parallel all-reduce that follows adds the
+// partials of all ranks.
+//
+// Reference behaviour: Mixtral routing in runner/safetensor/…/generation/moe/MoeForwardPass.java:39-128
+// and the EP dispatch contract of core/optimization/gollek-plugin-elastic-ep/…/binding/ElasticEpBinding.java:19-45.
+#include "../common/common.cuh"
+#include "launchers.h"
+
+using namespace gollek;
+
+namespace {
+
+constexpr int kMaxE = 64;
+constexpr int kMaxK = 8;
+
+__global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                        const __nv_bfloat16* __restrict__ wr, int T, int H, int E,
+                                                        int topk, int renorm, int e0, int e_loc, int* __restrict__ ids,
+                                                        float* __restrict__ wts, int* __restrict__ counts) {
+  __shared__ float s_logit[8][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const __nv_bfloat16* xr = x + (int64_t)t * ldx;
+  for (int ec = 0; ec < E; ec += 8) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int h = lane * 8; h < H; h += 256) {
+      float xv[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(xr + h), xv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (ec + e < E) {
+          float wv[8];
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(wr + (int64_t)(ec + e) * H + h), wv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[e] = fmaf(xv[i], wv[i], acc[e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = warp_sum(acc[e]);
+      if (lane == 0 && ec + e < E) s_logit[warp][ec + e] = v;
+    }
+  }
+  __syncwarp();
+  // softmax over E (lane i owns experts i and i + 32)
+  float v0 = lane < E ? s_logit[warp][lane] : -INFINITY;
+  float v1 = lane + 32 < E ? s_logit[warp][lane + 32] : -INFINITY;
+  const float m = warp_max(fmaxf(v0, v1));
+  float p0 = lane < E ? __expf(v0 - m) : 0.f;
+  float p1 = lane + 32 < E ? __expf(v1 - m) : 0.f;
+  const float inv = 1.f / warp_sum(p0 + p1);
+  p0 *= inv;
+  p1 *= inv;
+  int sel_id[kMaxK];
+  float sel_p[kMaxK];
+  float psum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxK; ++j) {
+    if (j >= topk) break;
+    // lane-local best of its two candidates (-1 marks taken / absent)
+    float bv = p0;
+    int bi = lane < E ? lane : 1 << 30;
+    if (lane + 32 < E && (p1 > bv || bi == (1 << 30))) {
+      bv = p1;
+      bi = lane + 32;
+    }
+    if (bi == (1 << 30)) bv = -1.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sel_id[j] = bi;
+    sel_p[j] = bv;
+    psum += bv;
+    if (bi == lane) p0 = -1.f;        // mark taken
+    if (bi == lane + 32) p1 = -1.f;
+  }
+  if (lane == 0) {
+    const float scale = renorm ? 1.f / psum : 1.f;
+    for (int j = 0; j < topk; ++j) {
+      ids[(int64_t)t * topk + j] = sel_id[j];
+      wts[(int64_t)t * topk + j] = sel_p[j] * scale;
+      const int le = sel_id[j] - e0;
+      if (le >= 0 && le < e_loc) atomicAdd(&counts[le], 1);
+    }
+  }
+}
+
+// ws layout (int32), fixed whatever e_loc is, so calls with different expert ranges can share it:
+//   counts[64] | cursor[64] | offsets[65] | num_m[1] | tile_group[max_tiles]
+// counts[0, e_loc) are zero between calls (route increments them, plan reads and re-zeroes them);
+// plan zeroes cursor[0, e_loc) before gather claims rows with it.
+constexpr int kWsCursor = kMaxE, kWsOffsets = 2 * kMaxE, kWsNumM = 3 * kMaxE + 1, kWsTiles = 3 * kMaxE + 2;
+
+__global__ void moe_plan_kernel(int* __restrict__ ws, int e_loc, int max_tiles) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int* counts = ws;
+  int* cursor = ws + kWsCursor;
+  int* offsets = ws + kWsOffsets;
+  int* num_m = ws + kWsNumM;
+  int* tile_group = ws + kWsTiles;
+  int off = 0, mt = 0;
+  for (int e = 0; e < e_loc; ++e) {
+    const int c = counts[e];
+    offsets[e] = off;
+    const int nt = (c + 127) / 128;
+    for (int i = 0; i < nt && mt < max_tiles; ++i) tile_group[mt++] = e;
+    off += nt * 128;
+    counts[e] = 0;
+    cursor[e] = 0;
+  }
+  offsets[e_loc] = off;
+  *num_m = mt;
+}
+
+__global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                         const int* __restrict__ ids, int rows, int topk, int H,
+                                                         int e0, int e_loc, int* __restrict__ ws,
+                                                         int* __restrict__ dest, __nv_bfloat16* __restrict__ xp) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int idx = blockIdx.x * 8 + warp;
+  if (idx >= rows) return;
+  const int e = ids[idx] - e0;
+  if (e < 0 || e >= e_loc) {
+    if (lane == 0) dest[idx] = -1;
+    return;
+  }
+  int* cursor = ws + kWsCursor;
+  const int* offsets = ws + kWsOffsets;
+  int pos = 0;
+  if (lane == 0) pos = atomicAdd(&cursor[e], 1);
+  pos = __shfl_sync(0xffffffffu, pos, 0);
+  const int d = offsets[e] + pos;
+  if (lane == 0) dest[idx] = d;
+  const __nv_bfloat16* src = x + (int64_t)(idx / topk) * ldx;
+  __nv_bfloat16* dst = xp + (int64_t)d * H;
+  for (int h = lane * 8; h < H; h += 256)
+    *reinterpret_cast<uint4*>(dst + h) = *reinterpret_cast<const uint4*>(src + h);
+}
+
+__global__ void __launch_bounds__(256) moe_combine_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                          const __nv_bfloat16* __restrict__ yp, int64_t ldy,
+                                                          const int* __restrict__ dest, const float* __restrict__ wts,
+                                                          int T, int topk, int H) {
+  const int groups = H / 8;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)T * groups) return;
+  const int t = (int)(i / groups), c = (int)(i % groups) * 8;
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    const int d = dest[(int64_t)t * topk + j];
+    if (d < 0) continue;
+    const float w = wts[(int64_t)t * topk + j];
+    float y[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(yp + (int64_t)d * ldy + c), y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, y[e], acc[e]);
+  }
+  *reinterpret_cast<uint4*>(out + (int64_t)t * ldo + c) = float_to_bf16x8(acc);
+}
+
+}  // namespace
+
+namespace gollek {
+
+int moe_capacity_rows(int T, int topk, int e_loc) {
+  const int64_t rows = (int64_t)T * topk + 127ll * e_loc;
+  return (int)((rows + 127) / 128 * 128);
+}
+
+int moe_ws_ints(int T, int topk, int e_loc) { return kWsTiles + moe_capacity_rows(T, topk, e_loc) / 128; }
+
+void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
+                        const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
+                        int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc, uint32_t* status,
+                        cudaStream_t s) {
+  throw_if(E > kMaxE || E < 1, "moe: at most 64 experts");
+  throw_if(topk < 1 || topk > kMaxK || topk > E, "moe: top-k must be in [1, min(8, E)]");
+  throw_if(H % 256 != 0, "moe: hidden size must be a multiple of 256");
+  throw_if(F % 64 != 0, "moe: expert FFN width must be a multiple of 64");
+  throw_if(ldx % 8 != 0 || ldo % 8 != 0, "moe: row pitches must keep 16-byte alignment");
+  throw_if(e0 < 0 || e_loc < 1 || e0 + e_loc > E, "moe: bad local expert range");
+  static_assert(kWsTiles == 3 * kMaxE + 2, "workspace layout");
+  if (T == 0) return;
+  const int cap = moe_capacity_rows(T, topk, e_loc);
+  auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  moe_route_kernel<<<(T + 7) / 8, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
+                                               renorm, e0, e_loc, ids, wts, ws);
+  check_launch("moe_route");
+  moe_plan_kernel<<<1, 32, 0, s>>>(ws, e_loc, cap / 128);
+  check_launch("moe_plan");
+  const int rows = T * topk;
+  moe_gather_kernel<<<(rows + 7) / 8, 256, 0, s>>>(xb, ldx, ids, rows, topk, H, e0, e_loc, ws, dest,
+                                                   reinterpret_cast<__nv_bfloat16*>(xp));
+  check_launch("moe_gather");
+  const int* num_m = ws + kWsNumM;
+  const int* tile_group = ws + kWsTiles;
+  // gate/up (interleaved in groups of 64 per expert) with the SwiGLU epilogue: hp [cap, F]
+  launch_gemm_grouped(hp, F, xp, H, w_gu, H, cap, 2 * F, H, e_loc, kEpiSwiglu, 0, tile_group, num_m, status, s);
+  // down: yp [cap, H]
+  launch_gemm_grouped(yp, H, hp, F, w_down, F, cap, H, F, e_loc, kEpiNone, 0, tile_group, num_m, status, s);
+  const int64_t threads = (int64_t)T * (H / 8);
+  moe_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(yp), H, dest, wts, T, topk,
+      H);
+  check_launch("moe_combine");
+}
+
+}  // namespace gollek

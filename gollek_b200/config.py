@@ -221,6 +221,7 @@ class EngineConfig:
     quantization: str = "none"                # none | fp8 | gguf
     device: str = "cuda"
     tensor_parallel_size: int = 1
+    enable_expert_parallel: bool = False  # MoE: experts partitioned over the TP ranks (EP = TP size)
     expert_parallel_size: int = 1
     # paged KV cache
     block_size: int = 16

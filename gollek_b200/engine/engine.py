@@ -51,7 +51,8 @@ class LLMEngine:
             model_cfg, weights, tok = load_model_source(cfg.model, keep_quantized=cfg.quantization == "gguf")
             self.tokenizer = self.tokenizer or tok
         self.model_cfg = model_cfg
-        self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm)
+        self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm,
+                                expert_parallel=cfg.enable_expert_parallel)
         if weights is None:
             self.model.init_random(cfg.seed, fp8=cfg.quantization == "fp8")
         else:

@@ -100,11 +100,18 @@ def _pad_cols(w: torch.Tensor, cols: int) -> torch.Tensor:
     return out
 
 
+def _copy_out(y: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+    if out is None:
+        return y
+    out.copy_(y)
+    return out
+
+
 class LlamaModel:
     """Llama / Mixtral decoder for serving (one TP rank)."""
 
     def __init__(self, cfg: ModelConfig, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
-                 comm: Optional[TPComm] = None):
+                 comm: Optional[TPComm] = None, expert_parallel: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
@@ -130,6 +137,21 @@ class LlamaModel:
         if cfg.vocab_size % tp:
             raise ValueError("vocab_size must be divisible by the TP size")
         self.V_local = cfg.vocab_size // tp
+        # MoE placement. Tensor-parallel experts: every rank holds all experts with their FFN width
+        # sharded. Expert parallel: rank r holds experts [r*E/tp, (r+1)*E/tp) at full width. In both
+        # cases the activations entering the MoE are replicated (attention is tensor parallel), so the
+        # rank's output is a partial sum completed by the all-reduce that follows.
+        self.expert_parallel = bool(expert_parallel and cfg.is_moe)
+        self.E_loc, self.e0, self.moe_F = 0, 0, self.F
+        if cfg.is_moe:
+            E = cfg.num_local_experts
+            if self.expert_parallel:
+                if E % tp:
+                    raise ValueError("num_local_experts must be divisible by the expert-parallel size")
+                self.E_loc, self.e0, self.moe_F = E // tp, r * (E // tp), cfg.intermediate_size
+            else:
+                self.E_loc, self.e0, self.moe_F = E, 0, f_shard
+        self.moe_F_pad = (self.moe_F + ops.SWIGLU_GROUP - 1) // ops.SWIGLU_GROUP * ops.SWIGLU_GROUP
         self.scale = 1.0 / math.sqrt(self.D)
         self.cos_sin = rope_cos_sin(cfg, max(cfg.max_position_embeddings, 8192), device=self.device)
         self.layers: List[Dict[str, torch.Tensor]] = []
@@ -156,15 +178,16 @@ class LlamaModel:
         def cat(ws):
             return cat_rows(ws) if isinstance(ws[0], QWeight) else torch.cat(ws, 0)
 
-        def gate_up(g, u):
+        def gate_up(g, u, fpad=None):
+            fpad = self.F_pad if fpad is None else fpad
             if isinstance(g, QWeight):
-                if self.F_pad != self.F:
+                if fpad != g.N:
                     raise ValueError("quantized FFN width must be a multiple of 64 per TP rank")
                 return interleave_rows(g, u)
-            return ops.interleave_gate_up(_pad_rows(g, self.F_pad), _pad_rows(u, self.F_pad))
+            return ops.interleave_gate_up(_pad_rows(g, fpad), _pad_rows(u, fpad))
 
-        def down(d):
-            return d if isinstance(d, QWeight) else _pad_cols(d, self.F_pad)
+        def down(d, fpad=None):
+            return d if isinstance(d, QWeight) else _pad_cols(d, self.F_pad if fpad is None else fpad)
 
         self.embed = t("model.embed_tokens.weight").contiguous()
         self.norm = t("model.norm.weight").contiguous()
@@ -187,12 +210,20 @@ class LlamaModel:
                 pe = p + "block_sparse_moe."
                 L["router"] = t(pe + "gate.weight").contiguous()
                 experts = []
-                for e in range(cfg.num_local_experts):
-                    g = t(pe + f"experts.{e}.w1.weight")[r * self.F:(r + 1) * self.F]
-                    u = t(pe + f"experts.{e}.w3.weight")[r * self.F:(r + 1) * self.F]
-                    d = t(pe + f"experts.{e}.w2.weight")[:, r * self.F:(r + 1) * self.F]
-                    experts.append((gate_up(g, u).contiguous(), down(d).contiguous()))
-                L["experts"] = experts
+                f0, f1 = (0, self.moe_F) if self.expert_parallel else (r * self.F, (r + 1) * self.F)
+                for e in range(self.e0, self.e0 + self.E_loc):
+                    g = t(pe + f"experts.{e}.w1.weight")[f0:f1]
+                    u = t(pe + f"experts.{e}.w3.weight")[f0:f1]
+                    d = t(pe + f"experts.{e}.w2.weight")[:, f0:f1]
+                    experts.append((gate_up(g, u, self.moe_F_pad).contiguous(),
+                                    down(d, self.moe_F_pad).contiguous()))
+                if all(isinstance(a, torch.Tensor) for a, _ in experts):
+                    # dense experts stacked for the grouped GEMMs
+                    L["moe_gu"] = torch.cat([a for a, _ in experts], 0)
+                    L["moe_down"] = torch.cat([b for _, b in experts], 0)
+                    del experts
+                else:
+                    L["experts"] = experts
             else:
                 g = t(p + "mlp.gate_proj.weight")[r * self.F:(r + 1) * self.F]
                 u = t(p + "mlp.up_proj.weight")[r * self.F:(r + 1) * self.F]
@@ -227,7 +258,12 @@ class LlamaModel:
             }
             if cfg.is_moe:
                 L["router"] = rnd(cfg.num_local_experts, h)
-                L["experts"] = [(rnd(2 * self.F_pad, h), rnd(h, self.F_pad)) for _ in range(cfg.num_local_experts)]
+                fp = self.moe_F_pad
+                if fp8:
+                    L["experts"] = [(rnd(2 * fp, h), rnd(h, fp)) for _ in range(self.E_loc)]
+                else:
+                    L["moe_gu"] = rnd(self.E_loc * 2 * fp, h)
+                    L["moe_down"] = rnd(self.E_loc * h, fp)
             else:
                 L["w_gate_up"] = rnd(2 * self.F_pad, h)
                 L["w_down"] = rnd(h, self.F_pad)
@@ -248,6 +284,11 @@ class LlamaModel:
             for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
                 if k in L and isinstance(L[k], torch.Tensor):
                     L[k] = quantize_weight(L[k])
+            if "moe_gu" in L:
+                fp, h = self.moe_F_pad, self.cfg.hidden_size
+                gu, dn = L.pop("moe_gu"), L.pop("moe_down")
+                L["experts"] = [(gu[e * 2 * fp:(e + 1) * 2 * fp], dn[e * h:(e + 1) * h]) for e in range(self.E_loc)]
+                del gu, dn
             if "experts" in L:
                 L["experts"] = [(quantize_weight(a), quantize_weight(b)) for a, b in L["experts"]]
         if self.device.type == "cuda":
@@ -286,14 +327,19 @@ class LlamaModel:
                                         out=out[nd:])
         return out
 
-    def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:
+    def _moe(self, x: torch.Tensor, L: dict, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's share of the MoE FFN (its local experts, or its FFN shard of every expert)."""
         cfg = self.cfg
-        logits = ops.linear(x, L["router"]).float()
-        probs = torch.softmax(logits, -1)
-        topw, topi = probs.topk(cfg.num_experts_per_tok, -1)
-        topw = (topw / topw.sum(-1, keepdim=True)).to(torch.float32)
-        out = torch.zeros(x.shape[0], cfg.hidden_size, dtype=torch.float32, device=x.device)
-        for e, (w_gu, w_d) in enumerate(L["experts"]):
+        if "moe_gu" in L:  # dense experts: route + permute + grouped tcgen05 GEMMs + combine
+            return ops.fused_moe(x, L["router"], L["moe_gu"], L["moe_down"], cfg.num_experts_per_tok,
+                                 self.e0, self.E_loc, out=out)
+        # quantized experts (GGUF / FP8): one expert at a time
+        topi, topw = ops.moe_route_ref(x, L["router"], cfg.num_experts_per_tok)
+        topw = topw.to(x.device)
+        topi = topi.to(x.device)
+        acc = torch.zeros(x.shape[0], cfg.hidden_size, dtype=torch.float32, device=x.device)
+        for le, (w_gu, w_d) in enumerate(L["experts"]):
+            e = self.e0 + le
             sel = (topi == e)
             rows = sel.any(-1).nonzero().flatten()
             if rows.numel() == 0:
@@ -301,8 +347,8 @@ class LlamaModel:
             xe = x.index_select(0, rows).contiguous()
             ye = ops.linear(ops.linear_swiglu(xe, w_gu), w_d).float()
             we = (topw * sel).sum(-1).index_select(0, rows)
-            out.index_add_(0, rows, ye * we[:, None])
-        return out.to(x.dtype)
+            acc.index_add_(0, rows, ye * we[:, None])
+        return _copy_out(acc.to(x.dtype), out)
 
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
                 hidden_only: bool = False) -> torch.Tensor:
@@ -328,11 +374,7 @@ class LlamaModel:
                 self.lora.apply(li, "o", a, h)
             x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
             if cfg.is_moe:
-                h = self._moe(x, L)
-                buf = self.comm.partial_buffer(T)
-                if buf is not None:
-                    buf.copy_(h)
-                    h = buf
+                h = self._moe(x, L, out=self.comm.partial_buffer(T))
             else:
                 h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"], out=self.comm.partial_buffer(T))
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm

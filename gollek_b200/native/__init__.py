@@ -41,6 +41,7 @@ CUDA_SOURCES = [
     "kernels/gguf.cu",
     "kernels/gemm_fp8.cu",
     "kernels/attention_tc.cu",
+    "kernels/moe.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

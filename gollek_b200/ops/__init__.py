@@ -335,3 +335,73 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
 
 def attention_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# ---------------------------------------------------------------------------- MoE (K12)
+_MOE_WS = {}
+
+
+def _moe_workspace(device: torch.device, ints: int) -> torch.Tensor:
+    """Per-device int32 routing workspace, zero-filled once (the plan kernel re-zeroes its counters
+    after each use, so the same buffer serves every layer, step and CUDA-graph replay)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _MOE_WS.get(key)
+    if ws is None or ws.numel() < ints:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("MoE workspace must be created before CUDA-graph capture (run one eager step)")
+        ws = torch.zeros(max(ints, 1 << 16), dtype=torch.int32, device=device)
+        _MOE_WS[key] = ws
+    return ws
+
+
+def moe_route_ref(x: torch.Tensor, router: torch.Tensor, top_k: int, renorm: bool = True):
+    """fp32 softmax top-k routing: (ids [T, k] int64, weights [T, k] fp32)."""
+    probs = torch.softmax(x.float() @ router.float().t(), dim=-1)
+    w, ids = probs.topk(top_k, dim=-1)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return ids, w
+
+
+def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, top_k: int,
+              e0: int = 0, e_loc: Optional[int] = None, renorm: bool = True,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Mixture-of-experts FFN over the local experts [e0, e0 + e_loc) of ``router.shape[0]``.
+
+    w_gu [e_loc * 2F, H]: per expert, gate/up rows interleaved in groups of 64 (SwiGLU epilogue);
+    w_down [e_loc * H, F]. Returns Σ over the token's top-k experts that are local of
+    weight · down(silu(gate) · up) — under expert parallelism a partial sum that the following
+    tensor-parallel all-reduce completes."""
+    T, H = x.shape
+    E = router.shape[0]
+    e_loc = E if e_loc is None else e_loc
+    F_ = w_down.shape[1]
+    if not x.is_cuda:
+        ids, w = moe_route_ref(x, router, top_k, renorm)
+        acc = torch.zeros(T, H, dtype=torch.float32)
+        for le in range(e_loc):
+            sel = ids == (e0 + le)
+            rows = sel.any(-1).nonzero().flatten()
+            if rows.numel() == 0:
+                continue
+            xe = x.index_select(0, rows)
+            he = ref.gemm_swiglu(xe, w_gu[le * 2 * F_:(le + 1) * 2 * F_])
+            ye = ref.gemm(he, w_down[le * H:(le + 1) * H]).float()
+            acc.index_add_(0, rows, ye * (w * sel).sum(-1).index_select(0, rows)[:, None])
+        return _cpu(acc.to(x.dtype), out)
+    C = _C()
+    out = torch.empty_like(x) if out is None else out
+    if T == 0:
+        return out
+    cap = C.moe_capacity_rows(T, top_k, e_loc)
+    ws = _moe_workspace(x.device, C.moe_ws_ints(T, top_k, e_loc))
+    dev = x.device
+    ids = torch.empty(T * top_k, dtype=torch.int32, device=dev)
+    dest = torch.empty(T * top_k, dtype=torch.int32, device=dev)
+    wts = torch.empty(T * top_k, dtype=torch.float32, device=dev)
+    xp = torch.empty(cap, H, dtype=x.dtype, device=dev)
+    hp = torch.empty(cap, F_, dtype=x.dtype, device=dev)
+    yp = torch.empty(cap, H, dtype=x.dtype, device=dev)
+    C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, yp, top_k, renorm, e0, e_loc)
+    LAUNCHES.add(6)
+    return out

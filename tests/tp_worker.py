@@ -7,7 +7,8 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
-def run_tp(rank, world, port, backend, comm_kind, prompts, max_tokens, result_q, num_layers=None):
+def run_tp(rank, world, port, backend, comm_kind, prompts, max_tokens, result_q, num_layers=None,
+           model="tiny-llama", expert_parallel=False):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
@@ -19,7 +20,7 @@ def run_tp(rank, world, port, backend, comm_kind, prompts, max_tokens, result_q,
         from gollek_b200.models.reference import init_random_weights
         from gollek_b200.parallel.dist import NcclComm, init_distributed, cpu_group
         init_distributed(backend=backend, timeout_s=60)
-        cfg = preset("tiny-llama")
+        cfg = preset(model)
         if num_layers:
             cfg.num_hidden_layers = num_layers
         w = init_random_weights(cfg, seed=0)
@@ -32,7 +33,8 @@ def run_tp(rank, world, port, backend, comm_kind, prompts, max_tokens, result_q,
             comm = NcclComm(rank, world)
         ec = EngineConfig(device=dev, dtype="bfloat16" if dev == "cuda" else "float32", block_size=16,
                           max_num_seqs=8, max_num_batched_tokens=256, max_model_len=512,
-                          use_cuda_graphs=False, tensor_parallel_size=world)
+                          use_cuda_graphs=False, tensor_parallel_size=world,
+                          enable_expert_parallel=expert_parallel)
         eng = LLMEngine(ec, model_cfg=cfg, weights=w.__getitem__, comm=comm, num_blocks=128)
         outs = eng.generate(prompts, SamplingParams(temperature=0.0, max_tokens=max_tokens, ignore_eos=True))
         if comm_kind == "fused":
