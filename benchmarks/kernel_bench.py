@@ -177,6 +177,24 @@ def main():
                 ms = time_cuda(lambda: ops.linear(x, fw, out=out), iters=args.iters, flush_bytes=flush)
                 rec(f"fp8_{name}_tp8_M{M}", ms, 2.0 * M * N * K, N * K + 2.0 * M * (K + N),
                     {"splits": ops.cuda_ext().gemm_fp8_splits(M, N, K, 0)})
+    if "gemm_sweep" in only:
+        # tile width x split-K at the token counts of a saturated serving step (~255 decodes + one prompt)
+        shapes = [("qkv", 6144, 4096, 0), ("o_proj", 4096, 4096, 1), ("gate_up_swiglu", 28672, 4096, 2),
+                  ("down", 4096, 14336, 1)]
+        for M in (1344, 2048, 4352):
+            for name, N, K, epi in shapes:
+                a = torch.randn(M, K, device=dev).bfloat16()
+                w = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+                res = torch.randn(M, N, device=dev).bfloat16() if epi == 1 else None
+                out = torch.empty(M, N // 2 if epi == 2 else N, device=dev, dtype=torch.bfloat16)
+                ws = torch.empty(4 * M * N, device=dev)
+                auto = ops.cuda_ext().gemm_plan(M, N, K, epi)
+                for bn in ((128, 256) if epi == 2 else (128, 256)):
+                    for sp in (1, 2, 3):
+                        fn = lambda: ops.cuda_ext().gemm_bf16(out, a, w, res, epi, bn, None, 0, sp, ws)
+                        ms = time_cuda(fn, iters=args.iters, flush_bytes=flush)
+                        rec(f"gemm_{name}_M{M}_bn{bn}_s{sp}", ms, 2.0 * M * N * K,
+                            2.0 * (M * K + N * K + M * N), {"auto": auto})
     if "moe" in only:
         # Mixtral-8x7B MoE layer (H 4096, F 14336, 8 experts, top-2): all experts on one GPU, and the
         # one-expert shard a rank holds under EP=8 (its partial sum; the all-reduce is not included)
@@ -192,10 +210,10 @@ def main():
                                iters=args.iters, flush_bytes=flush)
                 with torch.no_grad():
                     ids, _ = ops.moe_route_ref(x[:min(T, 4096)].float(), router.float(), k)
-                rows = T * k * e_loc / E  # expected routed rows on these experts (uniform router)
+                nrows = T * k * e_loc / E  # expected routed rows on these experts (uniform router)
                 active = min(e_loc, len(set(ids.flatten().tolist()) & set(range(e_loc))) or e_loc)
-                flops = 2.0 * rows * 3 * H * F
-                nbytes = active * 3.0 * H * F * 2 + 2.0 * 2 * T * H + 2.0 * rows * (2 * H + F)
+                flops = 2.0 * nrows * 3 * H * F
+                nbytes = active * 3.0 * H * F * 2 + 2.0 * 2 * T * H + 2.0 * nrows * (2 * H + F)
                 rec(f"moe_mixtral_{'all8' if e_loc == 8 else 'ep8_shard'}_T{T}", ms, flops, nbytes)
     if args.json:
         with open(args.json, "w") as f:

@@ -3,6 +3,7 @@
     python benchmarks/one_kernel.py gemm --M 8192 --N 28672 --K 4096 [--swiglu] [--reps 3]
     python benchmarks/one_kernel.py decode --B 256 --ctx 1200
     python benchmarks/one_kernel.py prefill --nseq 4 --L 2048
+    python benchmarks/one_kernel.py moe --T 256 --e-loc 1      (Mixtral-8x7B layer, one EP=8 shard)
 """
 from __future__ import annotations
 
@@ -19,7 +20,9 @@ from gollek_b200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "decode", "prefill"])
+    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe"])
+    ap.add_argument("--T", type=int, default=256)
+    ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
     ap.add_argument("--N", type=int, default=28672)
     ap.add_argument("--K", type=int, default=4096)
@@ -37,6 +40,14 @@ def main():
         w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
         for _ in range(a.reps):
             (ops.linear_swiglu(x, w, bn=a.bn) if a.swiglu else ops.linear(x, w, bn=a.bn))
+    elif a.kind == "moe":
+        H, F, E = 4096, 14336, 8
+        x = torch.randn(a.T, H, device=dev).bfloat16()
+        router = (torch.randn(E, H, device=dev) * 0.02).bfloat16()
+        gu = (torch.randn(a.e_loc * 2 * F, H, device=dev) * 0.02).bfloat16()
+        dn = (torch.randn(a.e_loc * H, F, device=dev) * 0.02).bfloat16()
+        for _ in range(a.reps):
+            ops.fused_moe(x, router, gu, dn, 2, e0=0, e_loc=a.e_loc)
     elif a.kind == "decode":
         Hq, Hk, D, bs = 32, 8, 128, 16
         nblk = (a.ctx + bs - 1) // bs

@@ -213,8 +213,8 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
 // xp/yp [cap, H] and hp [cap, F] bf16 scratch with cap = moe_capacity_rows(T, topk, e_loc).
 void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, torch::Tensor w_gu,
                      torch::Tensor w_down, torch::Tensor ws, torch::Tensor ids, torch::Tensor wts, torch::Tensor dest,
-                     torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, int64_t topk, bool renorm, int64_t e0,
-                     int64_t e_loc) {
+                     torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, c10::optional<torch::Tensor> ypart,
+                     int64_t topk, bool renorm, int64_t e0, int64_t e_loc) {
   for (auto* t : {&out, &x, &router, &w_gu, &w_down, &xp, &hp, &yp}) check_bf16(*t, "moe operand");
   check_same_device(x, w_gu);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "moe: x/out row-major [T, H]");
@@ -235,10 +235,25 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
                   ids.numel() >= (int64_t)T * topk && dest.numel() >= (int64_t)T * topk &&
                   wts.numel() >= (int64_t)T * topk,
               "moe: ids/dest int32 and wts fp32 of T*topk");
+  int bn_gu, bn_dn, splits;
+  moe_plan_host(T, (int)topk, E, (int)e_loc, H, F, bn_gu, bn_dn, splits);
+  float* yq = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(ypart.has_value() && ypart->is_cuda() && ypart->scalar_type() == at::kFloat &&
+                    ypart->numel() >= (int64_t)splits * cap * H,
+                "moe: split-K down projection needs an fp32 buffer of ", (int64_t)splits * cap * H, " elements");
+    yq = ypart->data_ptr<float>();
+  }
   launch_moe_forward(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), router.data_ptr(), w_gu.data_ptr(),
                      w_down.data_ptr(), ws.data_ptr<int>(), ids.data_ptr<int>(), wts.data_ptr<float>(),
-                     dest.data_ptr<int>(), xp.data_ptr(), hp.data_ptr(), yp.data_ptr(), T, H, F, E, (int)topk,
+                     dest.data_ptr<int>(), xp.data_ptr(), hp.data_ptr(), yp.data_ptr(), yq, T, H, F, E, (int)topk,
                      renorm ? 1 : 0, (int)e0, (int)e_loc, nullptr, cur_stream());
+}
+
+std::vector<int64_t> moe_plan_py(int64_t T, int64_t topk, int64_t E, int64_t e_loc, int64_t H, int64_t F) {
+  int a, b, c;
+  moe_plan_host((int)T, (int)topk, (int)E, (int)e_loc, (int)H, (int)F, a, b, c);
+  return {a, b, c};
 }
 
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
@@ -462,6 +477,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)");
   m.def("moe_capacity_rows", &moe_capacity_rows);
   m.def("moe_ws_ints", &moe_ws_ints);
+  m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");
   m.def("argmax", &argmax_out, "greedy argmax (K11)");
   m.def("apply_penalties", &apply_penalties_, "repetition/frequency/presence penalties (K11)");
   m.def("sample", &sample_out, "top-k/min-p/top-p sampling (K11)");

@@ -365,7 +365,8 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ C, int64_t ldc,
 template <int BN, int EPI>
 void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
                    int64_t ldr, int M, int N, int K, int splits, float* partial, uint32_t* status, int grid_limit,
-                   cudaStream_t s, const int* tile_group = nullptr, const int* num_m_dev = nullptr, int groups = 1) {
+                   cudaStream_t s, const int* tile_group = nullptr, const int* num_m_dev = nullptr, int groups = 1,
+                   bool reduce = true) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -384,7 +385,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
                                      partial, status, tile_group, num_m_dev);
   check_launch("gemm_bf16");
-  if (splits > 1) {
+  if (splits > 1 && reduce) {
     const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
     const int64_t threads = (int64_t)M * (out_n / 8);
     splitk_reduce_kernel<EPI><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
@@ -419,6 +420,17 @@ void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* res
 int gemm_pick_bn(int M, int N, int epi) {
   const int num_m = (M + 127) / 128;
   const int sms = num_sms();
+  if (num_m >= 4) {
+    // Compute-bound: the persistent grid runs ceil(tiles / SMs) rounds of tiles, so pick the width
+    // with the fewest rounds x tile time. A 128-wide tile takes ~0.57 of a 256-wide one (measured
+    // 1.14x lower per-FLOP throughput at M = 4352), which makes 128 win when 256-wide tiles leave a
+    // mostly idle last round (e.g. M = 1344, N = 4096: 176 tiles on 148 SMs).
+    auto cost = [&](int bn, double rel) {
+      const int tiles = num_m * ((N + bn - 1) / bn);
+      return (double)((tiles + sms - 1) / sms) * rel;
+    };
+    return cost(128, 0.57) < cost(256, 1.0) ? 128 : 256;
+  }
   if (epi == kEpiSwiglu) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
   if (num_m * ((N + 255) / 256) >= sms) return 256;
   if (num_m * ((N + 127) / 128) >= sms / 2) return 128;
@@ -483,7 +495,7 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
 
 void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, int M_cap,
                          int N, int K, int groups, int epi, int bn, const int* tile_group, const int* num_m_dev,
-                         uint32_t* status, cudaStream_t s) {
+                         int splits, float* partial, uint32_t* status, cudaStream_t s) {
   throw_if(K % 8 != 0, "grouped gemm: K must be a multiple of 8");
   throw_if(ldc % 8 != 0, "grouped gemm: output row pitch must keep 16-byte alignment");
   throw_if(M_cap % 128 != 0, "grouped gemm: row capacity must be a multiple of 128");
@@ -498,10 +510,13 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
     bn = (m_tiles * ((N + 255) / 256) >= num_sms() || epi == kEpiSwiglu) ? 256 : 128;
   }
   if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  if (splits < 1) splits = 1;
+  // split-K partials [splits, M_cap, N] are left for the caller to reduce (no reduce pass here)
+  throw_if(splits > 1 && (partial == nullptr || epi != kEpiNone), "grouped gemm: split-K needs fp32 partials, no epilogue");
 #define GOLLEK_GG_CASE(BNV, EPIV) \
   if (bn == BNV && epi == EPIV)   \
-    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, nullptr, 0, M_cap, N, K, 1, nullptr, status, 0, s, \
-                                    tile_group, num_m_dev, groups);
+    return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, nullptr, 0, M_cap, N, K, splits, partial, status, 0, s, \
+                                    tile_group, num_m_dev, groups, /*reduce=*/false);
   GOLLEK_GG_CASE(256, kEpiNone)
   GOLLEK_GG_CASE(128, kEpiNone)
   GOLLEK_GG_CASE(64, kEpiNone)

@@ -58,15 +58,16 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
 // expert, live M-tile count in device memory; B = experts stacked [groups * N, K].
 void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, int M_cap,
                          int N, int K, int groups, int epi, int bn, const int* tile_group, const int* num_m_dev,
-                         uint32_t* status, cudaStream_t s);
+                         int splits, float* partial, uint32_t* status, cudaStream_t s);
 
 // ---- MoE (K12 routing / permutation / combine around two grouped GEMMs)
 int moe_capacity_rows(int T, int topk, int e_loc);
 int moe_ws_ints(int T, int topk, int e_loc);
+void moe_plan_host(int T, int topk, int E, int e_loc, int H, int F, int& bn_gu, int& bn_dn, int& splits);
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
-                        int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc, uint32_t* status,
-                        cudaStream_t s);
+                        float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,
+                        uint32_t* status, cudaStream_t s);
 
 // ---- sampling (K11)
 void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s);

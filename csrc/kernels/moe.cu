@@ -19,7 +19,10 @@
 // Reference behaviour: Mixtral routing in runner/safetensor/…/generation/moe/MoeForwardPass.java:39-128
 // and the EP dispatch contract of core/optimization/gollek-plugin-elastic-ep/…/binding/ElasticEpBinding.java:19-45.
 #include "../common/common.cuh"
+#include "../common/tma_host.h"
 #include "launchers.h"
+
+#include <algorithm>
 
 using namespace gollek;
 
@@ -28,39 +31,68 @@ namespace {
 constexpr int kMaxE = 64;
 constexpr int kMaxK = 8;
 
+constexpr int kRouteTok = 4;  // tokens per routing CTA
+
+// Routing: one CTA per 4 tokens. All 256 threads split the hidden dimension (8 elements each per
+// 2048-wide stripe) and accumulate the 4 tokens x 8 experts of the current expert chunk, so the
+// router weights are read once per CTA and every thread has many independent loads in flight;
+// a shared-memory reduction gives the logits, then warp w < 4 does softmax / top-k for token w.
 __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                         const __nv_bfloat16* __restrict__ wr, int T, int H, int E,
                                                         int topk, int renorm, int e0, int e_loc, int* __restrict__ ids,
                                                         float* __restrict__ wts, int* __restrict__ counts) {
-  __shared__ float s_logit[8][kMaxE];
+  __shared__ float s_part[8][kRouteTok * 8];
+  __shared__ float s_logit[kRouteTok][kMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
-  const __nv_bfloat16* xr = x + (int64_t)t * ldx;
+  const int t0 = blockIdx.x * kRouteTok;
+  const int ntok = min(kRouteTok, T - t0);
   for (int ec = 0; ec < E; ec += 8) {
-    float acc[8];
+    float acc[kRouteTok][8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    for (int h = lane * 8; h < H; h += 256) {
-      float xv[8];
-      bf16x8_to_float(*reinterpret_cast<const uint4*>(xr + h), xv);
+    for (int a = 0; a < kRouteTok; ++a)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (ec + e < E) {
+      for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
+    for (int h = threadIdx.x * 8; h < H; h += 2048) {
+      uint4 wu[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        wu[e] = (ec + e < E) ? *reinterpret_cast<const uint4*>(wr + (int64_t)(ec + e) * H + h) : make_uint4(0, 0, 0, 0);
+      uint4 xu[kRouteTok];
+#pragma unroll
+      for (int a = 0; a < kRouteTok; ++a)
+        xu[a] = a < ntok ? *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + a) * ldx + h) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int a = 0; a < kRouteTok; ++a) {
+        float xv[8];
+        bf16x8_to_float(xu[a], xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
           float wv[8];
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(wr + (int64_t)(ec + e) * H + h), wv);
+          bf16x8_to_float(wu[e], wv);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[e] = fmaf(xv[i], wv[i], acc[e]);
+          for (int i = 0; i < 8; ++i) acc[a][e] = fmaf(xv[i], wv[i], acc[a][e]);
         }
       }
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float v = warp_sum(acc[e]);
-      if (lane == 0 && ec + e < E) s_logit[warp][ec + e] = v;
+    for (int a = 0; a < kRouteTok; ++a)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = warp_sum(acc[a][e]);
+        if (lane == 0) s_part[warp][a * 8 + e] = v;
+      }
+    __syncthreads();
+    if (threadIdx.x < kRouteTok * 8) {
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) v += s_part[w][threadIdx.x];
+      const int a = threadIdx.x >> 3, e = ec + (threadIdx.x & 7);
+      if (e < E) s_logit[a][e] = v;
     }
+    __syncthreads();
   }
-  __syncwarp();
+  if (warp >= ntok) return;
+  const int t = t0 + warp;
   // softmax over E (lane i owns experts i and i + 32)
   float v0 = lane < E ? s_logit[warp][lane] : -INFINITY;
   float v1 = lane + 32 < E ? s_logit[warp][lane + 32] : -INFINITY;
@@ -162,8 +194,11 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const __nv_bfloat16* __
     *reinterpret_cast<uint4*>(dst + h) = *reinterpret_cast<const uint4*>(src + h);
 }
 
+// yp: bf16 expert outputs [cap, H], or (splits > 1) the down GEMM's fp32 split-K partials
+// [splits, cap, H], summed here instead of in a separate reduce pass.
 __global__ void __launch_bounds__(256) moe_combine_kernel(__nv_bfloat16* __restrict__ out, int64_t ldo,
                                                           const __nv_bfloat16* __restrict__ yp, int64_t ldy,
+                                                          const float* __restrict__ ypart, int splits, int64_t cap,
                                                           const int* __restrict__ dest, const float* __restrict__ wts,
                                                           int T, int topk, int H) {
   const int groups = H / 8;
@@ -178,7 +213,17 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(__nv_bfloat16* __restr
     if (d < 0) continue;
     const float w = wts[(int64_t)t * topk + j];
     float y[8];
-    bf16x8_to_float(*reinterpret_cast<const uint4*>(yp + (int64_t)d * ldy + c), y);
+    if (splits > 1) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        const float* p = ypart + ((int64_t)sp * cap + d) * H + c;
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        y[0] += a.x; y[1] += a.y; y[2] += a.z; y[3] += a.w; y[4] += b.x; y[5] += b.y; y[6] += b.z; y[7] += b.w;
+      }
+    } else {
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(yp + (int64_t)d * ldy + c), y);
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, y[e], acc[e]);
   }
@@ -196,10 +241,27 @@ int moe_capacity_rows(int T, int topk, int e_loc) {
 
 int moe_ws_ints(int T, int topk, int e_loc) { return kWsTiles + moe_capacity_rows(T, topk, e_loc) / 128; }
 
+// Tile widths of the two grouped GEMMs and the down GEMM's split-K factor, from the expected live
+// M tiles (a uniform router puts T*topk/E rows on each expert). Few tiles (decode, or one expert per
+// rank under EP) would leave most SMs idle while the weights stream, so the down GEMM (K = F, long)
+// is split over K and the combine kernel sums its fp32 partials.
+void moe_plan_host(int T, int topk, int E, int e_loc, int H, int F, int& bn_gu, int& bn_dn, int& splits) {
+  const int sms = num_sms();
+  const int per_expert = (T * topk + E - 1) / E;
+  const int m_live = std::max(1, std::min(moe_capacity_rows(T, topk, e_loc) / 128, e_loc * ((per_expert + 127) / 128)));
+  bn_gu = (m_live * ((2 * F + 255) / 256) >= sms) ? 256 : 128;
+  if (m_live * ((H + 255) / 256) >= sms) bn_dn = 256;
+  else if (m_live * ((H + 127) / 128) >= sms / 2) bn_dn = 128;
+  else bn_dn = 64;
+  const int tiles = m_live * ((H + bn_dn - 1) / bn_dn);
+  splits = 1;
+  if (tiles < sms / 2) splits = std::max(1, std::min({(sms + tiles - 1) / tiles, F / 64 / 4, 8}));
+}
+
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
-                        int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc, uint32_t* status,
-                        cudaStream_t s) {
+                        float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,
+                        uint32_t* status, cudaStream_t s) {
   throw_if(E > kMaxE || E < 1, "moe: at most 64 experts");
   throw_if(topk < 1 || topk > kMaxK || topk > E, "moe: top-k must be in [1, min(8, E)]");
   throw_if(H % 256 != 0, "moe: hidden size must be a multiple of 256");
@@ -210,7 +272,7 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   if (T == 0) return;
   const int cap = moe_capacity_rows(T, topk, e_loc);
   auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
-  moe_route_kernel<<<(T + 7) / 8, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
+  moe_route_kernel<<<(T + kRouteTok - 1) / kRouteTok, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
                                                renorm, e0, e_loc, ids, wts, ws);
   check_launch("moe_route");
   moe_plan_kernel<<<1, 32, 0, s>>>(ws, e_loc, cap / 128);
@@ -221,14 +283,19 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   check_launch("moe_gather");
   const int* num_m = ws + kWsNumM;
   const int* tile_group = ws + kWsTiles;
+  int bn_gu, bn_dn, splits;
+  moe_plan_host(T, topk, E, e_loc, H, F, bn_gu, bn_dn, splits);
+  throw_if(splits > 1 && ypart == nullptr, "moe: split-K down projection needs the fp32 partial buffer");
   // gate/up (interleaved in groups of 64 per expert) with the SwiGLU epilogue: hp [cap, F]
-  launch_gemm_grouped(hp, F, xp, H, w_gu, H, cap, 2 * F, H, e_loc, kEpiSwiglu, 0, tile_group, num_m, status, s);
-  // down: yp [cap, H]
-  launch_gemm_grouped(yp, H, hp, F, w_down, F, cap, H, F, e_loc, kEpiNone, 0, tile_group, num_m, status, s);
+  launch_gemm_grouped(hp, F, xp, H, w_gu, H, cap, 2 * F, H, e_loc, kEpiSwiglu, bn_gu, tile_group, num_m, 1,
+                      nullptr, status, s);
+  // down: yp [cap, H] (bf16), or fp32 partials [splits, cap, H] summed by the combine
+  launch_gemm_grouped(yp, H, hp, F, w_down, F, cap, H, F, e_loc, kEpiNone, bn_dn, tile_group, num_m, splits,
+                      ypart, status, s);
   const int64_t threads = (int64_t)T * (H / 8);
   moe_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
-      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(yp), H, dest, wts, T, topk,
-      H);
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(yp), H, ypart, splits, cap,
+      dest, wts, T, topk, H);
   check_launch("moe_combine");
 }
 

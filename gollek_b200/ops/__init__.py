@@ -401,7 +401,14 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
     wts = torch.empty(T * top_k, dtype=torch.float32, device=dev)
     xp = torch.empty(cap, H, dtype=x.dtype, device=dev)
     hp = torch.empty(cap, F_, dtype=x.dtype, device=dev)
-    yp = torch.empty(cap, H, dtype=x.dtype, device=dev)
-    C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, yp, top_k, renorm, e0, e_loc)
+    _, _, splits = C.moe_plan(T, top_k, E, e_loc, H, F_)
+    if splits > 1:  # down projection split over K: fp32 partials summed by the combine kernel
+        yp = None
+        ypart = torch.empty(splits * cap * H, dtype=torch.float32, device=dev)
+    else:
+        yp = torch.empty(cap, H, dtype=x.dtype, device=dev)
+        ypart = None
+    C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, xp if yp is None else yp, ypart,
+                  top_k, renorm, e0, e_loc)
     LAUNCHES.add(6)
     return out

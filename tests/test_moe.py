@@ -121,3 +121,22 @@ def test_mixtral_engine_gpu_matches_oracle():
         for i, tok in enumerate(o.output_token_ids):
             row = logits[len(p) - 1 + i]
             assert row[tok] >= row.max() - 0.05, (i, tok, int(row.argmax()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [3, 64, 700])
+def test_fused_moe_gpu_one_expert_per_rank(T):
+    """EP=8 shards (one expert each: few output tiles, so the down projection is split over K and
+    the combine sums fp32 partials); the eight partial sums add up to the full layer."""
+    E, k, H, F = 8, 2, 4096, 1024
+    ws, router, gu, dn = _experts(E, H, F, seed=21)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(22)).to(bf).cuda()
+    rb, gub, dnb = router.to(bf).cuda(), gu.to(bf).cuda(), dn.to(bf).cuda()
+    assert ops.cuda_ext().moe_plan(T, k, E, 1, H, F)[2] > 1 or T > 64
+    full = ops.fused_moe(x, rb, gub, dnb, k)
+    parts = [ops.fused_moe(x, rb, gub[e * 2 * F:(e + 1) * 2 * F], dnb[e * H:(e + 1) * H], k, e0=e, e_loc=1)
+             for e in range(E)]
+    total = sum(p.float() for p in parts)
+    atol = 1e-2 * float(full.float().abs().max())
+    torch.testing.assert_close(total, full.float(), rtol=3e-2, atol=atol)
