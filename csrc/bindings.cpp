@@ -54,13 +54,15 @@ void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor re
 
 void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
                        c10::optional<torch::Tensor> cache, c10::optional<torch::Tensor> slots, int64_t H, int64_t Hk,
-                       int64_t D) {
+                       int64_t D, c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> q_norm,
+                       c10::optional<torch::Tensor> k_norm, double norm_eps) {
   check_bf16(qkv, "qkv");
   check_bf16(q_out, "q_out");
   check_i32(positions, "positions");
   check_cuda(cos_sin, "cos_sin");
-  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == D,
-              "cos_sin must be fp32 [max_pos, head_dim]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) <= D &&
+                  cos_sin.size(1) % 4 == 0,
+              "cos_sin must be fp32 [max_pos, rotary_dim <= head_dim]");
   TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (H + 2 * Hk) * D, "qkv shape mismatch");
   TORCH_CHECK(qkv.stride(0) % 8 == 0, "qkv row pitch must keep 16-byte alignment");
   const int T = qkv.size(0);
@@ -79,11 +81,28 @@ void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor pos
     sp = slots->data_ptr<int>();
     bs = cache->size(3);
   }
+  const void* bp = nullptr;
+  const void* qn = nullptr;
+  const void* kn = nullptr;
+  if (bias.has_value()) {
+    check_bf16(*bias, "bias");
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == (int64_t)(H + 2 * Hk) * D, "qkv bias [(H + 2Hk) * D]");
+    bp = bias->data_ptr();
+  }
+  if (q_norm.has_value() || k_norm.has_value()) {
+    TORCH_CHECK(q_norm.has_value() && k_norm.has_value(), "QK-norm needs both q and k weights");
+    check_bf16(*q_norm, "q_norm");
+    check_bf16(*k_norm, "k_norm");
+    TORCH_CHECK(q_norm->numel() == D && k_norm->numel() == D, "QK-norm weights are [head_dim]");
+    qn = q_norm->data_ptr();
+    kn = k_norm->data_ptr();
+  }
   launch_rope_kv_write(q_out.data_ptr(), qkv.data_ptr(), positions.data_ptr<int>(), cos_sin.data_ptr<float>(), cp,
-                       sp, T, H, Hk, D, bs, qkv.stride(0), (int)cos_sin.size(0), cur_stream());
+                       sp, T, H, Hk, D, bs, qkv.stride(0), (int)cos_sin.size(0), bp, qn, kn, (float)norm_eps,
+                       (int)cos_sin.size(1), cur_stream());
 }
 
-void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
+void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table, double scale) {
   check_bf16(table, "table");
   check_bf16(out, "out");
   check_i32(ids, "ids");
@@ -91,7 +110,7 @@ void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table) {
                   out.size(1) == table.size(1),
               "embedding: shapes");
   launch_embedding(out.data_ptr(), ids.data_ptr<int>(), table.data_ptr(), ids.size(0), table.size(1), table.size(0),
-                   cur_stream());
+                   (float)scale, cur_stream());
 }
 
 void silu_mul_out(torch::Tensor out, torch::Tensor x) {
@@ -103,7 +122,8 @@ void silu_mul_out(torch::Tensor out, torch::Tensor x) {
 
 void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                                 torch::Tensor seq_lens, double scale, int64_t num_splits,
-                                c10::optional<torch::Tensor> workspace, bool tensor_cores) {
+                                c10::optional<torch::Tensor> workspace, bool tensor_cores, int64_t window,
+                                double softcap) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(cache, "kv_cache");
@@ -128,12 +148,12 @@ void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tenso
   launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(),
                       tensor_cores ? (int)cache.size(0) : 0, block_tables.data_ptr<int>(),
                       block_tables.stride(0), seq_lens.data_ptr<int>(), B, H, cache.size(2), D, cache.size(3),
-                      (int)num_splits, (float)scale, po, pml, cur_stream());
+                      (int)num_splits, (float)scale, po, pml, (int)window, (float)softcap, cur_stream());
 }
 
 void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                                  torch::Tensor seq_lens, torch::Tensor query_start, torch::Tensor tiles,
-                                 double scale, bool tensor_cores) {
+                                 double scale, bool tensor_cores, int64_t window, double softcap) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(cache, "kv_cache");
@@ -150,13 +170,14 @@ void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tens
     launch_paged_prefill_tc(out.data_ptr(), out.stride(0), q.data_ptr(), q.size(0), q.stride(0), cache.data_ptr(),
                             cache.size(0), block_tables.data_ptr<int>(), block_tables.stride(0),
                             seq_lens.data_ptr<int>(), query_start.data_ptr<int>(), tiles.data_ptr<int>(),
-                            tiles.size(0), q.size(1), cache.size(2), (float)scale, cur_stream());
+                            tiles.size(0), q.size(1), cache.size(2), (float)scale, (int)window, (float)softcap,
+                            cur_stream());
     return;
   }
   launch_paged_prefill(out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), cache.data_ptr(),
                        block_tables.data_ptr<int>(), block_tables.stride(0), seq_lens.data_ptr<int>(),
                        query_start.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), q.size(1), cache.size(2),
-                       q.size(2), cache.size(3), (float)scale, cur_stream());
+                       q.size(2), cache.size(3), (float)scale, (int)window, (float)softcap, cur_stream());
 }
 
 void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
@@ -170,7 +191,7 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
   TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: K-major operands, row-major out");
   const int M = a.size(0), N = b.size(0), K = a.size(1);
   TORCH_CHECK(out.size(0) == M, "gemm: out rows");
-  if (epi == kEpiSwiglu) {
+  if (epi_gated((int)epi)) {
     TORCH_CHECK(out.size(1) == N / 2, "gemm swiglu: out [M, N/2]");
   } else {
     TORCH_CHECK(out.size(1) == N, "gemm: out [M, N]");

@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q,        // [B, H, D] rows at q_stride
     const __nv_bfloat16* __restrict__ cache,    // [NB, 2, Hk, BS, D]
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens, int Hk,
-    int num_splits, float scale_log2, int64_t q_stride, uint32_t* status) {
+    int num_splits, float scale_log2, int64_t q_stride, uint32_t* status, int window, float softcap_log2) {
   using C = DecodeCfg<D, G, BS>;
   constexpr int TILE = BS * D;                         // elements of one K (or V) tile
   constexpr uint32_t TILE_BYTES = TILE * 2;
@@ -78,8 +78,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
 
   const int L = seq_lens[b];
   const int nblocks = (L + BS - 1) / BS;
-  const int per = (nblocks + num_splits - 1) / num_splits;
-  const int blk_begin = split * per;
+  // sliding window: the query at position L-1 sees keys [L - window, L); earlier blocks are skipped
+  const int kv_lo = window > 0 ? max(0, L - window) : 0;
+  const int blk_lo = kv_lo / BS;
+  const int per = (nblocks - blk_lo + num_splits - 1) / num_splits;
+  const int blk_begin = blk_lo + split * per;
   const int blk_end = min(nblocks, blk_begin + per);
   const int nmine = blk_begin + warp < blk_end ? (blk_end - blk_begin - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
   const int* bt = block_tables + (int64_t)b * bt_stride;
@@ -160,8 +163,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
       float bm = -INFINITY;
 #pragma unroll
       for (int i = 0; i < C::NI; ++i) {
-        const bool valid = tok0 + i * C::TPI + tsub < L;
-        s[g][i] = valid ? s[g][i] : -INFINITY;
+        const int tk = tok0 + i * C::TPI + tsub;
+        const bool valid = tk < L && tk >= kv_lo;
+        float v = s[g][i];
+        if (softcap_log2 > 0.f) v = softcap_log2 * tanh_approx(v * (1.f / softcap_log2));
+        s[g][i] = valid ? v : -INFINITY;
         bm = fmaxf(bm, s[g][i]);
       }
 #pragma unroll
@@ -183,7 +189,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     for (int i = 0; i < C::NI; ++i) {
       float vf[8];
       bf16x8_to_float(*reinterpret_cast<const uint4*>(vt + (i * C::TPI + tsub) * D + c * 8), vf);
-      const bool valid = tok0 + i * C::TPI + tsub < L;
+      const bool valid = tok0 + i * C::TPI + tsub < L && tok0 + i * C::TPI + tsub >= kv_lo;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float p = valid ? s[g][i] : 0.f;
@@ -329,8 +335,11 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
     const __nv_bfloat16* __restrict__ cache,                  // [NB, 2, Hk, BS, D]
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens,
     const int* __restrict__ query_start, const int* __restrict__ tiles,  // tiles[i] = (b, q_off)
-    int H, int Hk, int BS, float scale_log2) {
-  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "head_dim");
+    int H, int Hk, int BS, float scale_log2, int window, float softcap_log2) {
+  static_assert(D % 16 == 0 && D >= 32 && D <= 256, "head_dim");
+  // head_dim 256: the O accumulator alone takes 128 registers per thread, so Q fragments are
+  // re-read from shared memory for every key tile instead of being held in registers
+  constexpr bool kQRegs = D <= 128;
   constexpr int KSTEPS = D / 16;  // k-steps over head dim for QK^T
   constexpr int DT = D / 8;       // n8 tiles over head dim for PV
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -357,6 +366,8 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
   const int last_q_pos = ctx0 + q_off + rows - 1;
   const int kv_end = min(L, last_q_pos + 1);
   const int n_tiles = (kv_end + kPfBN - 1) / kPfBN;
+  // sliding window: the first query row sees keys >= ctx0 + q_off - window + 1; earlier tiles skipped
+  const int t_lo = window > 0 ? max(0, ctx0 + q_off - window + 1) / kPfBN : 0;
   const int* bt = block_tables + (int64_t)b * bt_stride;
   const int64_t head_stride = (int64_t)BS * D;
 
@@ -375,7 +386,7 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
       cp_async16(dV + swz<D>(r, ch), vs, v);
     }
   };
-  if (n_tiles > 0) load_kv(0, 0);
+  if (n_tiles > t_lo) load_kv(t_lo, t_lo & 1);
   cp_async_commit();
 
   // ---- per-warp state: 16 query rows
@@ -385,22 +396,25 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
-  uint32_t qf[KSTEPS][4];
+  uint32_t qf[kQRegs ? KSTEPS : 1][4];
   const int r_lo = warp * 16 + (lane >> 2);  // rows held by this thread: r_lo, r_lo + 8
   const int qpos_lo = ctx0 + q_off + r_lo, qpos_hi = qpos_lo + 8;
+  auto load_qf = [&](uint32_t* dst, int ks) {
+    const int mi = lane >> 3, rr = lane & 7;
+    const int row = warp * 16 + (mi & 1) * 8 + rr;
+    const int ch = ks * 2 + (mi >> 1);
+    ldmatrix_x4(dst, sQ + swz<D>(row, ch));
+  };
 
-  for (int t = 0; t < n_tiles; ++t) {
+  for (int t = t_lo; t < n_tiles; ++t) {
     if (t + 1 < n_tiles) load_kv(t + 1, (t + 1) & 1);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    if (t == 0) {
+    if constexpr (kQRegs) {
+      if (t == t_lo) {
 #pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        const int mi = lane >> 3, rr = lane & 7;
-        const int row = warp * 16 + (mi & 1) * 8 + rr;
-        const int ch = ks * 2 + (mi >> 1);
-        ldmatrix_x4(qf[ks], sQ + swz<D>(row, ch));
+        for (int ks = 0; ks < KSTEPS; ++ks) load_qf(qf[ks], ks);
       }
     }
     const __nv_bfloat16* cK = sK + (t & 1) * kPfBN * D;
@@ -413,6 +427,14 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
       for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KSTEPS; ++ks) {
+      const uint32_t* qk;
+      uint32_t qtmp[4];
+      if constexpr (kQRegs) {
+        qk = qf[ks];
+      } else {
+        load_qf(qtmp, ks);
+        qk = qtmp;
+      }
 #pragma unroll
       for (int jp = 0; jp < kPfBN / 16; ++jp) {
         uint32_t bfr[4];
@@ -420,21 +442,36 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
         const int key = jp * 16 + (mi >> 1) * 8 + rr;
         const int ch = ks * 2 + (mi & 1);
         ldmatrix_x4(bfr, cK + swz<D>(key, ch));
-        mma_bf16_16816(s[2 * jp], qf[ks], bfr);
-        mma_bf16_16816(s[2 * jp + 1], qf[ks], bfr + 2);
+        mma_bf16_16816(s[2 * jp], qk, bfr);
+        mma_bf16_16816(s[2 * jp + 1], qk, bfr + 2);
       }
     }
     // mask + online softmax (log2 domain)
     const int kbase = t * kPfBN;
     float mx[2] = {-INFINITY, -INFINITY};
+    if (softcap_log2 > 0.f) {  // uniform branch: soft-capped scores (Gemma-2)
+      const float inv_cap = 1.f / softcap_log2;
+#pragma unroll
+      for (int j = 0; j < kPfBN / 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[j][e] = softcap_log2 * tanh_approx(s[j][e] * scale_log2 * inv_cap);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPfBN / 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[j][e] *= scale_log2;
+    }
+    // visible keys per row: [lo, hi] (causal, sequence end, sliding window), relative to kbase
+    const int hi0 = min(qpos_lo, kv_end - 1) - kbase, hi1 = min(qpos_hi, kv_end - 1) - kbase;
+    const int lo0 = (window > 0 ? qpos_lo - window + 1 : 0) - kbase;
+    const int lo1 = (window > 0 ? qpos_hi - window + 1 : 0) - kbase;
 #pragma unroll
     for (int j = 0; j < kPfBN / 8; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int kp = kbase + j * 8 + 2 * (lane & 3) + (e & 1);
-        const int qp = (e < 2) ? qpos_lo : qpos_hi;
-        float v = s[j][e] * scale_log2;
-        v = (kp > qp || kp >= kv_end) ? -INFINITY : v;
+        const int kp = j * 8 + 2 * (lane & 3) + (e & 1);
+        const bool vis = (e < 2) ? (kp <= hi0 && kp >= lo0) : (kp <= hi1 && kp >= lo1);
+        const float v = vis ? s[j][e] : -INFINITY;
         s[j][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -532,7 +569,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ seq_lens, int Hk, int num_splits, float scale_log2, int64_t q_stride,
-    uint32_t* status) {
+    uint32_t* status, int window, float softcap_log2) {
   static_assert(G >= 1 && G <= 16, "GQA group must fit the 16 MMA rows");
   constexpr int D = 128, BS = 16;
   extern __shared__ uint8_t dsm_raw[];
@@ -548,8 +585,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
 
   const int L = seq_lens[b];
   const int nblocks = (L + BS - 1) / BS;
-  const int per = (nblocks + num_splits - 1) / num_splits;
-  const int blk_begin = split * per;
+  // sliding window: the query at position L-1 sees keys [L - window, L); earlier blocks are skipped
+  const int kv_lo = window > 0 ? max(0, L - window) : 0;
+  const int blk_lo = kv_lo / BS;
+  const int per = (nblocks - blk_lo + num_splits - 1) / num_splits;
+  const int blk_begin = blk_lo + split * per;
   const int blk_end = min(nblocks, blk_begin + per);
   const int nmine = blk_begin + warp < blk_end ? (blk_end - blk_begin - warp + kDecodeWarps - 1) / kDecodeWarps : 0;
   const int* bt = block_tables + (int64_t)b * bt_stride;
@@ -617,12 +657,24 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     }
     const int tok0 = (blk_begin + warp + kDecodeWarps * j) * BS;
     float mx[2] = {-INFINITY, -INFINITY};
+    if (softcap_log2 > 0.f) {  // uniform branch: soft-capped scores (Gemma-2)
+      const float inv_cap = 1.f / softcap_log2;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] = softcap_log2 * tanh_approx(sc[nt][e] * scale_log2 * inv_cap);
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] *= scale_log2;
+    }
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int t = tok0 + nt * 8 + cq + (e & 1);
-        const float v = t < L ? sc[nt][e] * scale_log2 : -INFINITY;
+        const float v = (t < L && t >= kv_lo) ? sc[nt][e] : -INFINITY;
         sc[nt][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -737,7 +789,7 @@ constexpr size_t decode_tc_smem_bytes() {
 template <int G>
 void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks, const int* bt,
                       int bt_stride, const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po,
-                      float* pml, cudaStream_t s) {
+                      float* pml, int window, float softcap_log2, cudaStream_t s) {
   const uint64_t rows = (uint64_t)num_blocks * 2 * Hk * 16;
   CUtensorMap tm = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, 128, 16, 64,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -747,7 +799,7 @@ void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* ca
   dim3 grid(B, Hk, num_splits);
   kern<<<grid, kDecodeWarps * 32, smem, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), po, pml,
                                               reinterpret_cast<const __nv_bfloat16*>(q), bt, bt_stride, lens, Hk,
-                                              num_splits, scale_log2, q_stride, nullptr);
+                                              num_splits, scale_log2, q_stride, nullptr, window, softcap_log2);
   check_launch("paged_decode_attention (tensor cores)");
   if (num_splits > 1) {
     decode_combine_kernel<128><<<B * Hk * G, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml,
@@ -759,7 +811,7 @@ void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* ca
 template <int D, int G>
 void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cache, const int* bt, int bt_stride,
                      const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po, float* pml,
-                     cudaStream_t s) {
+                     int window, float softcap_log2, cudaStream_t s) {
   dim3 grid(B, Hk, num_splits);
   constexpr size_t smem = decode_smem_bytes<D, G, 16>();
   auto kern = paged_decode_kernel<D, G, 16>;
@@ -767,7 +819,7 @@ void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cac
   kern<<<grid, kDecodeWarps * 32, smem, s>>>(
       reinterpret_cast<__nv_bfloat16*>(out), po, pml, reinterpret_cast<const __nv_bfloat16*>(q),
       reinterpret_cast<const __nv_bfloat16*>(cache), bt, bt_stride, lens, Hk, num_splits, scale_log2, q_stride,
-      nullptr);
+      nullptr, window, softcap_log2);
   check_launch("paged_decode_attention");
   if (num_splits > 1) {
     decode_combine_kernel<D><<<B * Hk * G, D, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml, num_splits);
@@ -782,17 +834,18 @@ namespace gollek {
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         cudaStream_t s) {
+                         int window, float softcap, cudaStream_t s) {
   throw_if(block_size != 16, "decode attention is built for block_size 16");
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(num_splits > 1 && (part_o == nullptr || part_ml == nullptr), "split-KV decode needs a workspace");
   if (B == 0) return;
   const int G = H / Hk;
   const float sl = scale * kLog2e;
+  const float cl = softcap > 0.f ? softcap * kLog2e : 0.f;
   if (D == 128 && num_blocks > 0) {
 #define GOLLEK_DECODE_TC(GG) \
   if (G == GG) return launch_decode_tc<GG>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, B, Hk, \
-                                           num_splits, sl, part_o, part_ml, s);
+                                           num_splits, sl, part_o, part_ml, window, cl, s);
     GOLLEK_DECODE_TC(1)
     GOLLEK_DECODE_TC(2)
     GOLLEK_DECODE_TC(4)
@@ -803,7 +856,7 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
 #define GOLLEK_DECODE_CASE(DD, GG)                                                                            \
   if (D == DD && G == GG)                                                                                     \
     return launch_decode_t<DD, GG>(out, q, q_stride, cache, block_tables, bt_stride, seq_lens, B, Hk, num_splits, \
-                                   sl, part_o, part_ml, s);
+                                   sl, part_o, part_ml, window, cl, s);
   GOLLEK_DECODE_CASE(128, 1)
   GOLLEK_DECODE_CASE(128, 2)
   GOLLEK_DECODE_CASE(128, 4)
@@ -815,6 +868,10 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
   GOLLEK_DECODE_CASE(32, 2)
   GOLLEK_DECODE_CASE(32, 4)
   GOLLEK_DECODE_CASE(32, 8)
+  GOLLEK_DECODE_CASE(256, 1)
+  GOLLEK_DECODE_CASE(256, 2)
+  GOLLEK_DECODE_CASE(256, 4)
+  GOLLEK_DECODE_CASE(256, 8)
 #undef GOLLEK_DECODE_CASE
   throw_if(true, "decode attention: unsupported head_dim/group " + std::to_string(D) + "/" + std::to_string(G));
 }
@@ -822,10 +879,11 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
-                          cudaStream_t s) {
+                          int window, float softcap, cudaStream_t s) {
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   if (ntiles == 0) return;
   const float sl = scale * kLog2e;
+  const float cl = softcap > 0.f ? softcap * kLog2e : 0.f;
   dim3 grid(ntiles, H);
 #define GOLLEK_PREFILL_CASE(DD)                                                                               \
   if (D == DD) {                                                                                            \
@@ -835,10 +893,12 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
     kern<<<grid, kPfThreads, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(out), out_stride,                  \
                                         reinterpret_cast<const __nv_bfloat16*>(q), q_stride,                \
                                         reinterpret_cast<const __nv_bfloat16*>(cache), block_tables,        \
-                                        bt_stride, seq_lens, query_start, tiles, H, Hk, block_size, sl);    \
+                                        bt_stride, seq_lens, query_start, tiles, H, Hk, block_size, sl,     \
+                                        window, cl);                                                        \
     check_launch("paged_prefill_attention");                                                                \
     return;                                                                                                 \
   }
+  GOLLEK_PREFILL_CASE(256)
   GOLLEK_PREFILL_CASE(128)
   GOLLEK_PREFILL_CASE(64)
   GOLLEK_PREFILL_CASE(32)

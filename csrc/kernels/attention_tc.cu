@@ -84,7 +84,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
-                      const int* __restrict__ tiles, int H, int Hk, float scale_log2, uint32_t* status) {
+                      const int* __restrict__ tiles, int H, int Hk, float scale_log2, uint32_t* status, int window,
+                      float softcap_log2) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
@@ -110,7 +111,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ctx0 = L - qlen;
   const int rows = min(kTQ, qlen - q_off);
   const int kv_end = min(L, ctx0 + q_off + rows);
-  const int nt = (kv_end + kTK - 1) / kTK;
+  // KV tiles [j0, j0 + nt): with a sliding window the first query row sees keys >= its position - window + 1
+  const int j0 = window > 0 ? max(0, ctx0 + q_off - window + 1) / kTK : 0;
+  const int nt = (kv_end + kTK - 1) / kTK - j0;
   const int* bt = block_tables + (int64_t)b * bt_stride;
 
   if (threadIdx.x == 0) {
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* dk = sKV + st * 2 * kKVTile;
         uint8_t* dv = dk + kKVTile;
         for (int blk = 0; blk < kTK / kBS; ++blk) {
-          const int kb = (j * kTK) / kBS + blk;
+          const int kb = ((j0 + j) * kTK) / kBS + blk;
           const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
           const int rk = ((pb * 2 + 0) * Hk + kh) * kBS, rv = ((pb * 2 + 1) * Hk + kh) * kBS;
           tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &kv_full[st]);
@@ -257,11 +260,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[st]);
       float mx = -INFINITY;
-      const int k0 = j * kTK;
+      const int k0 = (j0 + j) * kTK;
+      if (softcap_log2 > 0.f) {  // uniform branch: soft-capped scores (Gemma-2)
+        const float inv_cap = 1.f / softcap_log2;
+#pragma unroll
+        for (int c = 0; c < kTK; ++c) s[c] = softcap_log2 * tanh_approx(s[c] * scale_log2 * inv_cap);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kTK; ++c) s[c] *= scale_log2;
+      }
+      // visible keys of this row: [klo, khi] (causal, sequence end, sliding window)
+      const int khi = min(qpos, kv_end - 1) - k0;
+      const int klo = (window > 0 ? qpos - window + 1 : 0) - k0;
 #pragma unroll
       for (int c = 0; c < kTK; ++c) {
-        const int kp = k0 + c;
-        const float v = (kp > qpos || kp >= kv_end) ? -INFINITY : s[c] * scale_log2;
+        const float v = (c > khi || c < klo) ? -INFINITY : s[c];
         s[c] = v;
         mx = fmaxf(mx, v);
       }
@@ -345,7 +358,7 @@ namespace gollek {
 void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
-                             int Hk, float scale, cudaStream_t s) {
+                             int Hk, float scale, int window, float softcap, cudaStream_t s) {
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(q_stride % 8 != 0, "prefill: q row pitch must keep 16-byte alignment");
   if (ntiles == 0) return;
@@ -358,7 +371,8 @@ void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64
   dim3 grid(ntiles, H);
   prefill_tc_kernel<<<grid, kThreads, kSmem, s>>>(tq, tkv, reinterpret_cast<__nv_bfloat16*>(out), out_stride,
                                                   block_tables, bt_stride, seq_lens, query_start, tiles, H, Hk,
-                                                  scale * 1.4426950408889634f, nullptr);
+                                                  scale * 1.4426950408889634f, nullptr, window,
+                                                  softcap > 0.f ? softcap * 1.4426950408889634f : 0.f);
   check_launch("paged_prefill_attention (tcgen05)");
 }
 

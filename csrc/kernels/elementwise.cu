@@ -75,48 +75,111 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* _
 // ---------------------------------------------------------------------------------------------
 // K2: RoPE + paged KV write. One CTA per token.
 // ---------------------------------------------------------------------------------------------
+// One CTA per token, one warp per head (q heads, then k heads): optional projection bias, optional
+// per-head RMSNorm (Qwen3 / Gemma-3 QK-norm: x * rsqrt(mean(x^2) + eps) * w over head_dim), then
+// NeoX rotation of the first `rot` dims (rot < D: partial rotary, or a head zero-padded to a
+// supported size); dims [rot, D) pass through. Lane l owns rotation pairs (j, j+1) and
+// (j+half, j+half+1) for j = 2l + 64i, half = rot / 2. V rows (+ bias) are copied into the cache.
+// The cos/sin table rows hold rot values (cos of the rot/2 pairs, then sin).
 __global__ void __launch_bounds__(128) rope_kv_write_kernel(
     __nv_bfloat16* __restrict__ q_out, const __nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
     const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ cache, const int* __restrict__ slots, int H,
-    int Hk, int D, int block_size, int64_t qkv_stride, int max_pos) {
+    int Hk, int D, int block_size, int64_t qkv_stride, int max_pos, const __nv_bfloat16* __restrict__ bias,
+    const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float norm_eps,
+    int rot) {
   const int t = blockIdx.x;
-  const int half = D >> 1;
+  const int half = rot >> 1;
   int pos = positions[t];
   pos = pos < 0 ? 0 : (pos >= max_pos ? max_pos - 1 : pos);
-  const float* cs = cos_sin + (int64_t)pos * D;
+  const float* cs = cos_sin + (int64_t)pos * rot;
   const __nv_bfloat16* row = qkv + (int64_t)t * qkv_stride;
   const int slot = slots ? slots[t] : -1;
   const int64_t blk = slot >= 0 ? slot / block_size : 0;
   const int off = slot >= 0 ? slot % block_size : 0;
-  // rotate q and k heads: each thread handles two adjacent rotation pairs
-  const int npairs2 = (H + Hk) * half / 2;
-  for (int i = threadIdx.x; i < npairs2; i += blockDim.x) {
-    const int p = 2 * i;
-    const int h = p / half, j = p % half;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kMaxI = 2;  // head_dim <= 256: at most two 64-wide pair groups per lane
+  for (int h = warp; h < H + Hk; h += 4) {
+    if (h >= H && slot < 0) break;
     const __nv_bfloat16* src = row + h * D;
-    float2 x1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
-    float2 x2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j + half));
-    float c0 = cs[j], c1 = cs[j + 1], s0 = cs[half + j], s1 = cs[half + j + 1];
-    __nv_bfloat162 y1 = __floats2bfloat162_rn(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
-    __nv_bfloat162 y2 = __floats2bfloat162_rn(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
-    if (h < H) {
-      __nv_bfloat16* dst = q_out + ((int64_t)t * H + h) * D;
-      *reinterpret_cast<__nv_bfloat162*>(dst + j) = y1;
-      *reinterpret_cast<__nv_bfloat162*>(dst + j + half) = y2;
-    } else if (slot >= 0) {
-      const int kh = h - H;
-      __nv_bfloat16* dst = cache + (((blk * 2 + 0) * Hk + kh) * block_size + off) * (int64_t)D;
-      *reinterpret_cast<__nv_bfloat162*>(dst + j) = y1;
-      *reinterpret_cast<__nv_bfloat162*>(dst + j + half) = y2;
+    float2 x1[kMaxI], x2[kMaxI];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxI; ++i) {
+      const int j = 2 * lane + 64 * i;
+      if (j < half) {
+        x1[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
+        x2[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j + half));
+        if (bias) {
+          const float2 b1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + h * D + j));
+          const float2 b2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + h * D + j + half));
+          x1[i].x += b1.x; x1[i].y += b1.y; x2[i].x += b2.x; x2[i].y += b2.y;
+        }
+        ss += x1[i].x * x1[i].x + x1[i].y * x1[i].y + x2[i].x * x2[i].x + x2[i].y * x2[i].y;
+      }
+    }
+    // pass-through dims [rot, D): at most 2 pairs per lane (D - rot <= 128)
+    float2 xp[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int e = rot + 2 * lane + 64 * i;
+      if (e < D) {
+        xp[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + e));
+        if (bias) {
+          const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(bias + h * D + e));
+          xp[i].x += b.x; xp[i].y += b.y;
+        }
+        ss += xp[i].x * xp[i].x + xp[i].y * xp[i].y;
+      }
+    }
+    const __nv_bfloat16* nw = h < H ? q_norm : k_norm;
+    float rs = 1.f;
+    if (nw) rs = rsqrtf(warp_sum(ss) / (float)D + norm_eps);
+    __nv_bfloat16* dst = h < H ? q_out + ((int64_t)t * H + h) * D
+                               : cache + (((blk * 2 + 0) * Hk + (h - H)) * block_size + off) * (int64_t)D;
+#pragma unroll
+    for (int i = 0; i < kMaxI; ++i) {
+      const int j = 2 * lane + 64 * i;
+      if (j < half) {
+        if (nw) {
+          const float2 w1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(nw + j));
+          const float2 w2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(nw + j + half));
+          x1[i].x *= rs * w1.x; x1[i].y *= rs * w1.y; x2[i].x *= rs * w2.x; x2[i].y *= rs * w2.y;
+        }
+        const float c0 = cs[j], c1 = cs[j + 1], s0 = cs[half + j], s1 = cs[half + j + 1];
+        *reinterpret_cast<__nv_bfloat162*>(dst + j) =
+            __floats2bfloat162_rn(x1[i].x * c0 - x2[i].x * s0, x1[i].y * c1 - x2[i].y * s1);
+        *reinterpret_cast<__nv_bfloat162*>(dst + j + half) =
+            __floats2bfloat162_rn(x2[i].x * c0 + x1[i].x * s0, x2[i].y * c1 + x1[i].y * s1);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int e = rot + 2 * lane + 64 * i;
+      if (e < D) {
+        if (nw) {
+          const float2 w = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(nw + e));
+          xp[i].x *= rs * w.x; xp[i].y *= rs * w.y;
+        }
+        *reinterpret_cast<__nv_bfloat162*>(dst + e) = __floats2bfloat162_rn(xp[i].x, xp[i].y);
+      }
     }
   }
   if (slot >= 0) {
     const int nv = Hk * D / 8;
-    const uint4* vsrc = reinterpret_cast<const uint4*>(row + (H + Hk) * D);
+    const __nv_bfloat16* vrow = row + (H + Hk) * D;
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       const int kh = (i * 8) / D, dd = (i * 8) % D;
       __nv_bfloat16* dst = cache + (((blk * 2 + 1) * Hk + kh) * block_size + off) * (int64_t)D + dd;
-      *reinterpret_cast<uint4*>(dst) = vsrc[i];
+      uint4 v = *reinterpret_cast<const uint4*>(vrow + i * 8);
+      if (bias) {
+        float f[8], b[8];
+        bf16x8_to_float(v, f);
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(bias + (H + Hk) * D + i * 8), b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] += b[e];
+        v = float_to_bf16x8(f);
+      }
+      *reinterpret_cast<uint4*>(dst) = v;
     }
   }
 }
@@ -124,14 +187,25 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(
 // ---------------------------------------------------------------------------------------------
 // K13: embedding gather (vectorised 16-byte copies).
 // ---------------------------------------------------------------------------------------------
+// scale != 1 multiplies the gathered row (Gemma's sqrt(hidden) embedding normaliser)
 __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int* __restrict__ ids,
-                                 const __nv_bfloat16* __restrict__ table, int d, int vocab) {
+                                 const __nv_bfloat16* __restrict__ table, int d, int vocab, float scale) {
   const int t = blockIdx.x;
   int id = ids[t];
   id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
   const uint4* src = reinterpret_cast<const uint4*>(table + (int64_t)id * d);
   uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)t * d);
-  for (int i = threadIdx.x; i < d / 8; i += blockDim.x) dst[i] = src[i];
+  for (int i = threadIdx.x; i < d / 8; i += blockDim.x) {
+    if (scale == 1.f) {
+      dst[i] = src[i];
+    } else {
+      float f[8];
+      bf16x8_to_float(src[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= scale;
+      dst[i] = float_to_bf16x8(f);
+    }
+  }
 }
 
 __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x, int d) {
@@ -177,21 +251,27 @@ void launch_rms_norm(void* out, const void* x, void* residual, const void* w, in
 
 void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
                           const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
-                          int max_pos, cudaStream_t s) {
-  throw_if(D % 16 != 0, "rope_kv_write: head_dim must be a multiple of 16");
+                          int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,
+                          int rot, cudaStream_t s) {
+  throw_if(D % 16 != 0 || D > 256, "rope_kv_write: head_dim must be a multiple of 16, <= 256");
+  throw_if(rot % 4 != 0 || rot > D || D - rot > 128, "rope_kv_write: rotary dims must be a multiple of 4, "
+                                                     "<= head_dim, with at most 128 pass-through dims");
   if (T == 0) return;
   rope_kv_write_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(q_out),
                                          reinterpret_cast<const __nv_bfloat16*>(qkv), positions, cos_sin,
                                          reinterpret_cast<__nv_bfloat16*>(cache), slots, H, Hk, D, block_size,
-                                         qkv_stride, max_pos);
+                                         qkv_stride, max_pos, reinterpret_cast<const __nv_bfloat16*>(bias),
+                                         reinterpret_cast<const __nv_bfloat16*>(q_norm),
+                                         reinterpret_cast<const __nv_bfloat16*>(k_norm), norm_eps, rot);
   check_launch("rope_kv_write");
 }
 
-void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s) {
+void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, float scale,
+                      cudaStream_t s) {
   throw_if(d % 8 != 0, "embedding: dim must be a multiple of 8");
   if (T == 0) return;
   embedding_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ids,
-                                     reinterpret_cast<const __nv_bfloat16*>(table), d, vocab);
+                                     reinterpret_cast<const __nv_bfloat16*>(table), d, vocab, scale);
   check_launch("embedding");
 }
 

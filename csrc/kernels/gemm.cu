@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(192, 1)
                     make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
           }
         }
-      } else if constexpr (EPI == kEpiSwiglu) {
+      } else if constexpr (EPI == kEpiSwiglu || EPI == kEpiGeglu) {
         const int out_n = N / 2;
 #pragma unroll 1
         for (int p = 0; p < BN / 128; ++p) {
@@ -274,8 +274,10 @@ __global__ void __launch_bounds__(192, 1)
                 if (col + 8 * j + 8 <= out_n) {
                   float v[8];
 #pragma unroll
-                  for (int e = 0; e < 8; ++e)
-                    v[e] = silu(__uint_as_float(g[8 * j + e])) * __uint_as_float(u[8 * j + e]);
+                  for (int e = 0; e < 8; ++e) {
+                    const float gv = __uint_as_float(g[8 * j + e]);
+                    v[e] = (EPI == kEpiSwiglu ? silu(gv) : gelu_tanh(gv)) * __uint_as_float(u[8 * j + e]);
+                  }
                   *reinterpret_cast<uint4*>(dst + 8 * j) = float_to_bf16x8(v);
                 }
               }
@@ -326,13 +328,13 @@ __global__ void __launch_bounds__(192, 1)
 template <int EPI>
 __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ C, int64_t ldc, const float* __restrict__ partial,
                                      const __nv_bfloat16* __restrict__ R, int64_t ldr, int M, int N, int splits) {
-  const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
+  const int out_n = (EPI == kEpiSwiglu || EPI == kEpiGeglu) ? N / 2 : N;
   const int groups = out_n / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)M * groups) return;
   const int row = idx / groups, col = (idx % groups) * 8;
   float v[8];
-  if constexpr (EPI == kEpiSwiglu) {
+  if constexpr (EPI == kEpiSwiglu || EPI == kEpiGeglu) {
     const int gc = (col / 64) * 128 + col % 64;  // gate column of the interleaved weight rows
     float g[8] = {0}, u[8] = {0};
     for (int s = 0; s < splits; ++s) {
@@ -343,7 +345,7 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ C, int64_t ldc,
       u[0] += u0.x; u[1] += u0.y; u[2] += u0.z; u[3] += u0.w; u[4] += u1.x; u[5] += u1.y; u[6] += u1.z; u[7] += u1.w;
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = silu(g[e]) * u[e];
+    for (int e = 0; e < 8; ++e) v[e] = (EPI == kEpiSwiglu ? silu(g[e]) : gelu_tanh(g[e])) * u[e];
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = 0.f;
@@ -386,7 +388,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
                                      partial, status, tile_group, num_m_dev);
   check_launch("gemm_bf16");
   if (splits > 1 && reduce) {
-    const int out_n = EPI == kEpiSwiglu ? N / 2 : N;
+    const int out_n = (EPI == kEpiSwiglu || EPI == kEpiGeglu) ? N / 2 : N;
     const int64_t threads = (int64_t)M * (out_n / 8);
     splitk_reduce_kernel<EPI><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<__nv_bfloat16*>(out), ldc, partial, reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N,
@@ -403,13 +405,15 @@ int device_num_sms() { return num_sms(); }
 
 void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* residual, int64_t ldr, int M, int N,
                    int splits, int epi, cudaStream_t s) {
-  const int out_n = epi == kEpiSwiglu ? N / 2 : N;
+  const int out_n = epi_gated(epi) ? N / 2 : N;
   const int64_t threads = (int64_t)M * (out_n / 8);
   const unsigned grid = (unsigned)((threads + 255) / 256);
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   auto* r = reinterpret_cast<const __nv_bfloat16*>(residual);
   if (epi == kEpiSwiglu)
     splitk_reduce_kernel<kEpiSwiglu><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
+  else if (epi == kEpiGeglu)
+    splitk_reduce_kernel<kEpiGeglu><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
   else if (epi == kEpiResidual)
     splitk_reduce_kernel<kEpiResidual><<<grid, 256, 0, s>>>(o, ldc, partial, r, ldr, M, N, splits);
   else
@@ -431,7 +435,7 @@ int gemm_pick_bn(int M, int N, int epi) {
     };
     return cost(128, 0.57) < cost(256, 1.0) ? 128 : 256;
   }
-  if (epi == kEpiSwiglu) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
+  if (epi_gated(epi)) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
   if (num_m * ((N + 255) / 256) >= sms) return 256;
   if (num_m * ((N + 127) / 128) >= sms / 2) return 128;
   return 64;
@@ -451,7 +455,7 @@ void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits) {
   (void)num_m;
   splits = 1;
   if (bn == 0) bn = gemm_pick_bn(M, N, epi);
-  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  if (epi_gated(epi) && bn < 128) bn = 128;
 }
 
 int gemm_splits(int M, int N, int K, int epi) {
@@ -466,7 +470,7 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
   throw_if(K % 8 != 0, "gemm: K must be a multiple of 8");
   throw_if(ldc % 8 != 0, "gemm: output row pitch must keep 16-byte alignment");
   if (M == 0) return;
-  if (epi == kEpiSwiglu) throw_if(N % 128 != 0, "gemm swiglu: N must be a multiple of 128");
+  if (epi_gated(epi)) throw_if(N % 128 != 0, "gemm swiglu/geglu: N must be a multiple of 128");
   else throw_if(N % 8 != 0, "gemm: N must be a multiple of 8");
   if (epi == kEpiResidual) throw_if(residual == nullptr || ldr % 8 != 0, "gemm residual: bf16 residual required");
   if (bn == 0) {
@@ -475,7 +479,7 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
     if (splits <= 0) splits = sp;
   }
   if (splits <= 0) splits = 1;
-  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  if (epi_gated(epi) && bn < 128) bn = 128;
   throw_if(splits > 1 && partial == nullptr, "gemm: split-K needs an fp32 workspace");
 #define GOLLEK_GEMM_CASE(BNV, EPIV) \
   if (bn == BNV && epi == EPIV)     \
@@ -489,6 +493,8 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
   GOLLEK_GEMM_CASE(64, kEpiResidual)
   GOLLEK_GEMM_CASE(256, kEpiSwiglu)
   GOLLEK_GEMM_CASE(128, kEpiSwiglu)
+  GOLLEK_GEMM_CASE(256, kEpiGeglu)
+  GOLLEK_GEMM_CASE(128, kEpiGeglu)
 #undef GOLLEK_GEMM_CASE
   throw_if(true, "gemm: unsupported tile width " + std::to_string(bn) + " / epilogue " + std::to_string(epi));
 }
@@ -509,7 +515,7 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
     const int m_tiles = std::max(groups, std::min(M_cap / 128, groups * 2));
     bn = (m_tiles * ((N + 255) / 256) >= num_sms() || epi == kEpiSwiglu) ? 256 : 128;
   }
-  if (epi == kEpiSwiglu && bn < 128) bn = 128;
+  if (epi_gated(epi) && bn < 128) bn = 128;
   if (splits < 1) splits = 1;
   // split-K partials [splits, M_cap, N] are left for the caller to reduce (no reduce pass here)
   throw_if(splits > 1 && (partial == nullptr || epi != kEpiNone), "grouped gemm: split-K needs fp32 partials, no epilogue");

@@ -25,27 +25,34 @@ void launch_rms_norm(void* out, const void* x, void* residual, const void* w, in
                      int64_t out_stride, float eps, cudaStream_t s);
 void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
                           const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
-                          int max_pos, cudaStream_t s);
-void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s);
+                          int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,
+                          int rot, cudaStream_t s);
+void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, float scale,
+                      cudaStream_t s);
 void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
 
 // ---- attention (K3, K4)
 // num_blocks > 0 enables the tensor-core path for head_dim 128 (needs the cache extent for its TMA map).
+// Attention options: window > 0 restricts each query to the `window` most recent keys (sliding
+// window, HF semantics kv > q - window); softcap > 0 applies softcap * tanh(score / softcap) to the
+// scaled scores before the softmax (Gemma-2). 0 disables either.
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         cudaStream_t s);
+                         int window, float softcap, cudaStream_t s);
 void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
-                             int Hk, float scale, cudaStream_t s);
+                             int Hk, float scale, int window, float softcap, cudaStream_t s);
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
-                          cudaStream_t s);
+                          int window, float softcap, cudaStream_t s);
 
 // ---- GEMM (K5, K8)
-enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2 };
+// Gated epilogues (SwiGLU, GeGLU) read gate/up rows interleaved in groups of 64 and write N/2 columns.
+enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3 };
+inline bool epi_gated(int epi) { return epi == kEpiSwiglu || epi == kEpiGeglu; }
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
 int gemm_splits(int M, int N, int K, int epi);

@@ -87,7 +87,8 @@ extern "C" __attribute__((visibility("default"))) int gollek_paged_decode_attent
   try {
     gollek::launch_paged_decode(out, q, q_stride, cache, head_dim == 128 ? num_blocks : 0, block_tables, bt_stride,
                                 seq_lens, B, H, Hk, head_dim, block_size, num_splits, scale,
-                                num_splits > 1 ? part_o : nullptr, num_splits > 1 ? part_ml : nullptr, stream);
+                                num_splits > 1 ? part_o : nullptr, num_splits > 1 ? part_ml : nullptr,
+                                /*window=*/0, /*softcap=*/0.f, stream);
   } catch (const std::runtime_error& e) {
     // argument checks say "unsupported" / "must"; launch failures carry the CUDA error string
     const std::string msg = e.what();

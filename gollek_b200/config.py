@@ -25,12 +25,15 @@ from typing import Any, Optional
 
 @dataclass
 class RopeScaling:
-    """RoPE frequency scaling (HF ``rope_scaling``): ``none``, ``linear`` or ``llama3``."""
+    """RoPE frequency scaling (HF ``rope_scaling``): ``none``, ``linear``, ``llama3`` or
+    ``longrope`` (Phi-3 long-context: per-pair short/long factors)."""
     kind: str = "none"
     factor: float = 1.0
     low_freq_factor: float = 1.0
     high_freq_factor: float = 4.0
     original_max_position_embeddings: int = 8192
+    short_factor: Optional[list] = None
+    long_factor: Optional[list] = None
 
     @staticmethod
     def from_hf(d: Optional[dict]) -> "RopeScaling":
@@ -39,19 +42,29 @@ class RopeScaling:
         kind = d.get("rope_type", d.get("type", "none")) or "none"
         if kind == "default":
             kind = "none"
+        if kind == "su":
+            kind = "longrope"
         return RopeScaling(
             kind=kind,
-            factor=float(d.get("factor", 1.0)),
+            factor=float(d.get("factor", 1.0) or 1.0),
             low_freq_factor=float(d.get("low_freq_factor", 1.0)),
             high_freq_factor=float(d.get("high_freq_factor", 4.0)),
-            original_max_position_embeddings=int(d.get("original_max_position_embeddings", 8192)),
+            original_max_position_embeddings=int(d.get("original_max_position_embeddings", 8192) or 8192),
+            short_factor=d.get("short_factor"),
+            long_factor=d.get("long_factor"),
         )
+
+
+# Model families handled by the decoder graph (models/llama.py). Llama-like families differ in
+# projection biases, QK-norm, sliding windows, norm placement and activation; Gemma adds a
+# sqrt(hidden) embedding scale, (1 + w) RMSNorm weights, GeGLU, sandwich norms and softcapping.
+FAMILIES = ("llama", "mistral", "mixtral", "qwen2", "qwen3", "gemma", "gemma2", "gemma3", "phi3")
 
 
 @dataclass
 class ModelConfig:
-    """Architecture hyper-parameters of a decoder-only transformer (Llama / Mixtral family)."""
-    architecture: str = "llama"          # "llama" | "mixtral"
+    """Architecture hyper-parameters of a decoder-only transformer (the families in ``FAMILIES``)."""
+    architecture: str = "llama"          # one of FAMILIES
     vocab_size: int = 32000
     hidden_size: int = 4096
     intermediate_size: int = 14336
@@ -68,13 +81,42 @@ class ModelConfig:
     num_local_experts: int = 0
     num_experts_per_tok: int = 0
     # extras some families use
-    attention_bias: bool = False
+    attention_bias: bool = False         # q/k/v projection biases (Qwen2)
+    qk_norm: bool = False                # per-head RMSNorm of q and k before RoPE (Qwen3, Gemma-3)
+    sliding_window: int = 0              # 0 = full attention
+    layer_types: Optional[list] = None   # per layer "full_attention" | "sliding_attention" (None: all
+                                         # layers sliding when sliding_window > 0)
+    rope_local_theta: float = 0.0        # RoPE base of sliding layers when it differs (Gemma-3)
+    attn_logit_softcapping: float = 0.0  # Gemma-2
+    final_logit_softcapping: float = 0.0
+    query_pre_attn_scalar: float = 0.0   # attention scale = this ** -0.5 (Gemma); 0 = head_dim
+    hidden_act: str = "silu"             # "silu" (SwiGLU) | "gelu_tanh" (GeGLU)
+    norm_unit_offset: bool = False       # RMSNorm scales by (1 + w) (Gemma)
+    embed_scale: float = 1.0             # embeddings multiplied by this (Gemma: sqrt(hidden))
+    sandwich_norm: bool = False          # norms after attention / MLP outputs too (Gemma-2/3)
     bos_token_id: int = 1
     eos_token_id: int = 2
 
     @property
     def is_moe(self) -> bool:
         return self.num_local_experts > 0
+
+    @property
+    def attn_scale(self) -> float:
+        return (self.query_pre_attn_scalar or self.head_dim) ** -0.5
+
+    def layer_window(self, i: int) -> int:
+        """Sliding window of layer ``i`` (0 = full attention)."""
+        if self.sliding_window <= 0:
+            return 0
+        if self.layer_types is None:
+            return self.sliding_window
+        return self.sliding_window if self.layer_types[i] == "sliding_attention" else 0
+
+    def layer_rope_theta(self, i: int) -> float:
+        if self.rope_local_theta and self.layer_window(i) > 0:
+            return self.rope_local_theta
+        return self.rope_theta
 
     @property
     def q_size(self) -> int:
@@ -103,40 +145,96 @@ class ModelConfig:
 
     @staticmethod
     def from_hf(d: dict) -> "ModelConfig":
-        """Parse a Hugging Face ``config.json`` dictionary."""
+        """Parse a Hugging Face ``config.json`` dictionary (transformers 4.x or 5.x layout)."""
+        if "text_config" in d and isinstance(d["text_config"], dict):  # multimodal wrappers (Gemma-3)
+            d = {**d["text_config"], "architectures": d.get("architectures")}
+            d.setdefault("model_type", "gemma3_text")
         archs = d.get("architectures") or []
-        model_type = d.get("model_type", "llama")
-        arch = "mixtral" if (model_type == "mixtral" or any("Mixtral" in a for a in archs)) else "llama"
+        mt = str(d.get("model_type", "llama"))
+        fam = {"llama": "llama", "mistral": "mistral", "mixtral": "mixtral", "qwen2": "qwen2", "qwen3": "qwen3",
+               "gemma": "gemma", "gemma2": "gemma2", "gemma3_text": "gemma3", "gemma3": "gemma3",
+               "phi3": "phi3"}.get(mt)
+        if fam is None:
+            fam = "mixtral" if any("Mixtral" in a for a in archs) else "llama"
+        gemma = fam.startswith("gemma")
         nh = int(d.get("num_attention_heads", 32))
         hs = int(d.get("hidden_size", 4096))
+        nl = int(d.get("num_hidden_layers", 32))
         eos = d.get("eos_token_id", 2)
         if isinstance(eos, list):
             eos = eos[0]
+        # RoPE: transformers 5 nests it in rope_parameters (per layer type for Gemma-3)
+        rp = d.get("rope_parameters") or {}
+        full_rp = rp.get("full_attention", rp) if isinstance(rp, dict) else {}
+        local_rp = rp.get("sliding_attention", {}) if isinstance(rp, dict) else {}
+        theta = d.get("rope_theta") or full_rp.get("rope_theta") or (1_000_000.0 if fam == "gemma3" else 10000.0)
+        scaling = d.get("rope_scaling")
+        if scaling is None and full_rp.get("rope_type") not in (None, "default"):
+            scaling = full_rp
+        if scaling and "original_max_position_embeddings" not in scaling and d.get("original_max_position_embeddings"):
+            scaling = {**scaling, "original_max_position_embeddings": d["original_max_position_embeddings"]}
+        local_theta = d.get("rope_local_base_freq") or local_rp.get("rope_theta") or (10000.0 if fam == "gemma3" else 0.0)
+        # sliding windows
+        sw = int(d.get("sliding_window") or 0)
+        layer_types = d.get("layer_types")
+        if fam in ("qwen2", "qwen3"):
+            if not d.get("use_sliding_window", False):
+                sw, layer_types = 0, None
+            elif layer_types is None:
+                mwl = int(d.get("max_window_layers", 0) or 0)
+                layer_types = ["sliding_attention" if i >= mwl else "full_attention" for i in range(nl)]
+        elif fam == "gemma2" and layer_types is None and sw:
+            layer_types = ["sliding_attention" if (i + 1) % 2 else "full_attention" for i in range(nl)]
+        elif fam == "gemma3" and layer_types is None and sw:
+            pat = int(d.get("sliding_window_pattern", 6) or 6)
+            layer_types = ["sliding_attention" if (i + 1) % pat else "full_attention" for i in range(nl)]
+        elif fam == "gemma":
+            sw, layer_types = 0, None
+        act = str(d.get("hidden_activation") or d.get("hidden_act") or "silu")
+        act = "gelu_tanh" if (gemma or act.startswith("gelu")) else "silu"
         return ModelConfig(
-            architecture=arch,
+            architecture=fam,
             vocab_size=int(d.get("vocab_size", 32000)),
             hidden_size=hs,
             intermediate_size=int(d.get("intermediate_size", 4 * hs)),
-            num_hidden_layers=int(d.get("num_hidden_layers", 32)),
+            num_hidden_layers=nl,
             num_attention_heads=nh,
-            num_key_value_heads=int(d.get("num_key_value_heads", nh)),
+            num_key_value_heads=int(d.get("num_key_value_heads", nh) or nh),
             head_dim=int(d.get("head_dim") or hs // nh),
-            rms_norm_eps=float(d.get("rms_norm_eps", 1e-5)),
-            rope_theta=float(d.get("rope_theta", (d.get("rope_parameters") or {}).get("rope_theta", 10000.0))),
-            rope_scaling=RopeScaling.from_hf(d.get("rope_scaling")),
+            rms_norm_eps=float(d.get("rms_norm_eps", 1e-6 if gemma else 1e-5)),
+            rope_theta=float(theta),
+            rope_scaling=RopeScaling.from_hf(scaling),
             max_position_embeddings=int(d.get("max_position_embeddings", 8192)),
-            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", gemma)),
             num_local_experts=int(d.get("num_local_experts", 0) or 0),
             num_experts_per_tok=int(d.get("num_experts_per_tok", 0) or 0),
-            attention_bias=bool(d.get("attention_bias", False)),
+            attention_bias=True if fam == "qwen2" else bool(d.get("attention_bias", False)),
+            qk_norm=fam in ("qwen3", "gemma3"),
+            sliding_window=sw,
+            layer_types=list(layer_types) if layer_types else None,
+            rope_local_theta=float(local_theta) if fam == "gemma3" else 0.0,
+            attn_logit_softcapping=float(d.get("attn_logit_softcapping") or 0.0),
+            final_logit_softcapping=float(d.get("final_logit_softcapping") or 0.0),
+            query_pre_attn_scalar=float(d.get("query_pre_attn_scalar") or 0.0) if gemma else 0.0,
+            hidden_act=act,
+            norm_unit_offset=gemma,
+            embed_scale=float(hs) ** 0.5 if gemma else 1.0,
+            sandwich_norm=fam in ("gemma2", "gemma3"),
             bos_token_id=int(d.get("bos_token_id", 1) or 1),
             eos_token_id=int(eos if eos is not None else 2),
         )
 
     def to_hf(self) -> dict:
+        fam = self.architecture
+        names = {"llama": ("LlamaForCausalLM", "llama"), "mistral": ("MistralForCausalLM", "mistral"),
+                 "mixtral": ("MixtralForCausalLM", "mixtral"), "qwen2": ("Qwen2ForCausalLM", "qwen2"),
+                 "qwen3": ("Qwen3ForCausalLM", "qwen3"), "gemma": ("GemmaForCausalLM", "gemma"),
+                 "gemma2": ("Gemma2ForCausalLM", "gemma2"), "gemma3": ("Gemma3ForCausalLM", "gemma3_text"),
+                 "phi3": ("Phi3ForCausalLM", "phi3")}
+        arch, mt = names.get(fam, names["mixtral" if self.is_moe else "llama"])
         d = {
-            "architectures": ["MixtralForCausalLM" if self.is_moe else "LlamaForCausalLM"],
-            "model_type": "mixtral" if self.is_moe else "llama",
+            "architectures": [arch],
+            "model_type": mt,
             "vocab_size": self.vocab_size,
             "hidden_size": self.hidden_size,
             "intermediate_size": self.intermediate_size,
@@ -151,15 +249,40 @@ class ModelConfig:
             "attention_bias": self.attention_bias,
             "bos_token_id": self.bos_token_id,
             "eos_token_id": self.eos_token_id,
-            "hidden_act": "silu",
+            "hidden_act": "gelu_pytorch_tanh" if self.hidden_act == "gelu_tanh" else "silu",
             "torch_dtype": "bfloat16",
         }
+        if fam.startswith("gemma"):
+            d["hidden_activation"] = d["hidden_act"]
+        if fam == "phi3":  # its default pad id (32000) lies outside small vocabularies
+            d["pad_token_id"] = min(32000, self.vocab_size - 1)
+        if self.sliding_window:
+            d["sliding_window"] = self.sliding_window
+            if fam in ("qwen2", "qwen3"):
+                d["use_sliding_window"] = True
+                d["max_window_layers"] = 0
+        elif fam in ("mistral", "phi3", "gemma2", "gemma3"):
+            d["sliding_window"] = None
+        if self.layer_types:
+            d["layer_types"] = list(self.layer_types)
+        if self.query_pre_attn_scalar:
+            q = self.query_pre_attn_scalar
+            d["query_pre_attn_scalar"] = int(q) if float(q).is_integer() else q
+        if fam in ("gemma2", "gemma3"):
+            d["attn_logit_softcapping"] = self.attn_logit_softcapping or None
+            d["final_logit_softcapping"] = self.final_logit_softcapping or None
+        if fam == "gemma3":
+            d["rope_local_base_freq"] = self.rope_local_theta or 10000.0
         if self.rope_scaling.kind != "none":
             rs = self.rope_scaling
             d["rope_scaling"] = {"rope_type": rs.kind, "factor": rs.factor,
                                  "low_freq_factor": rs.low_freq_factor,
                                  "high_freq_factor": rs.high_freq_factor,
                                  "original_max_position_embeddings": rs.original_max_position_embeddings}
+            if rs.kind == "longrope":
+                d["rope_scaling"] = {"type": "longrope", "short_factor": rs.short_factor,
+                                     "long_factor": rs.long_factor}
+                d["original_max_position_embeddings"] = rs.original_max_position_embeddings
         if self.is_moe:
             d["num_local_experts"] = self.num_local_experts
             d["num_experts_per_tok"] = self.num_experts_per_tok
@@ -186,6 +309,62 @@ PRESETS: dict[str, ModelConfig] = {
         num_hidden_layers=80, num_attention_heads=64, num_key_value_heads=8, head_dim=128,
         rms_norm_eps=1e-5, rope_theta=500000.0, max_position_embeddings=8192,
         bos_token_id=128000, eos_token_id=128001),
+    # tiny random-init members of the other families (tests: each exercises its family's features)
+    "tiny-qwen2": ModelConfig(
+        architecture="qwen2", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+        num_attention_heads=8, num_key_value_heads=2, head_dim=32, rms_norm_eps=1e-6, rope_theta=1e6,
+        attention_bias=True, tie_word_embeddings=True, max_position_embeddings=2048),
+    "tiny-qwen3": ModelConfig(
+        architecture="qwen3", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6,
+        qk_norm=True, max_position_embeddings=2048),
+    "tiny-mistral": ModelConfig(
+        architecture="mistral", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+        num_attention_heads=8, num_key_value_heads=2, head_dim=32, rope_theta=10000.0, sliding_window=24,
+        max_position_embeddings=2048),
+    "tiny-gemma": ModelConfig(
+        architecture="gemma", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+        num_attention_heads=2, num_key_value_heads=1, head_dim=256, rms_norm_eps=1e-6, hidden_act="gelu_tanh",
+        norm_unit_offset=True, embed_scale=16.0, tie_word_embeddings=True, max_position_embeddings=2048),
+    "tiny-gemma2": ModelConfig(
+        architecture="gemma2", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=64, rms_norm_eps=1e-6, hidden_act="gelu_tanh",
+        norm_unit_offset=True, embed_scale=16.0, tie_word_embeddings=True, sandwich_norm=True,
+        sliding_window=16, layer_types=["sliding_attention", "full_attention"] * 2, attn_logit_softcapping=50.0,
+        final_logit_softcapping=30.0, query_pre_attn_scalar=64.0, max_position_embeddings=2048),
+    "tiny-gemma3": ModelConfig(
+        architecture="gemma3", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=6,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=128, rms_norm_eps=1e-6, hidden_act="gelu_tanh",
+        norm_unit_offset=True, embed_scale=16.0, tie_word_embeddings=True, sandwich_norm=True, qk_norm=True,
+        sliding_window=16, layer_types=["sliding_attention"] * 5 + ["full_attention"], rope_theta=1e6,
+        rope_local_theta=10000.0, query_pre_attn_scalar=128.0, max_position_embeddings=2048),
+    "tiny-phi3": ModelConfig(
+        architecture="phi3", vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+        num_attention_heads=8, num_key_value_heads=8, head_dim=32, rope_theta=10000.0, sliding_window=40,
+        max_position_embeddings=2048),
+    # full-size members (random init for benchmarks; real checkpoints carry their own config.json)
+    "qwen2.5-7b": ModelConfig(
+        architecture="qwen2", vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+        num_attention_heads=28, num_key_value_heads=4, head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6,
+        attention_bias=True, max_position_embeddings=32768, eos_token_id=151645),
+    "qwen3-8b": ModelConfig(
+        architecture="qwen3", vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6,
+        qk_norm=True, max_position_embeddings=40960, eos_token_id=151645),
+    "mistral-7b": ModelConfig(
+        architecture="mistral", vocab_size=32768, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6, max_position_embeddings=32768),
+    "gemma-2-9b": ModelConfig(
+        architecture="gemma2", vocab_size=256000, hidden_size=3584, intermediate_size=14336, num_hidden_layers=42,
+        num_attention_heads=16, num_key_value_heads=8, head_dim=256, rms_norm_eps=1e-6, hidden_act="gelu_tanh",
+        norm_unit_offset=True, embed_scale=3584 ** 0.5, tie_word_embeddings=True, sandwich_norm=True,
+        sliding_window=4096, layer_types=["sliding_attention", "full_attention"] * 21, attn_logit_softcapping=50.0,
+        final_logit_softcapping=30.0, query_pre_attn_scalar=256.0, max_position_embeddings=8192,
+        bos_token_id=2, eos_token_id=1),
+    "phi-3-mini-4k": ModelConfig(
+        architecture="phi3", vocab_size=32064, hidden_size=3072, intermediate_size=8192, num_hidden_layers=32,
+        num_attention_heads=32, num_key_value_heads=32, head_dim=96, rope_theta=10000.0, sliding_window=2047,
+        max_position_embeddings=4096, eos_token_id=32000),
     "mixtral-8x7b": ModelConfig(
         architecture="mixtral", vocab_size=32000, hidden_size=4096, intermediate_size=14336,
         num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8, head_dim=128,

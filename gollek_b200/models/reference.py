@@ -1,9 +1,10 @@
 """Plain-PyTorch fp32 reference decoder (the correctness oracle).
 
-Dense (non-paged) forward of the Llama / Mixtral family in Hugging Face
-semantics: pre-norm RMSNorm, GQA attention with NeoX ("rotate-half") RoPE whose
-theta comes from the config, SwiGLU FFN or top-k softmax MoE, final RMSNorm and
-an untied lm_head. It restates what the reference's Direct engine computes
+Dense (non-paged) forward of the supported families (Llama, Mistral, Mixtral, Qwen2/3, Gemma 1/2/3,
+Phi-3) in Hugging Face semantics: pre-norm RMSNorm ((1 + w) for Gemma), GQA attention with NeoX
+("rotate-half") RoPE whose theta comes from the config (per layer type for Gemma-3), optional
+projection biases, QK-norm, sliding windows and logit softcapping, SwiGLU/GeGLU FFN or top-k softmax
+MoE, sandwich norms (Gemma-2/3), final RMSNorm and a tied or untied lm_head. It restates what the reference's Direct engine computes
 (runner/safetensor/gollek-safetensor-engine/…/engine/forward/DirectForwardPass.java:40-321,
 MoE routing …/generation/moe/MoeForwardPass.java:107-128) without its
 hard-coded RoPE theta, and is cross-checked against ``transformers`` in tests.
@@ -24,29 +25,49 @@ Weights = Dict[str, torch.Tensor]
 
 def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
                         dtype: torch.dtype = torch.float32, device: str = "cpu") -> Weights:
-    """Random-init weights of the architecture: every matrix ~ N(0, std), norm weights = 1.
+    """Random-init weights of the architecture under its Hugging Face names: every matrix and
+    bias ~ N(0, std); norm weights 1 (or ~N(0, 0.05) for the (1 + w) norms of Gemma).
 
     Tensors are generated in a fixed order from one generator seeded with ``seed`` so a
     checkpoint written from them is reproducible.
     """
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    h, q, kv, f = cfg.hidden_size, cfg.q_size, cfg.kv_size, cfg.intermediate_size
+    h, q, kv, f, D = cfg.hidden_size, cfg.q_size, cfg.kv_size, cfg.intermediate_size, cfg.head_dim
+    fam = cfg.architecture
 
-    def rnd(*shape):
+    def rnd(*shape, s=std):
         t = torch.empty(*shape, dtype=torch.float32 if dtype == torch.float32 else dtype, device=device)
-        t.normal_(0.0, std, generator=g)
+        t.normal_(0.0, s, generator=g)
         return t
+
+    def norm(n):
+        if cfg.norm_unit_offset:
+            return rnd(n, s=0.05).to(dtype)
+        return torch.ones(n, dtype=dtype, device=device)
 
     w: Weights = {"model.embed_tokens.weight": rnd(cfg.vocab_size, h)}
     for i in range(cfg.num_hidden_layers):
         p = f"model.layers.{i}."
-        w[p + "input_layernorm.weight"] = torch.ones(h, dtype=dtype, device=device)
-        w[p + "self_attn.q_proj.weight"] = rnd(q, h)
-        w[p + "self_attn.k_proj.weight"] = rnd(kv, h)
-        w[p + "self_attn.v_proj.weight"] = rnd(kv, h)
+        w[p + "input_layernorm.weight"] = norm(h)
+        if fam == "phi3":
+            w[p + "self_attn.qkv_proj.weight"] = rnd(q + 2 * kv, h)
+        else:
+            w[p + "self_attn.q_proj.weight"] = rnd(q, h)
+            w[p + "self_attn.k_proj.weight"] = rnd(kv, h)
+            w[p + "self_attn.v_proj.weight"] = rnd(kv, h)
+        if cfg.attention_bias:
+            w[p + "self_attn.q_proj.bias"] = rnd(q)
+            w[p + "self_attn.k_proj.bias"] = rnd(kv)
+            w[p + "self_attn.v_proj.bias"] = rnd(kv)
+        if cfg.qk_norm:
+            w[p + "self_attn.q_norm.weight"] = norm(D)
+            w[p + "self_attn.k_norm.weight"] = norm(D)
         w[p + "self_attn.o_proj.weight"] = rnd(h, q)
-        w[p + "post_attention_layernorm.weight"] = torch.ones(h, dtype=dtype, device=device)
+        w[p + "post_attention_layernorm.weight"] = norm(h)
+        if cfg.sandwich_norm:
+            w[p + "pre_feedforward_layernorm.weight"] = norm(h)
+            w[p + "post_feedforward_layernorm.weight"] = norm(h)
         if cfg.is_moe:
             w[p + "block_sparse_moe.gate.weight"] = rnd(cfg.num_local_experts, h)
             for e in range(cfg.num_local_experts):
@@ -54,20 +75,60 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
                 w[pe + "w1.weight"] = rnd(f, h)
                 w[pe + "w3.weight"] = rnd(f, h)
                 w[pe + "w2.weight"] = rnd(h, f)
+        elif fam == "phi3":
+            w[p + "mlp.gate_up_proj.weight"] = rnd(2 * f, h)
+            w[p + "mlp.down_proj.weight"] = rnd(h, f)
         else:
             w[p + "mlp.gate_proj.weight"] = rnd(f, h)
             w[p + "mlp.up_proj.weight"] = rnd(f, h)
             w[p + "mlp.down_proj.weight"] = rnd(h, f)
-    w["model.norm.weight"] = torch.ones(h, dtype=dtype, device=device)
+    w["model.norm.weight"] = norm(h)
     if not cfg.tie_word_embeddings:
         w["lm_head.weight"] = rnd(cfg.vocab_size, h)
     return w
 
 
-def rope_inv_freq(cfg: ModelConfig) -> torch.Tensor:
-    """Per-pair inverse frequencies, including ``linear`` and ``llama3`` scaling."""
+def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
+    """Layer ``i``'s tensors under canonical keys, whatever the family's checkpoint layout:
+    q, k, v, o, (q_bias, k_bias, v_bias), (q_norm, k_norm), in_norm, post_norm, (pre_ff_norm,
+    post_ff_norm), gate, up, down. ``get(name)`` returns a tensor (or a quantized weight that
+    supports row slicing). Phi-3's fused ``qkv_proj`` / ``gate_up_proj`` are split by rows."""
+    p = f"model.layers.{i}."
+    q_sz, kv_sz, f = cfg.q_size, cfg.kv_size, cfg.intermediate_size
+    t = {"in_norm": get(p + "input_layernorm.weight"), "post_norm": get(p + "post_attention_layernorm.weight"),
+         "o": get(p + "self_attn.o_proj.weight")}
+    if cfg.architecture == "phi3":
+        qkv = get(p + "self_attn.qkv_proj.weight")
+        t["q"], t["k"], t["v"] = qkv[:q_sz], qkv[q_sz:q_sz + kv_sz], qkv[q_sz + kv_sz:q_sz + 2 * kv_sz]
+    else:
+        t["q"] = get(p + "self_attn.q_proj.weight")
+        t["k"] = get(p + "self_attn.k_proj.weight")
+        t["v"] = get(p + "self_attn.v_proj.weight")
+    if cfg.attention_bias:
+        for n in ("q", "k", "v"):
+            t[n + "_bias"] = get(p + f"self_attn.{n}_proj.bias")
+    if cfg.qk_norm:
+        t["q_norm"] = get(p + "self_attn.q_norm.weight")
+        t["k_norm"] = get(p + "self_attn.k_norm.weight")
+    if cfg.sandwich_norm:
+        t["pre_ff_norm"] = get(p + "pre_feedforward_layernorm.weight")
+        t["post_ff_norm"] = get(p + "post_feedforward_layernorm.weight")
+    if not cfg.is_moe:
+        if cfg.architecture == "phi3":
+            gu = get(p + "mlp.gate_up_proj.weight")
+            t["gate"], t["up"] = gu[:f], gu[f:2 * f]
+        else:
+            t["gate"] = get(p + "mlp.gate_proj.weight")
+            t["up"] = get(p + "mlp.up_proj.weight")
+        t["down"] = get(p + "mlp.down_proj.weight")
+    return t
+
+
+def rope_inv_freq(cfg: ModelConfig, theta: Optional[float] = None, long: bool = False) -> torch.Tensor:
+    """Per-pair inverse frequencies, including ``linear``, ``llama3`` and ``longrope`` scaling."""
     d = cfg.head_dim
-    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+    theta = theta or cfg.rope_theta
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
     rs = cfg.rope_scaling
     if rs.kind == "linear":
         inv = inv / rs.factor
@@ -81,14 +142,28 @@ def rope_inv_freq(cfg: ModelConfig) -> torch.Tensor:
         mid = (wl <= low_wl) & (wl >= high_wl)
         scaled = torch.where(mid, (1 - smooth) * inv / rs.factor + smooth * inv, scaled)
         inv = scaled
+    elif rs.kind == "longrope":
+        fac = rs.long_factor if long else rs.short_factor
+        if fac is not None:
+            inv = inv / torch.tensor(fac, dtype=torch.float64)
     return inv.to(torch.float32)
 
 
-def rope_cos_sin(cfg: ModelConfig, max_pos: int, device="cpu") -> torch.Tensor:
-    """``[max_pos, head_dim]`` table: first half cos, second half sin (fp32)."""
-    inv = rope_inv_freq(cfg).to(device)
+def rope_cos_sin(cfg: ModelConfig, max_pos: int, device="cpu", theta: Optional[float] = None) -> torch.Tensor:
+    """``[max_pos, head_dim]`` table: first half cos, second half sin (fp32). ``longrope`` uses the
+    short factors below the original context length and the long ones from there on, with the
+    attention scaling sqrt(1 + ln(s) / ln(original)) for s = max_position / original."""
     t = torch.arange(max_pos, dtype=torch.float32, device=device)
-    freqs = torch.outer(t, inv)
+    rs = cfg.rope_scaling
+    if rs.kind == "longrope":
+        orig = rs.original_max_position_embeddings
+        fs = torch.outer(t, rope_inv_freq(cfg, theta, long=False).to(device))
+        fl = torch.outer(t, rope_inv_freq(cfg, theta, long=True).to(device))
+        freqs = torch.where((t >= orig)[:, None], fl, fs)
+        s = cfg.max_position_embeddings / orig
+        mscale = math.sqrt(1 + math.log(s) / math.log(orig)) if s > 1 else 1.0
+        return torch.cat([freqs.cos() * mscale, freqs.sin() * mscale], dim=-1)
+    freqs = torch.outer(t, rope_inv_freq(cfg, theta).to(device))
     return torch.cat([freqs.cos(), freqs.sin()], dim=-1)
 
 
@@ -102,9 +177,10 @@ def apply_rope_neox(x: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Ten
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
 
 
-def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool = False) -> torch.Tensor:
     xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+    wf = w.float() + 1.0 if unit_offset else w.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf).to(x.dtype)
 
 
 def moe_ref(x: torch.Tensor, gate_w: torch.Tensor, experts: list, top_k: int) -> torch.Tensor:
@@ -132,43 +208,73 @@ class ReferenceDecoder:
     def __init__(self, cfg: ModelConfig, weights: Weights):
         self.cfg = cfg
         self.w = {k: v.float() for k, v in weights.items()}
-        self.cos_sin = rope_cos_sin(cfg, max(cfg.max_position_embeddings, 4096))
+        n = max(cfg.max_position_embeddings, 4096)
+        self.cos_sin = rope_cos_sin(cfg, n)
+        self.cos_sin_local = rope_cos_sin(cfg, n, theta=cfg.rope_local_theta) if cfg.rope_local_theta else None
 
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
         """ids: [S] → logits [S, vocab] (fp32)."""
         cfg, w = self.cfg, self.w
         S = ids.shape[0]
         pos = torch.arange(S)
-        h = w["model.embed_tokens.weight"][ids.long()]
+        h = w["model.embed_tokens.weight"][ids.long()] * cfg.embed_scale
         H, Hk, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        mask = torch.full((S, S), float("-inf")).triu(1)
+        uo, eps = cfg.norm_unit_offset, cfg.rms_norm_eps
+        causal = torch.full((S, S), float("-inf")).triu(1)
         for i in range(cfg.num_hidden_layers):
-            p = f"model.layers.{i}."
-            x = rms_norm_ref(h, w[p + "input_layernorm.weight"], cfg.rms_norm_eps)
-            q = (x @ w[p + "self_attn.q_proj.weight"].t()).view(S, H, D)
-            k = (x @ w[p + "self_attn.k_proj.weight"].t()).view(S, Hk, D)
-            v = (x @ w[p + "self_attn.v_proj.weight"].t()).view(S, Hk, D)
-            q = apply_rope_neox(q, self.cos_sin, pos)
-            k = apply_rope_neox(k, self.cos_sin, pos)
+            L = layer_tensors(w.__getitem__, cfg, i)
+            x = rms_norm_ref(h, L["in_norm"], eps, uo)
+            q = x @ L["q"].t()
+            k = x @ L["k"].t()
+            v = x @ L["v"].t()
+            if cfg.attention_bias:
+                q, k, v = q + L["q_bias"], k + L["k_bias"], v + L["v_bias"]
+            q, k, v = q.view(S, H, D), k.view(S, Hk, D), v.view(S, Hk, D)
+            if cfg.qk_norm:
+                q = rms_norm_ref(q, L["q_norm"], eps, uo)
+                k = rms_norm_ref(k, L["k_norm"], eps, uo)
+            win = cfg.layer_window(i)
+            cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
+            q = apply_rope_neox(q, cs, pos)
+            k = apply_rope_neox(k, cs, pos)
             rep = H // Hk
             k = k.repeat_interleave(rep, dim=1)
             v = v.repeat_interleave(rep, dim=1)
-            s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(D) + mask
-            a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(S, H * D)
-            h = h + a @ w[p + "self_attn.o_proj.weight"].t()
-            x = rms_norm_ref(h, w[p + "post_attention_layernorm.weight"], cfg.rms_norm_eps)
+            s = torch.einsum("qhd,khd->hqk", q, k) * cfg.attn_scale
+            if cfg.attn_logit_softcapping:
+                c = cfg.attn_logit_softcapping
+                s = c * torch.tanh(s / c)
+            mask = causal
+            if win > 0:
+                mask = mask + torch.full((S, S), float("-inf")).tril(-win)
+            a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), v).reshape(S, H * D)
+            a = a @ L["o"].t()
+            if cfg.sandwich_norm:
+                h = h + rms_norm_ref(a, L["post_norm"], eps, uo)
+                x = rms_norm_ref(h, L["pre_ff_norm"], eps, uo)
+            else:
+                h = h + a
+                x = rms_norm_ref(h, L["post_norm"], eps, uo)
             if cfg.is_moe:
-                pe = p + "block_sparse_moe."
+                pe = f"model.layers.{i}.block_sparse_moe."
                 experts = [(w[pe + f"experts.{e}.w1.weight"], w[pe + f"experts.{e}.w3.weight"],
                             w[pe + f"experts.{e}.w2.weight"]) for e in range(cfg.num_local_experts)]
-                h = h + moe_ref(x, w[pe + "gate.weight"], experts, cfg.num_experts_per_tok)
+                m = moe_ref(x, w[pe + "gate.weight"], experts, cfg.num_experts_per_tok)
             else:
-                g = x @ w[p + "mlp.gate_proj.weight"].t()
-                u = x @ w[p + "mlp.up_proj.weight"].t()
-                h = h + (torch.nn.functional.silu(g) * u) @ w[p + "mlp.down_proj.weight"].t()
-        h = rms_norm_ref(h, w["model.norm.weight"], cfg.rms_norm_eps)
+                g = x @ L["gate"].t()
+                act = torch.nn.functional.silu(g) if cfg.hidden_act == "silu" else \
+                    torch.nn.functional.gelu(g, approximate="tanh")
+                m = (act * (x @ L["up"].t())) @ L["down"].t()
+            if cfg.sandwich_norm:
+                m = rms_norm_ref(m, L["post_ff_norm"], eps, uo)
+            h = h + m
+        h = rms_norm_ref(h, w["model.norm.weight"], eps, uo)
         head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
-        return h @ head.t()
+        logits = h @ head.t()
+        if cfg.final_logit_softcapping:
+            c = cfg.final_logit_softcapping
+            logits = c * torch.tanh(logits / c)
+        return logits
 
     def greedy(self, prompt: list, n_new: int) -> tuple:
         """Greedy decode by re-running the dense forward; returns (tokens, per-step logits)."""

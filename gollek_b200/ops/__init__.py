@@ -15,7 +15,7 @@ import torch
 from . import reference as ref
 from ..native import cuda_ext
 
-EPI_NONE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+EPI_NONE, EPI_RESIDUAL, EPI_SWIGLU, EPI_GEGLU = 0, 1, 2, 3
 SWIGLU_GROUP = 64
 
 
@@ -73,14 +73,18 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
 def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
                   kv_cache: Optional[torch.Tensor], slot_mapping: Optional[torch.Tensor],
                   num_heads: int, num_kv_heads: int, head_dim: int,
-                  q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  q_out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                  q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None,
+                  norm_eps: float = 1e-6) -> torch.Tensor:
+    """Split fused QKV (+ projection bias), per-head RMSNorm of q and k (QK-norm) when weights
+    are given, NeoX RoPE of q and k, paged KV-cache write; returns q [T, H, D]."""
     if not qkv.is_cuda:
         return _cpu(ref.rope_kv_write(qkv, positions, cos_sin, kv_cache, slot_mapping,
-                                      num_heads, num_kv_heads, head_dim), q_out)
+                                      num_heads, num_kv_heads, head_dim, bias, q_norm, k_norm, norm_eps), q_out)
     T = qkv.shape[0]
     q_out = torch.empty(T, num_heads, head_dim, dtype=qkv.dtype, device=qkv.device) if q_out is None else q_out
     _C().rope_kv_write(q_out, qkv, positions, cos_sin, kv_cache, slot_mapping,
-                       num_heads, num_kv_heads, head_dim)
+                       num_heads, num_kv_heads, head_dim, bias, q_norm, k_norm, float(norm_eps))
     return q_out
 
 
@@ -99,19 +103,22 @@ def decode_splits(num_seqs: int, num_kv_heads: int, max_seq_len: int, num_sms: i
 def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                            seq_lens: torch.Tensor, scale: float, num_splits: int = 1,
                            out: Optional[torch.Tensor] = None,
-                           workspace: Optional[torch.Tensor] = None, tensor_cores: bool = True) -> torch.Tensor:
+                           workspace: Optional[torch.Tensor] = None, tensor_cores: bool = True,
+                           window: int = 0, softcap: float = 0.0) -> torch.Tensor:
     """One query token per sequence: q [B, H, D]. head_dim 128 runs the tensor-core kernel
-    (``tensor_cores=False`` selects the CUDA-core kernel, used for other head sizes)."""
+    (``tensor_cores=False`` selects the CUDA-core kernel, used for other head sizes).
+    ``window`` > 0: sliding-window attention; ``softcap`` > 0: tanh soft-capped scores."""
     if not q.is_cuda:
         B = q.shape[0]
         qsl = torch.arange(B + 1, dtype=torch.int32)
-        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, qsl, scale), out)
+        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, qsl, scale, window, softcap), out)
     out = torch.empty_like(q) if out is None else out
     if num_splits > 1 and workspace is None:
         B, H, D = q.shape
         workspace = torch.empty(B * H * num_splits * (D + 2), dtype=torch.float32, device=q.device)
     _C(2 if num_splits > 1 else 1).paged_decode_attention(out, q, kv_cache, block_tables, seq_lens, float(scale),
-                                                          int(num_splits), workspace, bool(tensor_cores))
+                                                          int(num_splits), workspace, bool(tensor_cores),
+                                                          int(window), float(softcap))
     return out
 
 
@@ -133,17 +140,20 @@ def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
 def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                             seq_lens: torch.Tensor, query_start: torch.Tensor, scale: float,
                             tiles: Optional[torch.Tensor] = None,
-                            out: Optional[torch.Tensor] = None, tensor_cores: bool = True) -> torch.Tensor:
+                            out: Optional[torch.Tensor] = None, tensor_cores: bool = True,
+                            window: int = 0, softcap: float = 0.0) -> torch.Tensor:
     """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new).
     head_dim 128 runs on tcgen05/TMEM (128-row query tiles); other sizes on mma.sync (64 rows).
-    ``tiles`` must have been built with ``prefill_block_m`` rows per tile."""
+    ``tiles`` must have been built with ``prefill_block_m`` rows per tile. ``window`` > 0:
+    sliding-window attention; ``softcap`` > 0: tanh soft-capped scores."""
     if not q.is_cuda:
-        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale), out)
+        return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale, window, softcap),
+                    out)
     out = torch.empty_like(q) if out is None else out
     if tiles is None:
         tiles = prefill_tiles(query_start.tolist(), prefill_block_m(q.shape[2], tensor_cores)).to(q.device)
     _C().paged_prefill_attention(out, q, kv_cache, block_tables, seq_lens, query_start, tiles, float(scale),
-                                 bool(tensor_cores))
+                                 bool(tensor_cores), int(window), float(softcap))
     return out
 
 
@@ -264,17 +274,29 @@ def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
 
 
 def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.Tensor] = None,
-                  bn: int = 0) -> torch.Tensor:
-    """silu(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``."""
+                  bn: int = 0, act: str = "silu") -> torch.Tensor:
+    """act(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``;
+    ``act`` is ``silu`` (SwiGLU, Llama) or ``gelu_tanh`` (GeGLU, Gemma), fused in the GEMM epilogue."""
+    if act != "silu" and (_is_q(w_gate_up) or _is_fp8(w_gate_up)):
+        # quantized GeGLU: plain product, gate activation on the host-side graph
+        y = linear(a, w_gate_up)
+        return _copy_into(ref.glu_interleaved(y, SWIGLU_GROUP, act).to(a.dtype), out)
     if _is_q(w_gate_up):
         return _qlinear(a, w_gate_up, out, True)
     if _is_fp8(w_gate_up):
         return linear_fp8(a, w_gate_up, out, swiglu=True)
     if not a.is_cuda:
-        return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP), out)
+        return _cpu(ref.gemm_swiglu(a, w_gate_up, SWIGLU_GROUP, act), out)
     M, N = a.shape[0], w_gate_up.shape[0]
     out = torch.empty(M, N // 2, dtype=a.dtype, device=a.device) if out is None else out
-    _gemm(out, a, w_gate_up, None, EPI_SWIGLU, bn)
+    _gemm(out, a, w_gate_up, None, EPI_SWIGLU if act == "silu" else EPI_GEGLU, bn)
+    return out
+
+
+def _copy_into(y: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+    if out is None:
+        return y
+    out.copy_(y)
     return out
 
 
@@ -289,19 +311,23 @@ def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tenso
     return out
 
 
-def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None,
+              scale: float = 1.0) -> torch.Tensor:
+    """Row gather (x ``scale``: Gemma multiplies embeddings by sqrt(hidden))."""
     if _is_q(table):
         if not table.raw.is_cuda:
-            return _cpu(table.dequantize()[ids.long()].to(torch.float32), out)
+            return _cpu(table.dequantize()[ids.long()].to(torch.float32) * scale, out)
         if table.qtype != 8:
-            return embedding(ids, table.dequantize(), out)
+            return embedding(ids, table.dequantize(), out, scale)
         out = torch.empty(ids.shape[0], table.K, dtype=torch.bfloat16, device=table.device) if out is None else out
         _C().embedding_q8_0(out, ids, table.raw, table.N)
+        if scale != 1.0:
+            out.mul_(scale)
         return out
     if not table.is_cuda:
-        return _cpu(ref.embedding(ids, table), out)
+        return _cpu(ref.embedding(ids, table) * scale, out)
     out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device) if out is None else out
-    _C().embedding(out, ids, table)
+    _C().embedding(out, ids, table, float(scale))
     return out
 
 

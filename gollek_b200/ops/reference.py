@@ -34,23 +34,34 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
 
 def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
                   kv_cache: Optional[torch.Tensor], slot_mapping: torch.Tensor,
-                  num_heads: int, num_kv_heads: int, head_dim: int) -> torch.Tensor:
-    """Split fused QKV, apply NeoX RoPE to q and k, scatter k/v into the paged cache.
+                  num_heads: int, num_kv_heads: int, head_dim: int, bias: Optional[torch.Tensor] = None,
+                  q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None,
+                  norm_eps: float = 1e-6) -> torch.Tensor:
+    """Split fused QKV (+ bias), per-head RMSNorm of q/k when weights are given (QK-norm), apply
+    NeoX RoPE to q and k, scatter k/v into the paged cache.
 
     qkv: [T, (H + 2*Hk) * D]; returns rotated q [T, H, D]. Slots < 0 are skipped (padding).
     """
     T = qkv.shape[0]
     H, Hk, D = num_heads, num_kv_heads, head_dim
+    if bias is not None:
+        qkv = (qkv.float() + bias.float()).to(qkv.dtype)
     q = qkv[:, : H * D].view(T, H, D)
     k = qkv[:, H * D: (H + Hk) * D].view(T, Hk, D)
     v = qkv[:, (H + Hk) * D:].view(T, Hk, D)
+    if q_norm is not None:
+        def hnorm(x, w):
+            xf = x.float()
+            return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm_eps) * w.float()
+        q, k = hnorm(q, q_norm), hnorm(k, k_norm)
     cs = cos_sin[positions.long()].float()
-    cos, sin = cs[:, None, : D // 2], cs[:, None, D // 2:]
+    R = cos_sin.shape[1]  # rotary dims (< D: the remaining dims pass through)
+    cos, sin = cs[:, None, : R // 2], cs[:, None, R // 2:]
 
     def rot(x):
         xf = x.float()
-        x1, x2 = xf[..., : D // 2], xf[..., D // 2:]
-        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
+        x1, x2 = xf[..., : R // 2], xf[..., R // 2: R]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin, xf[..., R:]], -1)
 
     qr = rot(q).to(qkv.dtype)
     kr = rot(k).to(qkv.dtype)
@@ -65,12 +76,15 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
 
 
 def paged_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
-                    seq_lens: torch.Tensor, query_start_loc: torch.Tensor, scale: float) -> torch.Tensor:
+                    seq_lens: torch.Tensor, query_start_loc: torch.Tensor, scale: float,
+                    window: int = 0, softcap: float = 0.0) -> torch.Tensor:
     """Causal attention of each sequence's new queries over its paged KV.
 
     q: [T, H, D] (tokens of all sequences, concatenated); seq_lens[b] = total KV length
     of sequence b *including* its new tokens; query i of sequence b (q_len tokens) sits at
-    absolute position ``seq_lens[b] - q_len + i`` and attends to KV positions ≤ that.
+    absolute position ``seq_lens[b] - q_len + i`` and attends to KV positions ≤ that
+    (and, with ``window`` > 0, > position - window). ``softcap`` > 0 maps the scaled scores
+    through softcap · tanh(score / softcap) before the softmax.
     """
     T, H, D = q.shape
     Hk, bs = kv_cache.shape[2], kv_cache.shape[3]
@@ -91,9 +105,14 @@ def paged_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch
         v = v.repeat_interleave(rep, 1)
         qb = q[s:e].float()
         sc = torch.einsum("qhd,khd->hqk", qb, k) * scale
+        if softcap > 0:
+            sc = softcap * torch.tanh(sc / softcap)
         qpos = torch.arange(L - ql, L, device=q.device)
         kpos = torch.arange(L, device=q.device)
-        sc = sc.masked_fill(kpos[None, None, :] > qpos[None, :, None], float("-inf"))
+        masked = kpos[None, None, :] > qpos[None, :, None]
+        if window > 0:
+            masked = masked | (kpos[None, None, :] <= qpos[None, :, None] - window)
+        sc = sc.masked_fill(masked, float("-inf"))
         out[s:e] = torch.einsum("hqk,khd->qhd", torch.softmax(sc, -1), v).to(q.dtype)
     return out
 
@@ -119,13 +138,22 @@ def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, group: int = 64
     return torch.stack([g, u], 1).reshape(2 * F_, K)
 
 
-def gemm_swiglu(a: torch.Tensor, w_gu: torch.Tensor, group: int = 64) -> torch.Tensor:
-    """silu(a @ Wg.T) * (a @ Wu.T) for gate/up weights interleaved by ``interleave_gate_up``."""
+def glu_act(g: torch.Tensor, act: str) -> torch.Tensor:
+    """The gate activation of a gated FFN: ``silu`` (SwiGLU) or ``gelu_tanh`` (GeGLU)."""
+    return F.silu(g) if act == "silu" else F.gelu(g, approximate="tanh")
+
+
+def gemm_swiglu(a: torch.Tensor, w_gu: torch.Tensor, group: int = 64, act: str = "silu") -> torch.Tensor:
+    """act(a @ Wg.T) * (a @ Wu.T) for gate/up weights interleaved by ``interleave_gate_up``."""
     y = a.float() @ w_gu.float().t()
+    return glu_interleaved(y, group, act).to(a.dtype)
+
+
+def glu_interleaved(y: torch.Tensor, group: int = 64, act: str = "silu") -> torch.Tensor:
+    """act(gate) * up of a [M, 2F] product whose columns interleave gate/up in groups."""
     M = y.shape[0]
-    y = y.view(M, -1, 2, group)
-    out = F.silu(y[:, :, 0]) * y[:, :, 1]
-    return out.reshape(M, -1).to(a.dtype)
+    y = y.float().view(M, -1, 2, group)
+    return (glu_act(y[:, :, 0], act) * y[:, :, 1]).reshape(M, -1)
 
 
 def silu_mul(x: torch.Tensor) -> torch.Tensor:

@@ -77,3 +77,57 @@ def test_reference_mixtral_matches_hf():
     with torch.no_grad():
         theirs = model(ids[None]).logits[0]
     torch.testing.assert_close(ours, theirs, rtol=1e-4, atol=1e-4)
+
+
+import pytest  # noqa: E402
+
+
+def _hf_family_model(cfg, weights):
+    import transformers
+    d = cfg.to_hf()
+    mt = d.pop("model_type")
+    arch = d.pop("architectures")[0]
+    d.pop("torch_dtype", None)
+    hf_cfg = transformers.AutoConfig.for_model(mt, **d)
+    hf_cfg._attn_implementation = "eager"
+    model = getattr(transformers, arch)(hf_cfg).eval()
+    missing, unexpected = model.load_state_dict(weights, strict=False)
+    assert not [m for m in missing if "rotary" not in m and not m.endswith("lm_head.weight")], missing
+    assert not unexpected, unexpected
+    if cfg.tie_word_embeddings:
+        model.tie_weights()
+    return model
+
+
+@pytest.mark.parametrize("name,S", [("tiny-qwen2", 30), ("tiny-qwen3", 30), ("tiny-mistral", 48),
+                                    ("tiny-gemma", 30), ("tiny-gemma2", 40), ("tiny-gemma3", 40),
+                                    ("tiny-phi3", 56)])
+def test_reference_family_matches_hf(name, S):
+    """Each family's oracle forward (biases, QK-norm, windows longer than the sequence window,
+    softcaps, sandwich norms, GeGLU, (1 + w) norms, per-layer RoPE bases) equals transformers'."""
+    cfg = preset(name)
+    w = init_random_weights(cfg, seed=3)
+    ids = torch.randint(0, cfg.vocab_size, (S,), generator=torch.Generator().manual_seed(3))
+    ours = ReferenceDecoder(cfg, w).forward(ids)
+    hf = _hf_family_model(cfg, w)
+    with torch.no_grad():
+        theirs = hf(ids[None]).logits[0]
+    torch.testing.assert_close(ours, theirs, rtol=1e-4, atol=2e-4)
+
+
+def test_family_configs_parse_from_hf():
+    import transformers
+    from gollek_b200.config import ModelConfig
+    for name in ("tiny-qwen2", "tiny-qwen3", "tiny-mistral", "tiny-gemma", "tiny-gemma2", "tiny-gemma3", "tiny-phi3"):
+        cfg = preset(name)
+        d = cfg.to_hf()
+        mt = d.pop("model_type")
+        d.pop("architectures")
+        d.pop("torch_dtype", None)
+        hf_cfg = transformers.AutoConfig.for_model(mt, **d)
+        back = ModelConfig.from_hf(hf_cfg.to_dict())
+        for f in ("architecture", "head_dim", "sliding_window", "layer_types", "qk_norm", "attention_bias",
+                  "sandwich_norm", "norm_unit_offset", "hidden_act", "query_pre_attn_scalar",
+                  "attn_logit_softcapping", "final_logit_softcapping", "tie_word_embeddings"):
+            assert getattr(back, f) == getattr(cfg, f), (name, f, getattr(back, f), getattr(cfg, f))
+        assert abs(back.rope_theta - cfg.rope_theta) < 1e-3 and abs(back.embed_scale - cfg.embed_scale) < 1e-6
