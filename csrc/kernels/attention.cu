@@ -862,6 +862,7 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
   GOLLEK_DECODE_CASE(128, 4)
   GOLLEK_DECODE_CASE(128, 8)
   GOLLEK_DECODE_CASE(64, 1)
+  GOLLEK_DECODE_CASE(64, 2)
   GOLLEK_DECODE_CASE(64, 4)
   GOLLEK_DECODE_CASE(64, 8)
   GOLLEK_DECODE_CASE(32, 1)

@@ -53,6 +53,8 @@ class LoRAManager:
         self.device, self.dtype = dev, dt
         L = cfg.num_hidden_layers
         H, Hk, D = model.H, model.Hk, model.D
+        if getattr(model, "D_logical", D) != D:
+            raise NotImplementedError("multi-LoRA needs a kernel-native head size (32/64/128/256)")
         S = max_loras + 1
         hidden = cfg.hidden_size
         qkv_out = (H + 2 * Hk) * D

@@ -1,4 +1,5 @@
-"""Serving graph of the Llama family (Llama-2/3, Mistral) and Mixtral (top-k MoE).
+"""Serving graph of the decoder families: Llama-2/3, Mistral, Mixtral (top-k MoE), Qwen2/3,
+Gemma 1/2/3 and Phi-3 (their differences are ModelConfig switches; see ``config.FAMILIES``).
 
 One instance runs on one GPU (one process per GPU); under tensor parallelism it holds the
 rank's Megatron-style shard: QKV and gate/up column-parallel (whole heads / FFN slices),
@@ -26,7 +27,10 @@ import torch
 
 from .. import ops
 from ..config import ModelConfig
-from .reference import rope_cos_sin
+from .reference import layer_tensors, rope_cos_sin
+
+# head sizes the attention kernels are built for; other sizes are stored zero-padded to the next one
+_KERNEL_HEAD_DIMS = (32, 64, 128, 256)
 
 
 @dataclass
@@ -84,6 +88,21 @@ class TPComm:
         return t
 
 
+def _pad_heads(w: torch.Tensor, n_heads: int, d: int, d_pad: int, dim: int = 0) -> torch.Tensor:
+    """Zero-pad each of ``n_heads`` head blocks of width ``d`` along ``dim`` to ``d_pad``."""
+    if d == d_pad:
+        return w
+    if dim == 0:
+        v = w.reshape(n_heads, d, *w.shape[1:])
+        out = torch.zeros(n_heads, d_pad, *w.shape[1:], dtype=w.dtype, device=w.device)
+        out[:, :d] = v
+        return out.reshape(n_heads * d_pad, *w.shape[1:])
+    v = w.reshape(w.shape[0], n_heads, d)
+    out = torch.zeros(w.shape[0], n_heads, d_pad, dtype=w.dtype, device=w.device)
+    out[:, :, :d] = v
+    return out.reshape(w.shape[0], n_heads * d_pad)
+
+
 def _pad_rows(w: torch.Tensor, rows: int) -> torch.Tensor:
     if w.shape[0] == rows:
         return w
@@ -128,7 +147,10 @@ class LlamaModel:
         else:  # replicate KV heads across ranks
             self.Hk = 1
             self.kv_head0 = r * cfg.num_key_value_heads // tp
-        self.D = cfg.head_dim
+        self.D_logical = cfg.head_dim
+        self.D = next((d for d in _KERNEL_HEAD_DIMS if d >= cfg.head_dim), cfg.head_dim)
+        if self.D != cfg.head_dim and cfg.qk_norm:
+            raise ValueError(f"head_dim {cfg.head_dim} with QK-norm is not supported")
         f_shard = cfg.intermediate_size // tp
         if cfg.intermediate_size % tp:
             raise ValueError("intermediate_size must be divisible by the TP size")
@@ -152,8 +174,12 @@ class LlamaModel:
             else:
                 self.E_loc, self.e0, self.moe_F = E, 0, f_shard
         self.moe_F_pad = (self.moe_F + ops.SWIGLU_GROUP - 1) // ops.SWIGLU_GROUP * ops.SWIGLU_GROUP
-        self.scale = 1.0 / math.sqrt(self.D)
-        self.cos_sin = rope_cos_sin(cfg, max(cfg.max_position_embeddings, 8192), device=self.device)
+        self.scale = cfg.attn_scale
+        n_pos = max(cfg.max_position_embeddings, 8192)
+        self.cos_sin = rope_cos_sin(cfg, n_pos, device=self.device)
+        self.cos_sin_local = (rope_cos_sin(cfg, n_pos, device=self.device, theta=cfg.rope_local_theta)
+                              if cfg.rope_local_theta else None)
+        self.windows = [cfg.layer_window(i) for i in range(cfg.num_hidden_layers)]
         self.layers: List[Dict[str, torch.Tensor]] = []
         self.embed: Optional[torch.Tensor] = None
         self.norm: Optional[torch.Tensor] = None
@@ -189,23 +215,41 @@ class LlamaModel:
         def down(d, fpad=None):
             return d if isinstance(d, QWeight) else _pad_cols(d, self.F_pad if fpad is None else fpad)
 
+        Dl = self.D_logical
+
+        def norm_w(x):
+            # Gemma's RMSNorm scales by (1 + w): folded here so every norm kernel multiplies by w
+            if cfg.norm_unit_offset:
+                return (x.float() + 1.0).to(dt).contiguous()
+            return x.contiguous()
+
         self.embed = t("model.embed_tokens.weight").contiguous()
-        self.norm = t("model.norm.weight").contiguous()
+        self.norm = norm_w(t("model.norm.weight"))
         head_name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
         self.lm_head = t(head_name)[r * self.V_local:(r + 1) * self.V_local].contiguous()
         self.layers = []
         for i in range(cfg.num_hidden_layers):
             p = f"model.layers.{i}."
-            q = t(p + "self_attn.q_proj.weight")[r * H * D:(r + 1) * H * D]
-            k = t(p + "self_attn.k_proj.weight")[self.kv_head0 * D:(self.kv_head0 + Hk) * D]
-            v = t(p + "self_attn.v_proj.weight")[self.kv_head0 * D:(self.kv_head0 + Hk) * D]
-            o = t(p + "self_attn.o_proj.weight")[:, r * H * D:(r + 1) * H * D]
+            c = layer_tensors(t, cfg, i)
+            kv0, kv1 = self.kv_head0 * Dl, (self.kv_head0 + Hk) * Dl
+            q = _pad_heads(c["q"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D)
+            k = _pad_heads(c["k"][kv0:kv1], Hk, Dl, D)
+            v = _pad_heads(c["v"][kv0:kv1], Hk, Dl, D)
+            o = _pad_heads(c["o"][:, r * H * Dl:(r + 1) * H * Dl], H, Dl, D, dim=1)
             L = {
-                "in_norm": t(p + "input_layernorm.weight").contiguous(),
-                "post_norm": t(p + "post_attention_layernorm.weight").contiguous(),
+                "in_norm": norm_w(c["in_norm"]),
+                "post_norm": norm_w(c["post_norm"]),
                 "w_qkv": cat([q, k, v]).contiguous(),
                 "w_o": o.contiguous(),
             }
+            if cfg.attention_bias:
+                L["qkv_bias"] = torch.cat([_pad_heads(c["q_bias"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D),
+                                           _pad_heads(c["k_bias"][kv0:kv1], Hk, Dl, D),
+                                           _pad_heads(c["v_bias"][kv0:kv1], Hk, Dl, D)]).contiguous()
+            if cfg.qk_norm:
+                L["q_norm"], L["k_norm"] = norm_w(c["q_norm"]), norm_w(c["k_norm"])
+            if cfg.sandwich_norm:
+                L["pre_ff_norm"], L["post_ff_norm"] = norm_w(c["pre_ff_norm"]), norm_w(c["post_ff_norm"])
             if cfg.is_moe:
                 pe = p + "block_sparse_moe."
                 L["router"] = t(pe + "gate.weight").contiguous()
@@ -225,9 +269,9 @@ class LlamaModel:
                 else:
                     L["experts"] = experts
             else:
-                g = t(p + "mlp.gate_proj.weight")[r * self.F:(r + 1) * self.F]
-                u = t(p + "mlp.up_proj.weight")[r * self.F:(r + 1) * self.F]
-                d = t(p + "mlp.down_proj.weight")[:, r * self.F:(r + 1) * self.F]
+                g = c["gate"][r * self.F:(r + 1) * self.F]
+                u = c["up"][r * self.F:(r + 1) * self.F]
+                d = c["down"][:, r * self.F:(r + 1) * self.F]
                 L["w_gate_up"] = gate_up(g, u).contiguous()
                 L["w_down"] = down(d).contiguous()
             self.layers.append(L)
@@ -245,17 +289,25 @@ class LlamaModel:
             return x
 
         h = cfg.hidden_size
+        Dl, D = self.D_logical, self.D
+        ones = lambda n: torch.ones(n, dtype=dt, device=dev)  # noqa: E731
         self.embed = rnd(cfg.vocab_size, h)
-        self.norm = torch.ones(h, dtype=dt, device=dev)
+        self.norm = ones(h)
         self.lm_head = rnd(self.V_local, h)
         self.layers = []
         for _ in range(cfg.num_hidden_layers):
             L = {
-                "in_norm": torch.ones(h, dtype=dt, device=dev),
-                "post_norm": torch.ones(h, dtype=dt, device=dev),
-                "w_qkv": rnd((self.H + 2 * self.Hk) * self.D, h),
-                "w_o": rnd(h, self.H * self.D),
+                "in_norm": ones(h),
+                "post_norm": ones(h),
+                "w_qkv": _pad_heads(rnd((self.H + 2 * self.Hk) * Dl, h), self.H + 2 * self.Hk, Dl, D),
+                "w_o": _pad_heads(rnd(h, self.H * Dl), self.H, Dl, D, dim=1),
             }
+            if cfg.attention_bias:
+                L["qkv_bias"] = _pad_heads(rnd((self.H + 2 * self.Hk) * Dl), self.H + 2 * self.Hk, Dl, D)
+            if cfg.qk_norm:
+                L["q_norm"], L["k_norm"] = ones(D), ones(D)
+            if cfg.sandwich_norm:
+                L["pre_ff_norm"], L["post_ff_norm"] = ones(h), ones(h)
             if cfg.is_moe:
                 L["router"] = rnd(cfg.num_local_experts, h)
                 fp = self.moe_F_pad
@@ -315,16 +367,18 @@ class LlamaModel:
         return self.cfg.num_hidden_layers * 2 * self.Hk * block_size * self.D * torch.finfo(self.dtype).bits // 8
 
     # ------------------------------------------------------------------ forward
-    def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata) -> torch.Tensor:
+    def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata, window: int = 0) -> torch.Tensor:
         out = torch.empty_like(q)
         nd = meta.num_decode
+        cap = self.cfg.attn_logit_softcapping
         if nd > 0:
             ops.paged_decode_attention(q[:nd], cache, meta.decode_block_tables, meta.decode_seq_lens, self.scale,
-                                       meta.decode_splits, out=out[:nd], workspace=meta.decode_workspace)
+                                       meta.decode_splits, out=out[:nd], workspace=meta.decode_workspace,
+                                       window=window, softcap=cap)
         if meta.num_prefill_tokens > 0:
             ops.paged_prefill_attention(q[nd:], cache, meta.prefill_block_tables, meta.prefill_seq_lens,
                                         meta.prefill_query_start, self.scale, tiles=meta.prefill_tiles,
-                                        out=out[nd:])
+                                        out=out[nd:], window=window, softcap=cap)
         return out
 
     def _moe(self, x: torch.Tensor, L: dict, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -357,7 +411,7 @@ class LlamaModel:
         cfg = self.cfg
         eps = cfg.rms_norm_eps
         T = input_ids.shape[0]
-        h = ops.embedding(input_ids, self.embed)
+        h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
         n = len(self.layers)
         x = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
@@ -366,22 +420,37 @@ class LlamaModel:
             if self.lora is not None:
                 self.lora.apply(li, "qkv", x, qkv)
             cache = kv_cache[li] if kv_cache is not None else None
-            q = ops.rope_kv_write(qkv, meta.positions, self.cos_sin, cache, meta.slot_mapping,
-                                  self.H, self.Hk, self.D)
-            a = self._attention(q, cache, meta).view(T, self.H * self.D)
+            win = self.windows[li]
+            cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
+            q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
+                                  bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                                  norm_eps=eps)
+            a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
             h = ops.linear(a, L["w_o"], out=self.comm.partial_buffer(T))
             if self.lora is not None:
                 self.lora.apply(li, "o", a, h)
-            x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
+            if cfg.sandwich_norm:  # norm(attn) + residual, then the pre-FFN norm
+                h = ops.rms_norm(self.comm.all_reduce(h), L["post_norm"], eps)
+                x = ops.fused_add_rms_norm(h, residual, L["pre_ff_norm"], eps)
+            else:
+                x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
             if cfg.is_moe:
                 h = self._moe(x, L, out=self.comm.partial_buffer(T))
             else:
-                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"]), L["w_down"], out=self.comm.partial_buffer(T))
+                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act), L["w_down"],
+                               out=self.comm.partial_buffer(T))
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
-            x = self.comm.allreduce_add_rmsnorm(h, residual, nxt, eps)
+            if cfg.sandwich_norm:
+                h = ops.rms_norm(self.comm.all_reduce(h), L["post_ff_norm"], eps)
+                x = ops.fused_add_rms_norm(h, residual, nxt, eps)
+            else:
+                x = self.comm.allreduce_add_rmsnorm(h, residual, nxt, eps)
         if hidden_only:
             return x
         if meta.logits_indices is not None:
             x = x.index_select(0, meta.logits_indices)
-        logits = ops.linear(x, self.lm_head)
-        return self.comm.all_gather_last(logits)
+        logits = self.comm.all_gather_last(ops.linear(x, self.lm_head))
+        if cfg.final_logit_softcapping:
+            c = cfg.final_logit_softcapping
+            logits = torch.tanh(logits.float() / c).mul_(c).to(logits.dtype)
+        return logits

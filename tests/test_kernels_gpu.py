@@ -252,3 +252,81 @@ def test_paged_decode_attention_hd128(G, splits, tc):
     qsl = torch.arange(B + 1, dtype=torch.int32)
     ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl, scale)
     torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
+# ---------------------------------------------------------------------------- family features
+@pytest.mark.parametrize("H,Hk,D,tc", [(32, 8, 128, True), (32, 8, 128, False), (8, 2, 64, False),
+                                       (4, 2, 256, False), (8, 1, 256, False)])
+@pytest.mark.parametrize("window,softcap", [(0, 50.0), (40, 0.0), (100, 30.0)])
+def test_attention_window_softcap(H, Hk, D, tc, window, softcap):
+    """Sliding window (block skipping + mask) and tanh softcap in the decode and prefill kernels."""
+    lens = [1, 17, 100, 513, 40]
+    B = len(lens)
+    cache, bt, sl = _paged_setup(B, Hk, D, lens, seed=31)
+    q = bf(torch.randn(B, H, D, device=DEV, generator=_g(32)))
+    scale = 1 / math.sqrt(D)
+    qsl = torch.arange(B + 1, dtype=torch.int32)
+    if not (tc and D == 128):
+        if H // Hk not in (1, 2, 4, 8):
+            pytest.skip("group size not instantiated")
+    out = ops.paged_decode_attention(q, cache, bt, sl, scale, num_splits=3, tensor_cores=tc, window=window,
+                                     softcap=softcap)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl, scale, window, softcap)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+    # prefill with cached prefixes
+    specs = [(0, 70), (33, 20), (300, 200), (5, 130)]
+    plens = [p + n for p, n in specs]
+    cache, bt, sl = _paged_setup(len(specs), Hk, D, plens, seed=33)
+    qs = [0]
+    for _, n in specs:
+        qs.append(qs[-1] + n)
+    qp = bf(torch.randn(qs[-1], H, D, device=DEV, generator=_g(34)))
+    qslp = torch.tensor(qs, dtype=torch.int32, device=DEV)
+    outp = ops.paged_prefill_attention(qp, cache, bt, sl, qslp, scale, tensor_cores=tc, window=window,
+                                       softcap=softcap)
+    refp = R.paged_attention(qp.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qslp.cpu(), scale, window,
+                             softcap)
+    torch.testing.assert_close(outp.float().cpu(), refp, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("D,rot,bias,qkn", [(128, 128, True, False), (128, 128, False, True), (64, 64, True, True),
+                                            (128, 96, False, False), (256, 256, False, True), (32, 32, True, False)])
+def test_rope_bias_qknorm_partial(D, rot, bias, qkn):
+    from gollek_b200.config import preset
+    from gollek_b200.models.reference import rope_cos_sin
+    H, Hk, T = 4, 2, 37
+    cfg = preset("tiny-llama", head_dim=rot)
+    cs = rope_cos_sin(cfg, 512, device=DEV)
+    qkv = bf(torch.randn(T, (H + 2 * Hk) * D, device=DEV, generator=_g(40)))
+    b = bf(torch.randn((H + 2 * Hk) * D, device=DEV, generator=_g(41))) if bias else None
+    qn = bf(1 + 0.1 * torch.randn(D, device=DEV, generator=_g(42))) if qkn else None
+    kn = bf(1 + 0.1 * torch.randn(D, device=DEV, generator=_g(43))) if qkn else None
+    pos = torch.randint(0, 500, (T,), device=DEV, generator=_g(44)).int()
+    cache = torch.zeros(8, 2, Hk, 16, D, device=DEV, dtype=torch.bfloat16)
+    slots = torch.randperm(8 * 16, device=DEV, generator=_g(45))[:T].int()
+    q = ops.rope_kv_write(qkv, pos, cs, cache, slots, H, Hk, D, bias=b, q_norm=qn, k_norm=kn, norm_eps=1e-6)
+    cache_ref = torch.zeros_like(cache).float().cpu()
+    qr = R.rope_kv_write(qkv.float().cpu(), pos.cpu(), cs.cpu(), cache_ref, slots.cpu(), H, Hk, D,
+                         None if b is None else b.float().cpu(), None if qn is None else qn.float().cpu(),
+                         None if kn is None else kn.float().cpu(), 1e-6)
+    torch.testing.assert_close(q.float().cpu(), qr.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(cache.float().cpu(), cache_ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(7, 512, 256), (300, 2048, 1024), (1024, 6144, 4096)])
+@pytest.mark.parametrize("splits", [1, 2])
+def test_gemm_geglu(M, N, K, splits):
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(50)))
+    w = bf(torch.randn(N, K, device=DEV, generator=_g(51)) * 0.05)
+    out = torch.empty(M, N // 2, device=DEV, dtype=torch.bfloat16)
+    ws = torch.empty(splits * M * N, device=DEV)
+    ops.cuda_ext().gemm_bf16(out, a, w, None, ops.EPI_GEGLU, 0, None, 0, splits, ws)
+    ref = R.gemm_swiglu(a.float().cpu(), w.float().cpu(), 64, "gelu_tanh")
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_embedding_scale():
+    table = bf(torch.randn(100, 256, device=DEV, generator=_g(60)))
+    ids = torch.tensor([3, 99, 0, 42], dtype=torch.int32, device=DEV)
+    out = ops.embedding(ids, table, scale=16.0)
+    torch.testing.assert_close(out.float(), table[ids.long()].float() * 16.0, rtol=1e-2, atol=1e-2)
