@@ -7,6 +7,7 @@ torch::Tensor quantize_q4_k(torch::Tensor x);
 torch::Tensor dequantize_q4_k(torch::Tensor raw, int64_t n);
 void register_block_allocator(pybind11::module& m);
 void register_forelen(pybind11::module& m);
+void register_spec(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "gollek_b200 host runtime";
@@ -16,4 +17,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequantize_q4_k", &dequantize_q4_k);
   register_block_allocator(m);
   register_forelen(m);
+  register_spec(m);
 }

@@ -401,6 +401,12 @@ class EngineConfig:
     device: str = "cuda"
     tensor_parallel_size: int = 1
     enable_expert_parallel: bool = False  # MoE: experts partitioned over the TP ranks (EP = TP size)
+    # speculative decoding: "none" | "ngram" (prompt lookup) | "draft" (draft model ``draft_model``)
+    speculative_method: str = "none"
+    num_speculative_tokens: int = 4
+    ngram_min: int = 1
+    ngram_max: int = 4
+    draft_model: Optional[str] = None
     expert_parallel_size: int = 1
     # paged KV cache
     block_size: int = 16

@@ -73,6 +73,9 @@ class LLMEngine:
             nb = int(t)
         self.num_blocks = nb
         self.kv_cache = allocate_kv_cache(self.model.kv_cache_shape(nb, cfg.block_size), self.dtype, self.device)
+        if cfg.speculative_method == "draft" and cfg.enable_prefix_caching:
+            # a reused prefix block may carry target KV whose draft-model KV was never computed
+            cfg.enable_prefix_caching = False
         self.kv = KVCacheManager(nb, cfg.block_size, cfg.enable_prefix_caching)
         predictor = None
         if cfg.scheduling_policy == "wait":
@@ -86,6 +89,19 @@ class LLMEngine:
         self.seqs: Dict[str, Sequence] = {}
         self.metrics = EngineMetrics()
         self.eos_token_id = model_cfg.eos_token_id
+        # ---- speculative decoding
+        from .speculative import DraftModelProposer, NgramProposer, SpecStats
+        self.spec = None
+        self.spec_stats = SpecStats()
+        if cfg.speculative_method == "ngram":
+            self.spec = NgramProposer(cfg.num_speculative_tokens, cfg.ngram_min, cfg.ngram_max)
+        elif cfg.speculative_method == "draft":
+            if not cfg.draft_model:
+                raise ValueError("speculative_method 'draft' needs draft_model")
+            dcfg, dw, _ = load_model_source(cfg.draft_model)
+            self.spec = DraftModelProposer(self, dcfg, dw, cfg.num_speculative_tokens)
+        elif cfg.speculative_method != "none":
+            raise ValueError(f"unknown speculative_method {cfg.speculative_method!r}")
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: Optional[str], prompt: Union[str, List[int]],
@@ -129,6 +145,8 @@ class LLMEngine:
     def abort_request(self, request_id: str) -> bool:
         seq = self.scheduler.abort(request_id)
         self.seqs.pop(request_id, None)
+        if seq is not None and self.spec is not None and hasattr(self.spec, "forget"):
+            self.spec.forget(seq)
         return seq is not None
 
     def has_unfinished(self) -> bool:
@@ -157,12 +175,42 @@ class LLMEngine:
             return SeqStatus.FINISHED_LENGTH
         return None
 
+    def _speculate(self, sched) -> None:
+        """Turn decode chunks into verify chunks ``[last] + drafts`` where the proposer has drafts."""
+        from .scheduler import ScheduledChunk
+        K = self.cfg.num_speculative_tokens
+        seqs, ks = [], []
+        for c in sched.decode:
+            s = c.seq
+            room = min(s.params.max_tokens - len(s.output_token_ids), self.cfg.max_model_len - s.num_tokens) - 1
+            k = 0 if s.params.needs_penalties else max(0, min(K, room))
+            if k and not self.kv.ensure(s, s.num_tokens + k):
+                k = 0
+            seqs.append(s)
+            ks.append(k)
+        drafts = self.spec.propose(seqs, ks)
+        keep, verify = [], []
+        for c, d in zip(sched.decode, drafts):
+            if d:
+                last = c.seq.tokens(c.start, c.start + 1)
+                verify.append(ScheduledChunk(c.seq, c.start, 1 + len(d), True, tokens=list(last) + list(d),
+                                             verify=len(d)))
+                self.spec_stats.proposed += len(d)
+            else:
+                keep.append(c)
+        if verify:
+            self.spec_stats.steps += 1
+            sched.decode = keep
+            sched.prefill = verify + sched.prefill
+
     def step(self) -> List[RequestOutput]:
-        """One scheduler iteration: schedule, run the model, append tokens, retire finished."""
+        """One scheduler iteration: schedule, (draft,) run the model, append tokens, retire finished."""
         sched = self.scheduler.schedule()
         if sched.empty:
             return []
         t0 = time.perf_counter()
+        if self.spec is not None and sched.decode:
+            self._speculate(sched)
         sampled = self.runner.execute(sched)
         now = time.perf_counter()
         outputs: List[RequestOutput] = []
@@ -170,28 +218,43 @@ class LLMEngine:
         n_new = 0
         for c in sched.chunks:
             seq = c.seq
-            seq.num_computed_tokens = c.start + c.num_tokens
+            new = sampled[k] if c.sample else []
+            if c.verify:  # KV is valid for the last token and the accepted drafts
+                seq.num_computed_tokens = c.start + len(new)
+                self.spec_stats.accepted += len(new) - 1
+                if hasattr(self.spec, "accepted"):
+                    self.spec.accepted(seq)
+            else:
+                seq.num_computed_tokens = c.start + c.num_tokens
             self.kv.commit_full_blocks(seq)
             if not c.sample:
                 continue
-            tok = int(sampled[k])
             k += 1
-            seq.output_token_ids.append(tok)
-            seq.token_times.append(now)
-            n_new += 1
-            if seq.first_token_time is None:
-                seq.first_token_time = now
-            status = self._check_stop(seq, tok)
+            status = None
+            appended = []
+            for tok in new:
+                tok = int(tok)
+                seq.output_token_ids.append(tok)
+                seq.token_times.append(now)
+                appended.append(tok)
+                n_new += 1
+                if seq.first_token_time is None:
+                    seq.first_token_time = now
+                status = self._check_stop(seq, tok)
+                if status is not None:
+                    break
             finished = status is not None
             if finished:
                 seq.finish_time = now
                 self.scheduler.finish(seq, status)
                 self.seqs.pop(seq.request_id, None)
                 self.metrics.on_finish(seq)
+                if self.spec is not None and hasattr(self.spec, "forget"):
+                    self.spec.forget(seq)
             text = ""
             if self.tokenizer is not None and finished:
                 text = seq.output_text or self.tokenizer.decode(seq.output_token_ids)
-            outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, [tok],
+            outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, appended,
                                          finished, status.value if status else None, text))
         self.metrics.on_step(now - t0, sched.num_tokens, n_new, len(self.scheduler.running),
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))

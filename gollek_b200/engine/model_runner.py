@@ -28,8 +28,9 @@ from .sequence import Sequence
 class _Pinned:
     """Reusable pinned host staging buffers for one step."""
 
-    def __init__(self, max_tokens: int, max_seqs: int, max_blocks: int, pin: bool):
+    def __init__(self, max_tokens: int, max_seqs: int, max_blocks: int, pin: bool, max_rows: int = 0):
         kw = dict(pin_memory=pin)
+        max_rows = max(max_rows, max_seqs)
         self.input_ids = torch.zeros(max_tokens, dtype=torch.int32, **kw)
         self.positions = torch.zeros(max_tokens, dtype=torch.int32, **kw)
         self.slots = torch.zeros(max_tokens, dtype=torch.int32, **kw)
@@ -39,8 +40,8 @@ class _Pinned:
         self.seq_ids = torch.zeros(max_seqs, dtype=torch.int64)
         self.start = torch.zeros(max_seqs, dtype=torch.int32)
         self.n_new = torch.zeros(max_seqs, dtype=torch.int32)
-        self.logits_idx = torch.zeros(max_seqs, dtype=torch.int64, **kw)
-        self.sampled = torch.zeros(max_seqs, dtype=torch.int64, **kw)
+        self.logits_idx = torch.zeros(max_rows, dtype=torch.int64, **kw)
+        self.sampled = torch.zeros(max_rows, dtype=torch.int64, **kw)
 
 
 class _DecodeGraph:
@@ -68,8 +69,12 @@ class ModelRunner:
         self.is_cuda = self.device.type == "cuda"
         self.block_size = cfg.block_size
         self.max_blocks = (cfg.max_model_len + cfg.block_size - 1) // cfg.block_size
-        max_tokens = cfg.max_num_batched_tokens + cfg.max_num_seqs
-        self.host = _Pinned(max_tokens, cfg.max_num_seqs, self.max_blocks, self.is_cuda)
+        k_spec = cfg.num_speculative_tokens if cfg.speculative_method != "none" else 0
+        max_tokens = cfg.max_num_batched_tokens + cfg.max_num_seqs * (1 + k_spec)
+        self.host = _Pinned(max_tokens, cfg.max_num_seqs, self.max_blocks, self.is_cuda,
+                            max_rows=cfg.max_num_seqs * (1 + k_spec))
+        self.spec_step = 0
+        self.greedy_only = False  # draft-model runners: always argmax (deterministic proposals)
         self.graphs: Dict[int, _DecodeGraph] = {}
         self.graph_pool = None
         self.step_counter = 0
@@ -80,6 +85,8 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ batch preparation
     def _fill_host(self, out: SchedulerOutput) -> Tuple[int, int, List[Sequence], List[int]]:
+        """Stage the step's inputs. Logits rows: one per sampled chunk, ``verify + 1`` for a
+        speculative verify chunk (predictions after the last token and after each draft)."""
         chunks = out.chunks
         n = len(chunks)
         h = self.host
@@ -91,11 +98,11 @@ class ModelRunner:
             h.seq_ids[i] = c.seq.seq_id
             h.start[i] = c.start
             h.n_new[i] = c.num_tokens
-            toks = c.seq.tokens(c.start, c.start + c.num_tokens)
+            toks = c.tokens if c.tokens is not None else c.seq.tokens(c.start, c.start + c.num_tokens)
             ids[t:t + c.num_tokens] = toks
             t += c.num_tokens
             if c.sample:
-                sample_rows.append(t - 1)
+                sample_rows.extend(range(t - 1 - c.verify, t))
                 sample_seqs.append(c.seq)
         T = self.kv.tables.build_batch(h.seq_ids[:n], h.start[:n], h.n_new[:n], h.positions, h.slots,
                                        h.block_tables[:n], h.seq_lens[:n], h.query_start[: n + 1])
@@ -108,8 +115,9 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ execution
     @torch.inference_mode()
-    def execute(self, out: SchedulerOutput) -> List[int]:
-        """Run one step; returns the sampled token for every chunk with ``sample`` set (in order)."""
+    def execute(self, out: SchedulerOutput) -> List[List[int]]:
+        """Run one step; returns, for every chunk with ``sample`` set (in order), its new tokens: one
+        sampled token, or for a speculative verify chunk the accepted drafts plus one."""
         self.step_counter += 1
         n, T, sample_seqs, sample_rows = self._fill_host(out)
         if self.timer is not None:
@@ -121,7 +129,7 @@ class ModelRunner:
                 self.timer.end()
 
     def _execute(self, out: SchedulerOutput, n: int, T: int, sample_seqs: List[Sequence],
-                 sample_rows: List[int]) -> List[int]:
+                 sample_rows: List[int]) -> List[List[int]]:
         nd = len(out.decode)
         h = self.host
         dev = self.device
@@ -132,10 +140,10 @@ class ModelRunner:
                 ids.extend([c.seq.lora_id] * c.num_tokens)
             lora.set_batch(ids)
         lora_active = lora is not None and lora.active
-        all_greedy = all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
+        all_greedy = self.greedy_only or all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
         if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0 and not lora_active
-                and self._graph_for(nd) is not None):
-            return self._replay_decode(nd)
+                and all(c.verify == 0 for c in out.decode) and self._graph_for(nd) is not None):
+            return [[t] for t in self._replay_decode(nd)]
         nb = int(max(1, (int(h.seq_lens[:n].max()) + self.block_size - 1) // self.block_size))
         self.h2d_bytes += 4 * (3 * T + n * self.max_blocks + n + (n - nd + 1)) + 8 * max(1, len(sample_rows))
         self.d2h_bytes += 8 * len(sample_rows)
@@ -165,8 +173,34 @@ class ModelRunner:
             return []
         meta.logits_indices = h.logits_idx[:ns].to(dev, non_blocking=True)
         logits = self.model.forward(input_ids, meta, self.kv_cache)
-        ids = self.sample(logits, sample_seqs)
-        return ids
+        sampled = [c for c in out.chunks if c.sample]
+        if all(c.verify == 0 for c in sampled):
+            return [[t] for t in self.sample(logits, sample_seqs)]
+        # speculative verify chunks next to ordinary ones: split the logits rows
+        from .speculative import accept_drafts
+        plain_rows, ver_rows, plain_seqs, ver_chunks = [], [], [], []
+        r = 0
+        for c in sampled:
+            if c.verify:
+                ver_rows.extend(range(r, r + c.verify + 1))
+                ver_chunks.append(c)
+            else:
+                plain_rows.append(r)
+                plain_seqs.append(c.seq)
+            r += c.verify + 1
+        plain = self.sample(logits[plain_rows], plain_seqs) if plain_rows else []
+        self.spec_step += 1
+        acc = accept_drafts(logits[ver_rows], ver_chunks, [c.seq for c in ver_chunks], self.cfg.seed,
+                            self.spec_step)
+        res, pi, vi = [], 0, 0
+        for c in sampled:
+            if c.verify:
+                res.append(acc[vi])
+                vi += 1
+            else:
+                res.append([plain[pi]])
+                pi += 1
+        return res
 
     @torch.inference_mode()
     def run_hidden(self, out: SchedulerOutput) -> torch.Tensor:
@@ -187,7 +221,7 @@ class ModelRunner:
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
         dev = logits.device
         ns = len(seqs)
-        if all(s.params.greedy and not s.params.needs_penalties for s in seqs):
+        if self.greedy_only or all(s.params.greedy and not s.params.needs_penalties for s in seqs):
             out = ops.argmax(logits)
         else:
             lf = logits.float()

@@ -39,6 +39,10 @@ class ScheduledChunk:
     start: int          # first absolute position processed this step
     num_tokens: int     # tokens processed this step
     sample: bool        # produce a token at the end of this chunk
+    # speculative decoding: input tokens that are not (yet) the sequence's own (drafts), and the
+    # number of trailing draft tokens whose verification needs logits at every position
+    tokens: Optional[List[int]] = None
+    verify: int = 0
 
 
 @dataclass

@@ -48,6 +48,7 @@ HOST_SOURCES = [
     "host/gguf_quant.cpp",
     "host/block_allocator.cpp",
     "host/forelen.cpp",
+    "host/spec_ngram.cpp",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -258,6 +258,33 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     return out
 
 
+def filtered_probs(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+                   min_p: torch.Tensor) -> torch.Tensor:
+    """The distribution ``sample`` draws from, for every row at once (rows with temperature > 0):
+    softmax((x - max) / T) restricted to the top-k, then min-p, then renormalised top-p survivors.
+    Used by speculative decoding to accept or resample draft tokens exactly."""
+    lf = logits.float()
+    B, V = lf.shape
+    t = temperature.float().clamp_min(1e-6)[:, None]
+    m = lf.max(-1, keepdim=True).values
+    keep = torch.ones_like(lf, dtype=torch.bool)
+    k = top_k.long()
+    kk = torch.where((k > 0) & (k < V), k, torch.full_like(k, V))
+    kth = lf.sort(-1, descending=True).values.gather(1, (kk - 1)[:, None])
+    keep &= lf >= kth
+    mp = min_p.float()[:, None]
+    keep &= torch.where(mp > 0, lf >= m + t * torch.log(mp.clamp_min(1e-30)), torch.ones_like(keep))
+    w = torch.exp((lf - m) / t) * keep
+    sw, _ = w.sort(dim=-1, descending=True, stable=True)
+    cum = sw.cumsum(-1)
+    target = top_p.float()[:, None] * cum[:, -1:]
+    n_keep = (cum < target).sum(-1, keepdim=True) + 1
+    thr = sw.gather(1, (n_keep.clamp_max(V) - 1))
+    keep &= torch.where(top_p.float()[:, None] < 1.0, w >= thr, torch.ones_like(keep))
+    w = w * keep
+    return w / w.sum(-1, keepdim=True)
+
+
 def attention_dense(q, k, v, causal=True, scale=None):
     """Dense GQA attention, q [S,H,D], k/v [S,Hk,D] (test helper)."""
     S, H, D = q.shape
