@@ -277,6 +277,22 @@ std::vector<int64_t> moe_plan_py(int64_t T, int64_t topk, int64_t E, int64_t e_l
   return {a, b, c};
 }
 
+// cache [L, NB, 2, Hk, bs, D] bf16; packed [L, n, 2, Hk, bs, D] bf16; block_ids int32 [n] (device)
+void kv_blocks_py(torch::Tensor cache, torch::Tensor packed, torch::Tensor block_ids, bool gather) {
+  check_bf16(cache, "kv_cache");
+  check_bf16(packed, "packed");
+  check_i32(block_ids, "block_ids");
+  check_same_device(cache, packed);
+  TORCH_CHECK(cache.is_contiguous() && packed.is_contiguous() && cache.dim() == 6 && packed.dim() == 6,
+              "kv transfer: contiguous [L, blocks, 2, Hk, bs, D] tensors");
+  const int n = block_ids.numel();
+  TORCH_CHECK(packed.size(0) == cache.size(0) && packed.size(1) == n, "kv transfer: packed [L, n, ...]");
+  for (int d = 2; d < 6; ++d) TORCH_CHECK(packed.size(d) == cache.size(d), "kv transfer: block shape mismatch");
+  const int64_t span = cache.numel() / (cache.size(0) * cache.size(1));
+  launch_kv_blocks(cache.data_ptr(), packed.data_ptr(), block_ids.data_ptr<int>(), n, cache.size(0), cache.size(1),
+                   span, gather, cur_stream());
+}
+
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
   int bn = 0, sp = 1;
   gemm_plan((int)M, (int)N, (int)K, (int)epi, bn, sp);
@@ -497,6 +513,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("num_sms", &device_num_sms);
   m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)");
   m.def("moe_capacity_rows", &moe_capacity_rows);
+  m.def("kv_blocks", &kv_blocks_py, "gather (or scatter) one sequence's paged KV blocks, every layer");
   m.def("moe_ws_ints", &moe_ws_ints);
   m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");
   m.def("argmax", &argmax_out, "greedy argmax (K11)");

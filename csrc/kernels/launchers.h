@@ -76,6 +76,10 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
                         float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,
                         uint32_t* status, cudaStream_t s);
 
+// ---- KV block transfer (P/D disaggregation): packed [L, n, span] <-> cache [L, NB, span]
+void launch_kv_blocks(void* cache, void* packed, const int* block_ids, int n, int layers, int64_t num_blocks,
+                      int64_t span, bool gather, cudaStream_t s);
+
 // ---- sampling (K11)
 void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s);
 void launch_penalties(float* logits, int64_t stride, const int* triples, int n, const float* rep, const float* freq,

@@ -89,6 +89,9 @@ class LLMEngine:
         self.seqs: Dict[str, Sequence] = {}
         self.metrics = EngineMetrics()
         self.eos_token_id = model_cfg.eos_token_id
+        # prefill/decode disaggregation: called after a sequence's first token on a prefill engine;
+        # returning True means its KV was handed to a decode engine (engine.disagg)
+        self.handoff_hook = None
         # ---- speculative decoding
         from .speculative import DraftModelProposer, NgramProposer, SpecStats
         self.spec = None
@@ -243,6 +246,9 @@ class LLMEngine:
                 status = self._check_stop(seq, tok)
                 if status is not None:
                     break
+            if (self.handoff_hook is not None and len(seq.output_token_ids) == 1
+                    and status in (None, SeqStatus.FINISHED_LENGTH) and self.handoff_hook(seq)):
+                status = SeqStatus.FINISHED_HANDOFF
             finished = status is not None
             if finished:
                 seq.finish_time = now

@@ -66,10 +66,12 @@ class SeqStatus(enum.Enum):
     FINISHED_STOPPED = "stop"
     FINISHED_LENGTH = "length"
     FINISHED_ABORTED = "abort"
+    FINISHED_HANDOFF = "handoff"  # prefill node: KV and first token handed to a decode node
 
     @property
     def finished(self) -> bool:
-        return self in (SeqStatus.FINISHED_STOPPED, SeqStatus.FINISHED_LENGTH, SeqStatus.FINISHED_ABORTED)
+        return self in (SeqStatus.FINISHED_STOPPED, SeqStatus.FINISHED_LENGTH, SeqStatus.FINISHED_ABORTED,
+                        SeqStatus.FINISHED_HANDOFF)
 
 
 _seq_counter = itertools.count()

@@ -42,6 +42,7 @@ CUDA_SOURCES = [
     "kernels/gemm_fp8.cu",
     "kernels/attention_tc.cu",
     "kernels/moe.cu",
+    "kernels/kv_transfer.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

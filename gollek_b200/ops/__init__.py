@@ -438,3 +438,23 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
                   top_k, renorm, e0, e_loc)
     LAUNCHES.add(6)
     return out
+
+
+# ---------------------------------------------------------------------------- KV block transfer
+def kv_gather_blocks(cache: torch.Tensor, block_ids: torch.Tensor) -> torch.Tensor:
+    """packed [L, n, 2, Hk, bs, D] = cache[:, block_ids] (P/D hand-off of one sequence's KV)."""
+    if not cache.is_cuda:
+        return cache[:, block_ids.long()].contiguous()
+    L = cache.shape[0]
+    packed = torch.empty(L, block_ids.numel(), *cache.shape[2:], dtype=cache.dtype, device=cache.device)
+    _C().kv_blocks(cache, packed, block_ids.to(cache.device, torch.int32), True)
+    return packed
+
+
+def kv_scatter_blocks(cache: torch.Tensor, block_ids: torch.Tensor, packed: torch.Tensor) -> None:
+    """cache[:, block_ids] = packed (the receiving side of a hand-off)."""
+    if not cache.is_cuda:
+        cache[:, block_ids.long()] = packed.to(cache.dtype)
+        return
+    _C().kv_blocks(cache, packed.to(cache.device, cache.dtype).contiguous(), block_ids.to(cache.device, torch.int32),
+                   False)
