@@ -90,6 +90,27 @@ class BlockPool {
     has_hash_[b] = 1;
   }
 
+  // Every cached (hash, block) pair (prefix-cache snapshot).
+  std::vector<std::pair<int64_t, int32_t>> cached_items() const {
+    return std::vector<std::pair<int64_t, int32_t>>(map_.begin(), map_.end());
+  }
+
+  // Take a free block, register it under `h` as a cached block with no owner (evictable, LRU
+  // tail) and return it, so a snapshot's KV can be written into it; -1 if the hash is already
+  // cached or no block is free (cached blocks are never evicted for this).
+  int32_t adopt_cached(int64_t h) {
+    if (map_.count(h) || free_.empty()) return -1;
+    const int32_t b = free_.back();
+    free_.pop_back();
+    map_[h] = b;
+    hash_[b] = h;
+    has_hash_[b] = 1;
+    ref_[b] = 0;
+    lru_.push_back(b);
+    lru_pos_[b] = std::prev(lru_.end());
+    return b;
+  }
+
   void reset_cache() {
     for (int32_t b : lru_) {
       has_hash_[b] = 0;
@@ -234,7 +255,9 @@ void register_block_allocator(pybind11::module& m) {
       .def("lookup", &BlockPool::lookup)
       .def("contains", &BlockPool::contains)
       .def("insert", &BlockPool::insert)
-      .def("reset_cache", &BlockPool::reset_cache);
+      .def("reset_cache", &BlockPool::reset_cache)
+      .def("cached_items", &BlockPool::cached_items)
+      .def("adopt_cached", &BlockPool::adopt_cached);
   py::class_<SeqTables>(m, "SeqTables")
       .def(py::init<BlockPool*>(), py::keep_alive<1, 2>())
       .def("add", &SeqTables::add)

@@ -407,6 +407,10 @@ class EngineConfig:
     ngram_min: int = 1
     ngram_max: int = 4
     draft_model: Optional[str] = None
+    # checkpoint / resume: prefix-cache snapshot and unfinished-request snapshot paths (written at
+    # shutdown, read at startup when present)
+    prefix_cache_snapshot: Optional[str] = None
+    request_snapshot: Optional[str] = None
     expert_parallel_size: int = 1
     # paged KV cache
     block_size: int = 16

@@ -105,6 +105,15 @@ class LLMEngine:
             self.spec = DraftModelProposer(self, dcfg, dw, cfg.num_speculative_tokens)
         elif cfg.speculative_method != "none":
             raise ValueError(f"unknown speculative_method {cfg.speculative_method!r}")
+        # ---- resume from a previous run's snapshots
+        import os as _os
+        if cfg.prefix_cache_snapshot and _os.path.exists(cfg.prefix_cache_snapshot):
+            self.load_prefix_cache(cfg.prefix_cache_snapshot)
+        if cfg.request_snapshot and _os.path.exists(cfg.request_snapshot):
+            import json as _json
+            with open(cfg.request_snapshot) as f:
+                self.restore_requests(_json.load(f))
+            _os.remove(cfg.request_snapshot)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: Optional[str], prompt: Union[str, List[int]],
@@ -265,6 +274,23 @@ class LLMEngine:
         self.metrics.on_step(now - t0, sched.num_tokens, n_new, len(self.scheduler.running),
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
         return outputs
+
+    # ------------------------------------------------------------------ checkpoint / resume
+    def save_prefix_cache(self, path: str, max_blocks: int = 0) -> int:
+        from .persistence import save_prefix_cache
+        return save_prefix_cache(self, path, max_blocks)
+
+    def load_prefix_cache(self, path: str) -> int:
+        from .persistence import load_prefix_cache
+        return load_prefix_cache(self, path)
+
+    def snapshot_requests(self) -> List[dict]:
+        from .persistence import snapshot_requests
+        return snapshot_requests(self)
+
+    def restore_requests(self, reqs: List[dict]) -> List[str]:
+        from .persistence import restore_requests
+        return restore_requests(self, reqs)
 
     def embed(self, token_lists: List[List[int]]) -> List[List[float]]:
         """Mean-pooled, L2-normalised final hidden states (one prefill pass per input, KV blocks

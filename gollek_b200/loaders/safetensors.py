@@ -75,7 +75,10 @@ class SafetensorsFile:
     def close(self):
         self._buf = None
         if self._mm is not None:
-            self._mm.close()
+            try:
+                self._mm.close()
+            except BufferError:  # tensors still view the mapping: it is released with them
+                pass
         self._f.close()
 
 

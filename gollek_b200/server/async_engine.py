@@ -59,6 +59,17 @@ class AsyncEngine:
         self._subs.put(None)
         if self._thread is not None:
             self._thread.join(timeout=5)
+        # checkpoint what a restart can reuse (engine thread has stopped: safe to touch the engine)
+        cfg = self.engine.cfg
+        if getattr(cfg, "prefix_cache_snapshot", None):
+            try:
+                self.engine.save_prefix_cache(cfg.prefix_cache_snapshot)
+            except Exception as e:  # a failed snapshot must not block shutdown
+                self.error = self.error or e
+        if getattr(cfg, "request_snapshot", None):
+            import json
+            with open(cfg.request_snapshot, "w") as f:
+                json.dump(self.engine.snapshot_requests(), f)
 
     @property
     def healthy(self) -> bool:
