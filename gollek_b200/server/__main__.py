@@ -23,6 +23,11 @@ def main(argv=None):
     ap.add_argument("--max-model-len", type=int, default=None)
     ap.add_argument("--max-num-seqs", type=int, default=None)
     ap.add_argument("--rate-limit", type=float, default=0.0, help="requests/s per API key (0 = off)")
+    ap.add_argument("--tensor-parallel-size", type=int, default=None)
+    ap.add_argument("--comm", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--speculative-method", choices=["none", "ngram", "draft"], default=None)
+    ap.add_argument("--draft-model", default=None)
+    ap.add_argument("--enable-expert-parallel", action="store_true")
     args = ap.parse_args(argv)
     import uvicorn
     from ..config import EngineConfig
@@ -35,8 +40,20 @@ def main(argv=None):
             over[k] = getattr(args, k)
     if args.device == "cpu":
         over.update(dtype="float32", use_cuda_graphs=False)
+    for k in ("speculative_method", "draft_model"):
+        if getattr(args, k) is not None:
+            over[k] = getattr(args, k)
+    if args.enable_expert_parallel:
+        over["enable_expert_parallel"] = True
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.tensor_parallel_size is not None and args.tensor_parallel_size != world:
+        raise SystemExit(f"--tensor-parallel-size {args.tensor_parallel_size} needs torchrun with "
+                         f"--nproc-per-node {args.tensor_parallel_size} (WORLD_SIZE={world})")
+    over["tensor_parallel_size"] = world
     cfg = EngineConfig.load(args.config, **over)
     keys = args.api_key or [k for k in os.environ.get("GOLLEK_API_KEYS", "").split(",") if k]
+    if world > 1:
+        return _serve_tp(args, cfg, keys)
     ae = AsyncEngine(LLMEngine(cfg)).start()
     app = create_app(ae, model_name=args.served_model_name or os.path.basename(args.model.rstrip("/")),
                      api_keys=keys, rate=args.rate_limit)
@@ -44,6 +61,46 @@ def main(argv=None):
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:
         ae.shutdown(drain=True)
+
+
+def _serve_tp(args, cfg, keys):
+    """One process per GPU: rank 0 serves HTTP through a DriverEngine that publishes every step's
+    request events; the other ranks follow those events in lock-step."""
+    import torch.distributed as dist
+    import uvicorn
+    from ..engine.engine import LLMEngine
+    from ..parallel.control import ControlPlane, DriverEngine, follow
+    from ..parallel.dist import NcclComm, cpu_group, init_distributed
+    from .app import create_app
+    from .async_engine import AsyncEngine
+    from ..engine.engine import load_model_source
+    di = init_distributed(timeout_s=120)
+    mc, weights, tok = load_model_source(str(cfg.model), keep_quantized=cfg.quantization == "gguf")
+    if args.comm == "fused" and cfg.device != "cpu":
+        from ..parallel.symm import FusedTPComm
+        comm = FusedTPComm(di.rank, di.world_size, max_tokens=cfg.max_num_batched_tokens + cfg.max_num_seqs,
+                           hidden=mc.hidden_size, cpu_group=cpu_group())
+    else:
+        comm = NcclComm(di.rank, di.world_size)
+    engine = LLMEngine(cfg, model_cfg=mc, weights=weights, comm=comm, tokenizer=tok)
+    store = dist.distributed_c10d._get_default_store()
+    cp = ControlPlane(di.rank, di.world_size, store, timeout_s=3600.0).start_heartbeat()
+    try:
+        if di.rank != 0:
+            follow(engine, cp)
+            return
+        drv = DriverEngine(engine, cp)
+        ae = AsyncEngine(drv).start()
+        app = create_app(ae, model_name=args.served_model_name or os.path.basename(str(args.model).rstrip("/")),
+                         api_keys=keys, rate=args.rate_limit)
+        try:
+            uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+        finally:
+            ae.shutdown(drain=True)
+            drv.shutdown_workers()
+    finally:
+        cp.stop()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
