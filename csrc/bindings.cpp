@@ -370,6 +370,35 @@ void tp_ar_rmsnorm_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int
                        cur_stream());
 }
 
+// Row-parallel GEMM with the push epilogue: out = a · bᵀ ([T, N], this rank's inbox slot, a view of
+// the symmetric region) plus the same tiles into every peer's inbox and per-tile ready flags.
+void gemm_push_py(torch::Tensor out, torch::Tensor a, torch::Tensor b, int64_t bn, std::vector<uint64_t> bases,
+                  int64_t rank, int64_t inbox_off, int64_t slot_elems, int64_t flags_off, int64_t g_max,
+                  int64_t nt_max) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(out, "out");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
+              "push gemm: K-major operands");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == a.size(0) && out.size(1) == b.size(0), "push gemm: out [T, N]");
+  launch_gemm_push(out.data_ptr(), a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a.size(0), b.size(0),
+                   a.size(1), (int)bn, bases, (int)rank, inbox_off, slot_elems, flags_off, (int)g_max, (int)nt_max,
+                   nullptr, cur_stream());
+}
+
+void tp_push_ar_rmsnorm_py(std::vector<uint64_t> bases, int64_t rank, int64_t inbox_off, int64_t slot_elems,
+                           int64_t flags_off, int64_t g_max, int64_t nt_max, int64_t nt, torch::Tensor residual,
+                           torch::Tensor w, torch::Tensor x_out, double eps, double timeout_s, int64_t grid) {
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  check_bf16(x_out, "x_out");
+  TORCH_CHECK(residual.is_contiguous() && x_out.is_contiguous() && residual.sizes() == x_out.sizes(),
+              "residual / x_out must be contiguous [T, d]");
+  launch_tp_push_ar_rmsnorm(bases, (int)rank, inbox_off, slot_elems, flags_off, (int)g_max, (int)nt_max, (int)nt,
+                            residual.data_ptr(), w.data_ptr(), x_out.data_ptr(), residual.size(0), residual.size(1),
+                            (float)eps, timeout_s, (int)grid, cur_stream());
+}
+
 void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int64_t p1, int64_t parity,
                      torch::Tensor out, double timeout_s, int64_t grid) {
   check_bf16(out, "out");
@@ -499,6 +528,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_status", &symm_status_py);
   m.def("tp_allreduce_add_rmsnorm", &tp_ar_rmsnorm_py, "fused TP all-reduce + residual add + RMSNorm over P2P");
   m.def("tp_allreduce", &tp_allreduce_py, "TP all-reduce over P2P");
+  m.def("gemm_push", &gemm_push_py, "row-parallel tcgen05 GEMM pushing its tiles to every rank's inbox (C1)");
+  m.def("tp_push_allreduce_add_rmsnorm", &tp_push_ar_rmsnorm_py,
+        "reduce pushed partials from local memory + residual + RMSNorm (C1 consumer)");
   m.doc() = "gollek_b200 sm_100a kernels";
   m.def("rms_norm", &rms_norm_out, "RMSNorm (K1)");
   m.def("fused_add_rms_norm", &fused_add_rms_norm_out, "residual add + RMSNorm (K1)");

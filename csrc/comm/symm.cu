@@ -24,21 +24,11 @@
 // TMA on peer memory: plain ld/st.global over NVLink.
 #include "../common/common.cuh"
 #include "../kernels/launchers.h"
+#include "push.h"
 
 #include <vector>
 
 namespace gollek {
-
-// Header at the start of every rank's region (peers write into it).
-struct SymmHeader {
-  uint32_t flag_a[16];   // flag_a[src] = epoch when rank src entered call `epoch`
-  uint32_t flag_b[16];   // flag_b[src] = epoch when rank src finished phase 1
-  uint32_t arrive;       // local CTA arrive counter for barrier B
-  uint32_t epoch;        // last completed call
-  uint32_t status;       // kStatus* bits
-  uint32_t pad[29];
-};
-static_assert(sizeof(SymmHeader) == 256, "header size");
 
 constexpr int kArThreads = 512;
 
@@ -212,6 +202,95 @@ __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __n
   }
 }
 
+// Consumer of the push path: the row-parallel GEMM of every rank already stored its partial
+// tiles into this rank's inbox and raised per-(source, 32-row group, n-tile) flags. For each row:
+// wait (bounded) for the flags of its group from every source, then residual + Σ_p inbox[p][row]
+// in rank order (identical on every rank) → new residual, RMSNorm → x. All reads are local.
+__global__ void __launch_bounds__(kArThreads) tp_push_ar_rmsnorm_kernel(PushArgs a, int nt, int T, int d, float eps,
+                                                                         uint64_t timeout_ns,
+                                                                         __nv_bfloat16* __restrict__ residual,
+                                                                         const __nv_bfloat16* __restrict__ w,
+                                                                         __nv_bfloat16* __restrict__ x_out) {
+  SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(a.bases[a.rank] + a.flags_off);
+  const __nv_bfloat16* inbox = reinterpret_cast<const __nv_bfloat16*>(a.bases[a.rank] + a.inbox_off);
+  __shared__ uint32_t s_epoch;
+  __shared__ float red[kArThreads / 32];
+  __shared__ int s_group;
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
+    s_group = -1;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int nvec = d / 8;
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const int g = row >> 5;
+    if (g != s_group) {  // uniform across the CTA
+      for (int i = threadIdx.x; i < a.world * nt; i += blockDim.x) {
+        const int p = i / nt, t = i % nt;
+        if (!wait_geq(flags + ((int64_t)p * a.g_max + g) * a.nt_max + t, epoch, timeout_ns))
+          atomicOr(&me->status, kStatusPeerTimeout);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) s_group = g;
+    }
+    const int64_t base = (int64_t)row * d;
+    float ss = 0.f;
+    float vals[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int v = threadIdx.x + k * kArThreads;
+      if (v < nvec) {
+        const int64_t off = base + v * 8;
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), vals[k]);
+        for (int p = 0; p < a.world; ++p) {
+          float t[8];
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(inbox + (int64_t)p * a.slot_elems + off), t);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vals[k][e] += t[e];
+        }
+        const uint4 packed = float_to_bf16x8(vals[k]);
+        bf16x8_to_float(packed, vals[k]);
+        *reinterpret_cast<uint4*>(residual + off) = packed;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += vals[k][e] * vals[k][e];
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kArThreads / 32 ? red[threadIdx.x] : 0.f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float rs = rsqrtf(red[0] / (float)d + eps);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int v = threadIdx.x + k * kArThreads;
+      if (v < nvec) {
+        float wf[8];
+        bf16x8_to_float(*reinterpret_cast<const uint4*>(w + v * 8), wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vals[k][e] = vals[k][e] * rs * wf[e];
+        *reinterpret_cast<uint4*>(x_out + base + v * 8) = float_to_bf16x8(vals[k]);
+      }
+    }
+  }
+  // the call is complete on this rank once every CTA got here
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&me->arrive, 1u);
+    if (prev == gridDim.x - 1) {
+      me->arrive = 0;
+      me->epoch = epoch;
+    }
+  }
+}
+
 // Plain all-reduce (sum) of the partial buffer into `out` (no residual / norm), one-shot.
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(ArArgs a, __nv_bfloat16* __restrict__ out,
                                                                   int64_t nvec_total) {
@@ -316,6 +395,29 @@ void launch_tp_allreduce(const std::vector<uint64_t>& bases, int rank, int64_t p
   ArArgs a = make_args(bases, rank, p0, p1, 0, 0, 0, parity, true, 0.f, timeout_s);
   tp_allreduce_kernel<<<grid, kArThreads, 0, s>>>(a, reinterpret_cast<__nv_bfloat16*>(out), numel / 8);
   check_launch("tp_allreduce");
+}
+
+void launch_tp_push_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
+                               int64_t flags_off, int g_max, int nt_max, int nt, void* residual, const void* w,
+                               void* x_out, int T, int d, float eps, double timeout_s, int grid, cudaStream_t s) {
+  throw_if(d % 8 != 0 || d > 16 * kArThreads, "tp push all-reduce: hidden size must be a multiple of 8, <= 8192");
+  throw_if(bases.empty() || bases.size() > 8, "tp push all-reduce: 1..8 ranks");
+  throw_if((T + 31) / 32 > g_max || nt > nt_max, "tp push all-reduce: flag array too small for this call");
+  if (T == 0) return;
+  PushArgs p{};
+  for (size_t i = 0; i < bases.size(); ++i) p.bases[i] = reinterpret_cast<uint8_t*>(bases[i]);
+  p.inbox_off = inbox_off;
+  p.slot_elems = slot_elems;
+  p.flags_off = flags_off;
+  p.world = (int)bases.size();
+  p.rank = rank;
+  p.g_max = g_max;
+  p.nt_max = nt_max;
+  tp_push_ar_rmsnorm_kernel<<<grid, kArThreads, 0, s>>>(p, nt, T, d, eps, (uint64_t)(timeout_s * 1e9),
+                                                        reinterpret_cast<__nv_bfloat16*>(residual),
+                                                        reinterpret_cast<const __nv_bfloat16*>(w),
+                                                        reinterpret_cast<__nv_bfloat16*>(x_out));
+  check_launch("tp_push_allreduce_add_rmsnorm");
 }
 
 uint32_t symm_read_status(void* base) {

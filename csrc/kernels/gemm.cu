@@ -21,6 +21,7 @@
 //
 // Every mbarrier wait is bounded (globaltimer deadline); on timeout the CTA records a status bit,
 // stops issuing, drains its own in-flight copies/MMAs (bounded) and frees its TMEM before returning.
+#include "../comm/push.h"
 #include "../common/common.cuh"
 #include "../common/tma_host.h"
 #include "launchers.h"
@@ -78,7 +79,8 @@ __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
                      int M, int N, int K, int group_m, int splits, float* __restrict__ partial,
-                     uint32_t* status, const int* __restrict__ tile_group, const int* __restrict__ num_m_dev) {
+                     uint32_t* status, const int* __restrict__ tile_group, const int* __restrict__ num_m_dev,
+                     const PushArgs push) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -230,6 +232,11 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int lg = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
+    // push epilogue: the epoch the consumer of this call will wait for (it increments on completion)
+    uint32_t push_epoch = 0;
+    if constexpr (EPI == kEpiPush)
+      push_epoch = *reinterpret_cast<volatile const uint32_t*>(
+                       &reinterpret_cast<const SymmHeader*>(push.bases[push.rank])->epoch) + 1;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int m0, n0, kb0, kb1;
       unit_coords(u, m0, n0, kb0, kb1);
@@ -305,9 +312,29 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                   for (int e = 0; e < 8; ++e) v[e] += rr[e];
                 }
-                *reinterpret_cast<uint4*>(dst + 8 * j) = float_to_bf16x8(v);
+                const uint4 packed = float_to_bf16x8(v);
+                *reinterpret_cast<uint4*>(dst + 8 * j) = packed;
+                if constexpr (EPI == kEpiPush) {
+                  // the same bytes into this rank's slot of every peer's inbox (NVLink stores)
+                  const int64_t off = ((int64_t)push.rank * push.slot_elems + (int64_t)row * N + col + 8 * j) * 2;
+                  for (int p = 0; p < push.world; ++p) {
+                    if (p == push.rank) continue;
+                    *reinterpret_cast<uint4*>(push.bases[p] + push.inbox_off + off) = packed;
+                  }
+                }
               }
             }
+          }
+        }
+        if constexpr (EPI == kEpiPush) {
+          // publish this warp's 32 rows of the tile: every lane's stores ordered before the flags
+          __threadfence_system();
+          __syncwarp();
+          if (lane == 0) {
+            const int grp = (m0 >> 7) * 4 + lg;
+            const int64_t fi = ((int64_t)push.rank * push.g_max + grp) * push.nt_max + n0 / BN;
+            for (int p = 0; p < push.world; ++p)
+              st_release_sys(reinterpret_cast<uint32_t*>(push.bases[p] + push.flags_off) + fi, push_epoch);
           }
         }
       }
@@ -368,7 +395,7 @@ template <int BN, int EPI>
 void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
                    int64_t ldr, int M, int N, int K, int splits, float* partial, uint32_t* status, int grid_limit,
                    cudaStream_t s, const int* tile_group = nullptr, const int* num_m_dev = nullptr, int groups = 1,
-                   bool reduce = true) {
+                   bool reduce = true, const PushArgs* push = nullptr) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -385,7 +412,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
   kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
-                                     partial, status, tile_group, num_m_dev);
+                                     partial, status, tile_group, num_m_dev, push ? *push : PushArgs{});
   check_launch("gemm_bf16");
   if (splits > 1 && reduce) {
     const int out_n = (EPI == kEpiSwiglu || EPI == kEpiGeglu) ? N / 2 : N;
@@ -497,6 +524,34 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
   GOLLEK_GEMM_CASE(128, kEpiGeglu)
 #undef GOLLEK_GEMM_CASE
   throw_if(true, "gemm: unsupported tile width " + std::to_string(bn) + " / epilogue " + std::to_string(epi));
+}
+
+void launch_gemm_push(void* out, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int bn,
+                      const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
+                      int64_t flags_off, int g_max, int nt_max, uint32_t* status, cudaStream_t s) {
+  throw_if(K % 8 != 0 || N % 8 != 0, "push gemm: N and K must be multiples of 8");
+  throw_if(bases.empty() || bases.size() > 8 || rank < 0 || rank >= (int)bases.size(), "push gemm: 1..8 ranks");
+  throw_if((M + 31) / 32 > g_max || (N + bn - 1) / bn > nt_max, "push gemm: flag array too small for this call");
+  throw_if(inbox_off % 16 != 0 || (slot_elems * 2) % 16 != 0, "push gemm: inbox must keep 16-byte alignment");
+  if (M == 0) return;
+  PushArgs p{};
+  for (size_t i = 0; i < bases.size(); ++i) p.bases[i] = reinterpret_cast<uint8_t*>(bases[i]);
+  p.inbox_off = inbox_off;
+  p.slot_elems = slot_elems;
+  p.flags_off = flags_off;
+  p.world = (int)bases.size();
+  p.rank = rank;
+  p.g_max = g_max;
+  p.nt_max = nt_max;
+#define GOLLEK_PUSH_CASE(BNV) \
+  if (bn == BNV)              \
+    return launch_gemm_t<BNV, kEpiPush>(out, N, a, lda, b, ldb, nullptr, 0, M, N, K, 1, nullptr, status, 0, s, \
+                                        nullptr, nullptr, 1, true, &p);
+  GOLLEK_PUSH_CASE(256)
+  GOLLEK_PUSH_CASE(128)
+  GOLLEK_PUSH_CASE(64)
+#undef GOLLEK_PUSH_CASE
+  throw_if(true, "push gemm: unsupported tile width " + std::to_string(bn));
 }
 
 void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, int M_cap,

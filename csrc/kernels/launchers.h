@@ -51,7 +51,8 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
 
 // ---- GEMM (K5, K8)
 // Gated epilogues (SwiGLU, GeGLU) read gate/up rows interleaved in groups of 64 and write N/2 columns.
-enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3 };
+// kEpiPush: plain output, also pushed to every tensor-parallel peer's inbox (GEMM → all-reduce).
+enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3, kEpiPush = 4 };
 inline bool epi_gated(int epi) { return epi == kEpiSwiglu || epi == kEpiGeglu; }
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
@@ -60,6 +61,16 @@ int gemm_splits(int M, int N, int K, int epi);
 void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
                       const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, int splits,
                       float* partial, uint32_t* status, int grid_limit, cudaStream_t s);
+
+// Row-parallel GEMM fused with the all-reduce's data movement: C = A·Bᵀ written to `out` (this
+// rank's inbox slot) and to the same slot of every peer's inbox, with per-tile ready flags
+// (layout in csrc/comm/push.h). Followed by launch_tp_push_ar_rmsnorm.
+void launch_gemm_push(void* out, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int bn,
+                      const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
+                      int64_t flags_off, int g_max, int nt_max, uint32_t* status, cudaStream_t s);
+void launch_tp_push_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
+                               int64_t flags_off, int g_max, int nt_max, int nt, void* residual, const void* w,
+                               void* x_out, int T, int d, float eps, double timeout_s, int grid, cudaStream_t s);
 
 // Grouped GEMM (MoE experts): A rows grouped per expert and padded to 128, tile_group[m-tile] =
 // expert, live M-tile count in device memory; B = experts stacked [groups * N, K].

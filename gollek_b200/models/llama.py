@@ -80,6 +80,11 @@ class TPComm:
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         return t
 
+    def push_linear(self, a: torch.Tensor, w) -> Optional[torch.Tensor]:
+        """Row-parallel GEMM fused with the data movement of the all-reduce that follows (the
+        fused comm overrides this); None = run ``ops.linear`` into ``partial_buffer``."""
+        return None
+
     def allreduce_add_rmsnorm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
                               eps: float) -> torch.Tensor:
         return ops.fused_add_rms_norm(self.all_reduce(h), residual, w, eps)
@@ -381,6 +386,18 @@ class LlamaModel:
                                         out=out[nd:], window=window, softcap=cap)
         return out
 
+    def _row_linear(self, a: torch.Tensor, w, li: int, lora_kind: Optional[str] = None) -> torch.Tensor:
+        """o_proj / down_proj (row-parallel): under the fused TP comm the GEMM pushes its tiles to
+        every rank as it produces them; otherwise it writes the rank's partial for the collective."""
+        if self.lora is None and not self.cfg.sandwich_norm:
+            h = self.comm.push_linear(a, w)
+            if h is not None:
+                return h
+        h = ops.linear(a, w, out=self.comm.partial_buffer(a.shape[0]))
+        if self.lora is not None and lora_kind is not None:
+            self.lora.apply(li, lora_kind, a, h)
+        return h
+
     def _moe(self, x: torch.Tensor, L: dict, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """This rank's share of the MoE FFN (its local experts, or its FFN shard of every expert)."""
         cfg = self.cfg
@@ -426,9 +443,7 @@ class LlamaModel:
                                   bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
                                   norm_eps=eps)
             a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
-            h = ops.linear(a, L["w_o"], out=self.comm.partial_buffer(T))
-            if self.lora is not None:
-                self.lora.apply(li, "o", a, h)
+            h = self._row_linear(a, L["w_o"], li, "o")
             if cfg.sandwich_norm:  # norm(attn) + residual, then the pre-FFN norm
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, L["pre_ff_norm"], eps)
@@ -437,8 +452,7 @@ class LlamaModel:
             if cfg.is_moe:
                 h = self._moe(x, L, out=self.comm.partial_buffer(T))
             else:
-                h = ops.linear(ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act), L["w_down"],
-                               out=self.comm.partial_buffer(T))
+                h = self._row_linear(ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act), L["w_down"], li)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
             if cfg.sandwich_norm:
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_ff_norm"], eps)

@@ -9,12 +9,21 @@ region (``cudaIpcOpenMemHandle``). Region layout:
                         sum straight here (alternating per call, so a slow peer still reading
                         call k never sees call k+1's data)
     gather              [max_tokens, hidden] bf16: reduced row chunks (two-shot mode)
+    inbox[0], [1]       [world, push_max_tokens, hidden] bf16 each: the push path's per-source slots
+    flags               uint32 [world, push_max_tokens / 32, hidden / 64]: per-tile ready epochs
 
 ``FusedTPComm.allreduce_add_rmsnorm`` replaces "NCCL all-reduce → residual add → RMSNorm" with
 one kernel (csrc/comm/symm.cu). Decode-sized batches use the one-shot variant (one barrier,
 every rank sums all partials); larger ones the two-shot variant (reduce-scatter by rows, then
 all-gather fused with RMSNorm: 2(N-1)/N of the data crosses NVLink per rank instead of N-1).
 NCCL (``NcclComm``) remains the baseline and the correctness oracle.
+
+Push path (GEMM → all-reduce fused, decode-sized T ≤ ``push_max_tokens``): ``push_linear`` runs
+the row-parallel GEMM whose epilogue stores every finished tile into this rank's slot of *every*
+rank's inbox over NVLink and raises a ready flag per (source, 32-row group, n-tile); the
+following ``allreduce_add_rmsnorm`` waits for the flags of each row group and reduces the
+partials from local memory. The NVLink transfer overlaps the GEMM tile by tile and there is no
+barrier: the flags are the synchronisation.
 """
 from __future__ import annotations
 
@@ -77,14 +86,25 @@ class FusedTPComm(TPComm):
     fused_ar = True
 
     def __init__(self, rank: int, size: int, max_tokens: int, hidden: int, cpu_group=None,
-                 timeout_s: float = 5.0, one_shot_max_tokens: int = 128, grid: int = 0):
+                 timeout_s: float = 5.0, one_shot_max_tokens: int = 128, grid: int = 0,
+                 push_max_tokens: int = 256):
         super().__init__(rank, size)
         self.max_tokens, self.hidden = max_tokens, hidden
-        buf = max_tokens * hidden * 2
-        buf = (buf + 4095) // 4096 * 4096
+        rnd = lambda n: (n + 4095) // 4096 * 4096  # noqa: E731
+        buf = rnd(max_tokens * hidden * 2)
         self.off_p = [HEADER_BYTES, HEADER_BYTES + buf]
         self.off_g = HEADER_BYTES + 2 * buf
-        self.heap = SymmHeap(HEADER_BYTES + 3 * buf, rank, size, group=cpu_group)
+        end = HEADER_BYTES + 3 * buf
+        self.push_max = min(push_max_tokens, max_tokens) if (size > 1 and hidden % 8 == 0) else 0
+        self.slot = self.push_max * hidden
+        inbox = rnd(size * self.slot * 2)
+        self.off_inbox = [end, end + inbox]
+        self.g_max = max(1, (self.push_max + 31) // 32)
+        self.nt_max = (hidden + 63) // 64
+        self.off_flags = end + 2 * inbox
+        end = self.off_flags + rnd(size * self.g_max * self.nt_max * 4)
+        self.heap = SymmHeap(end, rank, size, group=cpu_group)
+        self._pushed = None  # (T, n-tiles) of a push GEMM awaiting its consumer
         self.timeout_s = timeout_s
         self.one_shot_max_tokens = one_shot_max_tokens
         self.calls = 0
@@ -98,6 +118,22 @@ class FusedTPComm(TPComm):
             raise ValueError(f"{T} tokens exceed the symmetric buffer ({self.max_tokens})")
         return self.heap.view(self.off_p[self.calls % 2], (T, self.hidden))
 
+    def push_linear(self, a: torch.Tensor, w: torch.Tensor) -> Optional[torch.Tensor]:
+        """Row-parallel ``a @ w.T`` with the push epilogue when it applies (bf16 weight producing
+        the hidden width, T within the push buffers); None = use partial_buffer + linear."""
+        T = a.shape[0]
+        if (not self.push_max or T == 0 or T > self.push_max or not isinstance(w, torch.Tensor) or not a.is_cuda
+                or w.dtype != torch.bfloat16 or a.dtype != torch.bfloat16 or w.shape[0] != self.hidden):
+            return None
+        ext = cuda_ext()
+        bn = ext.gemm_pick_bn(T, self.hidden, 0)
+        parity = self.calls % 2
+        out = self.heap.view(self.off_inbox[parity] + self.rank * self.slot * 2, (T, self.hidden))
+        ext.gemm_push(out, a, w, bn, self.heap.bases, self.rank, self.off_inbox[parity], self.slot, self.off_flags,
+                      self.g_max, self.nt_max)
+        self._pushed = (T, (self.hidden + bn - 1) // bn)
+        return out
+
     def _ensure_in_partial(self, h: torch.Tensor) -> None:
         buf = self.partial_buffer(h.shape[0])
         if h.data_ptr() != buf.data_ptr():
@@ -107,6 +143,18 @@ class FusedTPComm(TPComm):
                               eps: float) -> torch.Tensor:
         """residual += all_reduce(h); returns rms_norm(residual) * w (residual updated in place)."""
         T = h.shape[0]
+        if self._pushed is not None:
+            Tp, nt = self._pushed
+            self._pushed = None
+            if Tp != T:
+                raise RuntimeError("push GEMM and its all-reduce disagree on the token count")
+            x = torch.empty_like(residual)
+            cuda_ext().tp_push_allreduce_add_rmsnorm(self.heap.bases, self.rank, self.off_inbox[self.calls % 2],
+                                                     self.slot, self.off_flags, self.g_max, self.nt_max, nt,
+                                                     residual, w, x, float(eps), self.timeout_s,
+                                                     min(self.grid, max(1, T)))
+            self.calls += 1
+            return x
         self._ensure_in_partial(h)
         x = torch.empty_like(residual)
         one_shot = T <= self.one_shot_max_tokens

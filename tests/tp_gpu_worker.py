@@ -43,6 +43,31 @@ def run_collectives(rank, world, port, result_q):
             comm.all_reduce(t)
             torch.cuda.synchronize()
             errs.append((T, "ar", float(((t.float() - t_ref.float()).abs() / (1 + t_ref.float().abs())).max()), 0.0))
+        # GEMM -> all-reduce push path against (a) the pull kernels on the same GEMM output (bitwise)
+        # and (b) NCCL; push and pull calls interleave to exercise buffer parity and epochs
+        K = 1024
+        for T in (1, 7, 64, 200, 256):
+            for rep in range(2):
+                g = torch.Generator(device="cuda").manual_seed(5000 * T + rep * 10 + rank)
+                a = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+                wt = (torch.randn(d, K, device="cuda", generator=g) * 0.03).bfloat16()
+                gs = torch.Generator(device="cuda").manual_seed(11 * T + rep)
+                res = torch.randn(T, d, device="cuda", generator=gs).bfloat16()
+                w = (torch.rand(d, device="cuda", generator=gs) + 0.5).bfloat16()
+                res_pull = res.clone()
+                h = comm.push_linear(a, wt)
+                assert h is not None
+                x = comm.allreduce_add_rmsnorm(h, res, w, 1e-5)
+                hp = ops.linear(a, wt, out=comm.partial_buffer(T))
+                x_pull = comm.allreduce_add_rmsnorm(hp, res_pull, w, 1e-5)
+                h_ref = ops.linear(a, wt)
+                dist.all_reduce(h_ref)
+                res_ref = torch.randn(T, d, device="cuda", generator=torch.Generator(device="cuda").manual_seed(
+                    11 * T + rep)).bfloat16()
+                x_ref = ops.fused_add_rms_norm(h_ref, res_ref, w, 1e-5)
+                torch.cuda.synchronize()
+                errs.append((T, f"push{rep}", float(((x.float() - x_ref.float()).abs() / (1 + x_ref.float().abs())).max()),
+                             float((x.float() - x_pull.float()).abs().max() + (res.float() - res_pull.float()).abs().max())))
         comm.check()
         result_q.put((rank, errs, None))
         dist.barrier()
