@@ -27,6 +27,7 @@ barrier: the flags are the synchronisation.
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional
 
 import torch
@@ -87,7 +88,7 @@ class FusedTPComm(TPComm):
 
     def __init__(self, rank: int, size: int, max_tokens: int, hidden: int, cpu_group=None,
                  timeout_s: float = 5.0, one_shot_max_tokens: int = 128, grid: int = 0,
-                 push_max_tokens: int = 256):
+                 push_max_tokens: Optional[int] = None):
         super().__init__(rank, size)
         self.max_tokens, self.hidden = max_tokens, hidden
         rnd = lambda n: (n + 4095) // 4096 * 4096  # noqa: E731
@@ -95,6 +96,14 @@ class FusedTPComm(TPComm):
         self.off_p = [HEADER_BYTES, HEADER_BYTES + buf]
         self.off_g = HEADER_BYTES + 2 * buf
         end = HEADER_BYTES + 3 * buf
+        if push_max_tokens is None and os.environ.get("GOLLEK_TP_PUSH_MAX"):
+            push_max_tokens = int(os.environ["GOLLEK_TP_PUSH_MAX"])
+        if push_max_tokens is None:
+            # Off by default: measured at Llama-3-8B TP2 shapes (benchmarks/tp_collectives_bench.py) the
+            # push GEMM + local reduce (62.8 us at T=256, 186 us at T=1344) loses to GEMM + the pull
+            # kernel (46.2 / 89.8 us; NCCL 52.3 / 96.6): one-row-per-lane 16-byte remote stores and a
+            # system-scope fence per tile cost more than the pull kernel's single barrier at these sizes.
+            push_max_tokens = 0
         self.push_max = min(push_max_tokens, max_tokens) if (size > 1 and hidden % 8 == 0) else 0
         self.slot = self.push_max * hidden
         inbox = rnd(size * self.slot * 2)

@@ -17,7 +17,8 @@ def run_collectives(rank, world, port, result_q):
         from gollek_b200.parallel.symm import FusedTPComm
         init_distributed(backend="nccl", timeout_s=60)
         d = 4096
-        comm = FusedTPComm(rank, world, max_tokens=1024, hidden=d, cpu_group=cpu_group(), one_shot_max_tokens=16)
+        comm = FusedTPComm(rank, world, max_tokens=1024, hidden=d, cpu_group=cpu_group(), one_shot_max_tokens=16,
+                           push_max_tokens=256)
         errs = []
         for T in (1, 7, 16, 300, 1024):
             for rep in range(3):  # consecutive calls exercise the buffer parity and epochs
