@@ -55,6 +55,7 @@ def parse():
     p.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--no-fill", action="store_true")
+    p.add_argument("--no-async", action="store_true", help="synchronous scheduling (no host/device overlap)")
     return p.parse_args()
 
 
@@ -151,7 +152,8 @@ def main():
     ec = EngineConfig(model=args.model, device="cuda", dtype="bfloat16", tensor_parallel_size=di.world_size,
                       block_size=16, max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_batched_tokens,
                       max_model_len=args.prompt_max + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                      enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm)
+                      enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm,
+                      async_scheduling=not args.no_async)
     comm = None
     if di.world_size > 1:
         if args.comm == "fused":
@@ -213,7 +215,8 @@ def main():
                 first_seen[sq.request_id] = sq.scheduled_time
         tokens += len(outs)
         now = time.perf_counter()
-        token_log.extend((o.request_id, now, len(o.output_token_ids)) for o in outs)
+        # tokens generated so far (a trailing -1 is the next token, still in flight under async scheduling)
+        token_log.extend((o.request_id, now, len(o.output_token_ids) - (o.output_token_ids[-1] < 0)) for o in outs)
     t1 = time.perf_counter()
     ev1.record()
     torch.cuda.synchronize()

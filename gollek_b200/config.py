@@ -407,6 +407,10 @@ class EngineConfig:
     ngram_min: int = 1
     ngram_max: int = 4
     draft_model: Optional[str] = None
+    # overlap the host side of step N+1 (schedule, batch build, launches) with step N on the GPU;
+    # steps that need host-visible history (penalties, speculative decoding, P/D hand-off) run
+    # synchronously
+    async_scheduling: bool = True
     # checkpoint / resume: prefix-cache snapshot and unfinished-request snapshot paths (written at
     # shutdown, read at startup when present)
     prefix_cache_snapshot: Optional[str] = None

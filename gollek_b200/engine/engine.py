@@ -92,6 +92,7 @@ class LLMEngine:
         # prefill/decode disaggregation: called after a sequence's first token on a prefill engine;
         # returning True means its KV was handed to a decode engine (engine.disagg)
         self.handoff_hook = None
+        self._inflight = None  # async scheduling: the launched step whose tokens are not read back yet
         # ---- speculative decoding
         from .speculative import DraftModelProposer, NgramProposer, SpecStats
         self.spec = None
@@ -162,12 +163,13 @@ class LLMEngine:
         return seq is not None
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self._inflight is not None
 
     # ------------------------------------------------------------------ stepping
-    def _check_stop(self, seq: Sequence, tok: int) -> Optional[SeqStatus]:
+    def _check_stop(self, seq: Sequence, tok: int, n_out: Optional[int] = None) -> Optional[SeqStatus]:
+        """Stop test for ``tok``, the ``n_out``-th output token (default: the last one appended)."""
         p = seq.params
-        n_out = len(seq.output_token_ids)
+        n_out = len(seq.output_token_ids) if n_out is None else n_out
         if n_out >= p.min_tokens:
             if not p.ignore_eos and tok == self.eos_token_id:
                 seq.stop_reason = tok
@@ -176,14 +178,14 @@ class LLMEngine:
                 seq.stop_reason = tok
                 return SeqStatus.FINISHED_STOPPED
             if p.stop and self.tokenizer is not None:
-                seq.output_text = self.tokenizer.decode(seq.output_token_ids)
+                seq.output_text = self.tokenizer.decode(seq.output_token_ids[:n_out])
                 for s in p.stop:
                     idx = seq.output_text.find(s)
                     if idx >= 0:
                         seq.output_text = seq.output_text[:idx]
                         seq.stop_reason = s
                         return SeqStatus.FINISHED_STOPPED
-        if n_out >= p.max_tokens or seq.num_tokens >= self.cfg.max_model_len:
+        if n_out >= p.max_tokens or seq.num_prompt_tokens + n_out >= self.cfg.max_model_len:
             return SeqStatus.FINISHED_LENGTH
         return None
 
@@ -215,8 +217,74 @@ class LLMEngine:
             sched.decode = keep
             sched.prefill = verify + sched.prefill
 
+    def _needs_sync(self) -> bool:
+        if not self.cfg.async_scheduling or self.spec is not None or self.handoff_hook is not None:
+            return True
+        return any(s.params.needs_penalties for s in self.scheduler.running)
+
     def step(self) -> List[RequestOutput]:
-        """One scheduler iteration: schedule, (draft,) run the model, append tokens, retire finished."""
+        """One scheduler iteration. With async scheduling: schedule and launch this step, then read
+        back the previous one (its outputs are returned), so the host work of a step overlaps the
+        device work of the one before. Otherwise: schedule, (draft,) run, append, retire."""
+        if self._needs_sync():
+            outs = self._resolve_inflight()
+            return outs + self._step_sync()
+        sched = self.scheduler.schedule()
+        if sched.empty:
+            return self._resolve_inflight()
+        t0 = time.perf_counter()
+        h = self.runner.launch(sched, self._inflight)
+        for c in sched.chunks:
+            seq = c.seq
+            seq.num_computed_tokens = c.start + c.num_tokens
+            if c.sample:
+                seq.output_token_ids.append(-1)
+                seq.pending += 1
+                h.records.append((seq, len(seq.output_token_ids) - 1))
+        outs = self._resolve_inflight()
+        self._inflight = h
+        self.metrics.on_step(time.perf_counter() - t0, sched.num_tokens, len(outs), len(self.scheduler.running),
+                             len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
+        return outs
+
+    def _resolve_inflight(self) -> List[RequestOutput]:
+        """Read back the in-flight step: fill placeholders, stop checks, retire finished sequences."""
+        h = self._inflight
+        if h is None:
+            return []
+        self._inflight = None
+        toks = h.tokens()
+        now = time.perf_counter()
+        outputs: List[RequestOutput] = []
+        for (seq, idx), tok in zip(h.records, toks):
+            seq.pending -= 1
+            if seq.status.finished or idx >= len(seq.output_token_ids):
+                continue  # stopped at an earlier token (this one was computed past the stop) or aborted
+            tok = int(tok)
+            seq.output_token_ids[idx] = tok
+            seq.token_times.append(now)
+            if seq.first_token_time is None:
+                seq.first_token_time = now
+            status = self._check_stop(seq, tok, idx + 1)
+            finished = status is not None
+            if finished:
+                del seq.output_token_ids[idx + 1:]  # drop a token launched after the stop
+                seq.finish_time = now
+                self.scheduler.finish(seq, status)
+                self.seqs.pop(seq.request_id, None)
+                self.metrics.on_finish(seq)
+            elif self.kv.has(seq):
+                # positions < num_computed_tokens are inputs of launched steps, all resolved by now
+                # (the in-flight step's own placeholder sits at num_computed_tokens)
+                self.kv.commit_full_blocks(seq)
+            text = ""
+            if self.tokenizer is not None and finished:
+                text = seq.output_text or self.tokenizer.decode(seq.output_token_ids)
+            outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, [tok],
+                                         finished, status.value if status else None, text))
+        return outputs
+
+    def _step_sync(self) -> List[RequestOutput]:
         sched = self.scheduler.schedule()
         if sched.empty:
             return []

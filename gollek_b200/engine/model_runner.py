@@ -44,6 +44,23 @@ class _Pinned:
         self.sampled = torch.zeros(max_rows, dtype=torch.int64, **kw)
 
 
+class Inflight:
+    """A launched step whose sampled ids are still on their way to the host (async scheduling)."""
+
+    def __init__(self, sched, out_dev, host_buf, event, rows):
+        self.sched = sched
+        self.out_dev = out_dev      # device int64 [ns]: one sampled id per sampled chunk
+        self.host_buf = host_buf    # pinned int64 view receiving them
+        self.event = event          # recorded after the D2H copy
+        self.rows = rows            # seq_id -> row in out_dev
+        self.records = []           # (seq, index in output_token_ids) placeholders to fill
+
+    def tokens(self) -> List[int]:
+        if self.event is not None:
+            self.event.synchronize()
+        return self.host_buf.tolist()
+
+
 class _DecodeGraph:
     def __init__(self, bs: int):
         self.bs = bs
@@ -75,6 +92,10 @@ class ModelRunner:
                             max_rows=cfg.max_num_seqs * (1 + k_spec))
         self.spec_step = 0
         self.greedy_only = False  # draft-model runners: always argmax (deterministic proposals)
+        # async scheduling: two pinned receive buffers (step N's D2H is read while step N+1 runs)
+        rows = self.host.sampled.numel()
+        self.async_bufs = [torch.zeros(rows, dtype=torch.int64, pin_memory=self.is_cuda) for _ in range(2)]
+        self.async_flip = 0
         self.graphs: Dict[int, _DecodeGraph] = {}
         self.graph_pool = None
         self.step_counter = 0
@@ -91,6 +112,7 @@ class ModelRunner:
         n = len(chunks)
         h = self.host
         ids = h.input_ids.numpy()
+        self._pending_rows = []
         t = 0
         sample_rows: List[int] = []
         sample_seqs: List[Sequence] = []
@@ -100,6 +122,8 @@ class ModelRunner:
             h.n_new[i] = c.num_tokens
             toks = c.tokens if c.tokens is not None else c.seq.tokens(c.start, c.start + c.num_tokens)
             ids[t:t + c.num_tokens] = toks
+            if c.num_tokens and toks[-1] < 0:  # a token still being sampled by the in-flight step
+                self._pending_rows.append((t + c.num_tokens - 1, c.seq.seq_id))
             t += c.num_tokens
             if c.sample:
                 sample_rows.extend(range(t - 1 - c.verify, t))
@@ -120,6 +144,8 @@ class ModelRunner:
         sampled token, or for a speculative verify chunk the accepted drafts plus one."""
         self.step_counter += 1
         n, T, sample_seqs, sample_rows = self._fill_host(out)
+        if self._pending_rows:
+            raise RuntimeError("step inputs contain unresolved tokens: resolve the in-flight step first")
         if self.timer is not None:
             self.timer.begin()
         try:
@@ -128,8 +154,51 @@ class ModelRunner:
             if self.timer is not None:
                 self.timer.end()
 
+    @torch.inference_mode()
+    def launch(self, out: SchedulerOutput, prev: Optional[Inflight]) -> Inflight:
+        """Async scheduling: launch a step without waiting for it. Input tokens that the in-flight
+        step ``prev`` is still sampling are copied from its device output on the device; the
+        sampled ids of this step go to a pinned buffer asynchronously (``Inflight.tokens``)."""
+        self.step_counter += 1
+        n, T, sample_seqs, sample_rows = self._fill_host(out)
+        patch = None
+        if self._pending_rows:
+            if prev is None:
+                raise RuntimeError("unresolved input tokens without an in-flight step")
+            in_rows = [r for r, _ in self._pending_rows]
+            src = [prev.rows[sid] for _, sid in self._pending_rows]
+            patch = (prev.out_dev, in_rows, src)
+        if self.timer is not None:
+            self.timer.begin()
+        try:
+            res = self._execute(out, n, T, sample_seqs, sample_rows, patch=patch, sync=False)
+        finally:
+            if self.timer is not None:
+                self.timer.end()
+        out_dev = res
+        buf = self.async_bufs[self.async_flip][: out_dev.numel()]
+        self.async_flip ^= 1
+        ev = None
+        if self.is_cuda:
+            buf.copy_(out_dev, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+        else:
+            buf.copy_(out_dev)
+        rows = {c.seq.seq_id: i for i, c in enumerate([c for c in out.chunks if c.sample])}
+        self.d2h_bytes += 8 * out_dev.numel()
+        return Inflight(out, out_dev, buf, ev, rows)
+
+    def _patch_inputs(self, input_ids: torch.Tensor, patch) -> None:
+        prev_out, in_rows, src = patch
+        dev = input_ids.device
+        ir = torch.tensor(in_rows, dtype=torch.int64).to(dev, non_blocking=True)
+        sr = torch.tensor(src, dtype=torch.int64).to(dev, non_blocking=True)
+        input_ids.index_copy_(0, ir, prev_out.index_select(0, sr).to(input_ids.dtype))
+        self.h2d_bytes += 16 * len(in_rows)
+
     def _execute(self, out: SchedulerOutput, n: int, T: int, sample_seqs: List[Sequence],
-                 sample_rows: List[int]) -> List[List[int]]:
+                 sample_rows: List[int], patch=None, sync: bool = True):
         nd = len(out.decode)
         h = self.host
         dev = self.device
@@ -143,11 +212,15 @@ class ModelRunner:
         all_greedy = self.greedy_only or all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
         if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0 and not lora_active
                 and all(c.verify == 0 for c in out.decode) and self._graph_for(nd) is not None):
+            if not sync:
+                return self._replay_decode(nd, patch=patch, sync=False)
             return [[t] for t in self._replay_decode(nd)]
         nb = int(max(1, (int(h.seq_lens[:n].max()) + self.block_size - 1) // self.block_size))
         self.h2d_bytes += 4 * (3 * T + n * self.max_blocks + n + (n - nd + 1)) + 8 * max(1, len(sample_rows))
         self.d2h_bytes += 8 * len(sample_rows)
         input_ids = h.input_ids[:T].to(dev, non_blocking=True)
+        if patch is not None:
+            self._patch_inputs(input_ids, patch)
         positions = h.positions[:T].to(dev, non_blocking=True)
         slots = h.slots[:T].to(dev, non_blocking=True)
         bt = h.block_tables[:n].to(dev, non_blocking=True)[:, :nb]  # contiguous pinned rows; sliced on device
@@ -170,9 +243,11 @@ class ModelRunner:
         if ns == 0:
             meta.logits_indices = h.logits_idx[:1].to(dev, non_blocking=True)
             self.model.forward(input_ids, meta, self.kv_cache)
-            return []
+            return [] if sync else torch.zeros(0, dtype=torch.int64, device=dev)
         meta.logits_indices = h.logits_idx[:ns].to(dev, non_blocking=True)
         logits = self.model.forward(input_ids, meta, self.kv_cache)
+        if not sync:
+            return self._sample_device(logits, sample_seqs)
         sampled = [c for c in out.chunks if c.sample]
         if all(c.verify == 0 for c in sampled):
             return [[t] for t in self.sample(logits, sample_seqs)]
@@ -219,8 +294,17 @@ class ModelRunner:
         return self.model.forward(h.input_ids[:T].to(dev), meta, self.kv_cache, hidden_only=True)
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
-        dev = logits.device
+        out = self._sample_device(logits, seqs)
         ns = len(seqs)
+        if self.is_cuda:
+            self.host.sampled[:ns].copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return self.host.sampled[:ns].tolist()
+        return out.tolist()
+
+    def _sample_device(self, logits: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
+        """Sampled ids [ns] (int64, on the logits' device), without synchronising."""
+        dev = logits.device
         if self.greedy_only or all(s.params.greedy and not s.params.needs_penalties for s in seqs):
             out = ops.argmax(logits)
         else:
@@ -250,11 +334,7 @@ class ModelRunner:
                                   for s in seqs], dtype=torch.int64).to(dev)
             offs = torch.tensor([len(s.output_token_ids) for s in seqs], dtype=torch.int64).to(dev)
             out = ops.sample(lf, temps, tks, tps, mps, seeds, offs)
-        if self.is_cuda:
-            self.host.sampled[:ns].copy_(out, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            return self.host.sampled[:ns].tolist()
-        return out.tolist()
+        return out
 
     # ------------------------------------------------------------------ CUDA graphs
     def _bucket(self, nd: int) -> Optional[int]:
@@ -315,7 +395,7 @@ class ModelRunner:
         self.graphs[bs] = g
         return g
 
-    def _replay_decode(self, nd: int) -> List[int]:
+    def _replay_decode(self, nd: int, patch=None, sync: bool = True):
         g = self._graph_for(nd)
         h = self.host
         bs = g.bs
@@ -329,12 +409,16 @@ class ModelRunner:
             h.block_tables[nd:bs] = 0
             h.input_ids[nd:bs] = 0
         g.input_ids.copy_(h.input_ids[:bs], non_blocking=True)
+        if patch is not None:
+            self._patch_inputs(g.input_ids, patch)
         g.positions.copy_(h.positions[:bs], non_blocking=True)
         g.slots.copy_(h.slots[:bs], non_blocking=True)
         g.seq_lens.copy_(h.seq_lens[:bs], non_blocking=True)
         g.block_tables.copy_(h.block_tables[:bs], non_blocking=True)
         g.graph.replay()
         ops.LAUNCHES.add(g.launches)
+        if not sync:
+            return g.out_ids[:nd]
         self.host.sampled[:bs].copy_(g.out_ids, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return self.host.sampled[:nd].tolist()

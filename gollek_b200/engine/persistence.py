@@ -85,8 +85,11 @@ def snapshot_requests(engine) -> List[dict]:
         for s in q:
             if s.status.finished:
                 continue
+            # a token still in flight (async scheduling placeholder) is not part of the snapshot:
+            # it is generated again after the restore
             out.append({"request_id": s.request_id, "prompt_token_ids": list(s.prompt_token_ids),
-                        "output_token_ids": list(s.output_token_ids), "params": dataclasses.asdict(s.params),
+                        "output_token_ids": [t for t in s.output_token_ids if t >= 0],
+                        "params": dataclasses.asdict(s.params),
                         "lora_id": s.lora_id, "priority": getattr(s, "priority", 0)})
     return out
 

@@ -123,6 +123,8 @@ class Scheduler:
         for seq in list(self.running):
             if seq.status is not SeqStatus.RUNNING or not seq.is_decode:
                 continue
+            if len(seq.output_token_ids) >= seq.params.max_tokens or seq.num_tokens >= self.cfg.max_model_len:
+                continue  # async scheduling: at its limit with a token in flight; finishes on read-back
             while not self.kv.ensure(seq, seq.num_tokens):
                 victim = self.running[-1]
                 self._preempt(victim, out)
@@ -147,6 +149,8 @@ class Scheduler:
         # 3) admit waiting sequences
         while self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
             seq = self.waiting[0]
+            if seq.pending:  # preempted with a token still in flight: admit after read-back
+                break
             if not self._wait_admits(seq):
                 break
             self.kv.add(seq)

@@ -232,6 +232,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             raise HTTPException(400, str(e))
 
     def detok(ids: List[int]) -> str:
+        ids = [t for t in list(ids) if t >= 0]  # async scheduling: a token may still be in flight
         return st.tokenizer.decode(ids) if st.tokenizer is not None else " ".join(map(str, ids))
 
     def chat_prompt(messages) -> Union[str, List[int]]:
