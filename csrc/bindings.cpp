@@ -399,6 +399,15 @@ void tp_push_ar_rmsnorm_py(std::vector<uint64_t> bases, int64_t rank, int64_t in
                             (float)eps, timeout_s, (int)grid, cur_stream());
 }
 
+void tp_argmax_py(std::vector<uint64_t> bases, int64_t rank, torch::Tensor logits, int64_t vocab_offset,
+                  int64_t cand_off, int64_t cand_rows, int64_t parity, torch::Tensor out, double timeout_s) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "tp argmax: logits [B, V_local] row-major");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kLong && out.numel() >= logits.size(0), "tp argmax: out int64 [B]");
+  launch_tp_argmax(bases, (int)rank, logits.data_ptr(), logits.stride(0), logits.size(0), logits.size(1), vocab_offset,
+                   cand_off, (int)cand_rows, (int)parity, out.data_ptr<int64_t>(), timeout_s, cur_stream());
+}
+
 void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int64_t p1, int64_t parity,
                      torch::Tensor out, double timeout_s, int64_t grid) {
   check_bf16(out, "out");
@@ -528,6 +537,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_status", &symm_status_py);
   m.def("tp_allreduce_add_rmsnorm", &tp_ar_rmsnorm_py, "fused TP all-reduce + residual add + RMSNorm over P2P");
   m.def("tp_allreduce", &tp_allreduce_py, "TP all-reduce over P2P");
+  m.def("tp_argmax", &tp_argmax_py, "distributed greedy argmax of vocab-parallel logits over P2P (C5)");
   m.def("gemm_push", &gemm_push_py, "row-parallel tcgen05 GEMM pushing its tiles to every rank's inbox (C1)");
   m.def("tp_push_allreduce_add_rmsnorm", &tp_push_ar_rmsnorm_py,
         "reduce pushed partials from local memory + residual + RMSNorm (C1 consumer)");

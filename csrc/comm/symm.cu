@@ -291,6 +291,83 @@ __global__ void __launch_bounds__(kArThreads) tp_push_ar_rmsnorm_kernel(PushArgs
   }
 }
 
+// C5: distributed greedy argmax of a vocab-parallel lm_head. CTA b takes row b of this rank's
+// logit shard, finds its (max, lowest index) and stores the packed candidate — the float's
+// order-preserving key in the high word, ~global index in the low word, so one unsigned max
+// picks the larger logit and, among equal logits, the lower token id — into slot [rank][b] of
+// every rank's candidate array (double-buffered by call parity). The last CTA to finish
+// publishes flag_b[rank] = epoch to every peer, waits (bounded) for every peer's flag and
+// reduces the W candidates of every row into `out`. Only B x W x 8 bytes cross NVLink instead of
+// the B x V logits an all-gather would move.
+GOLLEK_DEVICE uint32_t float_order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kArThreads) tp_argmax_kernel(ArArgs a, const __nv_bfloat16* __restrict__ logits,
+                                                               int64_t stride, int V, int64_t vocab_offset, int B,
+                                                               int64_t cand_off, int cand_rows, int parity,
+                                                               int64_t* __restrict__ out) {
+  SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
+  __shared__ uint32_t s_epoch;
+  __shared__ unsigned long long s_best[kArThreads / 32];
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int b = blockIdx.x;
+  const __nv_bfloat16* row = logits + (int64_t)b * stride;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float f = __bfloat162float(row[i]);
+    const unsigned long long key = ((unsigned long long)float_order_key(f) << 32) |
+                                   (uint32_t)~(uint32_t)(vocab_offset + i);
+    best = key > best ? key : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArThreads / 32; ++w) best = s_best[w] > best ? s_best[w] : best;
+    best = s_best[0] > best ? s_best[0] : best;
+    const int64_t slot = ((int64_t)parity * a.world + a.rank) * cand_rows + b;
+    for (int p = 0; p < a.world; ++p)
+      reinterpret_cast<unsigned long long*>(a.bases[p] + cand_off)[slot] = best;
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(&me->arrive, 1u);
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  // last CTA: publish, wait for every peer, reduce every row
+  if (threadIdx.x < a.world) {
+    SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[threadIdx.x]);
+    st_release_sys(&peer->flag_b[a.rank], epoch);
+  }
+  if (threadIdx.x < a.world && !wait_geq(&me->flag_b[threadIdx.x], epoch, a.timeout_ns))
+    atomicOr(&me->status, kStatusPeerTimeout);
+  __syncthreads();
+  const unsigned long long* cand = reinterpret_cast<const unsigned long long*>(a.bases[a.rank] + cand_off);
+  for (int r = threadIdx.x; r < B; r += blockDim.x) {
+    unsigned long long m = 0ull;
+    for (int p = 0; p < a.world; ++p) {
+      const unsigned long long c = *reinterpret_cast<volatile const unsigned long long*>(
+          &cand[((int64_t)parity * a.world + p) * cand_rows + r]);
+      m = c > m ? c : m;
+    }
+    out[r] = (int64_t)(uint32_t)~(uint32_t)(m & 0xffffffffull);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    me->arrive = 0;
+    me->epoch = epoch;
+  }
+}
+
 // Plain all-reduce (sum) of the partial buffer into `out` (no residual / norm), one-shot.
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(ArArgs a, __nv_bfloat16* __restrict__ out,
                                                                   int64_t nvec_total) {
@@ -418,6 +495,18 @@ void launch_tp_push_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int
                                                         reinterpret_cast<const __nv_bfloat16*>(w),
                                                         reinterpret_cast<__nv_bfloat16*>(x_out));
   check_launch("tp_push_allreduce_add_rmsnorm");
+}
+
+void launch_tp_argmax(const std::vector<uint64_t>& bases, int rank, const void* logits, int64_t stride, int B, int V,
+                      int64_t vocab_offset, int64_t cand_off, int cand_rows, int parity, int64_t* out,
+                      double timeout_s, cudaStream_t s) {
+  throw_if(B > cand_rows, "tp argmax: more rows than candidate slots");
+  throw_if(cand_off % 8 != 0, "tp argmax: candidate array must be 8-byte aligned");
+  if (B == 0) return;
+  ArArgs a = make_args(bases, rank, 0, 0, 0, 0, 0, 0, true, 0.f, timeout_s);
+  tp_argmax_kernel<<<B, kArThreads, 0, s>>>(a, reinterpret_cast<const __nv_bfloat16*>(logits), stride, V,
+                                            vocab_offset, B, cand_off, cand_rows, parity, out);
+  check_launch("tp_argmax");
 }
 
 uint32_t symm_read_status(void* base) {

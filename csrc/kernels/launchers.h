@@ -68,6 +68,11 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
 void launch_gemm_push(void* out, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int bn,
                       const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
                       int64_t flags_off, int g_max, int nt_max, uint32_t* status, cudaStream_t s);
+// C5: greedy argmax over a vocab-parallel logits shard ([B, V] bf16 rows at `stride`, global
+// token ids start at vocab_offset); candidates cross NVLink, every rank gets the global ids.
+void launch_tp_argmax(const std::vector<uint64_t>& bases, int rank, const void* logits, int64_t stride, int B, int V,
+                      int64_t vocab_offset, int64_t cand_off, int cand_rows, int parity, int64_t* out,
+                      double timeout_s, cudaStream_t s);
 void launch_tp_push_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t inbox_off, int64_t slot_elems,
                                int64_t flags_off, int g_max, int nt_max, int nt, void* residual, const void* w,
                                void* x_out, int T, int d, float eps, double timeout_s, int grid, cudaStream_t s);

@@ -245,6 +245,16 @@ class ModelRunner:
             self.model.forward(input_ids, meta, self.kv_cache)
             return [] if sync else torch.zeros(0, dtype=torch.int64, device=dev)
         meta.logits_indices = h.logits_idx[:ns].to(dev, non_blocking=True)
+        if all_greedy and all(c.verify == 0 for c in out.chunks):
+            # greedy ids straight from the model (under TP: argmax over the vocab shards, no logits gather)
+            ids = self.model.forward(input_ids, meta, self.kv_cache, greedy=True)
+            if not sync:
+                return ids
+            if self.is_cuda:
+                self.host.sampled[:ns].copy_(ids, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+                return [[t] for t in self.host.sampled[:ns].tolist()]
+            return [[t] for t in ids.tolist()]
         logits = self.model.forward(input_ids, meta, self.kv_cache)
         if not sync:
             return self._sample_device(logits, sample_seqs)
@@ -379,16 +389,14 @@ class ModelRunner:
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             for _ in range(2):
-                logits = self.model.forward(g.input_ids, meta, self.kv_cache)
-                ops.argmax(logits)
+                self.model.forward(g.input_ids, meta, self.kv_cache, greedy=True)
         torch.cuda.current_stream().wait_stream(s)
         graph = torch.cuda.CUDAGraph()
         if self.graph_pool is None:
             self.graph_pool = torch.cuda.graph_pool_handle()
         n0 = ops.LAUNCHES.n
         with torch.cuda.graph(graph, pool=self.graph_pool):
-            g.logits = self.model.forward(g.input_ids, meta, self.kv_cache)
-            g.out_ids = ops.argmax(g.logits)
+            g.out_ids = self.model.forward(g.input_ids, meta, self.kv_cache, greedy=True)
         g.launches = ops.LAUNCHES.n - n0
         ops.LAUNCHES.n = n0
         g.graph = graph

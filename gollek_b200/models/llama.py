@@ -92,6 +92,10 @@ class TPComm:
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
         return t
 
+    def argmax_last(self, t: torch.Tensor, vocab_offset: int) -> torch.Tensor:
+        """Greedy token ids from vocab-parallel logit shards (ties: lowest token id)."""
+        return ops.argmax(t)
+
 
 def _pad_heads(w: torch.Tensor, n_heads: int, d: int, d_pad: int, dim: int = 0) -> torch.Tensor:
     """Zero-pad each of ``n_heads`` head blocks of width ``d`` along ``dim`` to ``d_pad``."""
@@ -422,7 +426,7 @@ class LlamaModel:
         return _copy_out(acc.to(x.dtype), out)
 
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
-                hidden_only: bool = False) -> torch.Tensor:
+                hidden_only: bool = False, greedy: bool = False) -> torch.Tensor:
         """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP), or with
         ``hidden_only`` the final-norm hidden states of every token [T, hidden]."""
         cfg = self.cfg
@@ -463,6 +467,8 @@ class LlamaModel:
             return x
         if meta.logits_indices is not None:
             x = x.index_select(0, meta.logits_indices)
+        if greedy:  # token ids: argmax over the vocab shards without gathering the logits
+            return self.comm.argmax_last(ops.linear(x, self.lm_head), self.comm.rank * self.V_local)
         logits = self.comm.all_gather_last(ops.linear(x, self.lm_head))
         if cfg.final_logit_softcapping:
             c = cfg.final_logit_softcapping

@@ -18,6 +18,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from .. import ops
 from ..models.llama import TPComm
 
 
@@ -92,6 +93,18 @@ class NcclComm(TPComm):
         if self.size > 1:
             dist.all_reduce(t, group=self.group)
         return t
+
+    def argmax_last(self, t: torch.Tensor, vocab_offset: int) -> torch.Tensor:
+        """Greedy ids from vocab shards: all-gather each rank's (max, id) per row, take the best."""
+        if self.size == 1:
+            return ops.argmax(t)
+        v, i = t.float().max(-1)
+        pair = torch.stack([v, (i + vocab_offset).float()], -1).contiguous()  # ids < 2^24: exact in fp32
+        parts = [torch.empty_like(pair) for _ in range(self.size)]
+        dist.all_gather(parts, pair, group=self.group)
+        allp = torch.stack(parts, 0)  # [W, B, 2]; ranks hold ascending id ranges, so the first max wins ties
+        best = allp[..., 0].argmax(0)
+        return allp[..., 1].gather(0, best[None])[0].long()
 
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
         """[B, V/tp] shards → [B, V] (vocab-parallel lm_head)."""

@@ -112,6 +112,9 @@ class FusedTPComm(TPComm):
         self.nt_max = (hidden + 63) // 64
         self.off_flags = end + 2 * inbox
         end = self.off_flags + rnd(size * self.g_max * self.nt_max * 4)
+        # C5 argmax candidates: [2 parities][world][max_tokens] packed (logit key, id) words
+        self.off_cand = end
+        end = self.off_cand + rnd(2 * size * max_tokens * 8)
         self.heap = SymmHeap(end, rank, size, group=cpu_group)
         self._pushed = None  # (T, n-tiles) of a push GEMM awaiting its consumer
         self.timeout_s = timeout_s
@@ -186,6 +189,18 @@ class FusedTPComm(TPComm):
             return t
         dist.all_reduce(t)
         return t
+
+    def argmax_last(self, t: torch.Tensor, vocab_offset: int) -> torch.Tensor:
+        """C5: greedy ids from the vocab shards; per row one (logit, id) candidate per rank crosses
+        NVLink (P2P kernel) instead of the all-gathered logits."""
+        if self.size == 1 or t.dtype != torch.bfloat16 or t.shape[0] > self.max_tokens:
+            return super().argmax_last(t, vocab_offset) if self.size == 1 else \
+                self.all_gather_last(t).float().argmax(-1)
+        out = torch.empty(t.shape[0], dtype=torch.int64, device=t.device)
+        cuda_ext().tp_argmax(self.heap.bases, self.rank, t.contiguous(), int(vocab_offset), self.off_cand,
+                             self.max_tokens, self.calls % 2, out, self.timeout_s)
+        self.calls += 1
+        return out
 
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
         if self.size == 1:

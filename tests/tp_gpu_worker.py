@@ -69,6 +69,18 @@ def run_collectives(rank, world, port, result_q):
                 torch.cuda.synchronize()
                 errs.append((T, f"push{rep}", float(((x.float() - x_ref.float()).abs() / (1 + x_ref.float().abs())).max()),
                              float((x.float() - x_pull.float()).abs().max() + (res.float() - res_pull.float()).abs().max())))
+        # C5 distributed argmax vs the argmax of the all-gathered logits (incl. a cross-rank tie)
+        V = 32000
+        for B in (1, 37, 256):
+            g = torch.Generator(device="cuda").manual_seed(77 * B + rank)
+            shard = torch.randn(B, V // world, device="cuda", generator=g).bfloat16()
+            if B > 1:
+                shard[1, 5] = 50.0  # same maximum on every rank: the lowest global id must win
+            ids = comm.argmax_last(shard, rank * (V // world))
+            full = comm.all_gather_last(shard)
+            ref = full.float().argmax(-1)
+            torch.cuda.synchronize()
+            errs.append((B, "argmax", float((ids != ref).sum()), 0.0))
         comm.check()
         result_q.put((rank, errs, None))
         dist.barrier()
