@@ -23,6 +23,7 @@ from ..config import EngineConfig, ModelConfig, PRESETS, preset
 from ..models.llama import LlamaModel, TPComm
 from ..native import host_ext
 from .kv_cache import KVCacheManager, allocate_kv_cache, num_blocks_from_memory
+from ..utils import tracing
 from .model_runner import ModelRunner
 from .scheduler import Scheduler
 from .sequence import RequestOutput, SamplingParams, Sequence, SeqStatus
@@ -229,11 +230,15 @@ class LLMEngine:
         if self._needs_sync():
             outs = self._resolve_inflight()
             return outs + self._step_sync()
+        tracing.nvtx_push("schedule")
         sched = self.scheduler.schedule()
+        tracing.nvtx_pop()
         if sched.empty:
             return self._resolve_inflight()
         t0 = time.perf_counter()
+        tracing.nvtx_push("launch")
         h = self.runner.launch(sched, self._inflight)
+        tracing.nvtx_pop()
         for c in sched.chunks:
             seq = c.seq
             seq.num_computed_tokens = c.start + c.num_tokens
@@ -241,7 +246,9 @@ class LLMEngine:
                 seq.output_token_ids.append(-1)
                 seq.pending += 1
                 h.records.append((seq, len(seq.output_token_ids) - 1))
+        tracing.nvtx_push("read-back")
         outs = self._resolve_inflight()
+        tracing.nvtx_pop()
         self._inflight = h
         self.metrics.on_step(time.perf_counter() - t0, sched.num_tokens, len(outs), len(self.scheduler.running),
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))

@@ -27,6 +27,7 @@ import torch
 
 from .. import ops
 from ..config import ModelConfig
+from ..utils import tracing
 from .reference import layer_tensors, rope_cos_sin
 
 # head sizes the attention kernels are built for; other sizes are stored zero-padded to the next one
@@ -436,7 +437,11 @@ class LlamaModel:
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
         n = len(self.layers)
         x = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
+        nv = tracing.nvtx_enabled()
         for li, L in enumerate(self.layers):
+            if nv:
+                tracing.nvtx_push(f"layer{li}")
+                tracing.nvtx_push("attn")
             qkv = ops.linear(x, L["w_qkv"])
             if self.lora is not None:
                 self.lora.apply(li, "qkv", x, qkv)
@@ -448,21 +453,33 @@ class LlamaModel:
                                   norm_eps=eps)
             a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
             h = self._row_linear(a, L["w_o"], li, "o")
+            if nv:
+                tracing.nvtx_pop()
+                tracing.nvtx_push("allreduce+norm")
             if cfg.sandwich_norm:  # norm(attn) + residual, then the pre-FFN norm
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, L["pre_ff_norm"], eps)
             else:
                 x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
+            if nv:
+                tracing.nvtx_pop()
+                tracing.nvtx_push("moe" if cfg.is_moe else "ffn")
             if cfg.is_moe:
                 h = self._moe(x, L, out=self.comm.partial_buffer(T))
             else:
                 h = self._row_linear(ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act), L["w_down"], li)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
+            if nv:
+                tracing.nvtx_pop()
+                tracing.nvtx_push("allreduce+norm")
             if cfg.sandwich_norm:
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_ff_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, nxt, eps)
             else:
                 x = self.comm.allreduce_add_rmsnorm(h, residual, nxt, eps)
+            if nv:
+                tracing.nvtx_pop()
+                tracing.nvtx_pop()
         if hidden_only:
             return x
         if meta.logits_indices is not None:
