@@ -411,6 +411,10 @@ class EngineConfig:
     # steps that need host-visible history (penalties, speculative decoding, P/D hand-off) run
     # synchronously
     async_scheduling: bool = True
+    # weight offload: the last `offload_layers` layers stream from pinned host memory, prefetched
+    # `offload_prefetch` layers ahead (for models larger than device memory; disables CUDA graphs)
+    offload_layers: int = 0
+    offload_prefetch: int = 2
     # checkpoint / resume: prefix-cache snapshot and unfinished-request snapshot paths (written at
     # shutdown, read at startup when present)
     prefix_cache_snapshot: Optional[str] = None

@@ -60,6 +60,9 @@ class LLMEngine:
             self.model.load_weights(weights)
             if cfg.quantization == "fp8":
                 self.model.quantize_fp8()
+        if cfg.offload_layers > 0 and self.device.type == "cuda":
+            self.model.enable_offload(cfg.offload_layers, cfg.offload_prefetch)
+            cfg.use_cuda_graphs = False
         # ---- KV cache
         bpb = self.model.kv_bytes_per_block(cfg.block_size)
         nb = num_blocks or cfg.num_gpu_blocks

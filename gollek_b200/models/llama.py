@@ -195,6 +195,17 @@ class LlamaModel:
         self.norm: Optional[torch.Tensor] = None
         self.lm_head: Optional[torch.Tensor] = None
         self.lora = None  # optional MultiLoRA hook (gollek_b200.engine.lora)
+        self.offload = None  # optional LayerOffload (weights of some layers streamed from host memory)
+
+    def enable_offload(self, num_layers: int, depth: int = 2) -> None:
+        """Keep the weights of the last ``num_layers`` layers in pinned host memory and stream them
+        in ``depth`` layers ahead of use (CUDA only; the engine disables CUDA graphs)."""
+        if num_layers <= 0 or self.device.type != "cuda":
+            return
+        from .offload import LayerOffload
+        n = len(self.layers)
+        self.offload = LayerOffload(self.layers, list(range(max(0, n - num_layers), n)), self.device, depth)
+        torch.cuda.empty_cache()
 
     # ------------------------------------------------------------------ weights
     def load_weights(self, get: Callable[[str], torch.Tensor]) -> None:
@@ -363,10 +374,14 @@ class LlamaModel:
         n = sum(nb(x) for x in (self.embed, self.norm, self.lm_head))
         for L in self.layers:
             for k, v in L.items():
+                if v is None:  # offloaded: lives in host memory
+                    continue
                 if k == "experts":
                     n += sum(nb(a) + nb(b) for a, b in v)
                 else:
                     n += nb(v)
+        if self.offload is not None:
+            n += sum(nb(t) for slot in self.offload.slots for t in slot.values())
         return n
 
     # ------------------------------------------------------------------ KV cache
@@ -438,7 +453,12 @@ class LlamaModel:
         n = len(self.layers)
         x = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
         nv = tracing.nvtx_enabled()
+        off = self.offload
+        if off is not None:
+            off.begin_forward()
         for li, L in enumerate(self.layers):
+            if off is not None:
+                L = off.acquire(li)
             if nv:
                 tracing.nvtx_push(f"layer{li}")
                 tracing.nvtx_push("attn")
@@ -480,6 +500,8 @@ class LlamaModel:
             if nv:
                 tracing.nvtx_pop()
                 tracing.nvtx_pop()
+            if off is not None:
+                off.release(li)
         if hidden_only:
             return x
         if meta.logits_indices is not None:
