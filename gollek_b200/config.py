@@ -415,6 +415,9 @@ class EngineConfig:
     # `offload_prefetch` layers ahead (for models larger than device memory; disables CUDA graphs)
     offload_layers: int = 0
     offload_prefetch: int = 2
+    # multi-tenant admission: tenant -> {"max_running": n, "max_kv_blocks": n}; requests of a tenant
+    # at its quota wait while other tenants' requests are admitted
+    tenant_quotas: dict = field(default_factory=dict)
     # checkpoint / resume: prefix-cache snapshot and unfinished-request snapshot paths (written at
     # shutdown, read at startup when present)
     prefix_cache_snapshot: Optional[str] = None

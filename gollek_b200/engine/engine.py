@@ -123,7 +123,7 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: Optional[str], prompt: Union[str, List[int]],
                     params: Optional[SamplingParams] = None, lora_id: int = 0,
-                    arrival_time: Optional[float] = None, priority: int = 0) -> str:
+                    arrival_time: Optional[float] = None, priority: int = 0, tenant: str = "") -> str:
         request_id = request_id or uuid.uuid4().hex
         if request_id in self.seqs:
             raise ValueError(f"duplicate request id {request_id}")
@@ -145,6 +145,7 @@ class LLMEngine:
         if lora_id and (self.lora_manager is None or lora_id not in self.lora_manager.adapters):
             raise ValueError(f"unknown LoRA adapter id {lora_id}")
         seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
+        seq.tenant = tenant or ""
         self.scheduler.add(seq)
         self.seqs[request_id] = seq
         self.metrics.on_arrival()

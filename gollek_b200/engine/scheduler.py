@@ -147,10 +147,16 @@ class Scheduler:
             out.prefill.append(ScheduledChunk(seq, seq.num_computed_tokens, n, n == remaining))
             budget -= n
         # 3) admit waiting sequences
+        quotas = self.cfg.tenant_quotas
+        usage = self._tenant_usage() if quotas else None
+        skipped = []  # waiting requests of tenants at their quota keep their place in the queue
         while self.waiting and budget > 0 and len(self.running) < self.cfg.max_num_seqs:
             seq = self.waiting[0]
             if seq.pending:  # preempted with a token still in flight: admit after read-back
                 break
+            if usage is not None and not self._tenant_admits(seq, usage):
+                skipped.append(self.waiting.popleft())
+                continue
             if not self._wait_admits(seq):
                 break
             self.kv.add(seq)
@@ -169,7 +175,32 @@ class Scheduler:
             self.running.append(seq)
             out.prefill.append(ScheduledChunk(seq, reused, n, n == remaining))
             budget -= n
+            if usage is not None and seq.tenant:
+                u = usage.setdefault(seq.tenant, [0, 0])
+                u[0] += 1
+                u[1] += self.kv.tables.num_blocks(seq.seq_id)
+        for seq in reversed(skipped):
+            self.waiting.appendleft(seq)
         return out
+
+    def _tenant_usage(self) -> Dict[str, List[int]]:
+        use: Dict[str, List[int]] = {}
+        for s in self.running:
+            if s.tenant:
+                u = use.setdefault(s.tenant, [0, 0])
+                u[0] += 1
+                u[1] += self.kv.tables.num_blocks(s.seq_id) if self.kv.has(s) else 0
+        return use
+
+    def _tenant_admits(self, seq, usage) -> bool:
+        q = self.cfg.tenant_quotas.get(seq.tenant) if seq.tenant else None
+        if not q:
+            return True
+        run, blocks = usage.get(seq.tenant, [0, 0])
+        if run >= q.get("max_running", 1 << 30):
+            return False
+        need = (seq.num_tokens + self.kv.block_size - 1) // self.kv.block_size
+        return blocks + need <= q.get("max_kv_blocks", 1 << 60)
 
     # ------------------------------------------------------------------ post-step update
     def finish(self, seq: Sequence, status: SeqStatus) -> None:

@@ -83,7 +83,7 @@ class Sequence:
     __slots__ = ("seq_id", "request_id", "prompt_token_ids", "output_token_ids", "params", "lora_id",
                  "arrival_time", "num_computed_tokens", "status", "first_token_time", "finish_time",
                  "token_times", "block_hashes", "num_preemptions", "predicted_len", "stop_reason",
-                 "output_text", "priority", "scheduled_time", "pending")
+                 "output_text", "priority", "scheduled_time", "pending", "tenant")
 
     def __init__(self, request_id: str, prompt_token_ids: List[int], params: SamplingParams,
                  lora_id: int = 0, arrival_time: Optional[float] = None, priority: int = 0):
@@ -107,6 +107,7 @@ class Sequence:
         self.priority = priority
         self.scheduled_time: Optional[float] = None
         self.pending = 0  # async scheduling: sampled tokens not yet read back (placeholders -1)
+        self.tenant = ""  # quota accounting (EngineConfig.tenant_quotas)
 
     @property
     def num_tokens(self) -> int:

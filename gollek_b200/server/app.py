@@ -20,7 +20,9 @@ Token counts are real (the reference estimates chars/4, OpenAiCompatibleResource
 from __future__ import annotations
 
 import asyncio
+import contextvars
 import json
+import os
 import time
 import uuid
 from datetime import datetime, timezone
@@ -30,6 +32,7 @@ from fastapi import FastAPI, Header, HTTPException, Request
 from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 from pydantic import BaseModel, Field
 
+from .. import errors
 from ..engine.sequence import SamplingParams
 from .async_engine import AsyncEngine, EngineDeadError
 from .resilience import Bulkhead, BulkheadFull, CircuitBreaker, CircuitOpen, RateLimited, RateLimiter
@@ -113,13 +116,19 @@ def _param(p: Dict[str, Any], *names, default=None):
     return default
 
 
+_TENANT = contextvars.ContextVar("gollek_tenant", default="")
+
+
 class ServerState:
-    def __init__(self, aengine: AsyncEngine, model_name: str, api_keys: Optional[List[str]] = None,
+    def __init__(self, aengine: AsyncEngine, model_name: str, api_keys=None,
                  rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
                  max_concurrent: int = 1024, max_queue: int = 4096):
         self.ae = aengine
         self.model_name = model_name
-        self.api_keys = set(api_keys or [])
+        # API key -> tenant ("" = no tenant); a list of keys means keys without tenants
+        self.api_keys: Dict[str, str] = dict(api_keys) if isinstance(api_keys, dict) else \
+            {k: "" for k in (api_keys or [])}
+        self.admin_key = os.environ.get("GOLLEK_ADMIN_KEY", "")
         self.bulkhead = Bulkhead(max_concurrent, max_queue)
         self.breaker = CircuitBreaker()
         self.limiter = RateLimiter(rate, burst)
@@ -182,23 +191,38 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     app = FastAPI(title="gollek-b200", version="0.1")
     app.state.server = st
 
+    def error_response(name: str, message: Optional[str] = None, status: Optional[int] = None) -> JSONResponse:
+        code = errors.CODES[name]
+        return JSONResponse({"error": errors.payload(code, message)}, status_code=status or code.http)
+
+    @app.exception_handler(HTTPException)
+    async def http_error(request: Request, exc: HTTPException):
+        code = errors.CODES.get(getattr(exc, "gollek_code", "")) or errors.for_http(exc.status_code)
+        body = errors.payload(code, str(exc.detail))
+        body["httpStatus"] = exc.status_code
+        return JSONResponse({"error": body}, status_code=exc.status_code)
+
     # -------------------------------------------------------------- middleware
     @app.middleware("http")
     async def auth_and_limits(request: Request, call_next):
         path = request.url.path
         open_paths = ("/health", "/q/health", "/metrics", "/docs", "/openapi.json")
-        if st.api_keys and not path.startswith(open_paths):
-            key = request.headers.get("x-api-key")
-            auth = request.headers.get("authorization", "")
-            if auth.lower().startswith("bearer "):
-                key = auth[7:].strip()
+        key = request.headers.get("x-api-key")
+        auth = request.headers.get("authorization", "")
+        if auth.lower().startswith("bearer "):
+            key = auth[7:].strip()
+        if path.startswith("/v1/admin"):
+            if (st.admin_key or st.api_keys) and key != st.admin_key:
+                return error_response("AUTH_FORBIDDEN", "admin routes need GOLLEK_ADMIN_KEY")
+        elif st.api_keys and not path.startswith(open_paths):
             if key not in st.api_keys:
-                return JSONResponse({"error": {"message": "invalid or missing API key", "type": "unauthorized"}},
-                                    status_code=401)
+                return error_response("AUTH_INVALID_KEY")
+        tenant = st.api_keys.get(key, "") if key else ""
+        _TENANT.set(tenant or request.headers.get("x-tenant-id", ""))
         try:
-            st.limiter.check(request.headers.get("x-api-key") or request.client.host if request.client else "anon")
+            st.limiter.check(key or (request.client.host if request.client else "anon"))
         except RateLimited as e:
-            return JSONResponse({"error": {"message": str(e), "type": "rate_limited"}}, status_code=429)
+            return error_response("RATE_LIMIT_EXCEEDED", str(e))
         return await call_next(request)
 
     # -------------------------------------------------------------- core runner
@@ -214,7 +238,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
 
                 async def consume():
                     nonlocal last
-                    async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, priority=priority):
+                    async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, priority=priority,
+                                                    tenant=_TENANT.get()):
                         last = out
 
                 await asyncio.wait_for(consume(), timeout=timeout or st.timeout)
@@ -248,7 +273,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         async def gen():
             nonlocal prev
             try:
-                async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id):
+                async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, tenant=_TENANT.get()):
                     text = detok(out.output_token_ids)
                     if out.finished and out.text:
                         text = out.text
@@ -483,4 +508,46 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         app.delete(base + "/{request_id}")(infer_cancel)
     app.post("/api/v1/inference")(infer_completions)
     app.post("/v1/inference")(infer_completions)
+
+    # -------------------------------------------------------------- jobs and administration
+    @app.get("/v1/jobs")
+    async def list_jobs():
+        return {"jobs": [{"jobId": j["jobId"], "status": j["status"]} for j in st.jobs.values()]}
+
+    @app.get("/v1/jobs/{job_id}")
+    async def get_job(job_id: str):
+        if job_id not in st.jobs:
+            e = HTTPException(404, "unknown job")
+            e.gollek_code = "ROUTING_JOB_NOT_FOUND"
+            raise e
+        return st.jobs[job_id]
+
+    @app.get("/v1/admin/api-keys")
+    async def admin_list_keys():
+        return {"keys": [{"key": k[:4] + "…" + k[-2:], "tenant": t} for k, t in st.api_keys.items()]}
+
+    @app.post("/v1/admin/api-keys")
+    async def admin_create_key(body: Dict[str, Any] = None):
+        import secrets
+        key = "gk-" + secrets.token_urlsafe(24)
+        st.api_keys[key] = str((body or {}).get("tenant", ""))
+        return {"key": key, "tenant": st.api_keys[key]}
+
+    @app.delete("/v1/admin/api-keys/{key}")
+    async def admin_revoke_key(key: str):
+        if key not in st.api_keys:
+            raise HTTPException(404, "unknown key")
+        del st.api_keys[key]
+        return {"revoked": True}
+
+    @app.get("/v1/admin/errors")
+    async def admin_error_codes():
+        return {"codes": [dict(name=c.name, code=c.code, http=c.http, retryable=c.retryable, message=c.message,
+                               category=c.category.value) for c in errors.CODES.values()]}
+
+    @app.get("/v1/admin/tenants")
+    async def admin_tenants():
+        use = st.engine.scheduler._tenant_usage()
+        return {"quotas": st.engine.cfg.tenant_quotas,
+                "usage": {t: {"running": u[0], "kv_blocks": u[1]} for t, u in use.items()}}
     return app

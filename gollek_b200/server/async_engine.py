@@ -87,9 +87,12 @@ class AsyncEngine:
     def _handle(self, sub) -> None:
         kind = sub[0]
         if kind == "add":
-            _, rid, prompt, params, lora_id, priority = sub
+            _, rid, prompt, params, lora_id, priority, tenant = sub
             try:
-                self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority)
+                if tenant:
+                    self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority, tenant=tenant)
+                else:
+                    self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority)
             except Exception as e:  # invalid request: report to that caller only
                 self._deliver(rid, e)
         elif kind == "abort":
@@ -134,7 +137,7 @@ class AsyncEngine:
     # ------------------------------------------------------------------ client API
     async def generate(self, prompt: Union[str, List[int]], params: SamplingParams,
                        request_id: Optional[str] = None, lora_id: int = 0,
-                       priority: int = 0) -> AsyncIterator[RequestOutput]:
+                       priority: int = 0, tenant: str = "") -> AsyncIterator[RequestOutput]:
         if self.error is not None:
             raise EngineDeadError(str(self.error))
         if self.draining:
@@ -146,7 +149,7 @@ class AsyncEngine:
             if rid in self._streams:
                 raise ValueError(f"duplicate request id {rid}")
             self._streams[rid] = (loop, q)
-        self._subs.put(("add", rid, prompt, params, lora_id, priority))
+        self._subs.put(("add", rid, prompt, params, lora_id, priority, tenant))
         finished = False
         try:
             while True:

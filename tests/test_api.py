@@ -107,3 +107,56 @@ def test_api_keys(tiny_weights):
         assert c.get("/v1/models", headers={"Authorization": "Bearer secret"}).status_code == 200
         assert c.get("/health").status_code == 200
     ae.shutdown()
+
+
+def test_error_payloads_admin_and_tenants(tiny_cfg, tiny_weights, monkeypatch):
+    """Errors carry catalogue codes; admin routes create/revoke keys bound to tenants; a tenant at
+    its running-request quota waits while another tenant's request is admitted."""
+    from fastapi.testclient import TestClient
+
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine
+    from gollek_b200.server.app import create_app
+    from gollek_b200.server.async_engine import AsyncEngine
+    monkeypatch.setenv("GOLLEK_ADMIN_KEY", "admin")
+    ec = EngineConfig(device="cpu", dtype="float32", max_num_seqs=4, max_num_batched_tokens=64, max_model_len=128,
+                      use_cuda_graphs=False, tenant_quotas={"t1": {"max_running": 1}})
+    eng = LLMEngine(ec, model_cfg=tiny_cfg, weights=tiny_weights.__getitem__, num_blocks=32)
+    ae = AsyncEngine(eng).start()
+    try:
+        app = create_app(ae, api_keys={"k1": "t1", "k2": "t2"})
+        with TestClient(app) as c:
+            r = c.get("/v1/models")
+            assert r.status_code == 401 and r.json()["error"]["code"] == "AUTH_101"
+            r = c.get("/v1/models/nope", headers={"x-api-key": "k1"})
+            assert r.status_code == 404 and r.json()["error"]["code"] == "MODEL_001"
+            r = c.post("/v1/completions", json={"prompt": [1, 2, 3], "temperature": -1}, headers={"x-api-key": "k1"})
+            assert r.status_code == 400 and r.json()["error"]["type"] == "VALIDATION"
+            assert c.get("/v1/admin/api-keys", headers={"x-api-key": "k1"}).status_code == 403
+            nk = c.post("/v1/admin/api-keys", json={"tenant": "t3"}, headers={"x-api-key": "admin"}).json()["key"]
+            assert c.get("/v1/models", headers={"x-api-key": nk}).status_code == 200
+            assert c.delete(f"/v1/admin/api-keys/{nk}", headers={"x-api-key": "admin"}).json()["revoked"]
+            assert c.get("/v1/models", headers={"x-api-key": nk}).status_code == 401
+            codes = c.get("/v1/admin/errors", headers={"x-api-key": "admin"}).json()["codes"]
+            assert any(x["code"] == "QUOTA_101" for x in codes)
+            assert c.get("/v1/admin/tenants", headers={"x-api-key": "admin"}).json()["quotas"] == {"t1": {"max_running": 1}}
+    finally:
+        ae.shutdown(drain=False)
+
+
+def test_tenant_quota_scheduling(tiny_cfg, tiny_weights):
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine
+    from gollek_b200.engine.sequence import SamplingParams
+    ec = EngineConfig(device="cpu", dtype="float32", max_num_seqs=8, max_num_batched_tokens=256, max_model_len=128,
+                      use_cuda_graphs=False, tenant_quotas={"a": {"max_running": 1}})
+    eng = LLMEngine(ec, model_cfg=tiny_cfg, weights=tiny_weights.__getitem__, num_blocks=64)
+    sp = SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True)
+    for i in range(3):
+        eng.add_request(f"a{i}", [1 + i, 2, 3], SamplingParams(**vars(sp)), tenant="a")
+    eng.add_request("b0", [4, 5, 6], SamplingParams(**vars(sp)), tenant="b")
+    eng.step()
+    running = {s.request_id for s in eng.scheduler.running}
+    assert "b0" in running and len([r for r in running if r.startswith("a")]) == 1
+    while eng.has_unfinished():
+        eng.step()
