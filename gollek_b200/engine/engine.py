@@ -97,6 +97,7 @@ class LLMEngine:
         # returning True means its KV was handed to a decode engine (engine.disagg)
         self.handoff_hook = None
         self._inflight = None  # async scheduling: the launched step whose tokens are not read back yet
+        self._n_host_sampling = 0  # live requests needing host-side sampling (forces synchronous steps)
         # ---- speculative decoding
         from .speculative import DraftModelProposer, NgramProposer, SpecStats
         self.spec = None
@@ -147,6 +148,8 @@ class LLMEngine:
         seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
         seq.tenant = tenant or ""
         self.scheduler.add(seq)
+        if params.needs_penalties or params.needs_host_sampling:
+            self._n_host_sampling += 1
         self.seqs[request_id] = seq
         self.metrics.on_arrival()
         return request_id
@@ -163,6 +166,8 @@ class LLMEngine:
     def abort_request(self, request_id: str) -> bool:
         seq = self.scheduler.abort(request_id)
         self.seqs.pop(request_id, None)
+        if seq is not None and (seq.params.needs_penalties or seq.params.needs_host_sampling):
+            self._n_host_sampling -= 1
         if seq is not None and self.spec is not None and hasattr(self.spec, "forget"):
             self.spec.forget(seq)
         return seq is not None
@@ -225,7 +230,8 @@ class LLMEngine:
     def _needs_sync(self) -> bool:
         if not self.cfg.async_scheduling or self.spec is not None or self.handoff_hook is not None:
             return True
-        return any(s.params.needs_penalties for s in self.scheduler.running)
+        # live requests whose sampling needs host-visible history (penalties, typical, mirostat, logprobs)
+        return self._n_host_sampling > 0
 
     def step(self) -> List[RequestOutput]:
         """One scheduler iteration. With async scheduling: schedule and launch this step, then read
@@ -282,6 +288,8 @@ class LLMEngine:
                 del seq.output_token_ids[idx + 1:]  # drop a token launched after the stop
                 seq.finish_time = now
                 self.scheduler.finish(seq, status)
+                if seq.params.needs_penalties or seq.params.needs_host_sampling:
+                    self._n_host_sampling -= 1
                 self.seqs.pop(seq.request_id, None)
                 self.metrics.on_finish(seq)
             elif self.kv.has(seq):
@@ -292,7 +300,8 @@ class LLMEngine:
             if self.tokenizer is not None and finished:
                 text = seq.output_text or self.tokenizer.decode(seq.output_token_ids)
             outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, [tok],
-                                         finished, status.value if status else None, text))
+                                         finished, status.value if status else None, text,
+                                         logprobs=seq.logprobs if seq.params.logprobs is not None else None))
         return outputs
 
     def _step_sync(self) -> List[RequestOutput]:
@@ -341,6 +350,8 @@ class LLMEngine:
             if finished:
                 seq.finish_time = now
                 self.scheduler.finish(seq, status)
+                if seq.params.needs_penalties or seq.params.needs_host_sampling:
+                    self._n_host_sampling -= 1
                 self.seqs.pop(seq.request_id, None)
                 self.metrics.on_finish(seq)
                 if self.spec is not None and hasattr(self.spec, "forget"):
@@ -349,7 +360,8 @@ class LLMEngine:
             if self.tokenizer is not None and finished:
                 text = seq.output_text or self.tokenizer.decode(seq.output_token_ids)
             outputs.append(RequestOutput(seq.request_id, seq.prompt_token_ids, seq.output_token_ids, appended,
-                                         finished, status.value if status else None, text))
+                                         finished, status.value if status else None, text,
+                                         logprobs=seq.logprobs if seq.params.logprobs is not None else None))
         self.metrics.on_step(now - t0, sched.num_tokens, n_new, len(self.scheduler.running),
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
         return outputs

@@ -209,7 +209,8 @@ class ModelRunner:
                 ids.extend([c.seq.lora_id] * c.num_tokens)
             lora.set_batch(ids)
         lora_active = lora is not None and lora.active
-        all_greedy = self.greedy_only or all(s.params.greedy and not s.params.needs_penalties for s in sample_seqs)
+        all_greedy = self.greedy_only or all(s.params.greedy and not s.params.needs_penalties
+                                             and not s.params.needs_host_sampling for s in sample_seqs)
         if (self.is_cuda and self.cfg.use_cuda_graphs and nd == n and all_greedy and nd > 0 and not lora_active
                 and all(c.verify == 0 for c in out.decode) and self._graph_for(nd) is not None):
             if not sync:
@@ -304,6 +305,9 @@ class ModelRunner:
         return self.model.forward(h.input_ids[:T].to(dev), meta, self.kv_cache, hidden_only=True)
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
+        special = [i for i, s in enumerate(seqs) if s.params.needs_host_sampling]
+        if special:
+            return self._sample_with_host_modes(logits, seqs, special)
         out = self._sample_device(logits, seqs)
         ns = len(seqs)
         if self.is_cuda:
@@ -311,6 +315,45 @@ class ModelRunner:
             torch.cuda.current_stream().synchronize()
             return self.host.sampled[:ns].tolist()
         return out.tolist()
+
+    def _sample_with_host_modes(self, logits: torch.Tensor, seqs: List[Sequence], special: List[int]) -> List[int]:
+        """Rows using typical / mirostat sampling or asking for logprobs: torch per row (after the
+        same penalties); the others go through the sampling kernel as usual."""
+        from .sampling_modes import sample_row
+        plain = [i for i in range(len(seqs)) if i not in set(special)]
+        toks = [0] * len(seqs)
+        if plain:
+            sub = self.sample(logits[plain], [seqs[i] for i in plain])
+            for i, t in zip(plain, sub):
+                toks[i] = t
+        lf = logits.float()
+        for i in special:
+            s = seqs[i]
+            row = lf[i].clone()
+            if s.params.needs_penalties:
+                pen = self._penalised(row[None], [s])
+                row = pen[0]
+            toks[i] = sample_row(row, lf[i], s, self.cfg.seed)
+        return toks
+
+    def _penalised(self, lf: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
+        dev = lf.device
+        trip = []
+        for r, s in enumerate(seqs):
+            ou, oc = np.unique(np.asarray([t for t in s.output_token_ids if t >= 0], dtype=np.int64),
+                               return_counts=True)
+            cnt = dict(zip(ou.tolist(), oc.tolist()))
+            toks = set(cnt)
+            if s.params.repetition_penalty != 1.0:
+                toks |= set(s.prompt_token_ids)
+            trip.extend((r, int(tok), int(cnt.get(tok, 0))) for tok in sorted(toks))
+        if trip:
+            tri = torch.tensor(trip, dtype=torch.int32).to(dev)
+            rep = torch.tensor([s.params.repetition_penalty for s in seqs], dtype=torch.float32).to(dev)
+            fr = torch.tensor([s.params.frequency_penalty for s in seqs], dtype=torch.float32).to(dev)
+            pr = torch.tensor([s.params.presence_penalty for s in seqs], dtype=torch.float32).to(dev)
+            ops.apply_penalties(lf, tri, rep, fr, pr)
+        return lf
 
     def _sample_device(self, logits: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
         """Sampled ids [ns] (int64, on the logits' device), without synchronising."""

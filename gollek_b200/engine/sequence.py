@@ -30,7 +30,11 @@ class SamplingParams:
     stop_token_ids: List[int] = field(default_factory=list)
     ignore_eos: bool = False
     seed: Optional[int] = None
-    logprobs: Optional[int] = None
+    logprobs: Optional[int] = None      # return the chosen token's and the top-k log-probabilities
+    typical_p: float = 1.0              # locally typical sampling mass (1 = off)
+    mirostat: int = 0                   # 2 = mirostat v2 (target surprise tau, learning rate eta)
+    mirostat_tau: float = 5.0
+    mirostat_eta: float = 0.1
 
     def validate(self) -> "SamplingParams":
         if self.temperature < 0:
@@ -47,6 +51,12 @@ class SamplingParams:
             raise ValueError("frequency/presence penalties must be in [-2, 2]")
         if self.max_tokens < 1:
             raise ValueError("max_tokens must be >= 1")
+        if not 0.0 < self.typical_p <= 1.0:
+            raise ValueError("typical_p must be in (0, 1]")
+        if self.mirostat not in (0, 2):
+            raise ValueError("mirostat must be 0 (off) or 2 (mirostat v2)")
+        if self.logprobs is not None and not 0 <= self.logprobs <= 20:
+            raise ValueError("logprobs must be in [0, 20]")
         if isinstance(self.stop, str):
             self.stop = [self.stop]
         return self
@@ -58,6 +68,11 @@ class SamplingParams:
     @property
     def needs_penalties(self) -> bool:
         return self.repetition_penalty != 1.0 or self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
+
+    @property
+    def needs_host_sampling(self) -> bool:
+        """Sampling modes served by the per-row host path (typical, mirostat, logprobs)."""
+        return self.typical_p < 1.0 or self.mirostat != 0 or self.logprobs is not None
 
 
 class SeqStatus(enum.Enum):
@@ -83,7 +98,7 @@ class Sequence:
     __slots__ = ("seq_id", "request_id", "prompt_token_ids", "output_token_ids", "params", "lora_id",
                  "arrival_time", "num_computed_tokens", "status", "first_token_time", "finish_time",
                  "token_times", "block_hashes", "num_preemptions", "predicted_len", "stop_reason",
-                 "output_text", "priority", "scheduled_time", "pending", "tenant")
+                 "output_text", "priority", "scheduled_time", "pending", "tenant", "mirostat_mu", "logprobs")
 
     def __init__(self, request_id: str, prompt_token_ids: List[int], params: SamplingParams,
                  lora_id: int = 0, arrival_time: Optional[float] = None, priority: int = 0):
@@ -108,6 +123,8 @@ class Sequence:
         self.scheduled_time: Optional[float] = None
         self.pending = 0  # async scheduling: sampled tokens not yet read back (placeholders -1)
         self.tenant = ""  # quota accounting (EngineConfig.tenant_quotas)
+        self.mirostat_mu: Optional[float] = None
+        self.logprobs: List[dict] = []  # per output token when params.logprobs is set
 
     @property
     def num_tokens(self) -> int:
@@ -149,3 +166,4 @@ class RequestOutput:
     finish_reason: Optional[str] = None
     text: str = ""
     metrics: dict = field(default_factory=dict)
+    logprobs: Optional[List[dict]] = None  # per output token (SamplingParams.logprobs)

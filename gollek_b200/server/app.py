@@ -63,6 +63,12 @@ class ChatRequest(BaseModel):
     n: int = 1
     user: Optional[str] = None
     adapter_id: Optional[str] = None
+    logprobs: Optional[bool] = None
+    top_logprobs: Optional[int] = None
+    typical_p: Optional[float] = None
+    mirostat: Optional[int] = None
+    mirostat_tau: Optional[float] = None
+    mirostat_eta: Optional[float] = None
 
 
 class CompletionRequest(BaseModel):
@@ -82,6 +88,11 @@ class CompletionRequest(BaseModel):
     ignore_eos: bool = False
     n: int = 1
     adapter_id: Optional[str] = None
+    logprobs: Optional[int] = None
+    typical_p: Optional[float] = None
+    mirostat: Optional[int] = None
+    mirostat_tau: Optional[float] = None
+    mirostat_eta: Optional[float] = None
 
 
 class EmbeddingRequest(BaseModel):
@@ -174,7 +185,16 @@ def build_sampling(st: ServerState, d: Dict[str, Any], defaults: Dict[str, Any])
         stop=list(stop),
         seed=_param(d, "seed"),
         ignore_eos=bool(_param(d, "ignore_eos", default=False)),
+        typical_p=float(_param(d, "typical_p", "typicalP", default=1.0)),
+        mirostat=int(_param(d, "mirostat", default=0)),
+        mirostat_tau=float(_param(d, "mirostat_tau", default=5.0)),
+        mirostat_eta=float(_param(d, "mirostat_eta", default=0.1)),
     )
+    lp = _param(d, "logprobs")
+    if lp is True:  # chat: logprobs=true + top_logprobs=k
+        sp.logprobs = int(_param(d, "top_logprobs", default=0) or 0)
+    elif lp is not None and lp is not False:
+        sp.logprobs = int(lp)
     try:
         return sp.validate()
     except ValueError as e:
@@ -359,13 +379,29 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             return await sse_stream(batch[0], sp, cid, lora, frame, final)
         outs = await asyncio.gather(*[run_full(p, SamplingParams(**vars(sp)), lora_id=lora) for p in batch])
         choices, pt, ct = [], 0, 0
+        def tokstr(t):
+            return st.tokenizer.decode([t]) if st.tokenizer is not None else str(t)
+
         for i, o in enumerate(outs):
+            lp = None
+            if o.logprobs is not None:
+                lp = {"tokens": [tokstr(e["token"]) for e in o.logprobs],
+                      "token_logprobs": [e["logprob"] for e in o.logprobs],
+                      "top_logprobs": [{tokstr(t): v for t, v in e.get("top", {}).items()} for e in o.logprobs]}
             choices.append({"index": i, "text": o.text or detok(o.output_token_ids), "finish_reason": o.finish_reason,
-                            "logprobs": None})
+                            "logprobs": lp})
             pt += len(o.prompt_token_ids)
             ct += len(o.output_token_ids)
         return {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name, "choices": choices,
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
+
+    def chat_logprobs(o):
+        if o.logprobs is None:
+            return None
+        ts = (lambda t: st.tokenizer.decode([t])) if st.tokenizer is not None else str
+        return {"content": [{"token": ts(e["token"]), "logprob": e["logprob"],
+                             "top_logprobs": [{"token": ts(t), "logprob": v} for t, v in e.get("top", {}).items()]}
+                            for e in o.logprobs]}
 
     async def _chat(req: ChatRequest, force_stream: bool = False):
         if req.n != 1:
@@ -396,7 +432,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         pt, ct = len(o.prompt_token_ids), len(o.output_token_ids)
         return {"id": cid, "object": "chat.completion", "created": _now(), "model": st.model_name,
                 "choices": [{"index": 0, "message": {"role": "assistant", "content": o.text or detok(o.output_token_ids)},
-                             "finish_reason": o.finish_reason}],
+                             "finish_reason": o.finish_reason, "logprobs": chat_logprobs(o)}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
 
     @app.post("/v1/chat/completions")
