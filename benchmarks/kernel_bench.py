@@ -165,6 +165,17 @@ def main():
                     ms = time_cuda(lambda: ops.linear(x, qw, out=out), iters=args.iters, flush_bytes=flush)
                     rec(f"gguf_{'q4k' if qtype == 12 else 'q8_0'}_{name}_M{M}", ms, 2.0 * M * N * K,
                         qw.nbytes() + 2.0 * M * (K + N))
+    if "int4" in only:
+        from gollek_b200.quant import int4 as I4
+        for name, N, K in (("qkv", 6144, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336)):
+            w = (torch.randn(N, K, device=dev) * 0.02)
+            for fmt, qw in (("int4g128", I4.quantize_rtn(w, 128)), ("nf4", I4.quantize_nf4(w, 64))):
+                qw = qw.to(dev)
+                for M in (1, 8, 256):
+                    x = torch.randn(M, K, device=dev).bfloat16()
+                    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                    ms = time_cuda(lambda: ops.linear(x, qw, out=out), iters=args.iters, flush_bytes=flush)
+                    rec(f"{fmt}_{name}_M{M}", ms, 2.0 * M * N * K, qw.nbytes() + 2.0 * M * (K + N))
     if "fp8" in only:
         from gollek_b200.quant import fp8 as F8
         # Llama-3-70B per-rank shapes at TP=8 (hidden 8192, 64/8 heads, ffn 28672)

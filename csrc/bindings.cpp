@@ -293,6 +293,39 @@ void kv_blocks_py(torch::Tensor cache, torch::Tensor packed, torch::Tensor block
                    span, gather, cur_stream());
 }
 
+// 4-bit weights: q uint8 [N, K/2], scale/zero bf16 [N, K/g] (zero absent for NF4)
+static void check_int4(torch::Tensor q, torch::Tensor scale, c10::optional<torch::Tensor> zero, int64_t N,
+                       int64_t K, int64_t g) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kByte && q.is_contiguous() && q.numel() == N * K / 2,
+              "int4: q must be uint8 [N, K/2]");
+  check_bf16(scale, "scale");
+  TORCH_CHECK(scale.is_contiguous() && scale.numel() == N * (K / g), "int4: scale [N, K/g]");
+  if (zero.has_value()) {
+    check_bf16(*zero, "zero");
+    TORCH_CHECK(zero->is_contiguous() && zero->numel() == N * (K / g), "int4: zero [N, K/g]");
+  }
+}
+
+void int4_gemv_py(torch::Tensor out, torch::Tensor x, torch::Tensor q, torch::Tensor scale,
+                  c10::optional<torch::Tensor> zero, int64_t N, int64_t K, int64_t g, bool lut, bool swiglu) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  check_int4(q, scale, zero, N, K, g);
+  TORCH_CHECK(x.dim() == 2 && x.size(1) == K && x.stride(1) == 1, "int4 gemv: x [M, K]");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == (swiglu ? N / 2 : N) && out.stride(1) == 1, "int4 gemv: out");
+  launch_int4_gemv(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), q.data_ptr(), scale.data_ptr(),
+                   zero.has_value() ? zero->data_ptr() : nullptr, x.size(0), N, K, g, lut, swiglu, cur_stream());
+}
+
+void int4_dequant_py(torch::Tensor out, torch::Tensor q, torch::Tensor scale, c10::optional<torch::Tensor> zero,
+                     int64_t N, int64_t K, int64_t g, bool lut) {
+  check_bf16(out, "out");
+  check_int4(q, scale, zero, N, K, g);
+  TORCH_CHECK(out.is_contiguous() && out.numel() == N * K, "int4 dequant: out [N, K]");
+  launch_int4_dequant(out.data_ptr(), q.data_ptr(), scale.data_ptr(), zero.has_value() ? zero->data_ptr() : nullptr,
+                      N, K, g, lut, cur_stream());
+}
+
 std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
   int bn = 0, sp = 1;
   gemm_plan((int)M, (int)N, (int)K, (int)epi, bn, sp);
@@ -555,6 +588,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("num_sms", &device_num_sms);
   m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)");
   m.def("moe_capacity_rows", &moe_capacity_rows);
+  m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
+  m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");
   m.def("kv_blocks", &kv_blocks_py, "gather (or scatter) one sequence's paged KV blocks, every layer");
   m.def("moe_ws_ints", &moe_ws_ints);
   m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");

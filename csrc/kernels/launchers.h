@@ -96,6 +96,12 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
 void launch_kv_blocks(void* cache, void* packed, const int* block_ids, int n, int layers, int64_t num_blocks,
                       int64_t span, bool gather, cudaStream_t s);
 
+// ---- 4-bit group-quantized weights (GPTQ / AWQ / RTN int4, NF4), canonical row-major layout
+void launch_int4_gemv(void* out, int64_t ldo, const void* x, int64_t ldx, const void* q, const void* scale,
+                      const void* zero, int M, int N, int K, int g, bool lut, bool swiglu, cudaStream_t s);
+void launch_int4_dequant(void* out, const void* q, const void* scale, const void* zero, int N, int K, int g, bool lut,
+                         cudaStream_t s);
+
 // ---- sampling (K11)
 void launch_argmax(int64_t* out, const void* logits, bool is_bf16, int B, int V, int64_t stride, cudaStream_t s);
 void launch_penalties(float* logits, int64_t stride, const int* triples, int n, const float* rep, const float* freq,

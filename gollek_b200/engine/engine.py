@@ -60,6 +60,8 @@ class LLMEngine:
             self.model.load_weights(weights)
             if cfg.quantization == "fp8":
                 self.model.quantize_fp8()
+            elif cfg.quantization in ("int4", "nf4"):
+                self.model.quantize_int4(cfg.quantization)
         if cfg.offload_layers > 0 and self.device.type == "cuda":
             self.model.enable_offload(cfg.offload_layers, cfg.offload_prefetch)
             cfg.use_cuda_graphs = False
@@ -445,7 +447,13 @@ def load_model_source(source: str, keep_quantized: bool = False):
         with open(os.path.join(d, "config.json")) as fh:
             cfg = ModelConfig.from_hf(json.load(fh))
         ck = SafetensorsCheckpoint(source)
-        return cfg, ck.get, load_tokenizer(d)
+        with open(os.path.join(d, "config.json")) as fh:
+            qc = json.load(fh).get("quantization_config") or {}
+        getter = ck.get
+        if qc.get("quant_method") in ("awq", "gptq"):
+            from ..quant.int4 import quantized_checkpoint_getter
+            getter = quantized_checkpoint_getter(ck, qc)
+        return cfg, getter, load_tokenizer(d)
     raise ValueError(f"unknown model source {source!r}")
 
 

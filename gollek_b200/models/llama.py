@@ -214,27 +214,33 @@ class LlamaModel:
         H, Hk, D = self.H, self.Hk, self.D
         dev, dt = self.device, self.dtype
 
+        from ..quant import int4 as I4
         from ..quant.gguf_weights import QWeight, cat_rows, interleave_rows
+        quantized = (QWeight, I4.Int4Weight)
 
         def t(name):
             v = get(name)
             if type(v).__name__ == "QuantizedWeight":  # GGUF blocks stay quantized on the device
                 return QWeight.from_quantized(v).to(dev)
+            if isinstance(v, I4.Int4Weight):  # GPTQ / AWQ / NF4 stay 4-bit on the device
+                return v.to(dev)
             return v.to(device=dev, dtype=dt)
 
         def cat(ws):
+            if isinstance(ws[0], I4.Int4Weight):
+                return I4.cat_rows(ws)
             return cat_rows(ws) if isinstance(ws[0], QWeight) else torch.cat(ws, 0)
 
         def gate_up(g, u, fpad=None):
             fpad = self.F_pad if fpad is None else fpad
-            if isinstance(g, QWeight):
+            if isinstance(g, quantized):
                 if fpad != g.N:
                     raise ValueError("quantized FFN width must be a multiple of 64 per TP rank")
-                return interleave_rows(g, u)
+                return I4.interleave_rows(g, u) if isinstance(g, I4.Int4Weight) else interleave_rows(g, u)
             return ops.interleave_gate_up(_pad_rows(g, fpad), _pad_rows(u, fpad))
 
         def down(d, fpad=None):
-            return d if isinstance(d, QWeight) else _pad_cols(d, self.F_pad if fpad is None else fpad)
+            return d if isinstance(d, quantized) else _pad_cols(d, self.F_pad if fpad is None else fpad)
 
         Dl = self.D_logical
 
@@ -348,6 +354,23 @@ class LlamaModel:
                 if "experts" in L:
                     L["experts"] = [(quantize_weight(a), quantize_weight(b)) for a, b in L["experts"]]
             self.layers.append(L)
+
+    def quantize_int4(self, kind: str = "int4", group: int = 128) -> None:
+        """Quantize the dense linear weights (qkv, o, gate/up, down) to 4 bits at load: ``int4`` =
+        round-to-nearest asymmetric int4 per ``group`` columns, ``nf4`` = NF4 with 64-column absmax
+        blocks. Per-row quantization, so the fused/interleaved row layouts are unaffected."""
+        from ..quant.int4 import quantize_nf4, quantize_rtn
+        for L in self.layers:
+            for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+                v = L.get(k)
+                if isinstance(v, torch.Tensor):
+                    K = v.shape[1]
+                    g = next(x for x in (group, 128, 64, 32) if K % x == 0) if K % 32 == 0 else None
+                    if g is None:
+                        raise ValueError(f"4-bit quantization needs K divisible by 32 (got {K})")
+                    L[k] = quantize_nf4(v, min(64, g)) if kind == "nf4" else quantize_rtn(v, g)
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
 
     def quantize_fp8(self) -> None:
         """Convert the linear weights (qkv, o, gate/up, down; experts too) to block-scaled FP8, layer by

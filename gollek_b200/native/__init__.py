@@ -43,6 +43,7 @@ CUDA_SOURCES = [
     "kernels/attention_tc.cu",
     "kernels/moe.cu",
     "kernels/kv_transfer.cu",
+    "kernels/int4.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

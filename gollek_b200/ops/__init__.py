@@ -219,6 +219,40 @@ def _qlinear(a: torch.Tensor, w, out: Optional[torch.Tensor], swiglu: bool) -> t
     return out
 
 
+INT4_GEMV_MAX_TOKENS = 8
+
+
+def _is_int4(w) -> bool:
+    return type(w).__name__ == "Int4Weight"
+
+
+def _int4_linear(a: torch.Tensor, w, out: Optional[torch.Tensor], swiglu: bool) -> torch.Tensor:
+    """Matmul with a 4-bit group-quantized weight (GPTQ / AWQ / NF4): fused dequant GEMV for up
+    to 8 tokens; otherwise L2-sized row chunks dequantized to bf16 and fed to the tcgen05 GEMM."""
+    M, N = a.shape[0], w.N
+    n_out = N // 2 if swiglu else N
+    if not a.is_cuda:
+        wd = w.dequantize(a.dtype)
+        y = ref.gemm_swiglu(a, wd, SWIGLU_GROUP) if swiglu else ref.gemm(a, wd)
+        return _cpu(y, out)
+    out = torch.empty(M, n_out, dtype=a.dtype, device=a.device) if out is None else out
+    if M <= INT4_GEMV_MAX_TOKENS:
+        _C().int4_gemv(out, a, w.q, w.scale, w.zero, N, w.K, w.group, w.nf4, swiglu)
+        return out
+    rows = max(128, GGUF_CHUNK_BYTES // (2 * w.K) // 128 * 128)
+    scratch = torch.empty(min(rows, N), w.K, dtype=torch.bfloat16, device=a.device)
+    for n0 in range(0, N, rows):
+        n1 = min(N, n0 + rows)
+        wd = scratch[: n1 - n0]
+        _C().int4_dequant(wd, w.q[n0:n1], w.scale[n0:n1], None if w.zero is None else w.zero[n0:n1], n1 - n0, w.K,
+                          w.group, w.nf4)
+        if swiglu:
+            _gemm(out[:, n0 // 2: n1 // 2], a, wd, None, EPI_SWIGLU, 0)
+        else:
+            _gemm(out[:, n0:n1], a, wd, None, EPI_NONE, 0)
+    return out
+
+
 def _is_q(w) -> bool:
     return type(w).__name__ == "QWeight"
 
@@ -259,8 +293,8 @@ def linear(a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = 
         if residual is not None:
             y.add_(residual)
         return y
-    if _is_q(w):
-        y = _qlinear(a, w, out, False)
+    if _is_q(w) or _is_int4(w):
+        y = (_qlinear if _is_q(w) else _int4_linear)(a, w, out, False)
         if residual is not None:
             y.add_(residual)
         return y
@@ -277,12 +311,14 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: Optional[torch.
                   bn: int = 0, act: str = "silu") -> torch.Tensor:
     """act(a @ Wg^T) * (a @ Wu^T) with gate/up rows interleaved by ``interleave_gate_up``;
     ``act`` is ``silu`` (SwiGLU, Llama) or ``gelu_tanh`` (GeGLU, Gemma), fused in the GEMM epilogue."""
-    if act != "silu" and (_is_q(w_gate_up) or _is_fp8(w_gate_up)):
+    if act != "silu" and (_is_q(w_gate_up) or _is_fp8(w_gate_up) or _is_int4(w_gate_up)):
         # quantized GeGLU: plain product, gate activation on the host-side graph
         y = linear(a, w_gate_up)
         return _copy_into(ref.glu_interleaved(y, SWIGLU_GROUP, act).to(a.dtype), out)
     if _is_q(w_gate_up):
         return _qlinear(a, w_gate_up, out, True)
+    if _is_int4(w_gate_up):
+        return _int4_linear(a, w_gate_up, out, True)
     if _is_fp8(w_gate_up):
         return linear_fp8(a, w_gate_up, out, swiglu=True)
     if not a.is_cuda:
