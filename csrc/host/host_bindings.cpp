@@ -8,6 +8,7 @@ torch::Tensor dequantize_q4_k(torch::Tensor raw, int64_t n);
 void register_block_allocator(pybind11::module& m);
 void register_forelen(pybind11::module& m);
 void register_spec(pybind11::module& m);
+void register_grammar(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "gollek_b200 host runtime";
@@ -18,4 +19,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_block_allocator(m);
   register_forelen(m);
   register_spec(m);
+  register_grammar(m);
 }

@@ -149,12 +149,29 @@ class LLMEngine:
             raise ValueError(f"unknown LoRA adapter id {lora_id}")
         seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
         seq.tenant = tenant or ""
+        if params.guided:
+            seq.guide = self._make_guide(params)
         self.scheduler.add(seq)
         if params.needs_penalties or params.needs_host_sampling:
             self._n_host_sampling += 1
         self.seqs[request_id] = seq
         self.metrics.on_arrival()
         return request_id
+
+    def _make_guide(self, params: SamplingParams):
+        """A constrained-decoding matcher for one request (vocabulary trie built on first use)."""
+        if self.tokenizer is None or not hasattr(self.tokenizer, "token_bytes"):
+            raise ValueError("constrained decoding needs a tokenizer with a byte vocabulary")
+        if getattr(self, "_grammar", None) is None:
+            toks = self.tokenizer.token_bytes()
+            toks = (toks + [b""] * self.model_cfg.vocab_size)[: self.model_cfg.vocab_size]
+            self._grammar = host_ext().GrammarCompiler(toks, int(self.eos_token_id))
+        try:
+            if params.guided_regex is not None:
+                return self._grammar.regex(params.guided_regex)
+            return self._grammar.json(True)
+        except Exception as e:
+            raise ValueError(f"invalid constraint: {e}") from e
 
     def add_lora(self, name: str, path: Optional[str] = None, seed: Optional[int] = None, rank: int = 16) -> int:
         """Register a PEFT adapter directory (or a random adapter when ``path`` is None); returns its id."""
@@ -182,6 +199,9 @@ class LLMEngine:
         """Stop test for ``tok``, the ``n_out``-th output token (default: the last one appended)."""
         p = seq.params
         n_out = len(seq.output_token_ids) if n_out is None else n_out
+        if seq.guide is not None and tok == self.eos_token_id:
+            seq.stop_reason = tok
+            return SeqStatus.FINISHED_STOPPED  # a constrained output ends when the grammar lets it
         if n_out >= p.min_tokens:
             if not p.ignore_eos and tok == self.eos_token_id:
                 seq.stop_reason = tok
@@ -209,7 +229,7 @@ class LLMEngine:
         for c in sched.decode:
             s = c.seq
             room = min(s.params.max_tokens - len(s.output_token_ids), self.cfg.max_model_len - s.num_tokens) - 1
-            k = 0 if s.params.needs_penalties else max(0, min(K, room))
+            k = 0 if (s.params.needs_penalties or s.params.needs_host_sampling) else max(0, min(K, room))
             if k and not self.kv.ensure(s, s.num_tokens + k):
                 k = 0
             seqs.append(s)

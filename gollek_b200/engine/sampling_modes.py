@@ -30,8 +30,12 @@ def _generator(seq: Sequence, base_seed: int, device) -> torch.Generator:
 
 
 def sample_row(row: torch.Tensor, raw: torch.Tensor, seq: Sequence, base_seed: int) -> int:
-    """row: penalised fp32 logits of one sequence; raw: its unpenalised logits (for logprobs)."""
+    """row: penalised fp32 logits of one sequence; raw: its unpenalised logits (for logprobs).
+    A constrained request (``seq.guide``) samples among the tokens its grammar allows."""
     p = seq.params
+    if seq.guide is not None:
+        allowed = seq.guide.mask().to(row.device)
+        row = torch.where(allowed, row, torch.full_like(row, float("-inf")))
     if p.greedy:
         tok = int(row.argmax())
     else:
@@ -73,6 +77,8 @@ def sample_row(row: torch.Tensor, raw: torch.Tensor, seq: Sequence, base_seed: i
         if p.mirostat == 2:
             observed = -math.log2(max(float(probs[tok]), 1e-30))
             seq.mirostat_mu = mu - p.mirostat_eta * (observed - p.mirostat_tau)
+    if seq.guide is not None:
+        seq.guide.advance(tok)
     if p.logprobs is not None:
         lp = torch.log_softmax(raw.float(), -1)
         entry = {"token": tok, "logprob": float(lp[tok])}

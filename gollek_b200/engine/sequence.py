@@ -35,6 +35,8 @@ class SamplingParams:
     mirostat: int = 0                   # 2 = mirostat v2 (target surprise tau, learning rate eta)
     mirostat_tau: float = 5.0
     mirostat_eta: float = 0.1
+    guided_json: bool = False           # constrain the output to a JSON object
+    guided_regex: Optional[str] = None  # constrain the output to a full match of this regex
 
     def validate(self) -> "SamplingParams":
         if self.temperature < 0:
@@ -72,7 +74,12 @@ class SamplingParams:
     @property
     def needs_host_sampling(self) -> bool:
         """Sampling modes served by the per-row host path (typical, mirostat, logprobs)."""
-        return self.typical_p < 1.0 or self.mirostat != 0 or self.logprobs is not None
+        return (self.typical_p < 1.0 or self.mirostat != 0 or self.logprobs is not None or self.guided_json
+                or self.guided_regex is not None)
+
+    @property
+    def guided(self) -> bool:
+        return self.guided_json or self.guided_regex is not None
 
 
 class SeqStatus(enum.Enum):
@@ -98,7 +105,8 @@ class Sequence:
     __slots__ = ("seq_id", "request_id", "prompt_token_ids", "output_token_ids", "params", "lora_id",
                  "arrival_time", "num_computed_tokens", "status", "first_token_time", "finish_time",
                  "token_times", "block_hashes", "num_preemptions", "predicted_len", "stop_reason",
-                 "output_text", "priority", "scheduled_time", "pending", "tenant", "mirostat_mu", "logprobs")
+                 "output_text", "priority", "scheduled_time", "pending", "tenant", "mirostat_mu", "logprobs",
+                 "guide")
 
     def __init__(self, request_id: str, prompt_token_ids: List[int], params: SamplingParams,
                  lora_id: int = 0, arrival_time: Optional[float] = None, priority: int = 0):
@@ -125,6 +133,7 @@ class Sequence:
         self.tenant = ""  # quota accounting (EngineConfig.tenant_quotas)
         self.mirostat_mu: Optional[float] = None
         self.logprobs: List[dict] = []  # per output token when params.logprobs is set
+        self.guide = None  # constrained decoding: native GrammarMatcher of the output so far
 
     @property
     def num_tokens(self) -> int:

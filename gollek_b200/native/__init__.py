@@ -51,6 +51,7 @@ HOST_SOURCES = [
     "host/block_allocator.cpp",
     "host/forelen.cpp",
     "host/spec_ngram.cpp",
+    "host/grammar.cpp",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -69,6 +69,8 @@ class ChatRequest(BaseModel):
     mirostat: Optional[int] = None
     mirostat_tau: Optional[float] = None
     mirostat_eta: Optional[float] = None
+    response_format: Optional[Dict[str, Any]] = None
+    guided_regex: Optional[str] = None
 
 
 class CompletionRequest(BaseModel):
@@ -93,6 +95,8 @@ class CompletionRequest(BaseModel):
     mirostat: Optional[int] = None
     mirostat_tau: Optional[float] = None
     mirostat_eta: Optional[float] = None
+    response_format: Optional[Dict[str, Any]] = None
+    guided_regex: Optional[str] = None
 
 
 class EmbeddingRequest(BaseModel):
@@ -190,6 +194,14 @@ def build_sampling(st: ServerState, d: Dict[str, Any], defaults: Dict[str, Any])
         mirostat_tau=float(_param(d, "mirostat_tau", default=5.0)),
         mirostat_eta=float(_param(d, "mirostat_eta", default=0.1)),
     )
+    rf = _param(d, "response_format") or {}
+    if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
+        sp.guided_json = True  # any JSON object (a json_schema's structure is not enforced)
+    if _param(d, "guided_json", "json"):
+        sp.guided_json = True
+    rx = _param(d, "guided_regex", "regex")
+    if rx:
+        sp.guided_regex = str(rx)
     lp = _param(d, "logprobs")
     if lp is True:  # chat: logprobs=true + top_logprobs=k
         sp.logprobs = int(_param(d, "top_logprobs", default=0) or 0)

@@ -14,6 +14,35 @@ import os
 from typing import Dict, List, Optional
 
 
+def _gpt2_byte_decoder() -> Dict[str, int]:
+    """Inverse of the GPT-2 byte-level BPE alphabet: printable Latin-1 bytes stand for themselves,
+    the remaining bytes are shifted to code points 256 + n in byte order."""
+    keep = list(range(ord("!"), ord("~") + 1)) + list(range(ord("¡"), ord("¬") + 1)) + list(range(ord("®"), ord("ÿ") + 1))
+    chars = list(keep)
+    n = 0
+    for b in range(256):
+        if b not in keep:
+            keep.append(b)
+            chars.append(256 + n)
+            n += 1
+    return {chr(c): b for b, c in zip(keep, chars)}
+
+
+def _piece_bytes(piece: str, byte_level: bool, dec: Dict[str, int]) -> bytes:
+    """Bytes a vocabulary piece stands for (byte-level BPE or SentencePiece conventions)."""
+    if byte_level:
+        try:
+            return bytes(dec[ch] for ch in piece)
+        except KeyError:
+            return piece.encode("utf-8")
+    if len(piece) == 6 and piece.startswith("<0x") and piece.endswith(">"):
+        try:
+            return bytes([int(piece[3:5], 16)])
+        except ValueError:
+            pass
+    return piece.replace("▁", " ").encode("utf-8")
+
+
 class ByteTokenizer:
     """UTF-8 bytes mapped to ids 3..258 (0 = pad, 1 = bos, 2 = eos)."""
     offset = 3
@@ -28,6 +57,13 @@ class ByteTokenizer:
     def decode(self, ids: List[int]) -> str:
         bs = bytes(i - self.offset for i in ids if self.offset <= i < self.offset + 256)
         return bs.decode("utf-8", errors="replace")
+
+    def token_bytes(self) -> List[bytes]:
+        out = [b""] * self.vocab_size
+        for b in range(256):
+            if b + self.offset < self.vocab_size:
+                out[b + self.offset] = bytes([b])
+        return out
 
     def apply_chat_template(self, messages: List[dict]) -> str:
         return default_chat_template(messages)
@@ -49,6 +85,18 @@ class HFTokenizer:
 
     def decode(self, ids: List[int]) -> str:
         return self.tok.decode(ids, skip_special_tokens=True)
+
+    def token_bytes(self) -> List[bytes]:
+        vocab = self.tok.get_vocab(with_added_tokens=True)
+        special = {t.content for t in self.tok.get_added_tokens_decoder().values() if t.special} \
+            if hasattr(self.tok, "get_added_tokens_decoder") else set()
+        byte_level = any(("Ġ" in p or "Ċ" in p) for p in list(vocab)[:5000])
+        dec = _gpt2_byte_decoder()
+        out = [b""] * max(self.vocab_size, max(vocab.values()) + 1)
+        for piece, i in vocab.items():
+            if piece not in special:
+                out[i] = _piece_bytes(piece, byte_level, dec)
+        return out
 
     def apply_chat_template(self, messages: List[dict]) -> str:
         if self.chat_template:
@@ -102,6 +150,12 @@ class GGUFTokenizer:
                     ids.append(self.byte_ids.get(b, 0))
                 i += 1
         return ids
+
+    def token_bytes(self) -> List[bytes]:
+        byte_level = any(("Ġ" in p or "Ċ" in p) for p in self.tokens[:5000])
+        dec = _gpt2_byte_decoder()
+        return [b"" if (p.startswith("<") and p.endswith(">") and len(p) != 6) else _piece_bytes(p, byte_level, dec)
+                for p in self.tokens]
 
     def decode(self, ids: List[int]) -> str:
         out = bytearray()
