@@ -109,12 +109,15 @@ def main():
             out = torch.empty_like(q)
             flops = 4.0 * nseq * (L * L / 2) * Hq * D
             nbytes = 2.0 * (2 * T * Hq * D + 2 * T * Hk * D)
-            for tc in (True, False):
-                tiles = ops.prefill_tiles(qs.tolist(), ops.prefill_block_m(D, tc)).to(dev)
+            work = ops.prefill_schedule(qs.tolist(), sl.tolist(), Hq, Hk, D).to(dev)
+            variants = [(f"tcgen05_emu{e}", work, True, e) for e in (0, 1, 2)]
+            variants += [("tcgen05_1tile", ops.prefill_tiles(qs.tolist(), 128).to(dev), True, 0),
+                         ("mmasync", ops.prefill_tiles(qs.tolist(), 64).to(dev), False, 0)]
+            for name, tiles, tc, emu in variants:
                 ms = time_cuda(lambda: ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D), tiles=tiles,
-                                                                   out=out, tensor_cores=tc),
+                                                                   out=out, tensor_cores=tc, emu=emu),
                                iters=args.iters, flush_bytes=flush)
-                rec(f"attn_prefill_{'tcgen05' if tc else 'mmasync'}_{nseq}x{L}", ms, flops, nbytes)
+                rec(f"attn_prefill_{name}_{nseq}x{L}", ms, flops, nbytes)
     if "norm" in only:
         d = 4096
         for T in (256, 8192):

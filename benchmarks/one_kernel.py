@@ -33,6 +33,7 @@ def main():
     ap.add_argument("--nseq", type=int, default=4)
     ap.add_argument("--L", type=int, default=2048)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--emu", type=int, default=None, help="prefill: FMA-pipe exponential share (0, 1, 2)")
     a = ap.parse_args()
     dev = "cuda"
     if a.kind == "gemm":
@@ -67,7 +68,7 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         q = torch.randn(T, Hq, D, device=dev).bfloat16()
         for _ in range(a.reps):
-            ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D))
+            ops.paged_prefill_attention(q, cache, bt, sl, qs, 1 / math.sqrt(D), emu=a.emu)
     torch.cuda.synchronize()
     print("ok")
 

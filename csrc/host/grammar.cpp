@@ -533,7 +533,9 @@ class JsonMatcher : public Matcher {
 
 class RegexMatcher : public Matcher {
  public:
-  explicit RegexMatcher(std::shared_ptr<const Nfa> nfa) : nfa_(std::move(nfa)) {
+  // id: the pattern's number in its compiler; part of the mask-cache key, since NFA state sets of
+  // different patterns are not comparable.
+  RegexMatcher(std::shared_ptr<const Nfa> nfa, uint64_t id) : nfa_(std::move(nfa)), id_(id) {
     s_.on.assign((nfa_->st.size() + 63) / 64, 0);
     add(s_, nfa_->start);
   }
@@ -564,7 +566,9 @@ class RegexMatcher : public Matcher {
       if (nfa_->st[k].kind == 2 && ((s_.on[k >> 6] >> (k & 63)) & 1)) return true;
     return false;
   }
-  std::string key() const override { return "r" + s_.key(); }
+  std::string key() const override {
+    return "r" + std::string(reinterpret_cast<const char*>(&id_), sizeof(id_)) + s_.key();
+  }
   void mask_into(const Trie& trie, bool* out) const override { walk_trie(trie, 0, *this, out); }
 
  private:
@@ -578,6 +582,7 @@ class RegexMatcher : public Matcher {
     }
   }
   std::shared_ptr<const Nfa> nfa_;
+  uint64_t id_;
   RegexState s_;
 };
 
@@ -612,6 +617,17 @@ class GrammarCompiler {
     return out;
   }
 
+  // Compiled NFA and id of a pattern (one per distinct pattern, reused by later requests).
+  std::pair<std::shared_ptr<const Nfa>, uint64_t> regex(const std::string& pattern) {
+    auto it = patterns_.find(pattern);
+    if (it != patterns_.end()) return it->second;
+    auto nfa = std::make_shared<const Nfa>(RegexCompiler(pattern).compile());
+    if (patterns_.size() >= kPatterns) patterns_.clear();  // ids stay unique: the counter keeps going
+    auto v = std::make_pair(nfa, next_id_++);
+    patterns_[pattern] = v;
+    return v;
+  }
+
   bool advance(Matcher& m, int64_t token, const std::vector<std::string>& token_bytes) const {
     if (token == eos_) return m.accepting();
     if (token < 0 || token >= (int64_t)token_bytes.size()) return false;
@@ -622,7 +638,10 @@ class GrammarCompiler {
 
  private:
   static constexpr size_t kCache = 4096;
+  static constexpr size_t kPatterns = 256;
   Trie trie_;
+  uint64_t next_id_ = 0;
+  std::unordered_map<std::string, std::pair<std::shared_ptr<const Nfa>, uint64_t>> patterns_;
   int64_t eos_;
   std::list<std::string> lru_;
   std::unordered_map<std::string, std::pair<torch::Tensor, std::list<std::string>::iterator>> cache_;
@@ -676,7 +695,7 @@ void register_grammar(pybind11::module& m) {
              return PyMatcher{c.g, c.bytes, std::make_unique<JsonMatcher>(top_object)};
            }, py::arg("top_object") = true)
       .def("regex", [](PyCompiler& c, const std::string& pattern) {
-        auto nfa = std::make_shared<const Nfa>(RegexCompiler(pattern).compile());
-        return PyMatcher{c.g, c.bytes, std::make_unique<RegexMatcher>(nfa)};
+        auto nfa = c.g->regex(pattern);
+        return PyMatcher{c.g, c.bytes, std::make_unique<RegexMatcher>(nfa.first, nfa.second)};
       });
 }

@@ -351,6 +351,384 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Two-tile prefill kernel (the serving default for head_dim 128).
+//
+// One CTA = two 128-row query tiles ("slots") that read the same KV tiles: two query heads of one
+// GQA group over the same rows (group size even), or two consecutive row tiles of one head.
+// 10 warps:
+//   warps 0-3  softmax of slot 0, warps 4-7 softmax of slot 1 (one query row per thread = TMEM lane)
+//   warp 8     TMA: both Q tiles once, then K and V of each 128-key tile (16-token paged boxes) into a
+//              2-stage ring with separate K / V barriers (S can start before V lands)
+//   warp 9     MMA (one thread): per KV tile j the tensor pipe runs PV0(j-1), S0(j), PV1(j-1), S1(j),
+//              so slot 1's softmax overlaps PV0/S0 and slot 0's overlaps PV1/S1
+// TMEM (512 columns): S0 | S1 | O0 | O1. P (bf16) is written back over the first 64 columns of its
+// S buffer and is the TMEM A operand of the PV MMA; tcgen05.mma ops of one thread run in issue
+// order, so PV_i(j-1) has read P_i before S_i(j) overwrites it.
+// Online softmax in the log2 domain keeps a running max that is only raised when a tile's max exceeds
+// it by more than 8 (P <= 2^8 stays exact enough in bf16), so O is rescaled in TMEM only on those
+// rare tiles; s_full_i(j) is committed after PV_i(j-1) was issued, so O_i is quiescent while the
+// softmax of tile j runs. Tiles that need no mask (below the causal diagonal, inside the sequence
+// and the window) skip the mask, and EMU > 0 evaluates a share of the exponentials with a cubic
+// on the FMA pipe instead of MUFU (EMU 1: every 4th column, 2: every 2nd).
+// ---------------------------------------------------------------------------------------------
+constexpr int kFaThreads = 320;
+constexpr int kFaSmem = 1024 + 2 * kQBytes + kStages * 2 * kKVTile + 256;
+
+GOLLEK_DEVICE float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x on the FMA pipe: x = n + f with n = round(x) (the 1.5 * 2^23 shifter), |f| <= 1/2, 2^f by a
+// cubic fitted to 2^f on [-1/2, 1/2] (relative error 7.5e-5, below bf16's 2^-8), 2^n added to the
+// exponent field. x is clamped to -125 so the result stays a normal float.
+GOLLEK_DEVICE float ex2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517150089144707f, f, 0.24261096119880676f), f, 0.6932609677314758f), f,
+                       0.9999280571937561f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+GOLLEK_DEVICE void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+struct FaSlot {
+  int h, q_off, rows, kv_end, a, b;  // KV tiles [a, b)
+};
+
+template <int EMU>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    prefill_fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                      __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
+                      int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
+                      const int4* __restrict__ work, int pair_heads, int H, int Hk, float scale_log2,
+                      uint32_t* status, int window, float softcap_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;                          // slot i at + i * kQBytes
+  uint8_t* sKV = sQ + 2 * kQBytes;             // stage s: K at + s*2*tile, V at + s*2*tile + tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * 2 * kKVTile);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;                 // [2]
+  uint64_t* v_full = bars + 3;                 // [2]
+  uint64_t* kv_empty = bars + 5;               // [2]
+  uint64_t* s_full = bars + 7;                 // [slot]
+  uint64_t* p_full = bars + 9;                 // [slot]
+  uint64_t* o_done = bars + 11;                // [slot]
+  uint64_t* done_bar = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int4 wk = work[blockIdx.y];
+  const int b = wk.x;
+  const int qs = query_start[b], qlen = query_start[b + 1] - qs;
+  const int L = seq_lens[b];
+  const int ctx0 = L - qlen;
+  FaSlot sl[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    FaSlot& t = sl[i];
+    t.h = pair_heads ? 2 * blockIdx.x + i : blockIdx.x;
+    t.q_off = pair_heads ? wk.y : (i == 0 ? wk.y : wk.z);
+    const bool valid = t.q_off >= 0 && t.q_off < qlen;
+    t.rows = valid ? min(kTQ, qlen - t.q_off) : 0;
+    t.kv_end = valid ? min(L, ctx0 + t.q_off + t.rows) : 0;
+    t.a = (valid && window > 0) ? max(0, ctx0 + t.q_off - window + 1) / kTK : 0;
+    t.b = valid ? (t.kv_end + kTK - 1) / kTK : 0;
+    if (t.b <= t.a) t.a = t.b = 0;
+  }
+  const int kh = sl[0].h / (H / Hk);
+  const bool v0 = sl[0].b > sl[0].a, v1 = sl[1].b > sl[1].a;
+  const int jlo = (v0 && v1) ? min(sl[0].a, sl[1].a) : (v0 ? sl[0].a : sl[1].a);
+  const int jhi = max(sl[0].b, sl[1].b);
+  const int kv_end = max(sl[0].kv_end, sl[1].kv_end);
+  const int* bt = block_tables + (int64_t)b * bt_stride;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (elect_one() && jhi > jlo) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmKV);
+      mbar_arrive_expect_tx(q_full, ((v0 ? 1 : 0) + (v1 ? 1 : 0)) * kQBytes);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        if (sl[i].b > sl[i].a) {
+          const int qrow = qs + sl[i].q_off;
+          tma_load_2d(sQ + i * kQBytes, &tmQ, sl[i].h * kD, qrow, q_full);
+          tma_load_2d(sQ + i * kQBytes + kQBytes / 2, &tmQ, sl[i].h * kD + 64, qrow, q_full);
+        }
+      }
+      int issued = 0;
+      bool ok = true;
+      for (int j = jlo; j < jhi; ++j) {
+        const int idx = j - jlo, st = idx & 1;
+        if (!waitq(&kv_empty[st], ((idx >> 1) & 1) ^ 1, status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dk = sKV + st * 2 * kKVTile;
+        uint8_t* dv = dk + kKVTile;
+        mbar_arrive_expect_tx(&k_full[st], kKVTile);
+        for (int blk = 0; blk < kTK / kBS; ++blk) {
+          const int kb = (j * kTK) / kBS + blk;
+          const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
+          const int rk = ((pb * 2 + 0) * Hk + kh) * kBS;
+          tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &k_full[st]);
+          tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &k_full[st]);
+        }
+        mbar_arrive_expect_tx(&v_full[st], kKVTile);
+        for (int blk = 0; blk < kTK / kBS; ++blk) {
+          const int kb = (j * kTK) / kBS + blk;
+          const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
+          const int rv = ((pb * 2 + 1) * Hk + kh) * kBS;
+          tma_load_2d(dv + blk * 2048, &tmKV, 0, rv, &v_full[st]);
+          tma_load_2d(dv + kKVTile / 2 + blk * 2048, &tmKV, 64, rv, &v_full[st]);
+        }
+        ++issued;
+      }
+      if (!ok) {
+        drainq(q_full, 0);
+        for (int x = max(0, issued - 2); x < issued; ++x) {
+          drainq(&k_full[x & 1], (x >> 1) & 1);
+          drainq(&v_full[x & 1], (x >> 1) & 1);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (elect_one() && jhi > jlo) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(kTQ, kTK);              // Q K^T, both K-major
+      constexpr uint32_t idesc_o = make_idesc_bf16(kTQ, kD) | (1u << 16);  // P (TMEM) V, V MN-major
+      bool ok = waitq(q_full, 0, status, abort_flag);
+      int np[2] = {0, 0};
+      for (int j = jlo; j <= jhi && ok; ++j) {
+        const int idx = j - jlo;
+        const bool prev = j > jlo, cur = j < jhi;
+        if (prev && !waitq(&v_full[(idx - 1) & 1], ((idx - 1) >> 1) & 1, status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        bool k_ready = false;
+        tcgen05_fence_after();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const uint32_t tS = tmem + i * kTK, tO = tmem + 256 + i * kD;
+          if (prev && j - 1 >= sl[i].a && j - 1 < sl[i].b) {
+            if (!waitq(&p_full[i], np[i] & 1, status, abort_flag)) {
+              ok = false;
+              break;
+            }
+            ++np[i];
+            tcgen05_fence_after();
+            const uint32_t v_addr = smem_u32(sKV + ((idx - 1) & 1) * 2 * kKVTile + kKVTile);
+#pragma unroll
+            for (int ks = 0; ks < kTK / 16; ++ks)
+              umma_f16_ts(tO, tS + ks * 8, make_desc_mn_sw128(v_addr + ks * 2048, kKVTile / 2), idesc_o,
+                          (j - 1 > sl[i].a || ks > 0) ? 1u : 0u);
+            if (j == sl[i].b) umma_commit(&o_done[i]);
+          }
+          if (cur && j >= sl[i].a && j < sl[i].b) {
+            if (!k_ready) {
+              if (!waitq(&k_full[idx & 1], (idx >> 1) & 1, status, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tcgen05_fence_after();
+              k_ready = true;
+            }
+            const uint32_t q_addr = smem_u32(sQ + i * kQBytes);
+            const uint32_t k_addr = smem_u32(sKV + (idx & 1) * 2 * kKVTile);
+#pragma unroll
+            for (int ks = 0; ks < kD / 16; ++ks) {
+              const uint64_t a = make_smem_desc_sw128(q_addr + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
+              const uint64_t bd = make_smem_desc_sw128(k_addr + (ks >> 2) * (kKVTile / 2) + (ks & 3) * 32);
+              umma_f16_ss(tS, a, bd, idesc_s, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[i]);
+          }
+        }
+        if (prev && ok) umma_commit(&kv_empty[(idx - 1) & 1]);
+      }
+      if (!ok) {
+        umma_commit(done_bar);
+        drainq(done_bar, 0);
+      }
+    }
+  } else {
+    // softmax: slot i = warp / 4, TMEM lane quarter = warp & 3, query row r = quarter * 32 + lane.
+    // Two passes over S in TMEM, 32 columns at a time (row max, then P): S is re-read instead of
+    // held in registers, which keeps the unrolled code small (instruction-cache bound otherwise).
+    const int i = warp >> 2, lg = warp & 3;
+    const FaSlot t = i == 0 ? sl[0] : sl[1];
+    const int r = lg * 32 + lane;
+    const int qpos = ctx0 + t.q_off + r;
+    const int qmin = ctx0 + t.q_off + lg * 32, qmax = qmin + 31;
+    const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
+    const uint32_t tS = tmem + i * kTK + lane_off, tO = tmem + 256 + i * kD + lane_off;
+    const bool capped = softcap_log2 > 0.f;
+    const float inv_cap = capped ? 1.f / softcap_log2 : 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int n = 0;
+    for (int j = t.a; j < t.b; ++j, ++n) {
+      if (!waitq(&s_full[i], n & 1, status, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tcgen05_fence_after();
+      const int k0 = j * kTK;
+      // visible keys of row qpos: [qpos - window + 1, min(qpos, kv_end - 1)] - k0
+      const bool need_mask = (k0 + kTK - 1 > qmin) || (k0 + kTK > t.kv_end) ||
+                             (window > 0 && k0 < qmax - window + 1);
+      const int khi = min(qpos, t.kv_end - 1) - k0;
+      const int klo = (window > 0 ? qpos - window + 1 : 0) - k0;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kTK; c0 += 32) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tS + c0, u);
+        tmem_ld_wait();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c0 + e <= khi && c0 + e >= klo) mx = fmaxf(mx, __uint_as_float(u[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(u[e]));
+        }
+      }
+      // running max in the scaled log2 domain (soft cap is monotonic: cap the raw max)
+      const float mnew = mx == -INFINITY ? -INFINITY
+                         : capped        ? softcap_log2 * tanh_approx(mx * scale_log2 * inv_cap)
+                                         : mx * scale_log2;
+      float corr = 1.f;
+      if (n == 0) {
+        m = mnew;
+      } else if (mnew > m + 8.f) {
+        corr = exp2f(m - mnew);
+        m = mnew;
+      }
+      const float ms = m == -INFINITY ? 0.f : m;
+      float psum = 0.f;
+      const int mode = capped ? 3 : need_mask ? 2 : (EMU > 0 ? 1 : 0);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kTK; c0 += 32) {
+        uint32_t u[32], pk[16];
+        tmem_ld_32x32b_x32(tS + c0, u);
+        tmem_ld_wait();
+        if (mode == 1) {  // full tile: a share of the exponentials on the FMA pipe
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
+            const float x1 = fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms);
+            const float p1 = (EMU == 2 || (e & 3) == 2) ? ex2_poly(x1) : ex2_mufu(x1);
+            psum += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
+          }
+        } else if (mode == 0) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
+            const float p1 = ex2_mufu(fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms));
+            psum += p0 + p1;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
+          }
+        } else {  // masked and / or soft-capped
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float p[2];
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              const int c = c0 + e + x;
+              float v = __uint_as_float(u[e + x]);
+              v = capped ? softcap_log2 * tanh_approx(v * scale_log2 * inv_cap) : v * scale_log2;
+              p[x] = (c <= khi && c >= klo) ? ex2_mufu(v - ms) : 0.f;
+            }
+            psum += p[0] + p[1];
+            pk[e >> 1] = pack_bf16x2(p[0], p[1]);
+          }
+        }
+        tmem_st_32x32b_x16(tS + (c0 >> 1), pk);
+      }
+      l = l * corr + psum;
+      if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
+#pragma unroll 1
+        for (int c = 0; c < kD; c += 32) {
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tO + c, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+          tmem_st_32x32b_x32(tO + c, u);
+        }
+      }
+      tmem_st_wait();
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[i]);
+    }
+    if (ok && t.b > t.a && waitq(&o_done[i], 0, status, abort_flag)) {
+      tcgen05_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = out + (int64_t)(qs + t.q_off + r) * out_stride + t.h * kD;
+#pragma unroll
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tO + c, u);
+        tmem_ld_wait();
+        if (r < t.rows) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            float f[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(u[e + x]) * inv;
+            *reinterpret_cast<uint4*>(dst + c + e) = float_to_bf16x8(f);
+          }
+        }
+      }
+    }
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tcgen05_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace
 
 namespace gollek {
@@ -374,6 +752,43 @@ void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64
                                                   scale * 1.4426950408889634f, nullptr, window,
                                                   softcap > 0.f ? softcap * 1.4426950408889634f : 0.f);
   check_launch("paged_prefill_attention (tcgen05)");
+}
+
+
+void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
+                             const void* cache, int num_blocks, const int* block_tables, int bt_stride,
+                             const int* seq_lens, const int* query_start, const int* work, int nwork, int H, int Hk,
+                             float scale, int window, float softcap, int emu, cudaStream_t s) {
+  throw_if(H % Hk != 0, "H must be a multiple of Hk");
+  throw_if(q_stride % 8 != 0, "prefill: q row pitch must keep 16-byte alignment");
+  throw_if(nwork > 65535, "prefill: too many query tiles in one launch");
+  if (nwork == 0) return;
+  const bool pair_heads = prefill_pairs_heads(H, Hk);
+  const uint64_t kv_rows = (uint64_t)num_blocks * 2 * Hk * kBS;
+  CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, (uint64_t)H * kD, q_stride, kTQ, 64,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tkv = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, kBS, 64,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  dim3 grid(pair_heads ? H / 2 : H, nwork);
+  const float sl2 = scale * 1.4426950408889634f, cap = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  auto* w4 = reinterpret_cast<const int4*>(work);
+#define GOLLEK_FA_LAUNCH(E)                                                                                        \
+  do {                                                                                                             \
+    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(prefill_fa_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                           kFaSmem));                                                              \
+    prefill_fa_kernel<E><<<grid, kFaThreads, kFaSmem, s>>>(tq, tkv, o, out_stride, block_tables, bt_stride,        \
+                                                           seq_lens, query_start, w4, pair_heads ? 1 : 0, H, Hk,   \
+                                                           sl2, nullptr, window, cap);                             \
+  } while (0)
+  if (emu == 2)
+    GOLLEK_FA_LAUNCH(2);
+  else if (emu == 1)
+    GOLLEK_FA_LAUNCH(1);
+  else
+    GOLLEK_FA_LAUNCH(0);
+#undef GOLLEK_FA_LAUNCH
+  check_launch("paged_prefill_attention (tcgen05, two-tile)");
 }
 
 }  // namespace gollek

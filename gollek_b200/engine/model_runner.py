@@ -238,8 +238,8 @@ class ModelRunner:
             meta.prefill_seq_lens = lens[nd:]
             meta.prefill_query_start = qs.to(dev, non_blocking=True)
             if self.is_cuda:
-                meta.prefill_tiles = ops.prefill_tiles(qs.tolist(), ops.prefill_block_m(self.model.D)).to(
-                    dev, non_blocking=True)
+                meta.prefill_tiles = ops.prefill_schedule(qs.tolist(), h.seq_lens[nd:n].tolist(), self.model.H,
+                                                          self.model.Hk, self.model.D).to(dev, non_blocking=True)
         ns = len(sample_rows)
         if ns == 0:
             meta.logits_indices = h.logits_idx[:1].to(dev, non_blocking=True)
@@ -301,7 +301,8 @@ class ModelRunner:
                             num_prefill_tokens=T, prefill_block_tables=bt, prefill_seq_lens=h.seq_lens[:n].to(dev),
                             prefill_query_start=qs.to(dev))
         if self.is_cuda:
-            meta.prefill_tiles = ops.prefill_tiles(qs.tolist(), ops.prefill_block_m(self.model.D)).to(dev)
+            meta.prefill_tiles = ops.prefill_schedule(qs.tolist(), h.seq_lens[:n].tolist(), self.model.H,
+                                                      self.model.Hk, self.model.D).to(dev)
         return self.model.forward(h.input_ids[:T].to(dev), meta, self.kv_cache, hidden_only=True)
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:

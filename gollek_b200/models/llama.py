@@ -52,7 +52,7 @@ class AttnMetadata:
     prefill_block_tables: Optional[torch.Tensor] = None  # [np, max_blocks] int32
     prefill_seq_lens: Optional[torch.Tensor] = None      # [np] int32
     prefill_query_start: Optional[torch.Tensor] = None   # [np + 1] int32 (relative)
-    prefill_tiles: Optional[torch.Tensor] = None         # [ntiles, 2] int32
+    prefill_tiles: Optional[torch.Tensor] = None         # ops.prefill_schedule work list (int32)
     logits_indices: Optional[torch.Tensor] = None        # [B_out] int64 rows for the lm_head
 
     @property

@@ -8,6 +8,7 @@ fallback: a CUDA tensor with the extension missing raises.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -137,23 +138,58 @@ def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
     return torch.tensor(tiles, dtype=torch.int32).view(-1, 2)
 
 
+# Share of the softmax exponentials the two-tile prefill kernel evaluates on the FMA pipe instead of
+# MUFU: 0 none, 1 every fourth column, 2 every second column.
+PREFILL_EMU = int(os.environ.get("GOLLEK_PREFILL_EMU", "1"))
+
+
+def prefill_schedule(query_start: list, seq_lens: list, H: int, Hk: int, head_dim: int,
+                     tensor_cores: bool = True) -> torch.Tensor:
+    """Work list of the prefill kernel for one batch.
+
+    head_dim 128 on tensor cores: int32 [n, 4] rows (sequence, query offset of slot 0, of slot 1 or
+    -1, KV extent), one per CTA row of the two-tile kernel: the two slots are two heads of a GQA
+    group over the same 128 query rows when the group size is even, else two consecutive 128-row
+    tiles of one head. Rows are sorted longest KV first, so the heaviest CTAs start first.
+    Otherwise: the [n, 2] (sequence, offset) 64-row tiles of the mma.sync kernel."""
+    if not (tensor_cores and head_dim == 128):
+        return prefill_tiles(query_start, 64)
+    pair_heads = (H // Hk) % 2 == 0
+    items = []
+    for b in range(len(query_start) - 1):
+        ql = query_start[b + 1] - query_start[b]
+        L = int(seq_lens[b])
+        ctx0 = L - ql
+        offs = list(range(0, ql, 128))
+        if pair_heads:
+            groups = [(o, o) for o in offs]
+        else:
+            groups = [(offs[k], offs[k + 1] if k + 1 < len(offs) else -1) for k in range(0, len(offs), 2)]
+        for o0, o1 in groups:
+            items.append((b, o0, o1, min(L, ctx0 + max(o0, o1) + 128)))
+    items.sort(key=lambda t: -t[3])
+    return torch.tensor(items, dtype=torch.int32).view(-1, 4)
+
+
 def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                             seq_lens: torch.Tensor, query_start: torch.Tensor, scale: float,
                             tiles: Optional[torch.Tensor] = None,
                             out: Optional[torch.Tensor] = None, tensor_cores: bool = True,
-                            window: int = 0, softcap: float = 0.0) -> torch.Tensor:
+                            window: int = 0, softcap: float = 0.0, emu: Optional[int] = None) -> torch.Tensor:
     """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new).
-    head_dim 128 runs on tcgen05/TMEM (128-row query tiles); other sizes on mma.sync (64 rows).
-    ``tiles`` must have been built with ``prefill_block_m`` rows per tile. ``window`` > 0:
-    sliding-window attention; ``softcap`` > 0: tanh soft-capped scores."""
+    head_dim 128 runs on tcgen05/TMEM (the two-tile kernel when ``tiles`` is a ``prefill_schedule``
+    work list); other sizes on mma.sync (64-row tiles). ``window`` > 0: sliding-window attention;
+    ``softcap`` > 0: tanh soft-capped scores."""
     if not q.is_cuda:
         return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale, window, softcap),
                     out)
     out = torch.empty_like(q) if out is None else out
     if tiles is None:
-        tiles = prefill_tiles(query_start.tolist(), prefill_block_m(q.shape[2], tensor_cores)).to(q.device)
+        tiles = prefill_schedule(query_start.tolist(), seq_lens.tolist(), q.shape[1], kv_cache.shape[2],
+                                 q.shape[2], tensor_cores).to(q.device)
     _C().paged_prefill_attention(out, q, kv_cache, block_tables, seq_lens, query_start, tiles, float(scale),
-                                 bool(tensor_cores), int(window), float(softcap))
+                                 bool(tensor_cores), int(window), float(softcap),
+                                 PREFILL_EMU if emu is None else int(emu))
     return out
 
 

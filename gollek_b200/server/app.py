@@ -36,6 +36,7 @@ from .. import errors
 from ..engine.sequence import SamplingParams
 from .async_engine import AsyncEngine, EngineDeadError
 from .resilience import Bulkhead, BulkheadFull, CircuitBreaker, CircuitOpen, RateLimited, RateLimiter
+from .tools import may_hold_tool_call, messages_for_template, parse_tool_calls, tool_choice_regex
 
 
 # ----------------------------------------------------------------------------- schemas
@@ -43,6 +44,8 @@ class ChatMessage(BaseModel):
     role: str = "user"
     content: Union[str, List[Dict[str, Any]], None] = ""
     name: Optional[str] = None
+    tool_calls: Optional[List[Dict[str, Any]]] = None
+    tool_call_id: Optional[str] = None
 
 
 class ChatRequest(BaseModel):
@@ -68,6 +71,9 @@ class ChatRequest(BaseModel):
     typical_p: Optional[float] = None
     mirostat: Optional[int] = None
     mirostat_tau: Optional[float] = None
+    tools: Optional[List[Dict[str, Any]]] = None
+    tool_choice: Union[str, Dict[str, Any], None] = None
+    parallel_tool_calls: Optional[bool] = None
     mirostat_eta: Optional[float] = None
     response_format: Optional[Dict[str, Any]] = None
     guided_regex: Optional[str] = None
@@ -292,14 +298,19 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         ids = [t for t in list(ids) if t >= 0]  # async scheduling: a token may still be in flight
         return st.tokenizer.decode(ids) if st.tokenizer is not None else " ".join(map(str, ids))
 
-    def chat_prompt(messages) -> Union[str, List[int]]:
+    def chat_prompt(messages, tools: Optional[List[dict]] = None) -> Union[str, List[int]]:
         if st.tokenizer is None:
             raise HTTPException(400, "model has no tokenizer for chat messages")
-        msgs = [m if isinstance(m, dict) else m.model_dump() for m in messages]
+        msgs = messages_for_template([m if isinstance(m, dict) else m.model_dump(exclude_none=True) for m in messages])
         tmpl = getattr(st.tokenizer, "apply_chat_template", None)
-        return tmpl(msgs) if tmpl else "\n".join(str(m.get("content", "")) for m in msgs)
+        if tmpl is None:
+            return "\n".join(str(m.get("content", "")) for m in msgs)
+        return tmpl(msgs, tools=tools) if tools else tmpl(msgs)
 
-    async def sse_stream(prompt, sp, rid, lora_id, frame, final_frame, done_marker=True):
+    async def sse_stream(prompt, sp, rid, lora_id, frame, final_frame, done_marker=True, tool_frame=None):
+        """Server-sent events of the text deltas. With ``tool_frame``, text from where a tool call may
+        begin is held back; at the end it is sent as one tool-call frame if it parses as calls, else
+        as text."""
         prev = ""
 
         async def gen():
@@ -309,9 +320,23 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                     text = detok(out.output_token_ids)
                     if out.finished and out.text:
                         text = out.text
-                    delta = text[len(prev):] if text.startswith(prev) else text
-                    prev = text
-                    yield "data: " + json.dumps(frame(delta, out)) + "\n\n"
+                    visible = text
+                    if tool_frame is not None:
+                        if out.finished:
+                            content, calls = parse_tool_calls(text)
+                            if calls:
+                                if content.startswith(prev) and len(content) > len(prev):
+                                    yield "data: " + json.dumps(frame(content[len(prev):], None)) + "\n\n"
+                                yield "data: " + json.dumps(tool_frame(calls, out)) + "\n\n"
+                                yield "data: " + json.dumps(final_frame(out)) + "\n\n"
+                                break
+                        else:
+                            hold = may_hold_tool_call(text)
+                            visible = text if hold < 0 else text[:hold]
+                    delta = visible[len(prev):] if visible.startswith(prev) else visible
+                    prev = visible
+                    if delta or out.finished:
+                        yield "data: " + json.dumps(frame(delta, out)) + "\n\n"
                     if out.finished:
                         yield "data: " + json.dumps(final_frame(out)) + "\n\n"
                 if done_marker:
@@ -422,8 +447,17 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         d["max_tokens"] = req.max_tokens or req.max_completion_tokens
         sp = build_sampling(st, d, OPENAI_DEFAULTS)
         lora = st.lora_id(req.adapter_id)
-        prompt = chat_prompt(req.messages)
+        tools = req.tools if (req.tools and req.tool_choice != "none") else None
+        if tools:
+            rx = tool_choice_regex(req.tool_choice)
+            if rx and not (sp.guided_json or sp.guided_regex):
+                sp.guided_regex = rx  # a forced call: the output is constrained to the call's shape
+        prompt = chat_prompt(req.messages, tools)
         cid = "chatcmpl-" + uuid.uuid4().hex
+
+        def keep_calls(calls):
+            return calls[:1] if req.parallel_tool_calls is False else calls
+
         if req.stream or force_stream:
             first = {"sent": False}
 
@@ -433,18 +467,34 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                     dd["role"] = "assistant"
                     first["sent"] = True
                 return {"id": cid, "object": "chat.completion.chunk", "created": _now(), "model": st.model_name,
-                        "choices": [{"index": 0, "delta": dd, "finish_reason": o.finish_reason}]}
+                        "choices": [{"index": 0, "delta": dd, "finish_reason": o.finish_reason if o else None}]}
+
+            def tool_frame(calls, o):
+                dd = {"tool_calls": [{"index": k, **c.openai()} for k, c in enumerate(keep_calls(calls))]}
+                if not first["sent"]:
+                    dd["role"] = "assistant"
+                    first["sent"] = True
+                return {"id": cid, "object": "chat.completion.chunk", "created": _now(), "model": st.model_name,
+                        "choices": [{"index": 0, "delta": dd, "finish_reason": "tool_calls"}]}
 
             final = lambda o: {"id": cid, "object": "chat.completion.chunk", "created": _now(), "model": st.model_name,  # noqa: E731
                                "choices": [], "usage": {"prompt_tokens": len(o.prompt_token_ids),
                                                         "completion_tokens": len(o.output_token_ids),
                                                         "total_tokens": len(o.prompt_token_ids) + len(o.output_token_ids)}}
-            return await sse_stream(prompt, sp, cid, lora, frame, final)
+            return await sse_stream(prompt, sp, cid, lora, frame, final, tool_frame=tool_frame if tools else None)
         o = await run_full(prompt, sp, lora_id=lora)
         pt, ct = len(o.prompt_token_ids), len(o.output_token_ids)
+        text = o.text or detok(o.output_token_ids)
+        message: Dict[str, Any] = {"role": "assistant", "content": text}
+        finish = o.finish_reason
+        if tools:
+            content, calls = parse_tool_calls(text)
+            if calls:
+                message = {"role": "assistant", "content": content or None,
+                           "tool_calls": [c.openai() for c in keep_calls(calls)]}
+                finish = "tool_calls"
         return {"id": cid, "object": "chat.completion", "created": _now(), "model": st.model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": o.text or detok(o.output_token_ids)},
-                             "finish_reason": o.finish_reason, "logprobs": chat_logprobs(o)}],
+                "choices": [{"index": 0, "message": message, "finish_reason": finish, "logprobs": chat_logprobs(o)}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
 
     @app.post("/v1/chat/completions")

@@ -65,8 +65,8 @@ class ByteTokenizer:
                 out[b + self.offset] = bytes([b])
         return out
 
-    def apply_chat_template(self, messages: List[dict]) -> str:
-        return default_chat_template(messages)
+    def apply_chat_template(self, messages: List[dict], tools: Optional[List[dict]] = None) -> str:
+        return default_chat_template(messages, tools)
 
 
 class HFTokenizer:
@@ -98,15 +98,21 @@ class HFTokenizer:
                 out[i] = _piece_bytes(piece, byte_level, dec)
         return out
 
-    def apply_chat_template(self, messages: List[dict]) -> str:
+    def apply_chat_template(self, messages: List[dict], tools: Optional[List[dict]] = None) -> str:
+        """The checkpoint's Jinja chat template; tool definitions go to the template's ``tools``
+        variable when it has one, else into a system message."""
         if self.chat_template:
             try:
                 import jinja2
-                return jinja2.Template(self.chat_template).render(messages=messages, add_generation_prompt=True,
-                                                                  bos_token="", eos_token="")
+                msgs = messages
+                if tools and "tools" not in self.chat_template:
+                    msgs, tools = _with_tools_system(messages, tools), None
+                return jinja2.Template(self.chat_template).render(messages=msgs, tools=tools,
+                                                                  add_generation_prompt=True, bos_token="",
+                                                                  eos_token="")
             except Exception:
                 pass
-        return default_chat_template(messages)
+        return default_chat_template(messages, tools)
 
 
 class GGUFTokenizer:
@@ -167,13 +173,31 @@ class GGUFTokenizer:
                 out += self.tokens[i].replace("▁", " ").encode("utf-8")
         return out.decode("utf-8", errors="replace").lstrip(" ")
 
-    def apply_chat_template(self, messages: List[dict]) -> str:
-        return default_chat_template(messages)
+    def apply_chat_template(self, messages: List[dict], tools: Optional[List[dict]] = None) -> str:
+        return default_chat_template(messages, tools)
 
 
-def default_chat_template(messages: List[dict]) -> str:
+def _with_tools_system(messages: List[dict], tools: List[dict]) -> List[dict]:
+    from ..server.tools import tools_preamble
+    pre = tools_preamble(tools)
+    if messages and messages[0].get("role") == "system":
+        first = dict(messages[0])
+        first["content"] = f"{first.get('content') or ''}\n\n{pre}"
+        return [first] + list(messages[1:])
+    return [{"role": "system", "content": pre}] + list(messages)
+
+
+def default_chat_template(messages: List[dict], tools: Optional[List[dict]] = None) -> str:
+    if tools:
+        messages = _with_tools_system(messages, tools)
     parts = []
     for m in messages:
+        if m.get("tool_calls"):  # an assistant turn that called tools
+            calls = "".join("<tool_call>" + json.dumps({"name": tc.get("function", {}).get("name"),
+                                                        "arguments": tc.get("function", {}).get("arguments")})
+                            + "</tool_call>" for tc in m["tool_calls"])
+            parts.append(f"<|assistant|>\n{m.get('content') or ''}{calls}\n")
+            continue
         content = m.get("content", "")
         if isinstance(content, list):
             content = "".join(c.get("text", "") for c in content if isinstance(c, dict))

@@ -100,6 +100,30 @@ def test_paged_prefill_attention(H, Hk, D):
     torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("H,Hk", [(32, 8), (28, 4), (8, 8), (12, 4)])
+@pytest.mark.parametrize("emu", [0, 1, 2])
+@pytest.mark.parametrize("qscale", [1.0, 6.0])
+def test_prefill_two_tile_kernel(H, Hk, emu, qscale):
+    """The two-tile tcgen05 prefill kernel: head pairs (even GQA groups) and row-tile pairs (odd
+    groups), FMA-pipe exponentials, and sharp score distributions (qscale 6) that move the running
+    max across tiles (O rescaled in TMEM) against the fp32 oracle."""
+    specs = [(0, 300), (1000, 260), (7, 1), (200, 129), (0, 640)]
+    lens = [p + n for p, n in specs]
+    D = 128
+    cache, bt, sl = _paged_setup(len(specs), Hk, D, lens, seed=23)
+    qs = [0]
+    for _, n in specs:
+        qs.append(qs[-1] + n)
+    q = bf(torch.randn(qs[-1], H, D, device=DEV, generator=_g(24)) * qscale)
+    qsl = torch.tensor(qs, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(D)
+    work = ops.prefill_schedule(qs, lens, H, Hk, D).to(DEV)
+    assert work.shape[1] == 4
+    out = ops.paged_prefill_attention(q, cache, bt, sl, qsl, scale, tiles=work, emu=emu)
+    ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl.cpu(), scale)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("H,Hk", [(32, 8), (4, 1), (64, 8), (8, 8)])
 @pytest.mark.parametrize("tensor_cores", [True, False])
 def test_paged_prefill_attention_d128(H, Hk, tensor_cores):

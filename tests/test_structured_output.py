@@ -82,3 +82,13 @@ def test_api_response_format_json():
             assert txt.lstrip().startswith("{")
     finally:
         ae.shutdown(drain=False)
+
+
+def test_mask_cache_separates_patterns():
+    """Masks are cached per matcher state; NFA states of two patterns must not share entries."""
+    toks = [b"", b"", b"<eos>", b"a", b"b", b"c"]
+    comp = host_ext().GrammarCompiler(toks, 2)
+    ma, mb = comp.regex("a+"), comp.regex("b+")
+    assert ma.mask().tolist() == [False, False, False, True, False, False]
+    assert mb.mask().tolist() == [False, False, False, False, True, False]
+    assert comp.regex("a+").mask().tolist() == ma.mask().tolist()
