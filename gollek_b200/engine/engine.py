@@ -428,6 +428,12 @@ class LLMEngine:
                 self.kv.free(seq)
         return vecs
 
+    def beam_search(self, prompt: Union[str, List[int]], params=None, lora_id: int = 0):
+        """Beam search (engine.beam); returns the best hypotheses (tokens, logprob, finish_reason)."""
+        from .beam import BeamParams, beam_search
+        ids = self.tokenizer.encode(prompt) if isinstance(prompt, str) else list(prompt)
+        return beam_search(self, ids, params or BeamParams(), lora_id)
+
     def generate(self, prompts: Seq[Union[str, List[int]]], params: Union[SamplingParams, List[SamplingParams], None] = None,
                  lora_ids: Optional[List[int]] = None) -> List[RequestOutput]:
         ids = []
@@ -486,3 +492,6 @@ class LLM:
 
     def generate(self, prompts, params: Optional[SamplingParams] = None, lora_ids=None) -> List[RequestOutput]:
         return self.engine.generate(prompts, params, lora_ids)
+
+    def beam_search(self, prompt, params=None, lora_id: int = 0):
+        return self.engine.beam_search(prompt, params, lora_id)

@@ -103,6 +103,10 @@ class CompletionRequest(BaseModel):
     mirostat_eta: Optional[float] = None
     response_format: Optional[Dict[str, Any]] = None
     guided_regex: Optional[str] = None
+    use_beam_search: bool = False
+    best_of: Optional[int] = None            # beam width (default max(n, 4))
+    length_penalty: float = 1.0
+    early_stopping: bool = False
 
 
 class EmbeddingRequest(BaseModel):
@@ -392,10 +396,38 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             raise HTTPException(404, f"model {model_id} not found")
         return {"id": st.model_name, "object": "model", "created": _now(), "owned_by": "gollek-b200"}
 
+    async def beam_completions(req: CompletionRequest, batch, lora: int, cid: str):
+        from ..engine.beam import BeamParams, abeam_search
+        if req.stream:
+            raise HTTPException(400, "beam search does not stream")
+        width = req.best_of or max(req.n, 4)
+        try:
+            bp = BeamParams(beam_width=width, max_tokens=req.max_tokens or 16, length_penalty=req.length_penalty,
+                            early_stopping=req.early_stopping, num_return=req.n, ignore_eos=req.ignore_eos)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+
+        async def expand(prefix, sp):
+            return await run_full(prefix, sp, lora_id=lora)
+
+        choices, pt, ct = [], 0, 0
+        for p in batch:
+            ids = list(p) if isinstance(p, list) else (st.tokenizer.encode(p) if st.tokenizer is not None else None)
+            if ids is None:
+                raise HTTPException(400, "model has no tokenizer")
+            hyps = await abeam_search(expand, ids, bp, st.engine.eos_token_id)
+            for h in hyps:
+                choices.append({"index": len(choices), "text": detok(h.tokens), "finish_reason": h.finish_reason,
+                                "logprobs": None, "score": h.score(bp.length_penalty)})
+                ct += len(h.tokens)
+            pt += len(ids)
+        return {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name, "choices": choices,
+                "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
+
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
-        if req.n != 1:
-            raise HTTPException(400, "only n=1 is supported")
+        if req.n != 1 and not req.use_beam_search:
+            raise HTTPException(400, "n > 1 needs use_beam_search")
         sp = build_sampling(st, req.model_dump(), {**OPENAI_DEFAULTS, "max_tokens": req.max_tokens or 16})
         lora = st.lora_id(req.adapter_id)
         prompts = req.prompt
@@ -404,6 +436,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         else:
             batch = [prompts]
         cid = "cmpl-" + uuid.uuid4().hex
+        if req.use_beam_search:
+            return await beam_completions(req, batch, lora, cid)
         if req.stream:
             if len(batch) != 1:
                 raise HTTPException(400, "streaming supports a single prompt")
