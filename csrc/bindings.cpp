@@ -286,6 +286,18 @@ std::vector<int64_t> moe_plan_py(int64_t T, int64_t topk, int64_t E, int64_t e_l
 }
 
 // cache [L, NB, 2, Hk, bs, D] bf16; packed [L, n, 2, Hk, bs, D] bf16; block_ids int32 [n] (device)
+torch::Tensor kv_key_norms_py(torch::Tensor cache, torch::Tensor block_ids) {
+  check_bf16(cache, "kv_cache");
+  check_i32(block_ids, "block_ids");
+  TORCH_CHECK(cache.is_contiguous() && cache.dim() == 6 && cache.size(2) == 2, "cache [L, NB, 2, Hk, bs, D]");
+  TORCH_CHECK(block_ids.is_contiguous() && block_ids.dim() == 1, "block_ids [n]");
+  auto out = torch::empty({block_ids.size(0)}, cache.options().dtype(torch::kFloat32));
+  launch_kv_key_norms(cache.data_ptr(), block_ids.data_ptr<int>(), out.data_ptr<float>(), (int)block_ids.size(0),
+                      (int)cache.size(0), cache.size(1), (int)cache.size(3), (int)cache.size(4), (int)cache.size(5),
+                      cur_stream());
+  return out;
+}
+
 void kv_blocks_py(torch::Tensor cache, torch::Tensor packed, torch::Tensor block_ids, bool gather) {
   check_bf16(cache, "kv_cache");
   check_bf16(packed, "packed");
@@ -599,6 +611,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
   m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");
   m.def("kv_blocks", &kv_blocks_py, "gather (or scatter) one sequence's paged KV blocks, every layer");
+  m.def("kv_key_norms", &kv_key_norms_py, "mean key L2 norm of each listed KV block (eviction scoring, K15)");
   m.def("moe_ws_ints", &moe_ws_ints);
   m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");
   m.def("argmax", &argmax_out, "greedy argmax (K11)");

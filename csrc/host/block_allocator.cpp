@@ -12,6 +12,7 @@
 //     (all-or-nothing) so the scheduler can preempt when the pool is exhausted.
 //   * build_batch(): writes positions, slot mapping, padded block tables, KV lengths and query
 //     offsets for one engine step straight into (pinned) int32 tensors.
+#include <algorithm>
 #include <torch/extension.h>
 
 #include <cstdint>
@@ -150,6 +151,36 @@ class SeqTables {
     if (it == tables_.end()) return;
     for (int32_t b : it->second) pool_->decref(b);
     tables_.erase(it);
+    dropped_.erase(seq);
+  }
+
+  // KV eviction: remove the blocks at table indices `idx` (sorted, unique, never the last block) and
+  // release them. The sequence's later tokens keep their logical positions; their KV slots shift
+  // down by the dropped tokens (`dropped`), so attention runs over the kept blocks only.
+  int64_t drop(int64_t seq, std::vector<int64_t> idx) {
+    auto& t = at(seq);
+    std::sort(idx.begin(), idx.end());
+    idx.erase(std::unique(idx.begin(), idx.end()), idx.end());
+    for (int64_t i : idx)
+      if (i < 0 || i + 1 >= (int64_t)t.size()) throw std::out_of_range("SeqTables.drop: bad block index");
+    std::vector<int32_t> kept;
+    kept.reserve(t.size() - idx.size());
+    size_t k = 0;
+    for (int64_t i = 0; i < (int64_t)t.size(); ++i) {
+      if (k < idx.size() && idx[k] == i) {
+        pool_->decref(t[i]);
+        ++k;
+      } else {
+        kept.push_back(t[i]);
+      }
+    }
+    t.swap(kept);
+    dropped_[seq] += (int64_t)idx.size() * pool_->block_size();
+    return (int64_t)idx.size();
+  }
+  int64_t dropped(int64_t seq) const {
+    auto it = dropped_.find(seq);
+    return it == dropped_.end() ? 0 : it->second;
   }
 
   void append_block(int64_t seq, int32_t b) { at(seq).push_back(b); }
@@ -160,6 +191,7 @@ class SeqTables {
   // Make room for `total_tokens` tokens; allocates missing blocks all-or-nothing.
   bool ensure_capacity(int64_t seq, int64_t total_tokens) {
     auto& t = at(seq);
+    total_tokens -= dropped(seq);
     const int64_t need = (total_tokens + pool_->block_size() - 1) / pool_->block_size();
     const int64_t have = (int64_t)t.size();
     if (need <= have) return true;
@@ -178,6 +210,7 @@ class SeqTables {
     return true;
   }
   int64_t blocks_needed(int64_t seq, int64_t total_tokens) const {
+    total_tokens -= dropped(seq);
     const int64_t need = (total_tokens + pool_->block_size() - 1) / pool_->block_size();
     return std::max<int64_t>(0, need - (int64_t)at_c(seq).size());
   }
@@ -207,19 +240,21 @@ class SeqTables {
     for (int64_t i = 0; i < n; ++i) {
       const auto& tab = at_c(ids[i]);
       const int64_t nb = (int64_t)tab.size();
+      const int64_t dr = dropped(ids[i]);  // tokens evicted before this step's positions
       if (nb > max_blocks) throw std::runtime_error("build_batch: block table wider than buffer");
-      if ((st[i] + nn[i] + bs - 1) / bs > nb) throw std::runtime_error("build_batch: sequence lacks KV blocks");
+      if (st[i] < dr) throw std::runtime_error("build_batch: new tokens inside evicted blocks");
+      if ((st[i] - dr + nn[i] + bs - 1) / bs > nb) throw std::runtime_error("build_batch: sequence lacks KV blocks");
       if (t + nn[i] > cap_tokens) throw std::runtime_error("build_batch: token buffer too small");
       int32_t* row = bt + i * bt_stride;
       for (int64_t j = 0; j < nb; ++j) row[j] = tab[j];
       for (int64_t j = nb; j < max_blocks; ++j) row[j] = 0;
       for (int64_t k = 0; k < nn[i]; ++k) {
-        const int64_t p = st[i] + k;
+        const int64_t p = st[i] + k, kp = p - dr;
         pos[t] = (int32_t)p;
-        sl[t] = (int32_t)(tab[p / bs] * bs + p % bs);
+        sl[t] = (int32_t)(tab[kp / bs] * bs + kp % bs);
         ++t;
       }
-      lens[i] = st[i] + nn[i];
+      lens[i] = (int32_t)(st[i] + nn[i] - dr);
       qs[i + 1] = (int32_t)t;
     }
     return t;
@@ -238,6 +273,7 @@ class SeqTables {
   }
   BlockPool* pool_;
   std::unordered_map<int64_t, std::vector<int32_t>> tables_;
+  std::unordered_map<int64_t, int64_t> dropped_;
 };
 
 void register_block_allocator(pybind11::module& m) {
@@ -268,5 +304,7 @@ void register_block_allocator(pybind11::module& m) {
       .def("blocks", &SeqTables::blocks)
       .def("ensure_capacity", &SeqTables::ensure_capacity)
       .def("blocks_needed", &SeqTables::blocks_needed)
-      .def("build_batch", &SeqTables::build_batch);
+      .def("build_batch", &SeqTables::build_batch)
+      .def("drop", &SeqTables::drop)
+      .def("dropped", &SeqTables::dropped);
 }

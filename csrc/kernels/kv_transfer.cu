@@ -37,6 +37,44 @@ __global__ void __launch_bounds__(256) kv_blocks_kernel(__nv_bfloat16* __restric
   }
 }
 
+// K15 (KV eviction scoring): mean L2 norm of the keys of each listed block over every layer,
+// KV head and token. One CTA per block; warp w takes rows (layer, head, token) w, w + 8, ...; a row
+// is head_dim contiguous bf16 values read as 16-byte vectors (head_dim <= 256 -> <= 1 vector per
+// lane). Keys with small norms draw the most attention (Devoto et al., "A Simple and Effective
+// L2 Norm-Based Strategy for KV Cache Compression", EMNLP 2024), so -norm ranks block importance.
+__global__ void __launch_bounds__(256) kv_key_norm_kernel(const __nv_bfloat16* __restrict__ cache,
+                                                          const int* __restrict__ block_ids, float* __restrict__ out,
+                                                          int layers, int64_t num_blocks, int Hk, int bs, int D) {
+  __shared__ float part[8];
+  const int i = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b = block_ids[i];
+  float acc = 0.f;
+  if (b >= 0 && b < num_blocks) {
+    const int rows = layers * Hk * bs, vec = D / 8;
+    for (int row = warp; row < rows; row += 8) {
+      const int l = row / (Hk * bs), rem = row % (Hk * bs);
+      // block layout [2, Hk, bs, D]: K is the first half
+      const __nv_bfloat16* k = cache + (((int64_t)l * num_blocks + b) * 2 * Hk * bs + rem) * D;
+      float ss = 0.f;
+      if (lane < vec) {
+        float f[8];
+        bf16x8_to_float(reinterpret_cast<const uint4*>(k)[lane], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+      }
+      ss = warp_sum(ss);
+      acc += sqrtf(ss);
+    }
+  }
+  if (lane == 0) part[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += part[w];
+    out[i] = t / (float)(layers * Hk * bs);
+  }
+}
+
 }  // namespace
 
 namespace gollek {
@@ -53,6 +91,15 @@ void launch_kv_blocks(void* cache, void* packed, const int* block_ids, int n, in
   else
     kv_blocks_kernel<false><<<grid, 256, 0, s>>>(c, p, block_ids, n, num_blocks, span);
   check_launch("kv block transfer");
+}
+
+void launch_kv_key_norms(const void* cache, const int* block_ids, float* out, int n, int layers, int64_t num_blocks,
+                         int Hk, int bs, int D, cudaStream_t s) {
+  throw_if(D % 8 != 0 || D > 256, "kv key norms: head_dim must be a multiple of 8, at most 256");
+  if (n == 0) return;
+  kv_key_norm_kernel<<<n, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(cache), block_ids, out, layers,
+                                       num_blocks, Hk, bs, D);
+  check_launch("kv_key_norms");
 }
 
 }  // namespace gollek

@@ -102,6 +102,9 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
                         uint32_t* status, cudaStream_t s);
 
 // ---- KV block transfer (P/D disaggregation): packed [L, n, span] <-> cache [L, NB, span]
+// Mean key L2 norm per listed block (KV eviction scoring); cache [L, NB, 2, Hk, bs, D] bf16.
+void launch_kv_key_norms(const void* cache, const int* block_ids, float* out, int n, int layers, int64_t num_blocks,
+                         int Hk, int bs, int D, cudaStream_t s);
 void launch_kv_blocks(void* cache, void* packed, const int* block_ids, int n, int layers, int64_t num_blocks,
                       int64_t span, bool gather, cudaStream_t s);
 

@@ -427,8 +427,18 @@ class EngineConfig:
     block_size: int = 16
     num_gpu_blocks: Optional[int] = None      # None => size from memory fraction
     gpu_memory_utilization: float = 0.85
-    kv_cache_dtype: str = "auto"              # auto (= model dtype) | fp8
+    kv_cache_dtype: str = "auto"              # auto (= model dtype)
     enable_prefix_caching: bool = True
+    # KV eviction under memory pressure (opt-in; changes outputs): when the block pool is more than
+    # `kv_eviction_threshold` full, the longest running sequences drop their least important KV
+    # blocks (key-norm + recency score) down to `kv_retention_target` of their blocks; the first
+    # `kv_protect_sink_blocks` blocks and the most recent `kv_protect_recent` fraction are kept
+    kv_eviction: bool = False
+    kv_eviction_threshold: float = 0.85
+    kv_retention_target: float = 0.6
+    kv_protect_sink_blocks: int = 1
+    kv_protect_recent: float = 0.2
+    kv_eviction_min_blocks: int = 8
     # scheduler
     max_num_seqs: int = 256
     max_num_batched_tokens: int = 8192

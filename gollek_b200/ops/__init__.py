@@ -523,6 +523,15 @@ def kv_gather_blocks(cache: torch.Tensor, block_ids: torch.Tensor) -> torch.Tens
     return packed
 
 
+def kv_key_norms(cache: torch.Tensor, block_ids: torch.Tensor) -> torch.Tensor:
+    """Mean key L2 norm of each listed block over layers, KV heads and tokens (KV eviction scoring)."""
+    ids = block_ids.to(cache.device, torch.int32)
+    if not cache.is_cuda:
+        k = cache[:, ids.long(), 0].float()                 # [L, n, Hk, bs, D]
+        return torch.linalg.vector_norm(k, dim=-1).mean(dim=(0, 2, 3))
+    return _C().kv_key_norms(cache, ids)
+
+
 def kv_scatter_blocks(cache: torch.Tensor, block_ids: torch.Tensor, packed: torch.Tensor) -> None:
     """cache[:, block_ids] = packed (the receiving side of a hand-off)."""
     if not cache.is_cuda:
