@@ -614,20 +614,25 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                              (window > 0 && k0 < qmax - window + 1);
       const int khi = min(qpos, t.kv_end - 1) - k0;
       const int klo = (window > 0 ? qpos - window + 1 : 0) - k0;
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kTK; c0 += 32) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tS + c0, u);
+      // pass 1: the four 32-column loads in flight at once, row max over 8 independent chains
+      float mx;
+      {
+        uint32_t u[kTK];
+#pragma unroll
+        for (int c = 0; c < kTK; c += 32) tmem_ld_32x32b_x32(tS + c, u + c);
         tmem_ld_wait();
+        float m8[8];
+#pragma unroll
+        for (int x = 0; x < 8; ++x) m8[x] = -INFINITY;
         if (need_mask) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c0 + e <= khi && c0 + e >= klo) mx = fmaxf(mx, __uint_as_float(u[e]));
+          for (int c = 0; c < kTK; ++c)
+            m8[c & 7] = fmaxf(m8[c & 7], (c <= khi && c >= klo) ? __uint_as_float(u[c]) : -INFINITY);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(u[e]));
+          for (int c = 0; c < kTK; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(u[c]));
         }
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       }
       // running max in the scaled log2 domain (soft cap is monotonic: cap the raw max)
       const float mnew = mx == -INFINITY ? -INFINITY
@@ -641,20 +646,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         m = mnew;
       }
       const float ms = m == -INFINITY ? 0.f : m;
-      float psum = 0.f;
       const int mode = capped ? 3 : need_mask ? 2 : (EMU > 0 ? 1 : 0);
-#pragma unroll 1
-      for (int c0 = 0; c0 < kTK; c0 += 32) {
-        uint32_t u[32], pk[16];
-        tmem_ld_32x32b_x32(tS + c0, u);
-        tmem_ld_wait();
+      // pass 2: S re-read 32 columns at a time, the next chunk's load overlapping this chunk's math
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      auto p_chunk = [&](const uint32_t* u, int c0) {
+        uint32_t pk[16];
         if (mode == 1) {  // full tile: a share of the exponentials on the FMA pipe
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
             const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
             const float x1 = fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms);
             const float p1 = (EMU == 2 || (e & 3) == 2) ? ex2_poly(x1) : ex2_mufu(x1);
-            psum += p0 + p1;
+            ps[(e >> 1) & 3] += p0 + p1;
             pk[e >> 1] = pack_bf16x2(p0, p1);
           }
         } else if (mode == 0) {
@@ -662,7 +665,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           for (int e = 0; e < 32; e += 2) {
             const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
             const float p1 = ex2_mufu(fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms));
-            psum += p0 + p1;
+            ps[(e >> 1) & 3] += p0 + p1;
             pk[e >> 1] = pack_bf16x2(p0, p1);
           }
         } else {  // masked and / or soft-capped
@@ -676,12 +679,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
               v = capped ? softcap_log2 * tanh_approx(v * scale_log2 * inv_cap) : v * scale_log2;
               p[x] = (c <= khi && c >= klo) ? ex2_mufu(v - ms) : 0.f;
             }
-            psum += p[0] + p[1];
+            ps[(e >> 1) & 3] += p[0] + p[1];
             pk[e >> 1] = pack_bf16x2(p[0], p[1]);
           }
         }
         tmem_st_32x32b_x16(tS + (c0 >> 1), pk);
+      };
+      {
+        uint32_t ua[32], ub[32];
+        tmem_ld_32x32b_x32(tS, ua);
+        tmem_ld_wait();
+#pragma unroll 1
+        for (int c0 = 0; c0 < kTK; c0 += 64) {
+          tmem_ld_32x32b_x32(tS + c0 + 32, ub);
+          p_chunk(ua, c0);
+          tmem_ld_wait();
+          if (c0 + 64 < kTK) tmem_ld_32x32b_x32(tS + c0 + 64, ua);
+          p_chunk(ub, c0 + 32);
+          tmem_ld_wait();
+        }
       }
+      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       l = l * corr + psum;
       if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
 #pragma unroll 1

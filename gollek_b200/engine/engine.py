@@ -92,6 +92,17 @@ class LLMEngine:
             from .lora import LoRAManager
             self.lora_manager = LoRAManager(self.model, cfg.max_loras, cfg.max_lora_rank)
         self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
+        if cfg.kv_cache_dtype not in ("auto", cfg.dtype):
+            raise ValueError(f"kv_cache_dtype {cfg.kv_cache_dtype!r}: the KV cache is kept in the model dtype")
+        self.evictor = None
+        if cfg.kv_eviction:
+            from .evicpress import KVEvictor
+            if cfg.tensor_parallel_size > 1:
+                raise ValueError("kv_eviction: not supported with tensor parallelism (per-rank scores differ)")
+            if model_cfg.sliding_window or model_cfg.layer_types:
+                raise ValueError("kv_eviction: not supported with sliding-window layers")
+            self.evictor = KVEvictor(cfg.kv_eviction_threshold, cfg.kv_retention_target, cfg.kv_protect_sink_blocks,
+                                     cfg.kv_protect_recent, cfg.kv_eviction_min_blocks)
         self.seqs: Dict[str, Sequence] = {}
         self.metrics = EngineMetrics()
         self.eos_token_id = model_cfg.eos_token_id
@@ -263,6 +274,8 @@ class LLMEngine:
             outs = self._resolve_inflight()
             return outs + self._step_sync()
         tracing.nvtx_push("schedule")
+        if self.evictor is not None:
+            self.evictor.run(self)
         sched = self.scheduler.schedule()
         tracing.nvtx_pop()
         if sched.empty:
@@ -327,6 +340,8 @@ class LLMEngine:
         return outputs
 
     def _step_sync(self) -> List[RequestOutput]:
+        if self.evictor is not None:
+            self.evictor.run(self)
         sched = self.scheduler.schedule()
         if sched.empty:
             return []

@@ -92,9 +92,21 @@ class KVCacheManager:
     def blocks_needed(self, seq: Sequence, total_tokens: int) -> int:
         return self.tables.blocks_needed(seq.seq_id, total_tokens)
 
+    def drop_blocks(self, seq: Sequence, idx: List[int]) -> int:
+        """KV eviction: release the blocks at table indices ``idx`` (never the last block); later
+        tokens keep their positions and attend over the kept blocks. Returns blocks freed."""
+        if not idx:
+            return 0
+        n = self.tables.drop(seq.seq_id, list(idx))
+        del seq.block_hashes[min(idx):]
+        return n
+
+    def dropped_tokens(self, seq: Sequence) -> int:
+        return self.tables.dropped(seq.seq_id) if self.tables.has(seq.seq_id) else 0
+
     def commit_full_blocks(self, seq: Sequence) -> None:
         """Register newly completed full blocks of ``seq`` in the prefix cache."""
-        if not self.enable_prefix_caching:
+        if not self.enable_prefix_caching or self.tables.dropped(seq.seq_id):
             return
         bs = self.block_size
         full = seq.num_computed_tokens // bs

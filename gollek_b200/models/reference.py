@@ -212,8 +212,9 @@ class ReferenceDecoder:
         self.cos_sin = rope_cos_sin(cfg, n)
         self.cos_sin_local = rope_cos_sin(cfg, n, theta=cfg.rope_local_theta) if cfg.rope_local_theta else None
 
-    def forward(self, ids: torch.Tensor) -> torch.Tensor:
-        """ids: [S] → logits [S, vocab] (fp32)."""
+    def forward(self, ids: torch.Tensor, key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """ids: [S] → logits [S, vocab] (fp32). ``key_mask`` [S, S] bool (optional): False hides key
+        k from query q on top of the causal mask (evicted KV)."""
         cfg, w = self.cfg, self.w
         S = ids.shape[0]
         pos = torch.arange(S)
@@ -245,6 +246,8 @@ class ReferenceDecoder:
                 c = cfg.attn_logit_softcapping
                 s = c * torch.tanh(s / c)
             mask = causal
+            if key_mask is not None:
+                mask = mask.masked_fill(~key_mask, float("-inf"))
             if win > 0:
                 mask = mask + torch.full((S, S), float("-inf")).tril(-win)
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), v).reshape(S, H * D)

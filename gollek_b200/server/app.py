@@ -364,6 +364,35 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         ok = st.ae.healthy and not st.ae.draining
         return JSONResponse({"status": "UP" if ok else "DOWN"}, status_code=200 if ok else 503)
 
+    # -------------------------------------------------------------- KV eviction (EVICPRESS routes)
+    @app.get("/v1/kvcache/stats")
+    async def kvcache_stats():
+        e = st.engine
+        ev = e.evictor
+        d = {"kv_total_blocks": e.kv.num_blocks, "kv_free_blocks": e.kv.num_free_blocks(),
+             "kv_utilization": e.kv.usage(), "eviction_enabled": ev is not None}
+        if ev is not None:
+            d.update({"eviction_threshold": ev.threshold, "retention_target": ev.retention_target,
+                      **{f"total_{k}": v for k, v in ev.stats.as_dict().items()}})
+        return d
+
+    @app.put("/v1/kvcache/retention")
+    async def kvcache_retention(target: float):
+        ev = st.engine.evictor
+        if ev is None:
+            raise HTTPException(409, "KV eviction is disabled (kv_eviction=false)")
+        if not 0.0 < target <= 1.0:
+            raise HTTPException(400, "target must be in (0, 1]")
+        old, ev.retention_target = ev.retention_target, target
+        return {"previous": old, "current": target}
+
+    @app.post("/v1/kvcache/evict-now")
+    async def kvcache_evict_now():
+        if st.engine.evictor is None:
+            raise HTTPException(409, "KV eviction is disabled (kv_eviction=false)")
+        freed = await st.ae.call(lambda eng: eng.evictor.run(eng, force=True))
+        return {"blocks_dropped": freed, "utilization": st.engine.kv.usage()}
+
     @app.get("/metrics")
     async def metrics():
         return PlainTextResponse(st.engine.metrics.prometheus())

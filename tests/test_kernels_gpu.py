@@ -354,3 +354,13 @@ def test_embedding_scale():
     ids = torch.tensor([3, 99, 0, 42], dtype=torch.int32, device=DEV)
     out = ops.embedding(ids, table, scale=16.0)
     torch.testing.assert_close(out.float(), table[ids.long()].float() * 16.0, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_kv_key_norms(D):
+    """K15 block scoring kernel (mean key L2 norm per block) against torch."""
+    cache = bf(torch.randn(3, 40, 2, 4, 16, D, device=DEV, generator=_g(50)))
+    ids = torch.tensor([39, 0, 17, 5], dtype=torch.int32, device=DEV)
+    got = ops.kv_key_norms(cache, ids)
+    want = torch.stack([cache[:, b, 0].float().norm(dim=-1).mean() for b in ids.tolist()])
+    torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-4)
