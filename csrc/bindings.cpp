@@ -286,6 +286,36 @@ std::vector<int64_t> moe_plan_py(int64_t T, int64_t topk, int64_t E, int64_t e_l
 }
 
 // cache [L, NB, 2, Hk, bs, D] bf16; packed [L, n, 2, Hk, bs, D] bf16; block_ids int32 [n] (device)
+void gdn_scan_py(torch::Tensor proj, torch::Tensor out, torch::Tensor state, torch::Tensor slots,
+                 torch::Tensor reset, torch::Tensor query_start, torch::Tensor a_log, torch::Tensor dt_bias,
+                 int64_t Hg) {
+  check_bf16(proj, "proj");
+  check_bf16(out, "out");
+  TORCH_CHECK(state.is_cuda() && state.scalar_type() == torch::kFloat32 && state.dim() == 4 &&
+                  state.stride(3) == 1 && state.stride(2) == state.size(3) && state.stride(1) == state.size(2) * state.size(3),
+              "state [slots, Hg, D, D] fp32 (slot stride free)");
+  check_i32(slots, "slots");
+  check_i32(reset, "reset");
+  check_i32(query_start, "query_start");
+  TORCH_CHECK(a_log.scalar_type() == torch::kFloat32 && dt_bias.scalar_type() == torch::kFloat32, "gates fp32");
+  TORCH_CHECK(proj.stride(1) == 1 && out.is_contiguous(), "layouts");
+  const int D = (int)state.size(3);
+  TORCH_CHECK(proj.size(1) >= 4 * Hg * D + 2 * Hg && out.size(0) == proj.size(0), "proj / out shapes");
+  launch_gdn_scan(proj.data_ptr(), proj.stride(0), out.data_ptr(), state.data_ptr<float>(), state.stride(0),
+                  slots.data_ptr<int>(), reset.data_ptr<int>(), query_start.data_ptr<int>(), (int)slots.size(0),
+                  a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (int)Hg, D, cur_stream());
+}
+
+void gdn_gated_norm_py(torch::Tensor y, torch::Tensor o, torch::Tensor g, torch::Tensor w, int64_t Hg, double eps) {
+  check_bf16(y, "y");
+  check_bf16(o, "o");
+  check_bf16(g, "g");
+  check_bf16(w, "w");
+  TORCH_CHECK(g.stride(1) == 1 && o.is_contiguous() && y.is_contiguous(), "layouts");
+  launch_gdn_gated_norm(y.data_ptr(), o.data_ptr(), g.data_ptr(), g.stride(0), w.data_ptr(), (int)o.size(0), (int)Hg,
+                        (int)w.size(0), (float)eps, cur_stream());
+}
+
 torch::Tensor kv_key_norms_py(torch::Tensor cache, torch::Tensor block_ids) {
   check_bf16(cache, "kv_cache");
   check_i32(block_ids, "block_ids");
@@ -611,6 +641,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
   m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");
   m.def("kv_blocks", &kv_blocks_py, "gather (or scatter) one sequence's paged KV blocks, every layer");
+  m.def("gdn_scan", &gdn_scan_py, "gated delta rule scan over varlen chunks (K14)");
+  m.def("gdn_gated_norm", &gdn_gated_norm_py, "RMSNorm(o) * w * silu(g) per head");
   m.def("kv_key_norms", &kv_key_norms_py, "mean key L2 norm of each listed KV block (eviction scoring, K15)");
   m.def("moe_ws_ints", &moe_ws_ints);
   m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");

@@ -102,6 +102,13 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
                         uint32_t* status, cudaStream_t s);
 
 // ---- KV block transfer (P/D disaggregation): packed [L, n, span] <-> cache [L, NB, span]
+// K14 gated delta rule: proj [T, ldp] = q | k | v | g | a | b per token (Hg heads of D = 128);
+// out [T, Hg, D] raw o; state [slots, Hg, D, D] fp32 of one layer (slot stride in elements).
+void launch_gdn_scan(const void* proj, int64_t ldp, void* out, float* state, int64_t state_slot_stride,
+                     const int* slots, const int* reset, const int* query_start, int n, const float* a_log,
+                     const float* dt_bias, int Hg, int D, cudaStream_t s);
+void launch_gdn_gated_norm(void* y, const void* o, const void* g, int64_t ldg, const void* w, int T, int Hg, int D,
+                           float eps, cudaStream_t s);
 // Mean key L2 norm per listed block (KV eviction scoring); cache [L, NB, 2, Hk, bs, D] bf16.
 void launch_kv_key_norms(const void* cache, const int* block_ids, float* out, int n, int layers, int64_t num_blocks,
                          int Hk, int bs, int D, cudaStream_t s);

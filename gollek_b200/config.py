@@ -94,6 +94,10 @@ class ModelConfig:
     norm_unit_offset: bool = False       # RMSNorm scales by (1 + w) (Gemma)
     embed_scale: float = 1.0             # embeddings multiplied by this (Gemma: sqrt(hidden))
     sandwich_norm: bool = False          # norms after attention / MLP outputs too (Gemma-2/3)
+    # hybrid gated-delta-rule / attention stacks: "H1" = {G,G,G,G,A,G}, "H2" = {G,G,A,G,G,A} per 6
+    # layers (G = Gated DeltaNet layer, A = softmax attention); None = attention only
+    hybrid_schedule: Optional[str] = None
+    gdn_num_heads: int = 0               # GDN heads (0: num_attention_heads); head dim 128
     bos_token_id: int = 1
     eos_token_id: int = 2
 
@@ -112,6 +116,23 @@ class ModelConfig:
         if self.layer_types is None:
             return self.sliding_window
         return self.sliding_window if self.layer_types[i] == "sliding_attention" else 0
+
+    def is_gdn_layer(self, i: int) -> bool:
+        """Layer ``i`` is a gated-delta-rule layer under the hybrid schedule."""
+        if not self.hybrid_schedule:
+            return False
+        pat = {"H1": (1, 1, 1, 1, 0, 1), "H2": (1, 1, 0, 1, 1, 0)}.get(self.hybrid_schedule.upper())
+        if pat is None:
+            raise ValueError(f"unknown hybrid_schedule {self.hybrid_schedule!r} (H1 | H2)")
+        return bool(pat[i % 6])
+
+    @property
+    def gdn_heads(self) -> int:
+        return self.gdn_num_heads or self.num_attention_heads
+
+    @property
+    def gdn_head_dim(self) -> int:
+        return 128
 
     def layer_rope_theta(self, i: int) -> float:
         if self.rope_local_theta and self.layer_window(i) > 0:
@@ -295,6 +316,10 @@ PRESETS: dict[str, ModelConfig] = {
         architecture="llama", vocab_size=32000, hidden_size=256, intermediate_size=688,
         num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2, head_dim=32,
         rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=2048),
+    "tiny-hybrid": ModelConfig(
+        architecture="llama", vocab_size=1024, hidden_size=256, intermediate_size=512,
+        num_hidden_layers=6, num_attention_heads=8, num_key_value_heads=2, head_dim=32,
+        rope_theta=10000.0, max_position_embeddings=2048, hybrid_schedule="H2", gdn_num_heads=2),
     "tiny-mixtral": ModelConfig(
         architecture="mixtral", vocab_size=1024, hidden_size=256, intermediate_size=512,
         num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2, head_dim=32,

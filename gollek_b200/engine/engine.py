@@ -65,6 +65,15 @@ class LLMEngine:
         if cfg.offload_layers > 0 and self.device.type == "cuda":
             self.model.enable_offload(cfg.offload_layers, cfg.offload_prefetch)
             cfg.use_cuda_graphs = False
+        # ---- hybrid GDN stacks: one recurrent-state slot per running sequence (+1 scratch slot for
+        # embeddings); the state is not block-addressable, so no prefix reuse, no speculative rollback
+        self.hybrid = self.model.num_gdn_layers > 0
+        if self.hybrid:
+            if cfg.speculative_method != "none" or cfg.enable_lora or cfg.kv_eviction:
+                raise ValueError("hybrid GDN models: speculative decoding, LoRA and KV eviction are not supported")
+            cfg.enable_prefix_caching = False
+            cfg.use_cuda_graphs = False
+            self.model.alloc_gdn_state(cfg.max_num_seqs + 1)
         # ---- KV cache
         bpb = self.model.kv_bytes_per_block(cfg.block_size)
         nb = num_blocks or cfg.num_gpu_blocks
@@ -82,7 +91,8 @@ class LLMEngine:
         if cfg.speculative_method == "draft" and cfg.enable_prefix_caching:
             # a reused prefix block may carry target KV whose draft-model KV was never computed
             cfg.enable_prefix_caching = False
-        self.kv = KVCacheManager(nb, cfg.block_size, cfg.enable_prefix_caching)
+        self.kv = KVCacheManager(nb, cfg.block_size, cfg.enable_prefix_caching,
+                                 state_slots=cfg.max_num_seqs + 1 if self.hybrid else 0)
         predictor = None
         if cfg.scheduling_policy == "wait":
             predictor = host_ext().LengthPredictor(64, 1.0, float(cfg.max_model_len), 0.05, 8)

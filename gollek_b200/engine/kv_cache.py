@@ -30,7 +30,8 @@ def block_hash(parent: int, tokens: List[int], salt: int = 0) -> int:
 
 
 class KVCacheManager:
-    def __init__(self, num_blocks: int, block_size: int = 16, enable_prefix_caching: bool = True):
+    def __init__(self, num_blocks: int, block_size: int = 16, enable_prefix_caching: bool = True,
+                 state_slots: int = 0):
         h = host_ext()
         self.block_size = block_size
         self.num_blocks = num_blocks
@@ -39,6 +40,8 @@ class KVCacheManager:
         self.enable_prefix_caching = enable_prefix_caching
         self.prefix_hits = 0
         self.prefix_queries = 0
+        # recurrent-state slots of hybrid GDN models: taken with the sequence's block table
+        self.free_state_slots = list(range(state_slots - 1, -1, -1)) if state_slots else None
 
     # ------------------------------------------------------------------ stats
     def num_free_blocks(self) -> int:
@@ -54,10 +57,17 @@ class KVCacheManager:
     def add(self, seq: Sequence) -> None:
         self.tables.add(seq.seq_id)
         seq.block_hashes = []
+        if self.free_state_slots is not None:
+            if not self.free_state_slots:
+                raise RuntimeError("no recurrent-state slot free (more running sequences than max_num_seqs)")
+            seq.state_slot = self.free_state_slots.pop()
 
     def free(self, seq: Sequence) -> None:
         self.tables.remove(seq.seq_id)
         seq.block_hashes = []
+        if self.free_state_slots is not None and seq.state_slot >= 0:
+            self.free_state_slots.append(seq.state_slot)
+            seq.state_slot = -1
 
     def has(self, seq: Sequence) -> bool:
         return self.tables.has(seq.seq_id)

@@ -102,6 +102,9 @@ class ModelRunner:
         self.num_sms = torch.cuda.get_device_properties(self.device).multi_processor_count if self.is_cuda else 148
         self.timer = None  # optional StepTimer (device span of every step, for benchmarks)
         self.h2d_bytes = 0  # host->device bytes copied by execute() (inputs of every step)
+        self.hybrid = getattr(model, "num_gdn_layers", 0) > 0
+        if self.hybrid:  # per-sequence recurrent-state slot and reset flag (hybrid GDN models)
+            self.gdn_host = torch.zeros(2, cfg.max_num_seqs + 1, dtype=torch.int32, pin_memory=self.is_cuda)
         self.d2h_bytes = 0  # device->host bytes read back (sampled token ids)
 
     # ------------------------------------------------------------------ batch preparation
@@ -120,6 +123,9 @@ class ModelRunner:
             h.seq_ids[i] = c.seq.seq_id
             h.start[i] = c.start
             h.n_new[i] = c.num_tokens
+            if self.hybrid:
+                self.gdn_host[0, i] = c.seq.state_slot
+                self.gdn_host[1, i] = 1 if c.start == 0 else 0
             toks = c.tokens if c.tokens is not None else c.seq.tokens(c.start, c.start + c.num_tokens)
             ids[t:t + c.num_tokens] = toks
             if c.num_tokens and toks[-1] < 0:  # a token still being sampled by the in-flight step
@@ -227,6 +233,7 @@ class ModelRunner:
         bt = h.block_tables[:n].to(dev, non_blocking=True)[:, :nb]  # contiguous pinned rows; sliced on device
         lens = h.seq_lens[:n].to(dev, non_blocking=True)
         meta = AttnMetadata(positions=positions, slot_mapping=slots, num_decode=nd)
+        self._gdn_meta(meta, n)
         if nd > 0:
             meta.decode_block_tables = bt[:nd]
             meta.decode_seq_lens = lens[:nd]
@@ -303,7 +310,18 @@ class ModelRunner:
         if self.is_cuda:
             meta.prefill_tiles = ops.prefill_schedule(qs.tolist(), h.seq_lens[:n].tolist(), self.model.H,
                                                       self.model.Hk, self.model.D).to(dev)
+        self._gdn_meta(meta, n)
         return self.model.forward(h.input_ids[:T].to(dev), meta, self.kv_cache, hidden_only=True)
+
+    def _gdn_meta(self, meta: AttnMetadata, n: int) -> None:
+        """Hybrid GDN models: state slot and reset flag of each sequence, token offsets of all."""
+        if not self.hybrid:
+            return
+        dev = self.device
+        meta.gdn_slots = self.gdn_host[0, :n].to(dev, non_blocking=True)
+        meta.gdn_reset = self.gdn_host[1, :n].to(dev, non_blocking=True)
+        meta.gdn_query_start = self.host.query_start[: n + 1].to(dev, non_blocking=True)
+        self.h2d_bytes += 4 * (3 * n + 1)
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
         special = [i for i, s in enumerate(seqs) if s.params.needs_host_sampling]

@@ -106,7 +106,7 @@ class Sequence:
                  "arrival_time", "num_computed_tokens", "status", "first_token_time", "finish_time",
                  "token_times", "block_hashes", "num_preemptions", "predicted_len", "stop_reason",
                  "output_text", "priority", "scheduled_time", "pending", "tenant", "mirostat_mu", "logprobs",
-                 "guide")
+                 "guide", "state_slot")
 
     def __init__(self, request_id: str, prompt_token_ids: List[int], params: SamplingParams,
                  lora_id: int = 0, arrival_time: Optional[float] = None, priority: int = 0):
@@ -134,6 +134,7 @@ class Sequence:
         self.mirostat_mu: Optional[float] = None
         self.logprobs: List[dict] = []  # per output token when params.logprobs is set
         self.guide = None  # constrained decoding: native GrammarMatcher of the output so far
+        self.state_slot = -1  # hybrid GDN models: recurrent-state slot while the sequence holds KV
 
     @property
     def num_tokens(self) -> int:

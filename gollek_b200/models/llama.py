@@ -54,6 +54,11 @@ class AttnMetadata:
     prefill_query_start: Optional[torch.Tensor] = None   # [np + 1] int32 (relative)
     prefill_tiles: Optional[torch.Tensor] = None         # ops.prefill_schedule work list (int32)
     logits_indices: Optional[torch.Tensor] = None        # [B_out] int64 rows for the lm_head
+    # hybrid GDN models: per sequence (batch order) its recurrent-state slot, whether the step starts
+    # it from the zero state, and the token offsets of all sequences
+    gdn_slots: Optional[torch.Tensor] = None             # [n] int32
+    gdn_reset: Optional[torch.Tensor] = None             # [n] int32
+    gdn_query_start: Optional[torch.Tensor] = None       # [n + 1] int32
 
     @property
     def num_tokens(self) -> int:
@@ -190,6 +195,22 @@ class LlamaModel:
         self.cos_sin_local = (rope_cos_sin(cfg, n_pos, device=self.device, theta=cfg.rope_local_theta)
                               if cfg.rope_local_theta else None)
         self.windows = [cfg.layer_window(i) for i in range(cfg.num_hidden_layers)]
+        # hybrid stacks: KV cache rows only for attention layers; GDN layers keep a recurrent state
+        # [slots, Hg, 128, 128] fp32 per layer instead
+        self.kv_index, self.gdn_index = [], []
+        na = ng = 0
+        for i in range(cfg.num_hidden_layers):
+            g = cfg.is_gdn_layer(i)
+            self.kv_index.append(-1 if g else na)
+            self.gdn_index.append(ng if g else -1)
+            na, ng = na + (not g), ng + g
+        self.num_kv_layers, self.num_gdn_layers = na, ng
+        self.Hg = 0
+        if ng:
+            if cfg.gdn_heads % tp:
+                raise ValueError("GDN heads must be divisible by the TP size")
+            self.Hg = cfg.gdn_heads // tp
+        self.gdn_state: Optional[torch.Tensor] = None
         self.layers: List[Dict[str, torch.Tensor]] = []
         self.embed: Optional[torch.Tensor] = None
         self.norm: Optional[torch.Tensor] = None
@@ -250,33 +271,7 @@ class LlamaModel:
                 return (x.float() + 1.0).to(dt).contiguous()
             return x.contiguous()
 
-        self.embed = t("model.embed_tokens.weight").contiguous()
-        self.norm = norm_w(t("model.norm.weight"))
-        head_name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
-        self.lm_head = t(head_name)[r * self.V_local:(r + 1) * self.V_local].contiguous()
-        self.layers = []
-        for i in range(cfg.num_hidden_layers):
-            p = f"model.layers.{i}."
-            c = layer_tensors(t, cfg, i)
-            kv0, kv1 = self.kv_head0 * Dl, (self.kv_head0 + Hk) * Dl
-            q = _pad_heads(c["q"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D)
-            k = _pad_heads(c["k"][kv0:kv1], Hk, Dl, D)
-            v = _pad_heads(c["v"][kv0:kv1], Hk, Dl, D)
-            o = _pad_heads(c["o"][:, r * H * Dl:(r + 1) * H * Dl], H, Dl, D, dim=1)
-            L = {
-                "in_norm": norm_w(c["in_norm"]),
-                "post_norm": norm_w(c["post_norm"]),
-                "w_qkv": cat([q, k, v]).contiguous(),
-                "w_o": o.contiguous(),
-            }
-            if cfg.attention_bias:
-                L["qkv_bias"] = torch.cat([_pad_heads(c["q_bias"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D),
-                                           _pad_heads(c["k_bias"][kv0:kv1], Hk, Dl, D),
-                                           _pad_heads(c["v_bias"][kv0:kv1], Hk, Dl, D)]).contiguous()
-            if cfg.qk_norm:
-                L["q_norm"], L["k_norm"] = norm_w(c["q_norm"]), norm_w(c["k_norm"])
-            if cfg.sandwich_norm:
-                L["pre_ff_norm"], L["post_ff_norm"] = norm_w(c["pre_ff_norm"]), norm_w(c["post_ff_norm"])
+        def ffn(L, c, p):
             if cfg.is_moe:
                 pe = p + "block_sparse_moe."
                 L["router"] = t(pe + "gate.weight").contiguous()
@@ -301,7 +296,53 @@ class LlamaModel:
                 d = c["down"][:, r * self.F:(r + 1) * self.F]
                 L["w_gate_up"] = gate_up(g, u).contiguous()
                 L["w_down"] = down(d).contiguous()
+
+        self.embed = t("model.embed_tokens.weight").contiguous()
+        self.norm = norm_w(t("model.norm.weight"))
+        head_name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
+        self.lm_head = t(head_name)[r * self.V_local:(r + 1) * self.V_local].contiguous()
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = f"model.layers.{i}."
+            c = layer_tensors(t, cfg, i)
+            if c.get("gdn"):
+                L = self._gdn_weights(c, norm_w)
+                ffn(L, c, p)
+                self.layers.append(L)
+                continue
+            kv0, kv1 = self.kv_head0 * Dl, (self.kv_head0 + Hk) * Dl
+            q = _pad_heads(c["q"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D)
+            k = _pad_heads(c["k"][kv0:kv1], Hk, Dl, D)
+            v = _pad_heads(c["v"][kv0:kv1], Hk, Dl, D)
+            o = _pad_heads(c["o"][:, r * H * Dl:(r + 1) * H * Dl], H, Dl, D, dim=1)
+            L = {
+                "in_norm": norm_w(c["in_norm"]),
+                "post_norm": norm_w(c["post_norm"]),
+                "w_qkv": cat([q, k, v]).contiguous(),
+                "w_o": o.contiguous(),
+            }
+            if cfg.attention_bias:
+                L["qkv_bias"] = torch.cat([_pad_heads(c["q_bias"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D),
+                                           _pad_heads(c["k_bias"][kv0:kv1], Hk, Dl, D),
+                                           _pad_heads(c["v_bias"][kv0:kv1], Hk, Dl, D)]).contiguous()
+            if cfg.qk_norm:
+                L["q_norm"], L["k_norm"] = norm_w(c["q_norm"]), norm_w(c["k_norm"])
+            if cfg.sandwich_norm:
+                L["pre_ff_norm"], L["post_ff_norm"] = norm_w(c["pre_ff_norm"]), norm_w(c["post_ff_norm"])
+            ffn(L, c, p)
             self.layers.append(L)
+
+    def _gdn_weights(self, c: dict, norm_w) -> Dict[str, torch.Tensor]:
+        """GDN layer: one fused input projection [q | k | v | g | a | b] of this rank's heads (rows
+        padded to 128), the row-parallel output projection and the fp32 gate parameters."""
+        r, Hg, GD = self.comm.rank, self.Hg, 128
+        sl, hs = slice(r * Hg * GD, (r + 1) * Hg * GD), slice(r * Hg, (r + 1) * Hg)
+        w_in = torch.cat([c["gq"][sl], c["gk"][sl], c["gv"][sl], c["gg"][sl], c["ga"][hs], c["gb"][hs]], 0)
+        rows = (w_in.shape[0] + 127) // 128 * 128
+        return {"gdn": True, "in_norm": norm_w(c["in_norm"]), "post_norm": norm_w(c["post_norm"]),
+                "w_gdn_in": _pad_rows(w_in, rows).contiguous(), "w_o": c["o"][:, sl].contiguous(),
+                "A_log": c["A_log"][hs].float().contiguous(), "dt_bias": c["dt_bias"][hs].float().contiguous(),
+                "gdn_norm": c["gnorm"].contiguous()}
 
     def init_random(self, seed: int = 0, std: float = 0.02, fp8: bool = False) -> None:
         """Random-init this rank's shard directly on the device (benchmarks; no checkpoint)."""
@@ -322,16 +363,23 @@ class LlamaModel:
         self.norm = ones(h)
         self.lm_head = rnd(self.V_local, h)
         self.layers = []
-        for _ in range(cfg.num_hidden_layers):
-            L = {
-                "in_norm": ones(h),
-                "post_norm": ones(h),
-                "w_qkv": _pad_heads(rnd((self.H + 2 * self.Hk) * Dl, h), self.H + 2 * self.Hk, Dl, D),
-                "w_o": _pad_heads(rnd(h, self.H * Dl), self.H, Dl, D, dim=1),
-            }
-            if cfg.attention_bias:
+        for li in range(cfg.num_hidden_layers):
+            if cfg.is_gdn_layer(li):
+                hd = self.Hg * 128
+                rows = (4 * hd + 2 * self.Hg + 127) // 128 * 128
+                L = {"gdn": True, "in_norm": ones(h), "post_norm": ones(h), "w_gdn_in": rnd(rows, h),
+                     "w_o": rnd(h, hd), "A_log": torch.full((self.Hg,), 1.0, device=dev),
+                     "dt_bias": torch.zeros(self.Hg, device=dev), "gdn_norm": ones(128)}
+            else:
+                L = {
+                    "in_norm": ones(h),
+                    "post_norm": ones(h),
+                    "w_qkv": _pad_heads(rnd((self.H + 2 * self.Hk) * Dl, h), self.H + 2 * self.Hk, Dl, D),
+                    "w_o": _pad_heads(rnd(h, self.H * Dl), self.H, Dl, D, dim=1),
+                }
+            if cfg.attention_bias and "w_qkv" in L:
                 L["qkv_bias"] = _pad_heads(rnd((self.H + 2 * self.Hk) * Dl), self.H + 2 * self.Hk, Dl, D)
-            if cfg.qk_norm:
+            if cfg.qk_norm and "w_qkv" in L:
                 L["q_norm"], L["k_norm"] = ones(D), ones(D)
             if cfg.sandwich_norm:
                 L["pre_ff_norm"], L["post_ff_norm"] = ones(h), ones(h)
@@ -409,10 +457,19 @@ class LlamaModel:
 
     # ------------------------------------------------------------------ KV cache
     def kv_cache_shape(self, num_blocks: int, block_size: int = 16) -> tuple:
-        return (self.cfg.num_hidden_layers, num_blocks, 2, self.Hk, block_size, self.D)
+        return (max(1, self.num_kv_layers), num_blocks, 2, self.Hk, block_size, self.D)
 
     def kv_bytes_per_block(self, block_size: int = 16) -> int:
-        return self.cfg.num_hidden_layers * 2 * self.Hk * block_size * self.D * torch.finfo(self.dtype).bits // 8
+        return max(1, self.num_kv_layers) * 2 * self.Hk * block_size * self.D * torch.finfo(self.dtype).bits // 8
+
+    def gdn_state_bytes(self, num_slots: int) -> int:
+        return self.num_gdn_layers * num_slots * self.Hg * 128 * 128 * 4
+
+    def alloc_gdn_state(self, num_slots: int) -> None:
+        """Recurrent states of the GDN layers: [gdn_layers, slots, Hg, 128, 128] fp32."""
+        if self.num_gdn_layers:
+            self.gdn_state = torch.zeros(self.num_gdn_layers, num_slots, self.Hg, 128, 128, dtype=torch.float32,
+                                         device=self.device)
 
     # ------------------------------------------------------------------ forward
     def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata, window: int = 0) -> torch.Tensor:
@@ -464,6 +521,17 @@ class LlamaModel:
             acc.index_add_(0, rows, ye * we[:, None])
         return _copy_out(acc.to(x.dtype), out)
 
+    def _gdn(self, x: torch.Tensor, L: Dict[str, torch.Tensor], meta: AttnMetadata, li: int) -> torch.Tensor:
+        """Gated delta rule layer: fused projection, K14 scan over the batch's sequences (state slots
+        per sequence), gated head norm; returns [T, Hg * 128] for the row-parallel output GEMM."""
+        if self.gdn_state is None or meta.gdn_slots is None:
+            raise RuntimeError("GDN layer without recurrent state / slot metadata")
+        proj = ops.linear(x, L["w_gdn_in"])
+        hd = self.Hg * 128
+        o = ops.gdn_scan(proj, self.gdn_state[self.gdn_index[li]], meta.gdn_slots, meta.gdn_reset,
+                         meta.gdn_query_start, L["A_log"], L["dt_bias"], self.Hg)
+        return ops.gdn_gated_norm(o, proj[:, 3 * hd:4 * hd], L["gdn_norm"], self.cfg.rms_norm_eps)
+
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
                 hidden_only: bool = False, greedy: bool = False) -> torch.Tensor:
         """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP), or with
@@ -485,16 +553,19 @@ class LlamaModel:
             if nv:
                 tracing.nvtx_push(f"layer{li}")
                 tracing.nvtx_push("attn")
-            qkv = ops.linear(x, L["w_qkv"])
-            if self.lora is not None:
-                self.lora.apply(li, "qkv", x, qkv)
-            cache = kv_cache[li] if kv_cache is not None else None
-            win = self.windows[li]
-            cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
-            q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
-                                  bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
-                                  norm_eps=eps)
-            a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
+            if L.get("gdn"):
+                a = self._gdn(x, L, meta, li)
+            else:
+                qkv = ops.linear(x, L["w_qkv"])
+                if self.lora is not None:
+                    self.lora.apply(li, "qkv", x, qkv)
+                cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
+                win = self.windows[li]
+                cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
+                q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
+                                      bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                                      norm_eps=eps)
+                a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
             h = self._row_linear(a, L["w_o"], li, "o")
             if nv:
                 tracing.nvtx_pop()

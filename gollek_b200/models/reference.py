@@ -50,20 +50,33 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
     for i in range(cfg.num_hidden_layers):
         p = f"model.layers.{i}."
         w[p + "input_layernorm.weight"] = norm(h)
-        if fam == "phi3":
+        if cfg.is_gdn_layer(i):  # gated delta rule layer of a hybrid stack
+            hd = cfg.gdn_heads * cfg.gdn_head_dim
+            pl = p + "linear_attn."
+            for n in ("q", "k", "v", "g"):
+                w[pl + f"{n}_proj.weight"] = rnd(hd, h)
+            w[pl + "a_proj.weight"] = rnd(cfg.gdn_heads, h)
+            w[pl + "b_proj.weight"] = rnd(cfg.gdn_heads, h)
+            w[pl + "A_log"] = torch.log(1.0 + 15.0 * torch.rand(cfg.gdn_heads, generator=g, device=device)).to(
+                torch.float32)
+            w[pl + "dt_bias"] = rnd(cfg.gdn_heads, s=0.5).to(torch.float32)
+            w[pl + "norm.weight"] = torch.ones(cfg.gdn_head_dim, dtype=dtype, device=device)
+            w[pl + "o_proj.weight"] = rnd(h, hd)
+        elif fam == "phi3":
             w[p + "self_attn.qkv_proj.weight"] = rnd(q + 2 * kv, h)
         else:
             w[p + "self_attn.q_proj.weight"] = rnd(q, h)
             w[p + "self_attn.k_proj.weight"] = rnd(kv, h)
             w[p + "self_attn.v_proj.weight"] = rnd(kv, h)
-        if cfg.attention_bias:
+        if cfg.attention_bias and not cfg.is_gdn_layer(i):
             w[p + "self_attn.q_proj.bias"] = rnd(q)
             w[p + "self_attn.k_proj.bias"] = rnd(kv)
             w[p + "self_attn.v_proj.bias"] = rnd(kv)
-        if cfg.qk_norm:
+        if cfg.qk_norm and not cfg.is_gdn_layer(i):
             w[p + "self_attn.q_norm.weight"] = norm(D)
             w[p + "self_attn.k_norm.weight"] = norm(D)
-        w[p + "self_attn.o_proj.weight"] = rnd(h, q)
+        if not cfg.is_gdn_layer(i):
+            w[p + "self_attn.o_proj.weight"] = rnd(h, q)
         w[p + "post_attention_layernorm.weight"] = norm(h)
         if cfg.sandwich_norm:
             w[p + "pre_feedforward_layernorm.weight"] = norm(h)
@@ -95,19 +108,29 @@ def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
     supports row slicing). Phi-3's fused ``qkv_proj`` / ``gate_up_proj`` are split by rows."""
     p = f"model.layers.{i}."
     q_sz, kv_sz, f = cfg.q_size, cfg.kv_size, cfg.intermediate_size
-    t = {"in_norm": get(p + "input_layernorm.weight"), "post_norm": get(p + "post_attention_layernorm.weight"),
-         "o": get(p + "self_attn.o_proj.weight")}
-    if cfg.architecture == "phi3":
+    if cfg.is_gdn_layer(i):
+        pl = p + "linear_attn."
+        t = {"in_norm": get(p + "input_layernorm.weight"), "post_norm": get(p + "post_attention_layernorm.weight"),
+             "gdn": True, "o": get(pl + "o_proj.weight"), "A_log": get(pl + "A_log"), "dt_bias": get(pl + "dt_bias"),
+             "gnorm": get(pl + "norm.weight")}
+        for n in ("q", "k", "v", "g", "a", "b"):
+            t["g" + n] = get(pl + f"{n}_proj.weight")
+    else:
+        t = {"in_norm": get(p + "input_layernorm.weight"), "post_norm": get(p + "post_attention_layernorm.weight"),
+             "o": get(p + "self_attn.o_proj.weight")}
+    if cfg.is_gdn_layer(i):
+        pass
+    elif cfg.architecture == "phi3":
         qkv = get(p + "self_attn.qkv_proj.weight")
         t["q"], t["k"], t["v"] = qkv[:q_sz], qkv[q_sz:q_sz + kv_sz], qkv[q_sz + kv_sz:q_sz + 2 * kv_sz]
     else:
         t["q"] = get(p + "self_attn.q_proj.weight")
         t["k"] = get(p + "self_attn.k_proj.weight")
         t["v"] = get(p + "self_attn.v_proj.weight")
-    if cfg.attention_bias:
+    if cfg.attention_bias and not cfg.is_gdn_layer(i):
         for n in ("q", "k", "v"):
             t[n + "_bias"] = get(p + f"self_attn.{n}_proj.bias")
-    if cfg.qk_norm:
+    if cfg.qk_norm and not cfg.is_gdn_layer(i):
         t["q_norm"] = get(p + "self_attn.q_norm.weight")
         t["k_norm"] = get(p + "self_attn.k_norm.weight")
     if cfg.sandwich_norm:
@@ -225,6 +248,12 @@ class ReferenceDecoder:
         for i in range(cfg.num_hidden_layers):
             L = layer_tensors(w.__getitem__, cfg, i)
             x = rms_norm_ref(h, L["in_norm"], eps, uo)
+            if L.get("gdn"):
+                a = self._gdn(x, L)
+                h = h + a
+                x = rms_norm_ref(h, L["post_norm"], eps, uo)
+                h = h + self._ffn(x, L, i)
+                continue
             q = x @ L["q"].t()
             k = x @ L["k"].t()
             v = x @ L["v"].t()
@@ -258,16 +287,7 @@ class ReferenceDecoder:
             else:
                 h = h + a
                 x = rms_norm_ref(h, L["post_norm"], eps, uo)
-            if cfg.is_moe:
-                pe = f"model.layers.{i}.block_sparse_moe."
-                experts = [(w[pe + f"experts.{e}.w1.weight"], w[pe + f"experts.{e}.w3.weight"],
-                            w[pe + f"experts.{e}.w2.weight"]) for e in range(cfg.num_local_experts)]
-                m = moe_ref(x, w[pe + "gate.weight"], experts, cfg.num_experts_per_tok)
-            else:
-                g = x @ L["gate"].t()
-                act = torch.nn.functional.silu(g) if cfg.hidden_act == "silu" else \
-                    torch.nn.functional.gelu(g, approximate="tanh")
-                m = (act * (x @ L["up"].t())) @ L["down"].t()
+            m = self._ffn(x, L, i)
             if cfg.sandwich_norm:
                 m = rms_norm_ref(m, L["post_ff_norm"], eps, uo)
             h = h + m
@@ -278,6 +298,31 @@ class ReferenceDecoder:
             c = cfg.final_logit_softcapping
             logits = c * torch.tanh(logits / c)
         return logits
+
+    def _ffn(self, x: torch.Tensor, L: dict, i: int) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        if cfg.is_moe:
+            pe = f"model.layers.{i}.block_sparse_moe."
+            experts = [(w[pe + f"experts.{e}.w1.weight"], w[pe + f"experts.{e}.w3.weight"],
+                        w[pe + f"experts.{e}.w2.weight"]) for e in range(cfg.num_local_experts)]
+            return moe_ref(x, w[pe + "gate.weight"], experts, cfg.num_experts_per_tok)
+        g = x @ L["gate"].t()
+        act = torch.nn.functional.silu(g) if cfg.hidden_act == "silu" else \
+            torch.nn.functional.gelu(g, approximate="tanh")
+        return (act * (x @ L["up"].t())) @ L["down"].t()
+
+    def _gdn(self, x: torch.Tensor, L: dict) -> torch.Tensor:
+        """Gated delta rule layer over the whole sequence (fresh state)."""
+        from ..ops import reference as ref_ops
+        cfg = self.cfg
+        Hg, D = cfg.gdn_heads, cfg.gdn_head_dim
+        S = x.shape[0]
+        proj = torch.cat([x @ L["g" + n].t() for n in ("q", "k", "v", "g", "a", "b")], dim=-1)
+        state = torch.zeros(1, Hg, D, D)
+        o = ref_ops.gdn_scan(proj, state, torch.zeros(1, dtype=torch.int32), torch.ones(1, dtype=torch.int32),
+                             torch.tensor([0, S], dtype=torch.int32), L["A_log"], L["dt_bias"], Hg)
+        y = ref_ops.gdn_gated_norm(o, proj[:, 3 * Hg * D:4 * Hg * D], L["gnorm"], cfg.rms_norm_eps)
+        return y @ L["o"].t()
 
     def greedy(self, prompt: list, n_new: int) -> tuple:
         """Greedy decode by re-running the dense forward; returns (tokens, per-step logits)."""

@@ -44,6 +44,7 @@ CUDA_SOURCES = [
     "kernels/moe.cu",
     "kernels/kv_transfer.cu",
     "kernels/int4.cu",
+    "kernels/gdn.cu",
 ]
 HOST_SOURCES = [
     "host/host_bindings.cpp",

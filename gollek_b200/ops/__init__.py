@@ -523,6 +523,32 @@ def kv_gather_blocks(cache: torch.Tensor, block_ids: torch.Tensor) -> torch.Tens
     return packed
 
 
+# ---------------------------------------------------------------------------- gated delta rule (K14)
+def gdn_scan(proj: torch.Tensor, state: torch.Tensor, slots: torch.Tensor, reset: torch.Tensor,
+             query_start: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor, Hg: int,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Gated delta rule over the varlen token batch. proj [T, >= 4*Hg*D + 2*Hg] holds q | k | v | g |
+    a | b per token; state [slots, Hg, D, D] fp32 (this layer) is read (unless ``reset``) and
+    updated per sequence; returns raw o [T, Hg, D]."""
+    if not proj.is_cuda:
+        return _cpu(ref.gdn_scan(proj, state, slots, reset, query_start, a_log, dt_bias, Hg).to(proj.dtype), out)
+    T, D = proj.shape[0], state.shape[-1]
+    out = torch.empty(T, Hg, D, dtype=proj.dtype, device=proj.device) if out is None else out
+    _C().gdn_scan(proj, out, state, slots, reset, query_start, a_log, dt_bias, Hg)
+    return out
+
+
+def gdn_gated_norm(o: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y [T, Hg*D] = RMSNorm_head(o) * w * silu(g) for o [T, Hg, D] and g a [T, Hg*D] view."""
+    if not o.is_cuda:
+        return _cpu(ref.gdn_gated_norm(o, g, w, eps), out)
+    T, Hg, D = o.shape
+    out = torch.empty(T, Hg * D, dtype=o.dtype, device=o.device) if out is None else out
+    _C().gdn_gated_norm(out, o, g, w, Hg, float(eps))
+    return out
+
+
 def kv_key_norms(cache: torch.Tensor, block_ids: torch.Tensor) -> torch.Tensor:
     """Mean key L2 norm of each listed block over layers, KV heads and tokens (KV eviction scoring)."""
     ids = block_ids.to(cache.device, torch.int32)

@@ -296,3 +296,44 @@ def attention_dense(q, k, v, causal=True, scale=None):
     if causal:
         s = s + torch.full((S, S), float("-inf"), device=q.device).triu(1)
     return torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).to(q.dtype)
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):
+    """alpha = exp(-exp(A_log) * softplus(a + dt_bias)), beta = sigmoid(b); a, b [T, Hg]."""
+    alpha = torch.exp(-torch.exp(a_log.float()) * torch.nn.functional.softplus(a.float() + dt_bias.float()))
+    return alpha, torch.sigmoid(b.float())
+
+
+def gdn_scan(proj: torch.Tensor, state: torch.Tensor, slots: torch.Tensor, reset: torch.Tensor,
+             query_start: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor, Hg: int) -> torch.Tensor:
+    """fp32 gated delta rule over varlen sequences (see csrc/kernels/gdn.cu); updates ``state`` in
+    place and returns raw o [T, Hg, D]."""
+    D = state.shape[-1]
+    HD = Hg * D
+    p = proj.float()
+    T = p.shape[0]
+    silu = torch.nn.functional.silu
+    q = torch.nn.functional.normalize(silu(p[:, :HD].view(T, Hg, D)), dim=-1, eps=1e-6) / math.sqrt(D)
+    k = torch.nn.functional.normalize(silu(p[:, HD:2 * HD].view(T, Hg, D)), dim=-1, eps=1e-6)
+    v = silu(p[:, 2 * HD:3 * HD].view(T, Hg, D))
+    alpha, beta = gdn_gates(p[:, 4 * HD:4 * HD + Hg], p[:, 4 * HD + Hg:4 * HD + 2 * Hg], a_log, dt_bias)
+    out = torch.zeros(T, Hg, D, dtype=torch.float32, device=proj.device)
+    qs = query_start.tolist()
+    for i in range(len(qs) - 1):
+        slot = int(slots[i])
+        S = torch.zeros(Hg, D, D, device=proj.device) if int(reset[i]) else state[slot].float().clone()
+        for t in range(qs[i], qs[i + 1]):
+            S = alpha[t].view(Hg, 1, 1) * S
+            u = beta[t].view(Hg, 1) * (v[t] - torch.einsum("hij,hi->hj", S, k[t]))
+            S = S + k[t].unsqueeze(-1) * u.unsqueeze(1)
+            out[t] = torch.einsum("hij,hi->hj", S, q[t])
+        state[slot] = S.to(state.dtype)
+    return out
+
+
+def gdn_gated_norm(o: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm over each head of o [T, Hg, D] times w, times silu(g) [T, Hg*D]; returns [T, Hg*D]."""
+    T, Hg, D = o.shape
+    of = o.float()
+    y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    return (y.reshape(T, Hg * D) * torch.nn.functional.silu(g.float())).to(o.dtype)
