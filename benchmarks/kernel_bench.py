@@ -5,7 +5,7 @@ Every number: median of CUDA-event timings on the launching stream after warm-up
 peaks in MEASURED_PEAKS.json (HBM copy GB/s, cuBLAS bf16 TFLOP/s burst). cuBLAS (torch.matmul)
 timings are printed beside our GEMMs as a reference point only.
 
-    python benchmarks/kernel_bench.py [--only gemm,attn,norm] [--json out.jsonl]
+    python benchmarks/kernel_bench.py [--only gemm,attn,norm,gdn] [--json out.jsonl]
 """
 from __future__ import annotations
 
@@ -118,6 +118,22 @@ def main():
                                                                    out=out, tensor_cores=tc, emu=emu),
                                iters=args.iters, flush_bytes=flush)
                 rec(f"attn_prefill_{name}_{nseq}x{L}", ms, flops, nbytes)
+    if "gdn" in only:
+        # K14 gated delta rule: decode (one token per sequence, state-bandwidth bound: the fp32 state of
+        # every head is read and written) and one long prefill sequence (CUDA-core FMAs)
+        Hg, D = 32, 128
+        for nseq, L in ((256, 1), (1, 4096), (8, 1024)):
+            T = nseq * L
+            proj = torch.randn(T, 4 * Hg * D + 2 * Hg, device=dev).bfloat16()
+            state = torch.zeros(nseq, Hg, D, D, device=dev)
+            slots = torch.arange(nseq, dtype=torch.int32, device=dev)
+            reset = torch.zeros(nseq, dtype=torch.int32, device=dev)
+            qs = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+            a_log, dt = torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev)
+            out = torch.empty(T, Hg, D, device=dev).bfloat16()
+            ms = time_cuda(lambda: ops.gdn_scan(proj, state, slots, reset, qs, a_log, dt, Hg, out=out),
+                           iters=args.iters, flush_bytes=flush)
+            rec(f"gdn_scan_{nseq}x{L}", ms, 6.0 * T * Hg * D * D, 2.0 * nseq * Hg * D * D * 4 + proj.numel() * 2)
     if "norm" in only:
         d = 4096
         for T in (256, 8192):

@@ -4,6 +4,7 @@
     python benchmarks/one_kernel.py decode --B 256 --ctx 1200
     python benchmarks/one_kernel.py prefill --nseq 4 --L 2048
     python benchmarks/one_kernel.py moe --T 256 --e-loc 1      (Mixtral-8x7B layer, one EP=8 shard)
+    python benchmarks/one_kernel.py gdn --nseq 256 --L 1       (gated delta rule decode, 32 heads)
 """
 from __future__ import annotations
 
@@ -20,7 +21,7 @@ from gollek_b200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe"])
+    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "gdn"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -49,6 +50,16 @@ def main():
         dn = (torch.randn(a.e_loc * H, F, device=dev) * 0.02).bfloat16()
         for _ in range(a.reps):
             ops.fused_moe(x, router, gu, dn, 2, e0=0, e_loc=a.e_loc)
+    elif a.kind == "gdn":
+        Hg, D = 32, 128
+        T = a.nseq * a.L
+        proj = torch.randn(T, 4 * Hg * D + 2 * Hg, device=dev).bfloat16()
+        state = torch.zeros(a.nseq, Hg, D, D, device=dev)
+        slots = torch.arange(a.nseq, dtype=torch.int32, device=dev)
+        reset = torch.zeros(a.nseq, dtype=torch.int32, device=dev)
+        qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
+        for _ in range(a.reps):
+            ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
     elif a.kind == "decode":
         Hq, Hk, D, bs = 32, 8, 128, 16
         nblk = (a.ctx + bs - 1) // bs
