@@ -10,10 +10,11 @@
 // with q, k = L2-normalised silu(projection) (q also scaled by dk^-1/2) and v = silu(projection)
 // (Yang, Kautz, Hatamizadeh, "Gated Delta Networks", ICLR 2025). Column j of S only depends on
 // column j and on the shared k, q, alpha, beta, so the value dimension splits across warps with no
-// reduction: one warp owns 16 columns of one head of one sequence, two lanes per column with 64
-// state rows each in registers (one shuffle joins their partial dot products). Tokens are staged 32
-// at a time (q, k normalised once per chunk in shared memory); the scan over the chunk is 3 x 64
-// FMAs per lane per token with broadcast shared-memory reads.
+// reduction: one CTA is one head of one sequence, its 8 warps own 16 value columns each, two lanes
+// per column with 64 state rows each in registers (one shuffle joins their partial dot products).
+// The CTA stages 16 tokens at a time (q, k normalised and v activated once per chunk in shared
+// memory); the scan over the chunk is 3 x 64 FMAs per lane per token with broadcast shared-memory
+// reads.
 // Decode (one token per sequence) and varlen prefill chunks are the same launch; `reset` starts a
 // sequence from the zero state (first chunk) instead of reading its slot.
 //
@@ -29,8 +30,8 @@ using namespace gollek;
 namespace {
 
 constexpr int kGdnD = 128;     // dk = dv
-constexpr int kGdnChunk = 32;  // tokens staged per chunk
-constexpr int kGdnCols = 16;   // value columns per warp (two lanes per column)
+constexpr int kGdnChunk = 16;  // tokens staged per chunk
+constexpr int kGdnThreads = 256;  // 8 warps x 16 value columns = one head per CTA
 
 struct GdnArgs {
   const __nv_bfloat16* proj;  // [T, ldp]: q | k | v | g (Hg*D each) | a | b (Hg each)
@@ -49,20 +50,22 @@ struct GdnArgs {
 
 GOLLEK_DEVICE float silu_f(float x) { return x / (1.f + __expf(-x)); }
 
-__global__ void __launch_bounds__(32) gdn_scan_kernel(const GdnArgs p) {
+__global__ void __launch_bounds__(kGdnThreads, 2) gdn_scan_kernel(const GdnArgs p) {
   __shared__ __align__(16) float qs[kGdnChunk][kGdnD];
   __shared__ __align__(16) float ks[kGdnChunk][kGdnD];
-  __shared__ float vs[kGdnChunk][kGdnCols];
+  __shared__ __align__(16) float vs[kGdnChunk][kGdnD];
+  __shared__ __align__(16) __nv_bfloat16 raw[kGdnChunk][3 * kGdnD];  // q | k | v of the head
   __shared__ float al[kGdnChunk], be[kGdnChunk];
-  const int b = blockIdx.x, h = blockIdx.y, j0 = blockIdx.z * kGdnCols, lane = threadIdx.x;
-  // lanes l and l + 16 share column col: rows [half * 64, half * 64 + 64) each, partial dot
-  // products combined with one shuffle
-  const int col = lane & (kGdnCols - 1), half = lane >> 4, r0 = half * (kGdnD / 2);
+  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp w owns value columns [16 w, 16 w + 16); lanes l and l + 16 share column col, rows
+  // [64 half, 64 half + 64) each, partial dot products joined with one shuffle
+  const int col = warp * 16 + (lane & 15), half = lane >> 4;
+  constexpr int R = kGdnD / 2;
+  const int r0 = half * R;
   const int t0 = p.query_start[b], t1 = p.query_start[b + 1];
   if (t1 <= t0) return;
   const int HD = p.Hg * kGdnD;
-  float* S = p.state + (int64_t)p.slots[b] * p.state_slot_stride + (int64_t)h * kGdnD * kGdnD + j0 + col;
-  constexpr int R = kGdnD / 2;
+  float* S = p.state + (int64_t)p.slots[b] * p.state_slot_stride + (int64_t)h * kGdnD * kGdnD + col;
   float s[R];
   if (p.reset[b]) {
 #pragma unroll
@@ -72,16 +75,32 @@ __global__ void __launch_bounds__(32) gdn_scan_kernel(const GdnArgs p) {
     for (int i = 0; i < R; ++i) s[i] = S[(int64_t)(r0 + i) * kGdnD];
   }
   const float A = __expf(p.a_log[h]), dtb = p.dt_bias[h];
+  constexpr int kVec = 3 * kGdnD / 8;  // 16-byte vectors per staged token
   for (int c0 = t0; c0 < t1; c0 += kGdnChunk) {
     const int nc = min(kGdnChunk, t1 - c0);
-    // stage: silu + L2 norm of q and k per token (lane covers dims 4*lane .. 4*lane+3), v, gates
-    for (int tt = 0; tt < nc; ++tt) {
-      const __nv_bfloat16* row = p.proj + (int64_t)(c0 + tt) * p.ldp;
-      float q4[4], k4[4], sq = 0.f, sk = 0.f;
+    __syncthreads();  // the previous chunk's staged rows are no longer read
+    // raw q, k, v rows of the head for the whole chunk: independent 16-byte loads by the CTA
+    for (int idx = tid; idx < nc * kVec; idx += kGdnThreads) {
+      const int tt = idx / kVec, vi = idx % kVec, part = vi / 16;
+      const __nv_bfloat16* row = p.proj + (int64_t)(c0 + tt) * p.ldp + part * HD + h * kGdnD + 8 * (vi % 16);
+      *reinterpret_cast<uint4*>(&raw[tt][8 * vi]) = *reinterpret_cast<const uint4*>(row);
+    }
+    if (tid < nc) {
+      const __nv_bfloat16* row = p.proj + (int64_t)(c0 + tid) * p.ldp + 4 * HD;
+      const float a = __bfloat162float(row[h]) + dtb, bb = __bfloat162float(row[p.Hg + h]);
+      const float sp = a > 20.f ? a : log1pf(__expf(a));
+      al[tid] = __expf(-A * sp);
+      be[tid] = 1.f / (1.f + __expf(-bb));
+    }
+    __syncthreads();
+    // silu + L2 norm of q and k, silu of v: warp w takes tokens w, w + 8, ...
+    for (int tt = warp; tt < nc; tt += kGdnThreads / 32) {
+      float q4[4], k4[4], v4[4], sq = 0.f, sk = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        q4[e] = silu_f(__bfloat162float(row[h * kGdnD + 4 * lane + e]));
-        k4[e] = silu_f(__bfloat162float(row[HD + h * kGdnD + 4 * lane + e]));
+        q4[e] = silu_f(__bfloat162float(raw[tt][4 * lane + e]));
+        k4[e] = silu_f(__bfloat162float(raw[tt][kGdnD + 4 * lane + e]));
+        v4[e] = silu_f(__bfloat162float(raw[tt][2 * kGdnD + 4 * lane + e]));
         sq = fmaf(q4[e], q4[e], sq);
         sk = fmaf(k4[e], k4[e], sk);
       }
@@ -90,16 +109,9 @@ __global__ void __launch_bounds__(32) gdn_scan_kernel(const GdnArgs p) {
       const float rq = rsqrtf(sq + 1e-6f) * p.q_scale, rk = rsqrtf(sk + 1e-6f);
       *reinterpret_cast<float4*>(&qs[tt][4 * lane]) = make_float4(q4[0] * rq, q4[1] * rq, q4[2] * rq, q4[3] * rq);
       *reinterpret_cast<float4*>(&ks[tt][4 * lane]) = make_float4(k4[0] * rk, k4[1] * rk, k4[2] * rk, k4[3] * rk);
-      if (lane < kGdnCols) vs[tt][lane] = silu_f(__bfloat162float(row[2 * HD + h * kGdnD + j0 + lane]));
+      *reinterpret_cast<float4*>(&vs[tt][4 * lane]) = make_float4(v4[0], v4[1], v4[2], v4[3]);
     }
-    if (lane < nc) {
-      const __nv_bfloat16* row = p.proj + (int64_t)(c0 + lane) * p.ldp + 4 * HD;
-      const float a = __bfloat162float(row[h]) + dtb, bb = __bfloat162float(row[p.Hg + h]);
-      const float sp = a > 20.f ? a : log1pf(__expf(a));
-      al[lane] = __expf(-A * sp);
-      be[lane] = 1.f / (1.f + __expf(-bb));
-    }
-    __syncwarp();
+    __syncthreads();
     for (int tt = 0; tt < nc; ++tt) {
       const float alpha = al[tt], beta = be[tt];
       float kd[4] = {0.f, 0.f, 0.f, 0.f};
@@ -130,9 +142,8 @@ __global__ void __launch_bounds__(32) gdn_scan_kernel(const GdnArgs p) {
       }
       float o = (od[0] + od[1]) + (od[2] + od[3]);
       o += __shfl_xor_sync(0xffffffffu, o, 16);
-      if (half == 0) p.out[((int64_t)(c0 + tt) * p.Hg + h) * kGdnD + j0 + col] = __float2bfloat16(o);
+      if (half == 0) p.out[((int64_t)(c0 + tt) * p.Hg + h) * kGdnD + col] = __float2bfloat16(o);
     }
-    __syncwarp();
   }
 #pragma unroll
   for (int i = 0; i < R; ++i) S[(int64_t)(r0 + i) * kGdnD] = s[i];
@@ -172,10 +183,11 @@ void launch_gdn_scan(const void* proj, int64_t ldp, void* out, float* state, int
                      const int* slots, const int* reset, const int* query_start, int n, const float* a_log,
                      const float* dt_bias, int Hg, int D, cudaStream_t s) {
   throw_if(D != kGdnD, "gdn: head_dim 128 only");
+  throw_if(ldp % 8 != 0, "gdn: projection rows must keep 16-byte alignment");
   if (n == 0) return;
   GdnArgs a{reinterpret_cast<const __nv_bfloat16*>(proj), ldp, reinterpret_cast<__nv_bfloat16*>(out), state,
             state_slot_stride, slots, reset, query_start, a_log, dt_bias, Hg, 1.f / sqrtf((float)D)};
-  gdn_scan_kernel<<<dim3(n, Hg, D / kGdnCols), 32, 0, s>>>(a);
+  gdn_scan_kernel<<<dim3(n, Hg), kGdnThreads, 0, s>>>(a);
   check_launch("gdn_scan");
 }
 

@@ -17,7 +17,7 @@ from gollek_b200.utils.tokenizer import ByteTokenizer
 
 def _proj(T, Hg, seed):
     g = torch.Generator().manual_seed(seed)
-    return torch.randn(T, 4 * Hg * 128 + 2 * Hg, generator=g)
+    return torch.randn(T, (4 * Hg * 128 + 2 * Hg + 7) // 8 * 8, generator=g)   # rows padded to 16 bytes
 
 
 def test_schedules():
