@@ -29,18 +29,18 @@ void check_same_device(const torch::Tensor& a, const torch::Tensor& b) {
   TORCH_CHECK(a.device() == b.device(), "tensors on different devices");
 }
 
-void rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps) {
+void rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps, bool center) {
   check_bf16(x, "x");
   check_bf16(out, "out");
   check_bf16(w, "w");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 && w.is_contiguous(), "rms_norm: row-major 2-D");
   TORCH_CHECK(out.sizes() == x.sizes() && w.numel() == x.size(1), "rms_norm: shape mismatch");
   launch_rms_norm(out.data_ptr(), x.data_ptr(), nullptr, w.data_ptr(), x.size(0), x.size(1), x.stride(0),
-                  out.stride(0), (float)eps, cur_stream());
+                  out.stride(0), (float)eps, cur_stream(), center);
 }
 
 void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w,
-                            double eps) {
+                            double eps, bool center) {
   check_bf16(x, "x");
   check_bf16(out, "out");
   check_bf16(residual, "residual");
@@ -49,7 +49,7 @@ void fused_add_rms_norm_out(torch::Tensor out, torch::Tensor x, torch::Tensor re
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 && w.is_contiguous(), "rms_norm: row-major 2-D");
   TORCH_CHECK(out.sizes() == x.sizes() && w.numel() == x.size(1), "rms_norm: shape mismatch");
   launch_rms_norm(out.data_ptr(), x.data_ptr(), residual.data_ptr(), w.data_ptr(), x.size(0), x.size(1),
-                  x.stride(0), out.stride(0), (float)eps, cur_stream());
+                  x.stride(0), out.stride(0), (float)eps, cur_stream(), center);
 }
 
 void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
@@ -625,8 +625,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_push_allreduce_add_rmsnorm", &tp_push_ar_rmsnorm_py,
         "reduce pushed partials from local memory + residual + RMSNorm (C1 consumer)");
   m.doc() = "gollek_b200 sm_100a kernels";
-  m.def("rms_norm", &rms_norm_out, "RMSNorm (K1)");
-  m.def("fused_add_rms_norm", &fused_add_rms_norm_out, "residual add + RMSNorm (K1)");
+  m.def("rms_norm", &rms_norm_out, "RMSNorm, or bias-free LayerNorm with center (K1)", py::arg("out"), py::arg("x"),
+        py::arg("w"), py::arg("eps"), py::arg("center") = false);
+  m.def("fused_add_rms_norm", &fused_add_rms_norm_out, "residual add + RMSNorm / LayerNorm (K1)", py::arg("out"),
+        py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("eps"), py::arg("center") = false);
   m.def("rope_kv_write", &rope_kv_write_out, "QKV split + RoPE + paged KV write (K2)");
   m.def("embedding", &embedding_out, "embedding gather (K13)");
   m.def("silu_mul", &silu_mul_out, "SwiGLU activation");

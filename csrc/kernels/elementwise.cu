@@ -21,13 +21,15 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* _
                                                                 const __nv_bfloat16* __restrict__ x,
                                                                 __nv_bfloat16* __restrict__ residual,
                                                                 const __nv_bfloat16* __restrict__ w, int d,
-                                                                int64_t x_stride, int64_t out_stride, float eps) {
+                                                                int64_t x_stride, int64_t out_stride, float eps,
+                                                                int center) {
+  // center != 0: LayerNorm without bias (Cohere): (x - mean) * rsqrt(var + eps) * w
   const int row = blockIdx.x;
   const int nvec = d >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * x_stride);
   uint4* rr = ADD ? reinterpret_cast<uint4*>(residual + (int64_t)row * d) : nullptr;
   float v[MAXV][8];
-  float ss = 0.f;
+  float ss = 0.f, sum = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     int idx = threadIdx.x + i * kNormThreads;
@@ -43,20 +45,34 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* _
         bf16x8_to_float(packed, v[i]);  // normalise the rounded residual, like the oracle
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      for (int j = 0; j < 8; ++j) {
+        ss += v[i][j] * v[i][j];
+        sum += v[i][j];
+      }
     }
   }
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[2][kNormThreads / 32];
   ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < kNormThreads / 32 ? red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) red[0] = t;
+  sum = warp_sum(sum);
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = ss;
+    red[1][threadIdx.x >> 5] = sum;
   }
   __syncthreads();
-  const float rs = rsqrtf(red[0] / (float)d + eps);
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kNormThreads / 32 ? red[0][threadIdx.x] : 0.f;
+    float u = threadIdx.x < kNormThreads / 32 ? red[1][threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    u = warp_sum(u);
+    if (threadIdx.x == 0) {
+      red[0][0] = t;
+      red[1][0] = u;
+    }
+  }
+  __syncthreads();
+  const float mean = center ? red[1][0] / (float)d : 0.f;
+  const float var = red[0][0] / (float)d - mean * mean;
+  const float rs = rsqrtf(fmaxf(var, 0.f) + eps);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* orow = reinterpret_cast<uint4*>(out + (int64_t)row * out_stride);
 #pragma unroll
@@ -66,7 +82,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(__nv_bfloat16* _
       float wf[8];
       bf16x8_to_float(wr[idx], wf);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = v[i][j] * rs * wf[j];
+      for (int j = 0; j < 8; ++j) v[i][j] = (v[i][j] - mean) * rs * wf[j];
       orow[idx] = float_to_bf16x8(v[i]);
     }
   }
@@ -226,7 +242,7 @@ __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
 namespace gollek {
 
 void launch_rms_norm(void* out, const void* x, void* residual, const void* w, int T, int d, int64_t x_stride,
-                     int64_t out_stride, float eps, cudaStream_t s) {
+                     int64_t out_stride, float eps, cudaStream_t s, bool center) {
   throw_if(d % 8 != 0 || d > 8 * 4 * kNormThreads, "rms_norm: hidden size must be a multiple of 8, <= 8192");
   throw_if(x_stride % 8 != 0 || out_stride % 8 != 0, "rms_norm: row stride must keep 16-byte alignment");
   if (T == 0) return;
@@ -235,9 +251,10 @@ void launch_rms_norm(void* out, const void* x, void* residual, const void* w, in
   auto* rp = reinterpret_cast<__nv_bfloat16*>(residual);
   auto* wp = reinterpret_cast<const __nv_bfloat16*>(w);
   const int nvec = d / 8;
+  const int c = center ? 1 : 0;
 #define GOLLEK_NORM(V)                                                                                        \
-  if (rp) rms_norm_kernel<V, true><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps);   \
-  else rms_norm_kernel<V, false><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps);
+  if (rp) rms_norm_kernel<V, true><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps, c);  \
+  else rms_norm_kernel<V, false><<<T, kNormThreads, 0, s>>>(o, xp, rp, wp, d, x_stride, out_stride, eps, c);
   if (nvec <= kNormThreads) {
     GOLLEK_NORM(1)
   } else if (nvec <= 2 * kNormThreads) {

@@ -22,7 +22,8 @@ inline void check_launch(const char* what) {
 
 // ---- elementwise (K1, K2, K13)
 void launch_rms_norm(void* out, const void* x, void* residual, const void* w, int T, int d, int64_t x_stride,
-                     int64_t out_stride, float eps, cudaStream_t s);
+                     int64_t out_stride, float eps, cudaStream_t s,
+                     bool center = false);
 void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
                           const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
                           int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,

@@ -58,7 +58,7 @@ class RopeScaling:
 # Model families handled by the decoder graph (models/llama.py). Llama-like families differ in
 # projection biases, QK-norm, sliding windows, norm placement and activation; Gemma adds a
 # sqrt(hidden) embedding scale, (1 + w) RMSNorm weights, GeGLU, sandwich norms and softcapping.
-FAMILIES = ("llama", "mistral", "mixtral", "qwen2", "qwen3", "gemma", "gemma2", "gemma3", "phi3")
+FAMILIES = ("llama", "mistral", "mixtral", "qwen2", "qwen3", "gemma", "gemma2", "gemma3", "phi3", "cohere2")
 
 
 @dataclass
@@ -94,6 +94,13 @@ class ModelConfig:
     norm_unit_offset: bool = False       # RMSNorm scales by (1 + w) (Gemma)
     embed_scale: float = 1.0             # embeddings multiplied by this (Gemma: sqrt(hidden))
     sandwich_norm: bool = False          # norms after attention / MLP outputs too (Gemma-2/3)
+    # Cohere-2: bias-free LayerNorm, attention and MLP in parallel off one norm, interleaved-pair RoPE
+    # on sliding-window layers only (full layers use no positions), logits times logit_scale
+    norm_center: bool = False
+    parallel_block: bool = False
+    rope_interleaved: bool = False
+    rope_sliding_only: bool = False
+    logit_scale: float = 1.0
     # hybrid gated-delta-rule / attention stacks: "H1" = {G,G,G,G,A,G}, "H2" = {G,G,A,G,G,A} per 6
     # layers (G = Gated DeltaNet layer, A = softmax attention); None = attention only
     hybrid_schedule: Optional[str] = None
@@ -174,7 +181,7 @@ class ModelConfig:
         mt = str(d.get("model_type", "llama"))
         fam = {"llama": "llama", "mistral": "mistral", "mixtral": "mixtral", "qwen2": "qwen2", "qwen3": "qwen3",
                "gemma": "gemma", "gemma2": "gemma2", "gemma3_text": "gemma3", "gemma3": "gemma3",
-               "phi3": "phi3"}.get(mt)
+               "phi3": "phi3", "cohere2": "cohere2", "yi": "llama"}.get(mt)
         if fam is None:
             fam = "mixtral" if any("Mixtral" in a for a in archs) else "llama"
         gemma = fam.startswith("gemma")
@@ -211,6 +218,10 @@ class ModelConfig:
             layer_types = ["sliding_attention" if (i + 1) % pat else "full_attention" for i in range(nl)]
         elif fam == "gemma":
             sw, layer_types = 0, None
+        elif fam == "cohere2" and layer_types is None and sw:
+            pat = int(d.get("sliding_window_pattern", 4) or 4)
+            layer_types = ["sliding_attention" if (i + 1) % pat else "full_attention" for i in range(nl)]
+        cohere = fam == "cohere2"
         act = str(d.get("hidden_activation") or d.get("hidden_act") or "silu")
         act = "gelu_tanh" if (gemma or act.startswith("gelu")) else "silu"
         return ModelConfig(
@@ -222,11 +233,11 @@ class ModelConfig:
             num_attention_heads=nh,
             num_key_value_heads=int(d.get("num_key_value_heads", nh) or nh),
             head_dim=int(d.get("head_dim") or hs // nh),
-            rms_norm_eps=float(d.get("rms_norm_eps", 1e-6 if gemma else 1e-5)),
+            rms_norm_eps=float(d.get("layer_norm_eps", 1e-5) if cohere else d.get("rms_norm_eps", 1e-6 if gemma else 1e-5)),
             rope_theta=float(theta),
             rope_scaling=RopeScaling.from_hf(scaling),
             max_position_embeddings=int(d.get("max_position_embeddings", 8192)),
-            tie_word_embeddings=bool(d.get("tie_word_embeddings", gemma)),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", gemma or cohere)),
             num_local_experts=int(d.get("num_local_experts", 0) or 0),
             num_experts_per_tok=int(d.get("num_experts_per_tok", 0) or 0),
             attention_bias=True if fam == "qwen2" else bool(d.get("attention_bias", False)),
@@ -241,6 +252,11 @@ class ModelConfig:
             norm_unit_offset=gemma,
             embed_scale=float(hs) ** 0.5 if gemma else 1.0,
             sandwich_norm=fam in ("gemma2", "gemma3"),
+            norm_center=cohere,
+            parallel_block=cohere,
+            rope_interleaved=cohere,
+            rope_sliding_only=cohere,
+            logit_scale=float(d.get("logit_scale", 1.0) or 1.0) if cohere else 1.0,
             bos_token_id=int(d.get("bos_token_id", 1) or 1),
             eos_token_id=int(eos if eos is not None else 2),
         )
@@ -251,7 +267,7 @@ class ModelConfig:
                  "mixtral": ("MixtralForCausalLM", "mixtral"), "qwen2": ("Qwen2ForCausalLM", "qwen2"),
                  "qwen3": ("Qwen3ForCausalLM", "qwen3"), "gemma": ("GemmaForCausalLM", "gemma"),
                  "gemma2": ("Gemma2ForCausalLM", "gemma2"), "gemma3": ("Gemma3ForCausalLM", "gemma3_text"),
-                 "phi3": ("Phi3ForCausalLM", "phi3")}
+                 "phi3": ("Phi3ForCausalLM", "phi3"), "cohere2": ("Cohere2ForCausalLM", "cohere2")}
         arch, mt = names.get(fam, names["mixtral" if self.is_moe else "llama"])
         d = {
             "architectures": [arch],
@@ -294,6 +310,10 @@ class ModelConfig:
             d["final_logit_softcapping"] = self.final_logit_softcapping or None
         if fam == "gemma3":
             d["rope_local_base_freq"] = self.rope_local_theta or 10000.0
+        if fam == "cohere2":
+            d["layer_norm_eps"] = d.pop("rms_norm_eps")
+            d["logit_scale"] = self.logit_scale
+            d["pad_token_id"] = 0
         if self.rope_scaling.kind != "none":
             rs = self.rope_scaling
             d["rope_scaling"] = {"rope_type": rs.kind, "factor": rs.factor,
@@ -320,6 +340,12 @@ PRESETS: dict[str, ModelConfig] = {
         architecture="llama", vocab_size=1024, hidden_size=256, intermediate_size=512,
         num_hidden_layers=6, num_attention_heads=8, num_key_value_heads=2, head_dim=32,
         rope_theta=10000.0, max_position_embeddings=2048, hybrid_schedule="H2", gdn_num_heads=2),
+    "tiny-cohere2": ModelConfig(
+        architecture="cohere2", vocab_size=1024, hidden_size=256, intermediate_size=512,
+        num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2, head_dim=32,
+        rope_theta=10000.0, max_position_embeddings=2048, tie_word_embeddings=True, sliding_window=24,
+        layer_types=["sliding_attention", "sliding_attention", "sliding_attention", "full_attention"],
+        norm_center=True, parallel_block=True, rope_interleaved=True, rope_sliding_only=True, logit_scale=0.25),
     "tiny-mixtral": ModelConfig(
         architecture="mixtral", vocab_size=1024, hidden_size=256, intermediate_size=512,
         num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2, head_dim=32,

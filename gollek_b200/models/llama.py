@@ -103,6 +103,14 @@ class TPComm:
         return ops.argmax(t)
 
 
+def _deinterleave_heads(w: torch.Tensor, n_heads: int, d: int) -> torch.Tensor:
+    """Reorder each head's rows to (0, 2, 4, ..., 1, 3, 5, ...): RoPE on interleaved pairs
+    (2i, 2i+1) of the original rows is rotate-half RoPE on pairs (i, i + d/2) of the reordered ones,
+    and q . k is unchanged when q and k are reordered alike."""
+    perm = torch.cat([torch.arange(0, d, 2), torch.arange(1, d, 2)]).to(w.device)
+    return w.reshape(n_heads, d, *w.shape[1:]).index_select(1, perm).reshape(w.shape)
+
+
 def _pad_heads(w: torch.Tensor, n_heads: int, d: int, d_pad: int, dim: int = 0) -> torch.Tensor:
     """Zero-pad each of ``n_heads`` head blocks of width ``d`` along ``dim`` to ``d_pad``."""
     if d == d_pad:
@@ -194,6 +202,10 @@ class LlamaModel:
         self.cos_sin = rope_cos_sin(cfg, n_pos, device=self.device)
         self.cos_sin_local = (rope_cos_sin(cfg, n_pos, device=self.device, theta=cfg.rope_local_theta)
                               if cfg.rope_local_theta else None)
+        self.cos_sin_none = None  # identity rotation (cos 1, sin 0) for layers without positions
+        if cfg.rope_sliding_only:
+            half = self.cos_sin.shape[1] // 2
+            self.cos_sin_none = torch.cat([torch.ones(n_pos, half), torch.zeros(n_pos, half)], 1).to(self.cos_sin)
         self.windows = [cfg.layer_window(i) for i in range(cfg.num_hidden_layers)]
         # hybrid stacks: KV cache rows only for attention layers; GDN layers keep a recurrent state
         # [slots, Hg, 128, 128] fp32 per layer instead
@@ -299,6 +311,8 @@ class LlamaModel:
 
         self.embed = t("model.embed_tokens.weight").contiguous()
         self.norm = norm_w(t("model.norm.weight"))
+        if cfg.logit_scale != 1.0:  # logits = norm(h) @ E^T * s: the scale folds into the final norm
+            self.norm = (self.norm.float() * cfg.logit_scale).to(dt).contiguous()
         head_name = "model.embed_tokens.weight" if cfg.tie_word_embeddings else "lm_head.weight"
         self.lm_head = t(head_name)[r * self.V_local:(r + 1) * self.V_local].contiguous()
         self.layers = []
@@ -311,13 +325,16 @@ class LlamaModel:
                 self.layers.append(L)
                 continue
             kv0, kv1 = self.kv_head0 * Dl, (self.kv_head0 + Hk) * Dl
-            q = _pad_heads(c["q"][r * H * Dl:(r + 1) * H * Dl], H, Dl, D)
-            k = _pad_heads(c["k"][kv0:kv1], Hk, Dl, D)
+            cq, ck = c["q"][r * H * Dl:(r + 1) * H * Dl], c["k"][kv0:kv1]
+            if cfg.rope_interleaved:  # pairs (2i, 2i+1) -> (i, i + D/2): the NeoX kernel rotates them
+                cq, ck = _deinterleave_heads(cq, H, Dl), _deinterleave_heads(ck, Hk, Dl)
+            q = _pad_heads(cq, H, Dl, D)
+            k = _pad_heads(ck, Hk, Dl, D)
             v = _pad_heads(c["v"][kv0:kv1], Hk, Dl, D)
             o = _pad_heads(c["o"][:, r * H * Dl:(r + 1) * H * Dl], H, Dl, D, dim=1)
             L = {
                 "in_norm": norm_w(c["in_norm"]),
-                "post_norm": norm_w(c["post_norm"]),
+                "post_norm": norm_w(c["post_norm"]) if c["post_norm"] is not None else None,
                 "w_qkv": cat([q, k, v]).contiguous(),
                 "w_o": o.contiguous(),
             }
@@ -521,6 +538,14 @@ class LlamaModel:
             acc.index_add_(0, rows, ye * we[:, None])
         return _copy_out(acc.to(x.dtype), out)
 
+    def _add_norm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """residual += all_reduce(h); returns norm(residual) * w (fused collective for RMSNorm;
+        all-reduce then the LayerNorm kernel for centred norms)."""
+        eps = self.cfg.rms_norm_eps
+        if self.cfg.norm_center:
+            return ops.fused_add_rms_norm(self.comm.all_reduce(h), residual, w, eps, center=True)
+        return self.comm.allreduce_add_rmsnorm(h, residual, w, eps)
+
     def _gdn(self, x: torch.Tensor, L: Dict[str, torch.Tensor], meta: AttnMetadata, li: int) -> torch.Tensor:
         """Gated delta rule layer: fused projection, K14 scan over the batch's sequences (state slots
         per sequence), gated head norm; returns [T, Hg * 128] for the row-parallel output GEMM."""
@@ -542,7 +567,8 @@ class LlamaModel:
         h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
         n = len(self.layers)
-        x = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
+        ctr = cfg.norm_center
+        x = ops.rms_norm(h, self.layers[0]["in_norm"], eps, center=ctr)
         nv = tracing.nvtx_enabled()
         off = self.offload
         if off is not None:
@@ -562,10 +588,26 @@ class LlamaModel:
                 cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
                 win = self.windows[li]
                 cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
+                if self.cos_sin_none is not None and win == 0:
+                    cs = self.cos_sin_none
                 q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
                                       bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
                                       norm_eps=eps)
                 a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
+            if cfg.parallel_block:  # h = attn(x) + mlp(x): the down GEMM adds the attention partial
+                ha = ops.linear(a, L["w_o"])
+                if self.lora is not None:
+                    self.lora.apply(li, "o", a, ha)
+                g = ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act)
+                h = ops.linear(g, L["w_down"], residual=ha, out=self.comm.partial_buffer(T))
+                nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
+                x = self._add_norm(h, residual, nxt)
+                if nv:
+                    tracing.nvtx_pop()
+                    tracing.nvtx_pop()
+                if off is not None:
+                    off.release(li)
+                continue
             h = self._row_linear(a, L["w_o"], li, "o")
             if nv:
                 tracing.nvtx_pop()
@@ -574,7 +616,7 @@ class LlamaModel:
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, L["pre_ff_norm"], eps)
             else:
-                x = self.comm.allreduce_add_rmsnorm(h, residual, L["post_norm"], eps)
+                x = self._add_norm(h, residual, L["post_norm"])
             if nv:
                 tracing.nvtx_pop()
                 tracing.nvtx_push("moe" if cfg.is_moe else "ffn")
@@ -590,14 +632,14 @@ class LlamaModel:
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_ff_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, nxt, eps)
             else:
-                x = self.comm.allreduce_add_rmsnorm(h, residual, nxt, eps)
+                x = self._add_norm(h, residual, nxt)
             if nv:
                 tracing.nvtx_pop()
                 tracing.nvtx_pop()
             if off is not None:
                 off.release(li)
         if hidden_only:
-            return x
+            return x / cfg.logit_scale if cfg.logit_scale != 1.0 else x
         if meta.logits_indices is not None:
             x = x.index_select(0, meta.logits_indices)
         if greedy:  # token ids: argmax over the vocab shards without gathering the logits

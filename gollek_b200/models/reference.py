@@ -77,7 +77,8 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
             w[p + "self_attn.k_norm.weight"] = norm(D)
         if not cfg.is_gdn_layer(i):
             w[p + "self_attn.o_proj.weight"] = rnd(h, q)
-        w[p + "post_attention_layernorm.weight"] = norm(h)
+        if not cfg.parallel_block:
+            w[p + "post_attention_layernorm.weight"] = norm(h)
         if cfg.sandwich_norm:
             w[p + "pre_feedforward_layernorm.weight"] = norm(h)
             w[p + "post_feedforward_layernorm.weight"] = norm(h)
@@ -116,8 +117,8 @@ def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
         for n in ("q", "k", "v", "g", "a", "b"):
             t["g" + n] = get(pl + f"{n}_proj.weight")
     else:
-        t = {"in_norm": get(p + "input_layernorm.weight"), "post_norm": get(p + "post_attention_layernorm.weight"),
-             "o": get(p + "self_attn.o_proj.weight")}
+        t = {"in_norm": get(p + "input_layernorm.weight"), "o": get(p + "self_attn.o_proj.weight"),
+             "post_norm": None if cfg.parallel_block else get(p + "post_attention_layernorm.weight")}
     if cfg.is_gdn_layer(i):
         pass
     elif cfg.architecture == "phi3":
@@ -200,8 +201,21 @@ def apply_rope_neox(x: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Ten
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
 
 
-def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool = False) -> torch.Tensor:
+def apply_rope_interleaved(x: torch.Tensor, cos_sin: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    """x: [T, H, D]; RoPE on interleaved pairs (2i, 2i+1) with frequency i (Cohere), fp32 math."""
+    d = x.shape[-1]
+    cs = cos_sin[positions.long()]
+    cos, sin = cs[:, None, : d // 2].float(), cs[:, None, d // 2:].float()
     xf = x.float()
+    x1, x2 = xf[..., 0::2], xf[..., 1::2]
+    return torch.stack([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).flatten(-2).to(x.dtype)
+
+
+def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool = False,
+                 center: bool = False) -> torch.Tensor:
+    xf = x.float()
+    if center:  # bias-free LayerNorm (Cohere)
+        xf = xf - xf.mean(-1, keepdim=True)
     wf = w.float() + 1.0 if unit_offset else w.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf).to(x.dtype)
 
@@ -243,11 +257,11 @@ class ReferenceDecoder:
         pos = torch.arange(S)
         h = w["model.embed_tokens.weight"][ids.long()] * cfg.embed_scale
         H, Hk, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        uo, eps = cfg.norm_unit_offset, cfg.rms_norm_eps
+        uo, eps, ctr = cfg.norm_unit_offset, cfg.rms_norm_eps, cfg.norm_center
         causal = torch.full((S, S), float("-inf")).triu(1)
         for i in range(cfg.num_hidden_layers):
             L = layer_tensors(w.__getitem__, cfg, i)
-            x = rms_norm_ref(h, L["in_norm"], eps, uo)
+            x = rms_norm_ref(h, L["in_norm"], eps, uo, ctr)
             if L.get("gdn"):
                 a = self._gdn(x, L)
                 h = h + a
@@ -265,8 +279,10 @@ class ReferenceDecoder:
                 k = rms_norm_ref(k, L["k_norm"], eps, uo)
             win = cfg.layer_window(i)
             cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
-            q = apply_rope_neox(q, cs, pos)
-            k = apply_rope_neox(k, cs, pos)
+            if not (cfg.rope_sliding_only and win == 0):
+                rope = apply_rope_interleaved if cfg.rope_interleaved else apply_rope_neox
+                q = rope(q, cs, pos)
+                k = rope(k, cs, pos)
             rep = H // Hk
             k = k.repeat_interleave(rep, dim=1)
             v = v.repeat_interleave(rep, dim=1)
@@ -281,6 +297,9 @@ class ReferenceDecoder:
                 mask = mask + torch.full((S, S), float("-inf")).tril(-win)
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), v).reshape(S, H * D)
             a = a @ L["o"].t()
+            if cfg.parallel_block:  # attention and MLP both read x (one norm per layer)
+                h = h + a + self._ffn(x, L, i)
+                continue
             if cfg.sandwich_norm:
                 h = h + rms_norm_ref(a, L["post_norm"], eps, uo)
                 x = rms_norm_ref(h, L["pre_ff_norm"], eps, uo)
@@ -291,9 +310,11 @@ class ReferenceDecoder:
             if cfg.sandwich_norm:
                 m = rms_norm_ref(m, L["post_ff_norm"], eps, uo)
             h = h + m
-        h = rms_norm_ref(h, w["model.norm.weight"], eps, uo)
+        h = rms_norm_ref(h, w["model.norm.weight"], eps, uo, ctr)
         head = w.get("lm_head.weight", w["model.embed_tokens.weight"])
         logits = h @ head.t()
+        if cfg.logit_scale != 1.0:
+            logits = logits * cfg.logit_scale
         if cfg.final_logit_softcapping:
             c = cfg.final_logit_softcapping
             logits = c * torch.tanh(logits / c)

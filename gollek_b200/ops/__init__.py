@@ -52,21 +52,23 @@ def _cpu(result: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
 
 
 # ----------------------------------------------------------------------------- norms
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None,
+             center: bool = False) -> torch.Tensor:
+    """RMSNorm(x) * w; ``center``: bias-free LayerNorm (x - mean) * rsqrt(var + eps) * w."""
     if not x.is_cuda:
-        return _cpu(ref.rms_norm(x, w, eps), out)
+        return _cpu(ref.rms_norm(x, w, eps, center=center), out)
     out = torch.empty_like(x) if out is None else out
-    _C().rms_norm(out, x, w, float(eps))
+    _C().rms_norm(out, x, w, float(eps), bool(center))
     return out
 
 
 def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
-                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """residual += x (in place); returns rms_norm(residual) * w."""
+                       out: Optional[torch.Tensor] = None, center: bool = False) -> torch.Tensor:
+    """residual += x (in place); returns rms_norm(residual) * w (LayerNorm with ``center``)."""
     if not x.is_cuda:
-        return _cpu(ref.fused_add_rms_norm(x, residual, w, eps), out)
+        return _cpu(ref.fused_add_rms_norm(x, residual, w, eps, center=center), out)
     out = torch.empty_like(x) if out is None else out
-    _C().fused_add_rms_norm(out, x, residual, w, float(eps))
+    _C().fused_add_rms_norm(out, x, residual, w, float(eps), bool(center))
     return out
 
 

@@ -19,17 +19,20 @@ import torch
 import torch.nn.functional as F
 
 
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, center: bool = False) -> torch.Tensor:
     xf = x.float()
+    if center:  # bias-free LayerNorm
+        xf = xf - xf.mean(-1, keepdim=True)
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
     return y.to(x.dtype)
 
 
-def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float):
+def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                       center: bool = False):
     """residual += x (in place, in residual's dtype); returns rms_norm(residual) * w."""
     r = (x.float() + residual.float())
     residual.copy_(r.to(residual.dtype))
-    return rms_norm(residual, w, eps)
+    return rms_norm(residual, w, eps, center)
 
 
 def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,

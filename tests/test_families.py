@@ -1,4 +1,4 @@
-"""Serving the non-Llama families (Qwen2/3, Mistral, Gemma 1/2/3, Phi-3) through the engine:
+"""Serving the non-Llama families (Qwen2/3, Mistral, Gemma 1/2/3, Phi-3, Cohere-2) through the engine:
 greedy tokens equal the fp32 oracle (itself checked against transformers) on CPU, with chunked
 prefill, prompts longer than the sliding windows and prefix reuse; on the GPU the sm_100a kernels
 (windows, softcaps, QK-norm, biases, GeGLU, head_dim 256) produce near-argmax tokens."""
@@ -10,7 +10,8 @@ from gollek_b200.engine.engine import LLMEngine
 from gollek_b200.engine.sequence import SamplingParams
 from gollek_b200.models.reference import ReferenceDecoder, init_random_weights
 
-FAMILIES = ["tiny-qwen2", "tiny-qwen3", "tiny-mistral", "tiny-gemma", "tiny-gemma2", "tiny-gemma3", "tiny-phi3"]
+FAMILIES = ["tiny-qwen2", "tiny-qwen3", "tiny-mistral", "tiny-gemma", "tiny-gemma2", "tiny-gemma3", "tiny-phi3",
+            "tiny-cohere2"]
 
 
 def _prompts(cfg, seed, lens):

@@ -33,6 +33,21 @@ def test_rms_norm(T, d):
     torch.testing.assert_close(y.float(), yr.float(), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("T,d", [(3, 256), (64, 4096), (5, 8192)])
+def test_layer_norm(T, d):
+    """K1 with center: bias-free LayerNorm (Cohere), plain and fused with the residual add."""
+    x = bf(torch.randn(T, d, device=DEV, generator=_g(4)) + 0.5)
+    w = bf(torch.randn(d, device=DEV, generator=_g(5)))
+    torch.testing.assert_close(ops.rms_norm(x, w, 1e-5, center=True).float(),
+                               R.rms_norm(x.float(), w.float(), 1e-5, center=True), rtol=2e-2, atol=2e-2)
+    res = bf(torch.randn(T, d, device=DEV, generator=_g(6)))
+    res_ref = res.clone()
+    y = ops.fused_add_rms_norm(x, res, w, 1e-5, center=True)
+    yr = R.fused_add_rms_norm(x, res_ref, w, 1e-5, center=True)
+    torch.testing.assert_close(res, res_ref, rtol=0, atol=0)
+    torch.testing.assert_close(y.float(), yr.float(), rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("H,Hk,D", [(32, 8, 128), (8, 2, 32), (4, 1, 128)])
 def test_rope_kv_write(H, Hk, D):
     from gollek_b200.config import preset

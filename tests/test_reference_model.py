@@ -101,7 +101,7 @@ def _hf_family_model(cfg, weights):
 
 @pytest.mark.parametrize("name,S", [("tiny-qwen2", 30), ("tiny-qwen3", 30), ("tiny-mistral", 48),
                                     ("tiny-gemma", 30), ("tiny-gemma2", 40), ("tiny-gemma3", 40),
-                                    ("tiny-phi3", 56)])
+                                    ("tiny-phi3", 56), ("tiny-cohere2", 40)])
 def test_reference_family_matches_hf(name, S):
     """Each family's oracle forward (biases, QK-norm, windows longer than the sequence window,
     softcaps, sandwich norms, GeGLU, (1 + w) norms, per-layer RoPE bases) equals transformers'."""
@@ -118,7 +118,8 @@ def test_reference_family_matches_hf(name, S):
 def test_family_configs_parse_from_hf():
     import transformers
     from gollek_b200.config import ModelConfig
-    for name in ("tiny-qwen2", "tiny-qwen3", "tiny-mistral", "tiny-gemma", "tiny-gemma2", "tiny-gemma3", "tiny-phi3"):
+    for name in ("tiny-qwen2", "tiny-qwen3", "tiny-mistral", "tiny-gemma", "tiny-gemma2", "tiny-gemma3", "tiny-phi3",
+                 "tiny-cohere2"):
         cfg = preset(name)
         d = cfg.to_hf()
         mt = d.pop("model_type")
@@ -128,6 +129,7 @@ def test_family_configs_parse_from_hf():
         back = ModelConfig.from_hf(hf_cfg.to_dict())
         for f in ("architecture", "head_dim", "sliding_window", "layer_types", "qk_norm", "attention_bias",
                   "sandwich_norm", "norm_unit_offset", "hidden_act", "query_pre_attn_scalar",
-                  "attn_logit_softcapping", "final_logit_softcapping", "tie_word_embeddings"):
+                  "attn_logit_softcapping", "final_logit_softcapping", "tie_word_embeddings", "norm_center",
+                  "parallel_block", "rope_interleaved", "rope_sliding_only", "logit_scale"):
             assert getattr(back, f) == getattr(cfg, f), (name, f, getattr(back, f), getattr(cfg, f))
         assert abs(back.rope_theta - cfg.rope_theta) < 1e-3 and abs(back.embed_scale - cfg.embed_scale) < 1e-6
