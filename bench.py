@@ -77,24 +77,50 @@ class ClockSampler:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.lines = []  # (host time, csv line) as nvidia-smi prints them
+        self.window = None
 
     def start(self):
+        """Start sampling (before the warm-up, so that nvidia-smi is printing by the time the timed
+        region begins); ``mark`` then restricts the summary to the timed region."""
+        import threading
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+
+        def reader(f):
+            for line in f:
+                self.lines.append((time.perf_counter(), line))
+
+        self.thread = threading.Thread(target=reader, args=(self.proc.stdout,), daemon=True)
+        self.thread.start()
+
+    def mark(self, t0: float, t1: float) -> None:
+        self.window = (t0, t1)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        self.thread.join(timeout=5)
+        lines = self.lines
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [ln for t, ln in lines if t0 <= t <= t1 + 0.25]
+            if not inside:  # a timed region shorter than the sampling period: the samples bracketing it
+                before = [ln for t, ln in lines if t < t0][-1:]
+                after = [ln for t, ln in lines if t > t1][:1]
+                inside = before + after
+            lines = [(0.0, ln) for ln in inside]
+        out = "".join(ln for _, ln in lines)
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
@@ -184,6 +210,8 @@ def main():
             refill()
             eng.step()
             guard += 1
+    clocks = ClockSampler(di.local_rank)
+    clocks.start()  # sampling from the warm-up on; the summary keeps the timed region's samples
     for _ in range(args.warmup):
         refill()
         eng.step()
@@ -191,13 +219,11 @@ def main():
     timer = StepTimer()
     eng.runner.timer = timer
     eng.runner.h2d_bytes = eng.runner.d2h_bytes = 0
-    clocks = ClockSampler(di.local_rank)
     tokens = 0
     token_log = []  # (request_id, time) of tokens produced in the window
     if di.world_size > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
     ops.LAUNCHES.reset()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
@@ -223,6 +249,7 @@ def main():
     launches = ops.LAUNCHES.reset()
     if di.world_size > 1:
         dist.barrier()
+    clocks.mark(t0, time.perf_counter())
     clk = clocks.stop()
     window_ms = ev0.elapsed_time(ev1)
     busy_ms = timer.total_ms()
