@@ -42,6 +42,8 @@ def parse(argv=None):
     p.add_argument("--device", default="cuda")
     p.add_argument("--decode-steps", type=int, default=64)
     p.add_argument("--scale", type=float, default=1.0, help="shrink batch / lengths (small runs)")
+    p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                   help="TP collectives: fused P2P kernels over the IPC heap, or NCCL")
     return p.parse_args(argv)
 
 
@@ -268,7 +270,15 @@ def main(argv=None):
     if cuda:
         torch.cuda.set_device(di.local_rank)
     if di.world_size > 1:
-        comm = NcclComm(di.rank, di.world_size)
+        if args.comm == "fused" and cuda:
+            from gollek_b200.config import preset
+            from gollek_b200.parallel.dist import cpu_group
+            from gollek_b200.parallel.symm import FusedTPComm
+            default = {"llama70b-fp8": "llama-3-70b", "mixtral-ep": "mixtral-8x7b", "gguf-lora": "llama-3-8b"}
+            hidden = preset(args.model or default[args.workload]).hidden_size
+            comm = FusedTPComm(di.rank, di.world_size, max_tokens=8192 + 256, hidden=hidden, cpu_group=cpu_group())
+        else:
+            comm = NcclComm(di.rank, di.world_size)
     {"llama70b-fp8": llama70b_fp8, "mixtral-ep": mixtral_ep, "gguf-lora": gguf_lora}[args.workload](args, di, comm)
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
