@@ -118,6 +118,41 @@ def main():
                                                                    out=out, tensor_cores=tc, emu=emu),
                                iters=args.iters, flush_bytes=flush)
                 rec(f"attn_prefill_{name}_{nseq}x{L}", ms, flops, nbytes)
+    if "lora" in only:
+        # K10 multi-LoRA shrink + expand on fused q/k/v (rank 16 x 3 modules), 64 adapters by Zipf(1.1)
+        from gollek_b200.native import cuda_ext
+        ext = cuda_ext()
+        K, r, S, N1, N2, N = 4096, 16, 64, 4096, 5120, 6144
+        A = (torch.randn(S, 3 * r, K, device=dev) * 0.02).bfloat16()
+        Bw = (torch.randn(S, N, r, device=dev) * 0.02).bfloat16()
+        scales = torch.ones(S, device=dev)
+        zipf = torch.tensor([1.0 / (i + 1) ** 1.1 for i in range(S)])
+        for T, per_seq in ((256, 1), (8192, 512)):
+            n_seq = T // per_seq
+            seq_ad = torch.multinomial(zipf, n_seq, replacement=True, generator=torch.Generator().manual_seed(3))
+            groups = {}
+            for i, a in enumerate(seq_ad.tolist()):
+                groups.setdefault(a, []).extend(range(i * per_seq, (i + 1) * per_seq))
+            seg_slot = sorted(groups)
+            seg_ptr, tok, tiles = [0], [], []
+            for i, sl in enumerate(seg_slot):
+                tiles += [[i, q] for q in range(len(tok), len(tok) + len(groups[sl]), 64)]
+                tok += groups[sl]
+                seg_ptr.append(len(tok))
+            d = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+            sp, tk, ss, tl = d(seg_ptr), d(tok), d(seg_slot), d(tiles)
+            mx = max(len(v) for v in groups.values())
+            x = torch.randn(T, K, device=dev).bfloat16()
+            y = torch.randn(T, N, device=dev).bfloat16()
+            V = torch.zeros(T, 3 * r, device=dev)
+
+            def run():
+                V.zero_()
+                ext.lora_shrink(V, x, A, sp, tk, ss, tl, mx)
+                ext.lora_expand(y, V, Bw, N1, N2, scales, sp, tk, ss, tl)
+            ms = time_cuda(run, iters=args.iters, flush_bytes=flush)
+            nbytes = 2.0 * (T * K + len(seg_slot) * 3 * r * K + 2 * T * N + len(seg_slot) * N * r)
+            rec(f"lora_qkv_T{T}_segs{len(seg_slot)}", ms, 2.0 * T * 3 * r * (K + N // 3), nbytes)
     if "gdn" in only:
         # K14 gated delta rule: decode (one token per sequence, state-bandwidth bound: the fp32 state of
         # every head is read and written) and one long prefill sequence (CUDA-core FMAs)

@@ -500,7 +500,7 @@ void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int6
 }
 
 void lora_shrink_py(torch::Tensor V, torch::Tensor x, torch::Tensor A, torch::Tensor seg_ptr, torch::Tensor tok_idx,
-                    torch::Tensor seg_slot) {
+                    torch::Tensor seg_slot, torch::Tensor tiles, int64_t max_seg) {
   check_cuda(V, "V");
   TORCH_CHECK(V.scalar_type() == at::kFloat && V.stride(1) == 1, "lora: V fp32 [T, R]");
   check_bf16(x, "x");
@@ -510,13 +510,15 @@ void lora_shrink_py(torch::Tensor V, torch::Tensor x, torch::Tensor A, torch::Te
   check_i32(seg_slot, "seg_slot");
   TORCH_CHECK(A.dim() == 3 && A.is_contiguous() && A.size(2) == x.size(1) && x.stride(1) == 1, "lora: A [slots, R, K]");
   TORCH_CHECK(V.size(1) >= A.size(1), "lora: V narrower than R");
+  check_i32(tiles, "tiles");
+  TORCH_CHECK(tiles.is_contiguous() && tiles.dim() == 2 && tiles.size(1) == 2, "lora: tiles [n, 2]");
   launch_lora_shrink(V.data_ptr<float>(), V.stride(0), x.data_ptr(), x.stride(0), A.data_ptr(), A.size(1), A.size(2),
-                     seg_ptr.data_ptr<int>(), tok_idx.data_ptr<int>(), seg_slot.data_ptr<int>(), seg_slot.numel(),
-                     cur_stream());
+                     seg_ptr.data_ptr<int>(), tok_idx.data_ptr<int>(), seg_slot.data_ptr<int>(), tiles.data_ptr<int>(),
+                     tiles.size(0), seg_slot.numel(), (int)max_seg, cur_stream());
 }
 
 void lora_expand_py(torch::Tensor Y, torch::Tensor V, torch::Tensor B, int64_t n1, int64_t n2, torch::Tensor scales,
-                    torch::Tensor seg_ptr, torch::Tensor tok_idx, torch::Tensor seg_slot) {
+                    torch::Tensor seg_ptr, torch::Tensor tok_idx, torch::Tensor seg_slot, torch::Tensor tiles) {
   check_bf16(Y, "Y");
   check_cuda(V, "V");
   check_bf16(B, "B");
@@ -525,7 +527,7 @@ void lora_expand_py(torch::Tensor Y, torch::Tensor V, torch::Tensor B, int64_t n
   TORCH_CHECK(scales.scalar_type() == at::kFloat, "lora: fp32 scales");
   launch_lora_expand(Y.data_ptr(), Y.stride(0), V.data_ptr<float>(), V.size(1), B.data_ptr(), B.size(1), B.size(2),
                      (int)n1, (int)n2, scales.data_ptr<float>(), seg_ptr.data_ptr<int>(), tok_idx.data_ptr<int>(),
-                     seg_slot.data_ptr<int>(), seg_slot.numel(), cur_stream());
+                     seg_slot.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), cur_stream());
 }
 
 void gguf_gemv_py(torch::Tensor y, torch::Tensor x, torch::Tensor W, int64_t qtype, int64_t N, int64_t K, bool swiglu) {

@@ -149,11 +149,14 @@ void launch_gguf_dequant(void* out, const void* W, int qtype, int64_t numel, cud
 void launch_embedding_q8_0(void* out, const int* ids, const void* table, int T, int d, int vocab, cudaStream_t s);
 
 // ---- multi-LoRA (K10)
+// tiles: int32 pairs (segment, first index into tok_idx) of 64-token tiles of the segments
+// V must be zero: K chunks accumulate atomically
 void launch_lora_shrink(float* V, int ldv, const void* x, int64_t ldx, const void* A, int R, int K,
-                        const int* seg_ptr, const int* tok_idx, const int* seg_slot, int num_segs, cudaStream_t s);
+                        const int* seg_ptr, const int* tok_idx, const int* seg_slot, const int* tiles, int num_tiles,
+                        int num_segs, int max_seg, cudaStream_t s);
 void launch_lora_expand(void* Y, int64_t ldy, const float* V, int ldv, const void* B, int N, int rank, int n1,
                         int n2, const float* scales, const int* seg_ptr, const int* tok_idx, const int* seg_slot,
-                        int num_segs, cudaStream_t s);
+                        const int* tiles, int num_tiles, cudaStream_t s);
 
 // ---- symmetric heap + tensor-parallel collectives (csrc/comm/symm.cu)
 void* symm_alloc(size_t bytes);

@@ -27,6 +27,7 @@ from collections import OrderedDict
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
+import numpy as np
 import torch
 
 from ..native import cuda_ext
@@ -172,25 +173,43 @@ class LoRAManager:
     # ------------------------------------------------------------------ per step
     def set_batch(self, token_adapter_ids: List[int]) -> None:
         """Group the step's tokens (in model-input order) by adapter slot; 0 = base model."""
-        ids = set(a for a in token_adapter_ids if a)
+        runs, t = [], 0
+        for a in token_adapter_ids:  # per-token ids as (adapter, start, length) runs
+            if runs and runs[-1][0] == a and runs[-1][1] + runs[-1][2] == t:
+                runs[-1][2] += 1
+            else:
+                runs.append([a, t, 1])
+            t += 1
+        self.set_batch_runs([tuple(r) for r in runs])
+
+    def set_batch_runs(self, runs: List[tuple]) -> None:
+        """Same from (adapter id, first token, token count) runs (one per scheduled chunk): the
+        work is per run, not per token."""
+        ids = set(a for a, _, n in runs if a and n)
         if not ids:
             self._batch = None
             return
         slots = {a: self.acquire(a, ids) for a in ids}
-        groups: Dict[int, List[int]] = {}
-        for t, a in enumerate(token_adapter_ids):
-            if a:
-                groups.setdefault(slots[a], []).append(t)
+        groups: Dict[int, List[tuple]] = {}
+        for a, t0, n in runs:
+            if a and n:
+                groups.setdefault(slots[a], []).append((t0, n))
         seg_slot = sorted(groups)
-        seg_ptr, tok = [0], []
-        for s in seg_slot:
-            tok.extend(groups[s])
-            seg_ptr.append(len(tok))
+        seg_ptr, parts, tiles = [0], [], []
+        total = 0
+        for i, s in enumerate(seg_slot):
+            cnt = sum(n for _, n in groups[s])
+            tiles.extend((i, p) for p in range(total, total + cnt, 64))  # 64-token tiles
+            parts.extend(np.arange(t0, t0 + n, dtype=np.int32) for t0, n in groups[s])
+            total += cnt
+            seg_ptr.append(total)
+        tok = np.concatenate(parts)
         dev = self.device
         self._batch = (torch.tensor(seg_ptr, dtype=torch.int32).to(dev, non_blocking=True),
-                       torch.tensor(tok, dtype=torch.int32).to(dev, non_blocking=True),
+                       torch.from_numpy(tok).to(dev, non_blocking=True),
                        torch.tensor(seg_slot, dtype=torch.int32).to(dev, non_blocking=True),
-                       seg_ptr, tok, seg_slot)
+                       seg_ptr, tok.tolist() if not dev.type == "cuda" else None, seg_slot,
+                       torch.tensor(tiles, dtype=torch.int32).view(-1, 2).to(dev, non_blocking=True))
 
     @property
     def active(self) -> bool:
@@ -200,7 +219,7 @@ class LoRAManager:
         """y += LoRA(x) for the tokens of adapter-using sequences (in place)."""
         if self._batch is None:
             return
-        seg_ptr, tok, seg_slot, seg_ptr_h, tok_h, seg_slot_h = self._batch
+        seg_ptr, tok, seg_slot, seg_ptr_h, tok_h, seg_slot_h, tiles = self._batch
         if mod == "qkv":
             A, B, n1, n2 = self.A_qkv[li], self.B_qkv[li], self.n1, self.n2
         else:
@@ -209,10 +228,11 @@ class LoRAManager:
         if not x.is_cuda:
             self._apply_ref(A, B, n1, n2, x, y, seg_ptr_h, tok_h, seg_slot_h)
             return
-        V = torch.zeros(x.shape[0], R, dtype=torch.float32, device=x.device)
+        max_seg = max(b - a for a, b in zip(seg_ptr_h[:-1], seg_ptr_h[1:]))
+        V = torch.zeros(x.shape[0], R, dtype=torch.float32, device=x.device)  # K chunks accumulate atomically
         ext = cuda_ext()
-        ext.lora_shrink(V, x, A, seg_ptr, tok, seg_slot)
-        ext.lora_expand(y, V, B, n1, n2, self.scales, seg_ptr, tok, seg_slot)
+        ext.lora_shrink(V, x, A, seg_ptr, tok, seg_slot, tiles, max_seg)
+        ext.lora_expand(y, V, B, n1, n2, self.scales, seg_ptr, tok, seg_slot, tiles)
 
     def _apply_ref(self, A, B, n1, n2, x, y, seg_ptr, tok, seg_slot) -> None:
         r = self.r

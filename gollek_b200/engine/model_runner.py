@@ -210,10 +210,11 @@ class ModelRunner:
         dev = self.device
         lora = self.model.lora
         if lora is not None:
-            ids = []
+            runs, t = [], 0
             for c in out.chunks:
-                ids.extend([c.seq.lora_id] * c.num_tokens)
-            lora.set_batch(ids)
+                runs.append((c.seq.lora_id, t, c.num_tokens))
+                t += c.num_tokens
+            lora.set_batch_runs(runs)
         lora_active = lora is not None and lora.active
         all_greedy = self.greedy_only or all(s.params.greedy and not s.params.needs_penalties
                                              and not s.params.needs_host_sampling for s in sample_seqs)

@@ -46,39 +46,47 @@ def test_multi_lora_batch_matches_merged_oracle_cpu(tiny_cfg, tiny_weights):
 
 
 @pytest.mark.gpu
-def test_lora_kernels_match_reference():
+@pytest.mark.parametrize("T,mods", [(37, 3), (300, 3), (300, 1), (12, 3)])
+def test_lora_kernels_match_reference(T, mods):
+    """Shrink (tensor cores) and expand over 64-token tiles of adapter segments, one segment
+    spanning several tiles, fused q/k/v (three rank blocks) or a single module."""
     from gollek_b200.native import cuda_ext
     torch.manual_seed(0)
-    T, K, r = 37, 4096, 16
+    K, r = 4096, 16
     S = 5
-    N1, N2, N = 4096, 5120, 6144
+    N = 6144 if mods == 3 else 4096
+    N1, N2 = (4096, 5120) if mods == 3 else (N, N)
     x = torch.randn(T, K, device="cuda").bfloat16()
-    A = (torch.randn(S, 3 * r, K, device="cuda") * 0.02).bfloat16()
+    A = (torch.randn(S, mods * r, K, device="cuda") * 0.02).bfloat16()
     B = (torch.randn(S, N, r, device="cuda") * 0.02).bfloat16()
     scales = torch.rand(S, device="cuda") + 0.5
     y = torch.randn(T, N, device="cuda").bfloat16()
-    slots = torch.randint(0, S, (T,)).tolist()
+    g = torch.Generator().manual_seed(1)
+    slots = torch.multinomial(torch.tensor([0.1, 0.6, 0.1, 0.1, 0.1]), T, replacement=True, generator=g).tolist()
     groups = {}
     for t, s in enumerate(slots):
         if s:
             groups.setdefault(s, []).append(t)
     seg_slot = sorted(groups)
-    seg_ptr, tok = [0], []
-    for s in seg_slot:
+    seg_ptr, tok, tiles = [0], [], []
+    for i, s in enumerate(seg_slot):
+        tiles += [[i, p] for p in range(len(tok), len(tok) + len(groups[s]), 64)]
         tok += groups[s]
         seg_ptr.append(len(tok))
     d = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
-    V = torch.zeros(T, 3 * r, device="cuda")
+    V = torch.zeros(T, mods * r, device="cuda")
     y2 = y.clone()
     ext = cuda_ext()
-    ext.lora_shrink(V, x, A, d(seg_ptr), d(tok), d(seg_slot))
-    ext.lora_expand(y2, V, B, N1, N2, scales, d(seg_ptr), d(tok), d(seg_slot))
+    ext.lora_shrink(V, x, A, d(seg_ptr), d(tok), d(seg_slot), d(tiles), max(len(v) for v in groups.values()))
+    ext.lora_expand(y2, V, B, N1, N2, scales, d(seg_ptr), d(tok), d(seg_slot), d(tiles))
     ref = y.float().clone()
     for t, s in enumerate(slots):
         if not s:
             continue
         v = x[t].float() @ A[s].float().t()
-        for lo, hi, ro in ((0, N1, 0), (N1, N2, r), (N2, N, 2 * r)):
+        torch.testing.assert_close(V[t], v, rtol=2e-2, atol=2e-3)
+        bounds = ((0, N1, 0), (N1, N2, r), (N2, N, 2 * r)) if mods == 3 else ((0, N, 0),)
+        for lo, hi, ro in bounds:
             ref[t, lo:hi] += scales[s] * (B[s][lo:hi].float() @ v[ro:ro + r])
     torch.testing.assert_close(y2.float(), ref, rtol=2e-2, atol=3e-2)
 
