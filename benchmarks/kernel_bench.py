@@ -169,6 +169,12 @@ def main():
             ms = time_cuda(lambda: ops.gdn_scan(proj, state, slots, reset, qs, a_log, dt, Hg, out=out),
                            iters=args.iters, flush_bytes=flush)
             rec(f"gdn_scan_{nseq}x{L}", ms, 6.0 * T * Hg * D * D, 2.0 * nseq * Hg * D * D * 4 + proj.numel() * 2)
+    if "kvnorm" in only:
+        # K15 KV eviction scoring: mean key norm of 512 blocks of a Llama-3-8B cache (every layer)
+        cache = torch.randn(32, 4096, 2, 8, 16, 128, device=dev).bfloat16()
+        ids = torch.randperm(4096, device=dev)[:512].int()
+        ms = time_cuda(lambda: ops.kv_key_norms(cache, ids), iters=args.iters, flush_bytes=flush)
+        rec("kv_key_norms_512blocks", ms, 0, 2.0 * 32 * 512 * 8 * 16 * 128)
     if "norm" in only:
         d = 4096
         for T in (256, 8192):
