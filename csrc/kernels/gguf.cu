@@ -22,33 +22,37 @@ namespace {
 constexpr int kGemvMaxTok = 16;
 constexpr int kGemvWarps = 8;
 
-GOLLEK_DEVICE void q4k_scale_min(int j, const uint8_t* sc12, float& sc, float& mn) {
-  uint8_t s, m;
-  if (j < 4) {
-    s = sc12[j] & 63;
-    m = sc12[j + 4] & 63;
-  } else {
-    s = (sc12[j + 4] & 0xF) | ((sc12[j - 4] >> 6) << 4);
-    m = (sc12[j + 4] >> 4) | ((sc12[j] >> 6) << 4);
-  }
-  sc = (float)s;
-  mn = (float)m;
-}
-
 GOLLEK_DEVICE float h2f(const uint8_t* p) {
   __half h;
   *reinterpret_cast<uint16_t*>(&h) = *reinterpret_cast<const uint16_t*>(p);
   return __half2float(h);
 }
 
-// Decode the 8 Q4_K weights lane `lane` owns in one 144-byte super-block.
-GOLLEK_DEVICE void q4k_decode8(const uint8_t* blk, int lane, float* w) {
-  const int j = lane >> 2, part = lane & 3;
-  const float d = h2f(blk), dmin = h2f(blk + 2);
-  float sc, mn;
-  q4k_scale_min(j, blk + 4, sc, mn);
-  const float a = d * sc, b = dmin * mn;
-  const uint2 q = *reinterpret_cast<const uint2*>(blk + 16 + 32 * (j >> 1) + part * 8);
+// Decode the 8 Q4_K weights lane `lane` owns in one 144-byte super-block, from the block's 16-byte
+// header (d, dmin, 12 bytes of packed 6-bit scales / mins) and the lane's 8 bytes of nibbles.
+GOLLEK_DEVICE uint32_t q4k_sbyte(const uint4& hdr, int i) {  // byte i of the 12 packed scale bytes
+  const uint32_t w = i < 4 ? hdr.y : (i < 8 ? hdr.z : hdr.w);
+  return (w >> (8 * (i & 3))) & 0xFF;
+}
+
+GOLLEK_DEVICE float half_bits(uint32_t bits) {
+  __half h;
+  *reinterpret_cast<uint16_t*>(&h) = (uint16_t)bits;
+  return __half2float(h);
+}
+
+GOLLEK_DEVICE void q4k_decode8_regs(const uint4 hdr, const uint2 q, int lane, float* w) {
+  const int j = lane >> 2;
+  const float d = half_bits(hdr.x & 0xFFFF), dmin = half_bits(hdr.x >> 16);
+  uint32_t sv, mv;
+  if (j < 4) {
+    sv = q4k_sbyte(hdr, j) & 63;
+    mv = q4k_sbyte(hdr, j + 4) & 63;
+  } else {
+    sv = (q4k_sbyte(hdr, j + 4) & 0xF) | ((q4k_sbyte(hdr, j - 4) >> 6) << 4);
+    mv = (q4k_sbyte(hdr, j + 4) >> 4) | ((q4k_sbyte(hdr, j) >> 6) << 4);
+  }
+  const float a = d * (float)sv, b = dmin * (float)mv;
   const uint32_t qq[2] = {q.x, q.y};
   const int shift = (j & 1) ? 4 : 0;
 #pragma unroll
@@ -56,6 +60,11 @@ GOLLEK_DEVICE void q4k_decode8(const uint8_t* blk, int lane, float* w) {
     const uint32_t byte = (qq[e >> 2] >> (8 * (e & 3))) & 0xFF;
     w[e] = a * (float)((byte >> shift) & 0xF) - b;
   }
+}
+
+GOLLEK_DEVICE void q4k_decode8(const uint8_t* blk, int lane, float* w) {
+  q4k_decode8_regs(*reinterpret_cast<const uint4*>(blk),
+                   *reinterpret_cast<const uint2*>(blk + 16 + 32 * (lane >> 3) + (lane & 3) * 8), lane, w);
 }
 
 template <int NT, bool SWIGLU>
@@ -85,19 +94,37 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16
 #pragma unroll
   for (int m = 0; m < NT; ++m) acc0[m] = acc1[m] = 0.f;
   const int koff = (lane >> 2) * 32 + (lane & 3) * 8;
-  for (int b = 0; b < nblk; ++b) {
-    float wa[8], wb[8];
-    q4k_decode8(w0 + b * 144, lane, wa);
-    q4k_decode8(w1 + b * 144, lane, wb);
+  const int qoff = 16 + 32 * (lane >> 3) + (lane & 3) * 8;  // lane's nibbles inside a block
+  // kBU super-blocks per round: their loads are all issued before any is decoded
+  constexpr int kBU = 4;
+  for (int b0 = 0; b0 < nblk; b0 += kBU) {
+    uint4 h0[kBU], h1[kBU];
+    uint2 q0[kBU], q1[kBU];
 #pragma unroll
-    for (int m = 0; m < NT; ++m) {
-      if (m < M) {
-        float xv[8];
-        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 256 + koff)), xv);
+    for (int u = 0; u < kBU; ++u) {
+      const int b = min(b0 + u, nblk - 1);
+      h0[u] = __ldg(reinterpret_cast<const uint4*>(w0 + b * 144));
+      h1[u] = __ldg(reinterpret_cast<const uint4*>(w1 + b * 144));
+      q0[u] = __ldg(reinterpret_cast<const uint2*>(w0 + b * 144 + qoff));
+      q1[u] = __ldg(reinterpret_cast<const uint2*>(w1 + b * 144 + qoff));
+    }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          acc0[m] = fmaf(wa[e], xv[e], acc0[m]);
-          acc1[m] = fmaf(wb[e], xv[e], acc1[m]);
+    for (int u = 0; u < kBU; ++u) {
+      const int b = b0 + u;
+      if (b >= nblk) break;
+      float wa[8], wb[8];
+      q4k_decode8_regs(h0[u], q0[u], lane, wa);
+      q4k_decode8_regs(h1[u], q1[u], lane, wb);
+#pragma unroll
+      for (int m = 0; m < NT; ++m) {
+        if (m < M) {
+          float xv[8];
+          bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 256 + koff)), xv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            acc0[m] = fmaf(wa[e], xv[e], acc0[m]);
+            acc1[m] = fmaf(wb[e], xv[e], acc1[m]);
+          }
         }
       }
     }

@@ -34,15 +34,17 @@ __constant__ float kNF4[16] = {-1.0f, -0.6961928009986877f, -0.5250730514526367f
                                0.7229568362236023f, 1.0f};
 
 // 32 weights of one row, k0 .. k0+31 (16 packed bytes), all in group k0 / g.
-GOLLEK_DEVICE void dequant32(const uint4 q, float s, float z, bool lut, float* w) {
+// lut_s: the NF4 levels in shared memory (lane-varying indices hit 16 distinct banks, where the
+// constant cache would serialise them)
+GOLLEK_DEVICE void dequant32(const uint4 q, float s, float z, bool lut, const float* lut_s, float* w) {
   const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
   for (int b = 0; b < 16; ++b) {
     const uint32_t byte = (qq[b >> 2] >> (8 * (b & 3))) & 0xFF;
     const int lo = byte & 0xF, hi = byte >> 4;
     if (lut) {
-      w[2 * b] = kNF4[lo] * s;
-      w[2 * b + 1] = kNF4[hi] * s;
+      w[2 * b] = lut_s[lo] * s;
+      w[2 * b + 1] = lut_s[hi] * s;
     } else {
       w[2 * b] = ((float)lo - z) * s;
       w[2 * b + 1] = ((float)hi - z) * s;
@@ -54,26 +56,39 @@ GOLLEK_DEVICE void dequant32(const uint4 q, float s, float z, bool lut, float* w
 template <int MT>
 GOLLEK_DEVICE void row_dot(const uint8_t* __restrict__ qrow, const __nv_bfloat16* __restrict__ srow,
                            const __nv_bfloat16* __restrict__ zrow, const __nv_bfloat16* __restrict__ x,
-                           int64_t ldx, int M, int K, int g, bool lut, int lane, float* acc) {
+                           int64_t ldx, int M, int K, int g, bool lut, const float* lut_s, int lane,
+                           float* acc) {
   const int chunks = K / 32;
-  for (int c = lane; c < chunks; c += 32) {
-    const int k0 = c * 32;
-    const uint4 q = *reinterpret_cast<const uint4*>(qrow + k0 / 2);
-    const int gi = k0 / g;
-    const float s = __bfloat162float(srow[gi]);
-    const float z = lut ? 0.f : __bfloat162float(zrow[gi]);
-    float w[32];
-    dequant32(q, s, z, lut, w);
+  constexpr int kU = 4;  // chunks per lane per round: their loads are issued before any is decoded
+  for (int c0 = lane; c0 < chunks; c0 += 32 * kU) {
+    uint4 qv[kU];
+    float sv[kU], zv[kU];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m < M) {
-        const __nv_bfloat16* xr = x + (int64_t)m * ldx + k0;
-        float xf[8];
+    for (int u = 0; u < kU; ++u) {
+      const int c = min(c0 + 32 * u, chunks - 1);
+      const int gi = (c * 32) / g;
+      qv[u] = __ldg(reinterpret_cast<const uint4*>(qrow + c * 16));
+      sv[u] = __bfloat162float(srow[gi]);
+      zv[u] = lut ? 0.f : __bfloat162float(zrow[gi]);
+    }
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(xr + 8 * v), xf);
+    for (int u = 0; u < kU; ++u) {
+      const int c = c0 + 32 * u;
+      if (c >= chunks) break;
+      const int k0 = c * 32;
+      float w[32];
+      dequant32(qv[u], sv[u], zv[u], lut, lut_s, w);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], w[8 * v + e], acc[m]);
+      for (int m = 0; m < MT; ++m) {
+        if (m < M) {
+          const __nv_bfloat16* xr = x + (int64_t)m * ldx + k0;
+          float xf[8];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(xr + 8 * v)), xf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[m] = fmaf(xf[e], w[8 * v + e], acc[m]);
+          }
         }
       }
     }
@@ -85,6 +100,9 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4_gemv_kernel(
     __nv_bfloat16* __restrict__ out, int64_t ldo, const __nv_bfloat16* __restrict__ x, int64_t ldx,
     const uint8_t* __restrict__ q, const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ zero,
     int M, int N_out, int K, int g, int lut) {
+  __shared__ float lut_s[16];
+  if (threadIdx.x < 16) lut_s[threadIdx.x] = kNF4[threadIdx.x];
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = blockIdx.x * kI4Warps + warp;
   if (col >= N_out) return;
@@ -95,10 +113,10 @@ __global__ void __launch_bounds__(kI4Warps * 32) int4_gemv_kernel(
   // SwiGLU: output column c reads gate row (c/64)*128 + c%64 and the up row 64 further
   const int n = SWIGLU ? (col / 64) * 128 + col % 64 : col;
   row_dot<kI4MaxTok>(q + (int64_t)n * (K / 2), scale + (int64_t)n * ng, zero ? zero + (int64_t)n * ng : nullptr, x, ldx,
-                     M, K, g, lut != 0, lane, acc);
+                     M, K, g, lut != 0, lut_s, lane, acc);
   if (SWIGLU)
     row_dot<kI4MaxTok>(q + (int64_t)(n + 64) * (K / 2), scale + (int64_t)(n + 64) * ng,
-                       zero ? zero + (int64_t)(n + 64) * ng : nullptr, x, ldx, M, K, g, lut != 0, lane, acc2);
+                       zero ? zero + (int64_t)(n + 64) * ng : nullptr, x, ldx, M, K, g, lut != 0, lut_s, lane, acc2);
 #pragma unroll
   for (int m = 0; m < kI4MaxTok; ++m) {
     if (m < M) {
@@ -114,6 +132,9 @@ __global__ void int4_dequant_kernel(__nv_bfloat16* __restrict__ out, const uint8
                                     const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ zero,
                                     int N, int K, int g, int lut) {
   // one thread per 32 weights of a row
+  __shared__ float lut_s[16];
+  if (threadIdx.x < 16) lut_s[threadIdx.x] = kNF4[threadIdx.x];
+  __syncthreads();
   const int chunks = K / 32;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)N * chunks) return;
@@ -123,7 +144,7 @@ __global__ void int4_dequant_kernel(__nv_bfloat16* __restrict__ out, const uint8
   const float s = __bfloat162float(scale[(int64_t)n * ng + gi]);
   const float z = lut ? 0.f : __bfloat162float(zero[(int64_t)n * ng + gi]);
   float w[32];
-  dequant32(qv, s, z, lut != 0, w);
+  dequant32(qv, s, z, lut != 0, lut_s, w);
   uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)n * K + k0);
 #pragma unroll
   for (int v = 0; v < 4; ++v) dst[v] = float_to_bf16x8(w + 8 * v);

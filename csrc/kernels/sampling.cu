@@ -96,7 +96,24 @@ __global__ void __launch_bounds__(kSampThreads) argmax_kernel(int64_t* __restric
   __shared__ ArgMax sh[32];
   const T* row = logits + (int64_t)blockIdx.x * stride;
   ArgMax best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{to_f(row[i]), i});
+  // 16-byte vector loads when the row is aligned (8 bf16 / 4 fp32 per load), two in flight
+  constexpr int kVec = 16 / sizeof(T);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  const int nv = aligned ? V / kVec : 0;
+  for (int v = threadIdx.x; v < nv; v += 2 * blockDim.x) {
+    const int v2 = v + blockDim.x;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(row) + v);
+    const uint4 b = v2 < nv ? __ldg(reinterpret_cast<const uint4*>(row) + v2) : a;
+    const T* ea = reinterpret_cast<const T*>(&a);
+    const T* eb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+    for (int e = 0; e < kVec; ++e) best = better(best, ArgMax{to_f(ea[e]), v * kVec + e});
+    if (v2 < nv) {
+#pragma unroll
+      for (int e = 0; e < kVec; ++e) best = better(best, ArgMax{to_f(eb[e]), v2 * kVec + e});
+    }
+  }
+  for (int i = nv * kVec + threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{to_f(row[i]), i});
   best = block_argmax(best, sh);
   if (threadIdx.x == 0) out[blockIdx.x] = best.i == 0x7fffffff ? 0 : best.i;
 }
@@ -116,19 +133,49 @@ __global__ void penalties_kernel(float* __restrict__ logits, int64_t stride, con
   *p = v;
 }
 
+// Calls f(value, index) for every element of a row: 16-byte vector loads when the row is aligned.
+template <typename T, typename F>
+GOLLEK_DEVICE void for_each_elem(const T* row, int V, F&& f) {
+  constexpr int kVec = 16 / sizeof(T);
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int nv = aligned ? V / kVec : 0;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(row) + v);
+    const T* e = reinterpret_cast<const T*>(&a);
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) f(to_f(e[j]), v * kVec + j);
+  }
+  for (int i = nv * kVec + threadIdx.x; i < V; i += blockDim.x) f(to_f(row[i]), i);
+}
+
+constexpr int kHistCopies = kSampThreads / 32;  // one radix histogram per warp (no atomic contention)
+
+// Sum the per-warp histograms into copy 0.
+template <typename H>
+GOLLEK_DEVICE void hist_reduce(H* hist) {
+  __syncthreads();
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    H t = 0;
+    for (int c = 0; c < kHistCopies; ++c) t += hist[c * 256 + b];
+    hist[b] = t;
+  }
+  __syncthreads();
+}
+
 // Radix select: largest key K such that #{keys >= K} >= k (i.e. the k-th largest key).
 template <typename T>
 GOLLEK_DEVICE uint32_t radix_kth_largest(const T* row, int V, int k, uint32_t* hist, uint32_t* sh_u) {
   uint32_t prefix = 0, mask = 0;
   int remaining = k;
+  uint32_t* mine = hist + (threadIdx.x >> 5) * 256;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    for (int i = threadIdx.x; i < 256 * kHistCopies; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const uint32_t key = ord_key(to_f(row[i]));
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-    }
-    __syncthreads();
+    for_each_elem(row, V, [&](float x, int) {
+      const uint32_t key = ord_key(x);
+      if ((key & mask) == prefix) atomicAdd(&mine[(key >> shift) & 255u], 1u);
+    });
+    hist_reduce(hist);
     if (threadIdx.x == 0) {
       int cum = 0, bin = 0;
       for (bin = 255; bin >= 0; --bin) {
@@ -155,16 +202,15 @@ GOLLEK_DEVICE uint32_t radix_mass_threshold(const T* row, int V, uint32_t floor_
                                             float target, float* hist_f, uint32_t* sh_u, float* sh_f) {
   uint32_t prefix = 0, mask = 0;
   float above = 0.f;
+  float* mine = hist_f + (threadIdx.x >> 5) * 256;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist_f[i] = 0.f;
+    for (int i = threadIdx.x; i < 256 * kHistCopies; i += blockDim.x) hist_f[i] = 0.f;
     __syncthreads();
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float x = to_f(row[i]);
+    for_each_elem(row, V, [&](float x, int) {
       const uint32_t key = ord_key(x);
-      if (key >= floor_key && (key & mask) == prefix)
-        atomicAdd(&hist_f[(key >> shift) & 255u], exp2f((x - m) * inv_t_log2));
-    }
-    __syncthreads();
+      if (key >= floor_key && (key & mask) == prefix) atomicAdd(&mine[(key >> shift) & 255u], exp2f((x - m) * inv_t_log2));
+    });
+    hist_reduce(hist_f);
     if (threadIdx.x == 0) {
       float cum = above;
       int bin;
@@ -195,14 +241,14 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(int64_t* __restric
                                                               const int64_t* __restrict__ offsets) {
   __shared__ ArgMax sha[32];
   __shared__ float shf[33];
-  __shared__ uint32_t hist[256];
+  __shared__ uint32_t hist[256 * kHistCopies];
   __shared__ uint32_t sh_u[2];
   const int b = blockIdx.x;
   const T* row = logits + (int64_t)b * stride;
   const float t = temps[b];
   // 1) max
   ArgMax best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{to_f(row[i]), i});
+  for_each_elem(row, V, [&](float x, int i) { best = better(best, ArgMax{x, i}); });
   best = block_argmax(best, sha);
   if (t <= 0.f) {
     if (threadIdx.x == 0) out[b] = best.i == 0x7fffffff ? 0 : best.i;
@@ -221,10 +267,9 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(int64_t* __restric
   const float tp = top_ps[b];
   if (tp < 1.f) {
     float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float x = to_f(row[i]);
+    for_each_elem(row, V, [&](float x, int) {
       if (ord_key(x) >= floor_key) z += exp2f((x - m) * inv_t_log2);
-    }
+    });
     z = block_sum(z, shf);
     floor_key = max(floor_key, radix_mass_threshold(row, V, floor_key, m, inv_t_log2, tp * z,
                                                     reinterpret_cast<float*>(hist), sh_u, shf));
@@ -232,14 +277,13 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(int64_t* __restric
   // 5) exponential race among survivors: argmax x/t + Gumbel(u)
   const uint32_t seed_mix = hash32((uint32_t)seeds[b] ^ hash32((uint32_t)offsets[b] + 0x9E3779B9u));
   ArgMax pick{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = to_f(row[i]);
-    if (ord_key(x) < floor_key) continue;
+  for_each_elem(row, V, [&](float x, int i) {
+    if (ord_key(x) < floor_key) return;
     const uint32_t h = hash32(seed_mix ^ hash32((uint32_t)i));
     const float u = ((float)(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
     const float g = -__logf(-__logf(u));
     pick = better(pick, ArgMax{(x - m) / t + g, i});
-  }
+  });
   pick = block_argmax(pick, sha);
   if (threadIdx.x == 0) out[b] = pick.i == 0x7fffffff ? best.i : pick.i;
 }
