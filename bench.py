@@ -1,15 +1,17 @@
 """Serving benchmark: output tokens/s of the whole box on Llama-3-8B (bf16, TP = number of GPUs).
 
 Workload (synthetic, random-init weights of the architecture): a saturating request stream
-(arrival rate above the service rate, modelled as all requests queued at t = 0 and the queue
+(arrival rate above the service rate: after a ramp that spreads the sequences' ages, the queue is
 refilled from the same seeded stream), prompts uniform in [128, 2048] tokens with ids uniform
 over the vocabulary, 256 output tokens per request, greedy sampling, EOS ignored, paged KV cache
 with block size 16 in bf16.
 
 One *step* is one ``LLMEngine.step()`` (one continuous-batching iteration: chunked prefill
 plus every running decode, sampling, H2D of the step's inputs from pinned memory and D2H of the
-sampled ids). Before the W warm-up steps the engine is filled (untimed) until its running set
-reaches ``max_num_seqs``; then exactly K steps are timed, bracketed by barrier + synchronize.
+sampled ids). Before the W warm-up steps the engine is ramped (untimed) over ``output_len`` steps
+with max_num_seqs / output_len arrivals per step, which fills the running set with sequences of
+evenly spread ages; then exactly K steps are timed, bracketed by barrier + synchronize, each one
+a steady-state step whatever K is.
 
 Reported:
   value      output tokens of the K steps / device time (sum over steps of the CUDA-event span of
@@ -50,8 +52,10 @@ def parse():
     p.add_argument("--prompt-min", type=int, default=128)
     p.add_argument("--prompt-max", type=int, default=2048)
     p.add_argument("--output-len", type=int, default=256)
-    p.add_argument("--max-num-seqs", type=int, default=256)
-    p.add_argument("--max-batched-tokens", type=int, default=8192)
+    p.add_argument("--max-num-seqs", type=int, default=None,
+                   help="concurrent sequences (default 256 per GPU: per-GPU work fixed as N grows)")
+    p.add_argument("--max-batched-tokens", type=int, default=None,
+                   help="tokens per engine step (default 8192 per GPU)")
     p.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--no-fill", action="store_true")
@@ -171,6 +175,13 @@ def main():
     di = init_distributed(timeout_s=300)
     if di.world_size != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={di.world_size}")
+    # weak scaling by default: concurrency and the per-step token budget grow with the GPU count
+    # (the KV capacity and the compute of the TP group grow with it), so per-GPU work stays fixed
+    weak = args.max_num_seqs is None and args.max_batched_tokens is None
+    if args.max_num_seqs is None:
+        args.max_num_seqs = 256 * di.world_size
+    if args.max_batched_tokens is None:
+        args.max_batched_tokens = 8192 * di.world_size
     torch.cuda.set_device(di.local_rank)
     mcfg = preset(args.model)
     if args.layers:
@@ -198,18 +209,23 @@ def main():
             rid, ids = stream.next()
             eng.add_request(rid, ids, SamplingParams(**vars(sp)))
 
-    for _ in range(args.num_requests):
-        rid, ids = stream.next()
-        eng.add_request(rid, ids, SamplingParams(**vars(sp)))
     if not args.no_graphs:
         eng.runner.capture_all()
-    # fill (untimed): ramp the running set to max_num_seqs
+    # ramp (untimed): requests arrive at max_num_seqs / output_len per step for output_len steps, so
+    # the running sequences' ages are spread evenly; from then on the queue is kept saturated and
+    # each step sees the steady serving mix (decodes of every age plus the chunked prefills of the
+    # requests admitted as others finish) instead of waves of equal-age sequences
     if not args.no_fill:
-        guard = 0
-        while len(eng.scheduler.running) < args.max_num_seqs and guard < 10000:
-            refill()
+        per_step = -(-args.max_num_seqs // args.output_len)
+        for _ in range(args.output_len):
+            for _ in range(per_step):
+                rid, ids = stream.next()
+                eng.add_request(rid, ids, SamplingParams(**vars(sp)))
             eng.step()
-            guard += 1
+    else:
+        for _ in range(args.num_requests):
+            rid, ids = stream.next()
+            eng.add_request(rid, ids, SamplingParams(**vars(sp)))
     clocks = ClockSampler(di.local_rank)
     clocks.start()  # sampling from the warm-up on; the summary keeps the timed region's samples
     for _ in range(args.warmup):
@@ -287,7 +303,7 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": round(busy_ms / steps, 3),
         "higher_is_better": True,
-        "scaling": "strong",
+        "scaling": "weak" if weak else "strong",
         "vs_baseline": round(value / BASELINE_TOK_S, 2),
         "dtype": "bf16",
         "data": "synthetic (random-init weights, uniform random token ids)",
@@ -297,7 +313,8 @@ def main():
             "global_batch": args.max_num_seqs,
             "seq_len": f"prompt U[{args.prompt_min},{args.prompt_max}] + {args.output_len} out",
             "parallelism": f"tp{di.world_size}",
-            "requests": f"saturating stream, first {args.num_requests} queued at t0, refilled",
+            "requests": "staggered ramp (max_num_seqs / output_len arrivals per step), then a saturating "
+                        "refilled queue",
             "max_num_batched_tokens": args.max_batched_tokens,
             "kv_block_size": 16,
             "l2": "inputs larger than L2 (16 GB of weights streamed per step)",
