@@ -60,12 +60,35 @@ struct ArArgs {
   uint64_t timeout_ns;
 };
 
+constexpr int kMaxWorld = 8;
+
+// acc += the 8-element bf16 vector at element offset `off` of buffer `buf_off` of every rank, in
+// rank order; all world loads (NVLink for the peers) are issued before the first add.
+GOLLEK_DEVICE void add_ranks(float* acc, const ArArgs& a, int64_t buf_off, int64_t off) {
+  const int world = a.world;
+  uint4 v[kMaxWorld];
+#pragma unroll
+  for (int p = 0; p < kMaxWorld; ++p)
+    if (p < world)
+      v[p] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + buf_off) + off);
+#pragma unroll
+  for (int p = 0; p < kMaxWorld; ++p) {
+    if (p < world) {
+      float t[8];
+      bf16x8_to_float(v[p], t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += t[e];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __nv_bfloat16* __restrict__ residual,
                                                                     const __nv_bfloat16* __restrict__ w,
                                                                     __nv_bfloat16* __restrict__ x_out) {
   SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
   __shared__ uint32_t s_epoch;
-  __shared__ float red[kArThreads / 32];
+  __shared__ float red[4 * (kArThreads / 32)];
+  __shared__ float red_rows[4];
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
@@ -99,13 +122,7 @@ __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __n
       const int64_t off = (int64_t)row * a.d + v * 8;
       float acc[8];
       bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), acc);
-      for (int p = 0; p < world; ++p) {
-        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
-        float t[8];
-        bf16x8_to_float(*reinterpret_cast<const uint4*>(src + off), t);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += t[e];
-      }
+      add_ranks(acc, a, a.partial_off[a.parity], off);
       *reinterpret_cast<uint4*>(gmine + off) = float_to_bf16x8(acc);
     }
     // ---- barrier B: last local CTA signals every peer
@@ -129,63 +146,84 @@ __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __n
     }
     __syncthreads();
   }
-  // ---- phase 2: gather rows (or reduce all rows, one-shot) + RMSNorm, one row per CTA iteration
+  // ---- phase 2: gather rows (or reduce all rows, one-shot) + RMSNorm; with many rows per CTA, kRows
+  // rows per iteration whose loads are all in flight before the first row's sum of squares is
+  // reduced (one row per iteration otherwise: the most CTAs busy for decode-sized T)
+  constexpr int kRows = 4;
+  const int nr = a.T > kRows * (int)gridDim.x ? kRows : 1;
   const int chunk = (a.T + world - 1) / world;
-  for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
-    const int64_t base = (int64_t)row * a.d;
-    float ss = 0.f;
-    // each thread owns up to 2 vectors of the row (d <= 8192)
-    float vals[2][8];
+  for (int row0 = blockIdx.x * nr; row0 < a.T; row0 += gridDim.x * nr) {
+    // each thread owns up to 2 vectors of each row (d <= 8192)
+    float vals[kRows][2][8];
+    float ss[kRows];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int v = threadIdx.x + k * kArThreads;
-      if (v < nvec) {
-        const int64_t off = base + v * 8;
-        if (a.one_shot) {
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), vals[k]);
-          for (int p = 0; p < world; ++p) {
-            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
-            float t[8];
-            bf16x8_to_float(*reinterpret_cast<const uint4*>(src + off), t);
+    for (int j = 0; j < kRows; ++j) {
+      ss[j] = 0.f;
+      const int row = j < nr ? row0 + j : a.T;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) vals[k][e] += t[e];
+      for (int k = 0; k < 2; ++k) {
+        const int v = threadIdx.x + k * kArThreads;
+        if (row < a.T && v < nvec) {
+          const int64_t off = (int64_t)row * a.d + v * 8;
+          if (a.one_shot) {
+            bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), vals[j][k]);
+            add_ranks(vals[j][k], a, a.partial_off[a.parity], off);
+          } else {
+            const int owner = min(row / chunk, world - 1);
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[owner] + a.gather_off);
+            bf16x8_to_float(*reinterpret_cast<const uint4*>(src + off), vals[j][k]);
           }
-          uint4 packed = float_to_bf16x8(vals[k]);
-          bf16x8_to_float(packed, vals[k]);
-          *reinterpret_cast<uint4*>(residual + off) = packed;
-        } else {
-          const int owner = min(row / chunk, world - 1);
-          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[owner] + a.gather_off);
-          const uint4 u = *reinterpret_cast<const uint4*>(src + off);
-          *reinterpret_cast<uint4*>(residual + off) = u;
-          bf16x8_to_float(u, vals[k]);
         }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss += vals[k][e] * vals[k][e];
       }
     }
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      const int row = j < nr ? row0 + j : a.T;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int v = threadIdx.x + k * kArThreads;
+        if (row < a.T && v < nvec) {
+          const int64_t off = (int64_t)row * a.d + v * 8;
+          uint4 packed = float_to_bf16x8(vals[j][k]);
+          if (a.one_shot) bf16x8_to_float(packed, vals[j][k]);  // normalise the rounded residual
+          *reinterpret_cast<uint4*>(residual + off) = packed;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss[j] += vals[j][k][e] * vals[j][k][e];
+        }
+      }
+      ss[j] = warp_sum(ss[j]);
+    }
+    if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+      for (int j = 0; j < kRows; ++j) red[j * (kArThreads / 32) + (threadIdx.x >> 5)] = ss[j];
+    }
     __syncthreads();
     if (threadIdx.x < 32) {
-      float t = threadIdx.x < kArThreads / 32 ? red[threadIdx.x] : 0.f;
-      t = warp_sum(t);
-      if (threadIdx.x == 0) red[0] = t;
-    }
-    __syncthreads();
-    const float rs = rsqrtf(red[0] / (float)a.d + a.eps);
-    __syncthreads();
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int v = threadIdx.x + k * kArThreads;
-      if (v < nvec) {
-        float wf[8];
-        bf16x8_to_float(*reinterpret_cast<const uint4*>(w + v * 8), wf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vals[k][e] = vals[k][e] * rs * wf[e];
-        *reinterpret_cast<uint4*>(x_out + base + v * 8) = float_to_bf16x8(vals[k]);
+      for (int j = 0; j < kRows; ++j) {
+        float t = threadIdx.x < kArThreads / 32 ? red[j * (kArThreads / 32) + threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red_rows[j] = t;
       }
     }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      const int row = j < nr ? row0 + j : a.T;
+      const float rs = rsqrtf(red_rows[j] / (float)a.d + a.eps);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int v = threadIdx.x + k * kArThreads;
+        if (row < a.T && v < nvec) {
+          float wf[8];
+          bf16x8_to_float(*reinterpret_cast<const uint4*>(w + v * 8), wf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vals[j][k][e] = vals[j][k][e] * rs * wf[e];
+          *reinterpret_cast<uint4*>(x_out + (int64_t)row * a.d + v * 8) = float_to_bf16x8(vals[j][k]);
+        }
+      }
+    }
+    __syncthreads();
   }
   // ---- epilogue: the call is complete on this rank once every CTA got here; CTA 0 records it
   if (a.one_shot) {
@@ -244,11 +282,18 @@ __global__ void __launch_bounds__(kArThreads) tp_push_ar_rmsnorm_kernel(PushArgs
       if (v < nvec) {
         const int64_t off = base + v * 8;
         bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), vals[k]);
-        for (int p = 0; p < a.world; ++p) {
-          float t[8];
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(inbox + (int64_t)p * a.slot_elems + off), t);
+        uint4 in[kMaxWorld];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) vals[k][e] += t[e];
+        for (int p = 0; p < kMaxWorld; ++p)
+          if (p < a.world) in[p] = *reinterpret_cast<const uint4*>(inbox + (int64_t)p * a.slot_elems + off);
+#pragma unroll
+        for (int p = 0; p < kMaxWorld; ++p) {
+          if (p < a.world) {
+            float t[8];
+            bf16x8_to_float(in[p], t);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) vals[k][e] += t[e];
+          }
         }
         const uint4 packed = float_to_bf16x8(vals[k]);
         bf16x8_to_float(packed, vals[k]);
@@ -387,13 +432,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(ArArgs a, __nv
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec_total;
        i += (int64_t)gridDim.x * blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int p = 0; p < a.world; ++p) {
-      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + a.partial_off[a.parity]);
-      float t[8];
-      bf16x8_to_float(*reinterpret_cast<const uint4*>(src + i * 8), t);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += t[e];
-    }
+    add_ranks(acc, a, a.partial_off[a.parity], i * 8);
     *reinterpret_cast<uint4*>(out + i * 8) = float_to_bf16x8(acc);
   }
   __syncthreads();
