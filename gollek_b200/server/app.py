@@ -227,7 +227,10 @@ OPENAI_DEFAULTS = dict(temperature=0.7, top_p=0.95, top_k=50, max_tokens=2048, r
 
 
 def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
-               rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0) -> FastAPI:
+               rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
+               engine_builder=None, drain_timeout_s: float = 30.0) -> FastAPI:
+    """``engine_builder(model) -> LLMEngine`` builds the engine of a hot-swap (default: the running
+    engine's configuration with ``model`` replaced)."""
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
     gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
     app = FastAPI(title="gollek-b200", version="0.1")
@@ -700,6 +703,44 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             raise HTTPException(404, "unknown key")
         del st.api_keys[key]
         return {"revoked": True}
+
+    # -------------------------------------------------------------- model hot-swap
+    from .hotswap import HotSwapManager, default_memory_check
+
+    def _default_builder(model: str):
+        import dataclasses
+        from ..engine.engine import LLMEngine
+        return LLMEngine(dataclasses.replace(st.engine.cfg, model=model))
+
+    swapper = HotSwapManager(st, engine_builder or _default_builder, drain_timeout_s,
+                             memory_check=default_memory_check if engine_builder is None else None)
+    app.state.hotswap = swapper
+
+    @app.post("/v1/admin/models/swap")
+    async def admin_swap(body: Dict[str, Any]):
+        model = (body or {}).get("model")
+        if not model:
+            raise HTTPException(400, "body needs a model (preset name or checkpoint path)")
+        try:
+            sw = swapper.begin(str(model), body.get("name"))
+        except MemoryError as e:
+            return error_response("DEVICE_OUT_OF_MEMORY", f"hot-swap refused: {e}")
+        except RuntimeError as e:
+            raise HTTPException(409, str(e))
+        return JSONResponse(sw.as_dict(), status_code=202)
+
+    @app.get("/v1/admin/models/swap")
+    async def admin_swap_list():
+        act = swapper.active
+        return {"active": act.as_dict() if act is not None and not act.done else None,
+                "swaps": [s.as_dict() for s in swapper.swaps.values()]}
+
+    @app.get("/v1/admin/models/swap/{swap_id}")
+    async def admin_swap_get(swap_id: str):
+        sw = swapper.swaps.get(swap_id)
+        if sw is None:
+            raise HTTPException(404, f"unknown swap {swap_id}")
+        return sw.as_dict()
 
     @app.get("/v1/admin/errors")
     async def admin_error_codes():
