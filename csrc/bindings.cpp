@@ -243,8 +243,20 @@ void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::opt
 void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, torch::Tensor w_gu,
                      torch::Tensor w_down, torch::Tensor ws, torch::Tensor ids, torch::Tensor wts, torch::Tensor dest,
                      torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, c10::optional<torch::Tensor> ypart,
-                     int64_t topk, bool renorm, int64_t e0, int64_t e_loc) {
+                     int64_t topk, bool renorm, int64_t e0, int64_t e_loc, int64_t scoring,
+                     c10::optional<torch::Tensor> score_bias, int64_t n_group, int64_t topk_group, double scale) {
   for (auto* t : {&out, &x, &router, &w_gu, &w_down, &xp, &hp, &yp}) check_bf16(*t, "moe operand");
+  MoeRouting rt;
+  rt.scoring = (int)scoring;
+  rt.n_group = (int)n_group;
+  rt.topk_group = (int)topk_group;
+  rt.scale = (float)scale;
+  if (score_bias.has_value()) {
+    TORCH_CHECK(score_bias->is_cuda() && score_bias->scalar_type() == at::kFloat && score_bias->is_contiguous() &&
+                    score_bias->numel() == router.size(0),
+                "moe: score correction bias must be fp32 [E] on the device");
+    rt.bias = score_bias->data_ptr<float>();
+  }
   check_same_device(x, w_gu);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "moe: x/out row-major [T, H]");
   const int T = x.size(0), H = x.size(1), E = router.size(0);
@@ -276,7 +288,7 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
   launch_moe_forward(out.data_ptr(), out.stride(0), x.data_ptr(), x.stride(0), router.data_ptr(), w_gu.data_ptr(),
                      w_down.data_ptr(), ws.data_ptr<int>(), ids.data_ptr<int>(), wts.data_ptr<float>(),
                      dest.data_ptr<int>(), xp.data_ptr(), hp.data_ptr(), yp.data_ptr(), yq, T, H, F, E, (int)topk,
-                     renorm ? 1 : 0, (int)e0, (int)e_loc, nullptr, cur_stream());
+                     renorm ? 1 : 0, (int)e0, (int)e_loc, rt, nullptr, cur_stream());
 }
 
 std::vector<int64_t> moe_plan_py(int64_t T, int64_t topk, int64_t E, int64_t e_loc, int64_t H, int64_t F) {
@@ -640,7 +652,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
   m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
   m.def("num_sms", &device_num_sms);
-  m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)");
+  m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)",
+        py::arg("out"), py::arg("x"), py::arg("router"), py::arg("w_gu"), py::arg("w_down"), py::arg("ws"),
+        py::arg("ids"), py::arg("wts"), py::arg("dest"), py::arg("xp"), py::arg("hp"), py::arg("yp"),
+        py::arg("ypart"), py::arg("topk"), py::arg("renorm"), py::arg("e0"), py::arg("e_loc"),
+        py::arg("scoring") = 0, py::arg("score_bias") = py::none(), py::arg("n_group") = 1,
+        py::arg("topk_group") = 1, py::arg("scale") = 1.0);
   m.def("moe_capacity_rows", &moe_capacity_rows);
   m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
   m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");

@@ -97,10 +97,20 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
 int moe_capacity_rows(int T, int topk, int e_loc);
 int moe_ws_ints(int T, int topk, int e_loc);
 void moe_plan_host(int T, int topk, int E, int e_loc, int H, int F, int& bn_gu, int& bn_dn, int& splits);
+// Router options: scoring 0 = softmax (Mixtral), 1 = sigmoid with the per-expert fp32 correction
+// ``bias`` added for the choice only, top-k limited to the topk_group best of n_group groups,
+// weights times ``scale`` (DeepSeek-V3).
+struct MoeRouting {
+  int scoring = 0;
+  const float* bias = nullptr;
+  int n_group = 1;
+  int topk_group = 1;
+  float scale = 1.f;
+};
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
                         float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,
-                        uint32_t* status, cudaStream_t s);
+                        const MoeRouting& rt, uint32_t* status, cudaStream_t s);
 
 // ---- KV block transfer (P/D disaggregation): packed [L, n, span] <-> cache [L, NB, span]
 // K14 gated delta rule: proj [T, ldp] = q | k | v | g | a | b per token (Hg heads of D = 128);

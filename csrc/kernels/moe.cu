@@ -1,8 +1,12 @@
 // K12: MoE routing and token permutation, plus the expert combine (sm_100a).
 //
-//   moe_route    one warp per token: router logits x·Wrᵀ (fp32 accumulate, E ≤ 64), softmax,
-//                top-k (k ≤ 8, ties to the lower expert id), optional renormalisation of the k
-//                weights (Mixtral), per-local-expert token counts (atomics).
+//   moe_route    router logits x·Wrᵀ (fp32 accumulate, E ≤ 256), then one warp per token scores
+//                and picks its top-k (k ≤ 8, ties to the lower expert id): softmax scores with
+//                optional renormalisation of the k weights (Mixtral), or sigmoid scores whose
+//                choice adds a per-expert correction bias, limited to the topk_group best of n_group
+//                expert groups (group score = sum of its two best choice scores), weights = the
+//                chosen sigmoid scores renormalised and times a scale (DeepSeek-V3); per-local-expert
+//                token counts (atomics).
 //   moe_plan     one thread: per-expert row offsets in the permuted buffer, each expert's rows
 //                padded to the 128-row GEMM tile, the M-tile → expert map for the grouped GEMM
 //                and the live M-tile count; re-zeroes the counters for the next call.
@@ -18,6 +22,8 @@
 //
 // Reference behaviour: Mixtral routing in runner/safetensor/…/generation/moe/MoeForwardPass.java:39-128
 // and the EP dispatch contract of core/optimization/gollek-plugin-elastic-ep/…/binding/ElasticEpBinding.java:19-45.
+// The DeepSeek-V3 router (sigmoid, correction bias, group limit, routed scaling) follows the
+// checkpoint's published routing rule; the reference serves those models through llama.cpp.
 #include "../common/common.cuh"
 #include "../common/tma_host.h"
 #include "launchers.h"
@@ -28,8 +34,9 @@ using namespace gollek;
 
 namespace {
 
-constexpr int kMaxE = 64;
+constexpr int kMaxE = 256;
 constexpr int kMaxK = 8;
+constexpr int kPerLane = kMaxE / 32;  // expert e = lane + 32 i is scored by lane (e & 31)
 
 constexpr int kRouteTok = 4;  // tokens per routing CTA
 
@@ -39,8 +46,9 @@ constexpr int kRouteTok = 4;  // tokens per routing CTA
 // a shared-memory reduction gives the logits, then warp w < 4 does softmax / top-k for token w.
 __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                         const __nv_bfloat16* __restrict__ wr, int T, int H, int E,
-                                                        int topk, int renorm, int e0, int e_loc, int* __restrict__ ids,
-                                                        float* __restrict__ wts, int* __restrict__ counts) {
+                                                        int topk, int renorm, int e0, int e_loc, MoeRouting rt,
+                                                        int* __restrict__ ids, float* __restrict__ wts,
+                                                        int* __restrict__ counts) {
   __shared__ float s_part[8][kRouteTok * 8];
   __shared__ float s_logit[kRouteTok][kMaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -93,46 +101,117 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
   }
   if (warp >= ntok) return;
   const int t = t0 + warp;
-  // softmax over E (lane i owns experts i and i + 32)
-  float v0 = lane < E ? s_logit[warp][lane] : -INFINITY;
-  float v1 = lane + 32 < E ? s_logit[warp][lane + 32] : -INFINITY;
-  const float m = warp_max(fmaxf(v0, v1));
-  float p0 = lane < E ? __expf(v0 - m) : 0.f;
-  float p1 = lane + 32 < E ? __expf(v1 - m) : 0.f;
-  const float inv = 1.f / warp_sum(p0 + p1);
-  p0 *= inv;
-  p1 *= inv;
+  float* lg = s_logit[warp];
+  // p: the weight score of each owned expert; c: its choice score (-inf: absent or already taken)
+  float p[kPerLane], c[kPerLane];
+  if (rt.scoring == 0) {  // softmax over E
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) m = fmaxf(m, lane + 32 * i < E ? lg[lane + 32 * i] : -INFINITY);
+    m = warp_max(m);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      p[i] = lane + 32 * i < E ? __expf(lg[lane + 32 * i] - m) : 0.f;
+      sum += p[i];
+    }
+    const float inv = 1.f / warp_sum(sum);
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      p[i] *= inv;
+      c[i] = lane + 32 * i < E ? p[i] : -INFINITY;
+    }
+  } else {  // sigmoid; the choice adds the correction bias
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      const int e = lane + 32 * i;
+      p[i] = e < E ? 1.f / (1.f + __expf(-lg[e])) : 0.f;
+      c[i] = e < E ? p[i] + (rt.bias ? rt.bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  if (rt.n_group > 1) {
+    // group score = sum of the two best choice scores of the group; keep the topk_group best groups
+    // (ties to the lower group) and score every expert outside them 0
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i)
+      if (lane + 32 * i < E) lg[lane + 32 * i] = c[i];
+    __syncwarp();
+    const int gs = E / rt.n_group;
+    float gscore = -INFINITY;
+    if (lane < rt.n_group) {
+      float b1 = -INFINITY, b2 = -INFINITY;
+      for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+        const float v = lg[e];
+        if (v > b1) {
+          b2 = b1;
+          b1 = v;
+        } else if (v > b2) {
+          b2 = v;
+        }
+      }
+      gscore = b1 + b2;
+    }
+    uint32_t keep = 0;
+    for (int j = 0; j < rt.topk_group; ++j) {
+      float bv = gscore;
+      int bi = lane < rt.n_group ? lane : 1 << 30;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (bi < 32) keep |= 1u << bi;
+      if (bi == lane) gscore = -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((keep >> (e / gs)) & 1u)) c[i] = 0.f;
+    }
+  }
   int sel_id[kMaxK];
   float sel_p[kMaxK];
   float psum = 0.f;
 #pragma unroll
   for (int j = 0; j < kMaxK; ++j) {
     if (j >= topk) break;
-    // lane-local best of its two candidates (-1 marks taken / absent)
-    float bv = p0;
-    int bi = lane < E ? lane : 1 << 30;
-    if (lane + 32 < E && (p1 > bv || bi == (1 << 30))) {
-      bv = p1;
-      bi = lane + 32;
+    // lane-local best (lowest id on ties: the scan runs in increasing id), then the warp's best
+    float bv = -INFINITY, bp = 0.f;
+    int bi = 1 << 30;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      if (lane + 32 * i < E && c[i] > bv) {
+        bv = c[i];
+        bp = p[i];
+        bi = lane + 32 * i;
+      }
     }
-    if (bi == (1 << 30)) bv = -1.f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const float op = __shfl_xor_sync(0xffffffffu, bp, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > bv || (ov == bv && oi < bi)) {
         bv = ov;
+        bp = op;
         bi = oi;
       }
     }
     sel_id[j] = bi;
-    sel_p[j] = bv;
-    psum += bv;
-    if (bi == lane) p0 = -1.f;        // mark taken
-    if (bi == lane + 32) p1 = -1.f;
+    sel_p[j] = bp;
+    psum += bp;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i)
+      if (bi == lane + 32 * i) c[i] = -INFINITY;  // taken
   }
   if (lane == 0) {
-    const float scale = renorm ? 1.f / psum : 1.f;
+    float scale = rt.scale;
+    if (renorm) scale /= psum + (rt.scoring == 0 ? 0.f : 1e-20f);
     for (int j = 0; j < topk; ++j) {
       ids[(int64_t)t * topk + j] = sel_id[j];
       wts[(int64_t)t * topk + j] = sel_p[j] * scale;
@@ -143,7 +222,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
 }
 
 // ws layout (int32), fixed whatever e_loc is, so calls with different expert ranges can share it:
-//   counts[64] | cursor[64] | offsets[65] | num_m[1] | tile_group[max_tiles]
+//   counts[256] | cursor[256] | offsets[257] | num_m[1] | tile_group[max_tiles]
 // counts[0, e_loc) are zero between calls (route increments them, plan reads and re-zeroes them);
 // plan zeroes cursor[0, e_loc) before gather claims rows with it.
 constexpr int kWsCursor = kMaxE, kWsOffsets = 2 * kMaxE, kWsNumM = 3 * kMaxE + 1, kWsTiles = 3 * kMaxE + 2;
@@ -261,8 +340,12 @@ void moe_plan_host(int T, int topk, int E, int e_loc, int H, int F, int& bn_gu, 
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
                         float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,
-                        uint32_t* status, cudaStream_t s) {
-  throw_if(E > kMaxE || E < 1, "moe: at most 64 experts");
+                        const MoeRouting& rt, uint32_t* status, cudaStream_t s) {
+  throw_if(E > kMaxE || E < 1, "moe: at most 256 experts");
+  throw_if(rt.scoring != 0 && rt.scoring != 1, "moe: scoring is 0 (softmax) or 1 (sigmoid)");
+  throw_if(rt.n_group < 1 || rt.n_group > 32 || E % rt.n_group != 0 || (rt.n_group > 1 && E / rt.n_group < 2) ||
+               rt.topk_group < 1 || rt.topk_group > rt.n_group,
+           "moe: n_group must divide E (at most 32 groups of >= 2 experts), 1 <= topk_group <= n_group");
   throw_if(topk < 1 || topk > kMaxK || topk > E, "moe: top-k must be in [1, min(8, E)]");
   throw_if(H % 256 != 0, "moe: hidden size must be a multiple of 256");
   throw_if(F % 64 != 0, "moe: expert FFN width must be a multiple of 64");
@@ -273,7 +356,7 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   const int cap = moe_capacity_rows(T, topk, e_loc);
   auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
   moe_route_kernel<<<(T + kRouteTok - 1) / kRouteTok, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
-                                               renorm, e0, e_loc, ids, wts, ws);
+                                               renorm, e0, e_loc, rt, ids, wts, ws);
   check_launch("moe_route");
   moe_plan_kernel<<<1, 32, 0, s>>>(ws, e_loc, cap / 128);
   check_launch("moe_plan");

@@ -25,8 +25,10 @@ from typing import Any, Optional
 
 @dataclass
 class RopeScaling:
-    """RoPE frequency scaling (HF ``rope_scaling``): ``none``, ``linear``, ``llama3`` or
-    ``longrope`` (Phi-3 long-context: per-pair short/long factors)."""
+    """RoPE frequency scaling (HF ``rope_scaling``): ``none``, ``linear``, ``llama3``,
+    ``longrope`` (Phi-3 long-context: per-pair short/long factors) or ``yarn`` (DeepSeek-V3:
+    NTK-by-parts interpolation between ``beta_fast`` and ``beta_slow`` rotations, cos/sin scaled
+    by mscale(factor, mscale) / mscale(factor, mscale_all_dim))."""
     kind: str = "none"
     factor: float = 1.0
     low_freq_factor: float = 1.0
@@ -34,6 +36,10 @@ class RopeScaling:
     original_max_position_embeddings: int = 8192
     short_factor: Optional[list] = None
     long_factor: Optional[list] = None
+    beta_fast: float = 32.0
+    beta_slow: float = 1.0
+    mscale: float = 0.0
+    mscale_all_dim: float = 0.0
 
     @staticmethod
     def from_hf(d: Optional[dict]) -> "RopeScaling":
@@ -52,13 +58,26 @@ class RopeScaling:
             original_max_position_embeddings=int(d.get("original_max_position_embeddings", 8192) or 8192),
             short_factor=d.get("short_factor"),
             long_factor=d.get("long_factor"),
+            beta_fast=float(d.get("beta_fast") or 32.0),
+            beta_slow=float(d.get("beta_slow") or 1.0),
+            mscale=float(d.get("mscale") or 0.0),
+            mscale_all_dim=float(d.get("mscale_all_dim") or 0.0),
         )
+
+
+def yarn_mscale(scale: float, m: float = 1.0) -> float:
+    """YaRN attention-temperature factor 0.1 * m * ln(scale) + 1 (1 for scale <= 1)."""
+    import math
+    return 1.0 if scale <= 1 else 0.1 * m * math.log(scale) + 1.0
 
 
 # Model families handled by the decoder graph (models/llama.py). Llama-like families differ in
 # projection biases, QK-norm, sliding windows, norm placement and activation; Gemma adds a
 # sqrt(hidden) embedding scale, (1 + w) RMSNorm weights, GeGLU, sandwich norms and softcapping.
-FAMILIES = ("llama", "mistral", "mixtral", "qwen2", "qwen3", "gemma", "gemma2", "gemma3", "phi3", "cohere2")
+# DeepSeek-V3 (also DeepSeek-R1 and Kimi-K2) adds multi-head latent attention and group-limited
+# sigmoid-routed MoE with shared experts.
+FAMILIES = ("llama", "mistral", "mixtral", "qwen2", "qwen3", "gemma", "gemma2", "gemma3", "phi3", "cohere2",
+            "deepseek_v3")
 
 
 @dataclass
@@ -105,6 +124,23 @@ class ModelConfig:
     # layers (G = Gated DeltaNet layer, A = softmax attention); None = attention only
     hybrid_schedule: Optional[str] = None
     gdn_num_heads: int = 0               # GDN heads (0: num_attention_heads); head dim 128
+    # multi-head latent attention (DeepSeek-V3): q = W_qb norm(W_qa x) (or W_q x without q_lora_rank),
+    # [c | k_rope] = W_kva x, [k_nope | v] = W_kvb norm(c) per head; RoPE on the qk_rope_head_dim dims
+    # (k_rope shared by all heads); head_dim = qk_nope_head_dim + qk_rope_head_dim
+    q_lora_rank: int = 0
+    kv_lora_rank: int = 0                # > 0 selects MLA
+    qk_nope_head_dim: int = 0
+    qk_rope_head_dim: int = 0
+    v_head_dim: int = 0
+    # MoE variants: expert width, shared experts, router scoring and group limit, dense first layers
+    moe_intermediate_size: int = 0       # 0: intermediate_size
+    n_shared_experts: int = 0
+    moe_scoring: str = "softmax"         # "softmax" (Mixtral) | "sigmoid" (DeepSeek-V3, bias-corrected choice)
+    n_group: int = 1                     # experts are chosen inside the topk_group best of n_group groups
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+    norm_topk_prob: bool = True
+    first_k_dense_replace: int = 0       # layers [0, k) use a dense MLP of intermediate_size
     bos_token_id: int = 1
     eos_token_id: int = 2
 
@@ -113,8 +149,28 @@ class ModelConfig:
         return self.num_local_experts > 0
 
     @property
+    def is_mla(self) -> bool:
+        return self.kv_lora_rank > 0
+
+    @property
+    def rope_dim(self) -> int:
+        """Rotary dims per head (the qk_rope_head_dim part under MLA)."""
+        return self.qk_rope_head_dim if self.is_mla else self.head_dim
+
+    @property
+    def moe_ffn(self) -> int:
+        return self.moe_intermediate_size or self.intermediate_size
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.is_moe and i >= self.first_k_dense_replace
+
+    @property
     def attn_scale(self) -> float:
-        return (self.query_pre_attn_scalar or self.head_dim) ** -0.5
+        s = (self.query_pre_attn_scalar or self.head_dim) ** -0.5
+        rs = self.rope_scaling
+        if self.is_mla and rs.kind == "yarn" and rs.mscale_all_dim:
+            s *= yarn_mscale(rs.factor, rs.mscale_all_dim) ** 2
+        return s
 
     def layer_window(self, i: int) -> int:
         """Sliding window of layer ``i`` (0 = full attention)."""
@@ -154,22 +210,34 @@ class ModelConfig:
     def kv_size(self) -> int:
         return self.num_key_value_heads * self.head_dim
 
+    def _attn_params(self) -> int:
+        h = self.hidden_size
+        if not self.is_mla:
+            return h * (self.q_size + 2 * self.kv_size) + self.q_size * h
+        nh, qk = self.num_attention_heads, self.head_dim
+        q = (h * self.q_lora_rank + self.q_lora_rank * nh * qk) if self.q_lora_rank else h * nh * qk
+        kv = h * (self.kv_lora_rank + self.qk_rope_head_dim) + self.kv_lora_rank * nh * (
+            self.qk_nope_head_dim + self.v_head_dim)
+        return q + kv + nh * self.v_head_dim * h
+
+    def _ffn_params(self, i: int, active: bool) -> int:
+        h = self.hidden_size
+        if not self.is_moe_layer(i):
+            return 3 * h * self.intermediate_size
+        n = self.num_experts_per_tok if active else self.num_local_experts
+        return 3 * h * self.moe_ffn * (n + self.n_shared_experts) + h * self.num_local_experts
+
     def num_params(self) -> int:
-        h, f, v = self.hidden_size, self.intermediate_size, self.vocab_size
-        attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
-        ffn = 3 * h * f * max(1, self.num_local_experts)
-        if self.is_moe:
-            ffn += h * self.num_local_experts
-        per_layer = attn + ffn + 2 * h
+        h, v = self.hidden_size, self.vocab_size
+        body = sum(self._attn_params() + self._ffn_params(i, False) + 2 * h for i in range(self.num_hidden_layers))
         emb = v * h * (1 if self.tie_word_embeddings else 2)
-        return self.num_hidden_layers * per_layer + emb + h
+        return body + emb + h
 
     def flops_per_token(self) -> float:
         """Dense matmul FLOPs per token (2 per MAC), ignoring attention scores."""
-        h, f = self.hidden_size, self.intermediate_size
-        attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
-        ffn = 3 * h * f * (self.num_experts_per_tok if self.is_moe else 1)
-        return 2.0 * (self.num_hidden_layers * (attn + ffn) + h * self.vocab_size)
+        h = self.hidden_size
+        body = sum(self._attn_params() + self._ffn_params(i, True) for i in range(self.num_hidden_layers))
+        return 2.0 * (body + h * self.vocab_size)
 
     @staticmethod
     def from_hf(d: dict) -> "ModelConfig":
@@ -181,7 +249,10 @@ class ModelConfig:
         mt = str(d.get("model_type", "llama"))
         fam = {"llama": "llama", "mistral": "mistral", "mixtral": "mixtral", "qwen2": "qwen2", "qwen3": "qwen3",
                "gemma": "gemma", "gemma2": "gemma2", "gemma3_text": "gemma3", "gemma3": "gemma3",
-               "phi3": "phi3", "cohere2": "cohere2", "yi": "llama"}.get(mt)
+               "phi3": "phi3", "cohere2": "cohere2", "yi": "llama", "deepseek_v3": "deepseek_v3",
+               "kimi_k2": "deepseek_v3"}.get(mt)
+        if fam is None and any("DeepseekV3" in a for a in archs):
+            fam = "deepseek_v3"
         if fam is None:
             fam = "mixtral" if any("Mixtral" in a for a in archs) else "llama"
         gemma = fam.startswith("gemma")
@@ -222,6 +293,18 @@ class ModelConfig:
             pat = int(d.get("sliding_window_pattern", 4) or 4)
             layer_types = ["sliding_attention" if (i + 1) % pat else "full_attention" for i in range(nl)]
         cohere = fam == "cohere2"
+        ds = fam == "deepseek_v3"
+        mla = {}
+        if ds:
+            mla = dict(q_lora_rank=int(d.get("q_lora_rank") or 0), kv_lora_rank=int(d.get("kv_lora_rank") or 512),
+                       qk_nope_head_dim=int(d.get("qk_nope_head_dim", 128)),
+                       qk_rope_head_dim=int(d.get("qk_rope_head_dim", 64)), v_head_dim=int(d.get("v_head_dim", 128)),
+                       moe_intermediate_size=int(d.get("moe_intermediate_size", 0) or 0),
+                       n_shared_experts=int(d.get("n_shared_experts", 0) or 0), moe_scoring="sigmoid",
+                       n_group=int(d.get("n_group", 1) or 1), topk_group=int(d.get("topk_group", 1) or 1),
+                       routed_scaling_factor=float(d.get("routed_scaling_factor", 1.0) or 1.0),
+                       norm_topk_prob=bool(d.get("norm_topk_prob", True)),
+                       first_k_dense_replace=int(d.get("first_k_dense_replace", 0) or 0))
         act = str(d.get("hidden_activation") or d.get("hidden_act") or "silu")
         act = "gelu_tanh" if (gemma or act.startswith("gelu")) else "silu"
         return ModelConfig(
@@ -232,13 +315,13 @@ class ModelConfig:
             num_hidden_layers=nl,
             num_attention_heads=nh,
             num_key_value_heads=int(d.get("num_key_value_heads", nh) or nh),
-            head_dim=int(d.get("head_dim") or hs // nh),
+            head_dim=(mla["qk_nope_head_dim"] + mla["qk_rope_head_dim"]) if ds else int(d.get("head_dim") or hs // nh),
             rms_norm_eps=float(d.get("layer_norm_eps", 1e-5) if cohere else d.get("rms_norm_eps", 1e-6 if gemma else 1e-5)),
             rope_theta=float(theta),
             rope_scaling=RopeScaling.from_hf(scaling),
             max_position_embeddings=int(d.get("max_position_embeddings", 8192)),
             tie_word_embeddings=bool(d.get("tie_word_embeddings", gemma or cohere)),
-            num_local_experts=int(d.get("num_local_experts", 0) or 0),
+            num_local_experts=int(d.get("n_routed_experts" if ds else "num_local_experts", 0) or 0),
             num_experts_per_tok=int(d.get("num_experts_per_tok", 0) or 0),
             attention_bias=True if fam == "qwen2" else bool(d.get("attention_bias", False)),
             qk_norm=fam in ("qwen3", "gemma3"),
@@ -254,11 +337,12 @@ class ModelConfig:
             sandwich_norm=fam in ("gemma2", "gemma3"),
             norm_center=cohere,
             parallel_block=cohere,
-            rope_interleaved=cohere,
+            rope_interleaved=cohere or (ds and bool(d.get("rope_interleave", True))),
             rope_sliding_only=cohere,
             logit_scale=float(d.get("logit_scale", 1.0) or 1.0) if cohere else 1.0,
             bos_token_id=int(d.get("bos_token_id", 1) or 1),
             eos_token_id=int(eos if eos is not None else 2),
+            **mla,
         )
 
     def to_hf(self) -> dict:
@@ -267,7 +351,8 @@ class ModelConfig:
                  "mixtral": ("MixtralForCausalLM", "mixtral"), "qwen2": ("Qwen2ForCausalLM", "qwen2"),
                  "qwen3": ("Qwen3ForCausalLM", "qwen3"), "gemma": ("GemmaForCausalLM", "gemma"),
                  "gemma2": ("Gemma2ForCausalLM", "gemma2"), "gemma3": ("Gemma3ForCausalLM", "gemma3_text"),
-                 "phi3": ("Phi3ForCausalLM", "phi3"), "cohere2": ("Cohere2ForCausalLM", "cohere2")}
+                 "phi3": ("Phi3ForCausalLM", "phi3"), "cohere2": ("Cohere2ForCausalLM", "cohere2"),
+                 "deepseek_v3": ("DeepseekV3ForCausalLM", "deepseek_v3")}
         arch, mt = names.get(fam, names["mixtral" if self.is_moe else "llama"])
         d = {
             "architectures": [arch],
@@ -320,6 +405,11 @@ class ModelConfig:
                                  "low_freq_factor": rs.low_freq_factor,
                                  "high_freq_factor": rs.high_freq_factor,
                                  "original_max_position_embeddings": rs.original_max_position_embeddings}
+            if rs.kind == "yarn":
+                d["rope_scaling"] = {"rope_type": "yarn", "factor": rs.factor, "beta_fast": rs.beta_fast,
+                                     "beta_slow": rs.beta_slow, "mscale": rs.mscale,
+                                     "mscale_all_dim": rs.mscale_all_dim,
+                                     "original_max_position_embeddings": rs.original_max_position_embeddings}
             if rs.kind == "longrope":
                 d["rope_scaling"] = {"type": "longrope", "short_factor": rs.short_factor,
                                      "long_factor": rs.long_factor}
@@ -327,6 +417,16 @@ class ModelConfig:
         if self.is_moe:
             d["num_local_experts"] = self.num_local_experts
             d["num_experts_per_tok"] = self.num_experts_per_tok
+        if fam == "deepseek_v3":
+            d.pop("head_dim")
+            d.pop("num_local_experts", None)
+            d.update(q_lora_rank=self.q_lora_rank or None, kv_lora_rank=self.kv_lora_rank,
+                     qk_nope_head_dim=self.qk_nope_head_dim, qk_rope_head_dim=self.qk_rope_head_dim,
+                     v_head_dim=self.v_head_dim, n_routed_experts=self.num_local_experts,
+                     moe_intermediate_size=self.moe_ffn, n_shared_experts=self.n_shared_experts,
+                     n_group=self.n_group, topk_group=self.topk_group,
+                     routed_scaling_factor=self.routed_scaling_factor, norm_topk_prob=self.norm_topk_prob,
+                     first_k_dense_replace=self.first_k_dense_replace, rope_interleave=self.rope_interleaved)
         return d
 
 
@@ -350,6 +450,13 @@ PRESETS: dict[str, ModelConfig] = {
         architecture="mixtral", vocab_size=1024, hidden_size=256, intermediate_size=512,
         num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2, head_dim=32,
         rope_theta=10000.0, num_local_experts=8, num_experts_per_tok=2, max_position_embeddings=2048),
+    "tiny-deepseek-v3": ModelConfig(
+        architecture="deepseek_v3", vocab_size=1024, hidden_size=256, intermediate_size=512,
+        num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=4, head_dim=96, rms_norm_eps=1e-6,
+        rope_theta=10000.0, max_position_embeddings=2048, q_lora_rank=128, kv_lora_rank=64,
+        qk_nope_head_dim=64, qk_rope_head_dim=32, v_head_dim=64, rope_interleaved=True,
+        num_local_experts=16, num_experts_per_tok=4, moe_intermediate_size=128, n_shared_experts=1,
+        moe_scoring="sigmoid", n_group=4, topk_group=2, routed_scaling_factor=2.5, first_k_dense_replace=1),
     "llama-3-8b": ModelConfig(
         architecture="llama", vocab_size=128256, hidden_size=4096, intermediate_size=14336,
         num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
@@ -421,6 +528,16 @@ PRESETS: dict[str, ModelConfig] = {
         num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
         rms_norm_eps=1e-5, rope_theta=1000000.0, num_local_experts=8, num_experts_per_tok=2,
         max_position_embeddings=32768),
+    "deepseek-v3": ModelConfig(
+        architecture="deepseek_v3", vocab_size=129280, hidden_size=7168, intermediate_size=18432,
+        num_hidden_layers=61, num_attention_heads=128, num_key_value_heads=128, head_dim=192, rms_norm_eps=1e-6,
+        rope_theta=10000.0, max_position_embeddings=163840,
+        rope_scaling=RopeScaling(kind="yarn", factor=40.0, original_max_position_embeddings=4096, beta_fast=32.0,
+                                 beta_slow=1.0, mscale=1.0, mscale_all_dim=1.0),
+        q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+        rope_interleaved=True, num_local_experts=256, num_experts_per_tok=8, moe_intermediate_size=2048,
+        n_shared_experts=1, moe_scoring="sigmoid", n_group=8, topk_group=4, routed_scaling_factor=2.5,
+        first_k_dense_replace=3, bos_token_id=0, eos_token_id=1),
 }
 
 

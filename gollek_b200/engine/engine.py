@@ -97,6 +97,8 @@ class LLMEngine:
         if cfg.scheduling_policy == "wait":
             predictor = host_ext().LengthPredictor(64, 1.0, float(cfg.max_model_len), 0.05, 8)
         self.scheduler = Scheduler(cfg, self.kv, predictor)
+        if self.model.cfg.is_mla and cfg.enable_lora:
+            raise ValueError("LoRA adapters on multi-head latent attention models are not supported")
         self.lora_manager = None
         if cfg.enable_lora:
             from .lora import LoRAManager

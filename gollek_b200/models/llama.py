@@ -32,6 +32,8 @@ from .reference import layer_tensors, rope_cos_sin
 
 # head sizes the attention kernels are built for; other sizes are stored zero-padded to the next one
 _KERNEL_HEAD_DIMS = (32, 64, 128, 256)
+# per-layer dense linear weights (quantized by ``quantize_fp8`` / ``quantize_int4``)
+_DENSE_KEYS = ("w_qkv", "w_o", "w_gate_up", "w_down", "w_qa_kva", "w_q", "w_q_b", "w_kv_b", "w_sh_gu", "w_sh_down")
 
 
 @dataclass
@@ -174,6 +176,8 @@ class LlamaModel:
         self.D = next((d for d in _KERNEL_HEAD_DIMS if d >= cfg.head_dim), cfg.head_dim)
         if self.D != cfg.head_dim and cfg.qk_norm:
             raise ValueError(f"head_dim {cfg.head_dim} with QK-norm is not supported")
+        if cfg.is_mla and (cfg.v_head_dim > self.D or cfg.head_dim > self.D):
+            raise ValueError("MLA head dims above 256 are not supported")
         f_shard = cfg.intermediate_size // tp
         if cfg.intermediate_size % tp:
             raise ValueError("intermediate_size must be divisible by the TP size")
@@ -190,13 +194,18 @@ class LlamaModel:
         self.E_loc, self.e0, self.moe_F = 0, 0, self.F
         if cfg.is_moe:
             E = cfg.num_local_experts
+            if cfg.moe_ffn % tp:
+                raise ValueError("the expert FFN width must be divisible by the TP size")
             if self.expert_parallel:
                 if E % tp:
                     raise ValueError("num_local_experts must be divisible by the expert-parallel size")
-                self.E_loc, self.e0, self.moe_F = E // tp, r * (E // tp), cfg.intermediate_size
+                self.E_loc, self.e0, self.moe_F = E // tp, r * (E // tp), cfg.moe_ffn
             else:
-                self.E_loc, self.e0, self.moe_F = E, 0, f_shard
+                self.E_loc, self.e0, self.moe_F = E, 0, cfg.moe_ffn // tp
         self.moe_F_pad = (self.moe_F + ops.SWIGLU_GROUP - 1) // ops.SWIGLU_GROUP * ops.SWIGLU_GROUP
+        # shared experts (DeepSeek-V3): one dense SwiGLU of n_shared * expert width, sharded like the MLP
+        self.sh_F = cfg.n_shared_experts * cfg.moe_ffn // tp if cfg.is_moe else 0
+        self.sh_F_pad = (self.sh_F + ops.SWIGLU_GROUP - 1) // ops.SWIGLU_GROUP * ops.SWIGLU_GROUP
         self.scale = cfg.attn_scale
         n_pos = max(cfg.max_position_embeddings, 8192)
         self.cos_sin = rope_cos_sin(cfg, n_pos, device=self.device)
@@ -283,16 +292,26 @@ class LlamaModel:
                 return (x.float() + 1.0).to(dt).contiguous()
             return x.contiguous()
 
-        def ffn(L, c, p):
-            if cfg.is_moe:
-                pe = p + "block_sparse_moe."
+        def ffn(L, c, p, i):
+            if cfg.is_moe_layer(i):
+                ds = cfg.moe_scoring == "sigmoid"  # DeepSeek-V3 names (mlp.*), else Mixtral's
+                pe = p + ("mlp." if ds else "block_sparse_moe.")
+                names = ("gate_proj", "up_proj", "down_proj") if ds else ("w1", "w3", "w2")
                 L["router"] = t(pe + "gate.weight").contiguous()
+                if ds:
+                    L["router_bias"] = get(pe + "gate.e_score_correction_bias").to(dev, torch.float32).contiguous()
+                    if cfg.n_shared_experts:
+                        s0, s1 = r * self.sh_F, (r + 1) * self.sh_F
+                        ps = pe + "shared_experts."
+                        L["w_sh_gu"] = gate_up(t(ps + "gate_proj.weight")[s0:s1], t(ps + "up_proj.weight")[s0:s1],
+                                               self.sh_F_pad).contiguous()
+                        L["w_sh_down"] = down(t(ps + "down_proj.weight")[:, s0:s1], self.sh_F_pad).contiguous()
                 experts = []
-                f0, f1 = (0, self.moe_F) if self.expert_parallel else (r * self.F, (r + 1) * self.F)
+                f0, f1 = (0, self.moe_F) if self.expert_parallel else (r * self.moe_F, (r + 1) * self.moe_F)
                 for e in range(self.e0, self.e0 + self.E_loc):
-                    g = t(pe + f"experts.{e}.w1.weight")[f0:f1]
-                    u = t(pe + f"experts.{e}.w3.weight")[f0:f1]
-                    d = t(pe + f"experts.{e}.w2.weight")[:, f0:f1]
+                    g = t(pe + f"experts.{e}.{names[0]}.weight")[f0:f1]
+                    u = t(pe + f"experts.{e}.{names[1]}.weight")[f0:f1]
+                    d = t(pe + f"experts.{e}.{names[2]}.weight")[:, f0:f1]
                     experts.append((gate_up(g, u, self.moe_F_pad).contiguous(),
                                     down(d, self.moe_F_pad).contiguous()))
                 if all(isinstance(a, torch.Tensor) for a, _ in experts):
@@ -319,9 +338,9 @@ class LlamaModel:
         for i in range(cfg.num_hidden_layers):
             p = f"model.layers.{i}."
             c = layer_tensors(t, cfg, i)
-            if c.get("gdn"):
-                L = self._gdn_weights(c, norm_w)
-                ffn(L, c, p)
+            if c.get("gdn") or cfg.is_mla:
+                L = self._gdn_weights(c, norm_w) if c.get("gdn") else self._mla_weights(c, norm_w)
+                ffn(L, c, p, i)
                 self.layers.append(L)
                 continue
             kv0, kv1 = self.kv_head0 * Dl, (self.kv_head0 + Hk) * Dl
@@ -346,7 +365,7 @@ class LlamaModel:
                 L["q_norm"], L["k_norm"] = norm_w(c["q_norm"]), norm_w(c["k_norm"])
             if cfg.sandwich_norm:
                 L["pre_ff_norm"], L["post_ff_norm"] = norm_w(c["pre_ff_norm"]), norm_w(c["post_ff_norm"])
-            ffn(L, c, p)
+            ffn(L, c, p, i)
             self.layers.append(L)
 
     def _gdn_weights(self, c: dict, norm_w) -> Dict[str, torch.Tensor]:
@@ -360,6 +379,55 @@ class LlamaModel:
                 "w_gdn_in": _pad_rows(w_in, rows).contiguous(), "w_o": c["o"][:, sl].contiguous(),
                 "A_log": c["A_log"][hs].float().contiguous(), "dt_bias": c["dt_bias"][hs].float().contiguous(),
                 "gdn_norm": c["gnorm"].contiguous()}
+
+    def _mla_weights(self, c: dict, norm_w) -> Dict[str, torch.Tensor]:
+        """Multi-head latent attention, decompressed into this rank's heads of the paged cache.
+
+        Each head of q and k is laid out [rope (qk_rope) | nope (qk_nope) | 0] and padded to the
+        kernel head size D, each v head [v | 0], so the fused RoPE + KV-write kernel rotates the
+        first qk_rope dims (its partial-rotary mode) and the attention kernels run unchanged.
+        Interleaved rope pairs are de-interleaved in the weight rows (NeoX rotation then gives
+        the same scores). The latent projection ``w_qa_kva`` = [q_a ; kv_a] runs once per token
+        (replicated over ranks); ``w_kv_b`` takes [norm(c) | k_rope] and carries k_rope into
+        every key head through an identity block, so one GEMM writes the whole k and v of the
+        rank's heads."""
+        cfg, r, H, D = self.cfg, self.comm.rank, self.H, self.D
+        nope, rd, vd, kvl = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        for k in ("q_a", "q_b", "q", "kv_a", "kv_b", "o"):
+            if k in c and not isinstance(c[k], torch.Tensor):
+                raise ValueError("MLA layers need bf16 / fp16 / fp32 checkpoint weights")
+
+        def deint(x):  # rows (2i, 2i+1) -> (i, rd/2 + i) along dim -2
+            return torch.cat([x[..., 0::2, :], x[..., 1::2, :]], -2) if cfg.rope_interleaved else x
+
+        def q_heads(wq):  # [nh * (nope + rd), K] -> [H * D, K]: this rank's heads, [rope | nope | 0]
+            K = wq.shape[1]
+            w = wq.view(-1, nope + rd, K)[r * H:(r + 1) * H]
+            out = torch.zeros(H, D, K, dtype=wq.dtype, device=wq.device)
+            out[:, :rd] = deint(w[:, nope:])
+            out[:, rd:rd + nope] = w[:, :nope]
+            return out.view(H * D, K)
+
+        kv_a = c["kv_a"]
+        kv_a = torch.cat([kv_a[:kvl], deint(kv_a[kvl:])], 0)
+        kvb = c["kv_b"].view(-1, nope + vd, kvl)[r * H:(r + 1) * H]
+        wk = torch.zeros(H, D, kvl + rd, dtype=kvb.dtype, device=kvb.device)
+        wk[:, :rd, kvl:] = torch.eye(rd, dtype=kvb.dtype, device=kvb.device)
+        wk[:, rd:rd + nope, :kvl] = kvb[:, :nope]
+        wv = torch.zeros(H, D, kvl + rd, dtype=kvb.dtype, device=kvb.device)
+        wv[:, :vd, :kvl] = kvb[:, nope:]
+        L = {"mla": True, "in_norm": norm_w(c["in_norm"]), "post_norm": norm_w(c["post_norm"]),
+             "kv_a_norm": c["kv_a_norm"].contiguous(),
+             "w_kv_b": torch.cat([wk.view(H * D, -1), wv.view(H * D, -1)], 0).contiguous(),
+             "w_o": _pad_heads(c["o"][:, r * H * vd:(r + 1) * H * vd], H, vd, D, dim=1).contiguous()}
+        if cfg.q_lora_rank:
+            L["w_qa_kva"] = torch.cat([c["q_a"], kv_a], 0).contiguous()
+            L["q_a_norm"] = c["q_a_norm"].contiguous()
+            L["w_q_b"] = q_heads(c["q_b"]).contiguous()
+        else:
+            L["w_qa_kva"] = kv_a.contiguous()
+            L["w_q"] = q_heads(c["q"]).contiguous()
+        return L
 
     def init_random(self, seed: int = 0, std: float = 0.02, fp8: bool = False) -> None:
         """Random-init this rank's shard directly on the device (benchmarks; no checkpoint)."""
@@ -381,7 +449,16 @@ class LlamaModel:
         self.lm_head = rnd(self.V_local, h)
         self.layers = []
         for li in range(cfg.num_hidden_layers):
-            if cfg.is_gdn_layer(li):
+            if cfg.is_mla:
+                H, D, kvl, rd = self.H, self.D, cfg.kv_lora_rank, cfg.qk_rope_head_dim
+                L = {"mla": True, "in_norm": ones(h), "post_norm": ones(h), "kv_a_norm": ones(kvl),
+                     "w_qa_kva": rnd(cfg.q_lora_rank + kvl + rd, h), "w_kv_b": rnd(2 * H * D, kvl + rd),
+                     "w_o": rnd(h, H * D)}
+                if cfg.q_lora_rank:
+                    L["q_a_norm"], L["w_q_b"] = ones(cfg.q_lora_rank), rnd(H * D, cfg.q_lora_rank)
+                else:
+                    L["w_q"] = rnd(H * D, h)
+            elif cfg.is_gdn_layer(li):
                 hd = self.Hg * 128
                 rows = (4 * hd + 2 * self.Hg + 127) // 128 * 128
                 L = {"gdn": True, "in_norm": ones(h), "post_norm": ones(h), "w_gdn_in": rnd(rows, h),
@@ -400,8 +477,12 @@ class LlamaModel:
                 L["q_norm"], L["k_norm"] = ones(D), ones(D)
             if cfg.sandwich_norm:
                 L["pre_ff_norm"], L["post_ff_norm"] = ones(h), ones(h)
-            if cfg.is_moe:
+            if cfg.is_moe_layer(li):
                 L["router"] = rnd(cfg.num_local_experts, h)
+                if cfg.moe_scoring == "sigmoid":
+                    L["router_bias"] = torch.zeros(cfg.num_local_experts, dtype=torch.float32, device=dev)
+                if self.sh_F:
+                    L["w_sh_gu"], L["w_sh_down"] = rnd(2 * self.sh_F_pad, h), rnd(h, self.sh_F_pad)
                 fp = self.moe_F_pad
                 if fp8:
                     L["experts"] = [(rnd(2 * fp, h), rnd(h, fp)) for _ in range(self.E_loc)]
@@ -413,8 +494,8 @@ class LlamaModel:
                 L["w_down"] = rnd(h, self.F_pad)
             if fp8:  # quantise this layer now so bf16 copies of all layers never coexist
                 from ..quant.fp8 import quantize_weight
-                for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
-                    if k in L:
+                for k in _DENSE_KEYS:
+                    if k in L and L[k].shape[1] % 128 == 0:
                         L[k] = quantize_weight(L[k])
                 if "experts" in L:
                     L["experts"] = [(quantize_weight(a), quantize_weight(b)) for a, b in L["experts"]]
@@ -426,7 +507,7 @@ class LlamaModel:
         blocks. Per-row quantization, so the fused/interleaved row layouts are unaffected."""
         from ..quant.int4 import quantize_nf4, quantize_rtn
         for L in self.layers:
-            for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+            for k in _DENSE_KEYS:
                 v = L.get(k)
                 if isinstance(v, torch.Tensor):
                     K = v.shape[1]
@@ -442,8 +523,8 @@ class LlamaModel:
         layer so the bf16 copies are released as it goes. Embedding, norms and lm_head stay bf16."""
         from ..quant.fp8 import quantize_weight
         for L in self.layers:
-            for k in ("w_qkv", "w_o", "w_gate_up", "w_down"):
-                if k in L and isinstance(L[k], torch.Tensor):
+            for k in _DENSE_KEYS:  # weights whose K is not a multiple of 128 stay bf16
+                if k in L and isinstance(L[k], torch.Tensor) and L[k].shape[1] % 128 == 0:
                     L[k] = quantize_weight(L[k])
             if "moe_gu" in L:
                 fp, h = self.moe_F_pad, self.cfg.hidden_size
@@ -515,14 +596,26 @@ class LlamaModel:
             self.lora.apply(li, lora_kind, a, h)
         return h
 
-    def _moe(self, x: torch.Tensor, L: dict, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """This rank's share of the MoE FFN (its local experts, or its FFN shard of every expert)."""
+    def _route(self, L: dict) -> dict:
         cfg = self.cfg
+        if cfg.moe_scoring == "softmax":
+            return {}
+        return dict(scoring=cfg.moe_scoring, bias=L.get("router_bias"), n_group=cfg.n_group,
+                    topk_group=cfg.topk_group, scale=cfg.routed_scaling_factor)
+
+    def _moe(self, x: torch.Tensor, L: dict, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """This rank's share of the MoE FFN (its local experts, or its FFN shard of every expert),
+        plus its shard of the shared experts when the family has them."""
+        cfg = self.cfg
+        if "w_sh_gu" in L:  # routed experts into a temporary, the shared expert's GEMM adds them
+            hm = self._moe(x, {k: v for k, v in L.items() if k not in ("w_sh_gu", "w_sh_down")})
+            return ops.linear(ops.linear_swiglu(x, L["w_sh_gu"]), L["w_sh_down"], residual=hm, out=out)
+        renorm = cfg.norm_topk_prob
         if "moe_gu" in L:  # dense experts: route + permute + grouped tcgen05 GEMMs + combine
             return ops.fused_moe(x, L["router"], L["moe_gu"], L["moe_down"], cfg.num_experts_per_tok,
-                                 self.e0, self.E_loc, out=out)
+                                 self.e0, self.E_loc, renorm=renorm, out=out, **self._route(L))
         # quantized experts (GGUF / FP8): one expert at a time
-        topi, topw = ops.moe_route_ref(x, L["router"], cfg.num_experts_per_tok)
+        topi, topw = ops.moe_route_ref(x, L["router"], cfg.num_experts_per_tok, renorm, **self._route(L))
         topw = topw.to(x.device)
         topi = topi.to(x.device)
         acc = torch.zeros(x.shape[0], cfg.hidden_size, dtype=torch.float32, device=x.device)
@@ -557,6 +650,24 @@ class LlamaModel:
                          meta.gdn_query_start, L["A_log"], L["dt_bias"], self.Hg)
         return ops.gdn_gated_norm(o, proj[:, 3 * hd:4 * hd], L["gdn_norm"], self.cfg.rms_norm_eps)
 
+    def _mla(self, x: torch.Tensor, L: Dict[str, torch.Tensor], meta: AttnMetadata, cache) -> torch.Tensor:
+        """Multi-head latent attention of this rank's heads: latent GEMM, latent norms, q and kv
+        up-projections written side by side into one [q | k | v] row, then the partial-rotary
+        RoPE + paged KV write and the attention kernels (see ``_mla_weights`` for the layout)."""
+        cfg, H, D, T = self.cfg, self.H, self.D, x.shape[0]
+        eps, ql, kvl = cfg.rms_norm_eps, cfg.q_lora_rank, cfg.kv_lora_rank
+        lat = ops.linear(x, L["w_qa_kva"])  # [T, q_lora + kv_lora + rope]
+        ckv = lat[:, ql:]
+        ops.rms_norm(ckv[:, :kvl], L["kv_a_norm"], eps, out=ckv[:, :kvl])  # in place: [norm(c) | k_rope]
+        qkv = torch.empty(T, 3 * H * D, dtype=x.dtype, device=x.device)
+        if ql:
+            ops.linear(ops.rms_norm(lat[:, :ql], L["q_a_norm"], eps), L["w_q_b"], out=qkv[:, :H * D])
+        else:
+            ops.linear(x, L["w_q"], out=qkv[:, :H * D])
+        ops.linear(ckv, L["w_kv_b"], out=qkv[:, H * D:])
+        q = ops.rope_kv_write(qkv, meta.positions, self.cos_sin, cache, meta.slot_mapping, H, H, D)
+        return self._attention(q, cache, meta, 0)
+
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
                 hidden_only: bool = False, greedy: bool = False) -> torch.Tensor:
         """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP), or with
@@ -581,6 +692,9 @@ class LlamaModel:
                 tracing.nvtx_push("attn")
             if L.get("gdn"):
                 a = self._gdn(x, L, meta, li)
+            elif L.get("mla"):
+                cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
+                a = self._mla(x, L, meta, cache).view(T, self.H * self.D)
             else:
                 qkv = ops.linear(x, L["w_qkv"])
                 if self.lora is not None:
@@ -619,8 +733,8 @@ class LlamaModel:
                 x = self._add_norm(h, residual, L["post_norm"])
             if nv:
                 tracing.nvtx_pop()
-                tracing.nvtx_push("moe" if cfg.is_moe else "ffn")
-            if cfg.is_moe:
+                tracing.nvtx_push("moe" if cfg.is_moe_layer(li) else "ffn")
+            if cfg.is_moe_layer(li):
                 h = self._moe(x, L, out=self.comm.partial_buffer(T))
             else:
                 h = self._row_linear(ops.linear_swiglu(x, L["w_gate_up"], act=cfg.hidden_act), L["w_down"], li)

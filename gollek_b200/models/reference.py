@@ -62,6 +62,19 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
             w[pl + "dt_bias"] = rnd(cfg.gdn_heads, s=0.5).to(torch.float32)
             w[pl + "norm.weight"] = torch.ones(cfg.gdn_head_dim, dtype=dtype, device=device)
             w[pl + "o_proj.weight"] = rnd(h, hd)
+        elif cfg.is_mla:
+            nh, qk = cfg.num_attention_heads, cfg.head_dim
+            pa = p + "self_attn."
+            if cfg.q_lora_rank:
+                w[pa + "q_a_proj.weight"] = rnd(cfg.q_lora_rank, h)
+                w[pa + "q_a_layernorm.weight"] = torch.ones(cfg.q_lora_rank, dtype=dtype, device=device)
+                w[pa + "q_b_proj.weight"] = rnd(nh * qk, cfg.q_lora_rank, s=0.1)
+            else:
+                w[pa + "q_proj.weight"] = rnd(nh * qk, h)
+            w[pa + "kv_a_proj_with_mqa.weight"] = rnd(cfg.kv_lora_rank + cfg.qk_rope_head_dim, h)
+            w[pa + "kv_a_layernorm.weight"] = torch.ones(cfg.kv_lora_rank, dtype=dtype, device=device)
+            w[pa + "kv_b_proj.weight"] = rnd(nh * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank, s=0.1)
+            w[pa + "o_proj.weight"] = rnd(h, nh * cfg.v_head_dim)
         elif fam == "phi3":
             w[p + "self_attn.qkv_proj.weight"] = rnd(q + 2 * kv, h)
         else:
@@ -75,14 +88,28 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
         if cfg.qk_norm and not cfg.is_gdn_layer(i):
             w[p + "self_attn.q_norm.weight"] = norm(D)
             w[p + "self_attn.k_norm.weight"] = norm(D)
-        if not cfg.is_gdn_layer(i):
+        if not cfg.is_gdn_layer(i) and not cfg.is_mla:
             w[p + "self_attn.o_proj.weight"] = rnd(h, q)
         if not cfg.parallel_block:
             w[p + "post_attention_layernorm.weight"] = norm(h)
         if cfg.sandwich_norm:
             w[p + "pre_feedforward_layernorm.weight"] = norm(h)
             w[p + "post_feedforward_layernorm.weight"] = norm(h)
-        if cfg.is_moe:
+        if cfg.is_moe_layer(i) and cfg.moe_scoring == "sigmoid":  # DeepSeek-V3 MoE
+            pm, fe = p + "mlp.", cfg.moe_ffn
+            w[pm + "gate.weight"] = rnd(cfg.num_local_experts, h, s=0.1)
+            w[pm + "gate.e_score_correction_bias"] = rnd(cfg.num_local_experts, s=0.05).float()
+            for e in range(cfg.num_local_experts):
+                pe = pm + f"experts.{e}."
+                w[pe + "gate_proj.weight"] = rnd(fe, h)
+                w[pe + "up_proj.weight"] = rnd(fe, h)
+                w[pe + "down_proj.weight"] = rnd(h, fe)
+            if cfg.n_shared_experts:
+                fs = fe * cfg.n_shared_experts
+                w[pm + "shared_experts.gate_proj.weight"] = rnd(fs, h)
+                w[pm + "shared_experts.up_proj.weight"] = rnd(fs, h)
+                w[pm + "shared_experts.down_proj.weight"] = rnd(h, fs)
+        elif cfg.is_moe_layer(i):
             w[p + "block_sparse_moe.gate.weight"] = rnd(cfg.num_local_experts, h)
             for e in range(cfg.num_local_experts):
                 pe = p + f"block_sparse_moe.experts.{e}."
@@ -102,10 +129,12 @@ def init_random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02,
     return w
 
 
-def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
+def layer_tensors(get, cfg: ModelConfig, i: int, moe: bool = False) -> dict:
     """Layer ``i``'s tensors under canonical keys, whatever the family's checkpoint layout:
     q, k, v, o, (q_bias, k_bias, v_bias), (q_norm, k_norm), in_norm, post_norm, (pre_ff_norm,
-    post_ff_norm), gate, up, down. ``get(name)`` returns a tensor (or a quantized weight that
+    post_ff_norm), gate, up, down; MLA: q_a, q_a_norm, q_b (or q), kv_a, kv_a_norm, kv_b; MoE layers:
+    with ``moe``, router, (router_bias), experts [(gate, up, down)], (shared (gate, up, down)) (the
+    serving model reads only its own experts by name instead). ``get(name)`` returns a tensor (or a quantized weight that
     supports row slicing). Phi-3's fused ``qkv_proj`` / ``gate_up_proj`` are split by rows."""
     p = f"model.layers.{i}."
     q_sz, kv_sz, f = cfg.q_size, cfg.kv_size, cfg.intermediate_size
@@ -121,6 +150,15 @@ def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
              "post_norm": None if cfg.parallel_block else get(p + "post_attention_layernorm.weight")}
     if cfg.is_gdn_layer(i):
         pass
+    elif cfg.is_mla:
+        pa = p + "self_attn."
+        if cfg.q_lora_rank:
+            t["q_a"], t["q_a_norm"] = get(pa + "q_a_proj.weight"), get(pa + "q_a_layernorm.weight")
+            t["q_b"] = get(pa + "q_b_proj.weight")
+        else:
+            t["q"] = get(pa + "q_proj.weight")
+        t["kv_a"], t["kv_a_norm"] = get(pa + "kv_a_proj_with_mqa.weight"), get(pa + "kv_a_layernorm.weight")
+        t["kv_b"] = get(pa + "kv_b_proj.weight")
     elif cfg.architecture == "phi3":
         qkv = get(p + "self_attn.qkv_proj.weight")
         t["q"], t["k"], t["v"] = qkv[:q_sz], qkv[q_sz:q_sz + kv_sz], qkv[q_sz + kv_sz:q_sz + 2 * kv_sz]
@@ -137,7 +175,21 @@ def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
     if cfg.sandwich_norm:
         t["pre_ff_norm"] = get(p + "pre_feedforward_layernorm.weight")
         t["post_ff_norm"] = get(p + "post_feedforward_layernorm.weight")
-    if not cfg.is_moe:
+    if cfg.is_moe_layer(i) and not moe:
+        pass
+    elif cfg.is_moe_layer(i) and cfg.moe_scoring == "sigmoid":
+        pm = p + "mlp."
+        t["router"], t["router_bias"] = get(pm + "gate.weight"), get(pm + "gate.e_score_correction_bias")
+        t["experts"] = [tuple(get(pm + f"experts.{e}.{n}_proj.weight") for n in ("gate", "up", "down"))
+                        for e in range(cfg.num_local_experts)]
+        if cfg.n_shared_experts:
+            t["shared"] = tuple(get(pm + f"shared_experts.{n}_proj.weight") for n in ("gate", "up", "down"))
+    elif cfg.is_moe_layer(i):
+        pm = p + "block_sparse_moe."
+        t["router"] = get(pm + "gate.weight")
+        t["experts"] = [tuple(get(pm + f"experts.{e}.{n}.weight") for n in ("w1", "w3", "w2"))
+                        for e in range(cfg.num_local_experts)]
+    else:
         if cfg.architecture == "phi3":
             gu = get(p + "mlp.gate_up_proj.weight")
             t["gate"], t["up"] = gu[:f], gu[f:2 * f]
@@ -149,12 +201,29 @@ def layer_tensors(get, cfg: ModelConfig, i: int) -> dict:
 
 
 def rope_inv_freq(cfg: ModelConfig, theta: Optional[float] = None, long: bool = False) -> torch.Tensor:
-    """Per-pair inverse frequencies, including ``linear``, ``llama3`` and ``longrope`` scaling."""
-    d = cfg.head_dim
+    """Per-pair inverse frequencies, including ``linear``, ``llama3``, ``longrope`` and ``yarn``
+    scaling (YaRN, arXiv 2309.00071: pairs that turn more than ``beta_fast`` times over the original
+    context keep their frequency, pairs that turn fewer than ``beta_slow`` times are divided by
+    ``factor``, with a linear ramp between)."""
+    d = cfg.rope_dim
     theta = theta or cfg.rope_theta
     inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
     rs = cfg.rope_scaling
-    if rs.kind == "linear":
+    if rs.kind == "yarn":
+        inv = inv.float().double()  # the published tables are computed in fp32
+        orig = rs.original_max_position_embeddings
+
+        def dim_of(rotations):  # pair index whose wavelength fits ``rotations`` times in ``orig``
+            return d * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(theta))
+
+        lo = max(math.floor(dim_of(rs.beta_fast)), 0)
+        hi = min(math.ceil(dim_of(rs.beta_slow)), d - 1)
+        if lo == hi:
+            hi += 0.001
+        ramp = ((torch.arange(d // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0, 1)
+        keep = 1 - ramp  # 1: extrapolate (original frequency), 0: interpolate (divided by factor)
+        inv = inv / rs.factor * (1 - keep) + inv * keep
+    elif rs.kind == "linear":
         inv = inv / rs.factor
     elif rs.kind == "llama3":
         low_wl = rs.original_max_position_embeddings / rs.low_freq_factor
@@ -188,6 +257,11 @@ def rope_cos_sin(cfg: ModelConfig, max_pos: int, device="cpu", theta: Optional[f
         mscale = math.sqrt(1 + math.log(s) / math.log(orig)) if s > 1 else 1.0
         return torch.cat([freqs.cos() * mscale, freqs.sin() * mscale], dim=-1)
     freqs = torch.outer(t, rope_inv_freq(cfg, theta).to(device))
+    if rs.kind == "yarn":
+        from ..config import yarn_mscale
+        att = yarn_mscale(rs.factor, rs.mscale) / yarn_mscale(rs.factor, rs.mscale_all_dim) \
+            if (rs.mscale and rs.mscale_all_dim) else yarn_mscale(rs.factor)
+        return torch.cat([freqs.cos() * att, freqs.sin() * att], dim=-1)
     return torch.cat([freqs.cos(), freqs.sin()], dim=-1)
 
 
@@ -220,12 +294,11 @@ def rms_norm_ref(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf).to(x.dtype)
 
 
-def moe_ref(x: torch.Tensor, gate_w: torch.Tensor, experts: list, top_k: int) -> torch.Tensor:
-    """Mixtral MoE: softmax over all experts → top-k → renormalise → weighted SwiGLU experts."""
-    logits = x.float() @ gate_w.float().t()
-    probs = torch.softmax(logits, dim=-1)
-    topw, topi = probs.topk(top_k, dim=-1)
-    topw = topw / topw.sum(-1, keepdim=True)
+def moe_ref(x: torch.Tensor, gate_w: torch.Tensor, experts: list, top_k: int, **route) -> torch.Tensor:
+    """MoE FFN: router top-k (Mixtral softmax by default; ``route`` selects DeepSeek-V3's sigmoid
+    group-limited routing, see ``ops.reference.moe_route``) → weighted SwiGLU experts."""
+    from ..ops.reference import moe_route
+    topi, topw = moe_route(x.float() @ gate_w.float().t(), top_k, **route)
     out = torch.zeros_like(x, dtype=torch.float32)
     for e, (w1, w3, w2) in enumerate(experts):
         mask = (topi == e)
@@ -237,6 +310,14 @@ def moe_ref(x: torch.Tensor, gate_w: torch.Tensor, experts: list, top_k: int) ->
         ye = (torch.nn.functional.silu(xe @ w1.float().t()) * (xe @ w3.float().t())) @ w2.float().t()
         out[rows] += wt[:, None] * ye
     return out.to(x.dtype)
+
+
+def route_options(cfg: ModelConfig, bias: Optional[torch.Tensor] = None) -> dict:
+    """Keyword options of ``ops.reference.moe_route`` for the family's router."""
+    if cfg.moe_scoring == "softmax":
+        return {}
+    return dict(renorm=cfg.norm_topk_prob, scoring=cfg.moe_scoring, bias=bias, n_group=cfg.n_group,
+                topk_group=cfg.topk_group, scale=cfg.routed_scaling_factor)
 
 
 class ReferenceDecoder:
@@ -268,6 +349,18 @@ class ReferenceDecoder:
                 x = rms_norm_ref(h, L["post_norm"], eps, uo)
                 h = h + self._ffn(x, L, i)
                 continue
+            win = cfg.layer_window(i)
+            mask = causal
+            if key_mask is not None:
+                mask = mask.masked_fill(~key_mask, float("-inf"))
+            if win > 0:
+                mask = mask + torch.full((S, S), float("-inf")).tril(-win)
+            if cfg.is_mla:
+                a = self._mla(x, L, pos, mask)
+                h = h + a
+                x = rms_norm_ref(h, L["post_norm"], eps, uo)
+                h = h + self._ffn(x, L, i)
+                continue
             q = x @ L["q"].t()
             k = x @ L["k"].t()
             v = x @ L["v"].t()
@@ -277,7 +370,6 @@ class ReferenceDecoder:
             if cfg.qk_norm:
                 q = rms_norm_ref(q, L["q_norm"], eps, uo)
                 k = rms_norm_ref(k, L["k_norm"], eps, uo)
-            win = cfg.layer_window(i)
             cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
             if not (cfg.rope_sliding_only and win == 0):
                 rope = apply_rope_interleaved if cfg.rope_interleaved else apply_rope_neox
@@ -290,11 +382,6 @@ class ReferenceDecoder:
             if cfg.attn_logit_softcapping:
                 c = cfg.attn_logit_softcapping
                 s = c * torch.tanh(s / c)
-            mask = causal
-            if key_mask is not None:
-                mask = mask.masked_fill(~key_mask, float("-inf"))
-            if win > 0:
-                mask = mask + torch.full((S, S), float("-inf")).tril(-win)
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), v).reshape(S, H * D)
             a = a @ L["o"].t()
             if cfg.parallel_block:  # attention and MLP both read x (one norm per layer)
@@ -320,13 +407,43 @@ class ReferenceDecoder:
             logits = c * torch.tanh(logits / c)
         return logits
 
+    def _mla(self, x: torch.Tensor, L: dict, pos: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+        """Multi-head latent attention (DeepSeek-V3), decompressed: per-head keys [k_nope | k_rope]
+        with one k_rope shared by all heads, values from the normalised latent. With
+        ``rope_interleaved`` the rope dims are pairs (2i, 2i+1), rotated and returned as
+        [evens | odds] (the layout the checkpoint's attention uses)."""
+        cfg = self.cfg
+        S, H, eps = x.shape[0], cfg.num_attention_heads, cfg.rms_norm_eps
+        nope, rd, vd = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+        if cfg.q_lora_rank:
+            q = rms_norm_ref(x @ L["q_a"].t(), L["q_a_norm"], eps) @ L["q_b"].t()
+        else:
+            q = x @ L["q"].t()
+        q = q.view(S, H, nope + rd)
+        ckv = x @ L["kv_a"].t()
+        kv = (rms_norm_ref(ckv[:, :cfg.kv_lora_rank], L["kv_a_norm"], eps) @ L["kv_b"].t()).view(S, H, nope + vd)
+        q_rot, k_rot = q[..., nope:], ckv[:, None, cfg.kv_lora_rank:]
+        if cfg.rope_interleaved:
+            q_rot = torch.cat([q_rot[..., 0::2], q_rot[..., 1::2]], -1)
+            k_rot = torch.cat([k_rot[..., 0::2], k_rot[..., 1::2]], -1)
+        q_rot = apply_rope_neox(q_rot, self.cos_sin, pos)
+        k_rot = apply_rope_neox(k_rot, self.cos_sin, pos)
+        q = torch.cat([q[..., :nope], q_rot], -1)
+        k = torch.cat([kv[..., :nope], k_rot.expand(S, H, rd)], -1)
+        s = torch.einsum("qhd,khd->hqk", q, k) * cfg.attn_scale
+        a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), kv[..., nope:]).reshape(S, H * vd)
+        return a @ L["o"].t()
+
     def _ffn(self, x: torch.Tensor, L: dict, i: int) -> torch.Tensor:
         cfg, w = self.cfg, self.w
-        if cfg.is_moe:
-            pe = f"model.layers.{i}.block_sparse_moe."
-            experts = [(w[pe + f"experts.{e}.w1.weight"], w[pe + f"experts.{e}.w3.weight"],
-                        w[pe + f"experts.{e}.w2.weight"]) for e in range(cfg.num_local_experts)]
-            return moe_ref(x, w[pe + "gate.weight"], experts, cfg.num_experts_per_tok)
+        if cfg.is_moe_layer(i):
+            M = layer_tensors(w.__getitem__, cfg, i, moe=True)
+            out = moe_ref(x, M["router"], M["experts"], cfg.num_experts_per_tok,
+                          **route_options(cfg, M.get("router_bias")))
+            if "shared" in M:
+                g, u, d = M["shared"]
+                out = out + (torch.nn.functional.silu(x @ g.t()) * (x @ u.t())) @ d.t()
+            return out
         g = x @ L["gate"].t()
         act = torch.nn.functional.silu(g) if cfg.hidden_act == "silu" else \
             torch.nn.functional.gelu(g, approximate="tanh")

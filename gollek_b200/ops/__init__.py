@@ -454,30 +454,35 @@ def _moe_workspace(device: torch.device, ints: int) -> torch.Tensor:
     return ws
 
 
-def moe_route_ref(x: torch.Tensor, router: torch.Tensor, top_k: int, renorm: bool = True):
-    """fp32 softmax top-k routing: (ids [T, k] int64, weights [T, k] fp32)."""
-    probs = torch.softmax(x.float() @ router.float().t(), dim=-1)
-    w, ids = probs.topk(top_k, dim=-1)
-    if renorm:
-        w = w / w.sum(-1, keepdim=True)
-    return ids, w
+def moe_route_ref(x: torch.Tensor, router: torch.Tensor, top_k: int, renorm: bool = True, **route):
+    """fp32 top-k routing: (ids [T, k] int64, weights [T, k] fp32); ``route`` holds the scoring
+    options of ``ops.reference.moe_route`` (scoring, bias, n_group, topk_group, scale)."""
+    return ref.moe_route(x.float() @ router.float().t(), top_k, renorm, **route)
 
 
 def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, top_k: int,
               e0: int = 0, e_loc: Optional[int] = None, renorm: bool = True,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, scoring: str = "softmax", bias: Optional[torch.Tensor] = None,
+              n_group: int = 1, topk_group: int = 1, scale: float = 1.0,
+              routing: Optional[dict] = None) -> torch.Tensor:
     """Mixture-of-experts FFN over the local experts [e0, e0 + e_loc) of ``router.shape[0]``.
 
     w_gu [e_loc * 2F, H]: per expert, gate/up rows interleaved in groups of 64 (SwiGLU epilogue);
     w_down [e_loc * H, F]. Returns Σ over the token's top-k experts that are local of
     weight · down(silu(gate) · up) — under expert parallelism a partial sum that the following
-    tensor-parallel all-reduce completes."""
+    tensor-parallel all-reduce completes. Routing: softmax top-k (Mixtral), or with
+    ``scoring="sigmoid"`` DeepSeek-V3's bias-corrected, group-limited choice (``bias`` fp32 [E],
+    ``n_group`` / ``topk_group``) with weights times ``scale``. A ``routing`` dict receives the
+    chosen expert ids and weights ("ids" [T, k], "wts" [T, k])."""
+    route = dict(scoring=scoring, bias=bias, n_group=n_group, topk_group=topk_group, scale=scale)
     T, H = x.shape
     E = router.shape[0]
     e_loc = E if e_loc is None else e_loc
     F_ = w_down.shape[1]
     if not x.is_cuda:
-        ids, w = moe_route_ref(x, router, top_k, renorm)
+        ids, w = moe_route_ref(x, router, top_k, renorm, **route)
+        if routing is not None:
+            routing.update(ids=ids, wts=w)
         acc = torch.zeros(T, H, dtype=torch.float32)
         for le in range(e_loc):
             sel = ids == (e0 + le)
@@ -509,8 +514,10 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
         yp = torch.empty(cap, H, dtype=x.dtype, device=dev)
         ypart = None
     C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, xp if yp is None else yp, ypart,
-                  top_k, renorm, e0, e_loc)
+                  top_k, renorm, e0, e_loc, 0 if scoring == "softmax" else 1, bias, n_group, topk_group, float(scale))
     LAUNCHES.add(6)
+    if routing is not None:
+        routing.update(ids=ids.view(T, top_k), wts=wts.view(T, top_k))
     return out
 
 

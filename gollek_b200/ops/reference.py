@@ -340,3 +340,42 @@ def gdn_gated_norm(o: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float
     of = o.float()
     y = of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * w.float()
     return (y.reshape(T, Hg * D) * torch.nn.functional.silu(g.float())).to(o.dtype)
+
+
+def moe_route(logits: torch.Tensor, top_k: int, renorm: bool = True, scoring: str = "softmax",
+              bias: Optional[torch.Tensor] = None, n_group: int = 1, topk_group: int = 1,
+              scale: float = 1.0):
+    """Router logits [T, E] (fp32) → (expert ids [T, k] int64, weights [T, k] fp32).
+
+    ``softmax`` (Mixtral): top-k of the softmax, renormalised over the k. ``sigmoid`` (DeepSeek-V3):
+    the choice score is sigmoid(logit) + bias; experts are split into ``n_group`` groups, each group
+    scored by the sum of its two best choice scores, and the top-k is taken inside the ``topk_group``
+    best groups (other experts' scores count as 0); the weights are the chosen experts' sigmoid
+    scores (without the bias), renormalised when ``renorm``, times ``scale``. Ties go to the lower
+    expert id (the CUDA router does the same)."""
+    logits = logits.float()
+    T, E = logits.shape
+    if scoring == "softmax":
+        probs = torch.softmax(logits, dim=-1)
+        choice = probs
+    else:
+        probs = torch.sigmoid(logits)
+        choice = probs + (bias.float() if bias is not None else 0.0)
+    if n_group > 1:
+        g = choice.view(T, n_group, E // n_group)
+        gscore = g.topk(2, dim=-1).values.sum(-1)
+        keep = _topk_lowest_index(gscore, topk_group)
+        gmask = torch.zeros(T, n_group, dtype=torch.bool, device=logits.device)
+        gmask.scatter_(1, keep, True)
+        choice = choice.masked_fill(~gmask.repeat_interleave(E // n_group, dim=1), 0.0)
+    ids = _topk_lowest_index(choice, top_k)
+    w = probs.gather(1, ids)
+    if renorm:
+        w = w / (w.sum(-1, keepdim=True) + (1e-20 if scoring != "softmax" else 0.0))
+    return ids, w * scale
+
+
+def _topk_lowest_index(x: torch.Tensor, k: int) -> torch.Tensor:
+    """Indices of the k largest entries per row, ties broken towards the lower index."""
+    # stable sort on descending value keeps equal values in index order
+    return torch.sort(x, dim=-1, descending=True, stable=True).indices[..., :k]
