@@ -319,6 +319,7 @@ class LLMEngine:
         self._inflight = None
         toks = h.tokens()
         now = time.perf_counter()
+        bs = self.kv.block_size
         outputs: List[RequestOutput] = []
         for (seq, idx), tok in zip(h.records, toks):
             seq.pending -= 1
@@ -339,7 +340,8 @@ class LLMEngine:
                     self._n_host_sampling -= 1
                 self.seqs.pop(seq.request_id, None)
                 self.metrics.on_finish(seq)
-            elif self.kv.has(seq):
+            elif (seq.num_computed_tokens // bs > len(seq.block_hashes) and seq.status is SeqStatus.RUNNING
+                  and self.kv.has(seq)):
                 # positions < num_computed_tokens are inputs of launched steps, all resolved by now
                 # (the in-flight step's own placeholder sits at num_computed_tokens)
                 self.kv.commit_full_blocks(seq)

@@ -116,11 +116,11 @@ class KVCacheManager:
 
     def commit_full_blocks(self, seq: Sequence) -> None:
         """Register newly completed full blocks of ``seq`` in the prefix cache."""
-        if not self.enable_prefix_caching or self.tables.dropped(seq.seq_id):
+        if not self.enable_prefix_caching:
             return
         bs = self.block_size
         full = seq.num_computed_tokens // bs
-        if full <= len(seq.block_hashes):
+        if full <= len(seq.block_hashes) or self.tables.dropped(seq.seq_id):
             return
         blocks = self.tables.blocks(seq.seq_id)
         parent = seq.block_hashes[-1] if seq.block_hashes else 0

@@ -115,29 +115,48 @@ class ModelRunner:
         n = len(chunks)
         h = self.host
         ids = h.input_ids.numpy()
-        self._pending_rows = []
+        self._pending_rows = pending = []
+        # per-chunk values are collected in lists and written with one numpy assignment per buffer:
+        # an element-wise torch ``__setitem__`` costs microseconds, which at thousands of running
+        # sequences per step made this loop the host's largest cost
+        seq_ids, starts, n_new = [0] * n, [0] * n, [0] * n
         t = 0
         sample_rows: List[int] = []
         sample_seqs: List[Sequence] = []
         for i, c in enumerate(chunks):
-            h.seq_ids[i] = c.seq.seq_id
-            h.start[i] = c.start
-            h.n_new[i] = c.num_tokens
-            if self.hybrid:
-                self.gdn_host[0, i] = c.seq.state_slot
-                self.gdn_host[1, i] = 1 if c.start == 0 else 0
-            toks = c.tokens if c.tokens is not None else c.seq.tokens(c.start, c.start + c.num_tokens)
-            ids[t:t + c.num_tokens] = toks
-            if c.num_tokens and toks[-1] < 0:  # a token still being sampled by the in-flight step
-                self._pending_rows.append((t + c.num_tokens - 1, c.seq.seq_id))
-            t += c.num_tokens
+            seq, k, st = c.seq, c.num_tokens, c.start
+            seq_ids[i], starts[i], n_new[i] = seq.seq_id, st, k
+            if c.tokens is not None:
+                toks = c.tokens
+            elif k == 1:
+                np_ = len(seq.prompt_token_ids)
+                toks = (seq.prompt_token_ids[st],) if st < np_ else (seq.output_token_ids[st - np_],)
+            else:
+                toks = seq.tokens(st, st + k)
+            if k == 1:
+                ids[t] = toks[0]
+            else:
+                ids[t:t + k] = toks
+            if k and toks[-1] < 0:  # a token still being sampled by the in-flight step
+                pending.append((t + k - 1, seq.seq_id))
+            t += k
             if c.sample:
-                sample_rows.extend(range(t - 1 - c.verify, t))
-                sample_seqs.append(c.seq)
+                if c.verify:
+                    sample_rows.extend(range(t - 1 - c.verify, t))
+                else:
+                    sample_rows.append(t - 1)
+                sample_seqs.append(seq)
+        h.seq_ids.numpy()[:n] = seq_ids
+        h.start.numpy()[:n] = starts
+        h.n_new.numpy()[:n] = n_new
+        if self.hybrid:
+            g = self.gdn_host.numpy()
+            g[0, :n] = [c.seq.state_slot for c in chunks]
+            g[1, :n] = [1 if c.start == 0 else 0 for c in chunks]
         T = self.kv.tables.build_batch(h.seq_ids[:n], h.start[:n], h.n_new[:n], h.positions, h.slots,
                                        h.block_tables[:n], h.seq_lens[:n], h.query_start[: n + 1])
         assert T == t
-        h.logits_idx[: len(sample_rows)] = torch.tensor(sample_rows, dtype=torch.int64)
+        h.logits_idx.numpy()[: len(sample_rows)] = sample_rows
         return n, T, sample_seqs, sample_rows
 
     def _decode_splits(self, nd: int, max_len: int) -> int:
