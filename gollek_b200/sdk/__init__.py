@@ -148,6 +148,14 @@ class GollekClient:
         j = self._post("/v1/embeddings", {"input": texts}).json()
         return [d["embedding"] for d in j["data"]]
 
+    def rag_ingest(self, collection: str, documents: List[dict], **kw) -> dict:
+        """Chunk, embed and index ``documents`` ([{"id", "content"}]) into ``collection``."""
+        return self._post("/v1/rag/ingest", {"collection": collection, "documents": documents, **kw}).json()
+
+    def rag_query(self, collection: str, question: str, **kw) -> dict:
+        """Answer ``question`` from the collection's most similar chunks: {answer, context_used, sources}."""
+        return self._post("/v1/rag/query", {"collection": collection, "question": question, **kw}).json()
+
     def list_models(self) -> List[str]:
         r = self.http.get(self.base + "/v1/models", timeout=self.timeout)
         return [m["id"] for m in r.json()["data"]]

@@ -29,7 +29,7 @@ from datetime import datetime, timezone
 from typing import Any, Dict, List, Optional, Union
 
 from fastapi import FastAPI, Header, HTTPException, Request
-from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
 from pydantic import BaseModel, Field
 
 from .. import errors
@@ -77,6 +77,7 @@ class ChatRequest(BaseModel):
     mirostat_eta: Optional[float] = None
     response_format: Optional[Dict[str, Any]] = None
     guided_regex: Optional[str] = None
+    rag: Optional[Dict[str, Any]] = None  # {"collection": name, "top_k": 4, "max_context_tokens": 1024}
 
 
 class CompletionRequest(BaseModel):
@@ -226,12 +227,41 @@ def build_sampling(st: ServerState, d: Dict[str, Any], defaults: Dict[str, Any])
 OPENAI_DEFAULTS = dict(temperature=0.7, top_p=0.95, top_k=50, max_tokens=2048, repetition_penalty=1.0)
 
 
+class RagDocument(BaseModel):
+    id: Optional[str] = None
+    content: str
+
+
+class RagIngestRequest(BaseModel):
+    collection: str
+    documents: List[RagDocument]
+    chunk_size: int = 800          # characters per chunk
+    chunk_overlap: int = 100
+    embeddingModel: Optional[str] = None
+
+
+class RagQueryRequest(BaseModel):
+    collection: str
+    question: str
+    topK: Optional[int] = None
+    top_k: Optional[int] = None
+    maxTokens: Optional[int] = None
+    max_tokens: Optional[int] = None
+    temperature: Optional[float] = None
+    max_context_tokens: int = 1024
+    min_similarity: float = -1.0
+    llmModel: Optional[str] = None
+    embeddingModel: Optional[str] = None
+
+
 def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
                rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
                engine_builder=None, drain_timeout_s: float = 30.0) -> FastAPI:
     """``engine_builder(model) -> LLMEngine`` builds the engine of a hot-swap (default: the running
     engine's configuration with ``model`` replaced)."""
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
+    from .rag import RagStore
+    st.rag = RagStore()
     gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
     app = FastAPI(title="gollek-b200", version="0.1")
     app.state.server = st
@@ -518,7 +548,12 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             rx = tool_choice_regex(req.tool_choice)
             if rx and not (sp.guided_json or sp.guided_regex):
                 sp.guided_regex = rx  # a forced call: the output is constrained to the call's shape
-        prompt = chat_prompt(req.messages, tools)
+        rag_sources = None
+        messages = req.messages
+        if req.rag:
+            messages, rag_sources = await rag_augment(
+                [m if isinstance(m, dict) else m.model_dump(exclude_none=True) for m in req.messages], req.rag)
+        prompt = chat_prompt(messages, tools)
         cid = "chatcmpl-" + uuid.uuid4().hex
 
         def keep_calls(calls):
@@ -559,9 +594,12 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                 message = {"role": "assistant", "content": content or None,
                            "tool_calls": [c.openai() for c in keep_calls(calls)]}
                 finish = "tool_calls"
-        return {"id": cid, "object": "chat.completion", "created": _now(), "model": st.model_name,
+        resp = {"id": cid, "object": "chat.completion", "created": _now(), "model": st.model_name,
                 "choices": [{"index": 0, "message": message, "finish_reason": finish, "logprobs": chat_logprobs(o)}],
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
+        if rag_sources is not None:
+            resp["rag_sources"] = rag_sources
+        return resp
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):
@@ -593,6 +631,72 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         return {"object": "list", "model": st.model_name,
                 "data": [{"object": "embedding", "index": i, "embedding": v} for i, v in enumerate(vecs)],
                 "usage": {"prompt_tokens": n, "total_tokens": n}}
+
+    # -------------------------------------------------------------- retrieval-augmented generation
+    def count_tokens(text: str) -> int:
+        return len(st.tokenizer.encode(text)) if st.tokenizer is not None else max(1, len(text) // 4)
+
+    async def rag_retrieve(collection: str, question: str, top_k: int, min_similarity: float = -1.0):
+        col = st.rag.get(collection)
+        if col is None:
+            raise HTTPException(404, f"unknown RAG collection {collection!r}")
+        qv = (await _embed([question]))[0]
+        return col.search(qv, top_k, min_similarity)
+
+    async def rag_augment(messages: List[dict], opts: Dict[str, Any]):
+        from .rag import augment_messages, build_context, last_user_text
+        hits = await rag_retrieve(str(opts.get("collection", "")), last_user_text(messages),
+                                  int(opts.get("top_k", 4)), float(opts.get("min_similarity", -1.0)))
+        ctx = build_context(hits, int(opts.get("max_context_tokens", 1024)), count_tokens)
+        msgs = augment_messages(messages, ctx) if hits else messages
+        return msgs, [h.source() for h in hits]
+
+    @app.post("/v1/rag/ingest")
+    async def rag_ingest(req: RagIngestRequest):
+        from .rag import chunk_text
+        if not req.documents:
+            raise HTTPException(400, "documents must be non-empty")
+        col = st.rag.get(req.collection, create=True)
+        n = 0
+        for k, doc in enumerate(req.documents):
+            chunks = chunk_text(doc.content, req.chunk_size, req.chunk_overlap)
+            if not chunks:
+                continue
+            vecs = await _embed(chunks)
+            col.add(doc.id or f"doc-{len(col)}-{k}", chunks, vecs)
+            n += len(chunks)
+        return {"collection": req.collection, "chunks": n, "status": "indexed"}
+
+    @app.post("/v1/rag/query")
+    async def rag_query(req: RagQueryRequest):
+        from .rag import augment_messages, build_context
+        top_k = req.topK or req.top_k or 4
+        hits = await rag_retrieve(req.collection, req.question, top_k, req.min_similarity)
+        msgs = [{"role": "user", "content": req.question}]
+        if hits:
+            msgs = augment_messages(msgs, build_context(hits, req.max_context_tokens, count_tokens))
+        d = {"max_tokens": req.maxTokens or req.max_tokens, "temperature": req.temperature}
+        sp = build_sampling(st, d, OPENAI_DEFAULTS)
+        o = await run_full(chat_prompt(msgs), sp, lora_id=0)
+        return {"answer": o.text or detok(o.output_token_ids), "context_used": bool(hits),
+                "sources": [h.source() for h in hits]}
+
+    @app.get("/v1/rag/collections")
+    async def rag_collections():
+        return {"collections": [{"name": n, "chunks": len(c)} for n, c in list(st.rag.collections.items())]}
+
+    @app.get("/v1/rag/collections/{name}")
+    async def rag_collection(name: str):
+        c = st.rag.get(name)
+        if c is None:
+            raise HTTPException(404, f"unknown RAG collection {name!r}")
+        return {"name": name, "chunks": len(c)}
+
+    @app.delete("/v1/rag/collections/{name}")
+    async def rag_drop(name: str):
+        if not st.rag.drop(name):
+            raise HTTPException(404, f"unknown RAG collection {name!r}")
+        return Response(status_code=204)
 
     # -------------------------------------------------------------- gollek platform routes
     def infer_prompt(req: InferRequest):
