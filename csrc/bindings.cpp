@@ -244,7 +244,8 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
                      torch::Tensor w_down, torch::Tensor ws, torch::Tensor ids, torch::Tensor wts, torch::Tensor dest,
                      torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, c10::optional<torch::Tensor> ypart,
                      int64_t topk, bool renorm, int64_t e0, int64_t e_loc, int64_t scoring,
-                     c10::optional<torch::Tensor> score_bias, int64_t n_group, int64_t topk_group, double scale) {
+                     c10::optional<torch::Tensor> score_bias, int64_t n_group, int64_t topk_group, double scale,
+                     c10::optional<torch::Tensor> expert_map) {
   for (auto* t : {&out, &x, &router, &w_gu, &w_down, &xp, &hp, &yp}) check_bf16(*t, "moe operand");
   MoeRouting rt;
   rt.scoring = (int)scoring;
@@ -256,6 +257,12 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
                     score_bias->numel() == router.size(0),
                 "moe: score correction bias must be fp32 [E] on the device");
     rt.bias = score_bias->data_ptr<float>();
+  }
+  if (expert_map.has_value()) {
+    TORCH_CHECK(expert_map->is_cuda() && expert_map->scalar_type() == at::kInt && expert_map->is_contiguous() &&
+                    expert_map->numel() == router.size(0),
+                "moe: expert map must be int32 [E] on the device (logical expert -> physical slot)");
+    rt.expert_map = expert_map->data_ptr<int>();
   }
   check_same_device(x, w_gu);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "moe: x/out row-major [T, H]");
@@ -657,7 +664,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ids"), py::arg("wts"), py::arg("dest"), py::arg("xp"), py::arg("hp"), py::arg("yp"),
         py::arg("ypart"), py::arg("topk"), py::arg("renorm"), py::arg("e0"), py::arg("e_loc"),
         py::arg("scoring") = 0, py::arg("score_bias") = py::none(), py::arg("n_group") = 1,
-        py::arg("topk_group") = 1, py::arg("scale") = 1.0);
+        py::arg("topk_group") = 1, py::arg("scale") = 1.0, py::arg("expert_map") = py::none());
   m.def("moe_capacity_rows", &moe_capacity_rows);
   m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
   m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");

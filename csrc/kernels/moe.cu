@@ -213,9 +213,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
     float scale = rt.scale;
     if (renorm) scale /= psum + (rt.scoring == 0 ? 0.f : 1e-20f);
     for (int j = 0; j < topk; ++j) {
-      ids[(int64_t)t * topk + j] = sel_id[j];
+      // routing runs over logical experts; ids (and the local counts) are physical slots
+      const int phys = rt.expert_map ? rt.expert_map[sel_id[j]] : sel_id[j];
+      ids[(int64_t)t * topk + j] = phys;
       wts[(int64_t)t * topk + j] = sel_p[j] * scale;
-      const int le = sel_id[j] - e0;
+      const int le = phys - e0;
       if (le >= 0 && le < e_loc) atomicAdd(&counts[le], 1);
     }
   }

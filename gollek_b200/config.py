@@ -569,6 +569,7 @@ class EngineConfig:
     device: str = "cuda"
     tensor_parallel_size: int = 1
     enable_expert_parallel: bool = False  # MoE: experts partitioned over the TP ranks (EP = TP size)
+    ep_rebalance_interval: int = 0        # EP: re-place experts by routed load every N engine steps (0 = off)
     # speculative decoding: "none" | "ngram" (prompt lookup) | "draft" (draft model ``draft_model``)
     speculative_method: str = "none"
     num_speculative_tokens: int = 4

@@ -97,6 +97,10 @@ class LLMEngine:
         if cfg.scheduling_policy == "wait":
             predictor = host_ext().LengthPredictor(64, 1.0, float(cfg.max_model_len), 0.05, 8)
         self.scheduler = Scheduler(cfg, self.kv, predictor)
+        self._steps = 0
+        self.ep_reports: List[dict] = []  # rebalances done: {"step", "layers": {layer: before/after/moved}}
+        if cfg.ep_rebalance_interval > 0 and getattr(self.model, "expert_parallel", False):
+            self.model.enable_expert_load_tracking()
         if self.model.cfg.is_mla and cfg.enable_lora:
             raise ValueError("LoRA adapters on multi-head latent attention models are not supported")
         self.lora_manager = None
@@ -282,6 +286,7 @@ class LLMEngine:
         """One scheduler iteration. With async scheduling: schedule and launch this step, then read
         back the previous one (its outputs are returned), so the host work of a step overlaps the
         device work of the one before. Otherwise: schedule, (draft,) run, append, retire."""
+        self._maybe_rebalance()
         if self._needs_sync():
             outs = self._resolve_inflight()
             return outs + self._step_sync()
@@ -310,6 +315,16 @@ class LLMEngine:
         self.metrics.on_step(time.perf_counter() - t0, sched.num_tokens, len(outs), len(self.scheduler.running),
                              len(self.scheduler.waiting), self.kv.usage(), len(sched.preempted))
         return outs
+
+    def _maybe_rebalance(self) -> None:
+        """Every ``ep_rebalance_interval`` steps (all ranks step in lockstep): re-place the experts by
+        their routed load. In-place weight moves are ordered after the in-flight step on the stream."""
+        self._steps += 1
+        n = self.cfg.ep_rebalance_interval
+        if n > 0 and self._steps % n == 0 and getattr(self.model, "expert_parallel", False):
+            rep = self.model.rebalance_experts()
+            if rep:
+                self.ep_reports.append({"step": self._steps, "layers": rep})
 
     def _resolve_inflight(self) -> List[RequestOutput]:
         """Read back the in-flight step: fill placeholders, stop checks, retire finished sequences."""

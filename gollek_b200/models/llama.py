@@ -23,6 +23,7 @@ import math
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional
 
+import numpy as np
 import torch
 
 from .. import ops
@@ -236,6 +237,7 @@ class LlamaModel:
         self.embed: Optional[torch.Tensor] = None
         self.norm: Optional[torch.Tensor] = None
         self.lm_head: Optional[torch.Tensor] = None
+        self.expert_perm: Dict[int, np.ndarray] = {}  # MoE layer -> physical slot -> logical expert (EP)
         self.lora = None  # optional MultiLoRA hook (gollek_b200.engine.lora)
         self.offload = None  # optional LayerOffload (weights of some layers streamed from host memory)
 
@@ -612,8 +614,14 @@ class LlamaModel:
             return ops.linear(ops.linear_swiglu(x, L["w_sh_gu"]), L["w_sh_down"], residual=hm, out=out)
         renorm = cfg.norm_topk_prob
         if "moe_gu" in L:  # dense experts: route + permute + grouped tcgen05 GEMMs + combine
-            return ops.fused_moe(x, L["router"], L["moe_gu"], L["moe_down"], cfg.num_experts_per_tok,
-                                 self.e0, self.E_loc, renorm=renorm, out=out, **self._route(L))
+            rt = {} if "expert_load" in L else None
+            y = ops.fused_moe(x, L["router"], L["moe_gu"], L["moe_down"], cfg.num_experts_per_tok,
+                              self.e0, self.E_loc, renorm=renorm, out=out, routing=rt,
+                              expert_map=L.get("expert_map"), **self._route(L))
+            if rt is not None:  # per-expert token counts for the rebalancer (physical expert ids)
+                ids = rt["ids"].reshape(-1).long()
+                L["expert_load"].index_add_(0, ids, torch.ones(ids.shape[0], dtype=torch.float32, device=ids.device))
+            return y
         # quantized experts (GGUF / FP8): one expert at a time
         topi, topw = ops.moe_route_ref(x, L["router"], cfg.num_experts_per_tok, renorm, **self._route(L))
         topw = topw.to(x.device)
@@ -630,6 +638,98 @@ class LlamaModel:
             we = (topw * sel).sum(-1).index_select(0, rows)
             acc.index_add_(0, rows, ye * we[:, None])
         return _copy_out(acc.to(x.dtype), out)
+
+    # ------------------------------------------------------------------ expert-parallel rebalancing
+    def enable_expert_load_tracking(self) -> None:
+        """Count the tokens routed to each expert of every MoE layer (one small add per layer and
+        step) so that ``rebalance_experts`` can move hot experts apart."""
+        for L in self.layers:
+            if "moe_gu" in L and "expert_load" not in L:
+                L["expert_load"] = torch.zeros(self.cfg.num_local_experts, dtype=torch.float32, device=self.device)
+            if "moe_gu" in L and "expert_map" not in L:  # created before any graph capture, updated in place
+                L["expert_map"] = torch.arange(self.cfg.num_local_experts, dtype=torch.int32, device=self.device)
+
+    def rebalance_experts(self, min_gain: float = 0.05, loads: Optional[Dict[int, np.ndarray]] = None) -> Dict[int, dict]:
+        """Re-place the experts of each MoE layer over the expert-parallel ranks so that the ranks'
+        routed-token loads even out (``parallel.ep_balance``). Collective: every rank calls it at
+        the same point between steps. ``loads`` (logical expert -> tokens, per layer) overrides the
+        tracked counters. A layer moves only when its max/mean rank load drops by ``min_gain``.
+        Routing stays over the logical experts (router rows never move, so group-limited routing and
+        tie-breaking are unchanged); the layer's logical -> physical expert map and the expert
+        weights are rewritten in place (same device addresses, so captured CUDA graphs stay valid);
+        returns {layer: {"before", "after", "moved"}}."""
+        from ..parallel.ep_balance import imbalance, moves, plan_placement
+        if not self.expert_parallel:
+            return {}
+        world = self.comm.size
+        E = self.cfg.num_local_experts
+        report = {}
+        for li, L in enumerate(self.layers):
+            if "moe_gu" not in L:
+                continue
+            perm = self.expert_perm.setdefault(li, np.arange(E))
+            if loads is not None and li in loads:
+                logical = np.asarray(loads[li], dtype=np.float64)
+            elif "expert_load" in L:
+                phys = L["expert_load"].double().cpu()
+                if world > 1 and torch.distributed.is_initialized():  # every rank takes the same decision
+                    t = phys.to(self.device) if torch.distributed.get_backend() == "nccl" else phys
+                    torch.distributed.all_reduce(t)
+                    phys = t.cpu() / world
+                logical = np.zeros(E)
+                logical[perm] = phys.numpy()
+                L["expert_load"].zero_()
+            else:
+                continue
+            before = imbalance(logical, perm, world)
+            new = plan_placement(logical, perm, world)
+            after = imbalance(logical, new, world)
+            if after > before * (1.0 - min_gain):
+                continue
+            self._move_experts(L, perm, new)
+            self.expert_perm[li] = new
+            report[li] = {"before": before, "after": after, "moved": len(moves(perm, new, world))}
+        return report
+
+    def _move_experts(self, L: dict, old: np.ndarray, new: np.ndarray) -> None:
+        """Placement ``old`` -> ``new`` (physical slot -> logical expert): update the logical ->
+        physical expert map, copy the experts that stay on this rank and exchange the others point to
+        point (messages posted in destination-slot order on both sides)."""
+        import torch.distributed as dist
+        world, rank, cap = self.comm.size, self.comm.rank, self.E_loc
+        to_old = torch.as_tensor(np.argsort(old))  # logical expert -> old physical slot
+        sel = to_old[torch.as_tensor(new)]          # new physical slot -> old physical slot
+        emap = torch.as_tensor(np.argsort(new), dtype=torch.int32)  # logical expert -> new physical slot
+        if "expert_map" in L:
+            L["expert_map"].copy_(emap.to(L["expert_map"].device))
+        else:
+            L["expert_map"] = emap.to(self.device)
+        gu, dn = L["moe_gu"], L["moe_down"]
+        rg, rd = gu.shape[0] // cap, dn.shape[0] // cap
+        new_gu, new_dn = torch.empty_like(gu), torch.empty_like(dn)
+        ops_ = []
+        for p_new in range(rank * cap, (rank + 1) * cap):
+            j, p_old = p_new - rank * cap, int(sel[p_new])
+            src = p_old // cap
+            if src == rank:
+                i = p_old - rank * cap
+                new_gu[j * rg:(j + 1) * rg].copy_(gu[i * rg:(i + 1) * rg])
+                new_dn[j * rd:(j + 1) * rd].copy_(dn[i * rd:(i + 1) * rd])
+            else:
+                ops_.append(dist.P2POp(dist.irecv, new_gu[j * rg:(j + 1) * rg], src, tag=2 * p_new))
+                ops_.append(dist.P2POp(dist.irecv, new_dn[j * rd:(j + 1) * rd], src, tag=2 * p_new + 1))
+        for p_new in range(len(new)):
+            p_old = int(sel[p_new])
+            dst = p_new // cap
+            if p_old // cap == rank and dst != rank:
+                i = p_old - rank * cap
+                ops_.append(dist.P2POp(dist.isend, gu[i * rg:(i + 1) * rg].contiguous(), dst, tag=2 * p_new))
+                ops_.append(dist.P2POp(dist.isend, dn[i * rd:(i + 1) * rd].contiguous(), dst, tag=2 * p_new + 1))
+        if ops_:
+            for w in dist.batch_isend_irecv(ops_):
+                w.wait()
+        gu.copy_(new_gu)
+        dn.copy_(new_dn)
 
     def _add_norm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """residual += all_reduce(h); returns norm(residual) * w (fused collective for RMSNorm;

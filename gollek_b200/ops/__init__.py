@@ -464,7 +464,7 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
               e0: int = 0, e_loc: Optional[int] = None, renorm: bool = True,
               out: Optional[torch.Tensor] = None, scoring: str = "softmax", bias: Optional[torch.Tensor] = None,
               n_group: int = 1, topk_group: int = 1, scale: float = 1.0,
-              routing: Optional[dict] = None) -> torch.Tensor:
+              routing: Optional[dict] = None, expert_map: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Mixture-of-experts FFN over the local experts [e0, e0 + e_loc) of ``router.shape[0]``.
 
     w_gu [e_loc * 2F, H]: per expert, gate/up rows interleaved in groups of 64 (SwiGLU epilogue);
@@ -473,7 +473,9 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
     tensor-parallel all-reduce completes. Routing: softmax top-k (Mixtral), or with
     ``scoring="sigmoid"`` DeepSeek-V3's bias-corrected, group-limited choice (``bias`` fp32 [E],
     ``n_group`` / ``topk_group``) with weights times ``scale``. A ``routing`` dict receives the
-    chosen expert ids and weights ("ids" [T, k], "wts" [T, k])."""
+    chosen expert ids and weights ("ids" [T, k], "wts" [T, k]). ``expert_map`` (int32 [E]) places
+    logical expert e (router row e) in physical slot expert_map[e]: routing is computed over the
+    logical experts, the weights and the returned ids are physical (expert-parallel re-placement)."""
     route = dict(scoring=scoring, bias=bias, n_group=n_group, topk_group=topk_group, scale=scale)
     T, H = x.shape
     E = router.shape[0]
@@ -481,6 +483,8 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
     F_ = w_down.shape[1]
     if not x.is_cuda:
         ids, w = moe_route_ref(x, router, top_k, renorm, **route)
+        if expert_map is not None:
+            ids = expert_map.to(ids.device).long()[ids]
         if routing is not None:
             routing.update(ids=ids, wts=w)
         acc = torch.zeros(T, H, dtype=torch.float32)
@@ -514,7 +518,8 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
         yp = torch.empty(cap, H, dtype=x.dtype, device=dev)
         ypart = None
     C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, xp if yp is None else yp, ypart,
-                  top_k, renorm, e0, e_loc, 0 if scoring == "softmax" else 1, bias, n_group, topk_group, float(scale))
+                  top_k, renorm, e0, e_loc, 0 if scoring == "softmax" else 1, bias, n_group, topk_group, float(scale),
+                  expert_map)
     LAUNCHES.add(6)
     if routing is not None:
         routing.update(ids=ids.view(T, top_k), wts=wts.view(T, top_k))

@@ -45,3 +45,45 @@ def run_tp(rank, world, port, backend, comm_kind, prompts, max_tokens, result_q,
     except Exception as e:  # report to the parent instead of hanging it
         import traceback
         result_q.put((rank, None, traceback.format_exc()))
+
+
+def run_ep_rebalance(rank, world, port, prompts, max_tokens, result_q, model):
+    """EP engine on gloo: generate, force a skewed re-placement (experts moved between ranks), generate
+    again; then an engine that rebalances every step from its tracked loads."""
+    import torch.distributed as dist
+    import numpy as np
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        from gollek_b200.config import EngineConfig, preset
+        from gollek_b200.engine.engine import LLMEngine
+        from gollek_b200.engine.sequence import SamplingParams
+        from gollek_b200.models.reference import init_random_weights
+        from gollek_b200.parallel.dist import NcclComm, init_distributed
+        init_distributed(backend="gloo", timeout_s=60)
+        cfg = preset(model)
+        w = init_random_weights(cfg, seed=0)
+        sp = SamplingParams(temperature=0.0, max_tokens=max_tokens, ignore_eos=True)
+
+        def engine(interval=0):
+            ec = EngineConfig(device="cpu", dtype="float32", block_size=16, max_num_seqs=8,
+                              max_num_batched_tokens=256, max_model_len=512, use_cuda_graphs=False,
+                              tensor_parallel_size=world, enable_expert_parallel=True,
+                              ep_rebalance_interval=interval)
+            return LLMEngine(ec, model_cfg=cfg, weights=w.__getitem__, comm=NcclComm(rank, world), num_blocks=128)
+
+        eng = engine()
+        first = [o.output_token_ids for o in eng.generate(prompts, sp)]
+        E = cfg.num_local_experts
+        skew = {li: np.linspace(100.0, 1.0, E) for li, L in enumerate(eng.model.layers) if "moe_gu" in L}
+        rep = eng.model.rebalance_experts(loads=skew)
+        moved = sum(r["moved"] for r in rep.values())
+        second = [o.output_token_ids for o in eng.generate(prompts, sp)]
+        eng2 = engine(interval=1)
+        third = [o.output_token_ids for o in eng2.generate(prompts, sp)]
+        result_q.put((rank, (first, second, third, moved, len(eng2.ep_reports)), None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+        result_q.put((rank, None, traceback.format_exc()))
