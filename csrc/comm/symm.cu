@@ -82,34 +82,6 @@ GOLLEK_DEVICE void add_ranks(float* acc, const ArArgs& a, int64_t buf_off, int64
   }
 }
 
-// Two rows at once (world <= 4): acc0 += Σ_p buf_p[off], acc1 += Σ_p buf_p[off + stride], in rank
-// order, with all 2 * world loads issued before the first add.
-constexpr int kPairWorld = 4;
-GOLLEK_DEVICE void add_ranks2(float* acc0, float* acc1, const ArArgs& a, int64_t buf_off, int64_t off,
-                              int64_t stride) {
-  const int world = a.world;
-  uint4 v0[kPairWorld], v1[kPairWorld];
-#pragma unroll
-  for (int p = 0; p < kPairWorld; ++p)
-    if (p < world) {
-      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(a.bases[p] + buf_off) + off;
-      v0[p] = *reinterpret_cast<const uint4*>(b);
-      v1[p] = *reinterpret_cast<const uint4*>(b + stride);
-    }
-#pragma unroll
-  for (int p = 0; p < kPairWorld; ++p) {
-    if (p < world) {
-      float t[8];
-      bf16x8_to_float(v0[p], t);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc0[e] += t[e];
-      bf16x8_to_float(v1[p], t);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc1[e] += t[e];
-    }
-  }
-}
-
 __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __nv_bfloat16* __restrict__ residual,
                                                                     const __nv_bfloat16* __restrict__ w,
                                                                     __nv_bfloat16* __restrict__ x_out) {
@@ -144,24 +116,14 @@ __global__ void __launch_bounds__(kArThreads) tp_ar_rmsnorm_kernel(ArArgs a, __n
     const int chunk = (a.T + world - 1) / world;
     const int r0 = a.rank * chunk, r1 = min(a.T, r0 + chunk);
     __nv_bfloat16* gmine = reinterpret_cast<__nv_bfloat16*>(a.bases[a.rank] + a.gather_off);
-    // rows strided over the CTAs, vectors over the threads (no per-vector index division); with
-    // up to 4 ranks two rows per iteration, so 2 * world loads are in flight before the adds
-    const int rstep = world <= kPairWorld ? 2 : 1;
-    for (int row = r0 + rstep * blockIdx.x; row < r1; row += rstep * gridDim.x) {
-      const bool two = rstep == 2 && row + 1 < r1;
-      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-        const int64_t off = (int64_t)row * a.d + v * 8;
-        float acc[2][8];
-        bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), acc[0]);
-        if (two) {
-          bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off + a.d), acc[1]);
-          add_ranks2(acc[0], acc[1], a, a.partial_off[a.parity], off, a.d);
-          *reinterpret_cast<uint4*>(gmine + off + a.d) = float_to_bf16x8(acc[1]);
-        } else {
-          add_ranks(acc[0], a, a.partial_off[a.parity], off);
-        }
-        *reinterpret_cast<uint4*>(gmine + off) = float_to_bf16x8(acc[0]);
-      }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)(r1 - r0) * nvec;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int row = r0 + (int)(i / nvec), v = (int)(i % nvec);
+      const int64_t off = (int64_t)row * a.d + v * 8;
+      float acc[8];
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(residual + off), acc);
+      add_ranks(acc, a, a.partial_off[a.parity], off);
+      *reinterpret_cast<uint4*>(gmine + off) = float_to_bf16x8(acc);
     }
     // ---- barrier B: last local CTA signals every peer
     __syncthreads();
