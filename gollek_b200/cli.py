@@ -112,6 +112,42 @@ def cmd_quantize(args):
         print(f"wrote {args.dst} (fp8 e4m3, 128x128 block scales)")
 
 
+def cmd_dequantize(args):
+    """A GPTQ / AWQ 4-bit checkpoint directory -> dense bf16 safetensors (plus its config.json without
+    the quantization block), for tools that need plain weights."""
+    import shutil
+
+    import torch
+    from .loaders.safetensors import SafetensorsCheckpoint, save_sharded
+    from .quant.int4 import Int4Weight, quantized_checkpoint_getter
+    with open(os.path.join(args.src, "config.json")) as f:
+        hf = json.load(f)
+    qc = hf.get("quantization_config")
+    if not qc or qc.get("quant_method") not in ("awq", "gptq"):
+        raise SystemExit(f"{args.src}: no GPTQ/AWQ quantization_config in config.json")
+    ck = SafetensorsCheckpoint(args.src)
+    get = quantized_checkpoint_getter(ck, qc)
+    out, n_q = {}, 0
+    for k in ck.keys():
+        if k.endswith((".qzeros", ".scales", ".g_idx")):
+            continue
+        name = k[:-8] + ".weight" if k.endswith(".qweight") else k
+        v = get(name)
+        if isinstance(v, Int4Weight):
+            v, n_q = v.dequantize(torch.float32), n_q + 1
+        out[name] = v.to(torch.bfloat16) if v.is_floating_point() else v
+    os.makedirs(args.dst, exist_ok=True)
+    save_sharded(out, args.dst)
+    hf.pop("quantization_config")
+    hf["torch_dtype"] = "bfloat16"
+    with open(os.path.join(args.dst, "config.json"), "w") as f:
+        json.dump(hf, f, indent=1)
+    for extra in ("tokenizer.json", "tokenizer_config.json", "generation_config.json", "special_tokens_map.json"):
+        if os.path.exists(os.path.join(args.src, extra)):
+            shutil.copy(os.path.join(args.src, extra), args.dst)
+    print(f"wrote {args.dst}: {n_q} {qc['quant_method']} linears dequantized, {len(out)} tensors")
+
+
 def cmd_show(args):
     if args.model.endswith(".gguf"):
         from .loaders.gguf import GGUFFile, GGML_TYPES, config_from_gguf
@@ -186,6 +222,10 @@ def build_parser():
     q.add_argument("dst")
     q.add_argument("--type", default="Q4_K")
     q.set_defaults(fn=cmd_quantize)
+    dq = sub.add_parser("dequantize", help="GPTQ/AWQ checkpoint -> dense bf16 safetensors")
+    dq.add_argument("src")
+    dq.add_argument("dst")
+    dq.set_defaults(fn=cmd_dequantize)
     sh = sub.add_parser("show")
     sh.add_argument("model")
     sh.add_argument("--max-tensors", type=int, default=40)

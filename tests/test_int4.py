@@ -116,3 +116,34 @@ def test_int4_engine_gpu(tiny_cfg, tiny_weights):
         for i, tok in enumerate(o.output_token_ids):
             row = logits[len(p) - 1 + i]
             assert row[tok] >= row.max() - 0.05, (i, tok)
+
+
+def test_cli_dequantize_awq_checkpoint(tmp_path):
+    """``gollek dequantize``: an AWQ checkpoint directory becomes dense bf16 safetensors whose
+    weights equal the 4-bit values, with unquantized tensors copied and the quant block removed."""
+    import json
+
+    from gollek_b200.cli import main
+    from gollek_b200.loaders.safetensors import SafetensorsCheckpoint, save_file
+    K, N, g = 256, 64, 128
+    codes = _rand_codes((K, N), 11)
+    zeros = torch.randint(1, 16, (K // g, N), generator=torch.Generator().manual_seed(12))
+    scales = (torch.rand(K // g, N, generator=torch.Generator().manual_seed(13)) * 0.02 + 0.001).half()
+    ref = ((codes.float() - zeros.float().repeat_interleave(g, 0)) * scales.float().repeat_interleave(g, 0)).t()
+    src, dst = tmp_path / "awq", tmp_path / "dense"
+    src.mkdir()
+    norm = torch.rand(K)
+    save_file({"model.layers.0.mlp.up_proj.qweight": I4._pack_words(codes, I4.AWQ_ORDER),
+               "model.layers.0.mlp.up_proj.qzeros": I4._pack_words(zeros, I4.AWQ_ORDER),
+               "model.layers.0.mlp.up_proj.scales": scales,
+               "model.layers.0.input_layernorm.weight": norm}, str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps({"model_type": "llama", "quantization_config": {
+        "quant_method": "awq", "bits": 4, "group_size": g, "version": "gemm"}}))
+    main(["dequantize", str(src), str(dst)])
+    ck = SafetensorsCheckpoint(str(dst))
+    assert sorted(ck.keys()) == ["model.layers.0.input_layernorm.weight", "model.layers.0.mlp.up_proj.weight"]
+    w = ck.get("model.layers.0.mlp.up_proj.weight")
+    assert w.dtype == torch.bfloat16 and w.shape == (N, K)
+    torch.testing.assert_close(w.float(), ref, rtol=1e-2, atol=1e-4)
+    torch.testing.assert_close(ck.get("model.layers.0.input_layernorm.weight").float(), norm, rtol=1e-2, atol=1e-3)
+    assert "quantization_config" not in json.loads((dst / "config.json").read_text())
