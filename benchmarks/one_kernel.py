@@ -9,6 +9,7 @@
 from __future__ import annotations
 
 import argparse
+import json
 import math
 import os
 import sys
@@ -21,7 +22,7 @@ from gollek_b200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "gdn"])
+    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -50,6 +51,33 @@ def main():
         dn = (torch.randn(a.e_loc * H, F, device=dev) * 0.02).bfloat16()
         for _ in range(a.reps):
             ops.fused_moe(x, router, gu, dn, 2, e0=0, e_loc=a.e_loc)
+    elif a.kind == "moe_ds":
+        # one expert-parallel rank (EP8) of a DeepSeek-V3 MoE layer: 32 of 256 experts, H 7168, expert
+        # FFN 2048, top-8 sigmoid routing with correction bias inside the 4 best of 8 expert groups
+        H, F, E, k = 7168, 2048, 256, 8
+        el = a.e_loc if a.e_loc != 8 else 32
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(a.T, H, device=dev, generator=g).bfloat16()
+        router = (torch.randn(E, H, device=dev, generator=g) * 0.02).bfloat16()
+        bias = torch.randn(E, device=dev, generator=g) * 0.01
+        gu = (torch.randn(el * 2 * F, H, device=dev, generator=g) * 0.02).bfloat16()
+        dn = (torch.randn(el * H, F, device=dev, generator=g) * 0.02).bfloat16()
+        opt = dict(scoring="sigmoid", bias=bias, n_group=8, topk_group=4, scale=2.5)
+        rt = {}
+        ops.fused_moe(x, router, gu, dn, k, e0=0, e_loc=el, routing=rt, **opt)
+        rows = int(((rt["ids"] >= 0) & (rt["ids"] < el)).sum())
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(a.reps):
+            ops.fused_moe(x, router, gu, dn, k, e0=0, e_loc=el, **opt)
+        ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / a.reps
+        wbytes = (gu.numel() + dn.numel()) * 2
+        print(json.dumps({"kind": "moe_ds", "T": a.T, "e_loc": el, "local_rows": rows, "ms": round(ms, 4),
+                          "weight_GBps": round(wbytes / ms / 1e6, 1),
+                          "expert_TFLOPs": round(6 * rows * H * F / ms / 1e9, 1)}))
     elif a.kind == "gdn":
         Hg, D = 32, 128
         T = a.nseq * a.L
