@@ -239,6 +239,8 @@ def build_parser():
 
 
 def main(argv=None):
+    from .utils.log import configure_logging
+    configure_logging()
     args = build_parser().parse_args(argv)
     args.fn(args)
 
