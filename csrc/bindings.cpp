@@ -245,7 +245,7 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
                      torch::Tensor xp, torch::Tensor hp, torch::Tensor yp, c10::optional<torch::Tensor> ypart,
                      int64_t topk, bool renorm, int64_t e0, int64_t e_loc, int64_t scoring,
                      c10::optional<torch::Tensor> score_bias, int64_t n_group, int64_t topk_group, double scale,
-                     c10::optional<torch::Tensor> expert_map) {
+                     c10::optional<torch::Tensor> expert_map, c10::optional<torch::Tensor> logits) {
   for (auto* t : {&out, &x, &router, &w_gu, &w_down, &xp, &hp, &yp}) check_bf16(*t, "moe operand");
   MoeRouting rt;
   rt.scoring = (int)scoring;
@@ -263,6 +263,12 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
                     expert_map->numel() == router.size(0),
                 "moe: expert map must be int32 [E] on the device (logical expert -> physical slot)");
     rt.expert_map = expert_map->data_ptr<int>();
+  }
+  if (logits.has_value()) {
+    TORCH_CHECK(logits->is_cuda() && logits->scalar_type() == at::kFloat && logits->is_contiguous() &&
+                    logits->numel() >= (int64_t)x.size(0) * router.size(0),
+                "moe: router logits scratch must be fp32 [T, E] on the device");
+    rt.logits = logits->data_ptr<float>();
   }
   check_same_device(x, w_gu);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "moe: x/out row-major [T, H]");
@@ -664,7 +670,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ids"), py::arg("wts"), py::arg("dest"), py::arg("xp"), py::arg("hp"), py::arg("yp"),
         py::arg("ypart"), py::arg("topk"), py::arg("renorm"), py::arg("e0"), py::arg("e_loc"),
         py::arg("scoring") = 0, py::arg("score_bias") = py::none(), py::arg("n_group") = 1,
-        py::arg("topk_group") = 1, py::arg("scale") = 1.0, py::arg("expert_map") = py::none());
+        py::arg("topk_group") = 1, py::arg("scale") = 1.0, py::arg("expert_map") = py::none(),
+        py::arg("logits") = py::none());
   m.def("moe_capacity_rows", &moe_capacity_rows);
   m.def("int4_gemv", &int4_gemv_py, "4-bit group-quantized GEMV (GPTQ/AWQ/NF4), optional SwiGLU");
   m.def("int4_dequant", &int4_dequant_py, "4-bit group-quantized weights to bf16");

@@ -107,6 +107,7 @@ struct MoeRouting {
   int topk_group = 1;
   float scale = 1.f;
   const int* expert_map = nullptr;  // logical expert -> physical slot (expert-parallel re-placement)
+  float* logits = nullptr;          // fp32 [T, E] scratch: when set, logits are computed on tensor cores first
 };
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,

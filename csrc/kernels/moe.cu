@@ -1,6 +1,8 @@
 // K12: MoE routing and token permutation, plus the expert combine (sm_100a).
 //
-//   moe_route    router logits x·Wrᵀ (fp32 accumulate, E ≤ 256), then one warp per token scores
+//   moe_logits   (E >= 32) router logits x·Wrᵀ on tensor cores (mma m16n8k16, fp32 accumulation)
+//   moe_route    router logits x·Wrᵀ (fp32 accumulate, E ≤ 256; read from moe_logits when it ran),
+//                then one warp per token scores
 //                and picks its top-k (k ≤ 8, ties to the lower expert id): softmax scores with
 //                optional renormalisation of the k weights (Mixtral), or sigmoid scores whose
 //                choice adds a per-expert correction bias, limited to the topk_group best of n_group
@@ -40,6 +42,81 @@ constexpr int kPerLane = kMaxE / 32;  // expert e = lane + 32 i is scored by lan
 
 constexpr int kRouteTok = 4;  // tokens per routing CTA
 
+// Router logits on tensor cores for many experts: logits[t, e] = x[t, :] . Wr[e, :] (bf16 operands,
+// fp32 accumulation, fixed summation order per element). CTA = 64 tokens x 64 experts; per 64-wide
+// K chunk both tiles are staged in shared memory with 16-byte loads (the next chunk prefetched into
+// registers) and warp w multiplies its 16 tokens against the 64 experts with mma m16n8k16.
+constexpr int kLgTile = 64, kLgK = 64, kLgPad = kLgK + 8;
+
+__device__ __forceinline__ void mma_bf16_16816(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__global__ void __launch_bounds__(128) moe_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                         const __nv_bfloat16* __restrict__ wr, int T, int H, int E,
+                                                         float* __restrict__ logits) {
+  __shared__ __align__(16) __nv_bfloat16 xs[kLgTile][kLgPad];
+  __shared__ __align__(16) __nv_bfloat16 ws[kLgTile][kLgPad];
+  const int t0 = blockIdx.x * kLgTile, e0 = blockIdx.y * kLgTile;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
+  float c[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+  uint4 xv[4], wv[4];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = tid + 128 * u, r = i >> 3, v = i & 7;
+      xv[u] = t0 + r < T ? *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + r) * ldx + k0 + 8 * v)
+                         : make_uint4(0, 0, 0, 0);
+      wv[u] = e0 + r < E ? *reinterpret_cast<const uint4*>(wr + (int64_t)(e0 + r) * H + k0 + 8 * v)
+                         : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load(0);
+  for (int k0 = 0; k0 < H; k0 += kLgK) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = tid + 128 * u, r = i >> 3, v = i & 7;
+      *reinterpret_cast<uint4*>(&xs[r][8 * v]) = xv[u];
+      *reinterpret_cast<uint4*>(&ws[r][8 * v]) = wv[u];
+    }
+    __syncthreads();
+    if (k0 + kLgK < H) load(k0 + kLgK);
+    if (t0 + warp * 16 < T) {
+#pragma unroll
+      for (int kk = 0; kk < kLgK; kk += 16) {
+        uint32_t a[4];
+        a[0] = *reinterpret_cast<const uint32_t*>(&xs[warp * 16 + g][kk + 2 * q]);
+        a[1] = *reinterpret_cast<const uint32_t*>(&xs[warp * 16 + g + 8][kk + 2 * q]);
+        a[2] = *reinterpret_cast<const uint32_t*>(&xs[warp * 16 + g][kk + 8 + 2 * q]);
+        a[3] = *reinterpret_cast<const uint32_t*>(&xs[warp * 16 + g + 8][kk + 8 + 2 * q]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t b[2];
+          b[0] = *reinterpret_cast<const uint32_t*>(&ws[8 * j + g][kk + 2 * q]);
+          b[1] = *reinterpret_cast<const uint32_t*>(&ws[8 * j + g][kk + 8 + 2 * q]);
+          mma_bf16_16816(c[j], a, b);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int r0 = t0 + warp * 16 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = e0 + 8 * j + 2 * q;
+    if (e < E) {  // E is even (checked by the launcher), so e + 1 < E too
+      if (r0 < T) *reinterpret_cast<float2*>(logits + (int64_t)r0 * E + e) = make_float2(c[j][0], c[j][1]);
+      if (r1 < T) *reinterpret_cast<float2*>(logits + (int64_t)r1 * E + e) = make_float2(c[j][2], c[j][3]);
+    }
+  }
+}
+
 // Routing: one CTA per 4 tokens. All 256 threads split the hidden dimension (8 elements each per
 // 2048-wide stripe) and accumulate the 4 tokens x 8 experts of the current expert chunk, so the
 // router weights are read once per CTA and every thread has many independent loads in flight;
@@ -54,7 +131,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTok;
   const int ntok = min(kRouteTok, T - t0);
-  for (int ec = 0; ec < E; ec += 8) {
+  if (rt.logits != nullptr) {  // logits computed by moe_logits_kernel
+    for (int i = threadIdx.x; i < ntok * E; i += blockDim.x) s_logit[i / E][i % E] = rt.logits[(int64_t)t0 * E + i];
+    __syncthreads();
+  }
+  for (int ec = 0; ec < (rt.logits != nullptr ? 0 : E); ec += 8) {
     float acc[kRouteTok][8];
 #pragma unroll
     for (int a = 0; a < kRouteTok; ++a)
@@ -357,6 +438,12 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   if (T == 0) return;
   const int cap = moe_capacity_rows(T, topk, e_loc);
   auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  if (rt.logits != nullptr) {
+    throw_if(E % 2 != 0, "moe: the tensor-core router needs an even expert count");
+    moe_logits_kernel<<<dim3((T + kLgTile - 1) / kLgTile, (E + kLgTile - 1) / kLgTile), 128, 0, s>>>(
+        xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, rt.logits);
+    check_launch("moe_logits");
+  }
   moe_route_kernel<<<(T + kRouteTok - 1) / kRouteTok, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
                                                renorm, e0, e_loc, rt, ids, wts, ws);
   check_launch("moe_route");

@@ -460,6 +460,9 @@ def moe_route_ref(x: torch.Tensor, router: torch.Tensor, top_k: int, renorm: boo
     return ref.moe_route(x.float() @ router.float().t(), top_k, renorm, **route)
 
 
+MOE_TC_ROUTER_MIN_EXPERTS = 32
+
+
 def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, top_k: int,
               e0: int = 0, e_loc: Optional[int] = None, renorm: bool = True,
               out: Optional[torch.Tensor] = None, scoring: str = "softmax", bias: Optional[torch.Tensor] = None,
@@ -511,6 +514,8 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
     xp = torch.empty(cap, H, dtype=x.dtype, device=dev)
     hp = torch.empty(cap, F_, dtype=x.dtype, device=dev)
     _, _, splits = C.moe_plan(T, top_k, E, e_loc, H, F_)
+    # many experts: the router GEMM (T x E x H) runs on tensor cores into an fp32 scratch first
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if E >= MOE_TC_ROUTER_MIN_EXPERTS else None
     if splits > 1:  # down projection split over K: fp32 partials summed by the combine kernel
         yp = None
         ypart = torch.empty(splits * cap * H, dtype=torch.float32, device=dev)
@@ -519,8 +524,8 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
         ypart = None
     C.moe_forward(out, x, router, w_gu, w_down, ws, ids, wts, dest, xp, hp, xp if yp is None else yp, ypart,
                   top_k, renorm, e0, e_loc, 0 if scoring == "softmax" else 1, bias, n_group, topk_group, float(scale),
-                  expert_map)
-    LAUNCHES.add(6)
+                  expert_map, logits)
+    LAUNCHES.add(7 if logits is not None else 6)
     if routing is not None:
         routing.update(ids=ids.view(T, top_k), wts=wts.view(T, top_k))
     return out
