@@ -35,7 +35,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def parse(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("--workload", required=True, choices=["llama70b-fp8", "mixtral-ep", "gguf-lora"])
+    p.add_argument("--workload", required=True, choices=["llama70b-fp8", "mixtral-ep", "deepseek-ep", "gguf-lora"])
     p.add_argument("--model", default=None, help="preset override (small runs)")
     p.add_argument("--layers", type=int, default=0, help="override the layer count (small runs)")
     p.add_argument("--ffn", type=int, default=0, help="override the FFN width (small runs)")
@@ -151,7 +151,9 @@ def mixtral_ep(args, di, comm):
     from gollek_b200.config import preset
     from gollek_b200.engine.sequence import SamplingParams
     cuda = args.device == "cuda"
-    mcfg = preset(args.model or "mixtral-8x7b")
+    ds = args.workload == "deepseek-ep"
+    mcfg = preset(args.model or ("deepseek-v3" if ds else "mixtral-8x7b"))
+    name = "deepseek-v3-ep" if ds else "mixtral-ep"
     if args.layers:
         mcfg.num_hidden_layers = args.layers
     if args.ffn:
@@ -171,7 +173,7 @@ def mixtral_ep(args, di, comm):
                                                                          ignore_eos=True))
     with DeviceTimer(cuda) as t:
         _run_until_done(eng, ids)
-    _emit(di.rank, {"workload": "mixtral-ep-prefill", "n_gpus": di.world_size, "sequences": n_pf, "prompt": L,
+    _emit(di.rank, {"workload": f"{name}-prefill", "layers": mcfg.num_hidden_layers, "n_gpus": di.world_size, "sequences": n_pf, "prompt": L,
                     "ms": round(t.ms, 2), "prefill_tok_s": round(n_pf * L / t.ms * 1e3, 1), "dtype": "bf16",
                     "parallelism": f"ep{di.world_size}+tp{di.world_size}", "data": "synthetic, random-init"})
     sp = SamplingParams(temperature=0.0, max_tokens=steps + 16, ignore_eos=True)
@@ -181,7 +183,7 @@ def mixtral_ep(args, di, comm):
         eng.step()
     with DeviceTimer(cuda) as t:
         n = sum(len(eng.step()) for _ in range(steps))
-    _emit(di.rank, {"workload": "mixtral-ep-decode", "n_gpus": di.world_size, "batch": B, "steps": steps,
+    _emit(di.rank, {"workload": f"{name}-decode", "layers": mcfg.num_hidden_layers, "n_gpus": di.world_size, "batch": B, "steps": steps,
                     "tokens": n, "ms": round(t.ms, 2), "tok_s": round(n / t.ms * 1e3, 1),
                     "tpot_ms": round(t.ms / steps, 3), "dtype": "bf16",
                     "parallelism": f"ep{di.world_size}+tp{di.world_size}", "data": "synthetic, random-init"})
@@ -274,12 +276,14 @@ def main(argv=None):
             from gollek_b200.config import preset
             from gollek_b200.parallel.dist import cpu_group
             from gollek_b200.parallel.symm import FusedTPComm
-            default = {"llama70b-fp8": "llama-3-70b", "mixtral-ep": "mixtral-8x7b", "gguf-lora": "llama-3-8b"}
+            default = {"llama70b-fp8": "llama-3-70b", "mixtral-ep": "mixtral-8x7b", "deepseek-ep": "deepseek-v3",
+                       "gguf-lora": "llama-3-8b"}
             hidden = preset(args.model or default[args.workload]).hidden_size
             comm = FusedTPComm(di.rank, di.world_size, max_tokens=8192 + 256, hidden=hidden, cpu_group=cpu_group())
         else:
             comm = NcclComm(di.rank, di.world_size)
-    {"llama70b-fp8": llama70b_fp8, "mixtral-ep": mixtral_ep, "gguf-lora": gguf_lora}[args.workload](args, di, comm)
+    {"llama70b-fp8": llama70b_fp8, "mixtral-ep": mixtral_ep, "deepseek-ep": mixtral_ep,
+     "gguf-lora": gguf_lora}[args.workload](args, di, comm)
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -15,6 +15,8 @@ import config_bench  # noqa: E402
      ["llama70b-fp8-decode"] + ["llama70b-fp8-prefill"] * 3),
     (["--workload", "mixtral-ep", "--model", "tiny-mixtral", "--scale", "0.02"],
      ["mixtral-ep-prefill", "mixtral-ep-decode"]),
+    (["--workload", "deepseek-ep", "--model", "tiny-deepseek-v3", "--scale", "0.02"],
+     ["deepseek-v3-ep-prefill", "deepseek-v3-ep-decode"]),
 ])
 def test_workloads_run(argv, expect, capsys):
     config_bench.main(argv + ["--device", "cpu"])
