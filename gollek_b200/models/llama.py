@@ -545,7 +545,7 @@ class LlamaModel:
         n = sum(nb(x) for x in (self.embed, self.norm, self.lm_head))
         for L in self.layers:
             for k, v in L.items():
-                if v is None:  # offloaded: lives in host memory
+                if v is None or isinstance(v, (bool, int, float)):  # offloaded (host memory) or a layer flag
                     continue
                 if k == "experts":
                     n += sum(nb(a) + nb(b) for a, b in v)
