@@ -133,10 +133,11 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(
         ss += x1[i].x * x1[i].x + x1[i].y * x1[i].y + x2[i].x * x2[i].x + x2[i].y * x2[i].y;
       }
     }
-    // pass-through dims [rot, D): at most 2 pairs per lane (D - rot <= 128)
-    float2 xp[2];
+    // pass-through dims [rot, D): at most kPass pairs per lane (D - rot <= 64 * kPass = 256)
+    constexpr int kPass = 4;
+    float2 xp[kPass];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kPass; ++i) {
       const int e = rot + 2 * lane + 64 * i;
       if (e < D) {
         xp[i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + e));
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(
       }
     }
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kPass; ++i) {
       const int e = rot + 2 * lane + 64 * i;
       if (e < D) {
         if (nw) {
@@ -271,8 +272,8 @@ void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, co
                           int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,
                           int rot, cudaStream_t s) {
   throw_if(D % 16 != 0 || D > 256, "rope_kv_write: head_dim must be a multiple of 16, <= 256");
-  throw_if(rot % 4 != 0 || rot > D || D - rot > 128, "rope_kv_write: rotary dims must be a multiple of 4, "
-                                                     "<= head_dim, with at most 128 pass-through dims");
+  throw_if(rot % 4 != 0 || rot > D || D - rot > 256, "rope_kv_write: rotary dims must be a multiple of 4, "
+                                                     "<= head_dim, with at most 256 pass-through dims");
   if (T == 0) return;
   rope_kv_write_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(q_out),
                                          reinterpret_cast<const __nv_bfloat16*>(qkv), positions, cos_sin,

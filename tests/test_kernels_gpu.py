@@ -329,7 +329,8 @@ def test_attention_window_softcap(H, Hk, D, tc, window, softcap):
 
 
 @pytest.mark.parametrize("D,rot,bias,qkn", [(128, 128, True, False), (128, 128, False, True), (64, 64, True, True),
-                                            (128, 96, False, False), (256, 256, False, True), (32, 32, True, False)])
+                                            (128, 96, False, False), (256, 256, False, True), (32, 32, True, False),
+                                            (256, 64, False, False), (128, 32, False, False)])
 def test_rope_bias_qknorm_partial(D, rot, bias, qkn):
     from gollek_b200.config import preset
     from gollek_b200.models.reference import rope_cos_sin
