@@ -266,8 +266,9 @@ void moe_forward_out(torch::Tensor out, torch::Tensor x, torch::Tensor router, t
   }
   if (logits.has_value()) {
     TORCH_CHECK(logits->is_cuda() && logits->scalar_type() == at::kFloat && logits->is_contiguous() &&
-                    logits->numel() >= (int64_t)x.size(0) * router.size(0),
-                "moe: router logits scratch must be fp32 [T, E] on the device");
+                    logits->numel() >= (int64_t)moe_logit_splits(x.size(0), router.size(0), x.size(1)) *
+                                           x.size(0) * router.size(0),
+                "moe: router logits scratch must be fp32 [moe_logit_splits(T, E, H), T, E] on the device");
     rt.logits = logits->data_ptr<float>();
   }
   check_same_device(x, w_gu);
@@ -680,6 +681,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_gated_norm", &gdn_gated_norm_py, "RMSNorm(o) * w * silu(g) per head");
   m.def("kv_key_norms", &kv_key_norms_py, "mean key L2 norm of each listed KV block (eviction scoring, K15)");
   m.def("moe_ws_ints", &moe_ws_ints);
+  m.def("moe_logit_splits", &moe_logit_splits, "K splits of the tensor-core router logits for (T, E, H)");
   m.def("moe_plan", &moe_plan_py, "(gate/up tile width, down tile width, down split-K) for a MoE call");
   m.def("argmax", &argmax_out, "greedy argmax (K11)");
   m.def("apply_penalties", &apply_penalties_, "repetition/frequency/presence penalties (K11)");

@@ -107,8 +107,10 @@ struct MoeRouting {
   int topk_group = 1;
   float scale = 1.f;
   const int* expert_map = nullptr;  // logical expert -> physical slot (expert-parallel re-placement)
-  float* logits = nullptr;          // fp32 [T, E] scratch: when set, logits are computed on tensor cores first
+  float* logits = nullptr;          // fp32 [splits, T, E] scratch: when set, logits are computed on tensor cores first
+  int logit_splits = 1;             // set by the launcher (moe_logit_splits)
 };
+int moe_logit_splits(int T, int E, int H);
 void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, const void* wr, const void* w_gu,
                         const void* w_down, int* ws, int* ids, float* wts, int* dest, void* xp, void* hp, void* yp,
                         float* ypart, int T, int H, int F, int E, int topk, int renorm, int e0, int e_loc,

@@ -58,7 +58,10 @@ __device__ __forceinline__ void mma_bf16_16816(float* d, const uint32_t* a, cons
 
 __global__ void __launch_bounds__(128) moe_logits_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                          const __nv_bfloat16* __restrict__ wr, int T, int H, int E,
-                                                         float* __restrict__ logits) {
+                                                         float* __restrict__ logits, int kchunk) {
+  // blockIdx.z: a K range of kchunk elements; its partial logits go to slab z of [splits, T, E]
+  logits += (int64_t)blockIdx.z * T * E;
+  const int kb = blockIdx.z * kchunk, ke = min(H, kb + kchunk);
   __shared__ __align__(16) __nv_bfloat16 xs[kLgTile][kLgPad];
   __shared__ __align__(16) __nv_bfloat16 ws[kLgTile][kLgPad];
   const int t0 = blockIdx.x * kLgTile, e0 = blockIdx.y * kLgTile;
@@ -77,8 +80,8 @@ __global__ void __launch_bounds__(128) moe_logits_kernel(const __nv_bfloat16* __
                          : make_uint4(0, 0, 0, 0);
     }
   };
-  load(0);
-  for (int k0 = 0; k0 < H; k0 += kLgK) {
+  if (kb < ke) load(kb);  // an empty trailing split writes zeros
+  for (int k0 = kb; k0 < ke; k0 += kLgK) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int i = tid + 128 * u, r = i >> 3, v = i & 7;
@@ -86,7 +89,7 @@ __global__ void __launch_bounds__(128) moe_logits_kernel(const __nv_bfloat16* __
       *reinterpret_cast<uint4*>(&ws[r][8 * v]) = wv[u];
     }
     __syncthreads();
-    if (k0 + kLgK < H) load(k0 + kLgK);
+    if (k0 + kLgK < ke) load(k0 + kLgK);
     if (t0 + warp * 16 < T) {
 #pragma unroll
       for (int kk = 0; kk < kLgK; kk += 16) {
@@ -131,8 +134,12 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const __nv_bfloat16* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTok;
   const int ntok = min(kRouteTok, T - t0);
-  if (rt.logits != nullptr) {  // logits computed by moe_logits_kernel
-    for (int i = threadIdx.x; i < ntok * E; i += blockDim.x) s_logit[i / E][i % E] = rt.logits[(int64_t)t0 * E + i];
+  if (rt.logits != nullptr) {  // logits computed by moe_logits_kernel: its K-split partials, added in order
+    for (int i = threadIdx.x; i < ntok * E; i += blockDim.x) {
+      float v = 0.f;
+      for (int z = 0; z < rt.logit_splits; ++z) v += rt.logits[(int64_t)z * T * E + (int64_t)t0 * E + i];
+      s_logit[i / E][i % E] = v;
+    }
     __syncthreads();
   }
   for (int ec = 0; ec < (rt.logits != nullptr ? 0 : E); ec += 8) {
@@ -401,6 +408,14 @@ int moe_capacity_rows(int T, int topk, int e_loc) {
   return (int)((rows + 127) / 128 * 128);
 }
 
+// K splits of the tensor-core router: about four 64 x 64 tiles per SM, each split at least four
+// 64-wide K chunks long.
+int moe_logit_splits(int T, int E, int H) {
+  const int tiles = ((T + kLgTile - 1) / kLgTile) * ((E + kLgTile - 1) / kLgTile);
+  const int want = (4 * num_sms() + tiles - 1) / tiles;
+  return std::max(1, std::min(want, H / kLgK / 4));
+}
+
 int moe_ws_ints(int T, int topk, int e_loc) { return kWsTiles + moe_capacity_rows(T, topk, e_loc) / 128; }
 
 // Tile widths of the two grouped GEMMs and the down GEMM's split-K factor, from the expected live
@@ -438,14 +453,17 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   if (T == 0) return;
   const int cap = moe_capacity_rows(T, topk, e_loc);
   auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  MoeRouting rr = rt;
   if (rt.logits != nullptr) {
     throw_if(E % 2 != 0, "moe: the tensor-core router needs an even expert count");
-    moe_logits_kernel<<<dim3((T + kLgTile - 1) / kLgTile, (E + kLgTile - 1) / kLgTile), 128, 0, s>>>(
-        xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, rt.logits);
+    rr.logit_splits = moe_logit_splits(T, E, H);
+    const int kchunk = (H / kLgK + rr.logit_splits - 1) / rr.logit_splits * kLgK;
+    moe_logits_kernel<<<dim3((T + kLgTile - 1) / kLgTile, (E + kLgTile - 1) / kLgTile, rr.logit_splits), 128, 0,
+                        s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, rt.logits, kchunk);
     check_launch("moe_logits");
   }
   moe_route_kernel<<<(T + kRouteTok - 1) / kRouteTok, 256, 0, s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk,
-                                               renorm, e0, e_loc, rt, ids, wts, ws);
+                                               renorm, e0, e_loc, rr, ids, wts, ws);
   check_launch("moe_route");
   moe_plan_kernel<<<1, 32, 0, s>>>(ws, e_loc, cap / 128);
   check_launch("moe_plan");

@@ -515,7 +515,8 @@ def fused_moe(x: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down:
     hp = torch.empty(cap, F_, dtype=x.dtype, device=dev)
     _, _, splits = C.moe_plan(T, top_k, E, e_loc, H, F_)
     # many experts: the router GEMM (T x E x H) runs on tensor cores into an fp32 scratch first
-    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if E >= MOE_TC_ROUTER_MIN_EXPERTS else None
+    logits = (torch.empty(C.moe_logit_splits(T, E, H), T, E, dtype=torch.float32, device=dev)
+              if E >= MOE_TC_ROUTER_MIN_EXPERTS else None)
     if splits > 1:  # down projection split over K: fp32 partials summed by the combine kernel
         yp = None
         ypart = torch.empty(splits * cap * H, dtype=torch.float32, device=dev)
