@@ -565,7 +565,7 @@ class EngineConfig:
     """Serving-engine configuration (one dataclass for everything the engine tunes)."""
     model: str = "tiny-llama"                 # preset name or checkpoint path
     dtype: str = "bfloat16"
-    quantization: str = "none"                # none | fp8 | gguf | int4 | nf4 (GPTQ/AWQ checkpoints: automatic)
+    quantization: str = "none"                # none | fp8 | int8 | gguf | int4 | nf4 (GPTQ/AWQ checkpoints: automatic)
     device: str = "cuda"
     tensor_parallel_size: int = 1
     enable_expert_parallel: bool = False  # MoE: experts partitioned over the TP ranks (EP = TP size)

@@ -62,6 +62,8 @@ class LLMEngine:
                 self.model.quantize_fp8()
             elif cfg.quantization in ("int4", "nf4"):
                 self.model.quantize_int4(cfg.quantization)
+            elif cfg.quantization == "int8":
+                self.model.quantize_int8()
         if cfg.offload_layers > 0 and self.device.type == "cuda":
             self.model.enable_offload(cfg.offload_layers, cfg.offload_prefetch)
             cfg.use_cuda_graphs = False

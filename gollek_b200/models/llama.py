@@ -520,6 +520,22 @@ class LlamaModel:
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
 
+    def quantize_int8(self) -> None:
+        """Weight-only int8: the dense linear weights become Q8_0 blocks (32 int8 values with one fp16
+        scale, symmetric round-to-nearest), served by the Q8_0 dequant-fused GEMV for small batches
+        and by in-L2 dequant + tcgen05 GEMM for large ones. Quantized on the host, layer by layer."""
+        from ..native import host_ext
+        from ..quant.gguf_weights import GGML_Q8_0, QWeight
+        h = host_ext()
+        for L in self.layers:
+            for k in _DENSE_KEYS:
+                v = L.get(k)
+                if isinstance(v, torch.Tensor) and v.shape[1] % 32 == 0:
+                    raw = h.quantize_q8_0(v.float().cpu().reshape(-1).contiguous())
+                    L[k] = QWeight(raw.to(v.device), v.shape[0], v.shape[1], GGML_Q8_0)
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
     def quantize_fp8(self) -> None:
         """Convert the linear weights (qkv, o, gate/up, down; experts too) to block-scaled FP8, layer by
         layer so the bf16 copies are released as it goes. Embedding, norms and lm_head stay bf16."""
