@@ -51,3 +51,37 @@ def test_clip_text_encoder_gpu():
         ref = m(input_ids=ids)
     torch.testing.assert_close(ours["last_hidden_state"].float().cpu(), ref.last_hidden_state, rtol=5e-2, atol=5e-2)
     torch.testing.assert_close(ours["text_embeds"].float().cpu(), ref.text_embeds, rtol=5e-2, atol=5e-2)
+
+
+def _hf_vision():
+    import transformers
+    vc = transformers.CLIPVisionConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                                       num_attention_heads=4, image_size=28, patch_size=7, projection_dim=32,
+                                       hidden_act="quick_gelu")
+    torch.manual_seed(0)
+    return vc, transformers.CLIPVisionModelWithProjection(vc).eval()
+
+
+def test_clip_vision_encoder_matches_hf():
+    from gollek_b200.models.clip import CLIPVisionConfig, CLIPVisionEncoder
+    vc, m = _hf_vision()
+    px = torch.randn(2, 3, 28, 28, generator=torch.Generator().manual_seed(2))
+    enc = CLIPVisionEncoder(CLIPVisionConfig.from_hf(vc.to_dict()), m.state_dict().__getitem__, device="cpu",
+                            dtype=torch.float32)
+    ours = enc.encode(px)
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    torch.testing.assert_close(ours["last_hidden_state"], ref.last_hidden_state, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(ours["image_embeds"], ref.image_embeds, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_clip_vision_encoder_gpu():
+    from gollek_b200.models.clip import CLIPVisionConfig, CLIPVisionEncoder
+    vc, m = _hf_vision()
+    px = torch.randn(2, 3, 28, 28, generator=torch.Generator().manual_seed(2))
+    enc = CLIPVisionEncoder(CLIPVisionConfig.from_hf(vc.to_dict()), m.state_dict().__getitem__, device="cuda")
+    ours = enc.encode(px)
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    torch.testing.assert_close(ours["image_embeds"].float().cpu(), ref.image_embeds, rtol=5e-2, atol=5e-2)
