@@ -22,6 +22,7 @@ from __future__ import annotations
 import asyncio
 import contextvars
 import json
+import re
 import os
 import time
 import uuid
@@ -262,6 +263,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
     from .rag import RagStore
     st.rag = RagStore()
+    from .plugins import ServerPlugins, UnsafeContent, redact_pii, split_reasoning
+    st.plugins = ServerPlugins.from_env()
     gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
     app = FastAPI(title="gollek-b200", version="0.1")
     app.state.server = st
@@ -549,12 +552,37 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             if rx and not (sp.guided_json or sp.guided_regex):
                 sp.guided_regex = rx  # a forced call: the output is constrained to the call's shape
         rag_sources = None
-        messages = req.messages
+        pl = st.plugins
+        info: Dict[str, Any] = {}
+        messages = [m if isinstance(m, dict) else m.model_dump(exclude_none=True) for m in req.messages]
+        if pl.safety is not None or pl.pii_redaction:  # request plugins: content safety, then PII redaction
+            for m in messages:
+                c = m.get("content")
+                if m.get("role") != "user" or not isinstance(c, str):
+                    continue
+                if pl.safety is not None:
+                    try:
+                        pl.safety.check(c)
+                    except UnsafeContent as e:
+                        raise HTTPException(400, str(e))
+                if pl.pii_redaction:
+                    m["content"], k = redact_pii(c)
+                    info["pii_redactions"] = info.get("pii_redactions", 0) + k
         if req.rag:
-            messages, rag_sources = await rag_augment(
-                [m if isinstance(m, dict) else m.model_dump(exclude_none=True) for m in req.messages], req.rag)
+            messages, rag_sources = await rag_augment(messages, req.rag)
         prompt = chat_prompt(messages, tools)
         cid = "chatcmpl-" + uuid.uuid4().hex
+        cache_key = qvec = None
+        if (pl.semantic_cache is not None and not (req.stream or force_stream) and not tools
+                and sp.temperature == 0 and not req.logprobs):
+            cache_key = json.dumps({"max_tokens": sp.max_tokens, "stop": req.stop, "rf": req.response_format,
+                                    "rx": req.guided_regex, "rag": req.rag, "adapter": req.adapter_id},
+                                   sort_keys=True, default=str)
+            qvec = (await _embed([prompt]))[0]
+            hit = pl.semantic_cache.lookup(cache_key, qvec)
+            if hit is not None:
+                return {**hit["response"], "id": cid, "created": _now(),
+                        "gollek": {**info, "semantic_cache": "hit", "similarity": round(hit["similarity"], 6)}}
 
         def keep_calls(calls):
             return calls[:1] if req.parallel_tool_calls is False else calls
@@ -599,7 +627,28 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
         if rag_sources is not None:
             resp["rag_sources"] = rag_sources
+        if pl.reasoning_split and isinstance(message.get("content"), str):
+            reasoning, answer = split_reasoning(message["content"])
+            if reasoning is not None:
+                message["content"], message["reasoning_content"] = answer, reasoning
+        if cache_key is not None:
+            pl.semantic_cache.store(cache_key, qvec, {"response": dict(resp)})
+            info["semantic_cache"] = "miss"
+        if info:
+            resp["gollek"] = info
         return resp
+
+    @app.get("/v1/admin/plugins")
+    async def plugins_get():
+        return st.plugins.describe()
+
+    @app.post("/v1/admin/plugins")
+    async def plugins_set(body: Dict[str, Any]):
+        try:
+            st.plugins.configure(body)
+        except (ValueError, TypeError, re.error) as e:
+            raise HTTPException(400, str(e))
+        return st.plugins.describe()
 
     @app.post("/v1/chat/completions")
     async def chat(req: ChatRequest):

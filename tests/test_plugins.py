@@ -1,0 +1,77 @@
+"""Server plugins: PII redaction, content safety, reasoning split and the semantic response cache,
+as functions and through /v1/chat/completions with /v1/admin/plugins."""
+import pytest
+
+from gollek_b200.config import EngineConfig, preset
+from gollek_b200.engine.engine import LLMEngine
+from gollek_b200.models.reference import init_random_weights
+from gollek_b200.server.plugins import ContentSafety, SemanticCache, UnsafeContent, redact_pii, split_reasoning
+from gollek_b200.utils.tokenizer import ByteTokenizer
+
+
+def test_redact_pii_kinds():
+    text = ("Mail ann.lee@example.co.uk or call +1 (415) 555-0133; card 4111 1111 1111 1111, "
+            "SSN 123-45-6789, order 2024 of 12 items")
+    out, n = redact_pii(text)
+    assert n == 4
+    for kind in ("EMAIL", "PHONE", "CC", "SSN"):
+        assert f"[REDACTED_{kind}]" in out
+    assert "2024" in out and "12 items" in out and "example" not in out
+
+
+def test_safety_and_reasoning_and_cache():
+    cs = ContentSafety(["forbidden"], [r"\bkill\s+all\b"])
+    cs.check("a harmless request")
+    with pytest.raises(UnsafeContent):
+        cs.check("This is FORBIDDEN text")
+    with pytest.raises(UnsafeContent):
+        cs.check("kill  all processes")
+    assert split_reasoning("<think>step 1\nstep 2</think>The answer is 4.") == ("step 1\nstep 2", "The answer is 4.")
+    assert split_reasoning("no blocks") == (None, "no blocks")
+    assert split_reasoning("<reasoning>half")[0] == "half"
+    c = SemanticCache(threshold=0.9, max_size=2)
+    c.store("k", [1.0, 0.0], {"response": 1})
+    assert c.lookup("k", [0.99, 0.05])["response"] == 1
+    assert c.lookup("other", [1.0, 0.0]) is None and c.lookup("k", [0.0, 1.0]) is None
+    c.store("k", [0.0, 1.0], {"response": 2})
+    c.store("k", [0.7, 0.7], {"response": 3})
+    assert c.lookup("k", [1.0, 0.0]) is None  # evicted beyond max_size
+
+
+def _engine():
+    cfg = preset("tiny-llama")
+    w = init_random_weights(cfg, seed=0)
+    ec = EngineConfig(device="cpu", dtype="float32", max_num_seqs=4, max_num_batched_tokens=256, max_model_len=512,
+                      use_cuda_graphs=False)
+    return LLMEngine(ec, model_cfg=cfg, weights=w.__getitem__, num_blocks=96,
+                     tokenizer=ByteTokenizer(cfg.vocab_size, cfg.eos_token_id))
+
+
+def test_plugins_through_chat_api():
+    from fastapi.testclient import TestClient
+
+    from gollek_b200.server.app import create_app
+    from gollek_b200.server.async_engine import AsyncEngine
+    ae = AsyncEngine(_engine()).start()
+    try:
+        with TestClient(create_app(ae)) as c:
+            cfg = c.post("/v1/admin/plugins", json={"pii_redaction": True, "blocked_keywords": ["secret plan"],
+                                                     "semantic_cache": {"threshold": 0.999}}).json()
+            assert cfg["pii_redaction"] and cfg["blocked_keywords"] == ["secret plan"]
+            body = {"messages": [{"role": "user", "content": "Tell me the SECRET PLAN"}], "max_tokens": 2}
+            r = c.post("/v1/chat/completions", json=body)
+            assert r.status_code == 400 and "blocked keyword" in r.text
+            msg = "write to bob@example.com about it"
+            red = "write to [REDACTED_EMAIL] about it"
+            base = {"max_tokens": 3, "temperature": 0.0}
+            a = c.post("/v1/chat/completions", json={**base, "messages": [{"role": "user", "content": msg}]}).json()
+            b = c.post("/v1/chat/completions", json={**base, "messages": [{"role": "user", "content": red}]}).json()
+            assert a["gollek"]["pii_redactions"] == 1 and a["gollek"]["semantic_cache"] == "miss"
+            # the redacted prompt is what the model saw: the second request is the same prompt -> cache hit
+            assert b["gollek"]["semantic_cache"] == "hit"
+            assert b["choices"][0]["message"] == a["choices"][0]["message"]
+            assert b["usage"] == a["usage"] and b["id"] != a["id"]
+            stats = c.get("/v1/admin/plugins").json()["semantic_cache"]
+            assert stats["hits"] == 1 and stats["misses"] == 1
+    finally:
+        ae.shutdown()
