@@ -79,6 +79,7 @@ class ChatRequest(BaseModel):
     response_format: Optional[Dict[str, Any]] = None
     guided_regex: Optional[str] = None
     rag: Optional[Dict[str, Any]] = None  # {"collection": name, "top_k": 4, "max_context_tokens": 1024}
+    mcp: bool = False  # offer the tools of the connected MCP servers (named <server>__<tool>)
 
 
 class CompletionRequest(BaseModel):
@@ -265,6 +266,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     st.rag = RagStore()
     from .plugins import ServerPlugins, UnsafeContent, redact_pii, split_reasoning
     st.plugins = ServerPlugins.from_env()
+    from .mcp import MCPError, MCPRegistry, tool_text
+    st.mcp = MCPRegistry()
     gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
     app = FastAPI(title="gollek-b200", version="0.1")
     app.state.server = st
@@ -547,6 +550,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         sp = build_sampling(st, d, OPENAI_DEFAULTS)
         lora = st.lora_id(req.adapter_id)
         tools = req.tools if (req.tools and req.tool_choice != "none") else None
+        if req.mcp and req.tool_choice != "none" and st.mcp.clients:
+            tools = (tools or []) + await asyncio.to_thread(st.mcp.openai_tools)
         if tools:
             rx = tool_choice_regex(req.tool_choice)
             if rx and not (sp.guided_json or sp.guided_regex):
@@ -637,6 +642,42 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         if info:
             resp["gollek"] = info
         return resp
+
+    # -------------------------------------------------------------- Model Context Protocol servers
+    @app.post("/v1/admin/mcp/servers")
+    async def mcp_connect(body: Dict[str, Any]):
+        name, cmd = body.get("name"), body.get("command")
+        if not name or not isinstance(cmd, list) or not cmd:
+            raise HTTPException(400, "name and command (argv list) are required")
+        try:
+            info = await asyncio.to_thread(st.mcp.connect, str(name), [str(c) for c in cmd],
+                                           float(body.get("timeout_s", 30.0)))
+        except (MCPError, OSError, ValueError) as e:
+            raise HTTPException(502, f"MCP server {name!r}: {e}")
+        return {"name": name, "protocolVersion": info.get("protocolVersion"), "serverInfo": info.get("serverInfo")}
+
+    @app.delete("/v1/admin/mcp/servers/{name}")
+    async def mcp_disconnect(name: str):
+        if not st.mcp.disconnect(name):
+            raise HTTPException(404, f"unknown MCP server {name!r}")
+        return Response(status_code=204)
+
+    @app.get("/v1/mcp/tools")
+    async def mcp_tools():
+        try:
+            return {"tools": await asyncio.to_thread(st.mcp.openai_tools)}
+        except MCPError as e:
+            raise HTTPException(502, str(e))
+
+    @app.post("/v1/mcp/tools/call")
+    async def mcp_call(body: Dict[str, Any]):
+        try:
+            res = await asyncio.to_thread(st.mcp.call, str(body.get("name", "")), body.get("arguments") or {})
+        except KeyError as e:
+            raise HTTPException(404, str(e))
+        except MCPError as e:
+            raise HTTPException(502, str(e))
+        return {"result": res, "text": tool_text(res), "isError": bool(res.get("isError", False))}
 
     @app.get("/v1/admin/plugins")
     async def plugins_get():
