@@ -147,12 +147,20 @@ def _param(p: Dict[str, Any], *names, default=None):
 _TENANT = contextvars.ContextVar("gollek_tenant", default="")
 
 
+_ROUTED: contextvars.ContextVar = contextvars.ContextVar("gollek_routed_model", default=None)
+
+
 class ServerState:
+    """Server-wide state. ``ae`` / ``model_name`` are the engine and name serving the current request:
+    the model router (``route``) picks one of ``routes`` by the request's ``model`` field, anything
+    else goes to the primary engine (the one hot-swap replaces)."""
+
     def __init__(self, aengine: AsyncEngine, model_name: str, api_keys=None,
                  rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
                  max_concurrent: int = 1024, max_queue: int = 4096):
-        self.ae = aengine
-        self.model_name = model_name
+        self._ae = aengine
+        self._model_name = model_name
+        self.routes: Dict[str, AsyncEngine] = {}  # extra served models by name
         # API key -> tenant ("" = no tenant); a list of keys means keys without tenants
         self.api_keys: Dict[str, str] = dict(api_keys) if isinstance(api_keys, dict) else \
             {k: "" for k in (api_keys or [])}
@@ -163,6 +171,29 @@ class ServerState:
         self.timeout = request_timeout
         self.jobs: Dict[str, Dict[str, Any]] = {}
         self.adapters: Dict[str, int] = {}  # adapter name -> engine LoRA id
+
+    @property
+    def ae(self) -> AsyncEngine:
+        r = _ROUTED.get()
+        return self.routes[r] if (r is not None and r in self.routes) else self._ae
+
+    @ae.setter
+    def ae(self, value: AsyncEngine) -> None:
+        self._ae = value
+
+    @property
+    def model_name(self) -> str:
+        r = _ROUTED.get()
+        return r if (r is not None and r in self.routes) else self._model_name
+
+    @model_name.setter
+    def model_name(self, value: str) -> None:
+        self._model_name = value
+
+    def route(self, model: Optional[str]) -> str:
+        """Select the engine for this request (by name; unknown or empty names go to the primary)."""
+        _ROUTED.set(model if (model and model in self.routes) else None)
+        return self.model_name
 
     @property
     def engine(self):
@@ -258,10 +289,12 @@ class RagQueryRequest(BaseModel):
 
 def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
                rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
-               engine_builder=None, drain_timeout_s: float = 30.0) -> FastAPI:
+               engine_builder=None, drain_timeout_s: float = 30.0,
+               routes: Optional[Dict[str, AsyncEngine]] = None) -> FastAPI:
     """``engine_builder(model) -> LLMEngine`` builds the engine of a hot-swap (default: the running
     engine's configuration with ``model`` replaced)."""
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
+    st.routes.update(routes or {})
     from .rag import RagStore
     st.rag = RagStore()
     from .plugins import ServerPlugins, UnsafeContent, redact_pii, split_reasoning
@@ -455,8 +488,11 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     # -------------------------------------------------------------- OpenAI
     @app.get("/v1/models")
     async def models():
-        return {"object": "list", "data": [{"id": st.model_name, "object": "model", "created": _now(),
-                                            "owned_by": "gollek-b200", "max_model_len": st.max_len()}]}
+        data = [{"id": st.model_name, "object": "model", "created": _now(), "owned_by": "gollek-b200",
+                 "max_model_len": st.max_len()}]
+        data += [{"id": n, "object": "model", "created": _now(), "owned_by": "gollek-b200",
+                  "max_model_len": e.engine.cfg.max_model_len} for n, e in st.routes.items()]
+        return {"object": "list", "data": data}
 
     @app.get("/v1/models/{model_id}")
     async def model(model_id: str):
@@ -494,6 +530,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
 
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
+        st.route(getattr(req, "model", None))
         if req.n != 1 and not req.use_beam_search:
             raise HTTPException(400, "n > 1 needs use_beam_search")
         sp = build_sampling(st, req.model_dump(), {**OPENAI_DEFAULTS, "max_tokens": req.max_tokens or 16})
@@ -543,6 +580,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                             for e in o.logprobs]}
 
     async def _chat(req: ChatRequest, force_stream: bool = False):
+        st.route(getattr(req, "model", None))
         if req.n != 1:
             raise HTTPException(400, "only n=1 is supported")
         d = req.model_dump()
@@ -716,6 +754,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
 
     @app.post("/v1/embeddings")
     async def embeddings(req: EmbeddingRequest):
+        st.route(getattr(req, "model", None))
         vecs = await _embed(req.input)
         n = sum(len(v) for v in vecs)
         return {"object": "list", "model": st.model_name,
@@ -795,6 +834,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         return chat_prompt([m.model_dump() for m in req.messages])
 
     async def infer_completions(req: InferRequest, x_request_id: Optional[str] = Header(None)):
+        st.route(getattr(req, "model", None))
         return await _infer(req, x_request_id)
 
     async def _infer(req: InferRequest, x_request_id: Optional[str] = None):
@@ -809,6 +849,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                 "timestamp": datetime.now(timezone.utc).isoformat(), "finishReason": o.finish_reason}
 
     async def infer_async(req: InferRequest):
+        st.route(getattr(req, "model", None))
         jid = req.requestId or uuid.uuid4().hex
         st.jobs[jid] = {"jobId": jid, "status": "PENDING", "result": None, "error": None}
 
@@ -831,6 +872,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         return st.jobs[job_id]
 
     async def infer_stream(req: InferRequest):
+        st.route(getattr(req, "model", None))
         rid = req.requestId or uuid.uuid4().hex
         sp = build_sampling(st, req.parameters, gollek_defaults)
         lora = st.lora_id(_param(req.parameters, "adapter_id", "adapterId", "lora"))
@@ -909,6 +951,25 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     swapper = HotSwapManager(st, engine_builder or _default_builder, drain_timeout_s,
                              memory_check=default_memory_check if engine_builder is None else None)
     app.state.hotswap = swapper
+
+    @app.post("/v1/admin/models")
+    async def admin_add_model(body: Dict[str, Any]):
+        """Serve another model next to the primary one; requests name it in ``model``."""
+        name, model = (body or {}).get("name"), (body or {}).get("model")
+        if not name or not model or name == st._model_name or name in st.routes:
+            raise HTTPException(400, "body needs a new name and a model (preset name or checkpoint path)")
+        from .async_engine import AsyncEngine as _AE
+        eng = await asyncio.to_thread(engine_builder or _default_builder, str(model))
+        st.routes[str(name)] = _AE(eng).start()
+        return {"name": name, "model": model, "served": [st._model_name] + list(st.routes)}
+
+    @app.delete("/v1/admin/models/{name}")
+    async def admin_remove_model(name: str):
+        ae = st.routes.pop(name, None)
+        if ae is None:
+            raise HTTPException(404, f"unknown routed model {name!r}")
+        await asyncio.to_thread(ae.shutdown, True, drain_timeout_s)
+        return Response(status_code=204)
 
     @app.post("/v1/admin/models/swap")
     async def admin_swap(body: Dict[str, Any]):
