@@ -94,7 +94,8 @@ def cmd_convert(args):
         cfg = ModelConfig.from_hf(json.load(f))
     ck = SafetensorsCheckpoint(args.src)
     w = {k: ck.get(k).float() for k in ck.keys()}
-    t = G.TYPE_BY_NAME[args.type.upper()]
+    t = args.type.upper()
+    t = t if t in G.MIXTURES else G.TYPE_BY_NAME[t]
     emb = G.TYPE_BY_NAME[args.embed_type.upper()] if args.embed_type else None
     G.write_llama_gguf(args.dst, cfg, w, t, embed_type=emb)
     print(f"wrote {args.dst} ({args.type})")
@@ -104,7 +105,8 @@ def cmd_quantize(args):
     from .loaders import gguf as G
     if args.src.endswith(".gguf"):
         cfg, w, f = G.load_llama_gguf(args.src)
-        G.write_llama_gguf(args.dst, cfg, w, G.TYPE_BY_NAME[args.type.upper()])
+        t = args.type.upper()
+        G.write_llama_gguf(args.dst, cfg, w, t if t in G.MIXTURES else G.TYPE_BY_NAME[t])
         print(f"wrote {args.dst} ({args.type})")
     else:
         from .quant.fp8 import quantize_checkpoint_fp8
@@ -214,7 +216,9 @@ def build_parser():
     cv = sub.add_parser("convert")
     cv.add_argument("src")
     cv.add_argument("dst")
-    cv.add_argument("--type", default="F16", choices=["F32", "F16", "BF16", "Q8_0", "Q4_K"])
+    gguf_types = ["F32", "F16", "BF16", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K",
+                  "Q6_K", "Q3_K_M", "Q4_K_M", "Q5_K_M"]
+    cv.add_argument("--type", default="F16", choices=gguf_types)
     cv.add_argument("--embed-type", default=None)
     cv.set_defaults(fn=cmd_convert)
     q = sub.add_parser("quantize")

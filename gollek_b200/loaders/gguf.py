@@ -4,8 +4,10 @@ Layout: ``"GGUF"`` magic, u32 version, u64 tensor count, u64 metadata count; met
 key/value pairs (typed, arrays allowed); tensor infos (name, n_dims, dims with ``ne[0]``
 fastest-varying, ggml type, offset); padding to ``general.alignment`` (default 32); data.
 
-Supported tensor types: F32, F16, BF16, Q8_0, Q4_K (ggml block layouts; quantizers and
-dequantizers are in the host C++ module). Covers the reference's GGUF loader
+Supported tensor types: F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K
+(ggml block layouts; quantizers and dequantizers are in the host C++ module, checked bit for bit
+against gguf-py). Q8_0 and Q4_K linear weights can stay quantized on the GPU (dequant-fused
+kernels); the other types are dequantized to the serving dtype at load. Covers the reference's GGUF loader
 (runner/gguf/gollek-gguf-core/…/gguf/core/GgmlType.java:8-42 type table;
 runner/gguf/gollek-gguf-loader/…/gguf/loader/GGUFLoader.java:38-190 metadata + mmap +
 Llama tensor mapping) and its converter's writer (runner/gguf/gollek-gguf-converter-java/…/
@@ -39,13 +41,48 @@ _SCALAR = {T_U8: "<B", T_I8: "<b", T_U16: "<H", T_I16: "<h", T_U32: "<I", T_I32:
 
 # ggml tensor types we handle: id -> (name, block elements, block bytes)
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_Q4_K, GGML_BF16 = 0, 1, 8, 12, 30
+GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_Q6_K = 2, 3, 6, 7, 10, 11, 13, 14
 GGML_TYPES = {
     GGML_F32: ("F32", 1, 4),
     GGML_F16: ("F16", 1, 2),
+    GGML_Q4_0: ("Q4_0", 32, 18),
+    GGML_Q4_1: ("Q4_1", 32, 20),
+    GGML_Q5_0: ("Q5_0", 32, 22),
+    GGML_Q5_1: ("Q5_1", 32, 24),
     GGML_Q8_0: ("Q8_0", 32, 34),
+    GGML_Q2_K: ("Q2_K", 256, 84),
+    GGML_Q3_K: ("Q3_K", 256, 110),
     GGML_Q4_K: ("Q4_K", 256, 144),
+    GGML_Q5_K: ("Q5_K", 256, 176),
+    GGML_Q6_K: ("Q6_K", 256, 210),
     GGML_BF16: ("BF16", 1, 2),
 }
+# types kept in their blocks on the GPU by the dequant-fused kernels
+SERVED_QUANTIZED = (GGML_Q8_0, GGML_Q4_K)
+
+
+def dequantize_blocks(raw: torch.Tensor, ggml_type: int, n: int) -> torch.Tensor:
+    """fp32 values of ``n`` elements stored as ggml blocks of ``ggml_type`` (CPU uint8 ``raw``)."""
+    from ..native import host_ext
+    h = host_ext()
+    raw = raw.cpu().contiguous()
+    if ggml_type == GGML_Q8_0:
+        return h.dequantize_q8_0(raw, n)
+    if ggml_type == GGML_Q4_K:
+        return h.dequantize_q4_k(raw, n)
+    return h.gguf_dequantize(raw, ggml_type, n)
+
+
+def quantize_blocks(t: torch.Tensor, ggml_type: int) -> torch.Tensor:
+    """ggml blocks (uint8) of ``t``'s values in ``ggml_type``."""
+    from ..native import host_ext
+    h = host_ext()
+    x = t.float().flatten().contiguous()
+    if ggml_type == GGML_Q8_0:
+        return h.quantize_q8_0(x)
+    if ggml_type == GGML_Q4_K:
+        return h.quantize_q4_k(x)
+    return h.gguf_quantize(x, ggml_type)
 TYPE_BY_NAME = {v[0]: k for k, v in GGML_TYPES.items()}
 
 
@@ -150,15 +187,17 @@ class GGUFFile:
         elif ti.ggml_type == GGML_BF16:
             t = raw.view(torch.bfloat16)
         else:
-            from ..native import host_ext
-            h = host_ext()
-            raw_c = raw.clone()
-            t = h.dequantize_q8_0(raw_c, ti.numel) if ti.ggml_type == GGML_Q8_0 else h.dequantize_q4_k(raw_c, ti.numel)
+            t = dequantize_blocks(raw.clone(), ti.ggml_type, ti.numel)
         return t.reshape(ti.shape).to(dtype)
 
     def close(self):
+        """Release the mapping; while zero-copy tensors returned by ``raw`` / ``get`` are alive the
+        mapping stays open and is released when the last of them goes away."""
         self._buf = None
-        self._mm.close()
+        try:
+            self._mm.close()
+        except BufferError:
+            pass
         self._f.close()
 
 
@@ -200,10 +239,7 @@ class GGUFWriter:
         elif ggml_type == GGML_BF16:
             data = t.bfloat16().contiguous().view(torch.uint8).numpy().tobytes()
         else:
-            from ..native import host_ext
-            h = host_ext()
-            q = h.quantize_q8_0(t.float().flatten()) if ggml_type == GGML_Q8_0 else h.quantize_q4_k(t.float().flatten())
-            data = q.numpy().tobytes()
+            data = quantize_blocks(t, ggml_type).numpy().tobytes()
         self.tensors.append((name, tuple(t.shape), ggml_type, data))
 
     @staticmethod
@@ -306,10 +342,43 @@ def gguf_to_hf_name(name: str) -> str:
     raise KeyError(name)
 
 
+# Tensor-type mixtures named like llama.cpp's file types: a base k-quant for most linears, more
+# bits for the tensors most sensitive to quantization (output, attention V, FFN down of the first
+# and last eighth of the layers and every third layer between them).
+MIXTURES = {"Q4_K_M": GGML_Q4_K, "Q5_K_M": GGML_Q5_K, "Q3_K_M": GGML_Q3_K, "Q4_K_S": GGML_Q4_K,
+            "Q5_K_S": GGML_Q5_K, "Q3_K_S": GGML_Q3_K, "Q3_K_L": GGML_Q3_K}
+
+
+def _more_bits(layer: int, n_layers: int) -> bool:
+    return layer < n_layers // 8 or layer >= 7 * n_layers // 8 or (layer - n_layers // 8) % 3 == 2
+
+
+def mixture_type(recipe: str, hf_name: str, n_layers: int) -> int:
+    """ggml type of one 2-D tensor under a ``*_K_M`` mixture."""
+    base = MIXTURES[recipe]
+    if hf_name == "lm_head.weight":
+        return GGML_Q6_K
+    if hf_name == "model.embed_tokens.weight":
+        return base
+    layer = int(hf_name.split(".")[2]) if hf_name.startswith("model.layers.") else 0
+    sensitive = hf_name.endswith(("v_proj.weight", "down_proj.weight", "w2.weight"))
+    if recipe.endswith("_S"):  # small: only the output matrix gets more bits
+        return base
+    if recipe == "Q3_K_L":
+        return GGML_Q5_K if sensitive or hf_name.endswith("o_proj.weight") else base
+    if recipe == "Q3_K_M":
+        if sensitive:
+            return GGML_Q5_K if layer < 2 or hf_name.endswith("v_proj.weight") and _more_bits(layer, n_layers) \
+                else GGML_Q4_K
+        return GGML_Q4_K if hf_name.endswith("o_proj.weight") else base
+    return GGML_Q6_K if sensitive and _more_bits(layer, n_layers) else base
+
+
 def write_llama_gguf(path: str, cfg: ModelConfig, weights: Dict[str, torch.Tensor],
-                     linear_type: int = GGML_F32, embed_type: Optional[int] = None,
-                     vocab: Optional[List[str]] = None) -> None:
-    """Write an HF-named Llama/Mixtral state dict as GGUF (norms always F32)."""
+                     linear_type: Any = GGML_F32, embed_type: Optional[int] = None,
+                     vocab: Optional[List[str]] = None, progress=None) -> None:
+    """Write an HF-named Llama/Mixtral state dict as GGUF (norms always F32). ``linear_type`` is a
+    ggml type id or a mixture name (``"Q4_K_M"``, ``"Q5_K_M"``, ``"Q3_K_M"``)."""
     w = GGUFWriter(path)
     arch = "llama"
     w.add("general.architecture", arch)
@@ -332,8 +401,14 @@ def write_llama_gguf(path: str, cfg: ModelConfig, weights: Dict[str, torch.Tenso
     w.add("tokenizer.ggml.tokens", vocab if vocab is not None else [f"<t{i}>" for i in range(cfg.vocab_size)], T_ARR, T_STR)
     w.add("tokenizer.ggml.bos_token_id", cfg.bos_token_id)
     w.add("tokenizer.ggml.eos_token_id", cfg.eos_token_id)
+    recipe = linear_type if isinstance(linear_type, str) else None
+    if recipe is not None and recipe not in MIXTURES:
+        raise ValueError(f"unknown mixture {recipe!r} (known: {sorted(MIXTURES)})")
     emb_t = linear_type if embed_type is None else embed_type
-    for name in weights:
+    names = list(weights)
+    for idx, name in enumerate(names):
+        if progress is not None:
+            progress(idx, len(names), name)  # may raise to cancel the conversion
         t = weights[name]
         g = hf_to_gguf_name(name)
         if name.endswith("q_proj.weight"):
@@ -342,10 +417,15 @@ def write_llama_gguf(path: str, cfg: ModelConfig, weights: Dict[str, torch.Tenso
             t = permute_qk(t, cfg.num_key_value_heads)
         if t.dim() == 1:
             gt = GGML_F32
+        elif recipe is not None and not (embed_type is not None and name == "model.embed_tokens.weight"):
+            gt = mixture_type(recipe, name, cfg.num_hidden_layers)
         elif name in ("model.embed_tokens.weight", "lm_head.weight"):
             gt = emb_t
         else:
             gt = linear_type
+        bs = GGML_TYPES[gt][1]
+        if t.dim() == 2 and t.shape[-1] % bs:
+            gt = GGML_F16  # rows that are not a whole number of blocks stay unquantized
         w.add_tensor(g, t, gt)
     w.write()
 
@@ -393,7 +473,7 @@ def load_llama_gguf(path: str, dtype: torch.dtype = torch.float32,
         hf = gguf_to_hf_name(name)
         is_q = hf.endswith("q_proj.weight")
         is_k = hf.endswith("k_proj.weight")
-        keep = keep_quantized and ti.ggml_type in (GGML_Q8_0, GGML_Q4_K) and len(ti.shape) == 2
+        keep = keep_quantized and ti.ggml_type in SERVED_QUANTIZED and len(ti.shape) == 2
         if hf == "model.embed_tokens.weight" and ti.ggml_type != GGML_Q8_0:
             keep = False  # the quantized embedding gather supports Q8_0 tables
         if keep:
@@ -423,9 +503,5 @@ class QuantizedWeight:
     ggml_type: int
 
     def dequantize(self) -> torch.Tensor:
-        from ..native import host_ext
-        h = host_ext()
         n = self.shape[0] * self.shape[1]
-        raw = self.raw.cpu().contiguous()
-        t = h.dequantize_q8_0(raw, n) if self.ggml_type == GGML_Q8_0 else h.dequantize_q4_k(raw, n)
-        return t.view(self.shape)
+        return dequantize_blocks(self.raw, self.ggml_type, n).view(self.shape)

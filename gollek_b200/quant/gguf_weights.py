@@ -75,11 +75,8 @@ class QWeight:
             out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.raw.device)
             cuda_ext().gguf_dequant(out, self.raw.contiguous(), self.qtype)
             return out
-        from ..native import host_ext
-        h = host_ext()
-        flat = self.raw.contiguous().view(-1)
-        t = h.dequantize_q8_0(flat, self.N * self.K) if self.qtype == GGML_Q8_0 else h.dequantize_q4_k(flat, self.N * self.K)
-        return t.view(self.N, self.K)
+        from ..loaders.gguf import dequantize_blocks
+        return dequantize_blocks(self.raw.contiguous().view(-1), self.qtype, self.N * self.K).view(self.N, self.K)
 
 
 def cat_rows(ws: Sequence[QWeight]) -> QWeight:
