@@ -3,9 +3,10 @@
 The reference ships BPE / HF-BPE / SentencePiece / WordPiece tokenizers and a GGUF
 metadata tokenizer (core/gollek-tokenizer-core/…/tokenizer/impl/*.java; runner/gguf/
 gollek-gguf-tokenizer/…/GGUFTokenizer.java:1-335) plus a streaming decoder. Here the HF path
-uses the ``tokenizers`` library, GGUF vocabularies get a greedy longest-match SentencePiece-style
-encoder over the stored pieces (scores break ties), and random-init presets use a byte-level
-tokenizer so text requests still work end to end.
+uses the ``tokenizers`` library; GGUF vocabularies are tokenized by their own metadata
+(SentencePiece BPE by piece scores, or byte-level BPE by ``tokenizer.ggml.merges``; checked
+against sentencepiece and HF ``tokenizers`` on the same vocabularies); random-init presets use a
+byte-level tokenizer so text requests still work end to end.
 """
 from __future__ import annotations
 
@@ -115,19 +116,53 @@ class HFTokenizer:
         return default_chat_template(messages, tools)
 
 
-class GGUFTokenizer:
-    """Vocabulary from ``tokenizer.ggml.tokens`` (+ scores); SentencePiece-style greedy encode."""
+# Pre-tokenizer split patterns of byte-level BPE vocabularies, by ``tokenizer.ggml.pre``: GPT-2's
+# (the default) and the one Llama-3 vocabularies were trained with (digits in groups of up to three).
+_PRE_PATTERNS = {
+    "default": r"""'s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+""",
+    "llama-bpe": r"""(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n]*"""
+                 r"""|\s*[\r\n]+|\s+(?!\S)|\s+""",
+}
+_PRE_PATTERNS["llama3"] = _PRE_PATTERNS["llama-bpe"]
+_PRE_PATTERNS["gpt2"] = _PRE_PATTERNS["default"]
 
-    def __init__(self, tokens: List[str], scores: Optional[List[float]] = None, bos: int = 1, eos: int = 2):
+# ggml token types (tokenizer.ggml.token_type)
+_TT_NORMAL, _TT_UNKNOWN, _TT_CONTROL, _TT_USER_DEFINED, _TT_UNUSED, _TT_BYTE = 1, 2, 3, 4, 5, 6
+
+
+class GGUFTokenizer:
+    """Tokenizer built from a GGUF file's ``tokenizer.ggml.*`` metadata.
+
+    * ``model == "llama"``: SentencePiece BPE. The text gets a leading space and spaces become
+      ``▁``; starting from single characters, the adjacent pair whose concatenation is a vocabulary
+      piece with the highest score is merged first (leftmost on ties) until no pair is in the
+      vocabulary; characters left outside it fall back to their ``<0xXX>`` byte pieces.
+    * ``model == "gpt2"``: byte-level BPE. The text is split by the vocabulary's pre-tokenizer
+      pattern (``tokenizer.ggml.pre``), each chunk's UTF-8 bytes are mapped to the GPT-2 byte
+      alphabet, and ``tokenizer.ggml.merges`` are applied lowest rank first.
+    Control / user-defined tokens that appear literally in the text are matched as single ids.
+    ``add_bos`` follows ``tokenizer.ggml.add_bos_token``; ``tokenizer.chat_template`` (Jinja) is used
+    by ``apply_chat_template`` when present.
+
+    Reference: runner/gguf/gollek-gguf-tokenizer/…/gguf/tokenizer/GGUFTokenizer.java:53-78 (merges and
+    vocabulary loading from the same metadata keys).
+    """
+
+    def __init__(self, tokens: List[str], scores: Optional[List[float]] = None, bos: int = 1, eos: int = 2,
+                 model: str = "llama", merges: Optional[List[str]] = None, token_types: Optional[List[int]] = None,
+                 pre: str = "default", add_bos: Optional[bool] = None, chat_template: Optional[str] = None):
         self.tokens = tokens
         self.vocab_size = len(tokens)
+        self.model = model
         self.scores = scores or [0.0] * len(tokens)
         self.bos, self.eos_token_id = bos, eos
+        self.token_types = token_types or [_TT_NORMAL] * len(tokens)
+        self.add_bos = (model == "llama") if add_bos is None else bool(add_bos)
+        self.chat_template = chat_template
         self.index: Dict[str, int] = {}
         for i, t in enumerate(tokens):
             if t not in self.index or self.scores[i] > self.scores[self.index[t]]:
                 self.index[t] = i
-        self.max_len = max((len(t) for t in tokens), default=1)
         self.byte_ids = {}
         for i, t in enumerate(tokens):
             if len(t) == 6 and t.startswith("<0x") and t.endswith(">"):
@@ -135,45 +170,200 @@ class GGUFTokenizer:
                     self.byte_ids[int(t[3:5], 16)] = i
                 except ValueError:
                     pass
+        self.special = {t: i for i, t in enumerate(tokens)
+                        if self.token_types[i] in (_TT_CONTROL, _TT_USER_DEFINED) and t}
+        self._special_re = None
+        if self.special:
+            import regex
+            self._special_re = regex.compile("|".join(regex.escape(t) for t in
+                                                      sorted(self.special, key=len, reverse=True)))
+        self.byte_level = model == "gpt2"
+        self.ranks: Dict[tuple, int] = {}
+        if self.byte_level:
+            import regex
+            for r, m in enumerate(merges or []):
+                a, _, b = m.partition(" ")
+                self.ranks[(a, b)] = r
+            self._pre = regex.compile(_PRE_PATTERNS.get(pre, _PRE_PATTERNS["default"]))
+            enc = {v: k for k, v in _gpt2_byte_decoder().items()}
+            self._byte_enc = [enc[b] for b in range(256)]
+        self._dec = _gpt2_byte_decoder()
+        self._cache: Dict[str, List[int]] = {}
 
     @staticmethod
     def from_metadata(meta: dict) -> "GGUFTokenizer":
         return GGUFTokenizer(meta.get("tokenizer.ggml.tokens", []), meta.get("tokenizer.ggml.scores"),
-                             int(meta.get("tokenizer.ggml.bos_token_id", 1)), int(meta.get("tokenizer.ggml.eos_token_id", 2)))
+                             int(meta.get("tokenizer.ggml.bos_token_id", 1)),
+                             int(meta.get("tokenizer.ggml.eos_token_id", 2)),
+                             model=str(meta.get("tokenizer.ggml.model", "llama")),
+                             merges=meta.get("tokenizer.ggml.merges"),
+                             token_types=meta.get("tokenizer.ggml.token_type"),
+                             pre=str(meta.get("tokenizer.ggml.pre", "default")),
+                             add_bos=meta.get("tokenizer.ggml.add_bos_token"),
+                             chat_template=meta.get("tokenizer.chat_template"))
 
-    def encode(self, text: str) -> List[int]:
-        s = "▁" + text.replace(" ", "▁")
-        ids, i = [], 0
-        while i < len(s):
-            for L in range(min(self.max_len, len(s) - i), 0, -1):
-                piece = s[i:i + L]
-                if piece in self.index:
-                    ids.append(self.index[piece])
-                    i += L
-                    break
+    # -- encoding
+    def encode(self, text: str, add_special: bool = True) -> List[int]:
+        ids: List[int] = [self.bos] if (add_special and self.add_bos) else []
+        parts = [(text, False)]
+        if self._special_re is not None:
+            parts, pos = [], 0
+            for m in self._special_re.finditer(text):
+                if m.start() > pos:
+                    parts.append((text[pos:m.start()], False))
+                parts.append((m.group(0), True))
+                pos = m.end()
+            if pos < len(text):
+                parts.append((text[pos:], False))
+        first = True
+        for chunk, is_special in parts:
+            if is_special:
+                ids.append(self.special[chunk])
+            elif self.byte_level:
+                ids += self._encode_bpe(chunk)
             else:
-                for b in s[i].encode("utf-8"):
-                    ids.append(self.byte_ids.get(b, 0))
-                i += 1
+                ids += self._encode_spm(chunk, first)
+            first = False
         return ids
 
+    def _encode_bpe(self, text: str) -> List[int]:
+        out: List[int] = []
+        for word in self._pre.findall(text):
+            hit = self._cache.get(word)
+            if hit is None:
+                hit = self._bpe_word("".join(self._byte_enc[b] for b in word.encode("utf-8")))
+                if len(self._cache) < 100000:
+                    self._cache[word] = hit
+            out += hit
+        return out
+
+    def _bpe_word(self, w: str) -> List[int]:
+        syms = list(w)
+        ranks = self.ranks
+        while len(syms) > 1:
+            best, bi = None, -1
+            for i in range(len(syms) - 1):
+                r = ranks.get((syms[i], syms[i + 1]))
+                if r is not None and (best is None or r < best):
+                    best, bi = r, i
+            if best is None:
+                break
+            a, b = syms[bi], syms[bi + 1]
+            merged, i = [], 0
+            while i < len(syms):  # every occurrence of the pair, left to right
+                if i < len(syms) - 1 and syms[i] == a and syms[i + 1] == b:
+                    merged.append(a + b)
+                    i += 2
+                else:
+                    merged.append(syms[i])
+                    i += 1
+            syms = merged
+        out = []
+        for sym in syms:
+            i = self.index.get(sym)
+            if i is not None:
+                out.append(i)
+            else:  # a piece outside the vocabulary: its single-byte pieces
+                out += [self.index.get(ch, 0) for ch in sym]
+        return out
+
+    def _encode_spm(self, text: str, leading: bool) -> List[int]:
+        import heapq
+        s = ("▁" if leading else "") + text.replace(" ", "▁")
+        if not s:
+            return []
+        syms = list(s)
+        n = len(syms)
+        prev = list(range(-1, n - 1))
+        nxt = list(range(1, n + 1))
+        alive = [True] * n
+        heap = []
+
+        def push(i):
+            j = nxt[i]
+            if j >= n:
+                return
+            piece = syms[i] + syms[j]
+            t = self.index.get(piece)
+            if t is not None:
+                heapq.heappush(heap, (-self.scores[t], i, piece))
+
+        for i in range(n - 1):
+            push(i)
+        while heap:
+            _, i, piece = heapq.heappop(heap)
+            j = nxt[i] if alive[i] else n
+            if not alive[i] or j >= n or syms[i] + syms[j] != piece:
+                continue  # stale entry
+            syms[i] = piece
+            alive[j] = False
+            nxt[i] = nxt[j]
+            if nxt[j] < n:
+                prev[nxt[j]] = i
+            if prev[i] >= 0:
+                push(prev[i])
+            push(i)
+        ids: List[int] = []
+        i = 0
+        while i < n:
+            t = self.index.get(syms[i])
+            if t is not None:
+                ids.append(t)
+            else:
+                ids += [self.byte_ids.get(b, 0) for b in syms[i].encode("utf-8")]
+            i = nxt[i]
+        return ids
+
+    # -- decoding
     def token_bytes(self) -> List[bytes]:
-        byte_level = any(("Ġ" in p or "Ċ" in p) for p in self.tokens[:5000])
-        dec = _gpt2_byte_decoder()
-        return [b"" if (p.startswith("<") and p.endswith(">") and len(p) != 6) else _piece_bytes(p, byte_level, dec)
-                for p in self.tokens]
+        out = []
+        for i, p in enumerate(self.tokens):
+            tt = self.token_types[i]
+            if tt in (_TT_CONTROL, _TT_UNUSED) or (p.startswith("<") and p.endswith(">") and len(p) != 6
+                                                  and tt != _TT_USER_DEFINED and not self.byte_level):
+                out.append(b"")
+            else:
+                out.append(_piece_bytes(p, self.byte_level, self._dec))
+        return out
 
     def decode(self, ids: List[int]) -> str:
         out = bytearray()
+        if self.byte_level:
+            for i in ids:
+                if 0 <= i < len(self.tokens) and self.token_types[i] != _TT_CONTROL:
+                    out += _piece_bytes(self.tokens[i], True, self._dec)
+            return out.decode("utf-8", errors="replace")
         inv_bytes = {v: k for k, v in self.byte_ids.items()}
         for i in ids:
             if i in inv_bytes:
                 out.append(inv_bytes[i])
-            elif 0 <= i < len(self.tokens):
+            elif 0 <= i < len(self.tokens) and self.token_types[i] != _TT_CONTROL:
                 out += self.tokens[i].replace("▁", " ").encode("utf-8")
-        return out.decode("utf-8", errors="replace").lstrip(" ")
+        text = out.decode("utf-8", errors="replace")
+        return text[1:] if text.startswith(" ") else text
 
     def apply_chat_template(self, messages: List[dict], tools: Optional[List[dict]] = None) -> str:
+        """The file's Jinja ``tokenizer.chat_template`` when present (``bos_token`` / ``eos_token`` set
+        to the vocabulary's pieces), else the built-in role-tag template."""
+        if self.chat_template:
+            try:
+                import jinja2
+                msgs = messages
+                if tools and "tools" not in self.chat_template:
+                    msgs, tools = _with_tools_system(messages, tools), None
+                env = jinja2.Environment()
+                env.globals["raise_exception"] = lambda m: (_ for _ in ()).throw(ValueError(m))
+                bos = self.tokens[self.bos] if 0 <= self.bos < len(self.tokens) else ""
+                eos = self.tokens[self.eos_token_id] if 0 <= self.eos_token_id < len(self.tokens) else ""
+                text = env.from_string(self.chat_template).render(messages=msgs, tools=tools,
+                                                                  add_generation_prompt=True, bos_token=bos,
+                                                                  eos_token=eos)
+                # encode() adds BOS itself: drop a rendered leading BOS so it is not doubled
+                if self.add_bos and bos and text.startswith(bos):
+                    text = text[len(bos):]
+                return text
+            except Exception:
+                pass
         return default_chat_template(messages, tools)
 
 
