@@ -1,8 +1,9 @@
 """Request / response plugins of the server: PII redaction, content safety, reasoning-block split and
 a semantic response cache.
 
-Reference behaviour: plugins/gollek-plugin-pii-redaction/…/PIIRedactionService.java (e-mail, phone,
-card and US SSN patterns replaced by typed ``[REDACTED_*]`` markers), plugins/gollek-plugin-content-
+Reference behaviour: plugins/gollek-plugin-pii-redaction/…/PIIRedactionService.java:60-107 (e-mail,
+phone, card, US SSN, IPv4 address, API-key assignment and AWS access-key patterns replaced by typed
+``[REDACTED_*]`` markers; custom patterns can be added), plugins/gollek-plugin-content-
 safety/…/ContentSafetyPlugin.java:64-110 (blocked keywords, case-insensitive, and blocked regular
 expressions reject the request), plugins/gollek-plugin-reasoning/…/OutputParser.java:111-112
 (``<think>`` / ``<reasoning>`` blocks separated from the answer) and plugins/gollek-plugin-semantic-
@@ -21,18 +22,35 @@ from typing import Dict, List, Optional, Tuple
 
 import numpy as np
 
+_OCTET = r"(?:25[0-5]|2[0-4]\d|1\d\d|[1-9]?\d)"
 PII_PATTERNS: List[Tuple[str, "re.Pattern"]] = [
+    # secrets first: their values may contain digit runs the later kinds would take
+    ("AWS_KEY", re.compile(r"\b(?:AKIA|ABIA|ACCA|ASIA)[0-9A-Z]{16}\b")),
+    ("API_KEY", re.compile(r"\b(?:api[_-]?key|apikey|secret[_-]?key|access[_-]?token)\s*[=:]\s*['\"]?[\w\-]{20,}['\"]?",
+                           re.IGNORECASE)),
     ("EMAIL", re.compile(r"\b[\w.%+-]+@[\w-]+(?:\.[\w-]+)*\.[A-Za-z]{2,}\b")),
+    # before PHONE: a dotted IPv4 address has enough digits to pass for a phone number
+    ("IP", re.compile(rf"(?<![\d.]){_OCTET}(?:\.{_OCTET}){{3}}(?![\d.])")),
     ("SSN", re.compile(r"\b\d{3}-\d{2}-\d{4}\b")),
     ("CC", re.compile(r"\b(?:\d[ -]?){12,18}\d\b")),
     ("PHONE", re.compile(r"(?<![\w-])\+?\(?\d{1,4}\)?(?:[ .-]?\(?\d{2,4}\)?){2,4}(?![\w-])")),
 ]
 
 
+def add_pii_pattern(kind: str, pattern: str, flags: int = 0, first: bool = False) -> None:
+    """Register a custom PII kind: matches become ``[REDACTED_<KIND>]`` (appended to the list, or
+    checked before the built-in kinds with ``first``)."""
+    entry = (kind.upper(), re.compile(pattern, flags))
+    if first:
+        PII_PATTERNS.insert(0, entry)
+    else:
+        PII_PATTERNS.append(entry)
+
+
 def redact_pii(text: str) -> Tuple[str, int]:
-    """Replace e-mail addresses, US social security numbers, card numbers and phone numbers (in that
-    order, so a card number is not taken for a phone number) by ``[REDACTED_<KIND>]``; returns the
-    text and the number of replacements."""
+    """Replace AWS access keys, API-key assignments, e-mail addresses, IPv4 addresses, US social
+    security numbers, card numbers and phone numbers (in that order, so a card number is not taken
+    for a phone number) by ``[REDACTED_<KIND>]``; returns the text and the number of replacements."""
     n = 0
     for kind, rx in PII_PATTERNS:
         def sub(m, kind=kind):
