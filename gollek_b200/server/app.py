@@ -304,6 +304,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     gollek_defaults = dict(vars(aengine.engine.cfg.sampling))
     app = FastAPI(title="gollek-b200", version="0.1")
     app.state.server = st
+    from .converter import register_converter_routes
+    st.converter = register_converter_routes(app)
 
     def error_response(name: str, message: Optional[str] = None, status: Optional[int] = None) -> JSONResponse:
         code = errors.CODES[name]
