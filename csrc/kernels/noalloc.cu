@@ -1,12 +1,15 @@
 // Allocation-free C entry point for split-KV paged decode attention.
 //
 // This entry point has no counterpart in the reference implementation; it exists for callers
-// of this library that cannot allocate device memory themselves. Examples: code running inside
-// a CUDA host callback or stream-ordered host function (where cudaMalloc must not be called),
-// hosts whose own memory manager owns the whole device budget and forbids allocations by
-// libraries, and latency-critical loops that must never enter an allocator. Such a caller passes
-// its inputs and its output buffer; the kernel's scratch (the split-KV partial results) lives in
-// one fixed file-scope device array instead of a caller- or allocator-provided workspace.
+// of this library that cannot allocate device memory themselves: hosts whose own memory manager
+// owns the whole device budget and forbids allocations by libraries, and latency-critical serving
+// loops that must never enter an allocator. Such a caller passes its inputs and its output buffer;
+// the kernel's scratch (the split-KV partial results) lives in one fixed file-scope device array
+// instead of a caller- or allocator-provided workspace. The C declarations are in noalloc.h.
+//
+// Call it from ordinary host code, not from inside a CUDA host callback or stream-ordered host
+// function: it makes CUDA runtime calls (device query, symbol lookup, launch), which CUDA does not
+// allow there.
 //
 // Contract:
 //   * Scratch capacity: kNoAllocScratchBytes (8 MiB) per device. A call needs
@@ -24,9 +27,9 @@
 #include <stdint.h>
 
 #include <mutex>
-#include <string>
 
 #include "launchers.h"
+#include "noalloc.h"
 
 namespace {
 
@@ -55,29 +58,32 @@ cudaError_t scratch_address(void** out) {
   return cudaSuccess;
 }
 
-}  // namespace
+// head_dim / group pairs the decode kernels are built for (csrc/kernels/attention.cu)
+bool decode_shape_supported(int head_dim, int group) {
+  const bool g8 = group == 1 || group == 2 || group == 4 || group == 8;
+  switch (head_dim) {
+    case 32: case 64: case 256: return g8;
+    case 128: return g8 || group == 16;
+    default: return false;
+  }
+}
 
-enum {
-  GOLLEK_NOALLOC_OK = 0,
-  GOLLEK_NOALLOC_ERR_ARGS = 1,      // null pointer or non-positive size
-  GOLLEK_NOALLOC_ERR_SCRATCH = 2,   // B * H * num_splits * (head_dim + 2) * 4 > scratch capacity
-  GOLLEK_NOALLOC_ERR_CUDA = 3,      // a CUDA runtime call failed (symbol lookup or launch)
-  GOLLEK_NOALLOC_ERR_UNSUPPORTED = 4,
-};
+}  // namespace
 
 // Split-KV paged decode attention without any allocation.
 //   out          [B, H, head_dim] bf16 (written)
 //   q            [B, H, head_dim] bf16, rows q_stride elements apart
 //   cache        [num_blocks, 2, Hk, block_size, head_dim] bf16 (one layer's paged KV)
 //   block_tables [B, bt_stride] int32, seq_lens [B] int32 (KV length per sequence)
-// Returns GOLLEK_NOALLOC_OK or one of the error codes above; `stream` may be 0.
+// Returns GOLLEK_NOALLOC_OK or one of the error codes of noalloc.h; `stream` may be 0.
 extern "C" __attribute__((visibility("default"))) int gollek_paged_decode_attention_noalloc(
     void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks, const int* block_tables,
     int bt_stride, const int* seq_lens, int B, int H, int Hk, int head_dim, int block_size, int num_splits,
     float scale, cudaStream_t stream) {
   if (!out || !q || !cache || !block_tables || !seq_lens || B <= 0 || H <= 0 || Hk <= 0 || head_dim <= 0 ||
-      num_splits <= 0 || num_blocks <= 0)
+      num_splits <= 0 || num_blocks <= 0 || H % Hk != 0)
     return GOLLEK_NOALLOC_ERR_ARGS;
+  if (block_size != 16 || !decode_shape_supported(head_dim, H / Hk)) return GOLLEK_NOALLOC_ERR_UNSUPPORTED;
   const size_t need = (size_t)B * H * num_splits * (head_dim + 2) * sizeof(float);
   if (need > kNoAllocScratchBytes) return GOLLEK_NOALLOC_ERR_SCRATCH;
   void* scratch = nullptr;
@@ -89,12 +95,7 @@ extern "C" __attribute__((visibility("default"))) int gollek_paged_decode_attent
                                 seq_lens, B, H, Hk, head_dim, block_size, num_splits, scale,
                                 num_splits > 1 ? part_o : nullptr, num_splits > 1 ? part_ml : nullptr,
                                 /*window=*/0, /*softcap=*/0.f, stream);
-  } catch (const std::runtime_error& e) {
-    // argument checks say "unsupported" / "must"; launch failures carry the CUDA error string
-    const std::string msg = e.what();
-    if (msg.find("unsupported") != std::string::npos || msg.find("must") != std::string::npos ||
-        msg.find("needs") != std::string::npos)
-      return GOLLEK_NOALLOC_ERR_UNSUPPORTED;
+  } catch (...) {  // the arguments were validated above: what remains is a failed launch
     return GOLLEK_NOALLOC_ERR_CUDA;
   }
   return GOLLEK_NOALLOC_OK;
