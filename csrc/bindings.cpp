@@ -525,6 +525,139 @@ void tp_allreduce_py(std::vector<uint64_t> bases, int64_t rank, int64_t p0, int6
                       cur_stream());
 }
 
+// NVLS: `uc` / `mc` are this rank's local and multicast addresses of the symmetric region.
+void tp_nvls_ar_rmsnorm_py(uint64_t uc, uint64_t mc, int64_t rank, int64_t world, int64_t p0, int64_t p1,
+                           int64_t x_off, int64_t parity, int64_t mode, torch::Tensor residual, torch::Tensor w,
+                           c10::optional<torch::Tensor> x_local, double eps, double timeout_s, int64_t grid) {
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  TORCH_CHECK(residual.dim() == 2 && residual.is_contiguous(), "residual must be contiguous [T, d]");
+  TORCH_CHECK(w.numel() == residual.size(1), "norm weight must have d elements");
+  void* xl = nullptr;
+  if (x_local.has_value()) {
+    check_bf16(*x_local, "x_local");
+    TORCH_CHECK(x_local->is_contiguous() && x_local->sizes() == residual.sizes(), "x_local must match residual");
+    xl = x_local->data_ptr();
+  }
+  launch_tp_nvls_ar_rmsnorm(uc, mc, (int)rank, (int)world, p0, p1, x_off, (int)parity, (int)mode, residual.data_ptr(),
+                            w.data_ptr(), xl, residual.size(0), residual.size(1), (float)eps, timeout_s, (int)grid,
+                            cur_stream());
+}
+
+void tp_nvls_allreduce_py(uint64_t uc, uint64_t mc, int64_t rank, int64_t world, int64_t p0, int64_t p1,
+                          int64_t parity, bool one_shot, int64_t numel, c10::optional<torch::Tensor> out,
+                          double timeout_s, int64_t grid) {
+  void* o = nullptr;
+  if (out.has_value()) {
+    check_bf16(*out, "out");
+    TORCH_CHECK(out->is_contiguous() && out->numel() == numel, "out must be contiguous with numel elements");
+    o = out->data_ptr();
+  }
+  launch_tp_nvls_allreduce(uc, mc, (int)rank, (int)world, p0, p1, (int)parity, one_shot, o, numel, timeout_s,
+                           (int)grid, cur_stream());
+}
+
+// ---------------------------------------------------------------- expert-parallel all-to-all (C3)
+static EpLayout ep_layout_from(const std::vector<int64_t>& v) {
+  TORCH_CHECK(v.size() == 8, "EP layout: [flags, counts, recv, meta, comb, x offsets, cap_src, cap_tok]");
+  EpLayout l;
+  l.flags_off = v[0];
+  l.counts_off = v[1];
+  l.recv_off = v[2];
+  l.meta_off = v[3];
+  l.comb_off = v[4];
+  l.x_off = v[5];
+  l.cap_src = (int)v[6];
+  l.cap_tok = (int)v[7];
+  return l;
+}
+
+void moe_route_py(torch::Tensor x, torch::Tensor router, int64_t topk, bool renorm, int64_t scoring,
+                  c10::optional<torch::Tensor> score_bias, int64_t n_group, int64_t topk_group, double scale,
+                  c10::optional<torch::Tensor> expert_map, c10::optional<torch::Tensor> logits, torch::Tensor ids,
+                  torch::Tensor wts, torch::Tensor scratch) {
+  check_bf16(x, "x");
+  check_bf16(router, "router");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && router.is_contiguous() && router.size(1) == x.size(1),
+              "moe route: x [T, H] row-major, router [E, H]");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && wts.scalar_type() == at::kFloat && ids.numel() >= x.size(0) * topk &&
+                  wts.numel() >= x.size(0) * topk,
+              "moe route: ids int32 / wts fp32 [T * k]");
+  MoeRouting rt;
+  rt.scoring = (int)scoring;
+  rt.n_group = (int)n_group;
+  rt.topk_group = (int)topk_group;
+  rt.scale = (float)scale;
+  if (score_bias.has_value()) rt.bias = score_bias->data_ptr<float>();
+  if (expert_map.has_value()) rt.expert_map = expert_map->data_ptr<int>();
+  if (logits.has_value()) rt.logits = logits->data_ptr<float>();
+  launch_moe_route(x.data_ptr(), x.stride(0), router.data_ptr(), x.size(0), x.size(1), router.size(0), (int)topk,
+                   renorm ? 1 : 0, rt, ids.data_ptr<int>(), wts.data_ptr<float>(), scratch.data_ptr<int>(),
+                   cur_stream());
+}
+
+void ep_dispatch_py(std::vector<uint64_t> bases, uint64_t mc, std::vector<int64_t> layout, int64_t rank, int64_t e_loc,
+                    int64_t k, torch::Tensor x, torch::Tensor ids, torch::Tensor ws, double timeout_s) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "EP dispatch: x [Tn, H] row-major");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.numel() >= x.size(0) * k, "EP dispatch: ids");
+  TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= ep_ws_ints((int)bases.size(), (int)e_loc), "EP dispatch: ws");
+  launch_ep_dispatch(bases, mc, ep_layout_from(layout), (int)rank, (int)e_loc, (int)k, x.data_ptr(), x.stride(0),
+                     x.size(1), ids.data_ptr<int>(), x.size(0), ws.data_ptr<int>(), timeout_s, cur_stream());
+}
+
+void ep_compact_py(std::vector<uint64_t> bases, uint64_t mc, std::vector<int64_t> layout, int64_t rank, int64_t e_loc,
+                   int64_t k, torch::Tensor xg, torch::Tensor comb_ptr, torch::Tensor tile_group, torch::Tensor num_m,
+                   double timeout_s) {
+  check_bf16(xg, "xg");
+  TORCH_CHECK(comb_ptr.scalar_type() == at::kLong && comb_ptr.numel() >= xg.size(0), "EP compact: comb_ptr int64 [cap]");
+  TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.numel() >= xg.size(0) / 128 &&
+                  num_m.scalar_type() == at::kInt,
+              "EP compact: tile map int32");
+  launch_ep_compact(bases, mc, ep_layout_from(layout), (int)rank, (int)e_loc, (int)k, xg.size(1), xg.data_ptr(),
+                    reinterpret_cast<uint64_t*>(comb_ptr.data_ptr<int64_t>()), xg.size(0), tile_group.data_ptr<int>(),
+                    num_m.data_ptr<int>(), timeout_s, cur_stream());
+}
+
+void ep_signal_py(std::vector<uint64_t> bases, uint64_t mc, std::vector<int64_t> layout, int64_t rank, int64_t e_loc,
+                  int64_t k, int64_t H, double timeout_s) {
+  launch_ep_signal(bases, mc, ep_layout_from(layout), (int)rank, (int)e_loc, (int)k, (int)H, timeout_s, cur_stream());
+}
+
+void ep_combine_norm_py(std::vector<uint64_t> bases, uint64_t mc, std::vector<int64_t> layout, int64_t rank,
+                        int64_t e_loc, int64_t k, int64_t r0, int64_t Tn, torch::Tensor wts, torch::Tensor residual,
+                        torch::Tensor w, double eps, double timeout_s) {
+  check_bf16(residual, "residual");
+  check_bf16(w, "w");
+  TORCH_CHECK(residual.dim() == 2 && residual.is_contiguous() && r0 + Tn <= residual.size(0), "EP combine: residual");
+  TORCH_CHECK(wts.scalar_type() == at::kFloat && wts.numel() >= Tn * k, "EP combine: wts fp32 [Tn * k]");
+  launch_ep_combine_norm(bases, mc, ep_layout_from(layout), (int)rank, (int)e_loc, (int)k, residual.size(1),
+                         residual.size(0), (int)r0, (int)Tn, wts.data_ptr<float>(), residual.data_ptr(), w.data_ptr(),
+                         (float)eps, timeout_s, cur_stream());
+}
+
+// Grouped (per-expert) GEMM: out = a · b_g^T per M tile (tile_group names g); epi 0 none, 2 SwiGLU,
+// 5 scatter (`out` is then the uint64 per-row destination table).
+void gemm_grouped_py(torch::Tensor out, torch::Tensor a, torch::Tensor b, int64_t N, int64_t groups, int64_t epi,
+                     torch::Tensor tile_group, torch::Tensor num_m) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && b.dim() == 2 && b.stride(1) == 1 && a.size(1) == b.size(1),
+              "grouped gemm: K-major operands");
+  TORCH_CHECK(b.size(0) == N * groups, "grouped gemm: b [groups * N, K]");
+  int64_t ldc = N;
+  if (epi == kEpiScatter) {
+    TORCH_CHECK(out.scalar_type() == at::kLong && out.numel() >= a.size(0), "grouped gemm scatter: int64 row table");
+  } else {
+    check_bf16(out, "out");
+    ldc = out.stride(0);
+    TORCH_CHECK(out.size(0) >= a.size(0), "grouped gemm: out rows");
+  }
+  launch_gemm_grouped(out.data_ptr(), ldc, a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), a.size(0), (int)N,
+                      a.size(1), (int)groups, (int)epi, 0, tile_group.data_ptr<int>(), num_m.data_ptr<int>(), 1,
+                      nullptr, nullptr, cur_stream());
+}
+
 void lora_shrink_py(torch::Tensor V, torch::Tensor x, torch::Tensor A, torch::Tensor seg_ptr, torch::Tensor tok_idx,
                     torch::Tensor seg_slot, torch::Tensor tiles, int64_t max_seg) {
   check_cuda(V, "V");
@@ -648,6 +781,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_status", &symm_status_py);
   m.def("tp_allreduce_add_rmsnorm", &tp_ar_rmsnorm_py, "fused TP all-reduce + residual add + RMSNorm over P2P");
   m.def("tp_allreduce", &tp_allreduce_py, "TP all-reduce over P2P");
+  m.def("tp_nvls_allreduce_add_rmsnorm", &tp_nvls_ar_rmsnorm_py,
+        "fused TP all-reduce + residual add + RMSNorm through NVLS multimem (sequence-parallel residual)");
+  m.def("tp_nvls_allreduce", &tp_nvls_allreduce_py, "TP all-reduce through NVLS multimem");
+  m.def("moe_route", &moe_route_py, "MoE routing only: physical expert ids and weights per token");
+  m.def("ep_ws_ints", &ep_ws_ints);
+  m.def("ep_dispatch", &ep_dispatch_py, "EP all-to-all dispatch: rows stored into the expert owners' buffers (P2P)");
+  m.def("ep_compact", &ep_compact_py, "EP: received rows into the grouped-GEMM layout + combine destinations");
+  m.def("ep_signal", &ep_signal_py, "EP: raise the combine flags of every source rank");
+  m.def("ep_combine_norm", &ep_combine_norm_py,
+        "EP combine: weighted sum of the returned rows + residual + RMSNorm, gathered via multimem.st");
+  m.def("gemm_grouped", &gemm_grouped_py, "grouped tcgen05 GEMM (none / SwiGLU / scatter epilogue)");
   m.def("tp_argmax", &tp_argmax_py, "distributed greedy argmax of vocab-parallel logits over P2P (C5)");
   m.def("gemm_push", &gemm_push_py, "row-parallel tcgen05 GEMM pushing its tiles to every rank's inbox (C1)");
   m.def("tp_push_allreduce_add_rmsnorm", &tp_push_ar_rmsnorm_py,

@@ -12,7 +12,17 @@ struct SymmHeader {
   uint32_t arrive;       // local CTA arrive counter for barrier B / call completion
   uint32_t epoch;        // last completed call
   uint32_t status;       // kStatus* bits
-  uint32_t pad[29];
+  // NVLS collectives (csrc/comm/nvls.cu): counters every rank increments on all ranks at once
+  // through the multicast address, and this rank's count of completed NVLS calls
+  uint32_t nv_a;         // += 1 per rank when its partial is written (barrier A)
+  uint32_t nv_c;         // += 1 per rank when its multicast stores are done (barrier C)
+  uint32_t nv_epoch;     // last completed NVLS call
+  uint32_t nv_arrive;    // local CTA arrive counter of the NVLS kernels
+  // expert-parallel all-to-all (csrc/comm/ep_a2a.cu)
+  uint32_t ep_epoch;     // last completed MoE layer
+  uint32_t ep_arrive;    // local CTA arrive counter of the combine kernel
+  uint32_t ep_done;      // += 1 per rank (multicast) when its gathered rows are stored
+  uint32_t pad[22];
 };
 static_assert(sizeof(SymmHeader) == 256, "header size");
 
@@ -27,6 +37,19 @@ struct PushArgs {
   int64_t slot_elems;    // elements per source slot (max_tokens * N)
   int64_t flags_off;     // byte offset of the uint32 flag array
   int world, rank, g_max, nt_max;
+};
+
+// Expert-parallel all-to-all region inside every rank's symmetric heap (csrc/comm/ep_a2a.cu);
+// byte offsets from the region base.
+struct EpLayout {
+  int64_t flags_off;   // uint32 [2][8]: dispatch flags (by source), combine flags (by expert owner)
+  int64_t counts_off;  // int32 [world][E_loc]: rows received from each source per local expert
+  int64_t recv_off;    // bf16 [world][cap_src][H]: rows received from each source
+  int64_t meta_off;    // int4 [world][cap_src]: (token * k + choice, local expert, slot within it, 0)
+  int64_t comb_off;    // bf16 [cap_tok * k][H]: expert rows returned to this (source) rank
+  int64_t x_off;       // bf16 [max_tokens][H]: gathered normalised rows (shared with the NVLS kernels)
+  int cap_src;         // rows one source may send one destination
+  int cap_tok;         // owned tokens per rank, at most
 };
 
 }  // namespace gollek

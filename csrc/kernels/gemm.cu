@@ -298,8 +298,14 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
           const int col = n0 + c;
-          if (row < M) {
-            __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+          __nv_bfloat16* dst = C + (int64_t)row * ldc + col;
+          bool store_row = row < M;
+          if constexpr (EPI == kEpiScatter) {  // per-row destination (0: padding row, skipped)
+            const uint64_t rp = store_row ? reinterpret_cast<const uint64_t*>(C)[row] : 0ull;
+            store_row = rp != 0ull;
+            dst = reinterpret_cast<__nv_bfloat16*>(rp) + col;
+          }
+          if (store_row) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               if (col + 8 * j + 8 <= N) {
@@ -574,6 +580,7 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
   if (splits < 1) splits = 1;
   // split-K partials [splits, M_cap, N] are left for the caller to reduce (no reduce pass here)
   throw_if(splits > 1 && (partial == nullptr || epi != kEpiNone), "grouped gemm: split-K needs fp32 partials, no epilogue");
+  throw_if(epi == kEpiScatter && splits > 1, "grouped gemm: the scatter epilogue has no split-K");
 #define GOLLEK_GG_CASE(BNV, EPIV) \
   if (bn == BNV && epi == EPIV)   \
     return launch_gemm_t<BNV, EPIV>(out, ldc, a, lda, b, ldb, nullptr, 0, M_cap, N, K, splits, partial, status, 0, s, \
@@ -583,6 +590,9 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
   GOLLEK_GG_CASE(64, kEpiNone)
   GOLLEK_GG_CASE(256, kEpiSwiglu)
   GOLLEK_GG_CASE(128, kEpiSwiglu)
+  GOLLEK_GG_CASE(256, kEpiScatter)
+  GOLLEK_GG_CASE(128, kEpiScatter)
+  GOLLEK_GG_CASE(64, kEpiScatter)
 #undef GOLLEK_GG_CASE
   throw_if(true, "grouped gemm: unsupported tile width " + std::to_string(bn));
 }

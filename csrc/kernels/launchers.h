@@ -10,6 +10,8 @@
 #include <string>
 #include <vector>
 
+#include "../comm/push.h"
+
 namespace gollek {
 
 inline void throw_if(bool bad, const std::string& msg) {
@@ -62,7 +64,9 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
 // ---- GEMM (K5, K8)
 // Gated epilogues (SwiGLU, GeGLU) read gate/up rows interleaved in groups of 64 and write N/2 columns.
 // kEpiPush: plain output, also pushed to every tensor-parallel peer's inbox (GEMM → all-reduce).
-enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3, kEpiPush = 4 };
+// kEpiScatter: output row r is stored at the address in a per-row table (the `out` argument is a
+// uint64 [M] table; 0 = skip the row); the destinations may be peer memory (NVLink stores)
+enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3, kEpiPush = 4, kEpiScatter = 5 };
 inline bool epi_gated(int epi) { return epi == kEpiSwiglu || epi == kEpiGeglu; }
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
@@ -184,5 +188,29 @@ void launch_tp_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t 
                           float eps, double timeout_s, int grid, cudaStream_t s);
 void launch_tp_allreduce(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int parity, void* out,
                          int64_t numel, double timeout_s, int grid, cudaStream_t s);
+
+// ---- expert-parallel all-to-all (csrc/comm/ep_a2a.cu); EpLayout in csrc/comm/push.h
+int ep_ws_ints(int world, int e_loc);
+void launch_ep_dispatch(const std::vector<uint64_t>& bases, uint64_t mc, const EpLayout& lay, int rank, int e_loc,
+                        int k, const void* x, int64_t ldx, int H, const int* ids, int Tn, int* ws, double timeout_s,
+                        cudaStream_t s);
+void launch_ep_compact(const std::vector<uint64_t>& bases, uint64_t mc, const EpLayout& lay, int rank, int e_loc,
+                       int k, int H, void* xg, uint64_t* comb_ptr, int cap_dst, int* tile_group, int* num_m,
+                       double timeout_s, cudaStream_t s);
+void launch_ep_signal(const std::vector<uint64_t>& bases, uint64_t mc, const EpLayout& lay, int rank, int e_loc,
+                      int k, int H, double timeout_s, cudaStream_t s);
+void launch_ep_combine_norm(const std::vector<uint64_t>& bases, uint64_t mc, const EpLayout& lay, int rank,
+                            int e_loc, int k, int H, int T, int r0, int Tn, const float* wts, void* residual,
+                            const void* w, float eps, double timeout_s, cudaStream_t s);
+void launch_moe_route(const void* x, int64_t ldx, const void* wr, int T, int H, int E, int topk, int renorm,
+                      const MoeRouting& rt, int* ids, float* wts, int* scratch, cudaStream_t s);
+
+// ---- NVLS (multimem) collectives over a multicast-bound symmetric region (csrc/comm/nvls.cu)
+// mode: 0 one-shot, 1 two-shot (x gathered into every rank's x buffer), 2 reduce-scatter (owned rows local)
+void launch_tp_nvls_ar_rmsnorm(uint64_t uc, uint64_t mc, int rank, int world, int64_t p0, int64_t p1, int64_t x_off,
+                               int parity, int mode, void* residual, const void* w, void* x_local, int T, int d,
+                               float eps, double timeout_s, int grid, cudaStream_t s);
+void launch_tp_nvls_allreduce(uint64_t uc, uint64_t mc, int rank, int world, int64_t p0, int64_t p1, int parity,
+                              bool one_shot, void* out, int64_t numel, double timeout_s, int grid, cudaStream_t s);
 
 }  // namespace gollek

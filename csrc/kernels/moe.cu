@@ -489,4 +489,30 @@ void launch_moe_forward(void* out, int64_t ldo, const void* x, int64_t ldx, cons
   check_launch("moe_combine");
 }
 
+// Routing only (expert-parallel all-to-all): physical expert ids and weights of every token; no
+// local expert counting (e_loc = 0).
+void launch_moe_route(const void* x, int64_t ldx, const void* wr, int T, int H, int E, int topk, int renorm,
+                      const MoeRouting& rt, int* ids, float* wts, int* scratch, cudaStream_t s) {
+  throw_if(E > kMaxE || E < 1, "moe route: at most 256 experts");
+  throw_if(topk < 1 || topk > kMaxK || topk > E, "moe route: top-k must be in [1, min(8, E)]");
+  throw_if(H % 256 != 0, "moe route: hidden size must be a multiple of 256");
+  throw_if(rt.n_group < 1 || rt.n_group > 32 || E % rt.n_group != 0 || rt.topk_group < 1 ||
+               rt.topk_group > rt.n_group,
+           "moe route: bad group-limited routing parameters");
+  if (T == 0) return;
+  auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  MoeRouting rr = rt;
+  if (rt.logits != nullptr) {
+    throw_if(E % 2 != 0, "moe: the tensor-core router needs an even expert count");
+    rr.logit_splits = moe_logit_splits(T, E, H);
+    const int kchunk = (H / kLgK + rr.logit_splits - 1) / rr.logit_splits * kLgK;
+    moe_logits_kernel<<<dim3((T + kLgTile - 1) / kLgTile, (E + kLgTile - 1) / kLgTile, rr.logit_splits), 128, 0,
+                        s>>>(xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, rt.logits, kchunk);
+    check_launch("moe_logits");
+  }
+  moe_route_kernel<<<(T + kRouteTok - 1) / kRouteTok, 256, 0, s>>>(
+      xb, ldx, reinterpret_cast<const __nv_bfloat16*>(wr), T, H, E, topk, renorm, 0, 0, rr, ids, wts, scratch);
+  check_launch("moe_route");
+}
+
 }  // namespace gollek

@@ -570,6 +570,9 @@ class EngineConfig:
     tensor_parallel_size: int = 1
     enable_expert_parallel: bool = False  # MoE: experts partitioned over the TP ranks (EP = TP size)
     ep_rebalance_interval: int = 0        # EP: re-place experts by routed load every N engine steps (0 = off)
+    # EP: token-sharded MoE layers with the NVLink all-to-all (dispatch -> grouped expert GEMMs ->
+    # combine) when the TP comm has an NVLink multicast object; otherwise replicated activations
+    ep_all_to_all: bool = True
     # speculative decoding: "none" | "ngram" (prompt lookup) | "draft" (draft model ``draft_model``)
     speculative_method: str = "none"
     num_speculative_tokens: int = 4

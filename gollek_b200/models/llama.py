@@ -89,6 +89,11 @@ class TPComm:
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         return t
 
+    def residual_rows(self, T: int) -> slice:
+        """Rows of the residual stream that ``allreduce_add_rmsnorm`` keeps up to date on this rank
+        (all of them, unless the implementation shards the residual by rows)."""
+        return slice(0, T)
+
     def push_linear(self, a: torch.Tensor, w) -> Optional[torch.Tensor]:
         """Row-parallel GEMM fused with the data movement of the all-reduce that follows (the
         fused comm overrides this); None = run ``ops.linear`` into ``partial_buffer``."""
@@ -192,6 +197,7 @@ class LlamaModel:
         # cases the activations entering the MoE are replicated (attention is tensor parallel), so the
         # rank's output is a partial sum completed by the all-reduce that follows.
         self.expert_parallel = bool(expert_parallel and cfg.is_moe)
+        self.ep_a2a = None  # parallel.ep_a2a.EPAllToAll once enable_ep_all_to_all() succeeded
         self.E_loc, self.e0, self.moe_F = 0, 0, self.F
         if cfg.is_moe:
             E = cfg.num_local_experts
@@ -270,13 +276,27 @@ class LlamaModel:
                 return v.to(dev)
             return v.to(device=dev, dtype=dt)
 
+        def dense(v):
+            if isinstance(v, QWeight):
+                return v.dequantize().to(device=dev, dtype=dt)
+            if isinstance(v, I4.Int4Weight):
+                return v.dequantize(dt).to(dev)
+            return v
+
+        def same_format(ws):
+            return len({(type(w), getattr(w, "qtype", None), getattr(w, "K", None)) for w in ws}) == 1
+
         def cat(ws):
+            if not same_format(ws):  # e.g. a GGUF mixture with a Q6_K v_proj beside Q4_K q/k: dense
+                return torch.cat([dense(w) for w in ws], 0)
             if isinstance(ws[0], I4.Int4Weight):
                 return I4.cat_rows(ws)
             return cat_rows(ws) if isinstance(ws[0], QWeight) else torch.cat(ws, 0)
 
         def gate_up(g, u, fpad=None):
             fpad = self.F_pad if fpad is None else fpad
+            if not same_format([g, u]):
+                g, u = dense(g), dense(u)
             if isinstance(g, quantized):
                 if fpad != g.N:
                     raise ValueError("quantized FFN width must be a multiple of 64 per TP rank")
@@ -707,6 +727,26 @@ class LlamaModel:
             report[li] = {"before": before, "after": after, "moved": len(moves(perm, new, world))}
         return report
 
+    def enable_ep_all_to_all(self, max_tokens: int) -> bool:
+        """Switch the MoE layers to token-sharded expert parallelism over the NVLink all-to-all
+        (parallel.ep_a2a). Needs expert parallelism, dense stacked experts without shared experts,
+        RMSNorm pre-norm blocks and a TP comm with NVLS; the residual stream then stays sharded by
+        rows in every layer. Collective: every rank calls it. Returns whether it is on."""
+        cfg, comm = self.cfg, self.comm
+        ok = (self.expert_parallel and comm.size > 1 and getattr(comm, "nvls", False)
+              and not cfg.sandwich_norm and not cfg.parallel_block and not cfg.norm_center
+              and self.lora is None and cfg.moe_scoring == "softmax"
+              and all("moe_gu" in L and "w_sh_gu" not in L for li, L in enumerate(self.layers)
+                      if cfg.is_moe_layer(li)))
+        if not ok:
+            return False
+        from ..parallel.ep_a2a import EPAllToAll
+        self.ep_a2a = EPAllToAll(comm.rank, comm.size, max_tokens, cfg.hidden_size, self.moe_F_pad,
+                                 cfg.num_local_experts, cfg.num_experts_per_tok, cpu_group=comm.cpu_group,
+                                 pg=comm.pg, timeout_s=comm.timeout_s)
+        comm.nvls_one_shot_max = 0  # every collective keeps the row-sharded residual
+        return True
+
     def _move_experts(self, L: dict, old: np.ndarray, new: np.ndarray) -> None:
         """Placement ``old`` -> ``new`` (physical slot -> logical expert): update the logical ->
         physical expert map, copy the experts that stay on this rank and exchange the others point to
@@ -842,6 +882,21 @@ class LlamaModel:
             if nv:
                 tracing.nvtx_pop()
                 tracing.nvtx_push("allreduce+norm")
+            if self.ep_a2a is not None and cfg.is_moe_layer(li):
+                # token-sharded MoE: reduce-scatter + norm of the owned rows, NVLink all-to-all through
+                # the experts, combine + residual + next norm gathered on every rank
+                from ..parallel.ep_a2a import owned_rows
+                xo = self.comm.reduce_scatter_add_rmsnorm(h, residual, L["post_norm"], eps)
+                r0, Tn = owned_rows(T, self.comm.rank, self.comm.size)
+                nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
+                x = self.ep_a2a.moe(xo[r0:r0 + Tn], residual, L["router"], L["moe_gu"], L["moe_down"], nxt, eps, T,
+                                    renorm=cfg.norm_topk_prob, expert_map=L.get("expert_map"))
+                if nv:
+                    tracing.nvtx_pop()
+                    tracing.nvtx_pop()
+                if off is not None:
+                    off.release(li)
+                continue
             if cfg.sandwich_norm:  # norm(attn) + residual, then the pre-FFN norm
                 h = ops.rms_norm(self.comm.all_reduce(h), L["post_norm"], eps)
                 x = ops.fused_add_rms_norm(h, residual, L["pre_ff_norm"], eps)
@@ -869,7 +924,10 @@ class LlamaModel:
             if off is not None:
                 off.release(li)
         if hidden_only:
-            return x / cfg.logit_scale if cfg.logit_scale != 1.0 else x
+            if cfg.logit_scale != 1.0:
+                return x / cfg.logit_scale
+            # x may be a view of a shared buffer of the TP comm or the all-to-all, rewritten by its next call
+            return x.clone() if (getattr(self.comm, "shares_x", False) or self.ep_a2a is not None) else x
         if meta.logits_indices is not None:
             x = x.index_select(0, meta.logits_indices)
         if greedy:  # token ids: argmax over the vocab shards without gathering the logits

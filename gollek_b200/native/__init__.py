@@ -36,6 +36,8 @@ CUDA_SOURCES = [
     "kernels/gemm.cu",
     "kernels/sampling.cu",
     "comm/symm.cu",
+    "comm/nvls.cu",
+    "comm/ep_a2a.cu",
     "kernels/noalloc.cu",
     "kernels/lora.cu",
     "kernels/gguf.cu",
@@ -49,6 +51,7 @@ CUDA_SOURCES = [
 HOST_SOURCES = [
     "host/host_bindings.cpp",
     "host/gguf_quant.cpp",
+    "host/gguf_kquants.cpp",
     "host/block_allocator.cpp",
     "host/forelen.cpp",
     "host/spec_ngram.cpp",
@@ -121,7 +124,8 @@ def _build(name: str, sources: list, cuda: bool, verbose: bool = False) -> str:
         name=name,
         sources=srcs,
         build_directory=os.path.join(BUILD_DIR, name),
-        extra_cflags=["-O3", "-std=c++17", "-fPIC"],
+        # no fused multiply-add contraction: dequantized values must round as the formats define
+        extra_cflags=["-O3", "-std=c++17", "-fPIC", "-ffp-contract=off"],
         extra_include_paths=[CSRC],
         verbose=verbose,
         is_python_module=True,

@@ -41,19 +41,38 @@ STATUS_PEER_TIMEOUT = 2
 
 
 class SymmHeap:
-    def __init__(self, nbytes: int, rank: int, world: int, group=None, device: Optional[int] = None):
-        ext = cuda_ext()
+    """One region of ``nbytes`` per rank, mapped by every peer.
+
+    Two backends: ``multicast=True`` allocates through torch's symmetric memory (cuMem VMM
+    allocations exchanged between the processes and bound to one NVLink multicast object), which
+    gives the peer addresses *and* a multicast address ``mc`` for the NVLS kernels; otherwise (or
+    when the driver/fabric offers no multicast) a cudaMalloc'd region shared by CUDA IPC handles.
+    ``bases[i]`` is rank i's region as mapped in this process; ``mc`` is 0 without multicast.
+    """
+
+    def __init__(self, nbytes: int, rank: int, world: int, group=None, device: Optional[int] = None,
+                 multicast: bool = False, pg=None):
         self.rank, self.world = rank, world
         dev = torch.cuda.current_device() if device is None else device
-        self.region = ext.symm_alloc(nbytes, dev)  # uint8 tensor over the local region
         self.nbytes = nbytes
+        self.peer_ptrs = {}
+        self.mc = 0
+        self.backend = "ipc"
+        self.multicast_error = ""
+        if multicast and world > 1:
+            try:
+                self._init_multicast(nbytes, rank, dev, pg, group)
+                return
+            except Exception as e:  # no multicast on this system: P2P kernels over IPC instead
+                self.multicast_error = f"{type(e).__name__}: {e}"
+        ext = cuda_ext()
+        self.region = ext.symm_alloc(nbytes, dev)  # uint8 tensor over the local region
         handle = ext.symm_ipc_handle(self.region)
         handles: List[bytes] = [b""] * world
         if world > 1:
             dist.all_gather_object(handles, handle, group=group)
         else:
             handles = [handle]
-        self.peer_ptrs = {}
         bases = []
         for i in range(world):
             if i == rank:
@@ -63,6 +82,36 @@ class SymmHeap:
                 self.peer_ptrs[i] = p
                 bases.append(p)
         self.bases = bases
+
+    def _init_multicast(self, nbytes: int, rank: int, dev: int, pg, group) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+        ok, why, t, hdl = False, "", None, None
+        try:
+            t = symm_mem.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", dev))
+            hdl = symm_mem.rendezvous(t, pg if pg is not None else dist.group.WORLD)
+            ptrs = [int(p) for p in hdl.buffer_ptrs]
+            # the multicast mapping covers the whole block: use it only when this tensor is the block
+            # (offset 0, large enough), so every offset the kernels touch lies inside the mapping
+            if int(hdl.multicast_ptr) == 0:  # no multicast object: no NVLS on this system
+                why = "no multicast support"
+            elif t.data_ptr() != ptrs[rank] or int(hdl.buffer_size) < nbytes or int(getattr(hdl, "offset", 0)):
+                why = f"symmetric tensor not at its block start ({t.data_ptr():#x} vs {ptrs[rank]:#x})"
+            else:
+                ok = True
+        except Exception as e:  # noqa: BLE001 - reported through the agreement below
+            why = f"{type(e).__name__}: {e}"
+        # every rank reaches this agreement, or the ranks would pick different kernels
+        flags = [None] * self.world
+        dist.all_gather_object(flags, (ok, why), group=group)
+        if not all(f[0] for f in flags):
+            raise RuntimeError("; ".join(f"rank {i}: {f[1]}" for i, f in enumerate(flags) if not f[0]))
+        t.zero_()
+        torch.cuda.synchronize(dev)
+        self.region = t
+        self._symm_handle = hdl  # keeps the mappings alive
+        self.bases = [int(p) for p in hdl.buffer_ptrs]
+        self.mc = int(hdl.multicast_ptr)
+        self.backend = "torch-symm+nvls"
 
     def view(self, offset: int, shape, dtype=torch.bfloat16) -> torch.Tensor:
         n = 1
@@ -75,9 +124,10 @@ class SymmHeap:
         return int(cuda_ext().symm_status(self.region))
 
     def close(self) -> None:
-        ext = cuda_ext()
-        for p in self.peer_ptrs.values():
-            ext.symm_close_peer(p)
+        if self.peer_ptrs:
+            ext = cuda_ext()
+            for p in self.peer_ptrs.values():
+                ext.symm_close_peer(p)
         self.peer_ptrs = {}
 
 
@@ -88,8 +138,10 @@ class FusedTPComm(TPComm):
 
     def __init__(self, rank: int, size: int, max_tokens: int, hidden: int, cpu_group=None,
                  timeout_s: float = 5.0, one_shot_max_tokens: int = 128, grid: int = 0,
-                 push_max_tokens: Optional[int] = None):
+                 push_max_tokens: Optional[int] = None, nvls: Optional[bool] = None, pg=None):
         super().__init__(rank, size)
+        if nvls is None:
+            nvls = os.environ.get("GOLLEK_TP_NVLS", "1") != "0"
         self.max_tokens, self.hidden = max_tokens, hidden
         rnd = lambda n: (n + 4095) // 4096 * 4096  # noqa: E731
         buf = rnd(max_tokens * hidden * 2)
@@ -115,7 +167,13 @@ class FusedTPComm(TPComm):
         # C5 argmax candidates: [2 parities][world][max_tokens] packed (logit key, id) words
         self.off_cand = end
         end = self.off_cand + rnd(2 * size * max_tokens * 8)
-        self.heap = SymmHeap(end, rank, size, group=cpu_group)
+        self.cpu_group, self.pg = cpu_group, pg
+        self.heap = SymmHeap(end, rank, size, group=cpu_group, multicast=nvls, pg=pg)
+        # NVLS (multimem through the switch) when the region is bound to a multicast object; the
+        # P2P pull kernels otherwise. Two-shot NVLS keeps the residual stream sharded by rows (each
+        # rank updates only the rows it reduces) and gathers the normalised rows into `off_g`.
+        self.nvls = self.heap.mc != 0
+        self.nvls_one_shot_max = int(os.environ.get("GOLLEK_NVLS_ONE_SHOT_MAX", one_shot_max_tokens))
         self._pushed = None  # (T, n-tiles) of a push GEMM awaiting its consumer
         self.timeout_s = timeout_s
         self.one_shot_max_tokens = one_shot_max_tokens
@@ -168,6 +226,8 @@ class FusedTPComm(TPComm):
             self.calls += 1
             return x
         self._ensure_in_partial(h)
+        if self.nvls:
+            return self._nvls_add_rmsnorm(T, residual, w, eps)
         x = torch.empty_like(residual)
         one_shot = T <= self.one_shot_max_tokens
         cuda_ext().tp_allreduce_add_rmsnorm(self.heap.bases, self.rank, self.off_p[0], self.off_p[1], self.off_g,
@@ -176,11 +236,73 @@ class FusedTPComm(TPComm):
         self.calls += 1
         return x
 
+    @property
+    def shares_x(self) -> bool:
+        """True when ``allreduce_add_rmsnorm`` may return a view of the shared heap (valid until
+        the next collective call): callers that keep it longer must copy it."""
+        return self.nvls
+
+    def residual_rows(self, T: int) -> slice:
+        if self.nvls and T > self.nvls_one_shot_max:  # two-shot NVLS: sequence-parallel residual
+            c = (T + self.size - 1) // self.size
+            return slice(min(T, self.rank * c), min(T, (self.rank + 1) * c))
+        return slice(0, T)
+
+    def _nvls_grid(self, rows: int) -> int:
+        return max(1, min(self.grid * 8, (rows + 7) // 8))  # one warp per row, 8 warps per CTA
+
+    def _nvls_add_rmsnorm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+        one_shot = T <= self.nvls_one_shot_max
+        parity = self.calls % 2
+        if one_shot:
+            x = torch.empty_like(residual)
+            rows = T
+        else:
+            x = self.heap.view(self.off_g, (T, self.hidden))
+            rows = (T + self.size - 1) // self.size
+        cuda_ext().tp_nvls_allreduce_add_rmsnorm(self.heap.bases[self.rank], self.heap.mc, self.rank, self.size,
+                                                 self.off_p[0], self.off_p[1], self.off_g, parity, 0 if one_shot else 1,
+                                                 residual, w, x if one_shot else None, float(eps), self.timeout_s,
+                                                 self._nvls_grid(rows))
+        self.calls += 1
+        return x
+
+    def reduce_scatter_add_rmsnorm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                                   eps: float) -> torch.Tensor:
+        """Sequence-parallel step before an expert-parallel all-to-all: residual rows this rank owns
+        (``residual_rows``) += the sum over ranks of h; returns a [T, d] tensor whose owned rows hold
+        rms_norm(residual) * w (other rows unset). Needs NVLS."""
+        if not self.nvls:
+            raise RuntimeError("reduce_scatter_add_rmsnorm needs NVLS (an NVLink multicast object)")
+        T = h.shape[0]
+        self._ensure_in_partial(h)
+        x = torch.empty_like(residual)
+        rows = (T + self.size - 1) // self.size
+        cuda_ext().tp_nvls_allreduce_add_rmsnorm(self.heap.bases[self.rank], self.heap.mc, self.rank, self.size,
+                                                 self.off_p[0], self.off_p[1], self.off_g, self.calls % 2, 2,
+                                                 residual, w, x, float(eps), self.timeout_s, self._nvls_grid(rows))
+        self.calls += 1
+        return x
+
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.size == 1:
             return t
         flat = t.reshape(-1)
         n = flat.numel()
+        if (self.nvls and n % self.hidden == 0 and n // self.hidden <= self.max_tokens
+                and t.dtype == torch.bfloat16):
+            rows = n // self.hidden
+            self._ensure_in_partial(t.reshape(rows, self.hidden))
+            parity = self.calls % 2
+            one_shot = rows <= self.nvls_one_shot_max
+            grid = max(1, min(self.grid * 4, (n // 8 // (1 if one_shot else self.size) + 1023) // 1024))
+            cuda_ext().tp_nvls_allreduce(self.heap.bases[self.rank], self.heap.mc, self.rank, self.size,
+                                         self.off_p[0], self.off_p[1], parity, one_shot, n,
+                                         t.reshape(-1) if one_shot else None, self.timeout_s, grid)
+            self.calls += 1
+            if one_shot:
+                return t
+            return self.heap.view(self.off_p[parity], tuple(t.shape))
         if n % self.hidden == 0 and n // self.hidden <= self.max_tokens and t.dtype == torch.bfloat16:
             self._ensure_in_partial(t.reshape(-1, self.hidden))
             cuda_ext().tp_allreduce(self.heap.bases, self.rank, self.off_p[0], self.off_p[1], self.calls % 2,

@@ -66,17 +66,33 @@ def test_fused_allreduce_rmsnorm_matches_nccl_2gpu():
                 assert ex < 0.02 and er < 0.02, (rank, T, rep, ex, er)
 
 
+WORLDS = [w for w in (2, 4, 8) if w <= torch.cuda.device_count()] or [2]
+
+
+@pytest.mark.parametrize("world", WORLDS)
+@pytest.mark.parametrize("kind", ["nvls", "p2p"])
+def test_fused_collectives_and_engine_vs_fp32_oracle(world, kind):
+    """The fused TP collectives (all-reduce + residual + RMSNorm at one-shot and two-shot sizes,
+    plain all-reduce, vocab-parallel argmax) and a two-layer Llama-3-8B-shaped TP engine, against
+    fp32 oracles, on every world size the box offers."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from tests.tp_gpu_worker import run_selfcheck
+    res = _spawn(run_selfcheck, world, kind)
+    for rank, out, err in res:
+        assert err is None, err
+        if kind == "nvls" and not out["nvls_active"]:
+            pytest.skip("no NVLink multicast on this system")
+        assert out["collectives"]["ok"], (rank, out["collectives"])
+        assert out["engine"]["ok"] and out["engine"]["ranks_agree"], (rank, out["engine"])
+        moe = out["moe_engine"]
+        assert moe["ok"] and moe["ranks_agree"], (rank, moe)
+        assert moe["ep_all_to_all"] == (kind == "nvls"), (rank, moe)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_engine_tp2_fused_vs_nccl():
-    from tests.tp_worker import run_tp
-    g = torch.Generator().manual_seed(3)
-    prompts = [torch.randint(0, 32000, (n,), generator=g).tolist() for n in (5, 40, 130)]
-    out = {}
-    for kind in ("nccl", "fused"):
-        res = _spawn(run_tp, 2, "nccl", kind, prompts, 8)
-        for rank, toks, err in res:
-            assert err is None, err
-        assert res[0][1] == res[1][1], "ranks disagree"
-        out[kind] = res[0][1]
-    agree = sum(a == b for x, y in zip(out["nccl"], out["fused"]) for a, b in zip(x, y)) / (8 * len(prompts))
-    assert agree >= 0.85, (agree, out)
+def test_engine_tp2_nccl_baseline_vs_fp32_oracle():
+    from tests.tp_gpu_worker import run_selfcheck
+    for rank, out, err in _spawn(run_selfcheck, 2, "nccl"):
+        assert err is None, err
+        assert out["engine"]["ok"], (rank, out["engine"])

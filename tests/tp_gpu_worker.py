@@ -17,8 +17,9 @@ def run_collectives(rank, world, port, result_q):
         from gollek_b200.parallel.symm import FusedTPComm
         init_distributed(backend="nccl", timeout_s=60)
         d = 4096
+        # the P2P pull / push kernels (full residual rows on every rank); NVLS is covered by run_selfcheck
         comm = FusedTPComm(rank, world, max_tokens=1024, hidden=d, cpu_group=cpu_group(), one_shot_max_tokens=16,
-                           push_max_tokens=256)
+                           push_max_tokens=256, nvls=False)
         errs = []
         for T in (1, 7, 16, 300, 1024):
             for rep in range(3):  # consecutive calls exercise the buffer parity and epochs
@@ -83,6 +84,41 @@ def run_collectives(rank, world, port, result_q):
             errs.append((B, "argmax", float((ids != ref).sum()), 0.0))
         comm.check()
         result_q.put((rank, errs, None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+        result_q.put((rank, None, traceback.format_exc()))
+
+
+def run_selfcheck(rank, world, port, kind, result_q):
+    """Collectives and a two-layer TP engine against fp32 oracles (gollek_b200.parallel.selfcheck).
+    ``kind``: "nvls" (multimem kernels), "p2p" (pull kernels) or "nccl" (engine with the NCCL
+    baseline comm)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        import torch.distributed as dist
+        from gollek_b200.parallel import selfcheck as sc
+        from gollek_b200.parallel.dist import NcclComm, cpu_group, init_distributed
+        from gollek_b200.parallel.symm import FusedTPComm
+        init_distributed(backend="nccl", timeout_s=120)
+        out = {}
+        if kind == "nccl":
+            out["engine"] = sc.engine_check(lambda mt, hid: NcclComm(rank, world))
+        else:
+            def make(mt, hid):
+                return FusedTPComm(rank, world, max_tokens=mt, hidden=hid, cpu_group=cpu_group(),
+                                   nvls=(kind == "nvls"))
+            comm = make(8192 + 64, 4096)
+            out["nvls_active"] = comm.nvls
+            out["collectives"] = sc.collectives_check(comm, sizes=(1, 7, 64, 129, 300, 1344, 8192))
+            out["engine"] = sc.engine_check(make)
+            # Mixtral-shaped slice with the experts partitioned over the ranks (the NVLink
+            # all-to-all under NVLS, replicated activations with the P2P kernels)
+            out["moe_engine"] = sc.engine_check(make, model="mixtral-8x7b", expert_parallel=True,
+                                                overrides={"intermediate_size": 2048})
+        result_q.put((rank, out, None))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
