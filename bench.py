@@ -78,6 +78,10 @@ def parse():
     p.add_argument("--rate", type=float, default=0.0,
                    help="poisson arrivals per second (default: 2x the measured steady service rate)")
     p.add_argument("--parallel", default="tp", choices=["tp", "dp"])
+    p.add_argument("--overlap-min-tokens", type=int, default=1024,
+                   help="TP: steps of at least this many tokens run as two halves whose collectives overlap "
+                        "the other half's compute (0 = off)")
+    p.add_argument("--overlap-sms", type=int, default=16, help="SMs the GEMMs leave free for the overlapped collectives")
     return p.parse_args()
 
 
@@ -287,7 +291,8 @@ def main():
                       block_size=16, max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_batched_tokens,
                       max_model_len=args.prompt_max + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
                       enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm,
-                      async_scheduling=not args.no_async)
+                      async_scheduling=not args.no_async, tp_overlap_min_tokens=args.overlap_min_tokens,
+                      tp_overlap_sms=args.overlap_sms)
     comm = None
     check = None
     tp = di.world_size if args.parallel == "tp" else 1
@@ -482,6 +487,8 @@ def main():
         res["check"] = check
     if comm is not None and hasattr(comm, "nvls"):
         res["config"]["comm"] += "+nvls" if comm.nvls else "+p2p"
+        if comm.nvls and args.overlap_min_tokens:
+            res["config"]["comm"] += f"+split-overlap(>={args.overlap_min_tokens} tokens, {args.overlap_sms} SMs)"
     if di.rank == 0:
         print(json.dumps(res))
     eng.runner.graphs.clear()

@@ -6,6 +6,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "common/tma_host.h"
 #include "kernels/launchers.h"
 
 using namespace gollek;
@@ -792,6 +793,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_norm", &ep_combine_norm_py,
         "EP combine: weighted sum of the returned rows + residual + RMSNorm, gathered via multimem.st");
   m.def("gemm_grouped", &gemm_grouped_py, "grouped tcgen05 GEMM (none / SwiGLU / scatter epilogue)");
+  m.def("set_gemm_sm_reserve", [](int64_t n) { gemm_sm_reserve() = (int)n; },
+        "SMs the persistent GEMM grids leave free (for a collective running beside them)");
   m.def("tp_argmax", &tp_argmax_py, "distributed greedy argmax of vocab-parallel logits over P2P (C5)");
   m.def("gemm_push", &gemm_push_py, "row-parallel tcgen05 GEMM pushing its tiles to every rank's inbox (C1)");
   m.def("tp_push_allreduce_add_rmsnorm", &tp_push_ar_rmsnorm_py,

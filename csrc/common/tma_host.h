@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -57,5 +58,13 @@ inline int num_sms() {
   });
   return n;
 }
+
+// SMs kept free of the persistent GEMM grids (0 = none). While a collective of one half of a
+// split batch runs on another stream, the GEMMs of the other half leave it these SMs.
+inline int& gemm_sm_reserve() {
+  static int r = 0;
+  return r;
+}
+inline int gemm_grid_sms() { return std::max(1, num_sms() - gemm_sm_reserve()); }
 
 }  // namespace gollek

@@ -414,7 +414,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   // grouped raster: a ~32 MB slab of A (group_m M-tiles) stays L2-resident while B streams
   const int64_t a_tile_bytes = (int64_t)Cfg::BM * K * 2;
   const int group_m = (int)std::max<int64_t>(1, std::min<int64_t>(num_m, (32ll << 20) / a_tile_bytes));
-  int grid = std::min(tiles * splits, num_sms());
+  int grid = std::min(tiles * splits, gemm_grid_sms());
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
   kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,

@@ -361,7 +361,7 @@ void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const f
   CUtensorMap tb = make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldb, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
   const int64_t a_tile_bytes = (int64_t)kBM * K;
   const int group_m = (int)std::max<int64_t>(1, std::min<int64_t>(num_m, (32ll << 20) / a_tile_bytes));
-  const int grid = std::min(tiles * splits, num_sms());
+  const int grid = std::min(tiles * splits, gemm_grid_sms());
   auto kern = gemm_fp8_kernel<kEpiNone>;
   GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
   kern<<<grid, kThreads, kSmem, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc, sa, sb, M, N, K, group_m,

@@ -573,6 +573,11 @@ class EngineConfig:
     # EP: token-sharded MoE layers with the NVLink all-to-all (dispatch -> grouped expert GEMMs ->
     # combine) when the TP comm has an NVLink multicast object; otherwise replicated activations
     ep_all_to_all: bool = True
+    # tensor parallelism: steps of at least this many tokens run as two halves whose collectives
+    # (on a second stream) overlap the other half's compute; the GEMMs leave `tp_overlap_sms` SMs
+    # free for them (0 = never split)
+    tp_overlap_min_tokens: int = 1024
+    tp_overlap_sms: int = 16
     # speculative decoding: "none" | "ngram" (prompt lookup) | "draft" (draft model ``draft_model``)
     speculative_method: str = "none"
     num_speculative_tokens: int = 4

@@ -112,6 +112,7 @@ class LLMEngine:
         if cfg.enable_expert_parallel and cfg.ep_all_to_all and self.device.type == "cuda" and self.comm.size > 1:
             # token-sharded MoE over the NVLink all-to-all when the comm supports it (collective)
             self.model.enable_ep_all_to_all(cfg.max_num_batched_tokens + cfg.max_num_seqs)
+        self.model.split_sms = cfg.tp_overlap_sms
         self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
         if cfg.kv_cache_dtype not in ("auto", cfg.dtype):
             raise ValueError(f"kv_cache_dtype {cfg.kv_cache_dtype!r}: the KV cache is kept in the model dtype")

@@ -106,6 +106,9 @@ class ModelRunner:
         if self.hybrid:  # per-sequence recurrent-state slot and reset flag (hybrid GDN models)
             self.gdn_host = torch.zeros(2, cfg.max_num_seqs + 1, dtype=torch.int32, pin_memory=self.is_cuda)
         self.d2h_bytes = 0  # device->host bytes read back (sampled token ids)
+        # steps of at least this many tokens run as two halves whose tensor-parallel collectives
+        # overlap the other half's compute (0 = never)
+        self.split_min_tokens = cfg.tp_overlap_min_tokens if cfg.tensor_parallel_size > 1 else 0
 
     # ------------------------------------------------------------------ batch preparation
     def _fill_host(self, out: SchedulerOutput) -> Tuple[int, int, List[Sequence], List[int]]:
@@ -158,6 +161,62 @@ class ModelRunner:
         assert T == t
         h.logits_idx.numpy()[: len(sample_rows)] = sample_rows
         return n, T, sample_seqs, sample_rows
+
+    def _half_meta(self, r0: int, r1: int, s0: int, s1: int, nd: int, positions: torch.Tensor, slots: torch.Tensor,
+                   bt: torch.Tensor, lens: torch.Tensor, cut: Optional[Tuple[int, int, int]]) -> AttnMetadata:
+        """Attention metadata of rows [r0, r1) = sequences [s0, s1) of the step. ``cut`` =
+        (sequence, first row, last row + 1) when a prefill sequence is split between the halves:
+        the first half sees its KV up to the cut, the second half its rows from the cut on."""
+        h = self.host
+        dev = self.device
+        m = AttnMetadata(positions=positions[r0:r1], slot_mapping=slots[r0:r1], num_decode=max(0, min(s1, nd) - s0))
+        ndh = m.num_decode
+        if ndh > 0:
+            m.decode_block_tables = bt[s0:s0 + ndh]
+            m.decode_seq_lens = lens[s0:s0 + ndh]
+            m.decode_splits = self._decode_splits(ndh, int(h.seq_lens[s0:s0 + ndh].max()))
+        p0 = max(s0, nd)
+        if s1 > p0:
+            q_lens, seq_lens = [], []
+            for i in range(p0, s1):
+                a, b = int(h.query_start[i]), int(h.query_start[i + 1])
+                L = int(h.seq_lens[i])
+                if cut is not None and cut[0] == i:
+                    if r0 <= a:      # first half: rows [a, cut) of this sequence, KV up to the cut
+                        L -= b - cut[1]
+                        b = cut[1]
+                    else:            # second half: rows [cut, b), full KV length
+                        a = cut[1]
+                q_lens.append(b - a)
+                seq_lens.append(L)
+            qs = [0]
+            for q in q_lens:
+                qs.append(qs[-1] + q)
+            m.num_prefill_tokens = qs[-1]
+            m.prefill_block_tables = bt[p0:s1]
+            m.prefill_seq_lens = torch.tensor(seq_lens, dtype=torch.int32).to(dev, non_blocking=True)
+            m.prefill_query_start = torch.tensor(qs, dtype=torch.int32).to(dev, non_blocking=True)
+            if self.is_cuda:
+                m.prefill_tiles = ops.prefill_schedule(qs, seq_lens, self.model.H, self.model.Hk,
+                                                       self.model.D).to(dev, non_blocking=True)
+        return m
+
+    def _split_halves(self, n: int, nd: int, T: int, positions: torch.Tensor, slots: torch.Tensor,
+                      bt: torch.Tensor, lens: torch.Tensor) -> tuple:
+        """Rows [0, T) in two halves of about T/2 rows (at a sequence boundary, or inside a prefill
+        sequence): (rows of the first half, metadata of each half)."""
+        qs = self.host.query_start
+        tA = T // 2
+        c = 0
+        while c < n and int(qs[c + 1]) <= tA:
+            c += 1
+        if c >= n or int(qs[c]) == tA:  # a sequence boundary
+            sA, sB, cut = c, c, None
+        else:                            # inside prefill sequence c
+            sA, sB, cut = c + 1, c, (c, tA, int(qs[c + 1]))
+        mA = self._half_meta(0, tA, 0, sA, nd, positions, slots, bt, lens, cut)
+        mB = self._half_meta(tA, T, sB, n, nd, positions, slots, bt, lens, cut)
+        return tA, mA, mB
 
     def _decode_splits(self, nd: int, max_len: int) -> int:
         return ops.decode_splits(nd, self.model.Hk, max_len, self.num_sms, self.block_size)
@@ -267,6 +326,9 @@ class ModelRunner:
             if self.is_cuda:
                 meta.prefill_tiles = ops.prefill_schedule(qs.tolist(), h.seq_lens[nd:n].tolist(), self.model.H,
                                                           self.model.Hk, self.model.D).to(dev, non_blocking=True)
+        if (self.split_min_tokens and T >= self.split_min_tokens and self.model.can_split_batch()
+                and not lora_active and all(c.verify == 0 for c in out.chunks)):
+            meta.halves = self._split_halves(n, nd, T, positions, slots, bt, lens)
         ns = len(sample_rows)
         if ns == 0:
             meta.logits_indices = h.logits_idx[:1].to(dev, non_blocking=True)

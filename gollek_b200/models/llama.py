@@ -62,6 +62,9 @@ class AttnMetadata:
     gdn_slots: Optional[torch.Tensor] = None             # [n] int32
     gdn_reset: Optional[torch.Tensor] = None             # [n] int32
     gdn_query_start: Optional[torch.Tensor] = None       # [n + 1] int32
+    # split batch (tensor-parallel overlap): (rows of the first half, metadata of each half); each
+    # half's collectives run while the other half computes
+    halves: Optional[tuple] = None
 
     @property
     def num_tokens(self) -> int:
@@ -93,6 +96,19 @@ class TPComm:
         """Rows of the residual stream that ``allreduce_add_rmsnorm`` keeps up to date on this rank
         (all of them, unless the implementation shards the residual by rows)."""
         return slice(0, T)
+
+    # split batches (two halves whose collectives overlap the other half's compute)
+    supports_split = False
+
+    def half_partial_buffer(self, half: int, T: int) -> Optional[torch.Tensor]:
+        return None
+
+    def gathered_rows(self, T: int) -> Optional[torch.Tensor]:
+        return None
+
+    def allreduce_add_rmsnorm_half(self, half: int, row0: int, h: torch.Tensor, residual: torch.Tensor,
+                                   w: torch.Tensor, eps: float) -> torch.Tensor:
+        return ops.fused_add_rms_norm(self.all_reduce(h), residual, w, eps)
 
     def push_linear(self, a: torch.Tensor, w) -> Optional[torch.Tensor]:
         """Row-parallel GEMM fused with the data movement of the all-reduce that follows (the
@@ -198,6 +214,7 @@ class LlamaModel:
         # rank's output is a partial sum completed by the all-reduce that follows.
         self.expert_parallel = bool(expert_parallel and cfg.is_moe)
         self.ep_a2a = None  # parallel.ep_a2a.EPAllToAll once enable_ep_all_to_all() succeeded
+        self.split_sms = 16  # SMs the GEMMs leave free while a split batch's collective runs
         self.E_loc, self.e0, self.moe_F = 0, 0, self.F
         if cfg.is_moe:
             E = cfg.num_local_experts
@@ -824,6 +841,103 @@ class LlamaModel:
         q = ops.rope_kv_write(qkv, meta.positions, self.cos_sin, cache, meta.slot_mapping, H, H, D)
         return self._attention(q, cache, meta, 0)
 
+    def can_split_batch(self) -> bool:
+        """Whether ``forward`` can run a step as two halves with overlapped collectives: dense
+        pre-norm decoder layers (no MoE, GDN, MLA, LoRA, offload, sandwich or parallel blocks,
+        centred norms) under a comm that supports it."""
+        cfg = self.cfg
+        return (getattr(self.comm, "supports_split", False) and self.comm.size > 1 and not cfg.is_moe
+                and self.num_gdn_layers == 0 and not cfg.is_mla and self.lora is None and self.offload is None
+                and not cfg.sandwich_norm and not cfg.parallel_block and not cfg.norm_center)
+
+    def _attn_block(self, x: torch.Tensor, L: dict, meta: AttnMetadata, kv_cache, li: int) -> torch.Tensor:
+        """QKV GEMM, RoPE + paged KV write, attention of the rows of ``x`` ([T, H*D] output)."""
+        cfg = self.cfg
+        qkv = ops.linear(x, L["w_qkv"])
+        cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
+        win = self.windows[li]
+        cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
+        if self.cos_sin_none is not None and win == 0:
+            cs = self.cos_sin_none
+        q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
+                              bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                              norm_eps=cfg.rms_norm_eps)
+        return self._attention(q, cache, meta, win).view(x.shape[0], self.H * self.D)
+
+    def _forward_split(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor]):
+        """The decoder layers over a step split in two halves (``meta.halves``): each half's
+        row-parallel GEMM is followed by its all-reduce + residual + RMSNorm on a second
+        (high-priority) stream, so one half's collective runs while the other half computes; the
+        persistent GEMMs leave ``split_sms`` SMs free for it. Returns the final-norm rows [T, H]."""
+        cfg = self.cfg
+        eps = cfg.rms_norm_eps
+        T = input_ids.shape[0]
+        tA, mA, mB = meta.halves
+        spans = [(0, tA, mA), (tA, T, mB)]
+        h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
+        residual = h
+        x0 = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
+        xs = [x0[0:tA], x0[tA:T]]
+        gathered = self.comm.gathered_rows(T)
+        if gathered is None:  # no shared buffer (single process): the halves' rows land here
+            gathered = torch.empty_like(h)
+        cuda = input_ids.is_cuda
+        comp = torch.cuda.current_stream() if cuda else None
+        side = self._split_stream() if cuda else None
+        ready = [None, None]  # event: the half's latest normalised rows are complete
+        ext = None
+        if cuda:
+            from ..native import cuda_ext
+            ext = cuda_ext()
+            ext.set_gemm_sm_reserve(self.split_sms)
+        n = len(self.layers)
+
+        def collective(hi, r0, r1, part, w):
+            if cuda:
+                e = torch.cuda.Event()
+                e.record(comp)
+                with torch.cuda.stream(side):
+                    side.wait_event(e)
+                    out = self.comm.allreduce_add_rmsnorm_half(hi, r0, part, residual[r0:r1], w, eps)
+                    ev = torch.cuda.Event()
+                    ev.record(side)
+                ready[hi] = ev
+            else:
+                out = self.comm.allreduce_add_rmsnorm_half(hi, r0, part, residual[r0:r1], w, eps)
+                if out.data_ptr() != gathered[r0:r1].data_ptr():
+                    gathered[r0:r1].copy_(out)
+                    out = gathered[r0:r1]
+            xs[hi] = out
+
+        try:
+            for li, L in enumerate(self.layers):
+                nxt = self.layers[li + 1]["in_norm"] if li + 1 < n else self.norm
+                for hi, (r0, r1, m) in enumerate(spans):
+                    if ready[hi] is not None:
+                        comp.wait_event(ready[hi])
+                    a = self._attn_block(xs[hi], L, m, kv_cache, li)
+                    part = ops.linear(a, L["w_o"], out=self.comm.half_partial_buffer(hi, r1 - r0))
+                    collective(hi, r0, r1, part, L["post_norm"])
+                for hi, (r0, r1, m) in enumerate(spans):
+                    if ready[hi] is not None:
+                        comp.wait_event(ready[hi])
+                    g = ops.linear_swiglu(xs[hi], L["w_gate_up"], act=cfg.hidden_act)
+                    part = ops.linear(g, L["w_down"], out=self.comm.half_partial_buffer(hi, r1 - r0))
+                    collective(hi, r0, r1, part, nxt)
+            for ev in ready:
+                if ev is not None:
+                    comp.wait_event(ev)
+        finally:
+            if ext is not None:
+                ext.set_gemm_sm_reserve(0)
+        return gathered
+
+    def _split_stream(self):
+        st = getattr(self, "_side_stream", None)
+        if st is None:
+            st = self._side_stream = torch.cuda.Stream(priority=-1)
+        return st
+
     def forward(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor],
                 hidden_only: bool = False, greedy: bool = False) -> torch.Tensor:
         """input_ids [T] int32 → logits [len(logits_indices), vocab] (gathered over TP), or with
@@ -831,6 +945,9 @@ class LlamaModel:
         cfg = self.cfg
         eps = cfg.rms_norm_eps
         T = input_ids.shape[0]
+        if meta.halves is not None and self.can_split_batch():
+            x = self._forward_split(input_ids, meta, kv_cache)
+            return self._head(x, meta, hidden_only, greedy)
         h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
         n = len(self.layers)
@@ -923,6 +1040,11 @@ class LlamaModel:
                 tracing.nvtx_pop()
             if off is not None:
                 off.release(li)
+        return self._head(x, meta, hidden_only, greedy)
+
+    def _head(self, x: torch.Tensor, meta: AttnMetadata, hidden_only: bool, greedy: bool) -> torch.Tensor:
+        """Final-norm rows → hidden states, greedy ids or logits."""
+        cfg = self.cfg
         if hidden_only:
             if cfg.logit_scale != 1.0:
                 return x / cfg.logit_scale

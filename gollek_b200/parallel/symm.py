@@ -237,6 +237,10 @@ class FusedTPComm(TPComm):
         return x
 
     @property
+    def supports_split(self) -> bool:
+        return self.nvls
+
+    @property
     def shares_x(self) -> bool:
         """True when ``allreduce_add_rmsnorm`` may return a view of the shared heap (valid until
         the next collective call): callers that keep it longer must copy it."""
@@ -266,6 +270,36 @@ class FusedTPComm(TPComm):
                                                  self._nvls_grid(rows))
         self.calls += 1
         return x
+
+    # ---- split batches: the rows of a step in two halves whose collectives overlap the other half's compute
+    def half_partial_buffer(self, half: int, T: int) -> torch.Tensor:
+        """Where the row-parallel GEMM of half ``half`` (0 or 1) of a split batch writes its partial."""
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the symmetric buffer ({self.max_tokens})")
+        return self.heap.view(self.off_p[half], (T, self.hidden))
+
+    def gathered_rows(self, T: int) -> torch.Tensor:
+        """The [T, d] buffer the halves' normalised rows are gathered into."""
+        return self.heap.view(self.off_g, (T, self.hidden))
+
+    def allreduce_add_rmsnorm_half(self, half: int, row0: int, h: torch.Tensor, residual: torch.Tensor,
+                                   w: torch.Tensor, eps: float) -> torch.Tensor:
+        """Two-shot NVLS all-reduce + residual + RMSNorm of one half of a split batch: rows
+        [row0, row0 + Th) of the step, partial in half buffer ``half``, ``residual`` the half's rows
+        (row-sharded inside the half), normalised rows gathered into rows [row0, row0 + Th) of
+        ``gathered_rows``. Every call waits for all ranks' stores (barrier C), so each half's
+        buffers can be rewritten by its next GEMM as soon as the call completed on this rank."""
+        Th = h.shape[0]
+        buf = self.half_partial_buffer(half, Th)
+        if h.data_ptr() != buf.data_ptr():
+            buf.copy_(h)
+        x_off = self.off_g + row0 * self.hidden * 2
+        cuda_ext().tp_nvls_allreduce_add_rmsnorm(self.heap.bases[self.rank], self.heap.mc, self.rank, self.size,
+                                                 self.off_p[half], self.off_p[half], x_off, 0, 1, residual, w, None,
+                                                 float(eps), self.timeout_s,
+                                                 self._nvls_grid((Th + self.size - 1) // self.size))
+        self.calls += 1
+        return self.heap.view(x_off, (Th, self.hidden))
 
     def reduce_scatter_add_rmsnorm(self, h: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
                                    eps: float) -> torch.Tensor:
