@@ -686,12 +686,16 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     # -------------------------------------------------------------- Model Context Protocol servers
     @app.post("/v1/admin/mcp/servers")
     async def mcp_connect(body: Dict[str, Any]):
-        name, cmd = body.get("name"), body.get("command")
-        if not name or not isinstance(cmd, list) or not cmd:
-            raise HTTPException(400, "name and command (argv list) are required")
+        """{"name", "command": [argv]} for a stdio server, or {"name", "url", "transport": "sse" | "http",
+        "headers"?} for an HTTP server."""
+        name, cmd, url = body.get("name"), body.get("command"), body.get("url")
+        if not name or not ((isinstance(cmd, list) and cmd) or isinstance(url, str)):
+            raise HTTPException(400, "name and either command (argv list) or url are required")
+        transport = str(body.get("transport", "http" if url else "stdio"))
         try:
-            info = await asyncio.to_thread(st.mcp.connect, str(name), [str(c) for c in cmd],
-                                           float(body.get("timeout_s", 30.0)))
+            info = await asyncio.to_thread(st.mcp.connect, str(name), [str(c) for c in cmd] if cmd else None,
+                                           float(body.get("timeout_s", 30.0)), url, transport,
+                                           body.get("headers"))
         except (MCPError, OSError, ValueError) as e:
             raise HTTPException(502, f"MCP server {name!r}: {e}")
         return {"name": name, "protocolVersion": info.get("protocolVersion"), "serverInfo": info.get("serverInfo")}

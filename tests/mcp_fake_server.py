@@ -10,40 +10,49 @@ TOOLS = [{"name": "add", "description": "add two integers",
                                                                        "properties": {"text": {"type": "string"}}}}]
 
 
-def reply(mid, result=None, error=None):
-    msg = {"jsonrpc": "2.0", "id": mid}
-    msg.update({"error": error} if error else {"result": result})
-    sys.stdout.write(json.dumps(msg) + "\n")
-    sys.stdout.flush()
-
-
-for line in sys.stdin:
-    req = json.loads(line)
+def handle(req):
+    """The JSON-RPC reply to one request (None for a notification)."""
     m, mid, p = req.get("method"), req.get("id"), req.get("params") or {}
     if mid is None:
-        continue  # notification
-    sys.stdout.write(json.dumps({"jsonrpc": "2.0", "method": "notifications/message", "params": {"level": "info"}}) + "\n")
+        return None
+
+    def ok(result):
+        return {"jsonrpc": "2.0", "id": mid, "result": result}
+
+    def err(code, message):
+        return {"jsonrpc": "2.0", "id": mid, "error": {"code": code, "message": message}}
+
     if m == "initialize":
-        reply(mid, {"protocolVersion": p.get("protocolVersion"), "capabilities": {"tools": {}},
-                    "serverInfo": {"name": "fake", "version": "1"}})
-    elif m == "tools/list":
-        reply(mid, {"tools": TOOLS})
-    elif m == "tools/call":
+        return ok({"protocolVersion": p.get("protocolVersion"), "capabilities": {"tools": {}},
+                   "serverInfo": {"name": "fake", "version": "1"}})
+    if m == "tools/list":
+        return ok({"tools": TOOLS})
+    if m == "tools/call":
         a = p.get("arguments", {})
         if p.get("name") == "add":
-            reply(mid, {"content": [{"type": "text", "text": str(int(a["a"]) + int(a["b"]))}], "isError": False})
-        elif p.get("name") == "echo":
-            reply(mid, {"content": [{"type": "text", "text": a.get("text", "")}]})
-        else:
-            reply(mid, error={"code": -32602, "message": "unknown tool"})
-    elif m == "resources/list":
-        reply(mid, {"resources": [{"uri": "mem://readme", "name": "readme"}]})
-    elif m == "resources/read":
-        reply(mid, {"contents": [{"uri": p["uri"], "text": "hello from the resource"}]})
-    elif m == "prompts/list":
-        reply(mid, {"prompts": [{"name": "greet", "arguments": [{"name": "who"}]}]})
-    elif m == "prompts/get":
+            return ok({"content": [{"type": "text", "text": str(int(a["a"]) + int(a["b"]))}], "isError": False})
+        if p.get("name") == "echo":
+            return ok({"content": [{"type": "text", "text": a.get("text", "")}]})
+        return err(-32602, "unknown tool")
+    if m == "resources/list":
+        return ok({"resources": [{"uri": "mem://readme", "name": "readme"}]})
+    if m == "resources/read":
+        return ok({"contents": [{"uri": p["uri"], "text": "hello from the resource"}]})
+    if m == "prompts/list":
+        return ok({"prompts": [{"name": "greet", "arguments": [{"name": "who"}]}]})
+    if m == "prompts/get":
         who = p.get("arguments", {}).get("who", "you")
-        reply(mid, {"messages": [{"role": "user", "content": {"type": "text", "text": f"Say hi to {who}"}}]})
-    else:
-        reply(mid, error={"code": -32601, "message": "method not found"})
+        return ok({"messages": [{"role": "user", "content": {"type": "text", "text": f"Say hi to {who}"}}]})
+    return err(-32601, "method not found")
+
+
+if __name__ == "__main__":
+    for line in sys.stdin:
+        req = json.loads(line)
+        rep = handle(req)
+        if rep is None:
+            continue  # notification
+        sys.stdout.write(json.dumps({"jsonrpc": "2.0", "method": "notifications/message",
+                                     "params": {"level": "info"}}) + "\n")
+        sys.stdout.write(json.dumps(rep) + "\n")
+        sys.stdout.flush()

@@ -83,3 +83,120 @@ def test_mcp_server_routes():
     finally:
         app.state.server.mcp.close()
         ae.shutdown()
+
+
+# ------------------------------------------------------------------------------ HTTP transports
+def _http_server():
+    """A fake MCP server speaking both HTTP transports: streamable HTTP at /mcp (JSON replies, an
+    event-stream reply for tools/call, a session id required after initialize) and HTTP+SSE at
+    /sse (endpoint event) + /messages."""
+    import json as _json
+    import queue as _queue
+    import threading
+    from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
+    from tests.mcp_fake_server import handle
+
+    sessions: dict = {}  # SSE session id -> queue of that connection's outgoing messages
+    sse_q: "_queue.Queue" = _queue.Queue()  # closes every SSE stream when None is put
+
+    class H(BaseHTTPRequestHandler):
+        def log_message(self, *a):
+            pass
+
+        def _body(self):
+            return _json.loads(self.rfile.read(int(self.headers.get("Content-Length", 0))))
+
+        def do_POST(self):
+            if self.path.startswith("/messages"):
+                sid = self.path.split("session=")[-1]
+                rep = handle(self._body())
+                if rep is not None and sid in sessions:
+                    sessions[sid].put(rep)
+                self.send_response(202)
+                self.end_headers()
+                return
+            req = self._body()
+            if req.get("method") != "initialize" and self.headers.get("Mcp-Session-Id") != "s-1":
+                self.send_response(400)
+                self.end_headers()
+                return
+            rep = handle(req)
+            if rep is None:
+                self.send_response(202)
+                self.end_headers()
+                return
+            if req.get("method") == "tools/call":  # reply as an event stream
+                body = ("event: message\ndata: " + _json.dumps(rep) + "\n\n").encode()
+                self.send_response(200)
+                self.send_header("Content-Type", "text/event-stream")
+            else:
+                body = _json.dumps(rep).encode()
+                self.send_response(200)
+                self.send_header("Content-Type", "application/json")
+            if req.get("method") == "initialize":
+                self.send_header("Mcp-Session-Id", "s-1")
+            self.send_header("Content-Length", str(len(body)))
+            self.end_headers()
+            self.wfile.write(body)
+
+        def do_GET(self):
+            if self.path != "/sse":
+                self.send_response(404)
+                self.end_headers()
+                return
+            sid = str(len(sessions) + 1)
+            mine: "_queue.Queue" = _queue.Queue()
+            sessions[sid] = mine
+            self.send_response(200)
+            self.send_header("Content-Type", "text/event-stream")
+            self.end_headers()
+            self.wfile.write(f"event: endpoint\ndata: /messages?session={sid}\n\n".encode())
+            self.wfile.flush()
+            while True:
+                try:
+                    rep = mine.get(timeout=0.2)
+                except _queue.Empty:
+                    if not sse_q.empty():
+                        return
+                    continue
+                if rep is None:
+                    return
+                try:
+                    self.wfile.write(("event: message\ndata: " + _json.dumps(rep) + "\n\n").encode())
+                    self.wfile.flush()
+                except OSError:
+                    return
+
+        def do_DELETE(self):
+            self.send_response(200)
+            self.end_headers()
+
+    srv = ThreadingHTTPServer(("127.0.0.1", 0), H)
+    srv.daemon_threads = True
+    threading.Thread(target=srv.serve_forever, daemon=True).start()
+    return srv, sse_q
+
+
+@pytest.mark.parametrize("transport,path", [("http", "/mcp"), ("sse", "/sse")])
+def test_mcp_http_transports(transport, path):
+    srv, q = _http_server()
+    url = f"http://127.0.0.1:{srv.server_address[1]}{path}"
+    c = MCPClient(url=url, transport=transport, timeout_s=10)
+    try:
+        info = c.initialize()
+        assert info["serverInfo"]["name"] == "fake"
+        if transport == "http":
+            assert c.session_id == "s-1"
+        assert [t["name"] for t in c.list_tools()] == ["add", "echo"]
+        assert tool_text(c.call_tool("add", {"a": 20, "b": 22})) == "42"
+        with pytest.raises(MCPError, match="unknown tool"):
+            c.call_tool("nope")
+        r = MCPRegistry()
+        r.connect("web", url=url, transport=transport, timeout_s=10)
+        assert tool_text(r.call("web__echo", {"text": "over http"})) == "over http"
+        r.close()
+    finally:
+        c.close()
+        q.put(None)
+        q.put(None)
+        srv.shutdown()
