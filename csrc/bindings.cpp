@@ -124,10 +124,19 @@ void silu_mul_out(torch::Tensor out, torch::Tensor x) {
 void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                                 torch::Tensor seq_lens, double scale, int64_t num_splits,
                                 c10::optional<torch::Tensor> workspace, bool tensor_cores, int64_t window,
-                                double softcap) {
+                                double softcap, c10::optional<torch::Tensor> kv_scales) {
   check_bf16(q, "q");
   check_bf16(out, "out");
-  check_bf16(cache, "kv_cache");
+  const float* scl = nullptr;
+  if (kv_scales.has_value()) {  // fp8 e4m3 cache (uint8 storage) + fp32 per-token scales
+    TORCH_CHECK(cache.scalar_type() == at::kByte && cache.is_cuda(), "fp8 kv_cache: uint8 storage on the device");
+    TORCH_CHECK(kv_scales->scalar_type() == at::kFloat && kv_scales->is_contiguous() &&
+                    kv_scales->numel() == cache.numel() / cache.size(4),
+                "kv_scales must be fp32 [NB, 2, Hk, bs]");
+    scl = kv_scales->data_ptr<float>();
+  } else {
+    check_bf16(cache, "kv_cache");
+  }
   check_i32(block_tables, "block_tables");
   check_i32(seq_lens, "seq_lens");
   TORCH_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2), "q must be [B, H, D] with packed heads");
@@ -149,7 +158,8 @@ void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tenso
   launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(),
                       tensor_cores ? (int)cache.size(0) : 0, block_tables.data_ptr<int>(),
                       block_tables.stride(0), seq_lens.data_ptr<int>(), B, H, cache.size(2), D, cache.size(3),
-                      (int)num_splits, (float)scale, po, pml, (int)window, (float)softcap, cur_stream());
+                      (int)num_splits, (float)scale, po, pml, (int)window, (float)softcap, cur_stream(),
+                      scl);
 }
 
 void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
@@ -637,6 +647,32 @@ void ep_combine_norm_py(std::vector<uint64_t> bases, uint64_t mc, std::vector<in
                          (float)eps, timeout_s, cur_stream());
 }
 
+// fp8 KV cache: step rows [T, 2, Hk, D] bf16 -> cache slots (uint8 e4m3 [NB, 2, Hk, bs, D]) + scales
+void kv_quant_fp8_py(torch::Tensor kv, torch::Tensor slots, torch::Tensor cache, torch::Tensor scales) {
+  check_bf16(kv, "kv");
+  check_i32(slots, "slots");
+  TORCH_CHECK(kv.dim() == 4 && kv.is_contiguous() && kv.size(1) == 2, "kv [T, 2, Hk, D]");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 5 && cache.is_contiguous() &&
+                  cache.size(2) == kv.size(2) && cache.size(4) == kv.size(3),
+              "fp8 cache uint8 [NB, 2, Hk, bs, D]");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.numel() == cache.numel() / cache.size(4), "scales fp32");
+  TORCH_CHECK(slots.numel() >= kv.size(0), "one slot per token");
+  launch_kv_quant_fp8(kv.data_ptr(), slots.data_ptr<int>(), cache.data_ptr(), scales.data_ptr<float>(), kv.size(0),
+                      kv.size(2), kv.size(3), cache.size(3), cur_stream());
+}
+
+void kv_dequant_blocks_py(torch::Tensor cache, torch::Tensor scales, torch::Tensor ids, torch::Tensor dst) {
+  check_i32(ids, "ids");
+  check_bf16(dst, "dst");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 5 && cache.is_contiguous(), "fp8 cache");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.numel() == cache.numel() / cache.size(4), "scales fp32");
+  TORCH_CHECK(dst.is_contiguous() && dst.dim() == 5 && dst.size(0) >= ids.numel() && dst.size(1) == 2 &&
+                  dst.size(2) == cache.size(2) && dst.size(3) == cache.size(3) && dst.size(4) == cache.size(4),
+              "dst bf16 [n, 2, Hk, bs, D]");
+  launch_kv_dequant_blocks(cache.data_ptr(), scales.data_ptr<float>(), ids.data_ptr<int>(), ids.numel(),
+                           cache.size(0), cache.size(2), cache.size(4), cache.size(3), dst.data_ptr(), cur_stream());
+}
+
 // Grouped (per-expert) GEMM: out = a · b_g^T per M tile (tile_group names g); epi 0 none, 2 SwiGLU,
 // 5 scatter (`out` is then the uint64 per-row destination table).
 void gemm_grouped_py(torch::Tensor out, torch::Tensor a, torch::Tensor b, int64_t N, int64_t groups, int64_t epi,
@@ -792,6 +828,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_signal", &ep_signal_py, "EP: raise the combine flags of every source rank");
   m.def("ep_combine_norm", &ep_combine_norm_py,
         "EP combine: weighted sum of the returned rows + residual + RMSNorm, gathered via multimem.st");
+  m.def("kv_quant_fp8", &kv_quant_fp8_py, "step K/V rows -> fp8 e4m3 cache slots + per-token scales");
+  m.def("kv_dequant_blocks", &kv_dequant_blocks_py, "fp8 cache blocks -> bf16 blocks (prefill over an fp8 cache)");
   m.def("gemm_grouped", &gemm_grouped_py, "grouped tcgen05 GEMM (none / SwiGLU / scatter epilogue)");
   m.def("set_gemm_sm_reserve", [](int64_t n) { gemm_sm_reserve() = (int)n; },
         "SMs the persistent GEMM grids leave free (for a collective running beside them)");

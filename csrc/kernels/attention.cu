@@ -321,6 +321,33 @@ GOLLEK_DEVICE void mma_bf16_16816(float* d, const uint32_t* a, const uint32_t* b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
+GOLLEK_DEVICE void mma_f16_16816(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+GOLLEK_DEVICE uint32_t pack_f16x2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// four e4m3 values (one 32-bit word, element 0 in the low byte) -> two f16x2 words (exact: every
+// e4m3 value is an f16 value)
+GOLLEK_DEVICE void e4m3x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
+GOLLEK_DEVICE uint32_t bf16x2_to_f16x2(uint32_t v) {
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v);
+  const float2 f = __bfloat1622float2(b);
+  return pack_f16x2(f.x, f.y);
+}
+
 // Swizzled offset (in elements) of 16-byte chunk `ch` of row `r` in a [rows][D] bf16 tile.
 template <int D>
 GOLLEK_DEVICE int swz(int r, int ch) {
@@ -557,29 +584,38 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
 constexpr int kTcStages = 3;
 constexpr int kTcTileBytes = 16 * 128 * 2;            // one K (or V) tile of a paged block
 constexpr int kTcStageBytes = 2 * kTcTileBytes;       // K + V
+// fp8 KV cache (e4m3, a fp32 scale per token and head): the ring holds fp8 tiles (one 16 x 128
+// byte TMA box each, 128-byte swizzle); each warp converts a stage to f16 in its staging tiles
+// (the same swizzled layout as the bf16 tiles) and runs f16 MMAs. Scores are multiplied by the
+// key scales, probabilities by the value scales (the softmax sum uses the unscaled ones).
+constexpr int kTcFp8TileBytes = 16 * 128;
 
 GOLLEK_DEVICE uint32_t sw128_off(int row, int chunk16) {  // byte offset inside a [rows][128 dims] bf16 tile
   const int box = chunk16 >> 3, cc = chunk16 & 7;
   return box * 2048 + row * 128 + ((cc ^ (row & 7)) << 4);
 }
 
-template <int G>
+template <int G, bool FP8>
 __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
-    const __grid_constant__ CUtensorMap tmap,      // cache rows [NB*2*Hk*16, 128] bf16
+    const __grid_constant__ CUtensorMap tmap,      // cache rows [NB*2*Hk*16, 128] bf16 (fp8: 128 bytes)
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ seq_lens, int Hk, int num_splits, float scale_log2, int64_t q_stride,
-    uint32_t* status, int window, float softcap_log2) {
+    uint32_t* status, int window, float softcap_log2, const float* __restrict__ kv_scales) {
   static_assert(G >= 1 && G <= 16, "GQA group must fit the 16 MMA rows");
   constexpr int D = 128, BS = 16;
+  constexpr int kStage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
+  constexpr int kStaging = FP8 ? kTcStageBytes : 0;  // per warp: K and V tiles converted to f16
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = dsm_raw + ((1024 - (smem_u32(dsm_raw) & 1023)) & 1023);
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int H = Hk * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* ring = dsm + warp * kTcStages * kTcStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + kDecodeWarps * kTcStages * kTcStageBytes) + warp * kTcStages;
-  float* sm_o = reinterpret_cast<float*>(dsm + kDecodeWarps * kTcStages * kTcStageBytes + kDecodeWarps * kTcStages * 8);
+  uint8_t* ring = dsm + warp * kTcStages * kStage;
+  uint8_t* stg = dsm + kDecodeWarps * kTcStages * kStage + warp * kStaging;
+  constexpr int kAfter = kDecodeWarps * kTcStages * kStage + kDecodeWarps * kStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + kAfter) + warp * kTcStages;
+  float* sm_o = reinterpret_cast<float*>(dsm + kAfter + kDecodeWarps * kTcStages * 8);
   float* sm_m = sm_o + kDecodeWarps * G * D;
   float* sm_l = sm_m + kDecodeWarps * G;
 
@@ -604,12 +640,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     const int st = j % kTcStages;
     const int pb = bt[blk_begin + warp + kDecodeWarps * j];
     const int rk = ((pb * 2 + 0) * Hk + kh) * BS, rv = ((pb * 2 + 1) * Hk + kh) * BS;
-    uint8_t* dst = ring + st * kTcStageBytes;
-    mbar_arrive_expect_tx(&bars[st], kTcStageBytes);
-    tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
-    tma_load_2d(dst + 2048, &tmap, 64, rk, &bars[st]);
-    tma_load_2d(dst + kTcTileBytes, &tmap, 0, rv, &bars[st]);
-    tma_load_2d(dst + kTcTileBytes + 2048, &tmap, 64, rv, &bars[st]);
+    uint8_t* dst = ring + st * kStage;
+    mbar_arrive_expect_tx(&bars[st], kStage);
+    if constexpr (FP8) {
+      tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
+      tma_load_2d(dst + kTcFp8TileBytes, &tmap, 0, rv, &bars[st]);
+    } else {
+      tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
+      tma_load_2d(dst + 2048, &tmap, 64, rk, &bars[st]);
+      tma_load_2d(dst + kTcTileBytes, &tmap, 0, rv, &bars[st]);
+      tma_load_2d(dst + kTcTileBytes + 2048, &tmap, 64, rv, &bars[st]);
+    }
   };
   int issued = 0;
   if (lane == 0)
@@ -625,6 +666,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     qf[ks][1] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D) : 0u;
     qf[ks][2] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D + 8) : 0u;
     qf[ks][3] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D + 8) : 0u;
+    if constexpr (FP8) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) qf[ks][e] = bf16x2_to_f16x2(qf[ks][e]);
+    }
   }
   float o[16][4];
 #pragma unroll
@@ -641,8 +686,44 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       ok = false;
       break;
     }
-    const uint32_t kt = smem_u32(ring + st * kTcStageBytes);
-    const uint32_t vt = kt + kTcTileBytes;
+    uint32_t kt = smem_u32(ring + st * kStage);
+    uint32_t vt = kt + kTcTileBytes;
+    float ksc[2][2], vsc[2][2];  // fp8: key / value scales of this lane's 4 token columns
+    if constexpr (FP8) {
+      const int pb = bt[blk_begin + warp + kDecodeWarps * j];
+      const float* kp = kv_scales + ((int64_t)(pb * 2 + 0) * Hk + kh) * BS;
+      const float* vp = kv_scales + ((int64_t)(pb * 2 + 1) * Hk + kh) * BS;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          ksc[nt][e] = kp[nt * 8 + cq + e];
+          vsc[nt][e] = vp[nt * 8 + cq + e];
+        }
+      // fp8 tiles (128-byte swizzled rows) -> f16 staging tiles: lane = (token row, half a row)
+      const uint8_t* src = ring + st * kStage;
+      const int row = lane >> 1, c0 = (lane & 1) * 4;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint8_t* tile = src + which * kTcFp8TileBytes;
+        uint8_t* dt = stg + which * kTcTileBytes;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = c0 + i;  // 16 fp8 dims [16c, 16c + 16)
+          const uint4 w = *reinterpret_cast<const uint4*>(tile + row * 128 + ((c ^ (row & 7)) << 4));
+          uint4 lo, hi;
+          e4m3x4_to_f16x4(w.x, lo.x, lo.y);
+          e4m3x4_to_f16x4(w.y, lo.z, lo.w);
+          e4m3x4_to_f16x4(w.z, hi.x, hi.y);
+          e4m3x4_to_f16x4(w.w, hi.z, hi.w);
+          *reinterpret_cast<uint4*>(dt + sw128_off(row, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(dt + sw128_off(row, 2 * c + 1)) = hi;
+        }
+      }
+      __syncwarp();
+      kt = smem_u32(stg);
+      vt = kt + kTcTileBytes;
+    }
     // S = Q K^T : 16 x 16 (two n-tiles of 8 tokens)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -652,8 +733,19 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                    : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
                    : "r"(kt + sw128_off(tok, ch)));
-      mma_bf16_16816(sc[0], qf[ks], bfr);
-      mma_bf16_16816(sc[1], qf[ks], bfr + 2);
+      if constexpr (FP8) {
+        mma_f16_16816(sc[0], qf[ks], bfr);
+        mma_f16_16816(sc[1], qf[ks], bfr + 2);
+      } else {
+        mma_bf16_16816(sc[0], qf[ks], bfr);
+        mma_bf16_16816(sc[1], qf[ks], bfr + 2);
+      }
+    }
+    if constexpr (FP8) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] *= ksc[nt][e & 1];
     }
     const int tok0 = (blk_begin + warp + kDecodeWarps * j) * BS;
     float mx[2] = {-INFINITY, -INFINITY};
@@ -707,8 +799,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       const float p2 = exp2f(sc[nt][2] - mnew[1]), p3 = exp2f(sc[nt][3] - mnew[1]);
       lrow[0] += p0 + p1;
       lrow[1] += p2 + p3;
-      pf[nt * 2 + 0] = pack_bf16x2(p0, p1);
-      pf[nt * 2 + 1] = pack_bf16x2(p2, p3);
+      if constexpr (FP8) {
+        pf[nt * 2 + 0] = pack_f16x2(p0 * vsc[nt][0], p1 * vsc[nt][1]);
+        pf[nt * 2 + 1] = pack_f16x2(p2 * vsc[nt][0], p3 * vsc[nt][1]);
+      } else {
+        pf[nt * 2 + 0] = pack_bf16x2(p0, p1);
+        pf[nt * 2 + 1] = pack_bf16x2(p2, p3);
+      }
     }
     // O += P V : 16 x 128 (16 n-tiles of 8 dims), one k-step of 16 tokens
 #pragma unroll
@@ -718,8 +815,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                    : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
                    : "r"(vt + sw128_off(tok, ch)));
-      mma_bf16_16816(o[2 * jd], pf, bfr);
-      mma_bf16_16816(o[2 * jd + 1], pf, bfr + 2);
+      if constexpr (FP8) {
+        mma_f16_16816(o[2 * jd], pf, bfr);
+        mma_f16_16816(o[2 * jd + 1], pf, bfr + 2);
+      } else {
+        mma_bf16_16816(o[2 * jd], pf, bfr);
+        mma_bf16_16816(o[2 * jd + 1], pf, bfr + 2);
+      }
     }
     __syncwarp();
     if (lane == 0 && issued < nmine) {
@@ -780,26 +882,31 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
   }
 }
 
-template <int G>
+template <int G, bool FP8>
 constexpr size_t decode_tc_smem_bytes() {
-  return 1024 + (size_t)kDecodeWarps * kTcStages * kTcStageBytes + kDecodeWarps * kTcStages * 8 +
+  constexpr size_t stage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
+  constexpr size_t staging = FP8 ? kTcStageBytes : 0;
+  return 1024 + (size_t)kDecodeWarps * kTcStages * stage + kDecodeWarps * staging + kDecodeWarps * kTcStages * 8 +
          (size_t)kDecodeWarps * G * 128 * 4 + 2 * kDecodeWarps * G * 4;
 }
 
-template <int G>
+template <int G, bool FP8>
 void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks, const int* bt,
                       int bt_stride, const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po,
-                      float* pml, int window, float softcap_log2, cudaStream_t s) {
+                      float* pml, int window, float softcap_log2, const float* kv_scales, cudaStream_t s) {
   const uint64_t rows = (uint64_t)num_blocks * 2 * Hk * 16;
-  CUtensorMap tm = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, 128, 16, 64,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
-  constexpr size_t smem = decode_tc_smem_bytes<G>();
-  auto kern = paged_decode_tc_kernel<G>;
+  CUtensorMap tm = FP8 ? make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, 128, 128, 16, 128,
+                                      CU_TENSOR_MAP_SWIZZLE_128B)
+                       : make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, 128, 16, 64,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  constexpr size_t smem = decode_tc_smem_bytes<G, FP8>();
+  auto kern = paged_decode_tc_kernel<G, FP8>;
   GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid(B, Hk, num_splits);
   kern<<<grid, kDecodeWarps * 32, smem, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), po, pml,
                                               reinterpret_cast<const __nv_bfloat16*>(q), bt, bt_stride, lens, Hk,
-                                              num_splits, scale_log2, q_stride, nullptr, window, softcap_log2);
+                                              num_splits, scale_log2, q_stride, nullptr, window, softcap_log2,
+                                              kv_scales);
   check_launch("paged_decode_attention (tensor cores)");
   if (num_splits > 1) {
     decode_combine_kernel<128><<<B * Hk * G, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml,
@@ -834,7 +941,7 @@ namespace gollek {
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         int window, float softcap, cudaStream_t s) {
+                         int window, float softcap, cudaStream_t s, const float* kv_scales) {
   throw_if(block_size != 16, "decode attention is built for block_size 16");
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(num_splits > 1 && (part_o == nullptr || part_ml == nullptr), "split-KV decode needs a workspace");
@@ -842,10 +949,23 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
   const int G = H / Hk;
   const float sl = scale * kLog2e;
   const float cl = softcap > 0.f ? softcap * kLog2e : 0.f;
+  if (kv_scales != nullptr) {  // fp8 e4m3 cache with per-token scales: tensor-core kernel, head_dim 128
+    throw_if(D != 128 || num_blocks <= 0, "fp8 KV cache: decode attention is built for head_dim 128");
+#define GOLLEK_DECODE_TC8(GG) \
+  if (G == GG) return launch_decode_tc<GG, true>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, \
+                                                 B, Hk, num_splits, sl, part_o, part_ml, window, cl, kv_scales, s);
+    GOLLEK_DECODE_TC8(1)
+    GOLLEK_DECODE_TC8(2)
+    GOLLEK_DECODE_TC8(4)
+    GOLLEK_DECODE_TC8(8)
+    GOLLEK_DECODE_TC8(16)
+#undef GOLLEK_DECODE_TC8
+    throw_if(true, "fp8 KV cache: unsupported GQA group " + std::to_string(G));
+  }
   if (D == 128 && num_blocks > 0) {
 #define GOLLEK_DECODE_TC(GG) \
-  if (G == GG) return launch_decode_tc<GG>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, B, Hk, \
-                                           num_splits, sl, part_o, part_ml, window, cl, s);
+  if (G == GG) return launch_decode_tc<GG, false>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, \
+                                                  B, Hk, num_splits, sl, part_o, part_ml, window, cl, nullptr, s);
     GOLLEK_DECODE_TC(1)
     GOLLEK_DECODE_TC(2)
     GOLLEK_DECODE_TC(4)

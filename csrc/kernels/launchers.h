@@ -39,10 +39,12 @@ void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
 // Attention options: window > 0 restricts each query to the `window` most recent keys (sliding
 // window, HF semantics kv > q - window); softcap > 0 applies softcap * tanh(score / softcap) to the
 // scaled scores before the softmax (Gemma-2). 0 disables either.
+// kv_scales != nullptr: the cache holds fp8 e4m3 values with one fp32 scale per (block, K/V, kv head,
+// token) in kv_scales [NB, 2, Hk, 16] (head_dim 128, tensor-core kernel).
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         int window, float softcap, cudaStream_t s);
+                         int window, float softcap, cudaStream_t s, const float* kv_scales = nullptr);
 void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
@@ -204,6 +206,12 @@ void launch_ep_combine_norm(const std::vector<uint64_t>& bases, uint64_t mc, con
                             const void* w, float eps, double timeout_s, cudaStream_t s);
 void launch_moe_route(const void* x, int64_t ldx, const void* wr, int T, int H, int E, int topk, int renorm,
                       const MoeRouting& rt, int* ids, float* wts, int* scratch, cudaStream_t s);
+
+// ---- fp8 e4m3 paged KV cache (csrc/kernels/kv_fp8.cu)
+void launch_kv_quant_fp8(const void* kv, const int* slots, void* cache, float* scales, int T, int Hk, int D,
+                         int block_size, cudaStream_t s);
+void launch_kv_dequant_blocks(const void* cache, const float* scales, const int* ids, int n, int num_blocks, int Hk,
+                              int D, int block_size, void* dst, cudaStream_t s);
 
 // ---- NVLS (multimem) collectives over a multicast-bound symmetric region (csrc/comm/nvls.cu)
 // mode: 0 one-shot, 1 two-shot (x gathered into every rank's x buffer), 2 reduce-scatter (owned rows local)

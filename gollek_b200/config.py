@@ -604,7 +604,7 @@ class EngineConfig:
     block_size: int = 16
     num_gpu_blocks: Optional[int] = None      # None => size from memory fraction
     gpu_memory_utilization: float = 0.85
-    kv_cache_dtype: str = "auto"              # auto (= model dtype)
+    kv_cache_dtype: str = "auto"              # auto (= model dtype) | fp8 (e4m3, a scale per token and head)
     enable_prefix_caching: bool = True
     # KV eviction under memory pressure (opt-in; changes outputs): when the block pool is more than
     # `kv_eviction_threshold` full, the longest running sequences drop their least important KV

@@ -56,6 +56,8 @@ def export_sequence(engine, seq: Sequence, model_id: str = "") -> KVHandoff:
     nb = (n_tok + engine.cfg.block_size - 1) // engine.cfg.block_size
     blocks = engine.kv.tables.blocks(seq.seq_id)[:nb]
     ids = torch.tensor(blocks, dtype=torch.int32)
+    if getattr(engine.model, "kv_scales", None) is not None:
+        raise ValueError("moving KV blocks of an fp8 cache (values + per-token scales) is not supported")
     kv = ops.kv_gather_blocks(engine.kv_cache, ids.to(engine.kv_cache.device))
     return KVHandoff(seq.request_id, model_id or str(engine.cfg.model), list(seq.prompt_token_ids),
                      list(seq.output_token_ids), dataclasses.asdict(seq.params), engine.cfg.block_size, kv,

@@ -76,7 +76,14 @@ class LLMEngine:
             cfg.enable_prefix_caching = False
             cfg.use_cuda_graphs = False
             self.model.alloc_gdn_state(cfg.max_num_seqs + 1)
-        # ---- KV cache
+        # ---- KV cache (bf16, or fp8 e4m3 with a scale per token and head)
+        kv_fp8 = cfg.kv_cache_dtype in ("fp8", "fp8_e4m3")
+        if kv_fp8:
+            if self.model.D != 128 or model_cfg.is_mla:
+                raise ValueError("kv_cache_dtype fp8: attention kernels are built for head_dim 128 (no MLA)")
+            if cfg.kv_eviction:
+                raise ValueError("kv_cache_dtype fp8: KV eviction moves blocks without their scales; not supported")
+            self.model.kv_fp8 = True
         bpb = self.model.kv_bytes_per_block(cfg.block_size)
         nb = num_blocks or cfg.num_gpu_blocks
         if nb is None:
@@ -89,7 +96,10 @@ class LLMEngine:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
             nb = int(t)
         self.num_blocks = nb
-        self.kv_cache = allocate_kv_cache(self.model.kv_cache_shape(nb, cfg.block_size), self.dtype, self.device)
+        shape = self.model.kv_cache_shape(nb, cfg.block_size)
+        self.kv_cache = allocate_kv_cache(shape, torch.uint8 if kv_fp8 else self.dtype, self.device)
+        if kv_fp8:
+            self.model.kv_scales = allocate_kv_cache(shape[:-1], torch.float32, self.device)
         if cfg.speculative_method == "draft" and cfg.enable_prefix_caching:
             # a reused prefix block may carry target KV whose draft-model KV was never computed
             cfg.enable_prefix_caching = False
@@ -114,8 +124,8 @@ class LLMEngine:
             self.model.enable_ep_all_to_all(cfg.max_num_batched_tokens + cfg.max_num_seqs)
         self.model.split_sms = cfg.tp_overlap_sms
         self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
-        if cfg.kv_cache_dtype not in ("auto", cfg.dtype):
-            raise ValueError(f"kv_cache_dtype {cfg.kv_cache_dtype!r}: the KV cache is kept in the model dtype")
+        if cfg.kv_cache_dtype not in ("auto", cfg.dtype, "fp8", "fp8_e4m3"):
+            raise ValueError(f"kv_cache_dtype {cfg.kv_cache_dtype!r}: auto (the model dtype) or fp8 (e4m3)")
         self.evictor = None
         if cfg.kv_eviction:
             from .evicpress import KVEvictor

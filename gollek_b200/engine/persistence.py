@@ -40,6 +40,8 @@ def save_prefix_cache(engine, path: str, max_blocks: int = 0) -> int:
         return 0
     hashes = torch.tensor([h for h, _ in items], dtype=torch.int64)
     ids = torch.tensor([b for _, b in items], dtype=torch.int32)
+    if getattr(engine.model, "kv_scales", None) is not None:
+        raise ValueError("moving KV blocks of an fp8 cache (values + per-token scales) is not supported")
     kv = ops.kv_gather_blocks(engine.kv_cache, ids.to(engine.kv_cache.device))  # [L, n, 2, Hk, bs, D]
     save_file({"hashes": hashes, "kv": kv.transpose(0, 1).contiguous().cpu()}, path,
               {"signature": json.dumps(_signature(engine))})

@@ -215,6 +215,9 @@ class LlamaModel:
         self.expert_parallel = bool(expert_parallel and cfg.is_moe)
         self.ep_a2a = None  # parallel.ep_a2a.EPAllToAll once enable_ep_all_to_all() succeeded
         self.split_sms = 16  # SMs the GEMMs leave free while a split batch's collective runs
+        # fp8 e4m3 KV cache: per (layer, block, K/V, kv head, token) scales [L, NB, 2, Hk, bs] fp32
+        self.kv_fp8 = False
+        self.kv_scales: Optional[torch.Tensor] = None
         self.E_loc, self.e0, self.moe_F = 0, 0, self.F
         if cfg.is_moe:
             E = cfg.num_local_experts
@@ -613,7 +616,12 @@ class LlamaModel:
         return (max(1, self.num_kv_layers), num_blocks, 2, self.Hk, block_size, self.D)
 
     def kv_bytes_per_block(self, block_size: int = 16) -> int:
+        if self.kv_fp8:  # one byte per value + an fp32 scale per token and head
+            return max(1, self.num_kv_layers) * 2 * self.Hk * block_size * (self.D + 4)
         return max(1, self.num_kv_layers) * 2 * self.Hk * block_size * self.D * torch.finfo(self.dtype).bits // 8
+
+    def _kv_scales(self, li: int) -> Optional[torch.Tensor]:
+        return self.kv_scales[self.kv_index[li]] if self.kv_scales is not None else None
 
     def gdn_state_bytes(self, num_slots: int) -> int:
         return self.num_gdn_layers * num_slots * self.Hg * 128 * 128 * 4
@@ -625,18 +633,19 @@ class LlamaModel:
                                          device=self.device)
 
     # ------------------------------------------------------------------ forward
-    def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata, window: int = 0) -> torch.Tensor:
+    def _attention(self, q: torch.Tensor, cache: torch.Tensor, meta: AttnMetadata, window: int = 0,
+                   kv_scales: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty_like(q)
         nd = meta.num_decode
         cap = self.cfg.attn_logit_softcapping
         if nd > 0:
             ops.paged_decode_attention(q[:nd], cache, meta.decode_block_tables, meta.decode_seq_lens, self.scale,
                                        meta.decode_splits, out=out[:nd], workspace=meta.decode_workspace,
-                                       window=window, softcap=cap)
+                                       window=window, softcap=cap, kv_scales=kv_scales)
         if meta.num_prefill_tokens > 0:
             ops.paged_prefill_attention(q[nd:], cache, meta.prefill_block_tables, meta.prefill_seq_lens,
                                         meta.prefill_query_start, self.scale, tiles=meta.prefill_tiles,
-                                        out=out[nd:], window=window, softcap=cap)
+                                        out=out[nd:], window=window, softcap=cap, kv_scales=kv_scales)
         return out
 
     def _row_linear(self, a: torch.Tensor, w, li: int, lora_kind: Optional[str] = None) -> torch.Tensor:
@@ -859,10 +868,11 @@ class LlamaModel:
         cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
         if self.cos_sin_none is not None and win == 0:
             cs = self.cos_sin_none
+        scl = self._kv_scales(li)
         q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
                               bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
-                              norm_eps=cfg.rms_norm_eps)
-        return self._attention(q, cache, meta, win).view(x.shape[0], self.H * self.D)
+                              norm_eps=cfg.rms_norm_eps, kv_scales=scl)
+        return self._attention(q, cache, meta, win, scl).view(x.shape[0], self.H * self.D)
 
     def _forward_split(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor]):
         """The decoder layers over a step split in two halves (``meta.halves``): each half's
@@ -977,10 +987,11 @@ class LlamaModel:
                 cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
                 if self.cos_sin_none is not None and win == 0:
                     cs = self.cos_sin_none
+                scl = self._kv_scales(li)
                 q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
                                       bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
-                                      norm_eps=eps)
-                a = self._attention(q, cache, meta, win).view(T, self.H * self.D)
+                                      norm_eps=eps, kv_scales=scl)
+                a = self._attention(q, cache, meta, win, scl).view(T, self.H * self.D)
             if cfg.parallel_block:  # h = attn(x) + mlp(x): the down GEMM adds the attention partial
                 ha = ops.linear(a, L["w_o"])
                 if self.lora is not None:

@@ -45,6 +45,7 @@ CUDA_SOURCES = [
     "kernels/attention_tc.cu",
     "kernels/moe.cu",
     "kernels/kv_transfer.cu",
+    "kernels/kv_fp8.cu",
     "kernels/int4.cu",
     "kernels/gdn.cu",
 ]

@@ -78,9 +78,20 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
                   num_heads: int, num_kv_heads: int, head_dim: int,
                   q_out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
                   q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None,
-                  norm_eps: float = 1e-6) -> torch.Tensor:
+                  norm_eps: float = 1e-6, kv_scales: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Split fused QKV (+ projection bias), per-head RMSNorm of q and k (QK-norm) when weights
-    are given, NeoX RoPE of q and k, paged KV-cache write; returns q [T, H, D]."""
+    are given, NeoX RoPE of q and k, paged KV-cache write; returns q [T, H, D]. With ``kv_scales``
+    the cache is fp8 e4m3 (uint8 storage): the step's K/V rows go through a bf16 scratch and are
+    quantized into their slots with one scale per token and head (``kv_quant_fp8``)."""
+    if kv_scales is not None and kv_cache is not None:
+        T = qkv.shape[0]
+        step = torch.empty(T, 2, num_kv_heads, 1, head_dim, dtype=torch.bfloat16 if qkv.is_cuda else qkv.dtype,
+                           device=qkv.device)
+        ident = torch.arange(T, dtype=torch.int32, device=qkv.device)
+        q = rope_kv_write(qkv, positions, cos_sin, step, ident, num_heads, num_kv_heads, head_dim, q_out, bias,
+                          q_norm, k_norm, norm_eps)
+        kv_quant_fp8(step.view(T, 2, num_kv_heads, head_dim), slot_mapping, kv_cache, kv_scales)
+        return q
     if not qkv.is_cuda:
         return _cpu(ref.rope_kv_write(qkv, positions, cos_sin, kv_cache, slot_mapping,
                                       num_heads, num_kv_heads, head_dim, bias, q_norm, k_norm, norm_eps), q_out)
@@ -107,10 +118,16 @@ def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables
                            seq_lens: torch.Tensor, scale: float, num_splits: int = 1,
                            out: Optional[torch.Tensor] = None,
                            workspace: Optional[torch.Tensor] = None, tensor_cores: bool = True,
-                           window: int = 0, softcap: float = 0.0) -> torch.Tensor:
+                           window: int = 0, softcap: float = 0.0,
+                           kv_scales: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One query token per sequence: q [B, H, D]. head_dim 128 runs the tensor-core kernel
     (``tensor_cores=False`` selects the CUDA-core kernel, used for other head sizes).
-    ``window`` > 0: sliding-window attention; ``softcap`` > 0: tanh soft-capped scores."""
+    ``window`` > 0: sliding-window attention; ``softcap`` > 0: tanh soft-capped scores.
+    ``kv_scales`` (fp32 [NB, 2, Hk, bs]): ``kv_cache`` holds fp8 e4m3 values (uint8 storage), value =
+    e4m3 * scale of its token and head (head_dim 128)."""
+    if kv_scales is not None and not q.is_cuda:
+        kv_cache = kv_dequant_fp8(kv_cache, kv_scales)
+        kv_scales = None
     if not q.is_cuda:
         B = q.shape[0]
         qsl = torch.arange(B + 1, dtype=torch.int32)
@@ -121,8 +138,53 @@ def paged_decode_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_tables
         workspace = torch.empty(B * H * num_splits * (D + 2), dtype=torch.float32, device=q.device)
     _C(2 if num_splits > 1 else 1).paged_decode_attention(out, q, kv_cache, block_tables, seq_lens, float(scale),
                                                           int(num_splits), workspace, bool(tensor_cores),
-                                                          int(window), float(softcap))
+                                                          int(window), float(softcap), kv_scales)
     return out
+
+
+# ---------------------------------------------------------------------------- fp8 KV cache
+FP8_E4M3_MAX = 448.0
+
+
+def kv_dequant_fp8(cache: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 values of an fp8 e4m3 cache (uint8 storage [..., bs, D]) with per-token scales [..., bs]."""
+    return cache.view(torch.float8_e4m3fn).float() * scales.unsqueeze(-1)
+
+
+def kv_quant_fp8(kv: torch.Tensor, slots: torch.Tensor, cache: torch.Tensor, scales: torch.Tensor) -> None:
+    """Write the step's K/V rows kv [T, 2, Hk, D] into an fp8 e4m3 cache (uint8 [NB, 2, Hk, bs, D])
+    at ``slots``: per (token, K/V, head) scale = absmax / 448, values round-to-nearest saturating."""
+    if kv.is_cuda:
+        _C().kv_quant_fp8(kv.contiguous(), slots, cache, scales)
+        return
+    T, _, Hk, D = kv.shape
+    bs = cache.shape[3]
+    x = kv.float()
+    amax = x.abs().amax(-1)
+    scl = torch.where(amax > 0, amax / FP8_E4M3_MAX, torch.ones_like(amax))
+    q = (x / scl.unsqueeze(-1)).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+    for t in range(T):
+        s = int(slots[t])
+        if s < 0:
+            continue
+        cache[s // bs, :, :, s % bs] = q[t]
+        scales[s // bs, :, :, s % bs] = scl[t]
+
+
+def kv_dequant_blocks(cache: torch.Tensor, scales: torch.Tensor, block_tables: torch.Tensor):
+    """bf16 copy of the blocks an fp8 cache's ``block_tables`` [n, mb] reference, as a [n * mb]-block
+    cache, with the matching [n, mb] table (prefill attention over an fp8 cache)."""
+    n, mb = block_tables.shape
+    ids = block_tables.reshape(-1).contiguous()
+    if not cache.is_cuda:
+        NB = cache.shape[0]
+        safe = ids.long().clamp(0, NB - 1)
+        tmp = kv_dequant_fp8(cache[safe], scales[safe])
+    else:
+        tmp = torch.empty(n * mb, *cache.shape[1:], dtype=torch.bfloat16, device=cache.device)
+        _C().kv_dequant_blocks(cache, scales, ids, tmp)
+    table = torch.arange(n * mb, dtype=torch.int32, device=cache.device).view(n, mb)
+    return tmp, table
 
 
 def prefill_block_m(head_dim: int, tensor_cores: bool = True) -> int:
@@ -177,11 +239,15 @@ def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_table
                             seq_lens: torch.Tensor, query_start: torch.Tensor, scale: float,
                             tiles: Optional[torch.Tensor] = None,
                             out: Optional[torch.Tensor] = None, tensor_cores: bool = True,
-                            window: int = 0, softcap: float = 0.0, emu: Optional[int] = None) -> torch.Tensor:
+                            window: int = 0, softcap: float = 0.0, emu: Optional[int] = None,
+                            kv_scales: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new).
     head_dim 128 runs on tcgen05/TMEM (the two-tile kernel when ``tiles`` is a ``prefill_schedule``
     work list); other sizes on mma.sync (64-row tiles). ``window`` > 0: sliding-window attention;
-    ``softcap`` > 0: tanh soft-capped scores."""
+    ``softcap`` > 0: tanh soft-capped scores. With ``kv_scales`` (fp8 cache) the referenced blocks
+    are dequantized into a bf16 copy first."""
+    if kv_scales is not None:
+        kv_cache, block_tables = kv_dequant_blocks(kv_cache, kv_scales, block_tables)
     if not q.is_cuda:
         return _cpu(ref.paged_attention(q, kv_cache, block_tables, seq_lens, query_start, scale, window, softcap),
                     out)
