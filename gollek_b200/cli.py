@@ -1,7 +1,7 @@
 """Command-line interface: ``python -m gollek_b200 <command>``.
 
 Commands follow the reference CLI (ui/gollek-cli/…/cli/commands/RunCommand.java:45-324 and
-siblings: run, chat, batch, list, show, convert, quantize, serve, providers, stats):
+siblings: run, chat, batch, list, show, convert, quantize, serve, providers, stats, pull):
 
   run       one-shot generation            chat      interactive chat loop
   batch     JSONL prompts → JSONL outputs  serve     HTTP server (OpenAI + gollek routes)
@@ -164,6 +164,20 @@ def cmd_show(args):
     print(f"parameters: {cfg.num_params() / 1e9:.2f} B")
 
 
+def cmd_pull(args):
+    from .utils import hub
+    if args.verify:
+        d = args.dest or os.path.join(os.environ.get("GOLLEK_HOME", os.path.expanduser("~/.gollek")), "models",
+                                      args.repo_id)
+        res = hub.verify(d)
+        print(json.dumps(res, indent=1))
+        if any(v != "ok" for v in res.values()):
+            sys.exit(1)
+        return
+    d = hub.pull(args.repo_id, args.revision, args.dest, args.allow, args.endpoint)
+    print(f"pulled {args.repo_id}@{args.revision} into {d}")
+
+
 def cmd_list(args):
     from .config import PRESETS
     print("presets:")
@@ -236,6 +250,14 @@ def build_parser():
     sh.set_defaults(fn=cmd_show)
     ls = sub.add_parser("list")
     ls.set_defaults(fn=cmd_list)
+    pl = sub.add_parser("pull", help="download a hub repository (resumable, sha256-verified)")
+    pl.add_argument("repo_id")
+    pl.add_argument("--revision", default="main")
+    pl.add_argument("--dest", default=None)
+    pl.add_argument("--allow", nargs="*", default=None, help="file name patterns (default: serving files)")
+    pl.add_argument("--endpoint", default=None)
+    pl.add_argument("--verify", action="store_true", help="re-check an existing pull against its manifest")
+    pl.set_defaults(fn=cmd_pull)
     be = sub.add_parser("bench")
     be.add_argument("rest", nargs=argparse.REMAINDER)
     be.set_defaults(fn=cmd_bench)
