@@ -7,6 +7,8 @@
 //              packed nibbles + the 6-bit scale/min of that sub-block) and applies them to every
 //              token; optional SwiGLU epilogue over gate/up rows interleaved in groups of 64.
 //   q8_0_gemv  same for Q8_0 (lm_head / embeddings of Q4_K_M-style checkpoints).
+//   q6k_gemv   same for Q6_K (the output matrix and the more-bits attn_v / ffn_down tensors of
+//              Q4_K_M files): lane l decodes weights [8l, 8l + 8) of each 210-byte super-block.
 //   dequant_*  whole-matrix dequantization to bf16 (prefill: followed by the tcgen05 GEMM).
 // Block layouts: ggml spec (see csrc/host/gguf_quant.cpp); the reference decodes these only on
 // the CPU (runner/gguf/gollek-gguf-loader/…/gguf/quant/Dequantizer.java, GGUFVectorOps.java:73-88).
@@ -193,6 +195,76 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q8_0_gemv_kernel(__nv_bfloat1
   }
 }
 
+// The 8 Q6_K weights [8g, 8g + 8) of one 210-byte super-block (ql[128] | qh[64] | int8 scales[16] |
+// fp16 d). Element i: half n = i / 128, quarter k = (i % 128) / 32, position p = i % 32; low 4 bits
+// from ql[64n + 32(k % 2) + p] (high nibble when k >= 2), 2 high bits from qh[32n + p] at bit 2k,
+// scale scales[8n + 2k + p / 16]; w = d * scale * (q - 32). Blocks are only 2-byte aligned.
+GOLLEK_DEVICE void q6k_decode8(const uint8_t* blk, int g, float* w) {
+  const int i0 = 8 * g;
+  const int n = i0 >> 7, r = i0 & 127, k = r >> 5, p0 = r & 31;
+  const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + 64 * n + 32 * (k & 1) + p0);
+  const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + 32 * n + p0);
+  const float d = h2f(blk + 208);
+  const float sc = d * (float)reinterpret_cast<const int8_t*>(blk + 192)[8 * n + 2 * k + (p0 >> 4)];
+  const int lshift = (k >> 1) * 4, hshift = 2 * k;
+#pragma unroll
+  for (int e2 = 0; e2 < 4; ++e2) {
+    const uint32_t l2 = ql[e2], h2 = qh[e2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t lo = ((l2 >> (8 * b)) >> lshift) & 0xF;
+      const uint32_t hi = ((h2 >> (8 * b)) >> hshift) & 0x3;
+      w[2 * e2 + b] = sc * (float)((int)(lo | (hi << 4)) - 32);
+    }
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kGemvWarps * 32) q6k_gemv_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                                   const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                   const uint8_t* __restrict__ W, int N, int K,
+                                                                   int M) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kGemvWarps + warp;
+  if (row >= N) return;
+  const int nblk = K / 256;
+  const uint8_t* wr = W + (int64_t)row * nblk * 210;
+  float acc[NT];
+#pragma unroll
+  for (int m = 0; m < NT; ++m) acc[m] = 0.f;
+  for (int b = 0; b < nblk; ++b) {
+    float w[8];
+    q6k_decode8(wr + (int64_t)b * 210, lane, w);
+#pragma unroll
+    for (int m = 0; m < NT; ++m) {
+      if (m < M) {
+        float xv[8];
+        bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 256 + lane * 8)), xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m] = fmaf(w[e], xv[e], acc[m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < NT; ++m) {
+    if (m < M) {
+      const float s = warp_sum(acc[m]);
+      if (lane == 0) y[(int64_t)m * ldy + row] = __float2bfloat16(s);
+    }
+  }
+}
+
+__global__ void dequant_q6k_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ W, int64_t nblocks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t b = wid; b < nblocks; b += nw) {
+    float w[8];
+    q6k_decode8(W + b * 210, lane, w);
+    *reinterpret_cast<uint4*>(out + b * 256 + lane * 8) = float_to_bf16x8(w);
+  }
+}
+
 // One 256-weight super-block per warp-iteration: lane l writes its 8 decoded weights.
 __global__ void dequant_q4k_kernel(__nv_bfloat16* __restrict__ out, const uint8_t* __restrict__ W,
                                    int64_t nblocks) {
@@ -247,6 +319,7 @@ void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const vo
   throw_if(M < 1 || M > kGemvMaxTok, "gguf gemv: 1..16 tokens");
   throw_if(qtype == 12 && K % 256 != 0, "Q4_K: K must be a multiple of 256");
   throw_if(qtype == 8 && K % 32 != 0, "Q8_0: K must be a multiple of 32");
+  throw_if(qtype == 14 && K % 256 != 0, "Q6_K: K must be a multiple of 256");
   throw_if(swiglu && (qtype != 12 || N % 128 != 0), "gguf gemv swiglu: Q4_K with N % 128 == 0");
   const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
   auto* yp = reinterpret_cast<__nv_bfloat16*>(y);
@@ -279,6 +352,19 @@ void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const vo
     GOLLEK_Q8(8)
     GOLLEK_Q8(16)
 #undef GOLLEK_Q8
+  } else if (qtype == 14) {
+    const int grid = (N + kGemvWarps - 1) / kGemvWarps;
+#define GOLLEK_Q6(NT)                                                                                 \
+  if (M <= NT) {                                                                                    \
+    q6k_gemv_kernel<NT><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);           \
+    check_launch("q6k_gemv");                                                                       \
+    return;                                                                                         \
+  }
+    GOLLEK_Q6(1)
+    GOLLEK_Q6(4)
+    GOLLEK_Q6(8)
+    GOLLEK_Q6(16)
+#undef GOLLEK_Q6
   }
   throw_if(true, "gguf gemv: unsupported ggml type " + std::to_string(qtype));
 }
@@ -295,6 +381,11 @@ void launch_gguf_dequant(void* out, const void* W, int qtype, int64_t numel, cud
     throw_if(numel % 32 != 0, "Q8_0 dequant: size");
     const int64_t nq = numel / 8;
     dequant_q8_0_kernel<<<(unsigned)((nq + 255) / 256), 256, 0, s>>>(op, wp, numel / 32);
+  } else if (qtype == 14) {
+    throw_if(numel % 256 != 0, "Q6_K dequant: size");
+    const int64_t nb = numel / 256;
+    const int grid = (int)std::min<int64_t>((nb + 7) / 8, 148 * 16);
+    dequant_q6k_kernel<<<grid, 256, 0, s>>>(op, wp, nb);
   } else {
     throw_if(true, "gguf dequant: unsupported ggml type " + std::to_string(qtype));
   }

@@ -58,7 +58,7 @@ GGML_TYPES = {
     GGML_BF16: ("BF16", 1, 2),
 }
 # types kept in their blocks on the GPU by the dequant-fused kernels
-SERVED_QUANTIZED = (GGML_Q8_0, GGML_Q4_K)
+SERVED_QUANTIZED = (GGML_Q8_0, GGML_Q4_K, GGML_Q6_K)
 
 
 def dequantize_blocks(raw: torch.Tensor, ggml_type: int, n: int) -> torch.Tensor:

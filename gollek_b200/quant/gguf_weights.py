@@ -17,8 +17,8 @@ from typing import List, Sequence
 
 import torch
 
-GGML_Q8_0, GGML_Q4_K = 8, 12
-BLOCK = {GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144)}
+GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 8, 12, 14
+BLOCK = {GGML_Q8_0: (32, 34), GGML_Q4_K: (256, 144), GGML_Q6_K: (256, 210)}
 
 
 class QWeight:

@@ -114,12 +114,14 @@ def test_gguf_py_written_q6_k_file_loads(tmp_path):
 
 
 def test_serve_mixed_q4_k_m_file_on_cpu(tmp_path):
-    """Q4_K tensors stay in their blocks (dequant-fused path), Q6_K ones are dequantized at load; the
-    greedy tokens match the fp32 oracle over the file's dequantized weights."""
+    """Q4_K and Q6_K tensors stay in their blocks (dequant-fused kernels; a fused q/k/v whose parts
+    differ in type is dequantized for that layer); the greedy tokens match the fp32 oracle over the
+    file's dequantized weights."""
     cfg, _, p = _mixed_file(tmp_path)
     cfg_q, wq, _ = G.load_llama_gguf(p, keep_quantized=True)
     assert isinstance(wq["model.layers.3.self_attn.q_proj.weight"], G.QuantizedWeight)
-    assert not isinstance(wq["model.layers.0.self_attn.v_proj.weight"], G.QuantizedWeight)  # Q6_K
+    assert isinstance(wq["model.layers.0.self_attn.v_proj.weight"], G.QuantizedWeight)  # Q6_K
+    assert wq["model.layers.0.self_attn.v_proj.weight"].ggml_type == G.GGML_Q6_K
     deq = {k: (v.dequantize() if isinstance(v, G.QuantizedWeight) else v) for k, v in wq.items()}
     prompt = torch.randint(0, cfg.vocab_size, (16,), generator=torch.Generator().manual_seed(2)).tolist()
     ref = ReferenceDecoder(cfg_q, deq).greedy(prompt, 5)[0]
@@ -128,3 +130,23 @@ def test_serve_mixed_q4_k_m_file_on_cpu(tmp_path):
     eng = LLMEngine(ec, model_cfg=cfg_q, weights=wq.__getitem__, num_blocks=16)
     out = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=5, ignore_eos=True))[0]
     assert out.output_token_ids == ref
+
+
+@pytest.mark.gpu
+def test_q6_k_gpu_dequant_and_gemv():
+    """Q6_K weights kept in their blocks on the GPU: dequantization equals the host decoder (bf16 of
+    the same fp32 values) and the decode GEMV matches x @ W^T for 1..16 tokens."""
+    from gollek_b200 import ops
+    from gollek_b200.quant.gguf_weights import QWeight
+    N, K = 768, 1024
+    w = torch.randn(N, K, generator=torch.Generator().manual_seed(6)) * 0.02
+    raw = G.quantize_blocks(w, G.GGML_Q6_K)
+    qw = QWeight(raw.cuda(), N, K, G.GGML_Q6_K)
+    host = G.dequantize_blocks(raw, G.GGML_Q6_K, N * K).view(N, K)
+    wd = qw.dequantize()
+    assert torch.equal(wd.cpu(), host.bfloat16())
+    for M in (1, 3, 16, 40):  # GEMV up to 16 rows, dequant + tcgen05 GEMM above
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        y = ops.linear(x, qw)
+        ref = x.float() @ host.cuda().t()
+        torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
