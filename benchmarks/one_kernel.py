@@ -5,6 +5,11 @@
     python benchmarks/one_kernel.py prefill --nseq 4 --L 2048
     python benchmarks/one_kernel.py moe --T 256 --e-loc 1      (Mixtral-8x7B layer, one EP=8 shard)
     python benchmarks/one_kernel.py gdn --nseq 256 --L 1       (gated delta rule decode, 32 heads)
+    python benchmarks/one_kernel.py decode_fp8 --B 64 --ctx 4096  (decode over an fp8 e4m3 KV cache)
+    python benchmarks/one_kernel.py q6k --M 1 --N 28672 --K 4096  (Q6_K decode GEMV)
+    python benchmarks/one_kernel.py fp8gemm --M 64 --N 1280 --K 8192 (block-scaled fp8 GEMM)
+The last three also print a CUDA-event time and the achieved fraction of the measured HBM copy
+bandwidth or sustained bf16 peak (fp8 GEMM: of twice it, the nominal fp8/bf16 ratio).
 """
 from __future__ import annotations
 
@@ -22,7 +27,8 @@ from gollek_b200 import ops  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn"])
+    ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn", "decode_fp8", "q6k",
+                                     "fp8gemm"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -88,6 +94,60 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         for _ in range(a.reps):
             ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
+    elif a.kind in ("decode_fp8", "q6k", "fp8gemm"):
+        HBM_GBS, BF16_TFLOPS = 6534.5, 1400.9  # measured copy bandwidth and sustained bf16 GEMM peak
+        if a.kind == "decode_fp8":
+            Hq, Hk, D, bs = 32, 8, 128, 16
+            nblk = (a.ctx + bs - 1) // bs
+            NB = a.B * nblk
+            cache = torch.randint(0, 120, (NB, 2, Hk, bs, D), dtype=torch.uint8, device=dev)  # finite e4m3
+            scl = torch.rand(NB, 2, Hk, bs, device=dev) * 0.01
+            bt = torch.randperm(NB, device=dev).int().view(a.B, nblk)
+            sl = torch.full((a.B,), a.ctx, dtype=torch.int32, device=dev)
+            q = torch.randn(a.B, Hq, D, device=dev).bfloat16()
+            sp = ops.decode_splits(a.B, Hk, a.ctx)
+
+            def fn():
+                ops.paged_decode_attention(q, cache, bt, sl, 1 / math.sqrt(D), sp, kv_scales=scl)
+            nbytes = cache.numel() + scl.numel() * 4
+            flops = None
+        elif a.kind == "q6k":
+            from gollek_b200.loaders import gguf as G
+            from gollek_b200.quant.gguf_weights import QWeight
+            raw = torch.randint(0, 255, (a.N * a.K // 256 * 210,), dtype=torch.uint8)
+            raw.view(-1, 210)[:, 208:210] = torch.tensor([0x00, 0x20], dtype=torch.uint8)  # d = 2^-7 (fp16)
+            qw = QWeight(raw.to(dev), a.N, a.K, G.GGML_Q6_K)
+            x = torch.randn(a.M, a.K, device=dev).bfloat16()
+
+            def fn():
+                ops.linear(x, qw)
+            nbytes = raw.numel()
+            flops = None
+        else:
+            from gollek_b200.quant.fp8 import quantize_weight
+            w8 = quantize_weight((torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16())
+            x = torch.randn(a.M, a.K, device=dev).bfloat16()
+
+            def fn():
+                ops.linear(x, w8)
+            nbytes = a.N * a.K + a.M * a.K * 2
+            flops = 2.0 * a.M * a.N * a.K
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record()
+        for _ in range(a.reps):
+            fn()
+        ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / a.reps
+        res = {"kind": a.kind, "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
+               "hbm_frac_of_measured": round(nbytes / ms / 1e6 / HBM_GBS, 3)}
+        if flops:
+            res["TFLOPs"] = round(flops / ms / 1e9, 1)
+            res["frac_of_2x_measured_bf16"] = round(flops / ms / 1e9 / (2 * BF16_TFLOPS), 3)
+        print(json.dumps(res))
     elif a.kind == "decode":
         Hq, Hk, D, bs = 32, 8, 128, 16
         nblk = (a.ctx + bs - 1) // bs

@@ -38,7 +38,7 @@ def _dtype(name: str) -> torch.dtype:
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, model_cfg: Optional[ModelConfig] = None,
                  weights: Optional[Callable[[str], torch.Tensor]] = None, comm: Optional[TPComm] = None,
-                 tokenizer=None, num_blocks: Optional[int] = None):
+                 tokenizer=None, num_blocks: Optional[int] = None, vision=None):
         self.cfg = cfg
         self.comm = comm or TPComm()
         dev = cfg.device
@@ -47,9 +47,17 @@ class LLMEngine:
         self.device = torch.device(dev)
         self.dtype = _dtype(cfg.dtype) if self.device.type == "cuda" else torch.float32
         self.tokenizer = tokenizer
+        # image encoder + projector of a vision-language checkpoint (models/vlm.py), or None
+        self.vision = vision
         # ---- model
         if model_cfg is None:
-            model_cfg, weights, tok = load_model_source(cfg.model, keep_quantized=cfg.quantization == "gguf")
+            if _is_llava(cfg.model):
+                from ..models.vlm import load_llava
+                from ..utils.tokenizer import load_tokenizer
+                model_cfg, weights, self.vision = load_llava(cfg.model, str(self.device), self.dtype)
+                tok = load_tokenizer(cfg.model)
+            else:
+                model_cfg, weights, tok = load_model_source(cfg.model, keep_quantized=cfg.quantization == "gguf")
             self.tokenizer = self.tokenizer or tok
         self.model_cfg = model_cfg
         self.model = LlamaModel(model_cfg, device=str(self.device), dtype=self.dtype, comm=self.comm,
@@ -169,7 +177,10 @@ class LLMEngine:
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: Optional[str], prompt: Union[str, List[int]],
                     params: Optional[SamplingParams] = None, lora_id: int = 0,
-                    arrival_time: Optional[float] = None, priority: int = 0, tenant: str = "") -> str:
+                    arrival_time: Optional[float] = None, priority: int = 0, tenant: str = "",
+                    images: Optional[list] = None) -> str:
+        """``images``: PIL images, HxWx3 uint8 arrays or pixel tensors [3, S, S] of a vision-language
+        model, one per image placeholder token in the prompt (in order)."""
         request_id = request_id or uuid.uuid4().hex
         if request_id in self.seqs:
             raise ValueError(f"duplicate request id {request_id}")
@@ -182,6 +193,9 @@ class LLMEngine:
             ids = list(prompt)
         if not ids:
             raise ValueError("empty prompt")
+        mm = None
+        if images:
+            ids, mm = self._image_rows(ids, images)
         if max(ids) >= self.model_cfg.vocab_size or min(ids) < 0:
             raise ValueError("prompt token id out of range")
         room = self.cfg.max_model_len - len(ids)
@@ -192,6 +206,8 @@ class LLMEngine:
             raise ValueError(f"unknown LoRA adapter id {lora_id}")
         seq = Sequence(request_id, ids, params, lora_id=lora_id, arrival_time=arrival_time, priority=priority)
         seq.tenant = tenant or ""
+        if mm is not None:
+            seq.mm_embeds, seq.mm_positions, seq.cache_salt = mm
         if params.guided:
             seq.guide = self._make_guide(params)
         self.scheduler.add(seq)
@@ -200,6 +216,35 @@ class LLMEngine:
         self.seqs[request_id] = seq
         self.metrics.on_arrival()
         return request_id
+
+    @property
+    def image_placeholder(self) -> Optional[str]:
+        """Prompt text that the tokenizer encodes to the image placeholder token (None: no vision)."""
+        if self.vision is None:
+            return None
+        idx = self.vision.image_token_index
+        fn = getattr(self.tokenizer, "token_text", None)
+        t = fn(idx) if fn is not None else None
+        return t if t else "<image>"
+
+    def _image_rows(self, ids: List[int], images: list):
+        """Expand the image placeholders of ``ids`` and encode the images: (ids, (projected rows,
+        their prompt positions, a salt from the pixel content))."""
+        if self.vision is None:
+            raise ValueError("this model takes no images")
+        from ..models.vlm import expand_image_tokens, preprocess_image
+        v = self.vision
+        n_ph = sum(1 for t in ids if t == v.image_token_index)
+        if n_ph != len(images):
+            raise ValueError(f"{len(images)} images for {n_ph} image placeholder tokens")
+        size = v.vcfg.image_size
+        pv = torch.stack([im.float() if isinstance(im, torch.Tensor) else preprocess_image(im, size)
+                          for im in images])
+        feats = v.encode(pv)  # [n, per_image, hidden]
+        ids, pos = expand_image_tokens(ids, v.image_token_index, v.tokens_per_image)
+        salt = hash(pv.numpy().tobytes()) & ((1 << 62) - 1) or 1
+        rows = feats.reshape(-1, feats.shape[-1]).to(self.device, self.dtype)
+        return ids, (rows, pos, salt)
 
     def _make_guide(self, params: SamplingParams):
         """A constrained-decoding matcher for one request (vocabulary trie built on first use)."""
@@ -495,19 +540,33 @@ class LLMEngine:
         return beam_search(self, ids, params or BeamParams(), lora_id)
 
     def generate(self, prompts: Seq[Union[str, List[int]]], params: Union[SamplingParams, List[SamplingParams], None] = None,
-                 lora_ids: Optional[List[int]] = None) -> List[RequestOutput]:
+                 lora_ids: Optional[List[int]] = None, images: Optional[List[Optional[list]]] = None
+                 ) -> List[RequestOutput]:
         ids = []
         for i, p in enumerate(prompts):
             sp = params[i] if isinstance(params, list) else (params or SamplingParams())
             sp = SamplingParams(**vars(sp))
             ids.append(self.add_request(f"gen-{uuid.uuid4().hex[:8]}-{i}", p, sp,
-                                        lora_id=lora_ids[i] if lora_ids else 0))
+                                        lora_id=lora_ids[i] if lora_ids else 0,
+                                        images=images[i] if images else None))
         final: Dict[str, RequestOutput] = {}
         while self.has_unfinished():
             for o in self.step():
                 if o.finished:
                     final[o.request_id] = o
         return [final[i] for i in ids]
+
+
+def _is_llava(source: str) -> bool:
+    """A checkpoint directory of a LLaVA-layout vision-language model."""
+    import json
+    p = os.path.join(source, "config.json") if os.path.isdir(source) else None
+    if p is None or not os.path.exists(p):
+        return False
+    with open(p) as fh:
+        c = json.load(fh)
+    archs = c.get("architectures") or []
+    return c.get("model_type") == "llava" or any("Llava" in a for a in archs)
 
 
 def load_model_source(source: str, keep_quantized: bool = False):

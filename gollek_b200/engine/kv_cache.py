@@ -24,7 +24,13 @@ from .sequence import Sequence
 _MASK63 = (1 << 63) - 1
 
 
-def block_hash(parent: int, tokens: List[int], salt: int = 0) -> int:
+def _salt(seq) -> object:
+    """Hash salt of a sequence's blocks: its LoRA adapter, and for multimodal prompts the image
+    content (placeholder token ids are equal for every image)."""
+    return seq.lora_id if not getattr(seq, "cache_salt", 0) else (seq.lora_id, seq.cache_salt)
+
+
+def block_hash(parent: int, tokens: List[int], salt: object = 0) -> int:
     """Chain hash of one full block (stable within a process; 63-bit, non-negative)."""
     return hash((parent, salt, tuple(tokens))) & _MASK63
 
@@ -85,7 +91,7 @@ class KVCacheManager:
         reused = 0
         for i in range(max_blocks):
             self.prefix_queries += 1
-            hsh = block_hash(parent, seq.tokens(i * bs, (i + 1) * bs), seq.lora_id)
+            hsh = block_hash(parent, seq.tokens(i * bs, (i + 1) * bs), _salt(seq))
             b = self.pool.lookup(hsh)
             if b < 0:
                 break
@@ -125,7 +131,7 @@ class KVCacheManager:
         blocks = self.tables.blocks(seq.seq_id)
         parent = seq.block_hashes[-1] if seq.block_hashes else 0
         for i in range(len(seq.block_hashes), full):
-            hsh = block_hash(parent, seq.tokens(i * bs, (i + 1) * bs), seq.lora_id)
+            hsh = block_hash(parent, seq.tokens(i * bs, (i + 1) * bs), _salt(seq))
             self.pool.insert(blocks[i], hsh)
             seq.block_hashes.append(hsh)
             parent = hsh

@@ -218,6 +218,25 @@ class ModelRunner:
         mB = self._half_meta(tA, T, sB, n, nd, positions, slots, bt, lens, cut)
         return tA, mA, mB
 
+    def _mm_meta(self, out: SchedulerOutput, meta: AttnMetadata) -> None:
+        """Batch rows of image positions in this step's prompt chunks, with their projected rows."""
+        import bisect
+        rows, embs = [], []
+        r = 0
+        for c in out.chunks:
+            seq = c.seq
+            pos = seq.mm_positions
+            if pos is not None and c.start < len(seq.prompt_token_ids):
+                lo, hi = c.start, c.start + c.num_tokens
+                j0, j1 = bisect.bisect_left(pos, lo), bisect.bisect_left(pos, hi)
+                if j1 > j0:
+                    rows.extend(r + p - lo for p in pos[j0:j1])
+                    embs.append(seq.mm_embeds[j0:j1])
+            r += c.num_tokens
+        if rows:
+            meta.mm_rows = torch.tensor(rows, dtype=torch.int64).to(self.device, non_blocking=True)
+            meta.mm_embeds = torch.cat(embs).to(self.device)
+
     def _decode_splits(self, nd: int, max_len: int) -> int:
         return ops.decode_splits(nd, self.model.Hk, max_len, self.num_sms, self.block_size)
 
@@ -326,6 +345,8 @@ class ModelRunner:
             if self.is_cuda:
                 meta.prefill_tiles = ops.prefill_schedule(qs.tolist(), h.seq_lens[nd:n].tolist(), self.model.H,
                                                           self.model.Hk, self.model.D).to(dev, non_blocking=True)
+        if any(c.seq.mm_positions is not None for c in out.chunks):
+            self._mm_meta(out, meta)
         if (self.split_min_tokens and T >= self.split_min_tokens and self.model.can_split_batch()
                 and not lora_active and all(c.verify == 0 for c in out.chunks)):
             meta.halves = self._split_halves(n, nd, T, positions, slots, bt, lens)

@@ -106,7 +106,7 @@ class Sequence:
                  "arrival_time", "num_computed_tokens", "status", "first_token_time", "finish_time",
                  "token_times", "block_hashes", "num_preemptions", "predicted_len", "stop_reason",
                  "output_text", "priority", "scheduled_time", "pending", "tenant", "mirostat_mu", "logprobs",
-                 "guide", "state_slot")
+                 "guide", "state_slot", "mm_embeds", "mm_positions", "cache_salt")
 
     def __init__(self, request_id: str, prompt_token_ids: List[int], params: SamplingParams,
                  lora_id: int = 0, arrival_time: Optional[float] = None, priority: int = 0):
@@ -133,6 +133,11 @@ class Sequence:
         self.tenant = ""  # quota accounting (EngineConfig.tenant_quotas)
         self.mirostat_mu: Optional[float] = None
         self.logprobs: List[dict] = []  # per output token when params.logprobs is set
+        # multimodal prompts: projected image rows [n, hidden] and the prompt positions they fill;
+        # cache_salt (the image content) keeps their KV blocks apart in the prefix cache
+        self.mm_embeds = None
+        self.mm_positions: Optional[List[int]] = None
+        self.cache_salt = 0
         self.guide = None  # constrained decoding: native GrammarMatcher of the output so far
         self.state_slot = -1  # hybrid GDN models: recurrent-state slot while the sequence holds KV
 

@@ -59,6 +59,14 @@ def _act(x: torch.Tensor, kind: str) -> torch.Tensor:
     return y.to(x.dtype)
 
 
+def _has(get, name: str) -> bool:
+    try:
+        get(name)
+        return True
+    except KeyError:
+        return False
+
+
 def _layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -> torch.Tensor:
     return ops.rms_norm(x.contiguous(), w, eps, center=True) + b
 
@@ -179,7 +187,8 @@ class CLIPVisionEncoder:
     def __init__(self, cfg: CLIPVisionConfig, get: Callable[[str], torch.Tensor], device: str = "cuda",
                  dtype: torch.dtype = torch.bfloat16):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
-        pre = "vision_model."
+        pre = "vision_tower.vision_model." if _has(get, "vision_tower.vision_model.pre_layrnorm.weight") \
+            else "vision_model."
 
         def t(n):
             return get(pre + n).to(self.device, dtype).contiguous()
@@ -197,10 +206,7 @@ class CLIPVisionEncoder:
         except KeyError:
             pass
 
-    @torch.inference_mode()
-    def encode(self, pixel_values: torch.Tensor) -> Dict[str, Optional[torch.Tensor]]:
-        """pixel_values [B, C, image_size, image_size] (already normalised) -> {"last_hidden_state"
-        [B, 1 + patches, d], "pooler_output" [B, d], "image_embeds" [B, proj] or None}."""
+    def _embed(self, pixel_values: torch.Tensor):
         cfg = self.cfg
         x = pixel_values.to(self.device, self.dtype)
         B = x.shape[0]
@@ -211,7 +217,27 @@ class CLIPVisionEncoder:
         pe = ops.linear(pm, self.patch_w).view(B, n, d)
         h = torch.cat([self.cls.view(1, 1, d).expand(B, 1, d), pe], 1) + self.pos[: n + 1][None]
         S = n + 1
-        h = _layer_norm(h.reshape(B * S, d), self.pre_w, self.pre_b, cfg.layer_norm_eps)
+        return _layer_norm(h.reshape(B * S, d), self.pre_w, self.pre_b, cfg.layer_norm_eps), B, S
+
+    @torch.inference_mode()
+    def hidden_state(self, pixel_values: torch.Tensor, layer: int = -1) -> torch.Tensor:
+        """Hidden state [B, 1 + patches, d] after ``layer`` blocks (HF ``hidden_states[layer]``: 0 is
+        the pre-LayerNorm embeddings, negative counts from the end)."""
+        cfg = self.cfg
+        n = len(self.layers)
+        k = layer if layer >= 0 else n + 1 + layer
+        h, B, S = self._embed(pixel_values)
+        h = _encoder(h, self.layers[:k], B, S, cfg.num_attention_heads, cfg.layer_norm_eps, cfg.hidden_act,
+                     causal=False)
+        return h.view(B, S, cfg.hidden_size)
+
+    @torch.inference_mode()
+    def encode(self, pixel_values: torch.Tensor) -> Dict[str, Optional[torch.Tensor]]:
+        """pixel_values [B, C, image_size, image_size] (already normalised) -> {"last_hidden_state"
+        [B, 1 + patches, d], "pooler_output" [B, d], "image_embeds" [B, proj] or None}."""
+        cfg = self.cfg
+        h, B, S = self._embed(pixel_values)
+        d = cfg.hidden_size
         h = _encoder(h, self.layers, B, S, cfg.num_attention_heads, cfg.layer_norm_eps, cfg.hidden_act, causal=False)
         last = h.view(B, S, d)
         pooled = _layer_norm(last[:, 0].contiguous(), self.post_w, self.post_b, cfg.layer_norm_eps)

@@ -65,6 +65,9 @@ class AttnMetadata:
     # split batch (tensor-parallel overlap): (rows of the first half, metadata of each half); each
     # half's collectives run while the other half computes
     halves: Optional[tuple] = None
+    # multimodal prompts: batch rows whose embedding is replaced by projected image rows
+    mm_rows: Optional[torch.Tensor] = None                # [k] int64
+    mm_embeds: Optional[torch.Tensor] = None              # [k, hidden]
 
     @property
     def num_tokens(self) -> int:
@@ -884,7 +887,7 @@ class LlamaModel:
         T = input_ids.shape[0]
         tA, mA, mB = meta.halves
         spans = [(0, tA, mA), (tA, T, mB)]
-        h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
+        h = self._embed_rows(input_ids, meta)
         residual = h
         x0 = ops.rms_norm(h, self.layers[0]["in_norm"], eps)
         xs = [x0[0:tA], x0[tA:T]]
@@ -942,6 +945,13 @@ class LlamaModel:
                 ext.set_gemm_sm_reserve(0)
         return gathered
 
+    def _embed_rows(self, input_ids: torch.Tensor, meta: AttnMetadata) -> torch.Tensor:
+        """Token embeddings, with the rows of image placeholders replaced by projected image rows."""
+        h = ops.embedding(input_ids, self.embed, scale=self.cfg.embed_scale)
+        if meta.mm_rows is not None and meta.mm_rows.numel():
+            h.index_copy_(0, meta.mm_rows, meta.mm_embeds.to(h.dtype))
+        return h
+
     def _split_stream(self):
         st = getattr(self, "_side_stream", None)
         if st is None:
@@ -958,7 +968,7 @@ class LlamaModel:
         if meta.halves is not None and self.can_split_batch():
             x = self._forward_split(input_ids, meta, kv_cache)
             return self._head(x, meta, hidden_only, greedy)
-        h = ops.embedding(input_ids, self.embed, scale=cfg.embed_scale)
+        h = self._embed_rows(input_ids, meta)
         residual = h  # the embedding output buffer becomes the residual stream (updated in place)
         n = len(self.layers)
         ctr = cfg.norm_center

@@ -343,7 +343,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
 
     # -------------------------------------------------------------- core runner
     async def run_full(prompt, sp: SamplingParams, rid: Optional[str] = None, lora_id: int = 0,
-                       priority: int = 0, timeout: Optional[float] = None):
+                       priority: int = 0, timeout: Optional[float] = None, images: Optional[list] = None):
         try:
             st.breaker.before()
         except CircuitOpen as e:
@@ -355,7 +355,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                 async def consume():
                     nonlocal last
                     async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, priority=priority,
-                                                    tenant=_TENANT.get()):
+                                                    tenant=_TENANT.get(), images=images):
                         last = out
 
                 await asyncio.wait_for(consume(), timeout=timeout or st.timeout)
@@ -385,7 +385,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
             return "\n".join(str(m.get("content", "")) for m in msgs)
         return tmpl(msgs, tools=tools) if tools else tmpl(msgs)
 
-    async def sse_stream(prompt, sp, rid, lora_id, frame, final_frame, done_marker=True, tool_frame=None):
+    async def sse_stream(prompt, sp, rid, lora_id, frame, final_frame, done_marker=True, tool_frame=None,
+                         images=None):
         """Server-sent events of the text deltas. With ``tool_frame``, text from where a tool call may
         begin is held back; at the end it is sent as one tool-call frame if it parses as calls, else
         as text."""
@@ -394,7 +395,8 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         async def gen():
             nonlocal prev
             try:
-                async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, tenant=_TENANT.get()):
+                async for out in st.ae.generate(prompt, sp, request_id=rid, lora_id=lora_id, tenant=_TENANT.get(),
+                                                images=images):
                     text = detok(out.output_token_ids)
                     if out.finished and out.text:
                         text = out.text
@@ -600,6 +602,16 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         pl = st.plugins
         info: Dict[str, Any] = {}
         messages = [m if isinstance(m, dict) else m.model_dump(exclude_none=True) for m in req.messages]
+        images = None
+        if any(isinstance(m.get("content"), list) for m in messages):  # OpenAI content parts
+            from ..models.vlm import flatten_content_parts
+            ph = getattr(st.engine, "image_placeholder", None) or "<image>"
+            try:
+                messages, images = await asyncio.to_thread(flatten_content_parts, messages, ph)
+            except Exception as e:  # bad URL / undecodable image / unknown part type
+                raise HTTPException(400, f"content parts: {e}")
+            if images and getattr(st.engine, "vision", None) is None:
+                raise HTTPException(400, "this model takes no images")
         if pl.safety is not None or pl.pii_redaction:  # request plugins: content safety, then PII redaction
             for m in messages:
                 c = m.get("content")
@@ -618,7 +630,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         prompt = chat_prompt(messages, tools)
         cid = "chatcmpl-" + uuid.uuid4().hex
         cache_key = qvec = None
-        if (pl.semantic_cache is not None and not (req.stream or force_stream) and not tools
+        if (pl.semantic_cache is not None and not (req.stream or force_stream) and not tools and not images
                 and sp.temperature == 0 and not req.logprobs):
             cache_key = json.dumps({"max_tokens": sp.max_tokens, "stop": req.stop, "rf": req.response_format,
                                     "rx": req.guided_regex, "rag": req.rag, "adapter": req.adapter_id},
@@ -655,8 +667,9 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                                "choices": [], "usage": {"prompt_tokens": len(o.prompt_token_ids),
                                                         "completion_tokens": len(o.output_token_ids),
                                                         "total_tokens": len(o.prompt_token_ids) + len(o.output_token_ids)}}
-            return await sse_stream(prompt, sp, cid, lora, frame, final, tool_frame=tool_frame if tools else None)
-        o = await run_full(prompt, sp, lora_id=lora)
+            return await sse_stream(prompt, sp, cid, lora, frame, final, tool_frame=tool_frame if tools else None,
+                                    images=images)
+        o = await run_full(prompt, sp, lora_id=lora, images=images)
         pt, ct = len(o.prompt_token_ids), len(o.output_token_ids)
         text = o.text or detok(o.output_token_ids)
         message: Dict[str, Any] = {"role": "assistant", "content": text}

@@ -87,12 +87,14 @@ class AsyncEngine:
     def _handle(self, sub) -> None:
         kind = sub[0]
         if kind == "add":
-            _, rid, prompt, params, lora_id, priority, tenant = sub
+            _, rid, prompt, params, lora_id, priority, tenant, images = sub
             try:
+                kw = {}
                 if tenant:
-                    self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority, tenant=tenant)
-                else:
-                    self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority)
+                    kw["tenant"] = tenant
+                if images:
+                    kw["images"] = images
+                self.engine.add_request(rid, prompt, params, lora_id=lora_id, priority=priority, **kw)
             except Exception as e:  # invalid request: report to that caller only
                 self._deliver(rid, e)
         elif kind == "abort":
@@ -137,7 +139,8 @@ class AsyncEngine:
     # ------------------------------------------------------------------ client API
     async def generate(self, prompt: Union[str, List[int]], params: SamplingParams,
                        request_id: Optional[str] = None, lora_id: int = 0,
-                       priority: int = 0, tenant: str = "") -> AsyncIterator[RequestOutput]:
+                       priority: int = 0, tenant: str = "", images: Optional[list] = None
+                       ) -> AsyncIterator[RequestOutput]:
         if self.error is not None:
             raise EngineDeadError(str(self.error))
         if self.draining:
@@ -149,7 +152,7 @@ class AsyncEngine:
             if rid in self._streams:
                 raise ValueError(f"duplicate request id {rid}")
             self._streams[rid] = (loop, q)
-        self._subs.put(("add", rid, prompt, params, lora_id, priority, tenant))
+        self._subs.put(("add", rid, prompt, params, lora_id, priority, tenant, images))
         finished = False
         try:
             while True:

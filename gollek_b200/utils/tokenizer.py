@@ -87,6 +87,10 @@ class HFTokenizer:
     def decode(self, ids: List[int]) -> str:
         return self.tok.decode(ids, skip_special_tokens=True)
 
+    def token_text(self, i: int) -> Optional[str]:
+        """The vocabulary string of token ``i`` (special tokens included)."""
+        return self.tok.id_to_token(i)
+
     def token_bytes(self) -> List[bytes]:
         vocab = self.tok.get_vocab(with_added_tokens=True)
         special = {t.content for t in self.tok.get_added_tokens_decoder().values() if t.special} \
@@ -315,6 +319,9 @@ class GGUFTokenizer:
         return ids
 
     # -- decoding
+    def token_text(self, i: int) -> Optional[str]:
+        return self.tokens[i] if 0 <= i < len(self.tokens) else None
+
     def token_bytes(self) -> List[bytes]:
         out = []
         for i, p in enumerate(self.tokens):
