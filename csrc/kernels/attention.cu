@@ -585,9 +585,17 @@ constexpr int kTcStages = 3;
 constexpr int kTcTileBytes = 16 * 128 * 2;            // one K (or V) tile of a paged block
 constexpr int kTcStageBytes = 2 * kTcTileBytes;       // K + V
 // fp8 KV cache (e4m3, a fp32 scale per token and head): the ring holds fp8 tiles (one 16 x 128
-// byte TMA box each, 128-byte swizzle); each warp converts a stage to f16 in its staging tiles
-// (the same swizzled layout as the bf16 tiles) and runs f16 MMAs. Scores are multiplied by the
-// key scales, probabilities by the value scales (the softmax sum uses the unscaled ones).
+// byte TMA box each, 128-byte swizzle) and every lane converts its MMA fragments straight from
+// them (cvt e4m3x2 -> f16x2, exact) for f16 MMAs, with no staging copy. Two fixed permutations
+// make each lane's fragment bytes contiguous, so a fragment group is one 16-byte shared load:
+//  * QK^T sums over dims, so any dim order shared by Q and K gives the same scores: logical
+//    k-step s = 4q + u, lane column c, offsets {0,1,8,9} + 2c read physical dims
+//    64q + 16c + 4u + {0,1,2,3} (Q is gathered in that order once, in registers);
+//  * P V: logical output column 8 jn + r (n-tile jn, lane row r) is physical dim 16 r + jn, so a
+//    lane reads bytes [16r, 16r + 16) of its four token rows and byte-permutes token pairs; the
+//    output partials are written back through the same map.
+// Scores are multiplied by the key scales, probabilities by the value scales (the softmax sum
+// uses the unscaled ones).
 constexpr int kTcFp8TileBytes = 16 * 128;
 
 GOLLEK_DEVICE uint32_t sw128_off(int row, int chunk16) {  // byte offset inside a [rows][128 dims] bf16 tile
@@ -605,15 +613,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
   static_assert(G >= 1 && G <= 16, "GQA group must fit the 16 MMA rows");
   constexpr int D = 128, BS = 16;
   constexpr int kStage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
-  constexpr int kStaging = FP8 ? kTcStageBytes : 0;  // per warp: K and V tiles converted to f16
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = dsm_raw + ((1024 - (smem_u32(dsm_raw) & 1023)) & 1023);
   const int b = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
   const int H = Hk * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = dsm + warp * kTcStages * kStage;
-  uint8_t* stg = dsm + kDecodeWarps * kTcStages * kStage + warp * kStaging;
-  constexpr int kAfter = kDecodeWarps * kTcStages * kStage + kDecodeWarps * kStaging;
+  constexpr int kAfter = kDecodeWarps * kTcStages * kStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + kAfter) + warp * kTcStages;
   float* sm_o = reinterpret_cast<float*>(dsm + kAfter + kDecodeWarps * kTcStages * 8);
   float* sm_m = sm_o + kDecodeWarps * G * D;
@@ -661,11 +667,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
   uint32_t qf[8][4];
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
-    const __nv_bfloat16* q0 = q + (int64_t)b * q_stride + (int64_t)(kh * G) * D + ks * 16 + cq;
-    qf[ks][0] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D) : 0u;
-    qf[ks][1] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D) : 0u;
-    qf[ks][2] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D + 8) : 0u;
-    qf[ks][3] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D + 8) : 0u;
+    // element offsets of the lane's two k-pairs: logical (2c, 2c + 8), or physical under the fp8 map
+    const int d0 = FP8 ? 64 * (ks >> 2) + 16 * (lane & 3) + 4 * (ks & 3) : ks * 16 + cq;
+    const int d1 = FP8 ? d0 + 2 : d0 + 8;
+    const __nv_bfloat16* q0 = q + (int64_t)b * q_stride + (int64_t)(kh * G) * D;
+    qf[ks][0] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D + d0) : 0u;
+    qf[ks][1] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D + d0) : 0u;
+    qf[ks][2] = r < G ? *reinterpret_cast<const uint32_t*>(q0 + r * D + d1) : 0u;
+    qf[ks][3] = r + 8 < G ? *reinterpret_cast<const uint32_t*>(q0 + (r + 8) * D + d1) : 0u;
     if constexpr (FP8) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) qf[ks][e] = bf16x2_to_f16x2(qf[ks][e]);
@@ -700,43 +709,38 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
           ksc[nt][e] = kp[nt * 8 + cq + e];
           vsc[nt][e] = vp[nt * 8 + cq + e];
         }
-      // fp8 tiles (128-byte swizzled rows) -> f16 staging tiles: lane = (token row, half a row)
-      const uint8_t* src = ring + st * kStage;
-      const int row = lane >> 1, c0 = (lane & 1) * 4;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint8_t* tile = src + which * kTcFp8TileBytes;
-        uint8_t* dt = stg + which * kTcTileBytes;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = c0 + i;  // 16 fp8 dims [16c, 16c + 16)
-          const uint4 w = *reinterpret_cast<const uint4*>(tile + row * 128 + ((c ^ (row & 7)) << 4));
-          uint4 lo, hi;
-          e4m3x4_to_f16x4(w.x, lo.x, lo.y);
-          e4m3x4_to_f16x4(w.y, lo.z, lo.w);
-          e4m3x4_to_f16x4(w.z, hi.x, hi.y);
-          e4m3x4_to_f16x4(w.w, hi.z, hi.w);
-          *reinterpret_cast<uint4*>(dt + sw128_off(row, 2 * c)) = lo;
-          *reinterpret_cast<uint4*>(dt + sw128_off(row, 2 * c + 1)) = hi;
-        }
-      }
-      __syncwarp();
-      kt = smem_u32(stg);
-      vt = kt + kTcTileBytes;
     }
     // S = Q K^T : 16 x 16 (two n-tiles of 8 tokens)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if constexpr (FP8) {
+      // lane (r, c) of n-tile nt reads token row 8 nt + r, 16-byte chunks c and 4 + c (the two dim
+      // halves); odd rows load the halves in the other order, so a quarter-warp reads 8 distinct
+      // 16-byte bank groups
+      const uint8_t* ktile = ring + st * kStage;
+      const int c = lane & 3, par = r & 1;
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t bfr[4];
-      const int tok = (mi >> 1) * 8 + rr, ch = 2 * ks + (mi & 1);
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
-                   : "r"(kt + sw128_off(tok, ch)));
-      if constexpr (FP8) {
-        mma_f16_16816(sc[0], qf[ks], bfr);
-        mma_f16_16816(sc[1], qf[ks], bfr + 2);
-      } else {
+      for (int nt = 0; nt < 2; ++nt) {
+        const int row = nt * 8 + r;
+        const uint8_t* rowp = ktile + row * 128;
+        const uint4 wa = *reinterpret_cast<const uint4*>(rowp + (((4 * par + c) ^ (row & 7)) << 4));
+        const uint4 wb = *reinterpret_cast<const uint4*>(rowp + (((4 * (par ^ 1) + c) ^ (row & 7)) << 4));
+        const uint4 h0 = par ? wb : wa, h1 = par ? wa : wb;
+        const uint32_t wd[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t bfr[2];
+          e4m3x4_to_f16x4(wd[ks], bfr[0], bfr[1]);
+          mma_f16_16816(sc[nt], qf[ks], bfr);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t bfr[4];
+        const int tok = (mi >> 1) * 8 + rr, ch = 2 * ks + (mi & 1);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
+                     : "r"(kt + sw128_off(tok, ch)));
         mma_bf16_16816(sc[0], qf[ks], bfr);
         mma_bf16_16816(sc[1], qf[ks], bfr + 2);
       }
@@ -808,17 +812,42 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       }
     }
     // O += P V : 16 x 128 (16 n-tiles of 8 dims), one k-step of 16 tokens
+    if constexpr (FP8) {
+      // lane (r, c): bytes [16r, 16r + 16) (physical dims 16r + jn) of token rows 2c, 2c+1, 2c+8,
+      // 2c+9; byte j of a row pair -> the (k, k+1) f16x2 of n-tile jn = j
+      const uint8_t* vtile = ring + st * kStage + kTcFp8TileBytes;
+      const int c = lane & 3;
+      auto ld = [&](int row) {
+        return *reinterpret_cast<const uint4*>(vtile + row * 128 + ((r ^ (row & 7)) << 4));
+      };
+      const uint4 va = ld(2 * c), vb = ld(2 * c + 1), vc = ld(2 * c + 8), vd = ld(2 * c + 9);
+      const uint32_t A[4] = {va.x, va.y, va.z, va.w}, Bv[4] = {vb.x, vb.y, vb.z, vb.w};
+      const uint32_t C[4] = {vc.x, vc.y, vc.z, vc.w}, Dv[4] = {vd.x, vd.y, vd.z, vd.w};
 #pragma unroll
-    for (int jd = 0; jd < 8; ++jd) {
-      uint32_t bfr[4];
-      const int tok = (mi & 1) * 8 + rr, ch = 2 * jd + (mi >> 1);
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
-                   : "r"(vt + sw128_off(tok, ch)));
-      if constexpr (FP8) {
-        mma_f16_16816(o[2 * jd], pf, bfr);
-        mma_f16_16816(o[2 * jd + 1], pf, bfr + 2);
-      } else {
+      for (int w = 0; w < 4; ++w) {
+        uint32_t lo_ab, hi_ab, lo_cd, hi_cd;  // interleaved token pairs: [x0 y0 x1 y1], [x2 y2 x3 y3]
+        asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(lo_ab) : "r"(A[w]), "r"(Bv[w]));
+        asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(hi_ab) : "r"(A[w]), "r"(Bv[w]));
+        asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(lo_cd) : "r"(C[w]), "r"(Dv[w]));
+        asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(hi_cd) : "r"(C[w]), "r"(Dv[w]));
+        uint32_t b01[2], b23[2], c01[2], c23[2];
+        e4m3x4_to_f16x4(lo_ab, b01[0], b23[0]);  // n-tiles 4w, 4w+1: tokens (2c, 2c+1)
+        e4m3x4_to_f16x4(lo_cd, b01[1], b23[1]);  //                   tokens (2c+8, 2c+9)
+        e4m3x4_to_f16x4(hi_ab, c01[0], c23[0]);  // n-tiles 4w+2, 4w+3
+        e4m3x4_to_f16x4(hi_cd, c01[1], c23[1]);
+        mma_f16_16816(o[4 * w + 0], pf, b01);
+        mma_f16_16816(o[4 * w + 1], pf, b23);
+        mma_f16_16816(o[4 * w + 2], pf, c01);
+        mma_f16_16816(o[4 * w + 3], pf, c23);
+      }
+    } else {
+#pragma unroll
+      for (int jd = 0; jd < 8; ++jd) {
+        uint32_t bfr[4];
+        const int tok = (mi & 1) * 8 + rr, ch = 2 * jd + (mi >> 1);
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(bfr[0]), "=r"(bfr[1]), "=r"(bfr[2]), "=r"(bfr[3])
+                     : "r"(vt + sw128_off(tok, ch)));
         mma_bf16_16816(o[2 * jd], pf, bfr);
         mma_bf16_16816(o[2 * jd + 1], pf, bfr + 2);
       }
@@ -845,8 +874,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     if (g < G) {
 #pragma unroll
       for (int jn = 0; jn < 16; ++jn) {
-        sm_o[(warp * G + g) * D + jn * 8 + cq] = o[jn][2 * h];
-        sm_o[(warp * G + g) * D + jn * 8 + cq + 1] = o[jn][2 * h + 1];
+        // logical column 8 jn + cq (+1); the fp8 path's physical dim is 16 (cq (+1)) + jn
+        const int d0 = FP8 ? 16 * cq + jn : jn * 8 + cq, d1 = FP8 ? d0 + 16 : d0 + 1;
+        sm_o[(warp * G + g) * D + d0] = o[jn][2 * h];
+        sm_o[(warp * G + g) * D + d1] = o[jn][2 * h + 1];
       }
       if ((lane & 3) == 0) {
         sm_m[warp * G + g] = mrow[h];
@@ -885,8 +916,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
 template <int G, bool FP8>
 constexpr size_t decode_tc_smem_bytes() {
   constexpr size_t stage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
-  constexpr size_t staging = FP8 ? kTcStageBytes : 0;
-  return 1024 + (size_t)kDecodeWarps * kTcStages * stage + kDecodeWarps * staging + kDecodeWarps * kTcStages * 8 +
+  return 1024 + (size_t)kDecodeWarps * kTcStages * stage + kDecodeWarps * kTcStages * 8 +
          (size_t)kDecodeWarps * G * 128 * 4 + 2 * kDecodeWarps * G * 4;
 }
 

@@ -38,10 +38,13 @@ __global__ void __launch_bounds__(256) kv_quant_fp8_kernel(const __nv_bfloat16* 
   const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
   const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
   const float amax = warp_max(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
-  const float scale = amax > 0.f ? amax / kE4m3Max : 1.f;
-  const float inv = 1.f / scale;
-  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a.x * inv, a.y * inv), __NV_SATFINITE, __NV_E4M3);
-  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(b.x * inv, b.y * inv), __NV_SATFINITE, __NV_E4M3);
+  const float scale = amax > 0.f ? __fdiv_rn(amax, kE4m3Max) : 1.f;
+  // x / scale correctly rounded (not x * (1 / scale)): the stored byte is a function of x and
+  // scale alone, equal to any IEEE restatement of the rule
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+      make_float2(__fdiv_rn(a.x, scale), __fdiv_rn(a.y, scale)), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+      make_float2(__fdiv_rn(b.x, scale), __fdiv_rn(b.y, scale)), __NV_SATFINITE, __NV_E4M3);
   const int64_t row = ((blk * 2 + which) * Hk + kh) * block_size + off;
   reinterpret_cast<uint32_t*>(cache + row * D)[lane] = (uint32_t)lo | ((uint32_t)hi << 16);
   if (lane == 0) scales[row] = scale;

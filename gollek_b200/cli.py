@@ -191,6 +191,21 @@ def cmd_list(args):
             print("  " + n)
 
 
+def cmd_transcribe(args):
+    """Speech to text with a Whisper checkpoint: prints the text (or JSON with segments)."""
+    import torch
+    from .models.whisper import WhisperASR
+    dev = args.device or ("cuda" if torch.cuda.is_available() else "cpu")
+    asr = WhisperASR(args.model, device=dev, dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
+    datas = [open(f, "rb").read() for f in args.files]
+    res = asr.transcribe(datas, language=args.language, task=args.task, timestamps=args.timestamps)
+    for f, r in zip(args.files, res):
+        if args.json:
+            print(json.dumps({"file": f, **r}))
+        else:
+            print(r["text"])
+
+
 def cmd_bench(args):
     import subprocess
     here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -258,6 +273,15 @@ def build_parser():
     pl.add_argument("--endpoint", default=None)
     pl.add_argument("--verify", action="store_true", help="re-check an existing pull against its manifest")
     pl.set_defaults(fn=cmd_pull)
+    tr = sub.add_parser("transcribe", help="speech to text (Whisper checkpoint, RIFF/WAVE input)")
+    tr.add_argument("files", nargs="+")
+    tr.add_argument("--model", "-m", required=True)
+    tr.add_argument("--language", default=None, help="default: detected")
+    tr.add_argument("--task", choices=["transcribe", "translate"], default="transcribe")
+    tr.add_argument("--timestamps", action="store_true")
+    tr.add_argument("--json", action="store_true")
+    tr.add_argument("--device", default=None)
+    tr.set_defaults(fn=cmd_transcribe)
     be = sub.add_parser("bench")
     be.add_argument("rest", nargs=argparse.REMAINDER)
     be.set_defaults(fn=cmd_bench)

@@ -149,7 +149,10 @@ class DriverEngine:
     def __getattr__(self, name):  # metrics, cfg, tokenizer, ... come from the local engine
         return getattr(self.engine, name)
 
-    def add_request(self, request_id, prompt, params=None, lora_id: int = 0, arrival_time=None, priority: int = 0):
+    def add_request(self, request_id, prompt, params=None, lora_id: int = 0, arrival_time=None, priority: int = 0,
+                    images=None):
+        if images:
+            raise ValueError("image inputs are served on a single GPU (tensor-parallel serving takes text only)")
         import dataclasses
         import time as _t
         from ..engine.sequence import SamplingParams

@@ -28,6 +28,7 @@ def main(argv=None):
     ap.add_argument("--speculative-method", choices=["none", "ngram", "draft"], default=None)
     ap.add_argument("--draft-model", default=None)
     ap.add_argument("--enable-expert-parallel", action="store_true")
+    ap.add_argument("--asr-model", default=None, help="Whisper checkpoint directory for /v1/audio/*")
     args = ap.parse_args(argv)
     import uvicorn
     from ..config import EngineConfig
@@ -56,11 +57,21 @@ def main(argv=None):
         return _serve_tp(args, cfg, keys)
     ae = AsyncEngine(LLMEngine(cfg)).start()
     app = create_app(ae, model_name=args.served_model_name or os.path.basename(args.model.rstrip("/")),
-                     api_keys=keys, rate=args.rate_limit)
+                     api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg))
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:
         ae.shutdown(drain=True)
+
+
+def _asr(args, cfg):
+    """The speech model behind /v1/audio/* (on rank 0's device), or None."""
+    if not args.asr_model:
+        return None
+    import torch
+    from ..models.whisper import WhisperASR
+    dev = str(cfg.device)
+    return WhisperASR(args.asr_model, device=dev, dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
 
 
 def _serve_tp(args, cfg, keys):
@@ -92,7 +103,7 @@ def _serve_tp(args, cfg, keys):
         drv = DriverEngine(engine, cp)
         ae = AsyncEngine(drv).start()
         app = create_app(ae, model_name=args.served_model_name or os.path.basename(str(args.model).rstrip("/")),
-                         api_keys=keys, rate=args.rate_limit)
+                         api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg))
         try:
             uvicorn.run(app, host=args.host, port=args.port, log_level="info")
         finally:

@@ -148,3 +148,31 @@ def test_chat_completions_with_image_url(tmp_path):
             assert r.status_code == 400
     finally:
         ae.shutdown()
+
+
+@pytest.mark.gpu
+def test_llava_engine_gpu(tmp_path):
+    """bf16 engine on the GPU: image features close to transformers' fp32 ones; the first greedy
+    token is (within bf16 rounding of) transformers' argmax."""
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine
+    from gollek_b200.engine.sequence import SamplingParams
+    m, d = _tiny_llava(tmp_path)
+    pixel = torch.randn(3, 56, 56, generator=torch.Generator().manual_seed(1))
+    ec = EngineConfig(model=d, device="cuda", dtype="bfloat16", max_num_seqs=2, max_num_batched_tokens=64,
+                      max_model_len=256)
+    eng = LLMEngine(ec, num_blocks=32)
+    feats = eng.vision.encode(pixel[None].cuda()).float().cpu()
+    with torch.no_grad():
+        ref_feats = m.model.get_image_features(pixel_values=pixel[None], vision_feature_layer=-2,
+                                               vision_feature_select_strategy="default")
+    if hasattr(ref_feats, "pooler_output"):  # transformers 5: projected rows per image in pooler_output
+        ref_feats = ref_feats.pooler_output
+    ref_feats = torch.cat(list(ref_feats)) if isinstance(ref_feats, (list, tuple)) else ref_feats
+    assert float((feats.reshape(-1) - ref_feats.reshape(-1)).norm() / ref_feats.norm()) < 3e-2
+    out = eng.generate([[5, 17, 319, 42, 99, 7]], SamplingParams(temperature=0.0, max_tokens=2, ignore_eos=True),
+                       images=[[pixel]])[0].output_token_ids
+    ids = torch.tensor([[5, 17] + [319] * 16 + [42, 99, 7]])
+    with torch.no_grad():
+        lg = m(input_ids=ids, pixel_values=pixel[None]).logits[0, -1]
+    assert float(lg[out[0]]) >= float(lg.max()) - 0.02 * float(lg.max() - lg.min())
