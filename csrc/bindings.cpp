@@ -100,7 +100,7 @@ void rope_kv_write_out(torch::Tensor q_out, torch::Tensor qkv, torch::Tensor pos
   }
   launch_rope_kv_write(q_out.data_ptr(), qkv.data_ptr(), positions.data_ptr<int>(), cos_sin.data_ptr<float>(), cp,
                        sp, T, H, Hk, D, bs, qkv.stride(0), (int)cos_sin.size(0), bp, qn, kn, (float)norm_eps,
-                       (int)cos_sin.size(1), cur_stream());
+                       (int)cos_sin.size(1), cur_stream(), cp ? (int)cache->size(0) : 0);
 }
 
 void embedding_out(torch::Tensor out, torch::Tensor ids, torch::Tensor table, double scale) {
@@ -156,10 +156,10 @@ void paged_decode_attention_out(torch::Tensor out, torch::Tensor q, torch::Tenso
     pml = po + (int64_t)B * H * num_splits * D;
   }
   launch_paged_decode(out.data_ptr(), q.data_ptr(), q.stride(0), cache.data_ptr(),
-                      tensor_cores ? (int)cache.size(0) : 0, block_tables.data_ptr<int>(),
+                      (int)cache.size(0), block_tables.data_ptr<int>(),
                       block_tables.stride(0), seq_lens.data_ptr<int>(), B, H, cache.size(2), D, cache.size(3),
                       (int)num_splits, (float)scale, po, pml, (int)window, (float)softcap, cur_stream(),
-                      scl);
+                      scl, tensor_cores);
 }
 
 void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
@@ -196,7 +196,8 @@ void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tens
   launch_paged_prefill(out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), cache.data_ptr(),
                        block_tables.data_ptr<int>(), block_tables.stride(0), seq_lens.data_ptr<int>(),
                        query_start.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), q.size(1), cache.size(2),
-                       q.size(2), cache.size(3), (float)scale, (int)window, (float)softcap, cur_stream());
+                       q.size(2), cache.size(3), (float)scale, (int)window, (float)softcap, cur_stream(),
+                       (int)cache.size(0));
 }
 
 void gemm_bf16_out(torch::Tensor out, torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> residual,
@@ -658,7 +659,7 @@ void kv_quant_fp8_py(torch::Tensor kv, torch::Tensor slots, torch::Tensor cache,
   TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.numel() == cache.numel() / cache.size(4), "scales fp32");
   TORCH_CHECK(slots.numel() >= kv.size(0), "one slot per token");
   launch_kv_quant_fp8(kv.data_ptr(), slots.data_ptr<int>(), cache.data_ptr(), scales.data_ptr<float>(), kv.size(0),
-                      kv.size(2), kv.size(3), cache.size(3), cur_stream());
+                      kv.size(2), kv.size(3), cache.size(3), cur_stream(), (int)cache.size(0));
 }
 
 void kv_dequant_blocks_py(torch::Tensor cache, torch::Tensor scales, torch::Tensor ids, torch::Tensor dst) {
@@ -831,6 +832,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_quant_fp8", &kv_quant_fp8_py, "step K/V rows -> fp8 e4m3 cache slots + per-token scales");
   m.def("kv_dequant_blocks", &kv_dequant_blocks_py, "fp8 cache blocks -> bf16 blocks (prefill over an fp8 cache)");
   m.def("gemm_grouped", &gemm_grouped_py, "grouped tcgen05 GEMM (none / SwiGLU / scatter epilogue)");
+  m.def(
+      "set_bounds_status",
+      [](c10::optional<torch::Tensor> st) {
+        if (!st.has_value()) {
+          bounds_status_slot() = nullptr;
+          return;
+        }
+        TORCH_CHECK(st->is_cuda() && st->scalar_type() == at::kInt && st->numel() >= 2 && st->is_contiguous(),
+                    "bounds status: int32 [2] on the GPU");
+        bounds_status_slot() = reinterpret_cast<uint32_t*>(st->data_ptr<int>());
+      },
+      "bind (or, with None, unbind) the device status word of the kernels' bounds checks");
   m.def("set_gemm_sm_reserve", [](int64_t n) { gemm_sm_reserve() = (int)n; },
         "SMs the persistent GEMM grids leave free (for a collective running beside them)");
   m.def("tp_argmax", &tp_argmax_py, "distributed greedy argmax of vocab-parallel logits over P2P (C5)");

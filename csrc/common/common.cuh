@@ -39,6 +39,26 @@ GOLLEK_DEVICE void report_status(uint32_t* status, uint32_t code) {
   if (status) atomicOr(status, code);
 }
 
+// Bounds checks of indices that kernels read from device memory (block-table entries, KV slots,
+// token ids, gathered row indices). They are compiled in unless -DGOLLEK_BOUNDS_CHECK=0 and are
+// active while the host has bound a status buffer (`bounds` != nullptr; a null pointer costs one
+// uniform branch). An index outside [0, n) ORs kStatusBounds into bounds[0], records the first bad
+// index in bounds[1] (sentinel 0xffffffff) and returns `safe` instead: a read then uses a valid
+// index (a wrong result, never a fault), a write is skipped by its caller. Nothing traps.
+#ifndef GOLLEK_BOUNDS_CHECK
+#define GOLLEK_BOUNDS_CHECK 1
+#endif
+GOLLEK_DEVICE int checked_index(int i, int n, uint32_t* bounds, int safe = 0) {
+#if GOLLEK_BOUNDS_CHECK
+  if (bounds != nullptr && (i < 0 || i >= n)) {
+    atomicOr(bounds, kStatusBounds);
+    atomicCAS(bounds + 1, 0xffffffffu, (uint32_t)i);
+    return safe;
+  }
+#endif
+  return i;
+}
+
 // ----------------------------------------------------------------------------
 // Small numeric helpers
 // ----------------------------------------------------------------------------

@@ -11,6 +11,14 @@
 
 namespace gollek {
 
+// Status buffer of the device bounds checks (uint32 [2]: status bits, first bad index), or nullptr
+// when checking is off. One slot per process (an inline function's static), set from Python.
+inline uint32_t*& bounds_status_slot() {
+  static uint32_t* p = nullptr;
+  return p;
+}
+inline uint32_t* bounds_status() { return bounds_status_slot(); }
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

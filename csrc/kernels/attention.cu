@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q,        // [B, H, D] rows at q_stride
     const __nv_bfloat16* __restrict__ cache,    // [NB, 2, Hk, BS, D]
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens, int Hk,
-    int num_splits, float scale_log2, int64_t q_stride, uint32_t* status, int window, float softcap_log2) {
+    int num_splits, float scale_log2, int64_t q_stride, uint32_t* status, int window, float softcap_log2,
+    int num_blocks) {
   using C = DecodeCfg<D, G, BS>;
   constexpr int TILE = BS * D;                         // elements of one K (or V) tile
   constexpr uint32_t TILE_BYTES = TILE * 2;
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_kernel(
   __syncwarp();
   auto issue = [&](int j) {  // lane 0 only
     const int st = j % kDecodeStages;
-    const int64_t pb = bt[blk_begin + warp + kDecodeWarps * j];
+    const int64_t pb = checked_index(bt[blk_begin + warp + kDecodeWarps * j], num_blocks, status);
     const __nv_bfloat16* kb = cache + ((pb * 2 + 0) * Hk + kh) * (int64_t)TILE;
     const __nv_bfloat16* vb = cache + ((pb * 2 + 1) * Hk + kh) * (int64_t)TILE;
     mbar_arrive_expect_tx(&bars[st], 2 * TILE_BYTES);
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
     const __nv_bfloat16* __restrict__ cache,                  // [NB, 2, Hk, BS, D]
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens,
     const int* __restrict__ query_start, const int* __restrict__ tiles,  // tiles[i] = (b, q_off)
-    int H, int Hk, int BS, float scale_log2, int window, float softcap_log2) {
+    int H, int Hk, int BS, float scale_log2, int window, float softcap_log2, int num_blocks, uint32_t* bounds) {
   static_assert(D % 16 == 0 && D >= 32 && D <= 256, "head_dim");
   // head_dim 256: the O accumulator alone takes 128 registers per thread, so Q fragments are
   // re-read from shared memory for every key tile instead of being held in registers
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_kernel(
       const int r = i / (D / 8), ch = i % (D / 8);
       const int kpos = tile * kPfBN + r;
       const bool v = kpos < kv_end;
-      const int64_t pb = v ? bt[kpos / BS] : 0;
+      const int64_t pb = v ? checked_index(bt[kpos / BS], num_blocks, bounds) : 0;
       const int off = kpos % BS;
       const __nv_bfloat16* ks = cache + ((pb * 2 + 0) * Hk + kh) * head_stride + off * D + ch * 8;
       const __nv_bfloat16* vs = cache + ((pb * 2 + 1) * Hk + kh) * head_stride + off * D + ch * 8;
@@ -604,12 +605,12 @@ GOLLEK_DEVICE uint32_t sw128_off(int row, int chunk16) {  // byte offset inside 
 }
 
 template <int G, bool FP8>
-__global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
+__global__ void __launch_bounds__(kDecodeWarps * 32, FP8 ? 4 : 1) paged_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmap,      // cache rows [NB*2*Hk*16, 128] bf16 (fp8: 128 bytes)
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
     const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ seq_lens, int Hk, int num_splits, float scale_log2, int64_t q_stride,
-    uint32_t* status, int window, float softcap_log2, const float* __restrict__ kv_scales) {
+    uint32_t* status, int window, float softcap_log2, const float* __restrict__ kv_scales, int num_blocks) {
   static_assert(G >= 1 && G <= 16, "GQA group must fit the 16 MMA rows");
   constexpr int D = 128, BS = 16;
   constexpr int kStage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
@@ -619,10 +620,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
   const int H = Hk * G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* ring = dsm + warp * kTcStages * kStage;
-  constexpr int kAfter = kDecodeWarps * kTcStages * kStage;
+  // fp8: the stage's 16 key and 16 value scales arrive by bulk copy on the tiles' barrier
+  constexpr int kScaleBytes = FP8 ? 2 * BS * 4 : 0;
+  float* sring = reinterpret_cast<float*>(dsm + kDecodeWarps * kTcStages * kStage) + warp * kTcStages * (kScaleBytes / 4);
+  constexpr int kAfter = kDecodeWarps * kTcStages * (kStage + kScaleBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + kAfter) + warp * kTcStages;
-  float* sm_o = reinterpret_cast<float*>(dsm + kAfter + kDecodeWarps * kTcStages * 8);
-  float* sm_m = sm_o + kDecodeWarps * G * D;
+  // a warp's output partials [G, D] fp32 go into its own ring once its loads are consumed
+  static_assert(G * D * 4 <= kTcStages * kStage, "partials must fit a warp's ring");
+  auto sm_o = [&](int w) { return reinterpret_cast<float*>(dsm + w * kTcStages * kStage); };
+  float* sm_m = reinterpret_cast<float*>(dsm + kAfter + kDecodeWarps * kTcStages * 8);
   float* sm_l = sm_m + kDecodeWarps * G;
 
   const int L = seq_lens[b];
@@ -644,13 +650,16 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
   __syncwarp();
   auto issue = [&](int j) {  // lane 0 only
     const int st = j % kTcStages;
-    const int pb = bt[blk_begin + warp + kDecodeWarps * j];
+    const int pb = checked_index(bt[blk_begin + warp + kDecodeWarps * j], num_blocks, status);
     const int rk = ((pb * 2 + 0) * Hk + kh) * BS, rv = ((pb * 2 + 1) * Hk + kh) * BS;
     uint8_t* dst = ring + st * kStage;
-    mbar_arrive_expect_tx(&bars[st], kStage);
+    mbar_arrive_expect_tx(&bars[st], kStage + kScaleBytes);
     if constexpr (FP8) {
       tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
       tma_load_2d(dst + kTcFp8TileBytes, &tmap, 0, rv, &bars[st]);
+      float* sd = sring + st * (kScaleBytes / 4);
+      bulk_g2s(sd, kv_scales + rk, BS * 4, &bars[st]);           // rows rk .. rk + 15: this block's key scales
+      bulk_g2s(sd + BS, kv_scales + rv, BS * 4, &bars[st]);      // and value scales
     } else {
       tma_load_2d(dst, &tmap, 0, rk, &bars[st]);
       tma_load_2d(dst + 2048, &tmap, 64, rk, &bars[st]);
@@ -699,9 +708,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
     uint32_t vt = kt + kTcTileBytes;
     float ksc[2][2], vsc[2][2];  // fp8: key / value scales of this lane's 4 token columns
     if constexpr (FP8) {
-      const int pb = bt[blk_begin + warp + kDecodeWarps * j];
-      const float* kp = kv_scales + ((int64_t)(pb * 2 + 0) * Hk + kh) * BS;
-      const float* vp = kv_scales + ((int64_t)(pb * 2 + 1) * Hk + kh) * BS;
+      const float* kp = sring + st * (kScaleBytes / 4);
+      const float* vp = kp + BS;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -726,12 +734,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
         const uint4 wb = *reinterpret_cast<const uint4*>(rowp + (((4 * (par ^ 1) + c) ^ (row & 7)) << 4));
         const uint4 h0 = par ? wb : wa, h1 = par ? wa : wb;
         const uint32_t wd[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        float sc_odd[4] = {0.f, 0.f, 0.f, 0.f};  // two accumulation chains of 4 MMAs, not one of 8
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           uint32_t bfr[2];
           e4m3x4_to_f16x4(wd[ks], bfr[0], bfr[1]);
-          mma_f16_16816(sc[nt], qf[ks], bfr);
+          mma_f16_16816((ks & 1) ? sc_odd : sc[nt], qf[ks], bfr);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] += sc_odd[e];
       }
     } else {
 #pragma unroll
@@ -876,8 +887,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       for (int jn = 0; jn < 16; ++jn) {
         // logical column 8 jn + cq (+1); the fp8 path's physical dim is 16 (cq (+1)) + jn
         const int d0 = FP8 ? 16 * cq + jn : jn * 8 + cq, d1 = FP8 ? d0 + 16 : d0 + 1;
-        sm_o[(warp * G + g) * D + d0] = o[jn][2 * h];
-        sm_o[(warp * G + g) * D + d1] = o[jn][2 * h + 1];
+        sm_o(warp)[g * D + d0] = o[jn][2 * h];
+        sm_o(warp)[g * D + d1] = o[jn][2 * h + 1];
       }
       if ((lane & 3) == 0) {
         sm_m[warp * G + g] = mrow[h];
@@ -897,7 +908,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
       const float mw = sm_m[w * G + g];
       const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       Lsum += sm_l[w * G + g] * f;
-      O += sm_o[(w * G + g) * D + d] * f;
+      O += sm_o(w)[g * D + d] * f;
     }
     const int hq = kh * G + g;
     if (num_splits == 1) {
@@ -915,9 +926,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32) paged_decode_tc_kernel(
 
 template <int G, bool FP8>
 constexpr size_t decode_tc_smem_bytes() {
-  constexpr size_t stage = FP8 ? 2 * kTcFp8TileBytes : kTcStageBytes;
-  return 1024 + (size_t)kDecodeWarps * kTcStages * stage + kDecodeWarps * kTcStages * 8 +
-         (size_t)kDecodeWarps * G * 128 * 4 + 2 * kDecodeWarps * G * 4;
+  constexpr size_t stage = FP8 ? 2 * kTcFp8TileBytes + 2 * 16 * 4 : kTcStageBytes;  // fp8: + the scales
+  return 1024 + (size_t)kDecodeWarps * kTcStages * stage + kDecodeWarps * kTcStages * 8 + 2 * kDecodeWarps * G * 4;
 }
 
 template <int G, bool FP8>
@@ -935,8 +945,8 @@ void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* ca
   dim3 grid(B, Hk, num_splits);
   kern<<<grid, kDecodeWarps * 32, smem, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), po, pml,
                                               reinterpret_cast<const __nv_bfloat16*>(q), bt, bt_stride, lens, Hk,
-                                              num_splits, scale_log2, q_stride, nullptr, window, softcap_log2,
-                                              kv_scales);
+                                              num_splits, scale_log2, q_stride, bounds_status(), window,
+                                              softcap_log2, kv_scales, num_blocks);
   check_launch("paged_decode_attention (tensor cores)");
   if (num_splits > 1) {
     decode_combine_kernel<128><<<B * Hk * G, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml,
@@ -948,7 +958,7 @@ void launch_decode_tc(void* out, const void* q, int64_t q_stride, const void* ca
 template <int D, int G>
 void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cache, const int* bt, int bt_stride,
                      const int* lens, int B, int Hk, int num_splits, float scale_log2, float* po, float* pml,
-                     int window, float softcap_log2, cudaStream_t s) {
+                     int window, float softcap_log2, int num_blocks, cudaStream_t s) {
   dim3 grid(B, Hk, num_splits);
   constexpr size_t smem = decode_smem_bytes<D, G, 16>();
   auto kern = paged_decode_kernel<D, G, 16>;
@@ -956,7 +966,7 @@ void launch_decode_t(void* out, const void* q, int64_t q_stride, const void* cac
   kern<<<grid, kDecodeWarps * 32, smem, s>>>(
       reinterpret_cast<__nv_bfloat16*>(out), po, pml, reinterpret_cast<const __nv_bfloat16*>(q),
       reinterpret_cast<const __nv_bfloat16*>(cache), bt, bt_stride, lens, Hk, num_splits, scale_log2, q_stride,
-      nullptr, window, softcap_log2);
+      num_blocks > 0 ? bounds_status() : nullptr, window, softcap_log2, num_blocks);
   check_launch("paged_decode_attention");
   if (num_splits > 1) {
     decode_combine_kernel<D><<<B * Hk * G, D, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), po, pml, num_splits);
@@ -971,7 +981,7 @@ namespace gollek {
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         int window, float softcap, cudaStream_t s, const float* kv_scales) {
+                         int window, float softcap, cudaStream_t s, const float* kv_scales, bool tensor_cores) {
   throw_if(block_size != 16, "decode attention is built for block_size 16");
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(num_splits > 1 && (part_o == nullptr || part_ml == nullptr), "split-KV decode needs a workspace");
@@ -992,7 +1002,7 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
 #undef GOLLEK_DECODE_TC8
     throw_if(true, "fp8 KV cache: unsupported GQA group " + std::to_string(G));
   }
-  if (D == 128 && num_blocks > 0) {
+  if (D == 128 && num_blocks > 0 && tensor_cores) {
 #define GOLLEK_DECODE_TC(GG) \
   if (G == GG) return launch_decode_tc<GG, false>(out, q, q_stride, cache, num_blocks, block_tables, bt_stride, seq_lens, \
                                                   B, Hk, num_splits, sl, part_o, part_ml, window, cl, nullptr, s);
@@ -1006,7 +1016,7 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
 #define GOLLEK_DECODE_CASE(DD, GG)                                                                            \
   if (D == DD && G == GG)                                                                                     \
     return launch_decode_t<DD, GG>(out, q, q_stride, cache, block_tables, bt_stride, seq_lens, B, Hk, num_splits, \
-                                   sl, part_o, part_ml, window, cl, s);
+                                   sl, part_o, part_ml, window, cl, num_blocks, s);
   GOLLEK_DECODE_CASE(128, 1)
   GOLLEK_DECODE_CASE(128, 2)
   GOLLEK_DECODE_CASE(128, 4)
@@ -1030,7 +1040,7 @@ void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void*
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
-                          int window, float softcap, cudaStream_t s) {
+                          int window, float softcap, cudaStream_t s, int num_blocks) {
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   if (ntiles == 0) return;
   const float sl = scale * kLog2e;
@@ -1045,7 +1055,8 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
                                         reinterpret_cast<const __nv_bfloat16*>(q), q_stride,                \
                                         reinterpret_cast<const __nv_bfloat16*>(cache), block_tables,        \
                                         bt_stride, seq_lens, query_start, tiles, H, Hk, block_size, sl,     \
-                                        window, cl);                                                        \
+                                        window, cl, num_blocks,                                             \
+                                        num_blocks > 0 ? bounds_status() : nullptr);                        \
     check_launch("paged_prefill_attention");                                                                \
     return;                                                                                                 \
   }

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
                       const int* __restrict__ tiles, int H, int Hk, float scale_log2, uint32_t* status, int window,
-                      float softcap_log2) {
+                      float softcap_log2, int num_blocks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* dv = dk + kKVTile;
         for (int blk = 0; blk < kTK / kBS; ++blk) {
           const int kb = ((j0 + j) * kTK) / kBS + blk;
-          const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
+          const int pb = checked_index((kb * kBS < kv_end) ? bt[kb] : bt[0], num_blocks, status);
           const int rk = ((pb * 2 + 0) * Hk + kh) * kBS, rv = ((pb * 2 + 1) * Hk + kh) * kBS;
           tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &kv_full[st]);
           tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &kv_full[st]);
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
                       const int4* __restrict__ work, int pair_heads, int H, int Hk, float scale_log2,
-                      uint32_t* status, int window, float softcap_log2) {
+                      uint32_t* status, int window, float softcap_log2, int num_blocks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;                          // slot i at + i * kQBytes
@@ -504,7 +504,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         mbar_arrive_expect_tx(&k_full[st], kKVTile);
         for (int blk = 0; blk < kTK / kBS; ++blk) {
           const int kb = (j * kTK) / kBS + blk;
-          const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
+          const int pb = checked_index((kb * kBS < kv_end) ? bt[kb] : bt[0], num_blocks, status);
           const int rk = ((pb * 2 + 0) * Hk + kh) * kBS;
           tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &k_full[st]);
           tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &k_full[st]);
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         mbar_arrive_expect_tx(&v_full[st], kKVTile);
         for (int blk = 0; blk < kTK / kBS; ++blk) {
           const int kb = (j * kTK) / kBS + blk;
-          const int pb = (kb * kBS < kv_end) ? bt[kb] : bt[0];
+          const int pb = checked_index((kb * kBS < kv_end) ? bt[kb] : bt[0], num_blocks, status);
           const int rv = ((pb * 2 + 1) * Hk + kh) * kBS;
           tma_load_2d(dv + blk * 2048, &tmKV, 0, rv, &v_full[st]);
           tma_load_2d(dv + kKVTile / 2 + blk * 2048, &tmKV, 64, rv, &v_full[st]);
@@ -767,8 +767,8 @@ void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64
   dim3 grid(ntiles, H);
   prefill_tc_kernel<<<grid, kThreads, kSmem, s>>>(tq, tkv, reinterpret_cast<__nv_bfloat16*>(out), out_stride,
                                                   block_tables, bt_stride, seq_lens, query_start, tiles, H, Hk,
-                                                  scale * 1.4426950408889634f, nullptr, window,
-                                                  softcap > 0.f ? softcap * 1.4426950408889634f : 0.f);
+                                                  scale * 1.4426950408889634f, bounds_status(), window,
+                                                  softcap > 0.f ? softcap * 1.4426950408889634f : 0.f, num_blocks);
   check_launch("paged_prefill_attention (tcgen05)");
 }
 
@@ -797,7 +797,7 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
                                            kFaSmem));                                                              \
     prefill_fa_kernel<E><<<grid, kFaThreads, kFaSmem, s>>>(tq, tkv, o, out_stride, block_tables, bt_stride,        \
                                                            seq_lens, query_start, w4, pair_heads ? 1 : 0, H, Hk,   \
-                                                           sl2, nullptr, window, cap);                             \
+                                                           sl2, bounds_status(), window, cap, num_blocks);         \
   } while (0)
   if (emu == 2)
     GOLLEK_FA_LAUNCH(2);

@@ -8,6 +8,7 @@
 // SiLU·up :261-290, RoPE runner/safetensor/gollek-safetensor-engine/…/attention/RopeFrequencyCache.java:49-107,
 // paged KV write …/attention/FlashAttentionKernel.java:166-194.
 #include "../common/common.cuh"
+#include "../common/tma_host.h"
 #include "launchers.h"
 
 using namespace gollek;
@@ -102,14 +103,16 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(
     const float* __restrict__ cos_sin, __nv_bfloat16* __restrict__ cache, const int* __restrict__ slots, int H,
     int Hk, int D, int block_size, int64_t qkv_stride, int max_pos, const __nv_bfloat16* __restrict__ bias,
     const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float norm_eps,
-    int rot) {
+    int rot, int num_blocks, uint32_t* bounds) {
   const int t = blockIdx.x;
   const int half = rot >> 1;
   int pos = positions[t];
   pos = pos < 0 ? 0 : (pos >= max_pos ? max_pos - 1 : pos);
   const float* cs = cos_sin + (int64_t)pos * rot;
   const __nv_bfloat16* row = qkv + (int64_t)t * qkv_stride;
-  const int slot = slots ? slots[t] : -1;
+  int slot = slots ? slots[t] : -1;
+  // a slot in a block beyond the pool is reported and its K/V write skipped
+  if (slot >= 0 && checked_index(slot / block_size, num_blocks, bounds, -1) < 0) slot = -1;
   const int64_t blk = slot >= 0 ? slot / block_size : 0;
   const int off = slot >= 0 ? slot % block_size : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -206,9 +209,11 @@ __global__ void __launch_bounds__(128) rope_kv_write_kernel(
 // ---------------------------------------------------------------------------------------------
 // scale != 1 multiplies the gathered row (Gemma's sqrt(hidden) embedding normaliser)
 __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int* __restrict__ ids,
-                                 const __nv_bfloat16* __restrict__ table, int d, int vocab, float scale) {
+                                 const __nv_bfloat16* __restrict__ table, int d, int vocab, float scale,
+                                 uint32_t* bounds) {
   const int t = blockIdx.x;
-  int id = ids[t];
+  const int raw = ids[t];
+  int id = checked_index(raw, vocab, bounds, raw < 0 ? 0 : vocab - 1);
   id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
   const uint4* src = reinterpret_cast<const uint4*>(table + (int64_t)id * d);
   uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)t * d);
@@ -270,7 +275,7 @@ void launch_rms_norm(void* out, const void* x, void* residual, const void* w, in
 void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
                           const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
                           int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,
-                          int rot, cudaStream_t s) {
+                          int rot, cudaStream_t s, int num_blocks) {
   throw_if(D % 16 != 0 || D > 256, "rope_kv_write: head_dim must be a multiple of 16, <= 256");
   throw_if(rot % 4 != 0 || rot > D || D - rot > 256, "rope_kv_write: rotary dims must be a multiple of 4, "
                                                      "<= head_dim, with at most 256 pass-through dims");
@@ -280,7 +285,8 @@ void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, co
                                          reinterpret_cast<__nv_bfloat16*>(cache), slots, H, Hk, D, block_size,
                                          qkv_stride, max_pos, reinterpret_cast<const __nv_bfloat16*>(bias),
                                          reinterpret_cast<const __nv_bfloat16*>(q_norm),
-                                         reinterpret_cast<const __nv_bfloat16*>(k_norm), norm_eps, rot);
+                                         reinterpret_cast<const __nv_bfloat16*>(k_norm), norm_eps, rot,
+                                         num_blocks, num_blocks > 0 ? bounds_status() : nullptr);
   check_launch("rope_kv_write");
 }
 
@@ -289,7 +295,8 @@ void launch_embedding(void* out, const int* ids, const void* table, int T, int d
   throw_if(d % 8 != 0, "embedding: dim must be a multiple of 8");
   if (T == 0) return;
   embedding_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(out), ids,
-                                     reinterpret_cast<const __nv_bfloat16*>(table), d, vocab, scale);
+                                     reinterpret_cast<const __nv_bfloat16*>(table), d, vocab, scale,
+                                     bounds_status());
   check_launch("embedding");
 }
 

@@ -340,6 +340,8 @@ void launch_weight_quant_fp8(void* q, float* scale, const void* w, int N, int K,
 void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* residual, int64_t ldr, int M, int N,
                    int splits, int epi, cudaStream_t s);
 
+int gemm_fp8_splits(int M, int N, int K, int epi);
+
 void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const float* sa, const void* b, int64_t ldb,
                      const float* sb, int M, int N, int K, int epi, int splits, float* partial, uint32_t* status,
                      cudaStream_t s) {
@@ -350,11 +352,7 @@ void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const f
   const int num_m = (M + kBM - 1) / kBM, num_n = N / kBN;
   const int tiles = num_m * num_n;
   const int num_kb = K / kBK;
-  if (splits <= 0) {  // fill the SMs for decode-sized M
-    splits = 1;
-    const int sms = num_sms();
-    if (tiles < sms) splits = std::max(1, std::min({(sms + tiles - 1) / tiles, num_kb / 4, 16}));
-  }
+  if (splits <= 0) splits = gemm_fp8_splits(M, N, K, epi);
   if (epi == kEpiSwiglu && splits == 1) splits = 2;  // SwiGLU is applied by the reduce pass
   throw_if(splits > 1 && partial == nullptr, "fp8 gemm: split-K needs an fp32 workspace");
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, lda, kBM, kBK, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -370,11 +368,13 @@ void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const f
   if (splits > 1) splitk_reduce(out, ldc, partial, nullptr, 0, M, N, splits, epi, s);
 }
 
+// Split-K factor for decode-sized M: as many K splits as fit the SMs in ONE wave (tiles x splits <=
+// SMs; a second wave of a few units would double the kernel time), at least 4 K blocks per split.
 int gemm_fp8_splits(int M, int N, int K, int epi) {
   const int tiles = ((M + kBM - 1) / kBM) * (N / kBN);
   int splits = 1;
-  const int sms = num_sms();
-  if (tiles < sms) splits = std::max(1, std::min({(sms + tiles - 1) / tiles, (K / kBK) / 4, 16}));
+  const int sms = gemm_grid_sms();
+  if (tiles < sms) splits = std::max(1, std::min({sms / tiles, (K / kBK) / 4, 16}));
   if (epi == kEpiSwiglu && splits == 1) splits = 2;
   return splits;
 }

@@ -13,6 +13,7 @@
 #include <cuda_fp8.h>
 
 #include "../common/common.cuh"
+#include "../common/tma_host.h"
 #include "launchers.h"
 
 namespace gollek {
@@ -24,7 +25,8 @@ constexpr float kE4m3Max = 448.f;
 // One warp per (token, K/V, kv head); D = 128: four values per lane.
 __global__ void __launch_bounds__(256) kv_quant_fp8_kernel(const __nv_bfloat16* __restrict__ kv,
                                                            const int* __restrict__ slots, uint8_t* __restrict__ cache,
-                                                           float* __restrict__ scales, int T, int Hk, int block_size) {
+                                                           float* __restrict__ scales, int T, int Hk, int block_size,
+                                                           int num_blocks, uint32_t* bounds) {
   constexpr int D = 128;
   const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (gw >= T * 2 * Hk) return;
@@ -32,6 +34,7 @@ __global__ void __launch_bounds__(256) kv_quant_fp8_kernel(const __nv_bfloat16* 
   const int which = rem / Hk, kh = rem % Hk;
   const int slot = slots[t];
   if (slot < 0) return;
+  if (checked_index(slot / block_size, num_blocks, bounds, -1) < 0) return;  // beyond the pool: skipped
   const int64_t blk = slot / block_size, off = slot % block_size;
   const __nv_bfloat16* src = kv + ((int64_t)(t * 2 + which) * Hk + kh) * D + lane * 4;
   const uint2 raw = *reinterpret_cast<const uint2*>(src);
@@ -83,13 +86,14 @@ __global__ void __launch_bounds__(256) kv_dequant_blocks_kernel(const uint8_t* _
 }  // namespace
 
 void launch_kv_quant_fp8(const void* kv, const int* slots, void* cache, float* scales, int T, int Hk, int D,
-                         int block_size, cudaStream_t s) {
+                         int block_size, cudaStream_t s, int num_blocks) {
   throw_if(D != 128, "fp8 KV cache: head_dim 128 only");
   if (T == 0) return;
   const int64_t warps = (int64_t)T * 2 * Hk;
   kv_quant_fp8_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(kv), slots,
                                                                    reinterpret_cast<uint8_t*>(cache), scales, T, Hk,
-                                                                   block_size);
+                                                                   block_size, num_blocks,
+                                                                   num_blocks > 0 ? bounds_status() : nullptr);
   check_launch("kv_quant_fp8");
 }
 

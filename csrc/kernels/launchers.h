@@ -29,7 +29,7 @@ void launch_rms_norm(void* out, const void* x, void* residual, const void* w, in
 void launch_rope_kv_write(void* q_out, const void* qkv, const int* positions, const float* cos_sin, void* cache,
                           const int* slots, int T, int H, int Hk, int D, int block_size, int64_t qkv_stride,
                           int max_pos, const void* bias, const void* q_norm, const void* k_norm, float norm_eps,
-                          int rot, cudaStream_t s);
+                          int rot, cudaStream_t s, int num_blocks = 0);
 void launch_embedding(void* out, const int* ids, const void* table, int T, int d, int vocab, float scale,
                       cudaStream_t s);
 void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
@@ -44,7 +44,8 @@ void launch_silu_mul(void* out, const void* x, int T, int d, cudaStream_t s);
 void launch_paged_decode(void* out, const void* q, int64_t q_stride, const void* cache, int num_blocks,
                          const int* block_tables, int bt_stride, const int* seq_lens, int B, int H, int Hk, int D,
                          int block_size, int num_splits, float scale, float* part_o, float* part_ml,
-                         int window, float softcap, cudaStream_t s, const float* kv_scales = nullptr);
+                         int window, float softcap, cudaStream_t s, const float* kv_scales = nullptr,
+                         bool tensor_cores = true);
 void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
@@ -61,7 +62,7 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,
-                          int window, float softcap, cudaStream_t s);
+                          int window, float softcap, cudaStream_t s, int num_blocks = 0);
 
 // ---- GEMM (K5, K8)
 // Gated epilogues (SwiGLU, GeGLU) read gate/up rows interleaved in groups of 64 and write N/2 columns.
@@ -209,7 +210,7 @@ void launch_moe_route(const void* x, int64_t ldx, const void* wr, int T, int H, 
 
 // ---- fp8 e4m3 paged KV cache (csrc/kernels/kv_fp8.cu)
 void launch_kv_quant_fp8(const void* kv, const int* slots, void* cache, float* scales, int T, int Hk, int D,
-                         int block_size, cudaStream_t s);
+                         int block_size, cudaStream_t s, int num_blocks = 0);
 void launch_kv_dequant_blocks(const void* cache, const float* scales, const int* ids, int n, int num_blocks, int Hk,
                               int D, int block_size, void* dst, cudaStream_t s);
 

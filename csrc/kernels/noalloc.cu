@@ -91,7 +91,7 @@ extern "C" __attribute__((visibility("default"))) int gollek_paged_decode_attent
   float* part_o = static_cast<float*>(scratch);
   float* part_ml = part_o + (size_t)B * H * num_splits * head_dim;
   try {
-    gollek::launch_paged_decode(out, q, q_stride, cache, head_dim == 128 ? num_blocks : 0, block_tables, bt_stride,
+    gollek::launch_paged_decode(out, q, q_stride, cache, num_blocks, block_tables, bt_stride,
                                 seq_lens, B, H, Hk, head_dim, block_size, num_splits, scale,
                                 num_splits > 1 ? part_o : nullptr, num_splits > 1 ? part_ml : nullptr,
                                 /*window=*/0, /*softcap=*/0.f, stream);

@@ -43,6 +43,37 @@ def _C(k: int = 1):
     return cuda_ext()
 
 
+class BoundsCheck:
+    """Device bounds checking of the indices kernels read from memory (block-table entries, KV
+    slots, token ids): while enabled, an index outside its pool records a status bit and the first
+    bad index in a device word, reads use a valid index instead and KV writes are skipped, so a
+    corrupt table gives wrong numbers and a readable report instead of a memory fault.
+
+        with ops.BoundsCheck() as bc:
+            ...                     # launches
+        bc.status()                 # (flags, first bad index or None); flag 4 = out of bounds
+    """
+    BOUNDS = 1 << 2
+
+    def __init__(self, device: Optional[torch.device] = None):
+        self.buf = torch.tensor([0, -1], dtype=torch.int32, device=device or "cuda")
+
+    def __enter__(self) -> "BoundsCheck":
+        cuda_ext().set_bounds_status(self.buf)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        torch.cuda.synchronize(self.buf.device)
+        cuda_ext().set_bounds_status(None)
+
+    def status(self):
+        flags, idx = (int(v) for v in self.buf.cpu())
+        return flags, (None if idx == -1 else idx & 0xFFFFFFFF)
+
+    def reset(self) -> None:
+        self.buf.copy_(torch.tensor([0, -1], dtype=torch.int32))
+
+
 def _cpu(result: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
     """CPU path: honour a caller-provided output buffer."""
     if out is None:
