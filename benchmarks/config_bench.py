@@ -41,6 +41,7 @@ def parse(argv=None):
     p.add_argument("--ffn", type=int, default=0, help="override the FFN width (small runs)")
     p.add_argument("--device", default="cuda")
     p.add_argument("--decode-steps", type=int, default=64)
+    p.add_argument("--skip-prefill", action="store_true", help="llama70b-fp8: decode only, no prefill sweep")
     p.add_argument("--scale", type=float, default=1.0, help="shrink batch / lengths (small runs)")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="TP collectives: fused P2P kernels over the IPC heap, or NCCL")
@@ -134,7 +135,7 @@ def llama70b_fp8(args, di, comm):
     while eng.has_unfinished():
         eng.step()
     # prefill sweep: batch 8 of L-token prompts, time until every first token is out
-    for L in (1024, 4096, 8192):
+    for L in (() if args.skip_prefill else (1024, 4096, 8192)):
         L = max(16, int(L * args.scale))
         ids = [f"p{L}-{i}" for i in range(8)]
         for r in ids:

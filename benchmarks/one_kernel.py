@@ -35,7 +35,7 @@ def _n_copies(weight_bytes: int) -> int:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn", "decode_fp8",
-                                     "decode_bf16", "q6k", "fp8gemm"])
+                                     "decode_bf16", "q6k", "fp8gemm", "gemm_bf16"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -43,6 +43,7 @@ def main():
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--bn", type=int, default=0)
     ap.add_argument("--swiglu", action="store_true")
+    ap.add_argument("--residual", action="store_true")
     ap.add_argument("--B", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1200)
     ap.add_argument("--nseq", type=int, default=4)
@@ -101,9 +102,24 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         for _ in range(a.reps):
             ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
-    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "fp8gemm"):
-        HBM_GBS, BF16_TFLOPS = 6534.5, 1400.9  # measured copy bandwidth and sustained bf16 GEMM peak
-        if a.kind == "decode_bf16":
+    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "fp8gemm", "gemm_bf16"):
+        # measured copy bandwidth, sustained and burst bf16 GEMM peaks
+        HBM_GBS, BF16_TFLOPS, BF16_BURST = 6534.5, 1400.9, 1672.7
+        if a.kind == "gemm_bf16":
+            # --swiglu: gate/up with the fused SwiGLU epilogue (N = 2 x FFN); --residual: + residual
+            w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
+            copies = [w.clone() for _ in range(_n_copies(a.N * a.K * 2))]
+            x = torch.randn(a.M, a.K, device=dev).bfloat16()
+            res = torch.randn(a.M, a.N, device=dev).bfloat16() if a.residual else None
+            turn = [0]
+
+            def fn():
+                wi = copies[turn[0] % len(copies)]
+                turn[0] += 1
+                ops.linear_swiglu(x, wi) if a.swiglu else ops.linear(x, wi, residual=res)
+            nbytes = a.N * a.K * 2 + a.M * a.K * 2
+            flops = 2.0 * a.M * a.N * a.K
+        elif a.kind == "decode_bf16":
             Hq, Hk, D, bs = 32, 8, 128, 16
             nblk = (a.ctx + bs - 1) // bs
             NB = a.B * nblk
@@ -179,7 +195,11 @@ def main():
                "hbm_frac_of_measured": round(nbytes / ms / 1e6 / HBM_GBS, 3)}
         if flops:
             res["TFLOPs"] = round(flops / ms / 1e9, 1)
-            res["frac_of_2x_measured_bf16"] = round(flops / ms / 1e9 / (2 * BF16_TFLOPS), 3)
+            if a.kind == "fp8gemm":
+                res["frac_of_2x_measured_bf16"] = round(flops / ms / 1e9 / (2 * BF16_TFLOPS), 3)
+            else:
+                res["frac_of_measured_bf16_sustained"] = round(flops / ms / 1e9 / BF16_TFLOPS, 3)
+                res["frac_of_measured_bf16_burst"] = round(flops / ms / 1e9 / BF16_BURST, 3)
         print(json.dumps(res))
     elif a.kind == "decode":
         Hq, Hk, D, bs = 32, 8, 128, 16

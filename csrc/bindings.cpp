@@ -420,6 +420,15 @@ std::vector<int64_t> gemm_plan_py(int64_t M, int64_t N, int64_t K, int64_t epi) 
   return {bn, sp};
 }
 
+std::vector<int64_t> gemm_retile_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
+  int bn = 0, sp = 1;
+  gemm_plan((int)M, (int)N, (int)K, (int)epi, bn, sp);
+  const int tiles = (int)((M + 127) / 128) * (int)((N + bn - 1) / bn);
+  int full = 0, bnt = 0;
+  if (sp == 1 && N % bn == 0) gemm_retile_plan(tiles, std::min(tiles, gemm_grid_sms()), bn, epi_gated((int)epi), full, bnt);
+  return {bn, full, bnt};
+}
+
 void argmax_out(torch::Tensor out, torch::Tensor logits) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "argmax: [B, V] logits");
@@ -755,7 +764,7 @@ void embedding_q8_0_py(torch::Tensor out, torch::Tensor ids, torch::Tensor table
 }
 
 void gemm_fp8_py(torch::Tensor out, torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, int64_t epi,
-                 int64_t splits, c10::optional<torch::Tensor> workspace) {
+                 int64_t splits, c10::optional<torch::Tensor> workspace, c10::optional<torch::Tensor> tile_cnt) {
   check_bf16(out, "out");
   check_cuda(a, "a");
   check_cuda(b, "b");
@@ -777,8 +786,15 @@ void gemm_fp8_py(torch::Tensor out, torch::Tensor a, torch::Tensor sa, torch::Te
                 "fp8 gemm: split-K ", sp, " needs an fp32 workspace of ", (int64_t)sp * M * N, " elements");
     part = workspace->data_ptr<float>();
   }
+  int* cnt = nullptr;
+  if (sp > 1 && tile_cnt.has_value()) {
+    const int64_t tiles = (int64_t)((M + 127) / 128) * (N / 128);
+    TORCH_CHECK(tile_cnt->is_cuda() && tile_cnt->scalar_type() == at::kInt && tile_cnt->numel() >= tiles,
+                "fp8 gemm: ", tiles, " zeroed int32 tile counters expected");
+    cnt = tile_cnt->data_ptr<int>();
+  }
   launch_gemm_fp8(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), sa.data_ptr<float>(), b.data_ptr(),
-                  b.stride(0), sb.data_ptr<float>(), M, N, K, (int)epi, sp, part, nullptr, cur_stream());
+                  b.stride(0), sb.data_ptr<float>(), M, N, K, (int)epi, sp, part, nullptr, cur_stream(), cnt);
 }
 
 void act_quant_fp8_py(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
@@ -803,7 +819,9 @@ int64_t gemm_fp8_splits_py(int64_t M, int64_t N, int64_t K, int64_t epi) {
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.def("gemm_fp8", &gemm_fp8_py, "block-scaled FP8 GEMM on tcgen05 (K6)");
+  m.def("gemm_fp8", &gemm_fp8_py, "block-scaled FP8 GEMM on tcgen05 (K6)", py::arg("out"), py::arg("a"),
+        py::arg("sa"), py::arg("b"), py::arg("sb"), py::arg("epi"), py::arg("splits"), py::arg("workspace"),
+        py::arg("tile_cnt") = py::none());
   m.def("gemm_fp8_splits", &gemm_fp8_splits_py);
   m.def("act_quant_fp8", &act_quant_fp8_py, "1x128 per-token-group FP8 quantisation (K7)");
   m.def("weight_quant_fp8", &weight_quant_fp8_py, "128x128 block FP8 weight quantisation");
@@ -860,9 +878,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &silu_mul_out, "SwiGLU activation");
   m.def("paged_decode_attention", &paged_decode_attention_out, "paged decode attention (K3)");
   m.def("paged_prefill_attention", &paged_prefill_attention_out, "paged prefill attention (K4)");
-  m.def("gemm_bf16", &gemm_bf16_out, "tcgen05 bf16 GEMM with fused epilogues (K5/K8)");
+  m.def("gemm_bf16", &gemm_bf16_out, "tcgen05 bf16 GEMM with fused epilogues (K5/K8)", py::arg("out"),
+        py::arg("a"), py::arg("b"), py::arg("residual"), py::arg("epi"), py::arg("bn"), py::arg("status"),
+        py::arg("grid_limit"), py::arg("splits"), py::arg("workspace"));
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
   m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
+  m.def("gemm_retile", &gemm_retile_py, "(tile width, whole-wave tiles, narrow tail tile width or 0) of a GEMM");
   m.def("num_sms", &device_num_sms);
   m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)",
         py::arg("out"), py::arg("x"), py::arg("router"), py::arg("w_gu"), py::arg("w_down"), py::arg("ws"),

@@ -77,10 +77,11 @@ GOLLEK_DEVICE void drain_bar(uint64_t* bar, uint32_t parity) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmBt,
                      __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
                      int M, int N, int K, int group_m, int splits, float* __restrict__ partial,
                      uint32_t* status, const int* __restrict__ tile_group, const int* __restrict__ num_m_dev,
-                     const PushArgs push) {
+                     const PushArgs push, int full_tiles, int bnt) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -103,20 +104,34 @@ __global__ void __launch_bounds__(192, 1)
   const int num_m = tile_group ? min(*num_m_dev, (M + Cfg::BM - 1) / Cfg::BM) : (M + Cfg::BM - 1) / Cfg::BM;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_units = num_tiles * splits;
+  // Tail re-tiling (bnt > 0): the first full_tiles tiles (whole waves of the grid) are BN wide; each
+  // remaining tile is cut into BN / bnt tiles bnt wide, so the last wave is a short one of narrow
+  // tiles instead of a mostly idle one of wide tiles. Each unit is a whole output tile (no split-K).
+  const int sub = bnt > 0 ? BN / bnt : 1;
+  const int num_units = bnt > 0 ? full_tiles + (num_tiles - full_tiles) * sub : num_tiles * splits;
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
   const int kb_per = (num_kb + splits - 1) / splits;
-  // work unit -> (m0, n0, k-block range). Units are split-major so CTAs running at the same time
-  // share a K slice of A; tiles follow a grouped raster (group_m M-tiles swept across all N tiles)
-  // so a slab of A stays resident in L2 while B streams.
-  auto unit_coords = [&](int u, int& m0, int& n0, int& kb0, int& kb1) {
-    const int ks = u / num_tiles, tile = u % num_tiles;
+  // work unit -> (m0, n0, k-block range, tile width). Units are split-major so CTAs running at the
+  // same time share a K slice of A; tiles follow a grouped raster (group_m M-tiles swept across all
+  // N tiles) so a slab of A stays resident in L2 while B streams.
+  auto unit_coords = [&](int u, int& m0, int& n0, int& kb0, int& kb1, int& bnu) {
+    int ks, tile, part = 0;
+    bnu = BN;
+    if (bnt > 0 && u >= full_tiles) {
+      ks = 0;
+      tile = full_tiles + (u - full_tiles) / sub;
+      part = (u - full_tiles) % sub;
+      bnu = bnt;
+    } else {
+      ks = u / num_tiles;
+      tile = u % num_tiles;
+    }
     const int gsz = group_m * num_n;
     const int g = tile / gsz, r = tile % gsz;
     const int first_m = g * group_m;
     const int gm = min(num_m - first_m, group_m);
     m0 = (first_m + r % gm) * Cfg::BM;
-    n0 = (r / gm) * BN;
+    n0 = (r / gm) * BN + part * bnu;
     kb0 = ks * kb_per;
     kb1 = min(num_kb, kb0 + kb_per);
   };
@@ -157,16 +172,16 @@ __global__ void __launch_bounds__(192, 1)
       int issued = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        int m0, n0, kb0, kb1;
-        unit_coords(u, m0, n0, kb0, kb1);
+        int m0, n0, kb0, kb1, bnu;
+        unit_coords(u, m0, n0, kb0, kb1, bnu);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bar(&empty[stage], phase ^ 1, status, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[stage], Cfg::A_BYTES + bnu * Cfg::BK * 2);
           tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, kb * Cfg::BK, m0, &full[stage]);
-          tma_load_2d(sB + stage * Cfg::B_BYTES, &tmB, kb * Cfg::BK,
+          tma_load_2d(sB + stage * Cfg::B_BYTES, bnu == BN ? &tmB : &tmBt, kb * Cfg::BK,
                       tile_group ? n0 + tile_group[m0 / Cfg::BM] * N : n0, &full[stage]);
           ++issued;
           if (++stage == STAGES) {
@@ -190,8 +205,9 @@ __global__ void __launch_bounds__(192, 1)
       int used = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
-        int m0, n0, kb0, kb1;
-        unit_coords(u, m0, n0, kb0, kb1);
+        int m0, n0, kb0, kb1, bnu;
+        unit_coords(u, m0, n0, kb0, kb1, bnu);
+        const uint32_t id = bnu == BN ? idesc : (bnu == 128 ? make_idesc_bf16(Cfg::BM, 128) : make_idesc_bf16(Cfg::BM, 64));
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!wait_bar(&tempty[acc], acc_phase ^ 1, status, abort_flag)) {
@@ -211,7 +227,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
             // +32 bytes along K inside the 128-byte swizzled row = +2 in the encoded address
-            umma_f16_ss(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            umma_f16_ss(d_tmem, a_desc + 2 * k, b_desc + 2 * k, id, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           *consumed = ++used;
@@ -238,8 +254,8 @@ __global__ void __launch_bounds__(192, 1)
       push_epoch = *reinterpret_cast<volatile const uint32_t*>(
                        &reinterpret_cast<const SymmHeader*>(push.bases[push.rank])->epoch) + 1;
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
-      int m0, n0, kb0, kb1;
-      unit_coords(u, m0, n0, kb0, kb1);
+      int m0, n0, kb0, kb1, bnu;
+      unit_coords(u, m0, n0, kb0, kb1, bnu);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!wait_bar(&tfull[acc], acc_phase, status, abort_flag)) break;
@@ -250,7 +266,7 @@ __global__ void __launch_bounds__(192, 1)
         // split-K: raw fp32 partial sums; the reduce kernel applies the epilogue
         float* prow = partial + ((int64_t)(u / num_tiles) * M + row) * N;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < bnu; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
@@ -266,7 +282,7 @@ __global__ void __launch_bounds__(192, 1)
       } else if constexpr (EPI == kEpiSwiglu || EPI == kEpiGeglu) {
         const int out_n = N / 2;
 #pragma unroll 1
-        for (int p = 0; p < BN / 128; ++p) {
+        for (int p = 0; p < bnu / 128; ++p) {
 #pragma unroll 1
           for (int h = 0; h < 64; h += 32) {
             uint32_t g[32], u[32];
@@ -293,7 +309,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < bnu; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
@@ -416,9 +432,18 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   const int group_m = (int)std::max<int64_t>(1, std::min<int64_t>(num_m, (32ll << 20) / a_tile_bytes));
   int grid = std::min(tiles * splits, gemm_grid_sms());
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
-  kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc,
+  // tail re-tiling: plain GEMMs only (no split-K, no grouped / push mode, whole output tiles)
+  int full_tiles = 0, bnt = 0;
+  if (splits == 1 && tile_group == nullptr && push == nullptr && N % BN == 0)
+    gemm_retile_plan(tiles, grid, BN, epi_gated(EPI), full_tiles, bnt);
+  CUtensorMap tbt = bnt > 0 ? make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)N * groups, K, ldb, bnt,
+                                           Cfg::BK, CU_TENSOR_MAP_SWIZZLE_128B)
+                            : tb;
+  if (bnt > 0) grid = std::min(full_tiles + (tiles - full_tiles) * (BN / bnt), std::max(grid, 1));
+  kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, tbt, reinterpret_cast<__nv_bfloat16*>(out), ldc,
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
-                                     partial, status, tile_group, num_m_dev, push ? *push : PushArgs{});
+                                     partial, status, tile_group, num_m_dev, push ? *push : PushArgs{}, full_tiles,
+                                     bnt);
   check_launch("gemm_bf16");
   if (splits > 1 && reduce) {
     const int out_n = (EPI == kEpiSwiglu || EPI == kEpiGeglu) ? N / 2 : N;
@@ -454,6 +479,39 @@ void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* res
   check_launch("split-K reduce");
 }
 
+// Relative time of one 128-row output tile of width bn (same K) against a 256-wide one: measured
+// 1.14x lower per-FLOP throughput of 128-wide tiles at M = 4352 gives 0.57; 64-wide tiles reload the
+// same A tile for a quarter of the MMA work.
+static double tile_time(int bn) { return bn >= 256 ? 1.0 : (bn == 128 ? 0.57 : 0.36); }
+
+void gemm_retile_plan(int tiles, int grid, int bn, bool gated, int& full_tiles, int& bnt) {
+  full_tiles = 0;
+  bnt = 0;
+  if (grid <= 0 || tiles <= grid) return;  // one partial wave: nothing to rebalance against
+  const int full = (tiles / grid) * grid, tail = tiles - full;
+  if (tail == 0) return;
+  double best = tile_time(bn);  // the tail as one more wave of bn-wide tiles
+  for (int t : {128, 64}) {
+    if (t >= bn || (gated && t < 128)) continue;  // gated epilogues need a gate/up pair (128 columns)
+    const int units = tail * (bn / t);
+    const double c = (double)((units + grid - 1) / grid) * tile_time(t);
+    if (c < 0.9 * best) {
+      best = c;
+      bnt = t;
+    }
+  }
+  if (bnt > 0) full_tiles = full;
+}
+
+// Output-tile waves x tile time for a bn-wide persistent GEMM, with the tail re-tiling.
+static double gemm_cost(int tiles, int sms, int bn, bool gated) {
+  int full, bnt;
+  gemm_retile_plan(tiles, sms, bn, gated, full, bnt);
+  if (bnt == 0) return (double)((tiles + sms - 1) / sms) * tile_time(bn);
+  const int units = (tiles - full) * (bn / bnt);
+  return (double)(full / sms) * tile_time(bn) + (double)((units + sms - 1) / sms) * tile_time(bnt);
+}
+
 int gemm_pick_bn(int M, int N, int epi) {
   const int num_m = (M + 127) / 128;
   const int sms = num_sms();
@@ -462,11 +520,8 @@ int gemm_pick_bn(int M, int N, int epi) {
     // with the fewest rounds x tile time. A 128-wide tile takes ~0.57 of a 256-wide one (measured
     // 1.14x lower per-FLOP throughput at M = 4352), which makes 128 win when 256-wide tiles leave a
     // mostly idle last round (e.g. M = 1344, N = 4096: 176 tiles on 148 SMs).
-    auto cost = [&](int bn, double rel) {
-      const int tiles = num_m * ((N + bn - 1) / bn);
-      return (double)((tiles + sms - 1) / sms) * rel;
-    };
-    return cost(128, 0.57) < cost(256, 1.0) ? 128 : 256;
+    auto cost = [&](int bn) { return gemm_cost(num_m * ((N + bn - 1) / bn), sms, bn, epi_gated(epi)); };
+    return cost(128) < cost(256) ? 128 : 256;
   }
   if (epi_gated(epi)) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
   if (num_m * ((N + 255) / 256) >= sms) return 256;

@@ -56,13 +56,26 @@ GOLLEK_DEVICE void drainb(uint64_t* bar, uint32_t parity) {
   while (!mbar_try_wait(bar, parity))
     if (gt() - t0 > kWait) break;
 }
+// Bounded wait until a shared counter reaches `target` (false on timeout or abort).
+GOLLEK_DEVICE bool spin_ge(volatile int* p, int target, volatile int* abort_flag, uint32_t* status) {
+  const uint64_t t0 = gt();
+  while (*p < target) {
+    if (*abort_flag) return false;
+    if (gt() - t0 > kWait) {
+      report_status(status, kStatusMbarTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     __nv_bfloat16* __restrict__ C, int64_t ldc, const float* __restrict__ sa,
                     const float* __restrict__ sb, int M, int N, int K, int group_m, int splits,
-                    float* __restrict__ partial, uint32_t* status) {
+                    float* __restrict__ partial, uint32_t* status, int* __restrict__ cnt, int epi) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sA = smem;
@@ -75,6 +88,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* consumed = abort_flag + 1;
+  volatile int* fx_last = consumed + 1;    // split-K fixup: this CTA finishes the tile
+  volatile int* fx_arrive = fx_last + 1;   // epilogue warps done with their partial rows
+  volatile int* fx_gen = fx_arrive + 1;    // fixups decided
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + kBN - 1) / kBN;
@@ -109,6 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     *consumed = 0;
+    *fx_arrive = 0;
+    *fx_gen = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -190,6 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lg = warp & 3, half = (warp - 2) >> 2;
     constexpr int kCols = kBN / 2;
     int kbc = 0;
+    int fx_seq = 0;  // split units this CTA has finished (the same sequence in all 8 epilogue warps)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       int m0, n0, kb0, kb1;
       unit_coords(u, m0, n0, kb0, kb1);
@@ -221,14 +240,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&pempty[pb]);
       }
       if (!ok) break;
-      if (row >= M) continue;
       const int col0 = n0 + half * kCols;
       if (splits > 1) {
-        float* prow = partial + ((int64_t)(u / num_tiles) * M + row) * N + col0;
+        if (row < M) {
+          float* prow = partial + ((int64_t)(u / num_tiles) * M + row) * N + col0;
 #pragma unroll
-        for (int c = 0; c < kCols; c += 4)
-          if (col0 + c + 4 <= N) *reinterpret_cast<float4*>(prow + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-      } else {  // (SwiGLU always runs split-K: the reduce pass pairs gate and up columns)
+          for (int c = 0; c < kCols; c += 4)
+            if (col0 + c + 4 <= N) *reinterpret_cast<float4*>(prow + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        }
+        if (cnt != nullptr) {
+          // the tile's last unit to finish sums the split partials and writes the output (no
+          // reduce kernel); the 8 epilogue warps meet through shared counters with bounded waits
+          const int tile = u % num_tiles;
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd((int*)fx_arrive, 1);
+          bool last = false;
+          if (lane == 0) {
+            if (warp == 2) {
+              if (spin_ge(fx_arrive, 8 * (fx_seq + 1), abort_flag, status)) {
+                __threadfence();
+                *fx_last = atomicAdd(&cnt[tile], 1) == splits - 1;
+              } else {
+                *fx_last = 0;
+              }
+              __threadfence_block();
+              *fx_gen = fx_seq + 1;
+            }
+            last = spin_ge(fx_gen, fx_seq + 1, abort_flag, status) && *fx_last;
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          ++fx_seq;
+          if (last) {
+            __threadfence();
+            if (row < M) {
+              const int64_t sstride = (int64_t)M * N;
+              const float* p0 = partial + (int64_t)row * N;
+              if (epi == kEpiSwiglu) {
+                // tile columns: gate n0 + [0, 64), up n0 + [64, 128); this warp writes outputs
+                // n0 / 2 + 32 half + [0, 32)
+#pragma unroll 1
+                for (int c = 0; c < 32; c += 8) {
+                  float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                  for (int sp = 0; sp < splits; ++sp) {
+                    const float* pg = p0 + sp * sstride + n0 + 32 * half + c;
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                      const float4 a = __ldcg(reinterpret_cast<const float4*>(pg) + q);
+                      const float4 b = __ldcg(reinterpret_cast<const float4*>(pg + 64) + q);
+                      g[4 * q] += a.x; g[4 * q + 1] += a.y; g[4 * q + 2] += a.z; g[4 * q + 3] += a.w;
+                      v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
+                    }
+                  }
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) v[e] *= silu(g[e]);
+                  *reinterpret_cast<uint4*>(C + (int64_t)row * ldc + n0 / 2 + 32 * half + c) = float_to_bf16x8(v);
+                }
+              } else {
+#pragma unroll 1
+                for (int c = 0; c < kCols; c += 8) {
+                  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                  for (int sp = 0; sp < splits; ++sp) {
+                    const float4* pv = reinterpret_cast<const float4*>(p0 + sp * sstride + col0 + c);
+                    const float4 a = __ldcg(pv), b = __ldcg(pv + 1);
+                    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+                  }
+                  *reinterpret_cast<uint4*>(C + (int64_t)row * ldc + col0 + c) = float_to_bf16x8(v);
+                }
+              }
+            }
+            if (warp == 2 && lane == 0) cnt[tile] = 0;  // ready for the next launch
+          }
+        }
+      } else if (row < M) {  // (SwiGLU always runs split-K: the reduce pairs gate and up columns)
 #pragma unroll
         for (int c = 0; c < kCols; c += 8) {
           if (col0 + c + 8 <= N)
@@ -344,7 +428,7 @@ int gemm_fp8_splits(int M, int N, int K, int epi);
 
 void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const float* sa, const void* b, int64_t ldb,
                      const float* sb, int M, int N, int K, int epi, int splits, float* partial, uint32_t* status,
-                     cudaStream_t s) {
+                     cudaStream_t s, int* tile_cnt) {
   throw_if(K % 128 != 0, "fp8 gemm: K must be a multiple of 128 (one scale block)");
   throw_if(N % 128 != 0, "fp8 gemm: N must be a multiple of 128");
   throw_if(lda % 16 != 0 || ldb % 16 != 0, "fp8 gemm: operand row pitch must be a multiple of 16 bytes");
@@ -362,10 +446,11 @@ void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const f
   const int grid = std::min(tiles * splits, gemm_grid_sms());
   auto kern = gemm_fp8_kernel<kEpiNone>;
   GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+  int* cnt = splits > 1 ? tile_cnt : nullptr;  // zeroed [tiles] counters: the kernel finishes split tiles
   kern<<<grid, kThreads, kSmem, s>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out), ldc, sa, sb, M, N, K, group_m,
-                                     splits, partial, status);
+                                     splits, partial, status, cnt, epi);
   check_launch("gemm_fp8");
-  if (splits > 1) splitk_reduce(out, ldc, partial, nullptr, 0, M, N, splits, epi, s);
+  if (splits > 1 && cnt == nullptr) splitk_reduce(out, ldc, partial, nullptr, 0, M, N, splits, epi, s);
 }
 
 // Split-K factor for decode-sized M: as many K splits as fit the SMs in ONE wave (tiles x splits <=

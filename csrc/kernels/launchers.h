@@ -14,6 +14,7 @@
 
 namespace gollek {
 
+
 inline void throw_if(bool bad, const std::string& msg) {
   if (bad) throw std::runtime_error(msg);
 }
@@ -74,6 +75,9 @@ inline bool epi_gated(int epi) { return epi == kEpiSwiglu || epi == kEpiGeglu; }
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
 int gemm_splits(int M, int N, int K, int epi);
+// Tail re-tiling of a persistent GEMM with `tiles` bn-wide output tiles on `grid` CTAs: full_tiles
+// (whole waves) stay bn wide, the rest are cut bnt wide (0: no re-tiling).
+void gemm_retile_plan(int tiles, int grid, int bn, bool gated, int& full_tiles, int& bnt);
 // splits: 0 = automatic (with bn = 0), 1 = none; partial: fp32 [splits, M, N] workspace when splits > 1.
 void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb,
                       const void* residual, int64_t ldr, int M, int N, int K, int epi, int bn, int splits,
@@ -156,7 +160,7 @@ int device_num_sms();
 // ---- block-scaled FP8 (K6, K7)
 void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const float* sa, const void* b, int64_t ldb,
                      const float* sb, int M, int N, int K, int epi, int splits, float* partial, uint32_t* status,
-                     cudaStream_t s);
+                     cudaStream_t s, int* tile_cnt = nullptr);
 int gemm_fp8_splits(int M, int N, int K, int epi);
 void launch_act_quant_fp8(void* q, float* scale, const void* x, int64_t ldx, int M, int K, cudaStream_t s);
 void launch_weight_quant_fp8(void* q, float* scale, const void* w, int N, int K, cudaStream_t s);

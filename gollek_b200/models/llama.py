@@ -902,7 +902,7 @@ class LlamaModel:
         if cuda:
             from ..native import cuda_ext
             ext = cuda_ext()
-            ext.set_gemm_sm_reserve(self.split_sms)
+            ops.set_gemm_sm_reserve(self.split_sms)
         n = len(self.layers)
 
         def collective(hi, r0, r1, part, w):
@@ -942,7 +942,7 @@ class LlamaModel:
                     comp.wait_event(ev)
         finally:
             if ext is not None:
-                ext.set_gemm_sm_reserve(0)
+                ops.set_gemm_sm_reserve(0)
         return gathered
 
     def _embed_rows(self, input_ids: torch.Tensor, meta: AttnMetadata) -> torch.Tensor:

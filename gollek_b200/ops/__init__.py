@@ -306,6 +306,15 @@ def gemm_plan(M: int, N: int, K: int, epi: int = EPI_NONE) -> tuple:
     return p
 
 
+_SM_RESERVE = [0]
+
+
+def set_gemm_sm_reserve(n: int) -> None:
+    """SMs the persistent GEMM grids leave free (for a collective running beside them)."""
+    _SM_RESERVE[0] = int(n)
+    cuda_ext().set_gemm_sm_reserve(int(n))
+
+
 def _gemm(out, a, w, residual, epi, bn):
     M, K = a.shape
     N = w.shape[0]
@@ -414,8 +423,11 @@ def linear_fp8(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, swiglu: b
     epi = EPI_SWIGLU if swiglu else EPI_NONE
     ext = cuda_ext()
     splits = ext.gemm_fp8_splits(M, w.N, w.K, epi)
-    ws = torch.empty(splits * M * w.N, dtype=torch.float32, device=a.device) if splits > 1 else None
-    _C(2 if splits > 1 else 1).gemm_fp8(out, xq, sa, w.q, w.scale, epi, splits, ws)
+    ws = cnt = None
+    if splits > 1:  # fp32 split partials, summed by each tile's last unit (zeroed tile counters)
+        ws = torch.empty(splits * M * w.N, dtype=torch.float32, device=a.device)
+        cnt = torch.zeros(((M + 127) // 128) * (w.N // 128), dtype=torch.int32, device=a.device)
+    _C().gemm_fp8(out, xq, sa, w.q, w.scale, epi, splits, ws, cnt)
     return out
 
 

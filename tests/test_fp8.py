@@ -51,19 +51,23 @@ def test_fp8_gemm_matches_oracle(M, N, K):
     xq_c, sa_c = F8.quantize_act(x.float().cpu())
     torch.testing.assert_close(sa.cpu(), sa_c, rtol=1e-2, atol=1e-6)
     ref = F8.reference_gemm(xq.cpu(), sa.cpu(), F8.FP8Weight(fw.q.cpu(), fw.scale.cpu(), N, K))
-    for splits in (1, 3):
+    tiles = ((M + 127) // 128) * (N // 128)
+    cnt = torch.zeros(tiles, dtype=torch.int32, device="cuda")
+    for splits, fixup in ((1, False), (3, False), (3, True), (5, True), (3, True)):
+        # fixup: the tile's last split unit sums the partials (counters must come back to zero)
         out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
         ws = torch.empty(splits * M * N, device="cuda") if splits > 1 else None
-        ops.cuda_ext().gemm_fp8(out, xq, sa, fw.q, fw.scale, 0, splits, ws)
+        ops.cuda_ext().gemm_fp8(out, xq, sa, fw.q, fw.scale, 0, splits, ws, cnt if fixup else None)
         torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2 * max(1.0, float(ref.abs().max()) / 4))
+        assert int(cnt.abs().sum()) == 0
     y = ops.linear(x, fw)  # automatic split choice
     torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=2e-2 * max(1.0, float(ref.abs().max()) / 4))
 
 
 @pytest.mark.gpu
-def test_fp8_swiglu():
+@pytest.mark.parametrize("M,F,K", [(33, 1024, 2048), (64, 3584, 8192)])
+def test_fp8_swiglu(M, F, K):
     from gollek_b200 import ops
-    M, F, K = 33, 1024, 2048
     g = torch.Generator(device="cuda").manual_seed(9)
     wg = (torch.randn(F, K, device="cuda", generator=g) * 0.03).bfloat16()
     wu = (torch.randn(F, K, device="cuda", generator=g) * 0.03).bfloat16()
@@ -73,4 +77,5 @@ def test_fp8_swiglu():
     xq, sa = F8.quantize_act(x)
     full = F8.reference_gemm(xq.cpu(), sa.cpu(), F8.FP8Weight(fw.q.cpu(), fw.scale.cpu(), fw.N, K)).view(M, -1, 2, 64)
     ref = (torch.nn.functional.silu(full[:, :, 0]) * full[:, :, 1]).reshape(M, -1)
-    torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=3e-2)
+    # bf16 output rounding grows with the magnitude (K = 8192 gives values of several units)
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=3e-2 * max(1.0, float(ref.abs().max()) / 4))

@@ -380,3 +380,55 @@ def test_kv_key_norms(D):
     got = ops.kv_key_norms(cache, ids)
     want = torch.stack([cache[:, b, 0].float().norm(dim=-1).mean() for b in ids.tolist()])
     torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(1344, 4096, 4096, 0), (1344, 4096, 14336, 1), (1344, 28672, 4096, 2),
+                                       (1344, 28672, 4096, 3), (1200, 4096, 2048, 0), (2500, 6144, 4096, 1)])
+def test_gemm_tail_retile(M, N, K, epi):
+    """The tiles past the grid's whole waves run as narrower tiles (a short last wave): equal to
+    the fp32 oracle for every epilogue."""
+    a = bf(torch.randn(M, K, device=DEV, generator=_g(40)) * 0.5)
+    w = bf(torch.randn(N, K, device=DEV, generator=_g(41)) * 0.02)
+    r = bf(torch.randn(M, N, device=DEV, generator=_g(42)))
+    bn, full, bnt = ops.cuda_ext().gemm_retile(M, N, K, epi)
+    if (M, N) in ((1344, 4096), (1200, 4096)):
+        assert full > 0 and bnt in (64, 128)  # the shapes this targets are re-tiled
+    if epi in (2, 3):
+        y = ops.linear_swiglu(a, w, act="silu" if epi == 2 else "gelu_tanh")
+        ref = R.gemm_swiglu(a.float(), w.float(), act="silu" if epi == 2 else "gelu_tanh")
+    else:
+        y = ops.linear(a, w, residual=r if epi == 1 else None)
+        ref = a.float() @ w.float().t() + (r.float() if epi == 1 else 0)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("temp,top_k,top_p,min_p", [(1.0, 0, 1.0, 0.0), (0.7, 20, 1.0, 0.0), (1.3, 0, 0.8, 0.0),
+                                                    (1.0, 40, 0.9, 0.05)])
+def test_sampler_distribution_matches_filtered_softmax(temp, top_k, top_p, min_p):
+    """Empirical token frequencies of many draws (one logits row, 16384 seeds) against the fp32
+    softmax over the top-k / min-p / top-p survivors: no draw outside the kept set, and a chi-square
+    test that accepts (p > 1e-4; fixed seeds, so the outcome is deterministic)."""
+    from scipy.stats import chisquare
+    V, N = 64, 16384
+    row = torch.randn(V, generator=torch.Generator().manual_seed(50)) * 1.5
+    logits = row[None].expand(N, V).contiguous()
+    t = torch.full((N,), temp)
+    k = torch.full((N,), top_k, dtype=torch.int32)
+    p = torch.full((N,), top_p)
+    mp = torch.full((N,), min_p)
+    seeds = torch.arange(N, dtype=torch.int64) * 7919 + 13
+    offs = torch.zeros(N, dtype=torch.int64)
+    draws = ops.sample(logits.to(DEV), t.to(DEV), k.to(DEV), p.to(DEV), mp.to(DEV), seeds.to(DEV), offs.to(DEV)).cpu()
+    probs = R.filtered_probs(row[None], t[:1], k[:1], p[:1], mp[:1])[0].double()
+    assert bool((probs[draws] > 0).all())  # never a filtered-out token
+    support = probs > 0
+    counts = torch.bincount(draws, minlength=V).double()[support]
+    expected = probs[support] * N
+    # merge rare tokens into one cell so every expected count is >= 5
+    order = expected.argsort(descending=True)
+    exp_s, cnt_s = expected[order], counts[order]
+    big = exp_s >= 5
+    e = torch.cat([exp_s[big], exp_s[~big].sum()[None]]) if (~big).any() else exp_s
+    c = torch.cat([cnt_s[big], cnt_s[~big].sum()[None]]) if (~big).any() else cnt_s
+    pval = chisquare(c.numpy(), e.numpy() * c.sum().item() / e.sum().item()).pvalue
+    assert pval > 1e-4, (pval, c.tolist(), e.tolist())
