@@ -35,7 +35,7 @@ def _n_copies(weight_bytes: int) -> int:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn", "decode_fp8",
-                                     "decode_bf16", "q6k", "fp8gemm", "gemm_bf16"])
+                                     "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -102,7 +102,7 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         for _ in range(a.reps):
             ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
-    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "fp8gemm", "gemm_bf16"):
+    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16"):
         # measured copy bandwidth, sustained and burst bf16 GEMM peaks
         HBM_GBS, BF16_TFLOPS, BF16_BURST = 6534.5, 1400.9, 1672.7
         if a.kind == "gemm_bf16":
@@ -148,6 +148,31 @@ def main():
                 ops.paged_decode_attention(q, cache, bt, sl, 1 / math.sqrt(D), sp, kv_scales=scl)
             nbytes = cache.numel() + scl.numel() * 4
             flops = None
+        elif a.kind in ("q4k", "int4"):
+            # Q4_K super-blocks (144 B / 256 weights, random nibbles and 6-bit scales, fp16 d = dmin =
+            # 2^-10) or GPTQ-style int4 (g128 scales); M tokens: GEMV for M <= 4, else the chunked
+            # dequant + tcgen05 GEMM
+            if a.kind == "q4k":
+                from gollek_b200.loaders import gguf as G
+                from gollek_b200.quant.gguf_weights import QWeight
+                raw = torch.randint(0, 255, (a.N * a.K // 256 * 144,), dtype=torch.uint8)
+                raw.view(-1, 144)[:, 0:4] = torch.tensor([0x00, 0x14, 0x00, 0x14], dtype=torch.uint8)
+                copies = [QWeight(raw.to(dev), a.N, a.K, G.GGML_Q4_K) for _ in range(_n_copies(raw.numel()))]
+                nbytes = raw.numel()
+            else:
+                from gollek_b200.quant.int4 import quantize_rtn
+                w4 = quantize_rtn((torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16())
+                wb = a.N * a.K // 2 + a.N * (a.K // 128) * 4
+                copies = [w4] + [quantize_rtn((torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16())
+                                 for _ in range(_n_copies(wb) - 1)]
+                nbytes = wb
+            x = torch.randn(a.M, a.K, device=dev).bfloat16()
+            turn = [0]
+
+            def fn():
+                ops.linear(x, copies[turn[0] % len(copies)])
+                turn[0] += 1
+            flops = 2.0 * a.M * a.N * a.K
         elif a.kind == "q6k":
             from gollek_b200.loaders import gguf as G
             from gollek_b200.quant.gguf_weights import QWeight
@@ -197,6 +222,8 @@ def main():
             res["TFLOPs"] = round(flops / ms / 1e9, 1)
             if a.kind == "fp8gemm":
                 res["frac_of_2x_measured_bf16"] = round(flops / ms / 1e9 / (2 * BF16_TFLOPS), 3)
+            elif a.kind in ("q4k", "int4"):
+                pass
             else:
                 res["frac_of_measured_bf16_sustained"] = round(flops / ms / 1e9 / BF16_TFLOPS, 3)
                 res["frac_of_measured_bf16_burst"] = round(flops / ms / 1e9 / BF16_BURST, 3)

@@ -273,40 +273,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++fx_seq;
           if (last) {
             __threadfence();
-            if (row < M) {
-              const int64_t sstride = (int64_t)M * N;
-              const float* p0 = partial + (int64_t)row * N;
-              if (epi == kEpiSwiglu) {
-                // tile columns: gate n0 + [0, 64), up n0 + [64, 128); this warp writes outputs
-                // n0 / 2 + 32 half + [0, 32)
-#pragma unroll 1
-                for (int c = 0; c < 32; c += 8) {
-                  float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                  for (int sp = 0; sp < splits; ++sp) {
-                    const float* pg = p0 + sp * sstride + n0 + 32 * half + c;
+            // all 256 epilogue threads share the tile's (row, 8-column group) items; each item's
+            // split partials are loaded 4 splits at a time with every load in flight
+            const int64_t sstride = (int64_t)M * N;
+            const int rows_valid = min(kBM, M - m0);
+            const bool glu = epi == kEpiSwiglu;
+            const int groups = glu ? 8 : 16;  // 8-column outputs per tile row
+            const int et = threadIdx.x - 64;  // 0..255
+            for (int it = et; it < rows_valid * groups; it += 256) {
+              const int r = m0 + it / groups, g8 = (it % groups) * 8;
+              const float* base = partial + (int64_t)r * N + n0 + g8;  // gate (SwiGLU) or plain columns
+              float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              for (int sp0 = 0; sp0 < splits; sp0 += 4) {
+                float4 va[4][2], vb[4][2];
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                      const float4 a = __ldcg(reinterpret_cast<const float4*>(pg) + q);
-                      const float4 b = __ldcg(reinterpret_cast<const float4*>(pg + 64) + q);
-                      g[4 * q] += a.x; g[4 * q + 1] += a.y; g[4 * q + 2] += a.z; g[4 * q + 3] += a.w;
-                      v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
+                for (int q = 0; q < 4; ++q) {
+                  if (sp0 + q < splits) {
+                    const float4* pa = reinterpret_cast<const float4*>(base + (sp0 + q) * sstride);
+                    va[q][0] = __ldcg(pa);
+                    va[q][1] = __ldcg(pa + 1);
+                    if (glu) {
+                      vb[q][0] = __ldcg(pa + 16);  // the up columns: 64 further
+                      vb[q][1] = __ldcg(pa + 17);
                     }
                   }
+                }
 #pragma unroll
-                  for (int e = 0; e < 8; ++e) v[e] *= silu(g[e]);
-                  *reinterpret_cast<uint4*>(C + (int64_t)row * ldc + n0 / 2 + 32 * half + c) = float_to_bf16x8(v);
-                }
-              } else {
-#pragma unroll 1
-                for (int c = 0; c < kCols; c += 8) {
-                  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                  for (int sp = 0; sp < splits; ++sp) {
-                    const float4* pv = reinterpret_cast<const float4*>(p0 + sp * sstride + col0 + c);
-                    const float4 a = __ldcg(pv), b = __ldcg(pv + 1);
-                    v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w; v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+                for (int q = 0; q < 4; ++q) {
+                  if (sp0 + q < splits) {
+                    a[0] += va[q][0].x; a[1] += va[q][0].y; a[2] += va[q][0].z; a[3] += va[q][0].w;
+                    a[4] += va[q][1].x; a[5] += va[q][1].y; a[6] += va[q][1].z; a[7] += va[q][1].w;
+                    if (glu) {
+                      b[0] += vb[q][0].x; b[1] += vb[q][0].y; b[2] += vb[q][0].z; b[3] += vb[q][0].w;
+                      b[4] += vb[q][1].x; b[5] += vb[q][1].y; b[6] += vb[q][1].z; b[7] += vb[q][1].w;
+                    }
                   }
-                  *reinterpret_cast<uint4*>(C + (int64_t)row * ldc + col0 + c) = float_to_bf16x8(v);
                 }
+              }
+              if (glu) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) a[e] = silu(a[e]) * b[e];
+                *reinterpret_cast<uint4*>(C + (int64_t)r * ldc + n0 / 2 + g8) = float_to_bf16x8(a);
+              } else {
+                *reinterpret_cast<uint4*>(C + (int64_t)r * ldc + n0 + g8) = float_to_bf16x8(a);
               }
             }
             if (warp == 2 && lane == 0) cnt[tile] = 0;  // ready for the next launch
