@@ -797,6 +797,28 @@ void gemm_fp8_py(torch::Tensor out, torch::Tensor a, torch::Tensor sa, torch::Te
                   b.stride(0), sb.data_ptr<float>(), M, N, K, (int)epi, sp, part, nullptr, cur_stream(), cnt);
 }
 
+void gemm_q4k_py(torch::Tensor out, torch::Tensor a, torch::Tensor w, int64_t N, int64_t K, int64_t epi,
+                 int64_t splits, c10::optional<torch::Tensor> workspace) {
+  check_bf16(a, "a");
+  check_bf16(out, "out");
+  check_cuda(w, "w");
+  TORCH_CHECK(w.scalar_type() == at::kByte && w.is_contiguous() && w.numel() == N * (K / 256) * 144,
+              "q4k gemm: raw Q4_K blocks [N, K/256 * 144] uint8");
+  TORCH_CHECK(a.stride(1) == 1 && a.size(1) == K && out.stride(1) == 1, "q4k gemm: a [M, K], row-major out");
+  const int M = a.size(0);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == (epi == kEpiSwiglu ? N / 2 : N), "q4k gemm: out shape");
+  int sp = (int)splits;
+  if (sp <= 0) sp = gemm_q4k_splits(M, (int)N, (int)K);
+  float* part = nullptr;
+  if (sp > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat && workspace->numel() >= (int64_t)sp * M * N,
+                "q4k gemm: split-K ", sp, " needs an fp32 workspace of ", (int64_t)sp * M * N, " elements");
+    part = workspace->data_ptr<float>();
+  }
+  launch_gemm_q4k(out.data_ptr(), out.stride(0), a.data_ptr(), a.stride(0), w.data_ptr(), M, (int)N, (int)K, (int)epi,
+                  sp, part, nullptr, cur_stream());
+}
+
 void act_quant_fp8_py(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
   check_bf16(x, "x");
   TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.is_contiguous() && scale.scalar_type() == at::kFloat,
@@ -883,6 +905,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("grid_limit"), py::arg("splits"), py::arg("workspace"));
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
   m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
+  m.def("gemm_q4k", &gemm_q4k_py, "Q4_K weight dequantized inside a tcgen05 GEMM (plain / SwiGLU)");
+  m.def("gemm_q4k_splits", [](int64_t M, int64_t N, int64_t K) { return gemm_q4k_splits((int)M, (int)N, (int)K); },
+        "split-K factor of the fused Q4_K GEMM");
   m.def("gemm_retile", &gemm_retile_py, "(tile width, whole-wave tiles, narrow tail tile width or 0) of a GEMM");
   m.def("num_sms", &device_num_sms);
   m.def("moe_forward", &moe_forward_out, "MoE layer: route, permute, grouped tcgen05 expert GEMMs, combine (K12)",

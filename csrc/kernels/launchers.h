@@ -164,6 +164,12 @@ void launch_gemm_fp8(void* out, int64_t ldc, const void* a, int64_t lda, const f
 int gemm_fp8_splits(int M, int N, int K, int epi);
 void launch_act_quant_fp8(void* q, float* scale, const void* x, int64_t ldx, int M, int K, cudaStream_t s);
 void launch_weight_quant_fp8(void* q, float* scale, const void* w, int N, int K, cudaStream_t s);
+// Q4_K weight (ggml super-blocks, [N rows] x [K / 256 x 144 bytes]) dequantized inside a tcgen05 GEMM
+// (csrc/kernels/gemm_q4k.cu): plain or SwiGLU epilogue (gate/up rows interleaved in groups of 64),
+// split-K partials reduced by splitk_reduce. splits <= 0: automatic.
+int gemm_q4k_splits(int M, int N, int K);
+void launch_gemm_q4k(void* out, int64_t ldc, const void* a, int64_t lda, const void* w, int M, int N, int K, int epi,
+                     int splits, float* partial, uint32_t* status, cudaStream_t s);
 void splitk_reduce(void* out, int64_t ldc, const float* partial, const void* residual, int64_t ldr, int M, int N,
                    int splits, int epi, cudaStream_t s);
 

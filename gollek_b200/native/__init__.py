@@ -41,7 +41,7 @@ CUDA_SOURCES = [
     "kernels/noalloc.cu",
     "kernels/lora.cu",
     "kernels/gguf.cu",
-    "kernels/gemm_fp8.cu",
+    "kernels/gemm_fp8.cu", "kernels/gemm_q4k.cu",
     "kernels/attention_tc.cu",
     "kernels/moe.cu",
     "kernels/kv_transfer.cu",

@@ -327,6 +327,7 @@ def _gemm(out, a, w, residual, epi, bn):
 
 
 GGUF_GEMV_MAX_TOKENS = 4
+Q4K_FUSED = os.environ.get("GOLLEK_Q4K_FUSED", "1") != "0"
 GGUF_CHUNK_BYTES = 48 << 20  # bf16 scratch per chunk: stays resident in the 126 MB L2
 
 
@@ -334,7 +335,8 @@ def _qlinear(a: torch.Tensor, w, out: Optional[torch.Tensor], swiglu: bool) -> t
     """Matmul with a GGUF-quantized weight.
 
     <= GGUF_GEMV_MAX_TOKENS rows: fused dequant GEMV (weights decoded in registers).
-    More rows: the weight is dequantized in row chunks of <= 48 MB of bf16 into a scratch buffer
+    More rows, Q4_K: the tcgen05 GEMM decodes the super-blocks into its shared-memory B tiles.
+    More rows, other types: the weight is dequantized in row chunks of <= 48 MB of bf16 into a scratch buffer
     that stays in L2, and each chunk is multiplied by the tcgen05 GEMM right away, so HBM sees
     the quantized bytes once plus the activations.
     """
@@ -348,6 +350,13 @@ def _qlinear(a: torch.Tensor, w, out: Optional[torch.Tensor], swiglu: bool) -> t
     out = torch.empty(M, n_out, dtype=a.dtype, device=a.device) if out is None else out
     if M <= GGUF_GEMV_MAX_TOKENS and (not swiglu or w.qtype == 12):
         _C().gguf_gemv(out, a, w.raw, w.qtype, N, w.K, swiglu)
+        return out
+    if w.qtype == 12 and Q4K_FUSED and N % 128 == 0 and w.K % 256 == 0 and a.stride(1) == 1 and a.stride(0) % 8 == 0:
+        # Q4_K: super-blocks decoded inside the tcgen05 GEMM (HBM reads 0.5625 bytes per weight)
+        ext = cuda_ext()
+        splits = ext.gemm_q4k_splits(M, N, w.K)
+        ws = torch.empty(splits * M * N, dtype=torch.float32, device=a.device) if splits > 1 else None
+        _C(2 if splits > 1 else 1).gemm_q4k(out, a, w.raw, N, w.K, EPI_SWIGLU if swiglu else EPI_NONE, splits, ws)
         return out
     rows = max(128, GGUF_CHUNK_BYTES // (2 * w.K) // 128 * 128)
     scratch = torch.empty(min(rows, N), w.K, dtype=torch.bfloat16, device=a.device)

@@ -150,3 +150,33 @@ def test_q6_k_gpu_dequant_and_gemv():
         y = ops.linear(x, qw)
         ref = x.float() @ host.cuda().t()
         torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(5, 256, 512), (64, 1024, 4096), (130, 6144, 4096), (300, 512, 2048)])
+def test_q4_k_fused_tcgen05_gemm(M, N, K):
+    """Q4_K super-blocks decoded inside the tcgen05 GEMM (more than 4 tokens): equal to x @ W^T over
+    the host dequantization of the same blocks; with split-K (small M) and whole tiles, and the
+    SwiGLU epilogue over gate/up rows interleaved in groups of 64."""
+    from gollek_b200 import ops
+    from gollek_b200.quant.gguf_weights import QWeight
+    g = torch.Generator().manual_seed(M + N)
+    w = torch.randn(N, K, generator=g) * 0.02
+    raw = G.quantize_blocks(w, G.GGML_Q4_K)
+    host = G.dequantize_blocks(raw, G.GGML_Q4_K, N * K).view(N, K)
+    qw = QWeight(raw.cuda(), N, K, G.GGML_Q4_K)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    ref = x.float() @ host.bfloat16().float().t()
+    y = ops.linear(x.cuda(), qw)
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=2e-2 * max(1.0, float(ref.abs().max()) / 4))
+    assert ops.cuda_ext().gemm_q4k_splits(M, N, K) >= 1
+    # SwiGLU: gate/up rows interleaved in groups of 64 (the layout the loader gives fused gate/up)
+    F = N // 2
+    wg, wu = torch.randn(F, K, generator=g) * 0.02, torch.randn(F, K, generator=g) * 0.02
+    wgu = ops.interleave_gate_up(wg, wu).contiguous()
+    raw2 = G.quantize_blocks(wgu, G.GGML_Q4_K)
+    host2 = G.dequantize_blocks(raw2, G.GGML_Q4_K, N * K).view(N, K).bfloat16().float()
+    qw2 = QWeight(raw2.cuda(), N, K, G.GGML_Q4_K)
+    y2 = ops.linear_swiglu(x.cuda(), qw2)
+    ref2 = ops.reference.gemm_swiglu(x.float(), host2)
+    torch.testing.assert_close(y2.float().cpu(), ref2, rtol=2e-2, atol=3e-2 * max(1.0, float(ref2.abs().max()) / 4))
