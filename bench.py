@@ -82,6 +82,8 @@ def parse():
                    help="TP: steps of at least this many tokens run as two halves whose collectives overlap "
                         "the other half's compute (0 = off)")
     p.add_argument("--overlap-sms", type=int, default=16, help="SMs the GEMMs leave free for the overlapped collectives")
+    p.add_argument("--overlap-min-world", type=int, default=4,
+                   help="TP: split-batch overlap only with at least this many ranks")
     return p.parse_args()
 
 
@@ -292,6 +294,7 @@ def main():
                       max_model_len=args.prompt_max + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
                       enable_prefix_caching=False, gpu_memory_utilization=0.90, comm_backend=args.comm,
                       async_scheduling=not args.no_async, tp_overlap_min_tokens=args.overlap_min_tokens,
+                      tp_overlap_min_world=args.overlap_min_world,
                       tp_overlap_sms=args.overlap_sms)
     comm = None
     check = None
@@ -487,7 +490,7 @@ def main():
         res["check"] = check
     if comm is not None and hasattr(comm, "nvls"):
         res["config"]["comm"] += "+nvls" if comm.nvls else "+p2p"
-        if comm.nvls and args.overlap_min_tokens:
+        if comm.nvls and args.overlap_min_tokens and di.world_size >= max(2, args.overlap_min_world):
             res["config"]["comm"] += f"+split-overlap(>={args.overlap_min_tokens} tokens, {args.overlap_sms} SMs)"
     if di.rank == 0:
         print(json.dumps(res))

@@ -108,7 +108,8 @@ class ModelRunner:
         self.d2h_bytes = 0  # device->host bytes read back (sampled token ids)
         # steps of at least this many tokens run as two halves whose tensor-parallel collectives
         # overlap the other half's compute (0 = never)
-        self.split_min_tokens = cfg.tp_overlap_min_tokens if cfg.tensor_parallel_size > 1 else 0
+        self.split_min_tokens = (cfg.tp_overlap_min_tokens
+                                 if cfg.tensor_parallel_size >= max(2, cfg.tp_overlap_min_world) else 0)
 
     # ------------------------------------------------------------------ batch preparation
     def _fill_host(self, out: SchedulerOutput) -> Tuple[int, int, List[Sequence], List[int]]:
