@@ -159,8 +159,8 @@ def mixtral_ep(args, di, comm):
         mcfg.num_hidden_layers = args.layers
     if args.ffn:
         mcfg.intermediate_size = args.ffn
-    n_pf, L, B, steps = max(1, int(16 * args.scale)), max(16, int(2048 * args.scale)), max(1, int(128 * args.scale)), \
-        max(4, int(256 * args.scale))
+    n_pf, L, B = max(1, int(16 * args.scale)), max(16, int(2048 * args.scale)), max(1, int(128 * args.scale))
+    steps = max(4, min(int(256 * args.scale), args.decode_steps))  # timed decode steps (TPOT is per step)
     kw = dict(model="mixtral-8x7b", device=args.device, dtype="bfloat16", tensor_parallel_size=di.world_size,
               enable_expert_parallel=di.world_size > 1, max_num_seqs=max(B, n_pf), max_num_batched_tokens=8192,
               max_model_len=L + steps + 32, enable_prefix_caching=False, use_cuda_graphs=cuda,
