@@ -35,7 +35,7 @@ def _n_copies(weight_bytes: int) -> int:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn", "decode_fp8",
-                                     "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16"])
+                                     "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -102,10 +102,32 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         for _ in range(a.reps):
             ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
-    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16"):
+    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope"):
         # measured copy bandwidth, sustained and burst bf16 GEMM peaks
         HBM_GBS, BF16_TFLOPS, BF16_BURST = 6534.5, 1400.9, 1672.7
-        if a.kind == "gemm_bf16":
+        if a.kind == "qkv_rope":
+            # Llama-3-8B QKV projection + RoPE + paged KV write for M tokens: fused epilogue
+            # (GOLLEK_ROPE_FUSED=1, default) or projection GEMM then rope_kv_write (=0)
+            H, Hk, D = 32, 8, 128
+            w = (torch.randn((H + 2 * Hk) * D, a.K, device=dev) * 0.02).bfloat16()
+            copies = [w.clone() for _ in range(_n_copies(w.numel() * 2))]
+            x = torch.randn(a.M, a.K, device=dev).bfloat16()
+            pos = torch.randint(0, 2048, (a.M,), device=dev).int()
+            inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev).float() / D))
+            ang = torch.arange(8192, device=dev).float()[:, None] * inv[None]
+            cos_sin = torch.cat([ang.cos(), ang.sin()], 1).contiguous()
+            NB = (a.M + 15) // 16 + 8
+            cache = torch.zeros(NB, 2, Hk, 16, D, dtype=torch.bfloat16, device=dev)
+            slots = torch.randperm(NB * 16, device=dev)[:a.M].int()
+            turn = [0]
+
+            def fn():
+                wi = copies[turn[0] % len(copies)]
+                turn[0] += 1
+                ops.linear_rope_kv(x, wi, pos, cos_sin, cache, slots, H, Hk, D)
+            nbytes = w.numel() * 2 + a.M * a.K * 2
+            flops = 2.0 * a.M * w.shape[0] * a.K
+        elif a.kind == "gemm_bf16":
             # --swiglu: gate/up with the fused SwiGLU epilogue (N = 2 x FFN); --residual: + residual
             w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
             copies = [w.clone() for _ in range(_n_copies(a.N * a.K * 2))]

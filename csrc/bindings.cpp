@@ -797,6 +797,42 @@ void gemm_fp8_py(torch::Tensor out, torch::Tensor a, torch::Tensor sa, torch::Te
                   b.stride(0), sb.data_ptr<float>(), M, N, K, (int)epi, sp, part, nullptr, cur_stream(), cnt);
 }
 
+void gemm_rope_kv_py(torch::Tensor q_out, torch::Tensor a, torch::Tensor w, torch::Tensor positions,
+                     torch::Tensor cos_sin, c10::optional<torch::Tensor> cache, c10::optional<torch::Tensor> slots,
+                     int64_t H, int64_t Hk) {
+  check_bf16(a, "x");
+  check_bf16(w, "w_qkv");
+  check_bf16(q_out, "q_out");
+  check_i32(positions, "positions");
+  check_same_device(a, w);
+  const int M = a.size(0), K = a.size(1);
+  TORCH_CHECK(a.stride(1) == 1 && w.stride(1) == 1 && w.size(1) == K && w.size(0) == (H + 2 * Hk) * 128,
+              "qkv gemm + rope: w [(H + 2 Hk) * 128, K]");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == (int64_t)M * H * 128, "qkv gemm + rope: q_out [T, H, 128]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == 128,
+              "qkv gemm + rope: cos/sin table [max_pos, 128] fp32 (full rotary)");
+  TORCH_CHECK(positions.numel() >= M, "qkv gemm + rope: one position per row");
+  RopeArgs r;
+  r.positions = positions.data_ptr<int>();
+  r.cos_sin = cos_sin.data_ptr<float>();
+  r.max_pos = (int)cos_sin.size(0);
+  r.q_out = q_out.data_ptr();
+  r.H = (int)H;
+  r.Hk = (int)Hk;
+  if (cache.has_value() && slots.has_value()) {
+    check_bf16(*cache, "kv_cache");
+    check_i32(*slots, "slots");
+    TORCH_CHECK(cache->dim() == 5 && cache->size(1) == 2 && cache->size(2) == Hk && cache->size(4) == 128 &&
+                    cache->is_contiguous() && slots->numel() >= M,
+                "qkv gemm + rope: cache [blocks, 2, Hk, block_size, 128] bf16, one slot per row");
+    r.cache = cache->data_ptr();
+    r.slots = slots->data_ptr<int>();
+    r.block_size = (int)cache->size(3);
+    r.num_blocks = (int)cache->size(0);
+  }
+  launch_gemm_rope_kv(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), M, K, r, cur_stream());
+}
+
 void gemm_q4k_py(torch::Tensor out, torch::Tensor a, torch::Tensor w, int64_t N, int64_t K, int64_t epi,
                  int64_t splits, c10::optional<torch::Tensor> workspace) {
   check_bf16(a, "a");
@@ -905,6 +941,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("grid_limit"), py::arg("splits"), py::arg("workspace"));
   m.def("gemm_pick_bn", &gemm_pick_bn, "tile width the GEMM would pick");
   m.def("gemm_plan", &gemm_plan_py, "(tile width, split-K factor) the GEMM picks for (M, N, K, epilogue)");
+  m.def("gemm_rope_kv", &gemm_rope_kv_py,
+        "QKV GEMM with the RoPE + paged KV-write epilogue (head_dim 128, full rotary, bf16 cache)");
   m.def("gemm_q4k", &gemm_q4k_py, "Q4_K weight dequantized inside a tcgen05 GEMM (plain / SwiGLU)");
   m.def("gemm_q4k_splits", [](int64_t M, int64_t N, int64_t K) { return gemm_q4k_splits((int)M, (int)N, (int)K); },
         "split-K factor of the fused Q4_K GEMM");

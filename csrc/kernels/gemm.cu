@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(192, 1)
                      __nv_bfloat16* __restrict__ C, int64_t ldc, const __nv_bfloat16* __restrict__ R, int64_t ldr,
                      int M, int N, int K, int group_m, int splits, float* __restrict__ partial,
                      uint32_t* status, const int* __restrict__ tile_group, const int* __restrict__ num_m_dev,
-                     const PushArgs push, int full_tiles, int bnt) {
+                     const PushArgs push, int full_tiles, int bnt, const RopeArgs rope) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -307,6 +307,63 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
+      } else if constexpr (EPI == kEpiRope) {
+        // head_dim-128 heads: q (rotated) -> q_out, k (rotated) / v -> the row's paged cache slot.
+        // The fp32 accumulator is rotated directly (one rounding, at the store).
+        const bool live = row < M;
+        int pos = live ? rope.positions[row] : 0;
+        pos = pos < 0 ? 0 : (pos >= rope.max_pos ? rope.max_pos - 1 : pos);
+        const float* cs = rope.cos_sin + (int64_t)pos * 128;
+        int slot = live && rope.slots != nullptr ? rope.slots[row] : -1;
+        if (slot >= 0 && (slot / rope.block_size >= rope.num_blocks)) slot = -1;  // beyond the pool: not written
+        auto* qo = reinterpret_cast<__nv_bfloat16*>(rope.q_out);
+        auto* kc = reinterpret_cast<__nv_bfloat16*>(rope.cache);
+#pragma unroll 1
+        for (int hb = 0; hb < bnu; hb += 128) {
+          const int head = (n0 + hb) >> 7;
+          __nv_bfloat16* dst = nullptr;
+          if (head < rope.H) {
+            dst = qo + ((int64_t)row * rope.H + head) * 128;
+          } else if (slot >= 0) {
+            const int which = head < rope.H + rope.Hk ? 0 : 1, kh = head - rope.H - which * rope.Hk;
+            const int64_t blk = slot / rope.block_size, off = slot % rope.block_size;
+            dst = kc + (((blk * 2 + which) * rope.Hk + kh) * rope.block_size + off) * 128;
+          }
+          const bool rotate = head < rope.H + rope.Hk;
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t x1[32], x2[32];
+            tmem_ld_32x32b_x32(tbase + hb + c, x1);
+            tmem_ld_32x32b_x32(tbase + hb + 64 + c, x2);
+            tmem_ld_wait();
+            if (!live || dst == nullptr) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float o1[8], o2[8];
+              if (rotate) {
+                const float4* cp = reinterpret_cast<const float4*>(cs + c + 8 * j);
+                const float4* sp = reinterpret_cast<const float4*>(cs + 64 + c + 8 * j);
+                const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+                const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float a = __uint_as_float(x1[8 * j + e]), b = __uint_as_float(x2[8 * j + e]);
+                  o1[e] = a * cv[e] - b * sv[e];
+                  o2[e] = b * cv[e] + a * sv[e];
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  o1[e] = __uint_as_float(x1[8 * j + e]);
+                  o2[e] = __uint_as_float(x2[8 * j + e]);
+                }
+              }
+              *reinterpret_cast<uint4*>(dst + c + 8 * j) = float_to_bf16x8(o1);
+              *reinterpret_cast<uint4*>(dst + 64 + c + 8 * j) = float_to_bf16x8(o2);
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < bnu; c += 32) {
@@ -417,7 +474,7 @@ template <int BN, int EPI>
 void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const void* b, int64_t ldb, const void* res,
                    int64_t ldr, int M, int N, int K, int splits, float* partial, uint32_t* status, int grid_limit,
                    cudaStream_t s, const int* tile_group = nullptr, const int* num_m_dev = nullptr, int groups = 1,
-                   bool reduce = true, const PushArgs* push = nullptr) {
+                   bool reduce = true, const PushArgs* push = nullptr, const RopeArgs* rope = nullptr) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta = make_tmap_2d(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, lda, Cfg::BM, Cfg::BK,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -435,7 +492,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   // tail re-tiling: plain GEMMs only (no split-K, no grouped / push mode, whole output tiles)
   int full_tiles = 0, bnt = 0;
   if (splits == 1 && tile_group == nullptr && push == nullptr && N % BN == 0)
-    gemm_retile_plan(tiles, grid, BN, epi_gated(EPI), full_tiles, bnt);
+    gemm_retile_plan(tiles, grid, BN, epi_wide(EPI), full_tiles, bnt);
   CUtensorMap tbt = bnt > 0 ? make_tmap_2d(b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)N * groups, K, ldb, bnt,
                                            Cfg::BK, CU_TENSOR_MAP_SWIZZLE_128B)
                             : tb;
@@ -443,7 +500,7 @@ void launch_gemm_t(void* out, int64_t ldc, const void* a, int64_t lda, const voi
   kern<<<grid, 192, Cfg::SMEM, s>>>(ta, tb, tbt, reinterpret_cast<__nv_bfloat16*>(out), ldc,
                                      reinterpret_cast<const __nv_bfloat16*>(res), ldr, M, N, K, group_m, splits,
                                      partial, status, tile_group, num_m_dev, push ? *push : PushArgs{}, full_tiles,
-                                     bnt);
+                                     bnt, rope ? *rope : RopeArgs{});
   check_launch("gemm_bf16");
   if (splits > 1 && reduce) {
     const int out_n = (EPI == kEpiSwiglu || EPI == kEpiGeglu) ? N / 2 : N;
@@ -520,10 +577,10 @@ int gemm_pick_bn(int M, int N, int epi) {
     // with the fewest rounds x tile time. A 128-wide tile takes ~0.57 of a 256-wide one (measured
     // 1.14x lower per-FLOP throughput at M = 4352), which makes 128 win when 256-wide tiles leave a
     // mostly idle last round (e.g. M = 1344, N = 4096: 176 tiles on 148 SMs).
-    auto cost = [&](int bn) { return gemm_cost(num_m * ((N + bn - 1) / bn), sms, bn, epi_gated(epi)); };
+    auto cost = [&](int bn) { return gemm_cost(num_m * ((N + bn - 1) / bn), sms, bn, epi_wide(epi)); };
     return cost(128) < cost(256) ? 128 : 256;
   }
-  if (epi_gated(epi)) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
+  if (epi_wide(epi)) return (num_m * ((N + 255) / 256) >= sms) ? 256 : 128;
   if (num_m * ((N + 255) / 256) >= sms) return 256;
   if (num_m * ((N + 127) / 128) >= sms / 2) return 128;
   return 64;
@@ -543,7 +600,7 @@ void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits) {
   (void)num_m;
   splits = 1;
   if (bn == 0) bn = gemm_pick_bn(M, N, epi);
-  if (epi_gated(epi) && bn < 128) bn = 128;
+  if (epi_wide(epi) && bn < 128) bn = 128;
 }
 
 int gemm_splits(int M, int N, int K, int epi) {
@@ -567,7 +624,7 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
     if (splits <= 0) splits = sp;
   }
   if (splits <= 0) splits = 1;
-  if (epi_gated(epi) && bn < 128) bn = 128;
+  if (epi_wide(epi) && bn < 128) bn = 128;
   throw_if(splits > 1 && partial == nullptr, "gemm: split-K needs an fp32 workspace");
 #define GOLLEK_GEMM_CASE(BNV, EPIV) \
   if (bn == BNV && epi == EPIV)     \
@@ -585,6 +642,25 @@ void launch_gemm_bf16(void* out, int64_t ldc, const void* a, int64_t lda, const 
   GOLLEK_GEMM_CASE(128, kEpiGeglu)
 #undef GOLLEK_GEMM_CASE
   throw_if(true, "gemm: unsupported tile width " + std::to_string(bn) + " / epilogue " + std::to_string(epi));
+}
+
+void launch_gemm_rope_kv(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int K, const RopeArgs& rope,
+                         cudaStream_t s) {
+  throw_if(K % 8 != 0, "qkv gemm: K must be a multiple of 8");
+  throw_if(rope.H <= 0 || rope.Hk <= 0 || rope.positions == nullptr || rope.cos_sin == nullptr || rope.q_out == nullptr,
+           "qkv gemm + rope: arguments");
+  throw_if(rope.max_pos <= 0 || (rope.cache != nullptr && (rope.slots == nullptr || rope.block_size <= 0)),
+           "qkv gemm + rope: cache arguments");
+  if (M == 0) return;
+  const int N = (rope.H + 2 * rope.Hk) * 128;
+  int bn = 0, splits = 1;
+  gemm_plan(M, N, K, kEpiRope, bn, splits);
+  // heads are 128 wide: 128- or 256-wide tiles hold whole heads (the re-tiled tail too)
+  if (bn == 256)
+    return launch_gemm_t<256, kEpiRope>(rope.q_out, N, a, lda, b, ldb, nullptr, 0, M, N, K, 1, nullptr, nullptr, 0, s,
+                                        nullptr, nullptr, 1, true, nullptr, &rope);
+  return launch_gemm_t<128, kEpiRope>(rope.q_out, N, a, lda, b, ldb, nullptr, 0, M, N, K, 1, nullptr, nullptr, 0, s,
+                                      nullptr, nullptr, 1, true, nullptr, &rope);
 }
 
 void launch_gemm_push(void* out, const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, int bn,
@@ -631,7 +707,7 @@ void launch_gemm_grouped(void* out, int64_t ldc, const void* a, int64_t lda, con
     const int m_tiles = std::max(groups, std::min(M_cap / 128, groups * 2));
     bn = (m_tiles * ((N + 255) / 256) >= num_sms() || epi == kEpiSwiglu) ? 256 : 128;
   }
-  if (epi_gated(epi) && bn < 128) bn = 128;
+  if (epi_wide(epi) && bn < 128) bn = 128;
   if (splits < 1) splits = 1;
   // split-K partials [splits, M_cap, N] are left for the caller to reduce (no reduce pass here)
   throw_if(splits > 1 && (partial == nullptr || epi != kEpiNone), "grouped gemm: split-K needs fp32 partials, no epilogue");

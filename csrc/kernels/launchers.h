@@ -70,8 +70,26 @@ void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t 
 // kEpiPush: plain output, also pushed to every tensor-parallel peer's inbox (GEMM → all-reduce).
 // kEpiScatter: output row r is stored at the address in a per-row table (the `out` argument is a
 // uint64 [M] table; 0 = skip the row); the destinations may be peer memory (NVLink stores)
-enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3, kEpiPush = 4, kEpiScatter = 5 };
+// kEpiRope: the QKV projection's epilogue: head_dim-128 heads [q (H) | k (Hk) | v (Hk)] per row;
+// NeoX RoPE of q and k heads (cos/sin of the row's position), q to q_out [T, H, 128], k / v into
+// the paged bf16 cache at the row's slot (the RopeArgs below); no [T, (H + 2Hk) * 128] output.
+enum GemmEpilogue : int { kEpiNone = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiGeglu = 3, kEpiPush = 4, kEpiScatter = 5,
+                          kEpiRope = 6 };
 inline bool epi_gated(int epi) { return epi == kEpiSwiglu || epi == kEpiGeglu; }
+// epilogues that need whole 128-column groups in a tile (gate/up pairs, head_dim-128 heads)
+inline bool epi_wide(int epi) { return epi_gated(epi) || epi == kEpiRope; }
+struct RopeArgs {
+  const int* positions = nullptr;   // [T]
+  const float* cos_sin = nullptr;   // [max_pos, 128]: 64 cos, then 64 sin
+  int max_pos = 0;
+  void* q_out = nullptr;            // bf16 [T, H, 128]
+  void* cache = nullptr;            // bf16 [num_blocks, 2, Hk, block_size, 128]
+  const int* slots = nullptr;       // [T] cache slot of each row (< 0: not written)
+  int H = 0, Hk = 0, block_size = 16, num_blocks = 0;
+};
+// QKV GEMM with the RoPE + paged KV-write epilogue (head_dim 128, full rotary, bf16 cache).
+void launch_gemm_rope_kv(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int K, const RopeArgs& rope,
+                         cudaStream_t s);
 int gemm_pick_bn(int M, int N, int epi);
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits);
 int gemm_splits(int M, int N, int K, int epi);

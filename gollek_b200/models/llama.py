@@ -862,19 +862,30 @@ class LlamaModel:
                 and self.num_gdn_layers == 0 and not cfg.is_mla and self.lora is None and self.offload is None
                 and not cfg.sandwich_norm and not cfg.parallel_block and not cfg.norm_center)
 
+    def _plain_qkv(self, L: dict, kv_scales) -> bool:
+        """The QKV projection can carry RoPE + the KV write in its GEMM epilogue: a plain bf16 weight,
+        no bias / QK-norm / LoRA / fp8 cache (``ops.linear_rope_kv`` checks the shapes)."""
+        return (self.lora is None and kv_scales is None and L.get("qkv_bias") is None and L.get("q_norm") is None
+                and isinstance(L["w_qkv"], torch.Tensor) and L["w_qkv"].dtype == torch.bfloat16
+                and L["w_qkv"].is_cuda)
+
     def _attn_block(self, x: torch.Tensor, L: dict, meta: AttnMetadata, kv_cache, li: int) -> torch.Tensor:
         """QKV GEMM, RoPE + paged KV write, attention of the rows of ``x`` ([T, H*D] output)."""
         cfg = self.cfg
-        qkv = ops.linear(x, L["w_qkv"])
         cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
         win = self.windows[li]
         cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
         if self.cos_sin_none is not None and win == 0:
             cs = self.cos_sin_none
         scl = self._kv_scales(li)
-        q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
-                              bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
-                              norm_eps=cfg.rms_norm_eps, kv_scales=scl)
+        if self._plain_qkv(L, scl):
+            q = ops.linear_rope_kv(x, L["w_qkv"], meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk,
+                                   self.D)
+        else:
+            qkv = ops.linear(x, L["w_qkv"])
+            q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
+                                  bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                                  norm_eps=cfg.rms_norm_eps, kv_scales=scl)
         return self._attention(q, cache, meta, win, scl).view(x.shape[0], self.H * self.D)
 
     def _forward_split(self, input_ids: torch.Tensor, meta: AttnMetadata, kv_cache: Optional[torch.Tensor]):
@@ -989,18 +1000,22 @@ class LlamaModel:
                 cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
                 a = self._mla(x, L, meta, cache).view(T, self.H * self.D)
             else:
-                qkv = ops.linear(x, L["w_qkv"])
-                if self.lora is not None:
-                    self.lora.apply(li, "qkv", x, qkv)
                 cache = kv_cache[self.kv_index[li]] if kv_cache is not None else None
                 win = self.windows[li]
                 cs = self.cos_sin_local if (self.cos_sin_local is not None and win > 0) else self.cos_sin
                 if self.cos_sin_none is not None and win == 0:
                     cs = self.cos_sin_none
                 scl = self._kv_scales(li)
-                q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
-                                      bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
-                                      norm_eps=eps, kv_scales=scl)
+                if self._plain_qkv(L, scl):  # RoPE + KV write in the QKV GEMM's epilogue
+                    q = ops.linear_rope_kv(x, L["w_qkv"], meta.positions, cs, cache, meta.slot_mapping, self.H,
+                                           self.Hk, self.D)
+                else:
+                    qkv = ops.linear(x, L["w_qkv"])
+                    if self.lora is not None:
+                        self.lora.apply(li, "qkv", x, qkv)
+                    q = ops.rope_kv_write(qkv, meta.positions, cs, cache, meta.slot_mapping, self.H, self.Hk, self.D,
+                                          bias=L.get("qkv_bias"), q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                                          norm_eps=eps, kv_scales=scl)
                 a = self._attention(q, cache, meta, win, scl).view(T, self.H * self.D)
             if cfg.parallel_block:  # h = attn(x) + mlp(x): the down GEMM adds the attention partial
                 ha = ops.linear(a, L["w_o"])

@@ -133,6 +133,28 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
     return q_out
 
 
+ROPE_FUSED = os.environ.get("GOLLEK_ROPE_FUSED", "1") != "0"
+
+
+def linear_rope_kv(x: torch.Tensor, w_qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
+                   kv_cache: Optional[torch.Tensor], slot_mapping: Optional[torch.Tensor], num_heads: int,
+                   num_kv_heads: int, head_dim: int) -> torch.Tensor:
+    """q = RoPE(x @ Wq^T); RoPE(x @ Wk^T) and x @ Wv^T written into the paged KV cache; returns q
+    [T, H, D]. On the GPU with a plain bf16 weight, head_dim 128, full rotary and a bf16 cache this is
+    one tcgen05 GEMM whose epilogue rotates q/k and stores q and the cache rows (the [T, (H + 2Hk) D]
+    projection is never written); otherwise the projection GEMM followed by ``rope_kv_write``."""
+    fused = (ROPE_FUSED and x.is_cuda and isinstance(w_qkv, torch.Tensor) and w_qkv.dtype == torch.bfloat16
+             and head_dim == 128 and cos_sin.shape[1] == 128 and x.stride(1) == 1 and x.stride(0) % 8 == 0
+             and (kv_cache is None or kv_cache.dtype == torch.bfloat16))
+    if not fused:
+        qkv = linear(x, w_qkv)
+        return rope_kv_write(qkv, positions, cos_sin, kv_cache, slot_mapping, num_heads, num_kv_heads, head_dim)
+    q = torch.empty(x.shape[0], num_heads, head_dim, dtype=x.dtype, device=x.device)
+    _C().gemm_rope_kv(q, x, w_qkv, positions, cos_sin, kv_cache if slot_mapping is not None else None,
+                      slot_mapping if kv_cache is not None else None, num_heads, num_kv_heads)
+    return q
+
+
 # ----------------------------------------------------------------------------- attention
 def decode_splits(num_seqs: int, num_kv_heads: int, max_seq_len: int, num_sms: int = 148,
                   block_size: int = 16) -> int:

@@ -432,3 +432,29 @@ def test_sampler_distribution_matches_filtered_softmax(temp, top_k, top_p, min_p
     c = torch.cat([cnt_s[big], cnt_s[~big].sum()[None]]) if (~big).any() else cnt_s
     pval = chisquare(c.numpy(), e.numpy() * c.sum().item() / e.sum().item()).pvalue
     assert pval > 1e-4, (pval, c.tolist(), e.tolist())
+
+
+@pytest.mark.parametrize("T", [1, 37, 300, 1344])
+def test_qkv_gemm_with_rope_kv_epilogue(T):
+    """The QKV GEMM's RoPE + paged KV-write epilogue equals the unfused projection GEMM followed by
+    rope_kv_write: q, and every cache row written (rows with slot -1 are not written)."""
+    H, Hk, D, K, NB, BS = 32, 8, 128, 4096, 128, 16
+    g = _g(60)
+    x = bf(torch.randn(T, K, device=DEV, generator=g) * 0.5)
+    w = bf(torch.randn((H + 2 * Hk) * D, K, device=DEV, generator=g) * 0.02)
+    pos = torch.randint(0, 900, (T,), device=DEV, generator=g).int()
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=DEV).float() / D))
+    ang = torch.arange(1024, device=DEV).float()[:, None] * inv[None]
+    cos_sin = torch.cat([ang.cos(), ang.sin()], 1).contiguous()
+    slots = torch.randperm(NB * BS, device=DEV, generator=g)[:T].int()
+    if T > 2:
+        slots[1] = -1
+    c1 = torch.zeros(NB, 2, Hk, BS, D, dtype=torch.bfloat16, device=DEV)
+    c2 = torch.zeros_like(c1)
+    q1 = ops.linear_rope_kv(x, w, pos, cos_sin, c1, slots, H, Hk, D)
+    qkv = ops.linear(x, w)
+    q2 = ops.rope_kv_write(qkv, pos, cos_sin, c2, slots, H, Hk, D)
+    torch.testing.assert_close(q1.float(), q2.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(c1.float(), c2.float(), rtol=1e-2, atol=1e-2)
+    written = (c1.abs().sum(dim=(1, 2, 4)) > 0).sum().item()
+    assert written == int((slots >= 0).sum())
