@@ -491,7 +491,11 @@ def main():
     if comm is not None and hasattr(comm, "nvls"):
         res["config"]["comm"] += "+nvls" if comm.nvls else "+p2p"
         if comm.nvls and args.overlap_min_tokens and di.world_size >= max(2, args.overlap_min_world):
-            res["config"]["comm"] += f"+split-overlap(>={args.overlap_min_tokens} tokens, {args.overlap_sms} SMs)"
+            state = eng.runner.split_overlap_state
+            res["config"]["comm"] += f"+split-overlap[{state}](>={args.overlap_min_tokens} tokens, {args.overlap_sms} SMs)"
+            tune = eng.runner._tune.get("ms_per_token")
+            if tune:
+                res["config"]["split_overlap_tuning_ms_per_token_sum_over_ranks"] = [round(v, 6) for v in tune]
     if di.rank == 0:
         print(json.dumps(res))
     eng.runner.graphs.clear()

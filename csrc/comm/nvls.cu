@@ -150,16 +150,24 @@ __global__ void __launch_bounds__(kNvThreads) tp_nvls_ar_rmsnorm_kernel(NvlsArgs
   const __nv_bfloat16* pmc = reinterpret_cast<const __nv_bfloat16*>(a.mc + a.partial_off[a.parity]);
   __nv_bfloat16* xmc = reinterpret_cast<__nv_bfloat16*>(a.mc + a.x_off);
   const int warps = gridDim.x * (kNvThreads / 32);
-  for (int row = r0 + blockIdx.x * (kNvThreads / 32) + (threadIdx.x >> 5); row < r1; row += warps) {
-    const int64_t base = (int64_t)row * a.d;
-    uint4 p[VPL], res[VPL];
+  // The next row's reductions are issued before this row is normalised, so a warp with several
+  // rows pays the NVSwitch round trip once (the grid is at most one CTA per SM).
+  int row = r0 + blockIdx.x * (kNvThreads / 32) + (threadIdx.x >> 5);
+  uint4 p[VPL];
+  if (row < r1) {
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int v = lane + 32 * j;
-      if (v < nvec) {
-        p[j] = mm_ld_reduce_bf16x8(pmc + base + v * 8);
-        res[j] = *reinterpret_cast<const uint4*>(residual + base + v * 8);
-      }
+      if (v < nvec) p[j] = mm_ld_reduce_bf16x8(pmc + (int64_t)row * a.d + v * 8);
+    }
+  }
+  for (; row < r1; row += warps) {
+    const int64_t base = (int64_t)row * a.d;
+    uint4 res[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int v = lane + 32 * j;
+      if (v < nvec) res[j] = *reinterpret_cast<const uint4*>(residual + base + v * 8);
     }
     float ss = 0.f;
 #pragma unroll
@@ -180,6 +188,14 @@ __global__ void __launch_bounds__(kNvThreads) tp_nvls_ar_rmsnorm_kernel(NvlsArgs
     }
     ss = warp_sum(ss);
     const float rs = rsqrtf(ss / (float)a.d + a.eps);
+    const int nxt = row + warps;  // prefetch: p[] is free once the new residual is in res[]
+    if (nxt < r1) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int v = lane + 32 * j;
+        if (v < nvec) p[j] = mm_ld_reduce_bf16x8(pmc + (int64_t)nxt * a.d + v * 8);
+      }
+    }
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int v = lane + 32 * j;

@@ -581,6 +581,9 @@ class EngineConfig:
     tp_overlap_min_tokens: int = 1024
     tp_overlap_sms: int = 16
     tp_overlap_min_world: int = 4
+    # measure instead of assuming: the first 12 eligible steps alternate split / whole, their device
+    # time per token is compared (medians, agreed across the ranks) and the faster mode is kept
+    tp_overlap_autotune: bool = True
     # speculative decoding: "none" | "ngram" (prompt lookup) | "draft" (draft model ``draft_model``)
     speculative_method: str = "none"
     num_speculative_tokens: int = 4

@@ -110,6 +110,10 @@ class ModelRunner:
         # overlap the other half's compute (0 = never)
         self.split_min_tokens = (cfg.tp_overlap_min_tokens
                                  if cfg.tensor_parallel_size >= max(2, cfg.tp_overlap_min_world) else 0)
+        # split-overlap auto-tuning (CUDA, tensor parallel): alternate split / whole on eligible steps,
+        # then keep the mode with the lower device time per token
+        self.split_auto = bool(self.split_min_tokens) and self.is_cuda and getattr(cfg, "tp_overlap_autotune", False)
+        self._tune = {"n": 0, "pending": [], "decided": None, "cur": None, "ms_per_token": None}
 
     # ------------------------------------------------------------------ batch preparation
     def _fill_host(self, out: SchedulerOutput) -> Tuple[int, int, List[Sequence], List[int]]:
@@ -252,11 +256,66 @@ class ModelRunner:
             raise RuntimeError("step inputs contain unresolved tokens: resolve the in-flight step first")
         if self.timer is not None:
             self.timer.begin()
+        tuning = self.split_auto and self._tune["decided"] is None
+        if tuning:
+            self._tune["cur"] = None
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         try:
             return self._execute(out, n, T, sample_seqs, sample_rows)
         finally:
             if self.timer is not None:
                 self.timer.end()
+            if tuning and self._tune["cur"] is not None:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                self._tune["pending"].append((self._tune["cur"], T, e0, e1))
+                if self._tune["n"] >= self.SPLIT_TUNE_STEPS:
+                    self._tune_decide()
+
+    SPLIT_TUNE_STEPS = 12
+
+    def _split_choice(self, eligible) -> bool:
+        """Whether this (eligible) step runs as two overlapped halves."""
+        if not eligible:
+            return False
+        if not self.split_auto:
+            return True
+        t = self._tune
+        if t["decided"] is not None:
+            return t["decided"]
+        t["cur"] = t["n"] % 2 == 0
+        t["n"] += 1
+        return t["cur"]
+
+    def _tune_decide(self) -> None:
+        """Median device ms per token of the split and the whole tuning steps, summed over the ranks
+        (every rank decides at the same eligible step, so all take the same mode)."""
+        import statistics
+        t = self._tune
+        per = {True: [], False: []}
+        for use, T, e0, e1 in t["pending"]:
+            e1.synchronize()
+            per[use].append(e0.elapsed_time(e1) / max(1, T))
+        med = torch.tensor([statistics.median(per[True]) if per[True] else float("inf"),
+                            statistics.median(per[False]) if per[False] else float("inf")],
+                           dtype=torch.float64, device=self.device)
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(med)
+        t["ms_per_token"] = (float(med[0]), float(med[1]))
+        t["decided"] = bool(med[0] < 0.98 * med[1])
+        t["pending"] = []
+
+    @property
+    def split_overlap_state(self) -> str:
+        """"off", "on", "tuning", or the auto-tuned choice ("auto:on" / "auto:off")."""
+        if not self.split_min_tokens:
+            return "off"
+        if not self.split_auto:
+            return "on"
+        d = self._tune["decided"]
+        return "tuning" if d is None else ("auto:on" if d else "auto:off")
 
     @torch.inference_mode()
     def launch(self, out: SchedulerOutput, prev: Optional[Inflight]) -> Inflight:
@@ -348,8 +407,8 @@ class ModelRunner:
                                                           self.model.Hk, self.model.D).to(dev, non_blocking=True)
         if any(c.seq.mm_positions is not None for c in out.chunks):
             self._mm_meta(out, meta)
-        if (self.split_min_tokens and T >= self.split_min_tokens and self.model.can_split_batch()
-                and not lora_active and all(c.verify == 0 for c in out.chunks)):
+        if self._split_choice(self.split_min_tokens and T >= self.split_min_tokens and self.model.can_split_batch()
+                              and not lora_active and all(c.verify == 0 for c in out.chunks)):
             meta.halves = self._split_halves(n, nd, T, positions, slots, bt, lens)
         ns = len(sample_rows)
         if ns == 0:

@@ -253,7 +253,9 @@ class FusedTPComm(TPComm):
         return slice(0, T)
 
     def _nvls_grid(self, rows: int) -> int:
-        return max(1, min(self.grid * 8, (rows + 7) // 8))  # one warp per row, 8 warps per CTA
+        # one warp per row, 8 warps per CTA, at most one CTA per SM (the kernel keeps one CTA
+        # resident per SM): larger row counts loop, with the next row's reductions prefetched
+        return max(1, min(self.grid, (rows + 7) // 8))
 
     def _nvls_add_rmsnorm(self, T: int, residual: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
         one_shot = T <= self.nvls_one_shot_max
