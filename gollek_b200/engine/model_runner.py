@@ -256,24 +256,30 @@ class ModelRunner:
             raise RuntimeError("step inputs contain unresolved tokens: resolve the in-flight step first")
         if self.timer is not None:
             self.timer.begin()
-        tuning = self.split_auto and self._tune["decided"] is None
-        if tuning:
-            self._tune["cur"] = None
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record()
         try:
-            return self._execute(out, n, T, sample_seqs, sample_rows)
+            return self._timed_execute(out, n, T, sample_seqs, sample_rows)
         finally:
             if self.timer is not None:
                 self.timer.end()
-            if tuning and self._tune["cur"] is not None:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
-                self._tune["pending"].append((self._tune["cur"], T, e0, e1))
-                if self._tune["n"] >= self.SPLIT_TUNE_STEPS:
-                    self._tune_decide()
 
     SPLIT_TUNE_STEPS = 12
+
+    def _timed_execute(self, out, n, T, sample_seqs, sample_rows, **kw):
+        """``_execute``, with the device time of split-overlap tuning steps recorded."""
+        tuning = self.split_auto and self._tune["decided"] is None
+        if not tuning:
+            return self._execute(out, n, T, sample_seqs, sample_rows, **kw)
+        self._tune["cur"] = None
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        res = self._execute(out, n, T, sample_seqs, sample_rows, **kw)
+        if self._tune["cur"] is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self._tune["pending"].append((self._tune["cur"], T, e0, e1))
+            if self._tune["n"] >= self.SPLIT_TUNE_STEPS:
+                self._tune_decide()
+        return res
 
     def _split_choice(self, eligible) -> bool:
         """Whether this (eligible) step runs as two overlapped halves."""
@@ -334,7 +340,7 @@ class ModelRunner:
         if self.timer is not None:
             self.timer.begin()
         try:
-            res = self._execute(out, n, T, sample_seqs, sample_rows, patch=patch, sync=False)
+            res = self._timed_execute(out, n, T, sample_seqs, sample_rows, patch=patch, sync=False)
         finally:
             if self.timer is not None:
                 self.timer.end()
