@@ -594,6 +594,10 @@ class EngineConfig:
     # steps that need host-visible history (penalties, speculative decoding, P/D hand-off) run
     # synchronously
     async_scheduling: bool = True
+    # host garbage collection: with thousands of running sequences every full collection walks all
+    # their token lists (~0.1 s each, every ~10 steps); raise the collection thresholds and freeze
+    # the objects built at start-up so a step's host work stays flat (cycles are still collected)
+    gc_tuning: bool = True
     # weight offload: the last `offload_layers` layers stream from pinned host memory, prefetched
     # `offload_prefetch` layers ahead (for models larger than device memory; disables CUDA graphs)
     offload_layers: int = 0

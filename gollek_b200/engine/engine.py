@@ -35,6 +35,17 @@ def _dtype(name: str) -> torch.dtype:
             "fp32": torch.float32, "float16": torch.float16}[name]
 
 
+def _tune_gc() -> None:
+    """Process-wide: rare full collections, and the start-up objects (weights' metadata, modules)
+    moved out of the collector's scans. Long-lived sequences' token lists would otherwise be walked
+    by every full collection."""
+    import gc
+    t0, t1, t2 = gc.get_threshold()
+    gc.set_threshold(max(t0, 50000), max(t1, 50), max(t2, 100))
+    gc.collect()
+    gc.freeze()
+
+
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, model_cfg: Optional[ModelConfig] = None,
                  weights: Optional[Callable[[str], torch.Tensor]] = None, comm: Optional[TPComm] = None,
@@ -132,6 +143,8 @@ class LLMEngine:
             self.model.enable_ep_all_to_all(cfg.max_num_batched_tokens + cfg.max_num_seqs)
         self.model.split_sms = cfg.tp_overlap_sms
         self.runner = ModelRunner(self.model, cfg, self.kv_cache, self.kv)
+        if getattr(cfg, "gc_tuning", False):
+            _tune_gc()
         if cfg.kv_cache_dtype not in ("auto", cfg.dtype, "fp8", "fp8_e4m3"):
             raise ValueError(f"kv_cache_dtype {cfg.kv_cache_dtype!r}: auto (the model dtype) or fp8 (e4m3)")
         self.evictor = None
