@@ -578,6 +578,21 @@ void tp_nvls_allreduce_py(uint64_t uc, uint64_t mc, int64_t rank, int64_t world,
                            (int)grid, cur_stream());
 }
 
+// Column all-gather of a [B, v] bf16 shard into a [B, ld] buffer at byte offset dst_off of every
+// rank's region; mc != 0 selects the NVLS multicast kernel.
+void tp_gather_cols_py(std::vector<uint64_t> bases, uint64_t mc, int64_t rank, torch::Tensor src, int64_t dst_off,
+                       int64_t ld, double timeout_s, int64_t grid) {
+  check_bf16(src, "src");
+  TORCH_CHECK(src.dim() == 2 && src.stride(1) == 1, "tp column gather: src [B, v] row-major");
+  TORCH_CHECK(rank >= 0 && rank < (int64_t)bases.size(), "tp column gather: bad rank");
+  if (mc != 0)
+    launch_tp_nvls_gather_cols(bases[rank], mc, (int)rank, (int)bases.size(), src.data_ptr(), src.stride(0),
+                               src.size(0), src.size(1), dst_off, ld, timeout_s, (int)grid, cur_stream());
+  else
+    launch_tp_gather_cols(bases, (int)rank, src.data_ptr(), src.stride(0), src.size(0), src.size(1), dst_off, ld,
+                          timeout_s, (int)grid, cur_stream());
+}
+
 // ---------------------------------------------------------------- expert-parallel all-to-all (C3)
 static EpLayout ep_layout_from(const std::vector<int64_t>& v) {
   TORCH_CHECK(v.size() == 8, "EP layout: [flags, counts, recv, meta, comb, x offsets, cap_src, cap_tok]");
@@ -898,6 +913,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_nvls_allreduce_add_rmsnorm", &tp_nvls_ar_rmsnorm_py,
         "fused TP all-reduce + residual add + RMSNorm through NVLS multimem (sequence-parallel residual)");
   m.def("tp_nvls_allreduce", &tp_nvls_allreduce_py, "TP all-reduce through NVLS multimem");
+  m.def("tp_gather_cols", &tp_gather_cols_py,
+        "all-gather of vocab-parallel column shards (P2P stores, or NVLS multicast stores when mc != 0)");
   m.def("moe_route", &moe_route_py, "MoE routing only: physical expert ids and weights per token");
   m.def("ep_ws_ints", &ep_ws_ints);
   m.def("ep_dispatch", &ep_dispatch_py, "EP all-to-all dispatch: rows stored into the expert owners' buffers (P2P)");

@@ -254,6 +254,39 @@ __global__ void __launch_bounds__(kNvThreads) tp_nvls_allreduce_kernel(NvlsArgs 
   nv_leave(a, epoch, !a.one_shot, &s_last);
 }
 
+// All-gather of column shards (vocab-parallel logits): rank r's [B, v] shard is stored once through
+// the multicast address into columns [r*v, (r+1)*v) of the [B, ld] buffer at `dst_off`, so the
+// switch writes it into every rank's copy (each shard byte crosses NVLink once per rank instead of
+// once per peer). Barrier A first (no rank overwrites a buffer a peer may still read), barrier C
+// last (every rank's shard has landed before the caller reads the gathered rows).
+__global__ void __launch_bounds__(kNvThreads) tp_nvls_gather_cols_kernel(NvlsArgs a,
+                                                                         const __nv_bfloat16* __restrict__ src,
+                                                                         int64_t src_stride, int B, int v,
+                                                                         int64_t dst_off, int64_t ld) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_last;
+  const uint32_t epoch = nv_enter(a, &s_epoch);
+  const int vv = v / 8;
+  const int64_t total = (int64_t)B * vv;
+  __nv_bfloat16* dmc = reinterpret_cast<__nv_bfloat16*>(a.mc + dst_off) + (int64_t)a.rank * v;
+  constexpr int kU = 4;  // 16-byte vectors in flight per thread
+  const int64_t stride = (int64_t)gridDim.x * kNvThreads;
+  for (int64_t i0 = (int64_t)blockIdx.x * kNvThreads + threadIdx.x; i0 < total; i0 += kU * stride) {
+    uint4 r[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < total) r[u] = *reinterpret_cast<const uint4*>(src + (i / vv) * src_stride + (i % vv) * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < total) mm_st_16(dmc + (i / vv) * ld + (i % vv) * 8, r[u]);
+    }
+  }
+  nv_leave(a, epoch, true, &s_last);
+}
+
 NvlsArgs make_nvls_args(uint64_t uc, uint64_t mc, int rank, int world, int64_t p0, int64_t p1, int64_t x_off,
                         int parity, bool one_shot, int T, int d, float eps, double timeout_s) {
   throw_if(world < 1 || world > 8, "NVLS collectives: 1..8 ranks");
@@ -311,6 +344,19 @@ void launch_tp_nvls_allreduce(uint64_t uc, uint64_t mc, int rank, int world, int
   NvlsArgs a = make_nvls_args(uc, mc, rank, world, p0, p1, 0, parity, one_shot, 0, 0, 0.f, timeout_s);
   tp_nvls_allreduce_kernel<<<grid, kNvThreads, 0, s>>>(a, numel / 8, reinterpret_cast<__nv_bfloat16*>(out));
   check_launch("tp_nvls_allreduce");
+}
+
+void launch_tp_nvls_gather_cols(uint64_t uc, uint64_t mc, int rank, int world, const void* src, int64_t src_stride,
+                                int B, int v, int64_t dst_off, int64_t ld, double timeout_s, int grid, cudaStream_t s) {
+  throw_if(v % 8 != 0 || src_stride % 8 != 0 || ld % 8 != 0 || dst_off % 16 != 0 ||
+               reinterpret_cast<uintptr_t>(src) % 16 != 0,
+           "NVLS column gather: shard width, strides and offsets must be whole 16-byte vectors");
+  throw_if(ld < (int64_t)world * v, "NVLS column gather: destination row narrower than world * v");
+  if (B == 0) return;
+  NvlsArgs a = make_nvls_args(uc, mc, rank, world, 0, 0, 0, 0, false, 0, 0, 0.f, timeout_s);
+  tp_nvls_gather_cols_kernel<<<grid, kNvThreads, 0, s>>>(a, reinterpret_cast<const __nv_bfloat16*>(src), src_stride,
+                                                         B, v, dst_off, ld);
+  check_launch("tp_nvls_gather_cols");
 }
 
 }  // namespace gollek

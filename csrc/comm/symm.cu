@@ -445,6 +445,71 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(ArArgs a, __nv
   }
 }
 
+// All-gather of column shards over P2P (vocab-parallel logits without NVLS): rank r stores its
+// [B, v] shard into columns [r*v, (r+1)*v) of the [B, ld] buffer at `dst_off` of every rank
+// (plain 16-byte stores over NVLink, 2-byte stores when the shard is not a whole number of
+// vectors). Barrier A first (no rank overwrites a buffer a peer may still read); the last CTA
+// then publishes flag_b and waits for every peer's, so the gathered rows are complete when the
+// kernel ends.
+__global__ void __launch_bounds__(kArThreads) tp_gather_cols_kernel(ArArgs a, const __nv_bfloat16* __restrict__ src,
+                                                                    int64_t src_stride, int B, int v, int64_t dst_off,
+                                                                    int64_t ld, int vec) {
+  SymmHeader* me = reinterpret_cast<SymmHeader*>(a.bases[a.rank]);
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(&me->epoch) + 1;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+    SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[threadIdx.x]);
+    st_release_sys(&peer->flag_a[a.rank], epoch);
+  }
+  if (threadIdx.x < a.world && !wait_geq(&me->flag_a[threadIdx.x], epoch, a.timeout_ns))
+    atomicOr(&me->status, kStatusPeerTimeout);
+  __syncthreads();
+  const int64_t col0 = (int64_t)a.rank * v;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const int vv = v / 8;
+    const int64_t total = (int64_t)B * vv;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+      const int64_t row = i / vv, c = (i % vv) * 8;
+      const uint4 x = *reinterpret_cast<const uint4*>(src + row * src_stride + c);
+#pragma unroll
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.bases[p] + dst_off) + row * ld + col0 + c) = x;
+    }
+  } else {
+    const int64_t total = (int64_t)B * v;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+      const int64_t row = i / v, c = i % v;
+      const __nv_bfloat16 x = src[row * src_stride + c];
+      for (int p = 0; p < a.world; ++p)
+        reinterpret_cast<__nv_bfloat16*>(a.bases[p] + dst_off)[row * ld + col0 + c] = x;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(&me->arrive, 1u);
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x < a.world) {
+    SymmHeader* peer = reinterpret_cast<SymmHeader*>(a.bases[threadIdx.x]);
+    st_release_sys(&peer->flag_b[a.rank], epoch);
+  }
+  if (threadIdx.x < a.world && !wait_geq(&me->flag_b[threadIdx.x], epoch, a.timeout_ns))
+    atomicOr(&me->status, kStatusPeerTimeout);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    me->arrive = 0;
+    me->epoch = epoch;
+  }
+}
+
 // ------------------------------------------------------------------------------- host side
 void* symm_alloc(size_t bytes) {
   void* p = nullptr;
@@ -546,6 +611,18 @@ void launch_tp_argmax(const std::vector<uint64_t>& bases, int rank, const void* 
   tp_argmax_kernel<<<B, kArThreads, 0, s>>>(a, reinterpret_cast<const __nv_bfloat16*>(logits), stride, V,
                                             vocab_offset, B, cand_off, cand_rows, parity, out);
   check_launch("tp_argmax");
+}
+
+void launch_tp_gather_cols(const std::vector<uint64_t>& bases, int rank, const void* src, int64_t src_stride, int B,
+                           int v, int64_t dst_off, int64_t ld, double timeout_s, int grid, cudaStream_t s) {
+  throw_if(ld < (int64_t)bases.size() * v, "tp column gather: destination row narrower than world * v");
+  throw_if(dst_off % 16 != 0, "tp column gather: destination offset must be 16-byte aligned");
+  if (B == 0) return;
+  ArArgs a = make_args(bases, rank, 0, 0, 0, 0, 0, 0, true, 0.f, timeout_s);
+  const bool vec = v % 8 == 0 && src_stride % 8 == 0 && ld % 8 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0;
+  tp_gather_cols_kernel<<<grid, kArThreads, 0, s>>>(a, reinterpret_cast<const __nv_bfloat16*>(src), src_stride, B, v,
+                                                    dst_off, ld, vec ? 1 : 0);
+  check_launch("tp_gather_cols");
 }
 
 uint32_t symm_read_status(void* base) {

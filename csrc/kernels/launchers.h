@@ -219,6 +219,10 @@ void launch_tp_ar_rmsnorm(const std::vector<uint64_t>& bases, int rank, int64_t 
                           float eps, double timeout_s, int grid, cudaStream_t s);
 void launch_tp_allreduce(const std::vector<uint64_t>& bases, int rank, int64_t p0, int64_t p1, int parity, void* out,
                          int64_t numel, double timeout_s, int grid, cudaStream_t s);
+// All-gather of [B, v] column shards into columns [rank*v, (rank+1)*v) of a [B, ld] buffer at
+// `dst_off` in every rank's region (vocab-parallel logits); P2P stores, or NVLS multicast stores.
+void launch_tp_gather_cols(const std::vector<uint64_t>& bases, int rank, const void* src, int64_t src_stride, int B,
+                           int v, int64_t dst_off, int64_t ld, double timeout_s, int grid, cudaStream_t s);
 
 // ---- expert-parallel all-to-all (csrc/comm/ep_a2a.cu); EpLayout in csrc/comm/push.h
 int ep_ws_ints(int world, int e_loc);
@@ -249,5 +253,7 @@ void launch_tp_nvls_ar_rmsnorm(uint64_t uc, uint64_t mc, int rank, int world, in
                                float eps, double timeout_s, int grid, cudaStream_t s);
 void launch_tp_nvls_allreduce(uint64_t uc, uint64_t mc, int rank, int world, int64_t p0, int64_t p1, int parity,
                               bool one_shot, void* out, int64_t numel, double timeout_s, int grid, cudaStream_t s);
+void launch_tp_nvls_gather_cols(uint64_t uc, uint64_t mc, int rank, int world, const void* src, int64_t src_stride,
+                                int B, int v, int64_t dst_off, int64_t ld, double timeout_s, int grid, cudaStream_t s);
 
 }  // namespace gollek

@@ -125,6 +125,9 @@ class TPComm:
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
         return t
 
+    def reserve_logits(self, v_local: int) -> None:
+        """Set up the buffers of the vocab-parallel logits gather (collective where it allocates)."""
+
     def argmax_last(self, t: torch.Tensor, vocab_offset: int) -> torch.Tensor:
         """Greedy token ids from vocab-parallel logit shards (ties: lowest token id)."""
         return ops.argmax(t)

@@ -3,13 +3,14 @@
 Run by every rank (one process per GPU) before a multi-GPU benchmark, and by the multi-GPU tests:
 
 * ``collectives_check`` — the fused all-reduce + residual + RMSNorm (one-shot and two-shot sizes,
-  consecutive calls so buffer parities and epochs advance), the plain all-reduce and the
-  vocab-parallel argmax, each against the fp32 result computed from every rank's inputs
+  consecutive calls so buffer parities and epochs advance), the plain all-reduce, the
+  vocab-parallel argmax and the vocab-parallel logits gather, each against the fp32 result computed from every rank's inputs
   (gathered in fp32 over the process group and summed in rank order).
 * ``engine_check`` — a two-layer slice of the Llama-3-8B shape (or of Mixtral with its experts
   partitioned over the ranks) served by the TP engine (chunked prefill with a two-shot-sized
   step, then batched decode) whose greedy tokens are checked against the dense fp32 oracle: every
-  chosen token's oracle logit, given the same history, must be within ``tol`` of the maximum.
+  chosen token's oracle logit, given the same history, must be within ``tol`` of the maximum;
+  seeded top-k / top-p requests must draw the same tokens on every rank.
 
 Both return plain dicts (JSON-ready) with the worst errors and an ``ok`` verdict that is the
 same on every rank.
@@ -73,11 +74,30 @@ def collectives_check(comm, sizes=(1, 7, 64, 129, 300, 1024), vocab: int = 32000
         dist.all_gather(full, shard)
         ref_ids = torch.cat(full, dim=1).float().argmax(-1)
         bad_argmax += int((ids != ref_ids).sum())
+    # vocab-parallel logits gather: bit-exact against the process group's all-gather; row counts past
+    # one buffer (chunked), fp32 shards (moved as bf16 units) and a shard width that is not a whole
+    # number of 16-byte vectors (2-byte stores)
+    bad_gather = 0
+    comm.reserve_logits(vocab // world)
+    per = getattr(comm, "lg_cap", 0) // (vocab // world * world * 2)
+    cases = [(1, vocab // world, torch.bfloat16), (37, vocab // world, torch.bfloat16),
+             (min(256, comm.max_tokens), vocab // world, torch.bfloat16), (5, vocab // world, torch.float32),
+             (3, 1001, torch.bfloat16)]
+    if per:
+        cases.append((per + 3, vocab // world, torch.bfloat16))
+    for B, v, dt in cases:
+        g = torch.Generator(device=dev).manual_seed(seed + 131 * B + v + rank)
+        shard = torch.randn(B, v, device=dev, generator=g).to(dt)
+        got = comm.all_gather_last(shard).clone()
+        full = [torch.empty_like(shard) for _ in range(world)]
+        dist.all_gather(full, shard)
+        bad_gather += int((got != torch.cat(full, dim=1)).sum())
     comm.check()
     torch.cuda.synchronize()
-    ok = worst_x < 0.02 and worst_r < 0.02 and worst_ar < 0.02 and bad_argmax == 0
+    ok = worst_x < 0.02 and worst_r < 0.02 and worst_ar < 0.02 and bad_argmax == 0 and bad_gather == 0
     return {"max_rel_err_x": round(worst_x, 6), "max_rel_err_residual": round(worst_r, 6),
             "max_rel_err_allreduce": round(worst_ar, 6), "argmax_mismatches": bad_argmax,
+            "logits_gather_mismatches": bad_gather,
             "nvls": bool(getattr(comm, "nvls", False)), "ok": _agree(ok, dev)}
 
 
@@ -114,6 +134,16 @@ def engine_check(comm_factory, layers: int = 2, vocab: int = 32000, new_tokens: 
     if ep_a2a:
         eng.model.ep_a2a.check()
     toks = [o.output_token_ids for o in outs]
+    # sampled requests (the vocab shards gathered, then the same seeded draw on every rank)
+    souts = eng.generate(prompts, SamplingParams(temperature=0.8, top_k=40, top_p=0.9, seed=11,
+                                                 max_tokens=new_tokens, ignore_eos=True))
+    if hasattr(comm, "check"):
+        comm.check()
+    stoks = [t for o in souts for t in o.output_token_ids]
+    sflat = torch.tensor(stoks, dtype=torch.int64, device=dev)
+    sall = [torch.empty_like(sflat) for _ in range(world)]
+    dist.all_gather(sall, sflat)
+    sampled_same = all(bool((a == sflat).all()) for a in sall) and len(stoks) == new_tokens * len(prompts)
     # every rank must hold the same tokens
     flat = torch.tensor([t for ts in toks for t in ts], dtype=torch.int64, device=dev)
     allt = [torch.empty_like(flat) for _ in range(world)]
@@ -130,9 +160,9 @@ def engine_check(comm_factory, layers: int = 2, vocab: int = 32000, new_tokens: 
         near = worst_gap_frac <= tol_frac
     res = torch.tensor([worst_gap_frac], device=dev)
     dist.broadcast(res, 0)
-    ok = _agree(same and (near if rank == 0 else True), dev)
+    ok = _agree(same and sampled_same and (near if rank == 0 else True), dev)
     del eng
     torch.cuda.empty_cache()
     return {"model": model, "layers": layers, "prompt_lens": list(prompt_lens), "new_tokens": new_tokens,
             "expert_parallel": expert_parallel, "ep_all_to_all": ep_a2a,
-            "ranks_agree": same, "max_logit_gap_over_std": round(float(res.item()), 5), "ok": ok}
+            "ranks_agree": same, "sampled_ranks_agree": sampled_same, "max_logit_gap_over_std": round(float(res.item()), 5), "ok": ok}

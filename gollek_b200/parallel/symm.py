@@ -132,7 +132,7 @@ class SymmHeap:
 
 
 class FusedTPComm(TPComm):
-    """Tensor-parallel collectives on the symmetric heap (own kernels), NCCL only for the logits gather."""
+    """Tensor-parallel collectives on the symmetric heap (own kernels, no NCCL on the step's path)."""
 
     fused_ar = True
 
@@ -178,6 +178,8 @@ class FusedTPComm(TPComm):
         self.timeout_s = timeout_s
         self.one_shot_max_tokens = one_shot_max_tokens
         self.calls = 0
+        self.lg_heap: Optional[SymmHeap] = None  # vocab-parallel logits gather (reserve_logits)
+        self.lg_cap, self.lg_off, self.lg_calls = 0, [0, 0], 0
         self.grid = grid or torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
         if size > 1:
             dist.barrier(group=cpu_group)
@@ -360,17 +362,60 @@ class FusedTPComm(TPComm):
         self.calls += 1
         return out
 
+    def reserve_logits(self, v_local: int, rows: int = 0) -> None:
+        """Symmetric buffers for the vocab-parallel logits gather: two [rows, world * v_local] bf16
+        buffers in a second heap (own barrier counters). Collective: every rank calls it at the same
+        point of its collective sequence; the first sampled (non-greedy) step does, so greedy-only
+        serving never allocates them."""
+        if self.size == 1 or self.lg_heap is not None:
+            return
+        rows = rows or int(os.environ.get("GOLLEK_TP_LOGITS_ROWS", min(self.max_tokens, 256)))
+        self.lg_cap = (rows * self.size * v_local * 2 + 4095) // 4096 * 4096
+        self.lg_off = [HEADER_BYTES, HEADER_BYTES + self.lg_cap]
+        self.lg_heap = SymmHeap(HEADER_BYTES + 2 * self.lg_cap, self.rank, self.size, group=self.cpu_group,
+                                multicast=self.nvls, pg=self.pg)
+
     def all_gather_last(self, t: torch.Tensor) -> torch.Tensor:
+        """[B, v] vocab shards → [B, world * v] with the column-gather kernel (NVLS multicast stores,
+        or P2P stores). Rows that fit one buffer come back as a view of the symmetric buffer, valid
+        until the second-next gather (the caller consumes them within the step); more rows are
+        gathered in chunks into a fresh tensor. Any dtype is moved as its bf16-sized units."""
         if self.size == 1:
             return t
+        if self.lg_heap is None:
+            self.reserve_logits(t.shape[1] * t.element_size() // 2)
         B, v = t.shape
-        buf = torch.empty(self.size, B, v, dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(buf, t.contiguous())
-        return buf.permute(1, 0, 2).reshape(B, self.size * v)
+        src = t.contiguous()
+        units = src if src.dtype == torch.bfloat16 else src.view(torch.bfloat16)
+        vu = units.shape[1]
+        ld = vu * self.size
+        per = self.lg_cap // (ld * 2)
+        if per < 1:
+            raise ValueError(f"logits row of {ld} units exceeds the gather buffer")
+        ext = cuda_ext()
+        nvls = self.lg_heap.mc != 0 and vu % 8 == 0
+        out = None if B <= per else torch.empty(B, ld, dtype=torch.bfloat16, device=t.device)
+        res = None
+        for r0 in range(0, B, per):
+            n = min(per, B - r0)
+            parity = self.lg_calls % 2
+            vec = n * vu // 8
+            grid = (max(1, min(2 * self.grid, (vec + 1023) // 1024)) if nvls
+                    else max(1, min(self.grid, (vec + 2047) // 2048)))
+            ext.tp_gather_cols(self.lg_heap.bases, self.lg_heap.mc if nvls else 0, self.rank, units[r0:r0 + n],
+                               self.lg_off[parity], ld, self.timeout_s, grid)
+            self.lg_calls += 1
+            view = self.lg_heap.view(self.lg_off[parity], (n, ld))
+            if out is None:
+                res = view
+            else:
+                out[r0:r0 + n].copy_(view)
+        res = res if out is None else out
+        return res if t.dtype == torch.bfloat16 else res.view(t.dtype)
 
     def check(self) -> None:
         """Raise if a device-side wait timed out (a peer missed a barrier)."""
-        st = self.heap.status()
+        st = self.heap.status() | (self.lg_heap.status() if self.lg_heap is not None else 0)
         if st:
             raise RuntimeError(f"tensor-parallel collective failed on rank {self.rank}: status 0x{st:x} "
                                f"(a peer did not reach the barrier within {self.timeout_s} s)")
