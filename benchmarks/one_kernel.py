@@ -8,6 +8,7 @@
     python benchmarks/one_kernel.py decode_fp8 --B 64 --ctx 4096  (decode over an fp8 e4m3 KV cache)
     python benchmarks/one_kernel.py q6k --M 1 --N 28672 --K 4096  (Q6_K decode GEMV)
     python benchmarks/one_kernel.py fp8gemm --M 64 --N 1280 --K 8192 (block-scaled fp8 GEMM)
+    python benchmarks/one_kernel.py norm --M 1344 --K 4096 --residual (residual add + RMSNorm)
 The last three also print a CUDA-event time (the repetitions captured as one CUDA graph, so host
 launch cost is excluded) and the achieved fraction of the measured HBM copy bandwidth or sustained
 bf16 peak (fp8 GEMM: of twice it, the nominal fp8/bf16 ratio). Weights smaller than 256 MB are
@@ -35,7 +36,8 @@ def _n_copies(weight_bytes: int) -> int:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("kind", choices=["gemm", "decode", "prefill", "moe", "moe_ds", "gdn", "decode_fp8",
-                                     "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope"])
+                                     "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope",
+                                     "norm"])
     ap.add_argument("--T", type=int, default=256)
     ap.add_argument("--e-loc", type=int, default=8)
     ap.add_argument("--M", type=int, default=8192)
@@ -102,7 +104,7 @@ def main():
         qs = torch.arange(0, T + 1, a.L, dtype=torch.int32, device=dev)
         for _ in range(a.reps):
             ops.gdn_scan(proj, state, slots, reset, qs, torch.zeros(Hg, device=dev), torch.zeros(Hg, device=dev), Hg)
-    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope"):
+    elif a.kind in ("decode_fp8", "decode_bf16", "q6k", "q4k", "int4", "fp8gemm", "gemm_bf16", "qkv_rope", "norm"):
         # measured copy bandwidth, sustained and burst bf16 GEMM peaks
         HBM_GBS, BF16_TFLOPS, BF16_BURST = 6534.5, 1400.9, 1672.7
         if a.kind == "qkv_rope":
@@ -127,6 +129,24 @@ def main():
                 ops.linear_rope_kv(x, wi, pos, cos_sin, cache, slots, H, Hk, D)
             nbytes = w.numel() * 2 + a.M * a.K * 2
             flops = 2.0 * a.M * w.shape[0] * a.K
+        elif a.kind == "norm":
+            # residual += x; out = RMSNorm(residual) * w for M rows of width K (--residual: fused add)
+            n = _n_copies(a.M * a.K * 2 * (2 if a.residual else 1))
+            xs = [torch.randn(a.M, a.K, device=dev).bfloat16() for _ in range(n)]
+            rs = [torch.randn(a.M, a.K, device=dev).bfloat16() for _ in range(n)] if a.residual else None
+            wn = torch.rand(a.K, device=dev).bfloat16()
+            outs = [torch.empty(a.M, a.K, device=dev, dtype=torch.bfloat16) for _ in range(n)]
+            turn = [0]
+
+            def fn():
+                i = turn[0] % n
+                turn[0] += 1
+                if a.residual:
+                    ops.fused_add_rms_norm(xs[i], rs[i], wn, 1e-5, out=outs[i])
+                else:
+                    ops.rms_norm(xs[i], wn, 1e-5, out=outs[i])
+            nbytes = a.M * a.K * 2 * (4 if a.residual else 2)
+            flops = None
         elif a.kind == "gemm_bf16":
             # --swiglu: gate/up with the fused SwiGLU epilogue (N = 2 x FFN); --residual: + residual
             w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()

@@ -64,6 +64,13 @@ def collectives_check(comm, sizes=(1, 7, 64, 129, 300, 1024), vocab: int = 32000
         ref = _gather_sum_fp32(t, world)
         out = comm.all_reduce(t).float()
         worst_ar = max(worst_ar, float(((out - ref).abs() / (1 + ref.abs())).max()))
+    # sizes that are not whole hidden-width rows, and one past the partial buffer (chunked)
+    for n in (8 * 1001, comm.max_tokens * d + 8 * 999):
+        g = torch.Generator(device=dev).manual_seed(seed + n + rank)
+        t = torch.randn(n, device=dev, generator=g).bfloat16()
+        ref = _gather_sum_fp32(t, world)
+        out = comm.all_reduce(t).float()
+        worst_ar = max(worst_ar, float(((out - ref).abs() / (1 + ref.abs())).max()))
     for B in (1, 37, min(256, comm.max_tokens)):
         g = torch.Generator(device=dev).manual_seed(seed + 77 * B + rank)
         shard = torch.randn(B, vocab // world, device=dev, generator=g).bfloat16()

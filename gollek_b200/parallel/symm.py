@@ -347,8 +347,32 @@ class FusedTPComm(TPComm):
                                     t, self.timeout_s, self.grid)
             self.calls += 1
             return t
+        if t.dtype == torch.bfloat16 and n % 8 == 0 and t.is_cuda:
+            # any other bf16 size: chunks of the partial buffer's capacity, one-shot kernels in place
+            work = flat if t.is_contiguous() else flat.clone()
+            cap = self.max_tokens * self.hidden // 8 * 8
+            for c0 in range(0, n, cap):
+                self._all_reduce_flat(work[c0:c0 + cap])
+            if work.data_ptr() != t.data_ptr():
+                t.copy_(work.view(t.shape))
+            return t
+        # other dtypes (fp32 statistics such as expert loads) never occur on the step path
         dist.all_reduce(t)
         return t
+
+    def _all_reduce_flat(self, c: torch.Tensor) -> None:
+        """In-place sum over ranks of a contiguous bf16 vector of at most the partial buffer's size."""
+        m = c.numel()
+        parity = self.calls % 2
+        self.heap.view(self.off_p[parity], (m,)).copy_(c)
+        if self.nvls:
+            grid = max(1, min(self.grid * 4, (m // 8 + 1023) // 1024))
+            cuda_ext().tp_nvls_allreduce(self.heap.bases[self.rank], self.heap.mc, self.rank, self.size,
+                                         self.off_p[0], self.off_p[1], parity, True, m, c, self.timeout_s, grid)
+        else:
+            cuda_ext().tp_allreduce(self.heap.bases, self.rank, self.off_p[0], self.off_p[1], parity, c,
+                                    self.timeout_s, self.grid)
+        self.calls += 1
 
     def argmax_last(self, t: torch.Tensor, vocab_offset: int) -> torch.Tensor:
         """C5: greedy ids from the vocab shards; per row one (logit, id) candidate per rank crosses

@@ -19,7 +19,9 @@ def bf(x):
     return x.to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("T,d", [(1, 256), (7, 4096), (33, 8192), (5, 1024)])
+@pytest.mark.parametrize("T,d", [(1, 256), (7, 4096), (33, 8192), (5, 1024),
+                                 # warp-per-row kernel (T >= 512), 4 / 8 / 16 vectors per lane, ragged d
+                                 (1344, 4096), (515, 2048), (600, 1000), (700, 8192)])
 def test_rms_norm(T, d):
     x = bf(torch.randn(T, d, device=DEV, generator=_g(1)))
     w = bf(torch.randn(d, device=DEV, generator=_g(2)))
@@ -33,7 +35,7 @@ def test_rms_norm(T, d):
     torch.testing.assert_close(y.float(), yr.float(), rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("T,d", [(3, 256), (64, 4096), (5, 8192)])
+@pytest.mark.parametrize("T,d", [(3, 256), (64, 4096), (5, 8192), (1100, 4096)])
 def test_layer_norm(T, d):
     """K1 with center: bias-free LayerNorm (Cohere), plain and fused with the residual add."""
     x = bf(torch.randn(T, d, device=DEV, generator=_g(4)) + 0.5)
