@@ -5,7 +5,7 @@ Every number: median of CUDA-event timings on the launching stream after warm-up
 peaks in MEASURED_PEAKS.json (HBM copy GB/s, cuBLAS bf16 TFLOP/s burst). cuBLAS (torch.matmul)
 timings are printed beside our GEMMs as a reference point only.
 
-    python benchmarks/kernel_bench.py [--only gemm,attn,norm,gdn] [--json out.jsonl]
+    python benchmarks/kernel_bench.py [--only gemm,attn,prefill,norm,gdn] [--json out.jsonl]
 """
 from __future__ import annotations
 
@@ -80,9 +80,9 @@ def main():
                 bn = ops.cuda_ext().gemm_pick_bn(M, N, 2 if sw else 0)
                 rec(f"gemm_{name}_M{M}", ms, flops, nbytes, {"shape": [M, N, K], "bn": bn,
                                                               "cublas_ms": round(cub, 4)})
-    if "attn" in only:
+    if "attn" in only or "prefill" in only:
         Hq, Hk, D, bs = 32, 8, 128, 16
-        for B, ctx in ((256, 1200), (64, 4096), (8, 2048), (1, 8192)):
+        for B, ctx in ((256, 1200), (64, 4096), (8, 2048), (1, 8192)) if "attn" in only else ():
             nblk = (ctx + bs - 1) // bs
             NB = B * nblk
             cache = torch.randn(NB, 2, Hk, bs, D, device=dev).bfloat16()
@@ -97,7 +97,7 @@ def main():
             nbytes = B * ctx * Hk * D * 2 * 2
             flops = 4.0 * B * ctx * Hq * D
             rec(f"attn_decode_B{B}_ctx{ctx}", ms, flops, nbytes, {"splits": splits})
-        for nseq, L in ((4, 2048), (8, 1024), (1, 8192)):
+        for nseq, L in ((4, 2048), (8, 1024), (1, 8192), (1, 1088), (2, 1024)):
             T = nseq * L
             nblk = L // bs
             NB = nseq * nblk
@@ -111,6 +111,9 @@ def main():
             nbytes = 2.0 * (2 * T * Hq * D + 2 * T * Hk * D)
             work = ops.prefill_schedule(qs.tolist(), sl.tolist(), Hq, Hk, D).to(dev)
             variants = [(f"tcgen05_emu{e}", work, True, e) for e in (0, 1, 2)]
+            for form in ("pairs", "rows"):  # both work-item forms, whichever the schedule picked
+                wf = ops.prefill_schedule(qs.tolist(), sl.tolist(), Hq, Hk, D, form=form).to(dev)
+                variants.append((f"tcgen05_{form}", wf, True, ops.PREFILL_EMU))
             variants += [("tcgen05_1tile", ops.prefill_tiles(qs.tolist(), 128).to(dev), True, 0),
                          ("mmasync", ops.prefill_tiles(qs.tolist(), 64).to(dev), False, 0)]
             for name, tiles, tc, emu in variants:

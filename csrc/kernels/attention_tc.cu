@@ -354,8 +354,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------------------------
 // Two-tile prefill kernel (the serving default for head_dim 128).
 //
-// One CTA = two 128-row query tiles ("slots") that read the same KV tiles: two query heads of one
-// GQA group over the same rows (group size even), or two consecutive row tiles of one head.
+// One CTA = one work item = two 128-row query tiles ("slots") that read the same KV tiles: two query
+// heads of one GQA group over the same rows (group size even), or two consecutive row tiles of one
+// head. Head pairs share each K/V tile between two heads and are the host's default where the group
+// size allows. The grid is one CTA per item, heaviest items first.
 // 10 warps:
 //   warps 0-3  softmax of slot 0, warps 4-7 softmax of slot 1 (one query row per thread = TMEM lane)
 //   warp 8     TMA: both Q tiles once, then K and V of each 128-key tile (16-token paged boxes) into a
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     prefill_fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
-                      const int4* __restrict__ work, int pair_heads, int H, int Hk, float scale_log2,
+                      const int4* __restrict__ work, int H, int Hk, float scale_log2,
                       uint32_t* status, int window, float softcap_log2, int num_blocks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -430,8 +432,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int4 wk = work[blockIdx.y];
+  const int4 wk = work[blockIdx.x];
   const int b = wk.x;
+  const int pair_heads = wk.w >> 16, hbase = wk.w & 0xffff;
   const int qs = query_start[b], qlen = query_start[b + 1] - qs;
   const int L = seq_lens[b];
   const int ctx0 = L - qlen;
@@ -439,7 +442,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     FaSlot& t = sl[i];
-    t.h = pair_heads ? 2 * blockIdx.x + i : blockIdx.x;
+    t.h = pair_heads ? hbase + i : hbase;
     t.q_off = pair_heads ? wk.y : (i == 0 ? wk.y : wk.z);
     const bool valid = t.q_off >= 0 && t.q_off < qlen;
     t.rows = valid ? min(kTQ, qlen - t.q_off) : 0;
@@ -779,15 +782,13 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
                              float scale, int window, float softcap, int emu, cudaStream_t s) {
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(q_stride % 8 != 0, "prefill: q row pitch must keep 16-byte alignment");
-  throw_if(nwork > 65535, "prefill: too many query tiles in one launch");
   if (nwork == 0) return;
-  const bool pair_heads = prefill_pairs_heads(H, Hk);
   const uint64_t kv_rows = (uint64_t)num_blocks * 2 * Hk * kBS;
   CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, (uint64_t)H * kD, q_stride, kTQ, 64,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tkv = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, kBS, 64,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
-  dim3 grid(pair_heads ? H / 2 : H, nwork);
+  dim3 grid(nwork);
   const float sl2 = scale * 1.4426950408889634f, cap = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   auto* w4 = reinterpret_cast<const int4*>(work);
@@ -796,7 +797,7 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
     GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(prefill_fa_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                            kFaSmem));                                                              \
     prefill_fa_kernel<E><<<grid, kFaThreads, kFaSmem, s>>>(tq, tkv, o, out_stride, block_tables, bt_stride,        \
-                                                           seq_lens, query_start, w4, pair_heads ? 1 : 0, H, Hk,   \
+                                                           seq_lens, query_start, w4, H, Hk,                       \
                                                            sl2, bounds_status(), window, cap, num_blocks);         \
   } while (0)
   if (emu == 2)

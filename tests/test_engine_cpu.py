@@ -82,3 +82,41 @@ def test_mixtral_engine_matches_oracle():
     eng = _engine(cfg, w)
     out = eng.generate([prompt], SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))[0]
     assert out.output_token_ids == ref_tokens
+
+
+def test_prefill_schedule_forms_cover_every_tile_once():
+    """The prefill work list covers every (head, 128-row query tile) exactly once in both forms,
+    heaviest items first; row-tile pairs are consecutive tiles; head pairs are the default when the
+    GQA group size is even."""
+    from gollek_b200 import ops
+    qs, lens = [0, 300, 560, 561, 690, 1330], [300, 1260, 8, 329, 640]
+    for H, Hk in ((32, 8), (28, 4), (12, 4)):
+        for form in (None, "rows", "pairs"):
+            if form == "pairs" and (H // Hk) % 2:
+                continue
+            w = ops.prefill_schedule(qs, lens, H, Hk, 128, form=form)
+            seen = []
+            costs = []
+            for b, o0, o1, code in w.tolist():
+                pair, h = code >> 16, code & 0xFFFF
+                ctx0 = lens[b] - (qs[b + 1] - qs[b])
+                c = lambda o: (min(lens[b], ctx0 + o + 128) + 127) // 128  # noqa: E731
+                if pair:
+                    assert o0 == o1 and h % 2 == 0
+                    seen += [(b, o0, h), (b, o0, h + 1)]
+                    costs.append(2 * c(o0))
+                else:
+                    seen.append((b, o0, h))
+                    costs.append(max(c(o0), c(o1) if o1 >= 0 else 0))
+                    if o1 >= 0:
+                        assert o1 == o0 + 128
+                        seen.append((b, o1, h))
+            want = [(b, o, h) for b in range(5) for o in range(0, qs[b + 1] - qs[b], 128) for h in range(H)]
+            assert sorted(seen) == sorted(want), (H, Hk, form)
+            assert costs == sorted(costs, reverse=True)
+    one = ops.prefill_schedule([0, 1088], [1088], 32, 8, 128, form="rows")
+    assert (one[:, 3] >> 16 == 0).all() and one.shape[0] == 32 * 5
+    assert sorted({(o0, o1) for _, o0, o1, _ in one.tolist()}) == [(0, 128), (256, 384), (512, 640), (768, 896),
+                                                                 (1024, -1)]
+    many = ops.prefill_schedule(list(range(0, 8 * 1024 + 1, 1024)), [1024] * 8, 32, 8, 128)
+    assert (many[:, 3] >> 16 == 1).all() and many.shape[0] == 8 * 8 * 16

@@ -134,11 +134,13 @@ def test_prefill_two_tile_kernel(H, Hk, emu, qscale):
     q = bf(torch.randn(qs[-1], H, D, device=DEV, generator=_g(24)) * qscale)
     qsl = torch.tensor(qs, dtype=torch.int32, device=DEV)
     scale = 1 / math.sqrt(D)
-    work = ops.prefill_schedule(qs, lens, H, Hk, D).to(DEV)
-    assert work.shape[1] == 4
-    out = ops.paged_prefill_attention(q, cache, bt, sl, qsl, scale, tiles=work, emu=emu)
     ref = R.paged_attention(q.float().cpu(), cache.float().cpu(), bt.cpu(), sl.cpu(), qsl.cpu(), scale)
-    torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2)
+    forms = [None, "rows"] + (["pairs"] if (H // Hk) % 2 == 0 else [])
+    for form in forms:  # the schedule's own choice, then each work-item form
+        work = ops.prefill_schedule(qs, lens, H, Hk, D, form=form).to(DEV)
+        assert work.shape[1] == 4
+        out = ops.paged_prefill_attention(q, cache, bt, sl, qsl, scale, tiles=work, emu=emu)
+        torch.testing.assert_close(out.float().cpu(), ref, rtol=2e-2, atol=2e-2, msg=lambda m: f"{form}: {m}")
 
 
 @pytest.mark.parametrize("H,Hk", [(32, 8), (4, 1), (64, 8), (8, 8)])
