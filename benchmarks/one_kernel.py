@@ -44,6 +44,7 @@ def main():
     ap.add_argument("--N", type=int, default=28672)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--bn", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=1, help="gemm_bf16: split-K factor (with --bn or the planned width)")
     ap.add_argument("--swiglu", action="store_true")
     ap.add_argument("--residual", action="store_true")
     ap.add_argument("--B", type=int, default=256)
@@ -155,10 +156,22 @@ def main():
             res = torch.randn(a.M, a.N, device=dev).bfloat16() if a.residual else None
             turn = [0]
 
-            def fn():
-                wi = copies[turn[0] % len(copies)]
-                turn[0] += 1
-                ops.linear_swiglu(x, wi) if a.swiglu else ops.linear(x, wi, residual=res)
+            if a.splits > 1 or a.bn:  # an explicit tile width / split-K factor (fp32 partials + reduce)
+                from gollek_b200.native import cuda_ext
+                epi = ops.EPI_SWIGLU if a.swiglu else (ops.EPI_RESIDUAL if a.residual else ops.EPI_NONE)
+                yo = torch.empty(a.M, a.N // 2 if a.swiglu else a.N, device=dev, dtype=torch.bfloat16)
+                ws = torch.empty(max(1, a.splits) * a.M * a.N, device=dev) if a.splits > 1 else None
+                bn = a.bn or ops.gemm_plan(a.M, a.N, a.K, epi)[0]
+
+                def fn():
+                    wi = copies[turn[0] % len(copies)]
+                    turn[0] += 1
+                    cuda_ext().gemm_bf16(yo, x, wi, res, epi, bn, None, 0, max(1, a.splits), ws)
+            else:
+                def fn():
+                    wi = copies[turn[0] % len(copies)]
+                    turn[0] += 1
+                    ops.linear_swiglu(x, wi) if a.swiglu else ops.linear(x, wi, residual=res)
             nbytes = a.N * a.K * 2 + a.M * a.K * 2
             flops = 2.0 * a.M * a.N * a.K
         elif a.kind == "decode_bf16":

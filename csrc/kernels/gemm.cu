@@ -586,20 +586,33 @@ int gemm_pick_bn(int M, int N, int epi) {
   return 64;
 }
 
-// Tile width and split-K factor for one GEMM. Small-M (decode) GEMMs use wide tiles (fewer
-// re-reads of A) and split K across CTAs so every SM streams part of the weight matrix.
+// Tile width and split-K factor for one GEMM.
+//
+// Decode-sized M (one or two 128-row tiles) with a narrow output (o_proj / down_proj, N = 4096):
+// without a split the GEMM has too few output tiles to occupy the GPU (64 tiles of 64 columns on 148
+// SMs), and each CTA streams its weight slice plus the whole activation from L2 alone. 128-wide
+// tiles split along K into s = floor(SMs / tiles) parts (one wave, fp32 partials summed with the
+// epilogue by a reduce pass) let every SM stream 1/s of the K range. Measured on B200 (M = 64 / 128 /
+// 256): o_proj 4096 x 4096 0.0179 / 0.0191 / 0.0199 -> 0.0129 / 0.0144 / 0.0165 ms, down_proj
+// 4096 x 14336 0.0462 / 0.0477 / 0.0491 -> 0.0276 / 0.0298 / 0.0375 ms. The qkv output (6144 wide,
+// K = 4096) lost with a split (M = 128: 0.0168 -> 0.0187 ms: the fp32 partials cost more than the
+// idle SMs), so outputs wider than 4096 split only for K >= 8192; gate/up (gated) and RoPE
+// epilogues never split.
 void gemm_plan(int M, int N, int K, int epi, int& bn, int& splits) {
   const int num_m = (M + 127) / 128;
   const int sms = num_sms();
-  const int num_kb = (K + 63) / 64;
-  // Measured at Llama-3-8B decode shapes (M = 64..256): wide tiles + split-K (fp32 partials and a
-  // reduce pass) lost to narrow tiles without split, so split-K is opt-in (explicit splits > 1).
-  (void)K;
-  (void)num_kb;
-  (void)sms;
-  (void)num_m;
   splits = 1;
-  if (bn == 0) bn = gemm_pick_bn(M, N, epi);
+  if (bn == 0) {
+    bn = gemm_pick_bn(M, N, epi);
+    if ((epi == kEpiNone || epi == kEpiResidual) && num_m <= 2 && N % 128 == 0) {
+      const int tiles = num_m * (N / 128);
+      const int s = std::min(8, sms / std::max(1, tiles));
+      if (2 * tiles <= sms && s >= 2 && K / s >= 1024 && (N <= 4096 || K >= 8192)) {
+        bn = 128;
+        splits = s;
+      }
+    }
+  }
   if (epi_wide(epi) && bn < 128) bn = 128;
 }
 

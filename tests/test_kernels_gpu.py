@@ -269,13 +269,21 @@ def test_gemm_split_k(epi, splits):
     torch.testing.assert_close(out.float(), y, rtol=2e-2, atol=3e-2)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 4096, 14336), (64, 6144, 4096), (256, 28672, 4096)])
-def test_gemm_auto_plan_decode_shapes(M, N, K):
+@pytest.mark.parametrize("M,N,K", [(256, 4096, 14336), (64, 6144, 4096), (256, 28672, 4096), (64, 4096, 14336),
+                                   (128, 4096, 4096), (1, 4096, 4096), (200, 4096, 4096)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_gemm_auto_plan_decode_shapes(M, N, K, residual):
+    """The planned tile width / split-K factor at decode sizes (narrow outputs split K over the SMs,
+    partials summed with the residual epilogue) against the fp32 oracle."""
     a = bf(torch.randn(M, K, device=DEV, generator=_g(33)) * 0.5)
     w = bf(torch.randn(N, K, device=DEV, generator=_g(34)) * 0.02)
-    bn, splits = ops.gemm_plan(M, N, K)
-    y = ops.linear(a, w)
-    torch.testing.assert_close(y.float(), a.float() @ w.float().t(), rtol=2e-2, atol=3e-2)
+    r = bf(torch.randn(M, N, device=DEV, generator=_g(35))) if residual else None
+    bn, splits = ops.gemm_plan(M, N, K, ops.EPI_RESIDUAL if residual else ops.EPI_NONE)
+    if N == 4096 and M <= 256 and K >= 4096:
+        assert splits >= 2 and bn == 128, (bn, splits)
+    y = ops.linear(a, w, residual=r)
+    ref = a.float() @ w.float().t() + (r.float() if residual else 0)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=3e-2)
 
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8, 16])
