@@ -13,9 +13,11 @@
 // Block layouts: ggml spec (see csrc/host/gguf_quant.cpp); the reference decodes these only on
 // the CPU (runner/gguf/gollek-gguf-loader/…/gguf/quant/Dequantizer.java, GGUFVectorOps.java:73-88).
 #include "../common/common.cuh"
+#include "../common/tma_host.h"
 #include "launchers.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 using namespace gollek;
 
@@ -64,19 +66,70 @@ GOLLEK_DEVICE void q4k_decode8_regs(const uint4 hdr, const uint2 q, int lane, fl
   }
 }
 
+// The GEMV's form of the same decode, without an integer-to-float conversion per weight. The 8
+// nibbles n_e become f_e = 1 + n_e / 16 by placing each nibble in the mantissa of 1.0f (one byte
+// permute per weight), and the lane's dot product with x over its 8 weights is
+//   sum_e (a n_e - b) x_e = 16 a sum_e f_e x_e - (16 a + b) sum_e x_e,
+// so a row costs one FMA per weight; sum_e x_e is shared by every row of the warp. a16 = 16 a and
+// c = 16 a + b come from the sub-block's scale and min.
+// Conversions on the ALU / FMA pipes instead of the conversion unit (measured at 87 % busy when every
+// lane converted its block's scales with F2F / I2F): a half's sign, exponent and mantissa moved into
+// float position and scaled by 2^112 (the exponent bias difference; exact for every finite half,
+// subnormals and zero included), and a small integer through the 2^23 magic constant.
+GOLLEK_DEVICE float half_bits_alu(uint32_t h) {
+  return __uint_as_float(((h & 0x8000u) << 16) | ((h & 0x7FFFu) << 13)) * 0x1p112f;
+}
+GOLLEK_DEVICE float small_uint_to_float(uint32_t v) {  // exact for v < 2^23
+  return __uint_as_float(0x4B000000u | v) - 8388608.f;
+}
+
+GOLLEK_DEVICE void q4k_scales_regs(const uint4 hdr, int lane, float& a16, float& c) {
+  const int j = lane >> 2;
+  const float d = half_bits_alu(hdr.x & 0xFFFF), dmin = half_bits_alu(hdr.x >> 16);
+  uint32_t sv, mv;
+  if (j < 4) {
+    sv = q4k_sbyte(hdr, j) & 63;
+    mv = q4k_sbyte(hdr, j + 4) & 63;
+  } else {
+    sv = (q4k_sbyte(hdr, j + 4) & 0xF) | ((q4k_sbyte(hdr, j - 4) >> 6) << 4);
+    mv = (q4k_sbyte(hdr, j + 4) >> 4) | ((q4k_sbyte(hdr, j) >> 6) << 4);
+  }
+  a16 = 16.f * (d * small_uint_to_float(sv));
+  c = a16 + dmin * small_uint_to_float(mv);
+}
+
+GOLLEK_DEVICE void q4k_unpack8_unit(const uint2 q, int lane, float* f) {
+  // nibble k of byte e (low for even sub-blocks, high for odd) -> bits 3..6 of that byte, 0x80 set:
+  // byte value 0x80 | n << 3 placed as byte 2 under 0x3F gives the float bits 0x3F800000 | n << 19
+  const bool hi = ((lane >> 2) & 1) != 0;
+  const uint32_t t0 = hi ? (q.x >> 1) : (q.x << 3), t1 = hi ? (q.y >> 1) : (q.y << 3);
+  const uint32_t v0 = (t0 & 0x78787878u) | 0x80808080u, v1 = (t1 & 0x78787878u) | 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(v0, 0x3F000000u, 0x7054));
+  f[1] = __uint_as_float(__byte_perm(v0, 0x3F000000u, 0x7154));
+  f[2] = __uint_as_float(__byte_perm(v0, 0x3F000000u, 0x7254));
+  f[3] = __uint_as_float(__byte_perm(v0, 0x3F000000u, 0x7354));
+  f[4] = __uint_as_float(__byte_perm(v1, 0x3F000000u, 0x7054));
+  f[5] = __uint_as_float(__byte_perm(v1, 0x3F000000u, 0x7154));
+  f[6] = __uint_as_float(__byte_perm(v1, 0x3F000000u, 0x7254));
+  f[7] = __uint_as_float(__byte_perm(v1, 0x3F000000u, 0x7354));
+}
+
 GOLLEK_DEVICE void q4k_decode8(const uint8_t* blk, int lane, float* w) {
   q4k_decode8_regs(*reinterpret_cast<const uint4*>(blk),
                    *reinterpret_cast<const uint2*>(blk + 16 + 32 * (lane >> 3) + (lane & 3) * 8), lane, w);
 }
 
-template <int NT, bool SWIGLU>
-__global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
-                                                                   const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                                                                   const uint8_t* __restrict__ W, int N, int K,
-                                                                   int M) {
-  // each warp owns a pair of rows: (n, n + 64) in SwiGLU mode (gate, up), (2i, 2i+1) otherwise
+// KS warps share a row pair, each over 1/KS of the super-blocks (partial sums added through shared
+// memory): a narrow matrix (4096 rows = 2048 pairs) otherwise gives each SM only ~14 warps, each
+// walking a long serial decode-and-FMA chain over all of K.
+template <int NT, bool SWIGLU, int KS>
+__global__ void __launch_bounds__(kGemvWarps * 32, NT == 1 ? 3 : 1)
+    q4k_gemv_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy, const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                    const uint8_t* __restrict__ W, int N, int K, int M) {
+  // each warp group of KS owns a pair of rows: (n, n + 64) in SwiGLU mode (gate, up), (2i, 2i+1) otherwise
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = blockIdx.x * kGemvWarps + warp;
+  const int pair = blockIdx.x * (kGemvWarps / KS) + warp / KS;
+  const int kq = warp % KS;
   int r0, r1;
   if (SWIGLU) {
     const int grp = pair / 64, within = pair % 64;
@@ -86,25 +139,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16
     r0 = 2 * pair;
     r1 = r0 + 1;
   }
-  if (r0 >= N) return;
+  const bool live = r0 < N;
+  if (KS == 1 && !live) return;
   const bool has1 = r1 < N;
   const int nblk = K / 256;
   const int64_t row_bytes = (int64_t)nblk * 144;
-  const uint8_t* w0 = W + (int64_t)r0 * row_bytes;
-  const uint8_t* w1 = W + (int64_t)(has1 ? r1 : r0) * row_bytes;
+  const uint8_t* w0 = W + (int64_t)(live ? r0 : 0) * row_bytes;
+  const uint8_t* w1 = W + (int64_t)(has1 ? r1 : (live ? r0 : 0)) * row_bytes;
   float acc0[NT], acc1[NT];
 #pragma unroll
   for (int m = 0; m < NT; ++m) acc0[m] = acc1[m] = 0.f;
   const int koff = (lane >> 2) * 32 + (lane & 3) * 8;
   const int qoff = 16 + 32 * (lane >> 3) + (lane & 3) * 8;  // lane's nibbles inside a block
+  const int bbeg = live ? kq * nblk / KS : 0, bend = live ? (kq + 1) * nblk / KS : 0;
   // kBU super-blocks per round: their loads are all issued before any is decoded
   constexpr int kBU = 4;
-  for (int b0 = 0; b0 < nblk; b0 += kBU) {
+  for (int b0 = bbeg; b0 < bend; b0 += kBU) {
     uint4 h0[kBU], h1[kBU];
     uint2 q0[kBU], q1[kBU];
 #pragma unroll
     for (int u = 0; u < kBU; ++u) {
-      const int b = min(b0 + u, nblk - 1);
+      const int b = min(b0 + u, bend - 1);
       h0[u] = __ldg(reinterpret_cast<const uint4*>(w0 + b * 144));
       h1[u] = __ldg(reinterpret_cast<const uint4*>(w1 + b * 144));
       q0[u] = __ldg(reinterpret_cast<const uint2*>(w0 + b * 144 + qoff));
@@ -113,30 +168,42 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16
 #pragma unroll
     for (int u = 0; u < kBU; ++u) {
       const int b = b0 + u;
-      if (b >= nblk) break;
-      float wa[8], wb[8];
-      q4k_decode8_regs(h0[u], q0[u], lane, wa);
-      q4k_decode8_regs(h1[u], q1[u], lane, wb);
+      if (b >= bend) break;
+      float fa[8], fb[8], a0, c0, a1, c1;
+      q4k_scales_regs(h0[u], lane, a0, c0);
+      q4k_scales_regs(h1[u], lane, a1, c1);
+      q4k_unpack8_unit(q0[u], lane, fa);
+      q4k_unpack8_unit(q1[u], lane, fb);
 #pragma unroll
       for (int m = 0; m < NT; ++m) {
         if (m < M) {
           float xv[8];
           bf16x8_to_float(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)m * ldx + b * 256 + koff)), xv);
+          float sx = 0.f, sa = 0.f, sb = 0.f;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            acc0[m] = fmaf(wa[e], xv[e], acc0[m]);
-            acc1[m] = fmaf(wb[e], xv[e], acc1[m]);
+            sx += xv[e];
+            sa = fmaf(fa[e], xv[e], sa);
+            sb = fmaf(fb[e], xv[e], sb);
           }
+          acc0[m] = fmaf(a0, sa, fmaf(-c0, sx, acc0[m]));
+          acc1[m] = fmaf(a1, sb, fmaf(-c1, sx, acc1[m]));
         }
       }
     }
   }
+  __shared__ float red[KS > 1 ? kGemvWarps : 1][2][NT];
 #pragma unroll
   for (int m = 0; m < NT; ++m) {
     if (m < M) {
-      const float s0 = warp_sum(acc0[m]);
-      const float s1 = warp_sum(acc1[m]);
-      if (lane == 0) {
+      float s0 = warp_sum(acc0[m]);
+      float s1 = warp_sum(acc1[m]);
+      if (KS > 1) {
+        if (lane == 0) {
+          red[KS > 1 ? warp : 0][0][m] = s0;
+          red[KS > 1 ? warp : 0][1][m] = s1;
+        }
+      } else if (lane == 0) {
         if (SWIGLU) {
           const int on = (r0 / 128) * 64 + r0 % 128;
           y[(int64_t)m * ldy + on] = __float2bfloat16(silu(s0) * s1);
@@ -146,6 +213,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q4k_gemv_kernel(__nv_bfloat16
         }
       }
     }
+  }
+  if (KS == 1) return;
+  __syncthreads();
+  if (!live || kq != 0 || lane >= NT || lane >= M) return;
+  // lane m sums token m's KS partials of the pair (in K order)
+  const int m = lane;
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int q = 0; q < KS; ++q) {
+    s0 += red[KS > 1 ? warp + q : 0][0][m];
+    s1 += red[KS > 1 ? warp + q : 0][1][m];
+  }
+  if (SWIGLU) {
+    const int on = (r0 / 128) * 64 + r0 % 128;
+    y[(int64_t)m * ldy + on] = __float2bfloat16(silu(s0) * s1);
+  } else {
+    y[(int64_t)m * ldy + r0] = __float2bfloat16(s0);
+    if (has1) y[(int64_t)m * ldy + r1] = __float2bfloat16(s1);
   }
 }
 
@@ -314,6 +399,12 @@ __global__ void embedding_q8_0_kernel(__nv_bfloat16* __restrict__ out, const int
 
 namespace gollek {
 
+// GOLLEK_GEMV_KSPLIT=0: one warp per row pair over all of K (read at every call)
+static bool gemv_ksplit_off() {
+  const char* e = getenv("GOLLEK_GEMV_KSPLIT");
+  return e && e[0] == '0';
+}
+
 void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const void* W, int qtype, int N, int K,
                       int M, bool swiglu, cudaStream_t s) {
   throw_if(M < 1 || M > kGemvMaxTok, "gguf gemv: 1..16 tokens");
@@ -326,19 +417,39 @@ void launch_gguf_gemv(void* y, int64_t ldy, const void* x, int64_t ldx, const vo
   const auto* wp = reinterpret_cast<const uint8_t*>(W);
   if (qtype == 12) {
     const int pairs = (N + 1) / 2;
-    const int grid = (pairs + kGemvWarps - 1) / kGemvWarps;
-#define GOLLEK_Q4K(NT)                                                                                          \
-  if (M <= NT) {                                                                                              \
-    if (swiglu) q4k_gemv_kernel<NT, true><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);   \
-    else q4k_gemv_kernel<NT, false><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);         \
+    // warps per row pair: enough warps for ~32 per SM, each over >= 8 super-blocks
+    const int nblk = K / 256;
+    int ks = 1;
+    while (ks < 4 && pairs * ks < 32 * num_sms() && nblk / (2 * ks) >= 8) ks *= 2;
+    if (gemv_ksplit_off()) ks = 1;
+    const int grid = (pairs * ks + kGemvWarps - 1) / kGemvWarps;
+#define GOLLEK_Q4K(NT, KS)                                                                                     \
+  if (M <= NT && ks == KS) {                                                                                  \
+    if (swiglu) q4k_gemv_kernel<NT, true, KS><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M); \
+    else q4k_gemv_kernel<NT, false, KS><<<grid, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);       \
     check_launch("q4k_gemv");                                                                                 \
     return;                                                                                                   \
   }
-    GOLLEK_Q4K(1)
-    GOLLEK_Q4K(4)
-    GOLLEK_Q4K(8)
-    GOLLEK_Q4K(16)
+    GOLLEK_Q4K(1, 1)
+    GOLLEK_Q4K(1, 2)
+    GOLLEK_Q4K(1, 4)
+    GOLLEK_Q4K(4, 1)
+    GOLLEK_Q4K(4, 2)
+    GOLLEK_Q4K(4, 4)
+    GOLLEK_Q4K(8, 1)
+    GOLLEK_Q4K(16, 1)
 #undef GOLLEK_Q4K
+    ks = 1;  // 8 / 16 tokens: no K split
+    const int grid1 = (pairs + kGemvWarps - 1) / kGemvWarps;
+    if (M <= 8) {
+      if (swiglu) q4k_gemv_kernel<8, true, 1><<<grid1, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);
+      else q4k_gemv_kernel<8, false, 1><<<grid1, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);
+    } else {
+      if (swiglu) q4k_gemv_kernel<16, true, 1><<<grid1, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);
+      else q4k_gemv_kernel<16, false, 1><<<grid1, kGemvWarps * 32, 0, s>>>(yp, ldy, xp, ldx, wp, N, K, M);
+    }
+    check_launch("q4k_gemv");
+    return;
   } else if (qtype == 8) {
     const int grid = (N + kGemvWarps - 1) / kGemvWarps;
 #define GOLLEK_Q8(NT)                                                                                 \

@@ -180,3 +180,31 @@ def test_q4_k_fused_tcgen05_gemm(M, N, K):
     y2 = ops.linear_swiglu(x.cuda(), qw2)
     ref2 = ops.reference.gemm_swiglu(x.float(), host2)
     torch.testing.assert_close(y2.float().cpu(), ref2, rtol=2e-2, atol=3e-2 * max(1.0, float(ref2.abs().max()) / 4))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,K", [(4096, 14336), (4097, 4096), (768, 1024), (6144, 2304)])
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_q4_k_gemv_k_split(N, K, swiglu, monkeypatch):
+    """The Q4_K decode GEMV with several warps per row pair (each over part of the super-blocks,
+    partial sums added in shared memory) and with one warp per pair: both against x @ W^T over the
+    host dequantization, for 1..16 tokens, an odd row count and the SwiGLU epilogue."""
+    from gollek_b200 import ops
+    from gollek_b200.quant.gguf_weights import QWeight
+    if swiglu:
+        N = (N // 128) * 128
+    g = torch.Generator().manual_seed(N + K)
+    w = torch.randn(N, K, generator=g) * 0.02
+    raw = G.quantize_blocks(w, G.GGML_Q4_K)
+    host = G.dequantize_blocks(raw, G.GGML_Q4_K, N * K).view(N, K).bfloat16().float()
+    qw = QWeight(raw.cuda(), N, K, G.GGML_Q4_K)
+    for M in (1, 3, 4, 7, 16):
+        if M > ops.GGUF_GEMV_MAX_TOKENS and N % 8:
+            continue  # the tcgen05 path above the GEMV sizes needs 16-byte output rows
+        x = torch.randn(M, K, generator=g).bfloat16().cuda()
+        ref = ops.reference.gemm_swiglu(x.float().cpu(), host) if swiglu else x.float().cpu() @ host.t()
+        for split in ("1", "0"):
+            monkeypatch.setenv("GOLLEK_GEMV_KSPLIT", split)
+            y = ops.linear_swiglu(x, qw) if swiglu else ops.linear(x, qw)
+            torch.testing.assert_close(y.float().cpu(), ref, rtol=2e-2, atol=2e-2 * max(1.0, float(ref.abs().max()) / 4),
+                                       msg=lambda m: f"{M} ksplit={split}: {m}")
