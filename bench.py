@@ -109,22 +109,31 @@ class ClockSampler:
         self.window = None
 
     def start(self):
-        """Start sampling (before the warm-up, so that nvidia-smi is printing by the time the timed
-        region begins); ``mark`` then restricts the summary to the timed region."""
+        """Start sampling (before the warm-up); ``mark`` then restricts the summary to the timed
+        region. A thread runs one-shot ``nvidia-smi --query-gpu`` calls every 200 ms and stamps each
+        answer with the host time of the call: a long-running ``nvidia-smi -lms`` writing into a pipe
+        block-buffers its lines, so they arrive late, in bursts, and not at all for short runs."""
+        import shutil
         import threading
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        if shutil.which("nvidia-smi") is None:
             return
+        self.proc = True
+        self._stop = threading.Event()
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.gpu)]
 
-        def reader(f):
-            for line in f:
-                self.lines.append((time.perf_counter(), line))
+        def poll():
+            while not self._stop.is_set():
+                t = time.perf_counter()
+                try:
+                    r = subprocess.run(cmd, capture_output=True, text=True, timeout=5)
+                    for line in r.stdout.splitlines():
+                        if line.strip():
+                            self.lines.append((t, line + "\n"))
+                except (OSError, subprocess.TimeoutExpired):
+                    pass
+                self._stop.wait(max(0.0, 0.2 - (time.perf_counter() - t)))
 
-        self.thread = threading.Thread(target=reader, args=(self.proc.stdout,), daemon=True)
+        self.thread = threading.Thread(target=poll, daemon=True)
         self.thread.start()
 
     def mark(self, t0: float, t1: float) -> None:
@@ -133,12 +142,8 @@ class ClockSampler:
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.thread.join(timeout=5)
+        self._stop.set()
+        self.thread.join(timeout=10)
         lines = self.lines
         if self.window is not None:
             t0, t1 = self.window
