@@ -18,6 +18,8 @@
 #include "../common/tma_host.h"
 #include "launchers.h"
 
+#include <cstdlib>
+
 using namespace gollek;
 
 namespace {
@@ -408,12 +410,66 @@ struct FaSlot {
   int h, q_off, rows, kv_end, a, b;  // KV tiles [a, b)
 };
 
+struct FaItem {
+  int b, qs, ctx0, kh, jlo, jhi, kv_end;
+  const int* bt;
+  FaSlot sl[2];
+};
+
+// Item of round r0 / gridDim.x for this CTA: rounds alternate direction over the heaviest-first list
+// (CTA c takes the c-th item of even rounds and the c-th from the end of odd ones), which evens out
+// the per-CTA totals a plain round-robin skews towards the low CTAs. -1: none left.
+GOLLEK_DEVICE int fa_snake(int r0, int nwork) {
+  const int round = r0 / (int)gridDim.x;
+  const int w = r0 + ((round & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return w < nwork ? w : -1;
+}
+
+// Work item w of the list: its sequence, slots (heads / row tiles) and KV tile range.
+GOLLEK_DEVICE FaItem fa_item(const int4* __restrict__ work, int w, const int* __restrict__ seq_lens,
+                             const int* __restrict__ query_start, const int* __restrict__ block_tables,
+                             int bt_stride, int H, int Hk, int window) {
+  FaItem it;
+  const int4 wk = work[w];
+  it.b = wk.x;
+  const int pair_heads = wk.w >> 16, hbase = wk.w & 0xffff;
+  it.qs = query_start[it.b];
+  const int qlen = query_start[it.b + 1] - it.qs;
+  const int L = seq_lens[it.b];
+  it.ctx0 = L - qlen;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    FaSlot& t = it.sl[i];
+    t.h = pair_heads ? hbase + i : hbase;
+    t.q_off = pair_heads ? wk.y : (i == 0 ? wk.y : wk.z);
+    const bool valid = t.q_off >= 0 && t.q_off < qlen;
+    t.rows = valid ? min(kTQ, qlen - t.q_off) : 0;
+    t.kv_end = valid ? min(L, it.ctx0 + t.q_off + t.rows) : 0;
+    t.a = (valid && window > 0) ? max(0, it.ctx0 + t.q_off - window + 1) / kTK : 0;
+    t.b = valid ? (t.kv_end + kTK - 1) / kTK : 0;
+    if (t.b <= t.a) t.a = t.b = 0;
+  }
+  it.kh = it.sl[0].h / (H / Hk);
+  const bool v0 = it.sl[0].b > it.sl[0].a, v1 = it.sl[1].b > it.sl[1].a;
+  it.jlo = (v0 && v1) ? min(it.sl[0].a, it.sl[1].a) : (v0 ? it.sl[0].a : it.sl[1].a);
+  it.jhi = max(it.sl[0].b, it.sl[1].b);
+  it.kv_end = max(it.sl[0].kv_end, it.sl[1].kv_end);
+  it.bt = block_tables + (int64_t)it.b * bt_stride;
+  return it;
+}
+
+// Persistent: each CTA runs one item per round of gridDim.x items (fa_snake order; the list is sorted
+// heaviest first). Across
+// items the KV ring, the S / P barriers and the Q buffer keep running counters, so the next item's Q
+// and first KV tiles load, and its first S MMAs run, while the softmax warps still normalise and store
+// the previous item's O: q_empty (committed after an item's last S MMA) frees the Q buffer, o_free[i]
+// (the slot's four softmax warps, after reading O_i) lets the next item's first PV overwrite O_i.
 template <int EMU>
 __global__ void __launch_bounds__(kFaThreads, 1)
     prefill_fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
-                      const int4* __restrict__ work, int H, int Hk, float scale_log2,
+                      const int4* __restrict__ work, int nwork, int H, int Hk, float scale_log2,
                       uint32_t* status, int window, float softcap_log2, int num_blocks) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -428,38 +484,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint64_t* p_full = bars + 9;                 // [slot]
   uint64_t* o_done = bars + 11;                // [slot]
   uint64_t* done_bar = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_empty = bars + 14;
+  uint64_t* o_free = bars + 15;                // [slot]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int4 wk = work[blockIdx.x];
-  const int b = wk.x;
-  const int pair_heads = wk.w >> 16, hbase = wk.w & 0xffff;
-  const int qs = query_start[b], qlen = query_start[b + 1] - qs;
-  const int L = seq_lens[b];
-  const int ctx0 = L - qlen;
-  FaSlot sl[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    FaSlot& t = sl[i];
-    t.h = pair_heads ? hbase + i : hbase;
-    t.q_off = pair_heads ? wk.y : (i == 0 ? wk.y : wk.z);
-    const bool valid = t.q_off >= 0 && t.q_off < qlen;
-    t.rows = valid ? min(kTQ, qlen - t.q_off) : 0;
-    t.kv_end = valid ? min(L, ctx0 + t.q_off + t.rows) : 0;
-    t.a = (valid && window > 0) ? max(0, ctx0 + t.q_off - window + 1) / kTK : 0;
-    t.b = valid ? (t.kv_end + kTK - 1) / kTK : 0;
-    if (t.b <= t.a) t.a = t.b = 0;
-  }
-  const int kh = sl[0].h / (H / Hk);
-  const bool v0 = sl[0].b > sl[0].a, v1 = sl[1].b > sl[1].a;
-  const int jlo = (v0 && v1) ? min(sl[0].a, sl[1].a) : (v0 ? sl[0].a : sl[1].a);
-  const int jhi = max(sl[0].b, sl[1].b);
-  const int kv_end = max(sl[0].kv_end, sl[1].kv_end);
-  const int* bt = block_tables + (int64_t)b * bt_stride;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
@@ -467,6 +501,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 4);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -482,107 +517,143 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    if (elect_one() && jhi > jlo) {
+    if (elect_one()) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmKV);
-      mbar_arrive_expect_tx(q_full, ((v0 ? 1 : 0) + (v1 ? 1 : 0)) * kQBytes);
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        if (sl[i].b > sl[i].a) {
-          const int qrow = qs + sl[i].q_off;
-          tma_load_2d(sQ + i * kQBytes, &tmQ, sl[i].h * kD, qrow, q_full);
-          tma_load_2d(sQ + i * kQBytes + kQBytes / 2, &tmQ, sl[i].h * kD + 64, qrow, q_full);
-        }
-      }
-      int issued = 0;
+      int g = 0, nq = 0;  // KV tiles and Q loads issued so far
       bool ok = true;
-      for (int j = jlo; j < jhi; ++j) {
-        const int idx = j - jlo, st = idx & 1;
-        if (!waitq(&kv_empty[st], ((idx >> 1) & 1) ^ 1, status, abort_flag)) {
+      for (int r0 = 0; r0 < nwork && ok; r0 += gridDim.x) {
+        const int w = fa_snake(r0, nwork);
+        if (w < 0) continue;
+        const FaItem it = fa_item(work, w, seq_lens, query_start, block_tables, bt_stride, H, Hk, window);
+        if (it.jhi <= it.jlo) continue;
+        // the previous item's S MMAs have read its Q tiles
+        if (nq > 0 && !waitq(q_empty, (nq - 1) & 1, status, abort_flag)) {
           ok = false;
           break;
         }
-        uint8_t* dk = sKV + st * 2 * kKVTile;
-        uint8_t* dv = dk + kKVTile;
-        mbar_arrive_expect_tx(&k_full[st], kKVTile);
-        for (int blk = 0; blk < kTK / kBS; ++blk) {
-          const int kb = (j * kTK) / kBS + blk;
-          const int pb = checked_index((kb * kBS < kv_end) ? bt[kb] : bt[0], num_blocks, status);
-          const int rk = ((pb * 2 + 0) * Hk + kh) * kBS;
-          tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &k_full[st]);
-          tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &k_full[st]);
+        const bool v0 = it.sl[0].b > it.sl[0].a, v1 = it.sl[1].b > it.sl[1].a;
+        mbar_arrive_expect_tx(q_full, ((v0 ? 1 : 0) + (v1 ? 1 : 0)) * kQBytes);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (it.sl[i].b > it.sl[i].a) {
+            const int qrow = it.qs + it.sl[i].q_off;
+            tma_load_2d(sQ + i * kQBytes, &tmQ, it.sl[i].h * kD, qrow, q_full);
+            tma_load_2d(sQ + i * kQBytes + kQBytes / 2, &tmQ, it.sl[i].h * kD + 64, qrow, q_full);
+          }
         }
-        mbar_arrive_expect_tx(&v_full[st], kKVTile);
-        for (int blk = 0; blk < kTK / kBS; ++blk) {
-          const int kb = (j * kTK) / kBS + blk;
-          const int pb = checked_index((kb * kBS < kv_end) ? bt[kb] : bt[0], num_blocks, status);
-          const int rv = ((pb * 2 + 1) * Hk + kh) * kBS;
-          tma_load_2d(dv + blk * 2048, &tmKV, 0, rv, &v_full[st]);
-          tma_load_2d(dv + kKVTile / 2 + blk * 2048, &tmKV, 64, rv, &v_full[st]);
+        ++nq;
+        for (int j = it.jlo; j < it.jhi; ++j, ++g) {
+          const int st = g & 1;
+          if (!waitq(&kv_empty[st], ((g >> 1) & 1) ^ 1, status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dk = sKV + st * 2 * kKVTile;
+          uint8_t* dv = dk + kKVTile;
+          mbar_arrive_expect_tx(&k_full[st], kKVTile);
+          for (int blk = 0; blk < kTK / kBS; ++blk) {
+            const int kb = (j * kTK) / kBS + blk;
+            const int pb = checked_index((kb * kBS < it.kv_end) ? it.bt[kb] : it.bt[0], num_blocks, status);
+            const int rk = ((pb * 2 + 0) * Hk + it.kh) * kBS;
+            tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &k_full[st]);
+            tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &k_full[st]);
+          }
+          mbar_arrive_expect_tx(&v_full[st], kKVTile);
+          for (int blk = 0; blk < kTK / kBS; ++blk) {
+            const int kb = (j * kTK) / kBS + blk;
+            const int pb = checked_index((kb * kBS < it.kv_end) ? it.bt[kb] : it.bt[0], num_blocks, status);
+            const int rv = ((pb * 2 + 1) * Hk + it.kh) * kBS;
+            tma_load_2d(dv + blk * 2048, &tmKV, 0, rv, &v_full[st]);
+            tma_load_2d(dv + kKVTile / 2 + blk * 2048, &tmKV, 64, rv, &v_full[st]);
+          }
         }
-        ++issued;
       }
-      if (!ok) {
-        drainq(q_full, 0);
-        for (int x = max(0, issued - 2); x < issued; ++x) {
+      if (!ok) {  // copies still in flight land before the CTA leaves
+        if (nq > 0) drainq(q_full, (nq - 1) & 1);
+        for (int x = max(0, g - 2); x < g; ++x) {
           drainq(&k_full[x & 1], (x >> 1) & 1);
           drainq(&v_full[x & 1], (x >> 1) & 1);
         }
       }
     }
   } else if (warp == 9) {
-    if (elect_one() && jhi > jlo) {
+    if (elect_one()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(kTQ, kTK);              // Q K^T, both K-major
       constexpr uint32_t idesc_o = make_idesc_bf16(kTQ, kD) | (1u << 16);  // P (TMEM) V, V MN-major
-      bool ok = waitq(q_full, 0, status, abort_flag);
-      int np[2] = {0, 0};
-      for (int j = jlo; j <= jhi && ok; ++j) {
-        const int idx = j - jlo;
-        const bool prev = j > jlo, cur = j < jhi;
-        if (prev && !waitq(&v_full[(idx - 1) & 1], ((idx - 1) >> 1) & 1, status, abort_flag)) {
+      int g = 0, nq = 0;
+      int np[2] = {0, 0};  // P tiles consumed per slot
+      int no[2] = {0, 0};  // items finished per slot (O handed to the epilogue)
+      bool ok = true;
+      for (int r0 = 0; r0 < nwork && ok; r0 += gridDim.x) {
+        const int w = fa_snake(r0, nwork);
+        if (w < 0) continue;
+        const FaItem it = fa_item(work, w, seq_lens, query_start, block_tables, bt_stride, H, Hk, window);
+        if (it.jhi <= it.jlo) continue;
+        if (!waitq(q_full, nq & 1, status, abort_flag)) {
           ok = false;
           break;
         }
-        bool k_ready = false;
-        tcgen05_fence_after();
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const uint32_t tS = tmem + i * kTK, tO = tmem + 256 + i * kD;
-          if (prev && j - 1 >= sl[i].a && j - 1 < sl[i].b) {
-            if (!waitq(&p_full[i], np[i] & 1, status, abort_flag)) {
-              ok = false;
-              break;
-            }
-            ++np[i];
-            tcgen05_fence_after();
-            const uint32_t v_addr = smem_u32(sKV + ((idx - 1) & 1) * 2 * kKVTile + kKVTile);
-#pragma unroll
-            for (int ks = 0; ks < kTK / 16; ++ks)
-              umma_f16_ts(tO, tS + ks * 8, make_desc_mn_sw128(v_addr + ks * 2048, kKVTile / 2), idesc_o,
-                          (j - 1 > sl[i].a || ks > 0) ? 1u : 0u);
-            if (j == sl[i].b) umma_commit(&o_done[i]);
+        for (int j = it.jlo; j <= it.jhi && ok; ++j) {
+          const int gi = g + (j - it.jlo);
+          const bool prev = j > it.jlo, cur = j < it.jhi;
+          if (prev && !waitq(&v_full[(gi - 1) & 1], ((gi - 1) >> 1) & 1, status, abort_flag)) {
+            ok = false;
+            break;
           }
-          if (cur && j >= sl[i].a && j < sl[i].b) {
-            if (!k_ready) {
-              if (!waitq(&k_full[idx & 1], (idx >> 1) & 1, status, abort_flag)) {
+          bool k_ready = false;
+          tcgen05_fence_after();
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const FaSlot& t = it.sl[i];
+            const uint32_t tS = tmem + i * kTK, tO = tmem + 256 + i * kD;
+            if (prev && j - 1 >= t.a && j - 1 < t.b) {
+              if (!waitq(&p_full[i], np[i] & 1, status, abort_flag)) {
+                ok = false;
+                break;
+              }
+              ++np[i];
+              // the first PV of an item overwrites O_i: the previous item's epilogue must have read it
+              if (j - 1 == t.a && no[i] > 0 && !waitq(&o_free[i], (no[i] - 1) & 1, status, abort_flag)) {
                 ok = false;
                 break;
               }
               tcgen05_fence_after();
-              k_ready = true;
-            }
-            const uint32_t q_addr = smem_u32(sQ + i * kQBytes);
-            const uint32_t k_addr = smem_u32(sKV + (idx & 1) * 2 * kKVTile);
+              const uint32_t v_addr = smem_u32(sKV + ((gi - 1) & 1) * 2 * kKVTile + kKVTile);
 #pragma unroll
-            for (int ks = 0; ks < kD / 16; ++ks) {
-              const uint64_t a = make_smem_desc_sw128(q_addr + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
-              const uint64_t bd = make_smem_desc_sw128(k_addr + (ks >> 2) * (kKVTile / 2) + (ks & 3) * 32);
-              umma_f16_ss(tS, a, bd, idesc_s, ks > 0 ? 1u : 0u);
+              for (int ks = 0; ks < kTK / 16; ++ks)
+                umma_f16_ts(tO, tS + ks * 8, make_desc_mn_sw128(v_addr + ks * 2048, kKVTile / 2), idesc_o,
+                            (j - 1 > t.a || ks > 0) ? 1u : 0u);
+              if (j == t.b) {
+                umma_commit(&o_done[i]);
+                ++no[i];
+              }
             }
-            umma_commit(&s_full[i]);
+            if (cur && j >= t.a && j < t.b) {
+              if (!k_ready) {
+                if (!waitq(&k_full[gi & 1], (gi >> 1) & 1, status, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                tcgen05_fence_after();
+                k_ready = true;
+              }
+              const uint32_t q_addr = smem_u32(sQ + i * kQBytes);
+              const uint32_t k_addr = smem_u32(sKV + (gi & 1) * 2 * kKVTile);
+#pragma unroll
+              for (int ks = 0; ks < kD / 16; ++ks) {
+                const uint64_t a = make_smem_desc_sw128(q_addr + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
+                const uint64_t bd = make_smem_desc_sw128(k_addr + (ks >> 2) * (kKVTile / 2) + (ks & 3) * 32);
+                umma_f16_ss(tS, a, bd, idesc_s, ks > 0 ? 1u : 0u);
+              }
+              umma_commit(&s_full[i]);
+            }
           }
+          if (prev && ok) umma_commit(&kv_empty[(gi - 1) & 1]);
+          if (j == it.jhi - 1 && ok) umma_commit(q_empty);  // the item's last S MMAs read Q
         }
-        if (prev && ok) umma_commit(&kv_empty[(idx - 1) & 1]);
+        g += it.jhi - it.jlo;
+        ++nq;
       }
       if (!ok) {
         umma_commit(done_bar);
@@ -594,149 +665,163 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // Two passes over S in TMEM, 32 columns at a time (row max, then P): S is re-read instead of
     // held in registers, which keeps the unrolled code small (instruction-cache bound otherwise).
     const int i = warp >> 2, lg = warp & 3;
-    const FaSlot t = i == 0 ? sl[0] : sl[1];
     const int r = lg * 32 + lane;
-    const int qpos = ctx0 + t.q_off + r;
-    const int qmin = ctx0 + t.q_off + lg * 32, qmax = qmin + 31;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
     const uint32_t tS = tmem + i * kTK + lane_off, tO = tmem + 256 + i * kD + lane_off;
     const bool capped = softcap_log2 > 0.f;
     const float inv_cap = capped ? 1.f / softcap_log2 : 0.f;
-    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    int n = 0;
-    for (int j = t.a; j < t.b; ++j, ++n) {
-      if (!waitq(&s_full[i], n & 1, status, abort_flag)) {
+    int ns = 0, no = 0;  // S tiles and items of this slot so far
+    for (int r0 = 0; r0 < nwork && ok; r0 += gridDim.x) {
+        const int w = fa_snake(r0, nwork);
+        if (w < 0) continue;
+      const FaItem it = fa_item(work, w, seq_lens, query_start, block_tables, bt_stride, H, Hk, window);
+      const FaSlot t = i == 0 ? it.sl[0] : it.sl[1];
+      if (it.jhi <= it.jlo || t.b <= t.a) continue;
+      const int ctx0 = it.ctx0;
+      const int qpos = ctx0 + t.q_off + r;
+      const int qmin = ctx0 + t.q_off + lg * 32, qmax = qmin + 31;
+      float m = -INFINITY, l = 0.f;
+      int n = 0;
+      for (int j = t.a; j < t.b; ++j, ++n) {
+        if (!waitq(&s_full[i], ns & 1, status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        ++ns;
+        tcgen05_fence_after();
+        const int k0 = j * kTK;
+        // visible keys of row qpos: [qpos - window + 1, min(qpos, kv_end - 1)] - k0
+        const bool need_mask = (k0 + kTK - 1 > qmin) || (k0 + kTK > t.kv_end) ||
+                               (window > 0 && k0 < qmax - window + 1);
+        const int khi = min(qpos, t.kv_end - 1) - k0;
+        const int klo = (window > 0 ? qpos - window + 1 : 0) - k0;
+        // pass 1: the four 32-column loads in flight at once, row max over 8 independent chains
+        float mx;
+        {
+          uint32_t u[kTK];
+  #pragma unroll
+          for (int c = 0; c < kTK; c += 32) tmem_ld_32x32b_x32(tS + c, u + c);
+          tmem_ld_wait();
+          float m8[8];
+  #pragma unroll
+          for (int x = 0; x < 8; ++x) m8[x] = -INFINITY;
+          if (need_mask) {
+  #pragma unroll
+            for (int c = 0; c < kTK; ++c)
+              m8[c & 7] = fmaxf(m8[c & 7], (c <= khi && c >= klo) ? __uint_as_float(u[c]) : -INFINITY);
+          } else {
+  #pragma unroll
+            for (int c = 0; c < kTK; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(u[c]));
+          }
+          mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        }
+        // running max in the scaled log2 domain (soft cap is monotonic: cap the raw max)
+        const float mnew = mx == -INFINITY ? -INFINITY
+                           : capped        ? softcap_log2 * tanh_approx(mx * scale_log2 * inv_cap)
+                                           : mx * scale_log2;
+        float corr = 1.f;
+        if (n == 0) {
+          m = mnew;
+        } else if (mnew > m + 8.f) {
+          corr = exp2f(m - mnew);
+          m = mnew;
+        }
+        const float ms = m == -INFINITY ? 0.f : m;
+        const int mode = capped ? 3 : need_mask ? 2 : (EMU > 0 ? 1 : 0);
+        // pass 2: S re-read 32 columns at a time, the next chunk's load overlapping this chunk's math
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+        auto p_chunk = [&](const uint32_t* u, int c0) {
+          uint32_t pk[16];
+          if (mode == 1) {  // full tile: a share of the exponentials on the FMA pipe
+  #pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
+              const float x1 = fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms);
+              const float p1 = (EMU == 2 || (e & 3) == 2) ? ex2_poly(x1) : ex2_mufu(x1);
+              ps[(e >> 1) & 3] += p0 + p1;
+              pk[e >> 1] = pack_bf16x2(p0, p1);
+            }
+          } else if (mode == 0) {
+  #pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
+              const float p1 = ex2_mufu(fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms));
+              ps[(e >> 1) & 3] += p0 + p1;
+              pk[e >> 1] = pack_bf16x2(p0, p1);
+            }
+          } else {  // masked and / or soft-capped
+  #pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float p[2];
+  #pragma unroll
+              for (int x = 0; x < 2; ++x) {
+                const int c = c0 + e + x;
+                float v = __uint_as_float(u[e + x]);
+                v = capped ? softcap_log2 * tanh_approx(v * scale_log2 * inv_cap) : v * scale_log2;
+                p[x] = (c <= khi && c >= klo) ? ex2_mufu(v - ms) : 0.f;
+              }
+              ps[(e >> 1) & 3] += p[0] + p[1];
+              pk[e >> 1] = pack_bf16x2(p[0], p[1]);
+            }
+          }
+          tmem_st_32x32b_x16(tS + (c0 >> 1), pk);
+        };
+        {
+          uint32_t ua[32], ub[32];
+          tmem_ld_32x32b_x32(tS, ua);
+          tmem_ld_wait();
+  #pragma unroll 1
+          for (int c0 = 0; c0 < kTK; c0 += 64) {
+            tmem_ld_32x32b_x32(tS + c0 + 32, ub);
+            p_chunk(ua, c0);
+            tmem_ld_wait();
+            if (c0 + 64 < kTK) tmem_ld_32x32b_x32(tS + c0 + 64, ua);
+            p_chunk(ub, c0 + 32);
+            tmem_ld_wait();
+          }
+        }
+        const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+        l = l * corr + psum;
+        if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
+  #pragma unroll 1
+          for (int c = 0; c < kD; c += 32) {
+            uint32_t u[32];
+            tmem_ld_32x32b_x32(tO + c, u);
+            tmem_ld_wait();
+  #pragma unroll
+            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
+            tmem_st_32x32b_x32(tO + c, u);
+          }
+        }
+        tmem_st_wait();
+        tcgen05_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[i]);
+      }
+      if (!ok || !waitq(&o_done[i], no & 1, status, abort_flag)) {
         ok = false;
         break;
       }
-      tcgen05_fence_after();
-      const int k0 = j * kTK;
-      // visible keys of row qpos: [qpos - window + 1, min(qpos, kv_end - 1)] - k0
-      const bool need_mask = (k0 + kTK - 1 > qmin) || (k0 + kTK > t.kv_end) ||
-                             (window > 0 && k0 < qmax - window + 1);
-      const int khi = min(qpos, t.kv_end - 1) - k0;
-      const int klo = (window > 0 ? qpos - window + 1 : 0) - k0;
-      // pass 1: the four 32-column loads in flight at once, row max over 8 independent chains
-      float mx;
-      {
-        uint32_t u[kTK];
-#pragma unroll
-        for (int c = 0; c < kTK; c += 32) tmem_ld_32x32b_x32(tS + c, u + c);
-        tmem_ld_wait();
-        float m8[8];
-#pragma unroll
-        for (int x = 0; x < 8; ++x) m8[x] = -INFINITY;
-        if (need_mask) {
-#pragma unroll
-          for (int c = 0; c < kTK; ++c)
-            m8[c & 7] = fmaxf(m8[c & 7], (c <= khi && c >= klo) ? __uint_as_float(u[c]) : -INFINITY);
-        } else {
-#pragma unroll
-          for (int c = 0; c < kTK; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(u[c]));
-        }
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      }
-      // running max in the scaled log2 domain (soft cap is monotonic: cap the raw max)
-      const float mnew = mx == -INFINITY ? -INFINITY
-                         : capped        ? softcap_log2 * tanh_approx(mx * scale_log2 * inv_cap)
-                                         : mx * scale_log2;
-      float corr = 1.f;
-      if (n == 0) {
-        m = mnew;
-      } else if (mnew > m + 8.f) {
-        corr = exp2f(m - mnew);
-        m = mnew;
-      }
-      const float ms = m == -INFINITY ? 0.f : m;
-      const int mode = capped ? 3 : need_mask ? 2 : (EMU > 0 ? 1 : 0);
-      // pass 2: S re-read 32 columns at a time, the next chunk's load overlapping this chunk's math
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      auto p_chunk = [&](const uint32_t* u, int c0) {
-        uint32_t pk[16];
-        if (mode == 1) {  // full tile: a share of the exponentials on the FMA pipe
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
-            const float x1 = fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms);
-            const float p1 = (EMU == 2 || (e & 3) == 2) ? ex2_poly(x1) : ex2_mufu(x1);
-            ps[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
-          }
-        } else if (mode == 0) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
-            const float p1 = ex2_mufu(fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms));
-            ps[(e >> 1) & 3] += p0 + p1;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
-          }
-        } else {  // masked and / or soft-capped
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float p[2];
-#pragma unroll
-            for (int x = 0; x < 2; ++x) {
-              const int c = c0 + e + x;
-              float v = __uint_as_float(u[e + x]);
-              v = capped ? softcap_log2 * tanh_approx(v * scale_log2 * inv_cap) : v * scale_log2;
-              p[x] = (c <= khi && c >= klo) ? ex2_mufu(v - ms) : 0.f;
-            }
-            ps[(e >> 1) & 3] += p[0] + p[1];
-            pk[e >> 1] = pack_bf16x2(p[0], p[1]);
-          }
-        }
-        tmem_st_32x32b_x16(tS + (c0 >> 1), pk);
-      };
-      {
-        uint32_t ua[32], ub[32];
-        tmem_ld_32x32b_x32(tS, ua);
-        tmem_ld_wait();
-#pragma unroll 1
-        for (int c0 = 0; c0 < kTK; c0 += 64) {
-          tmem_ld_32x32b_x32(tS + c0 + 32, ub);
-          p_chunk(ua, c0);
-          tmem_ld_wait();
-          if (c0 + 64 < kTK) tmem_ld_32x32b_x32(tS + c0 + 64, ua);
-          p_chunk(ub, c0 + 32);
-          tmem_ld_wait();
-        }
-      }
-      const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      l = l * corr + psum;
-      if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
-#pragma unroll 1
-        for (int c = 0; c < kD; c += 32) {
-          uint32_t u[32];
-          tmem_ld_32x32b_x32(tO + c, u);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
-          tmem_st_32x32b_x32(tO + c, u);
-        }
-      }
-      tmem_st_wait();
-      tcgen05_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[i]);
-    }
-    if (ok && t.b > t.a && waitq(&o_done[i], 0, status, abort_flag)) {
+      ++no;
       tcgen05_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = out + (int64_t)(qs + t.q_off + r) * out_stride + t.h * kD;
+      __nv_bfloat16* dst = out + (int64_t)(it.qs + t.q_off + r) * out_stride + t.h * kD;
+      uint32_t u[kD];
 #pragma unroll
-      for (int c = 0; c < kD; c += 32) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tO + c, u);
-        tmem_ld_wait();
-        if (r < t.rows) {
+      for (int c = 0; c < kD; c += 32) tmem_ld_32x32b_x32(tO + c, u + c);
+      tmem_ld_wait();
+      // O_i is in registers: the next item's first PV may overwrite it
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[i]);
+      if (r < t.rows) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            float f[8];
+        for (int e = 0; e < kD; e += 8) {
+          float f[8];
 #pragma unroll
-            for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(u[e + x]) * inv;
-            *reinterpret_cast<uint4*>(dst + c + e) = float_to_bf16x8(f);
-          }
+          for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(u[e + x]) * inv;
+          *reinterpret_cast<uint4*>(dst + e) = float_to_bf16x8(f);
         }
       }
     }
@@ -788,7 +873,9 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tkv = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, kBS, 64,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
-  dim3 grid(nwork);
+  // one CTA per SM looping over the items; GOLLEK_PREFILL_PERSISTENT=0: one CTA per item
+  const char* pe = getenv("GOLLEK_PREFILL_PERSISTENT");
+  dim3 grid((pe && pe[0] == '0') ? nwork : std::min(nwork, num_sms()));
   const float sl2 = scale * 1.4426950408889634f, cap = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   auto* w4 = reinterpret_cast<const int4*>(work);
@@ -797,7 +884,7 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
     GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(prefill_fa_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                                            kFaSmem));                                                              \
     prefill_fa_kernel<E><<<grid, kFaThreads, kFaSmem, s>>>(tq, tkv, o, out_stride, block_tables, bt_stride,        \
-                                                           seq_lens, query_start, w4, H, Hk,                       \
+                                                           seq_lens, query_start, w4, nwork, H, Hk,                \
                                                            sl2, bounds_status(), window, cap, num_blocks);         \
   } while (0)
   if (emu == 2)
