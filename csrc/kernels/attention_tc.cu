@@ -700,18 +700,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         float mx;
         {
           uint32_t u[kTK];
-  #pragma unroll
+#pragma unroll
           for (int c = 0; c < kTK; c += 32) tmem_ld_32x32b_x32(tS + c, u + c);
           tmem_ld_wait();
           float m8[8];
-  #pragma unroll
+#pragma unroll
           for (int x = 0; x < 8; ++x) m8[x] = -INFINITY;
           if (need_mask) {
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < kTK; ++c)
               m8[c & 7] = fmaxf(m8[c & 7], (c <= khi && c >= klo) ? __uint_as_float(u[c]) : -INFINITY);
           } else {
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < kTK; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(u[c]));
           }
           mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
@@ -734,7 +734,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         auto p_chunk = [&](const uint32_t* u, int c0) {
           uint32_t pk[16];
           if (mode == 1) {  // full tile: a share of the exponentials on the FMA pipe
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 32; e += 2) {
               const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
               const float x1 = fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms);
@@ -743,7 +743,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
               pk[e >> 1] = pack_bf16x2(p0, p1);
             }
           } else if (mode == 0) {
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 32; e += 2) {
               const float p0 = ex2_mufu(fmaf(__uint_as_float(u[e]), scale_log2, -ms));
               const float p1 = ex2_mufu(fmaf(__uint_as_float(u[e + 1]), scale_log2, -ms));
@@ -751,10 +751,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
               pk[e >> 1] = pack_bf16x2(p0, p1);
             }
           } else {  // masked and / or soft-capped
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 32; e += 2) {
               float p[2];
-  #pragma unroll
+#pragma unroll
               for (int x = 0; x < 2; ++x) {
                 const int c = c0 + e + x;
                 float v = __uint_as_float(u[e + x]);
@@ -771,7 +771,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           uint32_t ua[32], ub[32];
           tmem_ld_32x32b_x32(tS, ua);
           tmem_ld_wait();
-  #pragma unroll 1
+#pragma unroll 1
           for (int c0 = 0; c0 < kTK; c0 += 64) {
             tmem_ld_32x32b_x32(tS + c0 + 32, ub);
             p_chunk(ua, c0);
@@ -784,12 +784,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const float psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         l = l * corr + psum;
         if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
-  #pragma unroll 1
+#pragma unroll 1
           for (int c = 0; c < kD; c += 32) {
             uint32_t u[32];
             tmem_ld_32x32b_x32(tO + c, u);
             tmem_ld_wait();
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * corr);
             tmem_st_32x32b_x32(tO + c, u);
           }
