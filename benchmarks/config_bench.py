@@ -43,6 +43,8 @@ def parse(argv=None):
     p.add_argument("--decode-steps", type=int, default=64)
     p.add_argument("--skip-prefill", action="store_true", help="llama70b-fp8: decode only, no prefill sweep")
     p.add_argument("--scale", type=float, default=1.0, help="shrink batch / lengths (small runs)")
+    p.add_argument("--kv-cache-dtype", default="auto", choices=["auto", "fp8"],
+                   help="llama70b-fp8: KV cache in the model dtype, or fp8 e4m3 with a scale per token and head")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="TP collectives: fused P2P kernels over the IPC heap, or NCCL")
     return p.parse_args(argv)
@@ -111,7 +113,7 @@ def llama70b_fp8(args, di, comm):
     kw = dict(model="llama-3-70b", device=args.device, dtype="bfloat16", quantization="fp8",
               tensor_parallel_size=di.world_size, max_num_seqs=max(B, 8), max_num_batched_tokens=8192,
               max_model_len=max(ctx + gen, int(8192 * args.scale) + 16) + 16, enable_prefix_caching=False,
-              use_cuda_graphs=cuda, gpu_memory_utilization=0.9)
+              use_cuda_graphs=cuda, gpu_memory_utilization=0.9, kv_cache_dtype=args.kv_cache_dtype)
     eng = _engine(mcfg, kw, comm=comm)
     rng = np.random.default_rng(0)
     V = mcfg.vocab_size
@@ -129,6 +131,7 @@ def llama70b_fp8(args, di, comm):
     _emit(di.rank, {"workload": "llama70b-fp8-decode", "n_gpus": di.world_size, "batch": B, "context": ctx,
                     "steps": K, "tokens": n, "ms": round(t.ms, 2), "tok_s": round(n / t.ms * 1e3, 1),
                     "tpot_ms": round(t.ms / K, 3), "dtype": "fp8 (block-scaled weights and activations)",
+                    "kv_cache_dtype": args.kv_cache_dtype,
                     "data": "synthetic, random-init"})
     for i in range(B):
         eng.abort_request(f"d{i}")
