@@ -6,7 +6,7 @@ siblings: run, chat, batch, list, show, convert, quantize, serve, providers, sta
   run       one-shot generation            chat      interactive chat loop
   batch     JSONL prompts → JSONL outputs  serve     HTTP server (OpenAI + gollek routes)
   convert   safetensors → GGUF (F32/F16/Q8_0/Q4_K)
-  quantize  GGUF → GGUF at another type, or safetensors → block-scaled FP8 safetensors
+  quantize  GGUF → GGUF at another type, or safetensors → block-scaled FP8 / AWQ / AutoRound / QuIP
   show      model config and tensor table  list      presets and models under $GOLLEK_HOME
   bench     serving benchmark (bench.py)
 """
@@ -108,6 +108,15 @@ def cmd_quantize(args):
         t = args.type.upper()
         G.write_llama_gguf(args.dst, cfg, w, t if t in G.MIXTURES else G.TYPE_BY_NAME[t])
         print(f"wrote {args.dst} ({args.type})")
+    elif args.method in ("awq", "autoround", "quip"):
+        from .quant.offline import quantize_checkpoint
+        calib = None
+        if args.calib_file:  # one calibration sequence of token ids per line
+            with open(args.calib_file) as f:
+                calib = [[int(t) for t in ln.split()] for ln in f if ln.strip()]
+        r = quantize_checkpoint(args.src, args.dst, args.method, group=args.group, calib_ids=calib,
+                                iters=args.iters, stages=args.stages)
+        print(f"wrote {args.dst} ({r['method']}: {r['linears']} linears quantized)")
     else:
         from .quant.fp8 import quantize_checkpoint_fp8
         quantize_checkpoint_fp8(args.src, args.dst)
@@ -115,26 +124,34 @@ def cmd_quantize(args):
 
 
 def cmd_dequantize(args):
-    """A GPTQ / AWQ 4-bit checkpoint directory -> dense bf16 safetensors (plus its config.json without
-    the quantization block), for tools that need plain weights."""
+    """A GPTQ / AWQ / AutoRound 4-bit or QuIP checkpoint directory -> dense bf16 safetensors (plus its
+    config.json without the quantization block), for tools that need plain weights."""
     import shutil
 
     import torch
     from .loaders.safetensors import SafetensorsCheckpoint, save_sharded
-    from .quant.int4 import Int4Weight, quantized_checkpoint_getter
+    from .quant.int4 import QUANT_METHODS, Int4Weight, quantized_checkpoint_getter
     with open(os.path.join(args.src, "config.json")) as f:
         hf = json.load(f)
     qc = hf.get("quantization_config")
-    if not qc or qc.get("quant_method") not in ("awq", "gptq"):
-        raise SystemExit(f"{args.src}: no GPTQ/AWQ quantization_config in config.json")
+    if not qc or qc.get("quant_method") not in QUANT_METHODS:
+        raise SystemExit(f"{args.src}: no GPTQ / AWQ / AutoRound / QuIP quantization_config in config.json")
     ck = SafetensorsCheckpoint(args.src)
     get = quantized_checkpoint_getter(ck, qc)
+    keys = set(ck.keys())
     out, n_q = {}, 0
     for k in ck.keys():
-        if k.endswith((".qzeros", ".scales", ".g_idx")):
+        if k.endswith((".qzeros", ".scales", ".g_idx", ".zp")) or ".quip_codes" in k:
             continue
-        name = k[:-8] + ".weight" if k.endswith(".qweight") else k
+        if k.endswith(".scale") and k[:-6] + ".weight" in keys:  # AutoRound native scale
+            continue
+        if k.endswith(".quip_scales"):
+            name = k[:-len(".quip_scales")] + ".weight"
+        else:
+            name = k[:-8] + ".weight" if k.endswith(".qweight") else k
         v = get(name)
+        if qc.get("quant_method") == "quip" and k.endswith(".quip_scales"):
+            n_q += 1
         if isinstance(v, Int4Weight):
             v, n_q = v.dequantize(torch.float32), n_q + 1
         out[name] = v.to(torch.bfloat16) if v.is_floating_point() else v
@@ -253,9 +270,15 @@ def build_parser():
     q = sub.add_parser("quantize")
     q.add_argument("src")
     q.add_argument("dst")
-    q.add_argument("--type", default="Q4_K")
+    q.add_argument("--type", default="Q4_K", help="GGUF source: target ggml type or mixture")
+    q.add_argument("--method", default="fp8", choices=["fp8", "awq", "autoround", "quip"],
+                   help="safetensors source: block-scaled fp8, AWQ or AutoRound int4 (calibrated), QuIP lattice")
+    q.add_argument("--group", type=int, default=128, help="awq / autoround: input columns per scale")
+    q.add_argument("--iters", type=int, default=200, help="autoround: signed-gradient steps per linear")
+    q.add_argument("--stages", type=int, default=1, help="quip: 1 (2.25 bits per weight) or 2 (4.25)")
+    q.add_argument("--calib-file", default=None, help="awq / autoround: token ids, one sequence per line")
     q.set_defaults(fn=cmd_quantize)
-    dq = sub.add_parser("dequantize", help="GPTQ/AWQ checkpoint -> dense bf16 safetensors")
+    dq = sub.add_parser("dequantize", help="GPTQ / AWQ / AutoRound / QuIP checkpoint -> dense bf16 safetensors")
     dq.add_argument("src")
     dq.add_argument("dst")
     dq.set_defaults(fn=cmd_dequantize)

@@ -608,8 +608,8 @@ def load_model_source(source: str, keep_quantized: bool = False):
         with open(os.path.join(d, "config.json")) as fh:
             qc = json.load(fh).get("quantization_config") or {}
         getter = ck.get
-        if qc.get("quant_method") in ("awq", "gptq"):
-            from ..quant.int4 import quantized_checkpoint_getter
+        from ..quant.int4 import QUANT_METHODS, quantized_checkpoint_getter
+        if qc.get("quant_method") in QUANT_METHODS:
             getter = quantized_checkpoint_getter(ck, qc)
         return cfg, getter, load_tokenizer(d)
     raise ValueError(f"unknown model source {source!r}")

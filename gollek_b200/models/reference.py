@@ -326,6 +326,9 @@ class ReferenceDecoder:
     def __init__(self, cfg: ModelConfig, weights: Weights):
         self.cfg = cfg
         self.w = {k: v.float() for k, v in weights.items()}
+        # capture(layer, site, x): called with the input rows of the dense linears of the standard
+        # decoder layer, site in {"qkv", "o", "gate_up", "down"} (offline quantizer calibration)
+        self.capture = None
         n = max(cfg.max_position_embeddings, 4096)
         self.cos_sin = rope_cos_sin(cfg, n)
         self.cos_sin_local = rope_cos_sin(cfg, n, theta=cfg.rope_local_theta) if cfg.rope_local_theta else None
@@ -361,6 +364,8 @@ class ReferenceDecoder:
                 x = rms_norm_ref(h, L["post_norm"], eps, uo)
                 h = h + self._ffn(x, L, i)
                 continue
+            if self.capture is not None:
+                self.capture(i, "qkv", x)
             q = x @ L["q"].t()
             k = x @ L["k"].t()
             v = x @ L["v"].t()
@@ -383,6 +388,8 @@ class ReferenceDecoder:
                 c = cfg.attn_logit_softcapping
                 s = c * torch.tanh(s / c)
             a = torch.einsum("hqk,khd->qhd", torch.softmax(s + mask, -1), v).reshape(S, H * D)
+            if self.capture is not None:
+                self.capture(i, "o", a)
             a = a @ L["o"].t()
             if cfg.parallel_block:  # attention and MLP both read x (one norm per layer)
                 h = h + a + self._ffn(x, L, i)
@@ -444,10 +451,15 @@ class ReferenceDecoder:
                 g, u, d = M["shared"]
                 out = out + (torch.nn.functional.silu(x @ g.t()) * (x @ u.t())) @ d.t()
             return out
+        if self.capture is not None:
+            self.capture(i, "gate_up", x)
         g = x @ L["gate"].t()
         act = torch.nn.functional.silu(g) if cfg.hidden_act == "silu" else \
             torch.nn.functional.gelu(g, approximate="tanh")
-        return (act * (x @ L["up"].t())) @ L["down"].t()
+        hmid = act * (x @ L["up"].t())
+        if self.capture is not None:
+            self.capture(i, "down", hmid)
+        return hmid @ L["down"].t()
 
     def _gdn(self, x: torch.Tensor, L: dict) -> torch.Tensor:
         """Gated delta rule layer over the whole sequence (fresh state)."""

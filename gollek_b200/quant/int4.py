@@ -234,10 +234,48 @@ def from_gptq(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
                       zeros.t().to(torch.bfloat16).contiguous(), N, K, group)
 
 
+QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip")
+
+
 def quantized_checkpoint_getter(ck, quant_config: dict):
-    """Wrap a checkpoint reader so that ``get("….weight")`` of a GPTQ/AWQ-quantized linear returns
-    an ``Int4Weight`` (or bf16 for act-order GPTQ) built from its qweight/qzeros/scales."""
+    """Wrap a checkpoint reader so that ``get("….weight")`` of a quantized linear returns an
+    ``Int4Weight`` (or bf16 for act-order GPTQ): GPTQ / AWQ from qweight / qzeros / scales; AutoRound
+    from its native weight / scale / zp tensors or from GPTQ-named ones; QuIP (``quant/quip.py``) from
+    its lattice codes, dequantized to bf16 here."""
     method = quant_config.get("quant_method")
+    if method == "quip":
+        from .quip import QuipWeight
+        stages, seed = int(quant_config.get("stages", 1)), int(quant_config.get("seed", 0))
+        keys_q = set(ck.keys())
+
+        def get_quip(name: str):
+            base = name[:-7] if name.endswith(".weight") else name
+            if base + ".quip_scales" in keys_q:
+                sc = ck.get(base + ".quip_scales")
+                codes = [ck.get(f"{base}.quip_codes{i}") for i in range(stages)]
+                N, K = sc.shape[0], codes[0].shape[1] * 8
+                return QuipWeight(codes, sc, N, K, seed).dequantize(torch.float32).to(torch.bfloat16)
+            return ck.get(name)
+        return get_quip
+    if method in ("auto-round", "autoround", "intel/auto-round"):
+        from .autoround import from_autoround
+        group_ar = int(quant_config.get("group_size", 128))
+        if int(quant_config.get("bits", 4)) != 4:
+            raise ValueError(f"{method}: only 4-bit checkpoints are supported")
+        keys_ar = set(ck.keys())
+
+        def get_ar(name: str):
+            if name.endswith(".weight"):
+                base = name[:-7]
+                if base + ".scale" in keys_ar:  # native naming: the packed int32 words under .weight
+                    zp = ck.get(base + ".zp") if base + ".zp" in keys_ar else None
+                    return from_autoround(ck.get(name), ck.get(base + ".scale"), zp, group_ar)
+                if base + ".qweight" in keys_ar:
+                    g_idx = ck.get(base + ".g_idx") if base + ".g_idx" in keys_ar else None
+                    return from_gptq(ck.get(base + ".qweight"), ck.get(base + ".qzeros"), ck.get(base + ".scales"),
+                                     group_ar, g_idx)
+            return ck.get(name)
+        return get_ar
     bits = int(quant_config.get("bits", quant_config.get("w_bit", 4)))
     group = int(quant_config.get("group_size", quant_config.get("q_group_size", 128)))
     if bits != 4:

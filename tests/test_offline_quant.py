@@ -1,0 +1,135 @@
+"""Offline quantizers: QuIP#-style lattice codes, AutoRound, AWQ scale search, and the checkpoint
+pipeline that writes what the engine serves (CPU)."""
+import json
+
+import pytest
+import torch
+
+from gollek_b200.config import preset
+from gollek_b200.loaders.safetensors import save_file
+from gollek_b200.models.reference import ReferenceDecoder, init_random_weights
+from gollek_b200.quant import quip as Q
+from gollek_b200.quant.autoround import from_autoround, quantize_autoround, to_autoround
+from gollek_b200.quant.awq import awq_search, to_awq
+from gollek_b200.quant.int4 import Int4Weight, from_awq, quantize_rtn
+
+
+def _rel(a, b):
+    return float((a - b).norm() / b.norm())
+
+
+def test_e8_codebook_and_nearest_point():
+    cb = Q.codebook()
+    assert cb.shape == (56881, 8)  # 1 + 240 + 2160 + 6720 + 17520 + 30240 points of squared norm <= 10
+    n2 = (cb ** 2).sum(1)
+    assert sorted(set(n2.tolist())) == [0.0, 2.0, 4.0, 6.0, 8.0, 10.0]
+    x = torch.randn(3000, 8, generator=torch.Generator().manual_seed(1))
+    p = Q.nearest_e8(x)
+    bf = cb[((x[:, None, :] - cb[None]) ** 2).sum(-1).argmin(1)]
+    inside = (p * p).sum(1) <= 10
+    assert inside.sum() > 2000 and torch.equal(p[inside], bf[inside])
+    assert torch.equal(cb[Q._index(bf)], bf)
+
+
+@pytest.mark.parametrize("N,K", [(256, 1792), (96, 512)])
+def test_quip_roundtrip_and_error(N, K):
+    g = torch.Generator().manual_seed(N)
+    w = torch.randn(N, K, generator=g) * 0.02
+    w[3, 5] = 0.5  # an outlier: spread by the incoherence transform
+    assert _rel(Q.coherent(Q.incoherent(w, 4), 4), w) < 1e-5
+    q1, q2 = Q.quantize_quip(w, stages=1, seed=4), Q.quantize_quip(w, stages=2, seed=4)
+    assert q1.bits_per_weight() == pytest.approx(2.25) and q2.bits_per_weight() == pytest.approx(4.25)
+    e1, e2 = _rel(q1.dequantize(), w), _rel(q2.dequantize(), w)
+    assert e1 < 0.34 and e2 < 0.12 and e2 < e1 / 2.5
+
+
+def test_autoround_lowers_output_error_and_native_format():
+    g = torch.Generator().manual_seed(0)
+    N, K = 128, 512
+    W = torch.randn(N, K, generator=g) * 0.02
+    X = torch.randn(768, K, generator=g)
+    X[:, :8] *= 10  # a few large activation channels
+    ref = X @ W.t()
+    oerr = lambda q: _rel(X @ q.dequantize().t(), ref)  # noqa: E731
+    q = quantize_autoround(W, X, 128, iters=150)
+    assert oerr(q) < 0.95 * oerr(quantize_rtn(W, 128))
+    t = to_autoround(q)
+    assert t["weight"].dtype == torch.int32 and t["weight"].shape == (N // 8, K) and t["zp"].dtype == torch.int32
+    assert torch.equal(from_autoround(t["weight"], t["scale"], t["zp"], 128).dequantize(), q.dequantize())
+    sym = from_autoround(t["weight"], t["scale"], None, 128)  # symmetric checkpoints: zero point 8
+    assert torch.equal(sym.zero.float(), torch.full_like(sym.zero.float(), 8.0))
+
+
+def test_awq_search_lowers_output_error_and_awq_format():
+    g = torch.Generator().manual_seed(2)
+    K = 512
+    Ws = [torch.randn(n, K, generator=g) * 0.02 for n in (256, 128)]
+    X = torch.randn(1024, K, generator=g)
+    X[:, 100:104] *= 30
+    s, qs = awq_search(Ws, X, 128)
+    err = sum(float(((X @ (q.dequantize() / s[None]).t() - X @ w.t()) ** 2).sum()) for q, w in zip(qs, Ws))
+    err_rtn = sum(float(((X @ quantize_rtn(w, 128).dequantize().t() - X @ w.t()) ** 2).sum()) for w in Ws)
+    assert err < 0.9 * err_rtn
+    t = to_awq(qs[0])
+    back = from_awq(t["qweight"], t["qzeros"], t["scales"].float(), 128)
+    torch.testing.assert_close(back.dequantize(), qs[0].dequantize(), rtol=1e-2, atol=1e-4)  # fp16 scales
+
+
+@pytest.mark.parametrize("method", ["awq", "autoround", "quip"])
+def test_quantize_checkpoint_serves(tmp_path, method):
+    """A small Llama-family checkpoint quantized by each method: the engine loads it (int4 weights for
+    AWQ / AutoRound, bf16 for QuIP), the dense model rebuilt from what it loads stays close to the fp32
+    model, and the engine decodes from it."""
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine, load_model_source
+    from gollek_b200.engine.sequence import SamplingParams
+    from gollek_b200.quant.offline import quantize_checkpoint
+    cfg = preset("tiny-llama", intermediate_size=512, num_hidden_layers=2)
+    w = init_random_weights(cfg, seed=0)
+    src, dst = tmp_path / "src", tmp_path / "dst"
+    src.mkdir()
+    save_file(w, str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps(cfg.to_hf()))
+    summary = quantize_checkpoint(str(src), str(dst), method, group=64, calib_seqs=2, calib_len=64, iters=60,
+                                  stages=2 if method == "quip" else 1)
+    assert summary["linears"] == 7 * cfg.num_hidden_layers
+    qcfg, get, _ = load_model_source(str(dst))
+    dense = {}
+    for k in w:
+        v = get(k)
+        if isinstance(v, Int4Weight):
+            assert method in ("awq", "autoround")
+            v = v.dequantize(torch.float32)
+        dense[k] = v.float()
+    ids = torch.randint(0, cfg.vocab_size, (48,), generator=torch.Generator().manual_seed(7))
+    lf = ReferenceDecoder(cfg, w).forward(ids)
+    lq = ReferenceDecoder(cfg, dense).forward(ids)
+    assert _rel(lq, lf) < 0.2, _rel(lq, lf)
+    ec = EngineConfig(device="cpu", dtype="float32", block_size=16, max_num_seqs=2, max_num_batched_tokens=128,
+                      max_model_len=128, use_cuda_graphs=False)
+    eng = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=16)
+    out = eng.generate([ids[:20].tolist()], SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True))[0]
+    assert len(out.output_token_ids) == 4
+
+
+@pytest.mark.parametrize("method", ["autoround", "quip"])
+def test_cli_quantize_then_dequantize(tmp_path, method):
+    """``gollek quantize --method`` then ``gollek dequantize``: a dense bf16 checkpoint with every
+    original tensor name, close to the original weights."""
+    import argparse
+    from gollek_b200 import cli
+    from gollek_b200.loaders.safetensors import SafetensorsCheckpoint
+    cfg = preset("tiny-llama", intermediate_size=512, num_hidden_layers=1)
+    w = init_random_weights(cfg, seed=1)
+    src = tmp_path / "src"
+    src.mkdir()
+    save_file(w, str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps(cfg.to_hf()))
+    cli.cmd_quantize(argparse.Namespace(src=str(src), dst=str(tmp_path / "q"), method=method, group=64, iters=20,
+                                        stages=2, calib_file=None, type="Q4_K"))
+    cli.cmd_dequantize(argparse.Namespace(src=str(tmp_path / "q"), dst=str(tmp_path / "dq")))
+    ck = SafetensorsCheckpoint(str(tmp_path / "dq"))
+    assert set(ck.keys()) == set(w.keys())
+    k = "model.layers.0.mlp.down_proj.weight"
+    assert ck.get(k).dtype == torch.bfloat16 and _rel(ck.get(k).float(), w[k].float()) < 0.2
+    assert "quantization_config" not in json.loads((tmp_path / "dq" / "config.json").read_text())
