@@ -507,9 +507,9 @@ class LLMEngine:
         return outputs
 
     # ------------------------------------------------------------------ checkpoint / resume
-    def save_prefix_cache(self, path: str, max_blocks: int = 0) -> int:
+    def save_prefix_cache(self, path: str, max_blocks: int = 0, compress: str = "") -> int:
         from .persistence import save_prefix_cache
-        return save_prefix_cache(self, path, max_blocks)
+        return save_prefix_cache(self, path, max_blocks, compress)
 
     def load_prefix_cache(self, path: str) -> int:
         from .persistence import load_prefix_cache

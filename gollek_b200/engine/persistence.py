@@ -30,8 +30,44 @@ def _signature(engine) -> dict:
             "tp_rank": engine.comm.rank, "tp_size": engine.comm.size, "vocab": m.cfg.vocab_size}
 
 
-def save_prefix_cache(engine, path: str, max_blocks: int = 0) -> int:
-    """Write the engine's cached prefix blocks to ``path``; returns the number of blocks saved."""
+def _tq_save(kv: torch.Tensor, bits: int) -> dict:
+    """KV [L, n, 2, Hk, bs, D] -> TurboQuant tensors per (layer, K/V, head): every token's vector of
+    that head, the D/4 channels of largest RMS at bits + 1 and the rest at ``bits``."""
+    from ..quant.turboquant import quantize_kv
+    L, n, _, Hk, bs, D = kv.shape
+    out = {}
+    for layer in range(L):
+        for kvi in range(2):
+            for h in range(Hk):
+                q = quantize_kv(kv[layer, :, kvi, h].reshape(n * bs, D).float().cpu(), bits, D // 4)
+                p = f"tq.{layer}.{kvi}.{h}."
+                out[p + "idx"] = q.outlier_idx
+                for part, d in (("hi", q.hi), ("lo", q.lo)):
+                    out[p + part + "_codes"] = d["codes"]
+                    out[p + part + "_norm"] = d["norm"]
+    return out
+
+
+def _tq_load(f, rows, L: int, Hk: int, bs: int, D: int, bits: int, n: int) -> torch.Tensor:
+    """Rows ``rows`` of the snapshot's n blocks -> KV [L, len(rows), 2, Hk, bs, D] (fp32)."""
+    from ..quant.turboquant import KVQuantized, dequantize_kv
+    out = torch.empty(L, len(rows), 2, Hk, bs, D)
+    r = torch.tensor(rows)
+    for layer in range(L):
+        for kvi in range(2):
+            for h in range(Hk):
+                p = f"tq.{layer}.{kvi}.{h}."
+                q = KVQuantized(f.get(p + "idx"), {"codes": f.get(p + "hi_codes"), "norm": f.get(p + "hi_norm")},
+                                {"codes": f.get(p + "lo_codes"), "norm": f.get(p + "lo_norm")}, D, bits)
+                out[layer, :, kvi, h] = dequantize_kv(q).view(n, bs, D)[r]
+    return out
+
+
+def save_prefix_cache(engine, path: str, max_blocks: int = 0, compress: str = "") -> int:
+    """Write the engine's cached prefix blocks to ``path``; returns the number of blocks saved.
+    ``compress="turboquant"`` stores the KV at 2.5 bits per value (``quant/turboquant.py``, 6.4x
+    smaller than bf16); the blocks restored from it are approximate, so outputs that use them can
+    differ slightly from a recomputation."""
     items = engine.kv.pool.cached_items()
     if max_blocks:
         items = items[:max_blocks]
@@ -43,8 +79,15 @@ def save_prefix_cache(engine, path: str, max_blocks: int = 0) -> int:
     if getattr(engine.model, "kv_scales", None) is not None:
         raise ValueError("moving KV blocks of an fp8 cache (values + per-token scales) is not supported")
     kv = ops.kv_gather_blocks(engine.kv_cache, ids.to(engine.kv_cache.device))  # [L, n, 2, Hk, bs, D]
-    save_file({"hashes": hashes, "kv": kv.transpose(0, 1).contiguous().cpu()}, path,
-              {"signature": json.dumps(_signature(engine))})
+    meta = {"signature": json.dumps(_signature(engine))}
+    if compress == "turboquant":
+        tensors = {"hashes": hashes, **_tq_save(kv, 2)}
+        meta.update(compress="turboquant", bits="2", shape=json.dumps(list(kv.shape)))
+    elif compress:
+        raise ValueError(f"unknown KV compression {compress!r} (turboquant)")
+    else:
+        tensors = {"hashes": hashes, "kv": kv.transpose(0, 1).contiguous().cpu()}
+    save_file(tensors, path, meta)
     return len(items)
 
 
@@ -59,7 +102,8 @@ def load_prefix_cache(engine, path: str) -> int:
         hashes = f.get("hashes").tolist()
         if not hashes:
             return 0
-        kv = f.get("kv")  # [n, L, 2, Hk, bs, D]
+        compressed = f.metadata.get("compress") == "turboquant"
+        kv = None if compressed else f.get("kv")  # [n, L, 2, Hk, bs, D]
         taken, rows = [], []
         for i, h in enumerate(hashes):
             b = engine.kv.pool.adopt_cached(int(h))
@@ -70,7 +114,11 @@ def load_prefix_cache(engine, path: str) -> int:
             taken.append(b)
             rows.append(i)
         if taken:
-            sel = kv[torch.tensor(rows)].transpose(0, 1).contiguous()  # a copy: the mapping can close
+            if compressed:
+                L, n, _, Hk, bs, D = json.loads(f.metadata["shape"])
+                sel = _tq_load(f, rows, L, Hk, bs, D, int(f.metadata["bits"]), n)
+            else:
+                sel = kv[torch.tensor(rows)].transpose(0, 1).contiguous()  # a copy: the mapping can close
             ops.kv_scatter_blocks(engine.kv_cache, torch.tensor(taken, dtype=torch.int32).to(engine.kv_cache.device),
                                   sel.to(engine.kv_cache.device, engine.kv_cache.dtype))
             del sel
