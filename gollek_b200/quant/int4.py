@@ -234,7 +234,7 @@ def from_gptq(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
                       zeros.t().to(torch.bfloat16).contiguous(), N, K, group)
 
 
-QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip")
+QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip", "bitsandbytes")
 
 
 def quantized_checkpoint_getter(ck, quant_config: dict):
@@ -243,6 +243,9 @@ def quantized_checkpoint_getter(ck, quant_config: dict):
     from its native weight / scale / zp tensors or from GPTQ-named ones; QuIP (``quant/quip.py``) from
     its lattice codes, dequantized to bf16 here."""
     method = quant_config.get("quant_method")
+    if method == "bitsandbytes":
+        from .bnb import bnb_getter
+        return bnb_getter(ck)
     if method == "quip":
         from .quip import QuipWeight
         stages, seed = int(quant_config.get("stages", 1)), int(quant_config.get("seed", 0))

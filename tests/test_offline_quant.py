@@ -159,3 +159,51 @@ def test_turboquant_distortion_unbiased_inner_products_and_kv_split():
     assert 8 * qk.nbytes() / kv.numel() == pytest.approx(2.5, abs=0.02)
     u = T.TurboQuantMSE(128, 2)
     assert _rel(T.dequantize_kv(qk), kv) < 0.7 * _rel(u.dequantize(u.quantize(kv)), kv)
+
+
+@pytest.mark.parametrize("double_quant", [False, True])
+def test_bitsandbytes_checkpoint_loading(tmp_path, double_quant):
+    """bitsandbytes-serialized NF4 (plain and double-quantized statistics), FP4-style code maps and
+    LLM.int8 rows: NF4 loads as an NF4 Int4Weight (served by the int4 kernels), the others as bf16,
+    all close to the original matrix; the engine decodes from such a checkpoint."""
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine, load_model_source
+    from gollek_b200.engine.sequence import SamplingParams
+    from gollek_b200.quant.bnb import to_bnb4
+    cfg = preset("tiny-llama", intermediate_size=512, num_hidden_layers=1)
+    w = init_random_weights(cfg, seed=3)
+    out = {}
+    fp4_map = torch.tensor([0.0, 0.0052, 0.6667, 1.0, 0.3333, 0.5, 0.1667, 0.25,
+                            -0.0, -0.0052, -0.6667, -1.0, -0.3333, -0.5, -0.1667, -0.25])
+    for k, v in w.items():
+        if k.endswith("proj.weight"):
+            if "o_proj" in k:  # LLM.int8 rows
+                scb = v.float().abs().amax(1)
+                out[k] = torch.round(v.float() / scb[:, None] * 127).to(torch.int8)
+                out[k[:-7] + ".SCB"] = scb
+            else:
+                qm = fp4_map if "down_proj" in k else None
+                for suf, t in to_bnb4(v, 64, qm, double_quant, "fp4" if qm is not None else "nf4").items():
+                    out[k + suf] = t
+        else:
+            out[k] = v
+    d = tmp_path / "bnb"
+    d.mkdir()
+    save_file(out, str(d / "model.safetensors"))
+    hf = cfg.to_hf()
+    hf["quantization_config"] = {"quant_method": "bitsandbytes", "load_in_4bit": True, "bnb_4bit_quant_type": "nf4",
+                                 "bnb_4bit_use_double_quant": double_quant}
+    (d / "config.json").write_text(json.dumps(hf))
+    qcfg, get, _ = load_model_source(str(d))
+    g = get("model.layers.0.mlp.gate_proj.weight")
+    assert isinstance(g, Int4Weight) and g.nf4 and g.group == 64
+    for n, tol in (("mlp.gate_proj", 0.12), ("mlp.down_proj", 0.35), ("self_attn.o_proj", 0.02)):
+        k = f"model.layers.0.{n}.weight"
+        v = get(k)
+        v = v.dequantize() if isinstance(v, Int4Weight) else v.float()
+        assert _rel(v, w[k].float()) < tol, (n, _rel(v, w[k].float()))
+    ec = EngineConfig(device="cpu", dtype="float32", block_size=16, max_num_seqs=2, max_num_batched_tokens=64,
+                      max_model_len=64, use_cuda_graphs=False)
+    eng = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=8)
+    outp = eng.generate([[5, 6, 7, 8]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
+    assert len(outp.output_token_ids) == 3
