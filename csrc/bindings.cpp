@@ -177,12 +177,13 @@ void paged_prefill_attention_out(torch::Tensor out, torch::Tensor q, torch::Tens
               "out must be [T, H, D]");
   TORCH_CHECK(cache.is_contiguous() && cache.dim() == 5 && cache.size(4) == q.size(2), "cache [NB, 2, Hk, bs, D]");
   TORCH_CHECK(block_tables.stride(1) == 1 && tiles.is_contiguous() && query_start.is_contiguous(), "metadata layout");
-  if (tensor_cores && q.size(2) == 128 && cache.size(3) == 16 && tiles.dim() == 2 && tiles.size(1) == 4) {
+  if (tensor_cores && (q.size(2) == 128 || q.size(2) == 64) && cache.size(3) == 16 && tiles.dim() == 2 &&
+      tiles.size(1) == 4) {
     launch_paged_prefill_fa(out.data_ptr(), out.stride(0), q.data_ptr(), q.size(0), q.stride(0), cache.data_ptr(),
                             cache.size(0), block_tables.data_ptr<int>(), block_tables.stride(0),
                             seq_lens.data_ptr<int>(), query_start.data_ptr<int>(), tiles.data_ptr<int>(),
                             tiles.size(0), q.size(1), cache.size(2), (float)scale, (int)window, (float)softcap,
-                            (int)emu, cur_stream());
+                            (int)emu, cur_stream(), (int)q.size(2));
     return;
   }
   if (tensor_cores && q.size(2) == 128 && cache.size(3) == 16) {

@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // on the FMA pipe instead of MUFU (EMU 1: every 4th column, 2: every 2nd).
 // ---------------------------------------------------------------------------------------------
 constexpr int kFaThreads = 320;
-constexpr int kFaSmem = 1024 + 2 * kQBytes + kStages * 2 * kKVTile + 256;
+constexpr int fa_smem(int hd) { return 1024 + 2 * kTQ * hd * 2 + kStages * 2 * kTK * hd * 2 + 256; }
 
 GOLLEK_DEVICE float ex2_mufu(float x) {
   float y;
@@ -464,18 +464,22 @@ GOLLEK_DEVICE FaItem fa_item(const int4* __restrict__ work, int w, const int* __
 // and first KV tiles load, and its first S MMAs run, while the softmax warps still normalise and store
 // the previous item's O: q_empty (committed after an item's last S MMA) frees the Q buffer, o_free[i]
 // (the slot's four softmax warps, after reading O_i) lets the next item's first PV overwrite O_i.
-template <int EMU>
+template <int EMU, int HD>
 __global__ void __launch_bounds__(kFaThreads, 1)
     prefill_fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                       __nv_bfloat16* __restrict__ out, int64_t out_stride, const int* __restrict__ block_tables,
                       int bt_stride, const int* __restrict__ seq_lens, const int* __restrict__ query_start,
                       const int4* __restrict__ work, int nwork, int H, int Hk, float scale_log2,
                       uint32_t* status, int window, float softcap_log2, int num_blocks) {
+  // head size HD (64 or 128): Q / K / V tiles are HD / 64 boxes of 64 dims (128-byte swizzle), each
+  // box 128 rows x 128 bytes
+  constexpr int QB = kTQ * HD * 2, KVT = kTK * HD * 2, NBOX = HD / 64;
+  constexpr int BOXQ = kTQ * 64 * 2, BOXK = kTK * 64 * 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sQ = smem;                          // slot i at + i * kQBytes
-  uint8_t* sKV = sQ + 2 * kQBytes;             // stage s: K at + s*2*tile, V at + s*2*tile + tile
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * 2 * kKVTile);
+  uint8_t* sQ = smem;                          // slot i at + i * QB
+  uint8_t* sKV = sQ + 2 * QB;             // stage s: K at + s*2*tile, V at + s*2*tile + tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * 2 * KVT);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;                 // [2]
   uint64_t* v_full = bars + 3;                 // [2]
@@ -533,13 +537,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           break;
         }
         const bool v0 = it.sl[0].b > it.sl[0].a, v1 = it.sl[1].b > it.sl[1].a;
-        mbar_arrive_expect_tx(q_full, ((v0 ? 1 : 0) + (v1 ? 1 : 0)) * kQBytes);
+        mbar_arrive_expect_tx(q_full, ((v0 ? 1 : 0) + (v1 ? 1 : 0)) * QB);
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           if (it.sl[i].b > it.sl[i].a) {
             const int qrow = it.qs + it.sl[i].q_off;
-            tma_load_2d(sQ + i * kQBytes, &tmQ, it.sl[i].h * kD, qrow, q_full);
-            tma_load_2d(sQ + i * kQBytes + kQBytes / 2, &tmQ, it.sl[i].h * kD + 64, qrow, q_full);
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx)
+              tma_load_2d(sQ + i * QB + bx * BOXQ, &tmQ, it.sl[i].h * HD + 64 * bx, qrow, q_full);
           }
         }
         ++nq;
@@ -549,23 +554,23 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* dk = sKV + st * 2 * kKVTile;
-          uint8_t* dv = dk + kKVTile;
-          mbar_arrive_expect_tx(&k_full[st], kKVTile);
+          uint8_t* dk = sKV + st * 2 * KVT;
+          uint8_t* dv = dk + KVT;
+          mbar_arrive_expect_tx(&k_full[st], KVT);
           for (int blk = 0; blk < kTK / kBS; ++blk) {
             const int kb = (j * kTK) / kBS + blk;
             const int pb = checked_index((kb * kBS < it.kv_end) ? it.bt[kb] : it.bt[0], num_blocks, status);
             const int rk = ((pb * 2 + 0) * Hk + it.kh) * kBS;
-            tma_load_2d(dk + blk * 2048, &tmKV, 0, rk, &k_full[st]);
-            tma_load_2d(dk + kKVTile / 2 + blk * 2048, &tmKV, 64, rk, &k_full[st]);
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx) tma_load_2d(dk + bx * BOXK + blk * 2048, &tmKV, 64 * bx, rk, &k_full[st]);
           }
-          mbar_arrive_expect_tx(&v_full[st], kKVTile);
+          mbar_arrive_expect_tx(&v_full[st], KVT);
           for (int blk = 0; blk < kTK / kBS; ++blk) {
             const int kb = (j * kTK) / kBS + blk;
             const int pb = checked_index((kb * kBS < it.kv_end) ? it.bt[kb] : it.bt[0], num_blocks, status);
             const int rv = ((pb * 2 + 1) * Hk + it.kh) * kBS;
-            tma_load_2d(dv + blk * 2048, &tmKV, 0, rv, &v_full[st]);
-            tma_load_2d(dv + kKVTile / 2 + blk * 2048, &tmKV, 64, rv, &v_full[st]);
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx) tma_load_2d(dv + bx * BOXK + blk * 2048, &tmKV, 64 * bx, rv, &v_full[st]);
           }
         }
       }
@@ -580,7 +585,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   } else if (warp == 9) {
     if (elect_one()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(kTQ, kTK);              // Q K^T, both K-major
-      constexpr uint32_t idesc_o = make_idesc_bf16(kTQ, kD) | (1u << 16);  // P (TMEM) V, V MN-major
+      constexpr uint32_t idesc_o = make_idesc_bf16(kTQ, HD) | (1u << 16);  // P (TMEM) V, V MN-major
       int g = 0, nq = 0;
       int np[2] = {0, 0};  // P tiles consumed per slot
       int no[2] = {0, 0};  // items finished per slot (O handed to the epilogue)
@@ -606,7 +611,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const FaSlot& t = it.sl[i];
-            const uint32_t tS = tmem + i * kTK, tO = tmem + 256 + i * kD;
+            const uint32_t tS = tmem + i * kTK, tO = tmem + 256 + i * HD;
             if (prev && j - 1 >= t.a && j - 1 < t.b) {
               if (!waitq(&p_full[i], np[i] & 1, status, abort_flag)) {
                 ok = false;
@@ -619,10 +624,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 break;
               }
               tcgen05_fence_after();
-              const uint32_t v_addr = smem_u32(sKV + ((gi - 1) & 1) * 2 * kKVTile + kKVTile);
+              const uint32_t v_addr = smem_u32(sKV + ((gi - 1) & 1) * 2 * KVT + KVT);
 #pragma unroll
               for (int ks = 0; ks < kTK / 16; ++ks)
-                umma_f16_ts(tO, tS + ks * 8, make_desc_mn_sw128(v_addr + ks * 2048, kKVTile / 2), idesc_o,
+                umma_f16_ts(tO, tS + ks * 8, make_desc_mn_sw128(v_addr + ks * 2048, BOXK), idesc_o,
                             (j - 1 > t.a || ks > 0) ? 1u : 0u);
               if (j == t.b) {
                 umma_commit(&o_done[i]);
@@ -638,12 +643,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 tcgen05_fence_after();
                 k_ready = true;
               }
-              const uint32_t q_addr = smem_u32(sQ + i * kQBytes);
-              const uint32_t k_addr = smem_u32(sKV + (gi & 1) * 2 * kKVTile);
+              const uint32_t q_addr = smem_u32(sQ + i * QB);
+              const uint32_t k_addr = smem_u32(sKV + (gi & 1) * 2 * KVT);
 #pragma unroll
-              for (int ks = 0; ks < kD / 16; ++ks) {
-                const uint64_t a = make_smem_desc_sw128(q_addr + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
-                const uint64_t bd = make_smem_desc_sw128(k_addr + (ks >> 2) * (kKVTile / 2) + (ks & 3) * 32);
+              for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint64_t a = make_smem_desc_sw128(q_addr + (ks >> 2) * (BOXQ) + (ks & 3) * 32);
+                const uint64_t bd = make_smem_desc_sw128(k_addr + (ks >> 2) * (BOXK) + (ks & 3) * 32);
                 umma_f16_ss(tS, a, bd, idesc_s, ks > 0 ? 1u : 0u);
               }
               umma_commit(&s_full[i]);
@@ -667,7 +672,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int i = warp >> 2, lg = warp & 3;
     const int r = lg * 32 + lane;
     const uint32_t lane_off = (uint32_t)(lg * 32) << 16;
-    const uint32_t tS = tmem + i * kTK + lane_off, tO = tmem + 256 + i * kD + lane_off;
+    const uint32_t tS = tmem + i * kTK + lane_off, tO = tmem + 256 + i * HD + lane_off;
     const bool capped = softcap_log2 > 0.f;
     const float inv_cap = capped ? 1.f / softcap_log2 : 0.f;
     bool ok = true;
@@ -785,7 +790,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         l = l * corr + psum;
         if (__any_sync(0xffffffffu, corr != 1.f)) {  // O_i is quiescent: PV_i(j-1) completed before S_i(j)
 #pragma unroll 1
-          for (int c = 0; c < kD; c += 32) {
+          for (int c = 0; c < HD; c += 32) {
             uint32_t u[32];
             tmem_ld_32x32b_x32(tO + c, u);
             tmem_ld_wait();
@@ -806,10 +811,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       ++no;
       tcgen05_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = out + (int64_t)(it.qs + t.q_off + r) * out_stride + t.h * kD;
-      uint32_t u[kD];
+      __nv_bfloat16* dst = out + (int64_t)(it.qs + t.q_off + r) * out_stride + t.h * HD;
+      uint32_t u[HD];
 #pragma unroll
-      for (int c = 0; c < kD; c += 32) tmem_ld_32x32b_x32(tO + c, u + c);
+      for (int c = 0; c < HD; c += 32) tmem_ld_32x32b_x32(tO + c, u + c);
       tmem_ld_wait();
       // O_i is in registers: the next item's first PV may overwrite it
       tcgen05_fence_before();
@@ -817,7 +822,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       if (lane == 0) mbar_arrive(&o_free[i]);
       if (r < t.rows) {
 #pragma unroll
-        for (int e = 0; e < kD; e += 8) {
+        for (int e = 0; e < HD; e += 8) {
           float f[8];
 #pragma unroll
           for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(u[e + x]) * inv;
@@ -864,14 +869,15 @@ void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64
 void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* work, int nwork, int H, int Hk,
-                             float scale, int window, float softcap, int emu, cudaStream_t s) {
+                             float scale, int window, float softcap, int emu, cudaStream_t s, int head_dim) {
   throw_if(H % Hk != 0, "H must be a multiple of Hk");
   throw_if(q_stride % 8 != 0, "prefill: q row pitch must keep 16-byte alignment");
+  throw_if(head_dim != 64 && head_dim != 128, "two-tile tcgen05 prefill: head_dim 64 or 128");
   if (nwork == 0) return;
   const uint64_t kv_rows = (uint64_t)num_blocks * 2 * Hk * kBS;
-  CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, (uint64_t)H * kD, q_stride, kTQ, 64,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tkv = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, kBS, 64,
+  CUtensorMap tq = make_tmap_2d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q_rows, (uint64_t)H * head_dim, q_stride, kTQ,
+                                64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tkv = make_tmap_2d(cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, head_dim, head_dim, kBS, 64,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
   // one CTA per SM looping over the items; GOLLEK_PREFILL_PERSISTENT=0: one CTA per item
   const char* pe = getenv("GOLLEK_PREFILL_PERSISTENT");
@@ -879,20 +885,30 @@ void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64
   const float sl2 = scale * 1.4426950408889634f, cap = softcap > 0.f ? softcap * 1.4426950408889634f : 0.f;
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   auto* w4 = reinterpret_cast<const int4*>(work);
-#define GOLLEK_FA_LAUNCH(E)                                                                                        \
+#define GOLLEK_FA_LAUNCH(E, HDV)                                                                                   \
   do {                                                                                                             \
-    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(prefill_fa_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                           kFaSmem));                                                              \
-    prefill_fa_kernel<E><<<grid, kFaThreads, kFaSmem, s>>>(tq, tkv, o, out_stride, block_tables, bt_stride,        \
-                                                           seq_lens, query_start, w4, nwork, H, Hk,                \
-                                                           sl2, bounds_status(), window, cap, num_blocks);         \
+    GOLLEK_CUDA_CHECK(cudaFuncSetAttribute(prefill_fa_kernel<E, HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                           fa_smem(HDV)));                                                         \
+    prefill_fa_kernel<E, HDV><<<grid, kFaThreads, fa_smem(HDV), s>>>(tq, tkv, o, out_stride, block_tables,         \
+                                                                     bt_stride, seq_lens, query_start, w4, nwork,  \
+                                                                     H, Hk, sl2, bounds_status(), window, cap,     \
+                                                                     num_blocks);                                  \
   } while (0)
-  if (emu == 2)
-    GOLLEK_FA_LAUNCH(2);
-  else if (emu == 1)
-    GOLLEK_FA_LAUNCH(1);
-  else
-    GOLLEK_FA_LAUNCH(0);
+  if (head_dim == 64) {
+    if (emu == 2)
+      GOLLEK_FA_LAUNCH(2, 64);
+    else if (emu == 1)
+      GOLLEK_FA_LAUNCH(1, 64);
+    else
+      GOLLEK_FA_LAUNCH(0, 64);
+  } else {
+    if (emu == 2)
+      GOLLEK_FA_LAUNCH(2, 128);
+    else if (emu == 1)
+      GOLLEK_FA_LAUNCH(1, 128);
+    else
+      GOLLEK_FA_LAUNCH(0, 128);
+  }
 #undef GOLLEK_FA_LAUNCH
   check_launch("paged_prefill_attention (tcgen05, two-tile)");
 }

@@ -51,14 +51,14 @@ void launch_paged_prefill_tc(void* out, int64_t out_stride, const void* q, int64
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* tiles, int ntiles, int H,
                              int Hk, float scale, int window, float softcap, cudaStream_t s);
-// Two-tile tcgen05 prefill (head_dim 128, block 16). work: one int4 per CTA (sequence, query offset of
+// Two-tile tcgen05 prefill (head_dim 64 or 128, block 16). work: one int4 per CTA (sequence, query offset of
 // slot 0, query offset of slot 1 or -1, (pair << 16) | head): pair = 1 runs heads head and head + 1 (one
 // GQA group, so the group size must be even) over the same query rows; pair = 0 runs two query tiles
 // of one head. emu: share of exponentials on the FMA pipe (0 none, 1 a quarter, 2 half).
 void launch_paged_prefill_fa(void* out, int64_t out_stride, const void* q, int64_t q_rows, int64_t q_stride,
                              const void* cache, int num_blocks, const int* block_tables, int bt_stride,
                              const int* seq_lens, const int* query_start, const int* work, int nwork, int H, int Hk,
-                             float scale, int window, float softcap, int emu, cudaStream_t s);
+                             float scale, int window, float softcap, int emu, cudaStream_t s, int head_dim = 128);
 void launch_paged_prefill(void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* cache,
                           const int* block_tables, int bt_stride, const int* seq_lens, const int* query_start,
                           const int* tiles, int ntiles, int H, int Hk, int D, int block_size, float scale,

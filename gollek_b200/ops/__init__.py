@@ -241,8 +241,9 @@ def kv_dequant_blocks(cache: torch.Tensor, scales: torch.Tensor, block_tables: t
 
 
 def prefill_block_m(head_dim: int, tensor_cores: bool = True) -> int:
-    """Query rows per CTA of the prefill kernel (128 on the tcgen05 path, 64 on the mma.sync path)."""
-    return 128 if (tensor_cores and head_dim == 128) else 64
+    """Query rows per CTA of the prefill kernel (128 on the tcgen05 path for head_dim 64 / 128, 64 on
+    the mma.sync path)."""
+    return 128 if (tensor_cores and head_dim in (64, 128)) else 64
 
 
 def prefill_tiles(query_start: list, block_m: int = 64) -> torch.Tensor:
@@ -264,7 +265,7 @@ def prefill_schedule(query_start: list, seq_lens: list, H: int, Hk: int, head_di
                      tensor_cores: bool = True, form: Optional[str] = None) -> torch.Tensor:
     """Work list of the prefill kernel for one batch.
 
-    head_dim 128 on tensor cores: int32 [n, 4] rows (sequence, query offset of slot 0, of slot 1 or
+    head_dim 64 / 128 on tensor cores: int32 [n, 4] rows (sequence, query offset of slot 0, of slot 1 or
     -1, (pair << 16) | head), one per CTA of the two-tile kernel, heaviest first. Two forms:
     head pairs (pair = 1: heads h, h+1 of one GQA group over the same 128 query rows, each K/V tile
     loaded once for both; needs an even group size) and row-tile pairs (pair = 0: one head, two
@@ -273,7 +274,7 @@ def prefill_schedule(query_start: list, seq_lens: list, H: int, Hk: int, head_di
     tile costs nearly as much with one active slot as with two, so pairing tile i with tile n-1-i
     (every item the same n+1 KV tiles) lost even on a short single prompt (1 x 1088 tokens,
     32 / 8 heads: 0.0389 vs 0.0348 ms). ``form`` ("pairs" / "rows") forces a form. Otherwise: the [n, 2] (sequence, offset) 64-row tiles of the mma.sync kernel."""
-    if not (tensor_cores and head_dim == 128):
+    if not (tensor_cores and head_dim in (64, 128)):
         return prefill_tiles(query_start, 64)
     seqs = []
     for b in range(len(query_start) - 1):
@@ -309,7 +310,7 @@ def paged_prefill_attention(q: torch.Tensor, kv_cache: torch.Tensor, block_table
                             window: int = 0, softcap: float = 0.0, emu: Optional[int] = None,
                             kv_scales: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Varlen causal attention of new tokens q [T, H, D] over the paged KV (prefix + new).
-    head_dim 128 runs on tcgen05/TMEM (the two-tile kernel when ``tiles`` is a ``prefill_schedule``
+    head_dim 64 / 128 runs on tcgen05/TMEM (the two-tile kernel when ``tiles`` is a ``prefill_schedule``
     work list); other sizes on mma.sync (64-row tiles). ``window`` > 0: sliding-window attention;
     ``softcap`` > 0: tanh soft-capped scores. With ``kv_scales`` (fp8 cache) the referenced blocks
     are dequantized into a bf16 copy first."""

@@ -120,13 +120,13 @@ def test_paged_prefill_attention(H, Hk, D):
 @pytest.mark.parametrize("H,Hk", [(32, 8), (28, 4), (8, 8), (12, 4)])
 @pytest.mark.parametrize("emu", [0, 1, 2])
 @pytest.mark.parametrize("qscale", [1.0, 6.0])
-def test_prefill_two_tile_kernel(H, Hk, emu, qscale):
-    """The two-tile tcgen05 prefill kernel: head pairs (even GQA groups) and row-tile pairs (odd
-    groups), FMA-pipe exponentials, and sharp score distributions (qscale 6) that move the running
-    max across tiles (O rescaled in TMEM) against the fp32 oracle."""
+@pytest.mark.parametrize("D", [128, 64])
+def test_prefill_two_tile_kernel(H, Hk, emu, qscale, D):
+    """The two-tile tcgen05 prefill kernel at head_dim 128 and 64: head pairs (even GQA groups) and
+    row-tile pairs (odd groups), FMA-pipe exponentials, and sharp score distributions (qscale 6) that
+    move the running max across tiles (O rescaled in TMEM) against the fp32 oracle."""
     specs = [(0, 300), (1000, 260), (7, 1), (200, 129), (0, 640)]
     lens = [p + n for p, n in specs]
-    D = 128
     cache, bt, sl = _paged_setup(len(specs), Hk, D, lens, seed=23)
     qs = [0]
     for _, n in specs:
