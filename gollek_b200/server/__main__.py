@@ -29,6 +29,8 @@ def main(argv=None):
     ap.add_argument("--draft-model", default=None)
     ap.add_argument("--enable-expert-parallel", action="store_true")
     ap.add_argument("--asr-model", default=None, help="Whisper checkpoint directory for /v1/audio/*")
+    ap.add_argument("--tts-model", default=None, help="SpeechT5 text-to-speech directory for /v1/audio/speech")
+    ap.add_argument("--tts-vocoder", default=None, help="HiFi-GAN vocoder directory for /v1/audio/speech")
     args = ap.parse_args(argv)
     import uvicorn
     from ..config import EngineConfig
@@ -57,7 +59,7 @@ def main(argv=None):
         return _serve_tp(args, cfg, keys)
     ae = AsyncEngine(LLMEngine(cfg)).start()
     app = create_app(ae, model_name=args.served_model_name or os.path.basename(args.model.rstrip("/")),
-                     api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg))
+                     api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg))
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:
@@ -72,6 +74,19 @@ def _asr(args, cfg):
     from ..models.whisper import WhisperASR
     dev = str(cfg.device)
     return WhisperASR(args.asr_model, device=dev, dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
+
+
+def _tts(args, cfg):
+    """The text-to-speech model behind /v1/audio/speech (on rank 0's device), or None."""
+    if not args.tts_model:
+        return None
+    if not args.tts_vocoder:
+        raise SystemExit("--tts-model needs --tts-vocoder (a HiFi-GAN checkpoint directory)")
+    import torch
+    from ..models.speecht5 import SpeechSynth
+    dev = str(cfg.device)
+    return SpeechSynth(args.tts_model, args.tts_vocoder, device=dev,
+                       dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
 
 
 def _serve_tp(args, cfg, keys):
@@ -103,7 +118,7 @@ def _serve_tp(args, cfg, keys):
         drv = DriverEngine(engine, cp)
         ae = AsyncEngine(drv).start()
         app = create_app(ae, model_name=args.served_model_name or os.path.basename(str(args.model).rstrip("/")),
-                         api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg))
+                         api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg))
         try:
             uvicorn.run(app, host=args.host, port=args.port, log_level="info")
         finally:

@@ -290,10 +290,10 @@ class RagQueryRequest(BaseModel):
 def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
                rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
                engine_builder=None, drain_timeout_s: float = 30.0,
-               routes: Optional[Dict[str, AsyncEngine]] = None, asr=None) -> FastAPI:
+               routes: Optional[Dict[str, AsyncEngine]] = None, asr=None, tts=None) -> FastAPI:
     """``engine_builder(model) -> LLMEngine`` builds the engine of a hot-swap (default: the running
     engine's configuration with ``model`` replaced). ``asr``: a ``WhisperASR`` behind the
-    /v1/audio endpoints."""
+    /v1/audio transcription endpoints; ``tts``: a ``SpeechSynth`` behind /v1/audio/speech."""
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
     st.routes.update(routes or {})
     from .rag import RagStore
@@ -308,7 +308,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
     from .converter import register_converter_routes
     st.converter = register_converter_routes(app)
     from .audio import register_audio_routes
-    st.asr = register_audio_routes(app, asr)
+    st.asr = register_audio_routes(app, asr, tts)
 
     def error_response(name: str, message: Optional[str] = None, status: Optional[int] = None) -> JSONResponse:
         code = errors.CODES[name]

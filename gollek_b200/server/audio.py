@@ -1,5 +1,5 @@
-"""OpenAI audio endpoints over a Whisper model: POST /v1/audio/transcriptions and
-/v1/audio/translations (multipart ``file``, ``model``, ``language``, ``prompt``, ``response_format``
+"""OpenAI audio endpoints: POST /v1/audio/speech over a SpeechT5 + HiFi-GAN model (text to WAV), and
+over a Whisper model POST /v1/audio/transcriptions and /v1/audio/translations (multipart ``file``, ``model``, ``language``, ``prompt``, ``response_format``
 json | text | verbose_json | srt | vtt, ``temperature``).
 
 Requests that arrive together are batched: one worker thread takes every pending upload with the
@@ -17,7 +17,7 @@ import threading
 from typing import Any, Dict, List, Optional
 
 from fastapi import FastAPI, File, Form, HTTPException, UploadFile
-from fastapi.responses import JSONResponse, PlainTextResponse
+from fastapi.responses import JSONResponse, PlainTextResponse, Response
 
 FORMATS = ("json", "text", "verbose_json", "srt", "vtt")
 
@@ -87,9 +87,34 @@ class ASRBatcher:
         self.q.put(None)
 
 
-def register_audio_routes(app: FastAPI, asr) -> Optional[ASRBatcher]:
-    """Mount the audio endpoints (501 when no speech model is loaded)."""
+def register_audio_routes(app: FastAPI, asr, tts=None) -> Optional[ASRBatcher]:
+    """Mount the audio endpoints (501 when the model they need is not loaded). ``tts``: a
+    ``SpeechSynth`` behind POST /v1/audio/speech (JSON ``input``, ``voice``, ``response_format``
+    wav | pcm, ``seed``; the response is the audio bytes)."""
     batcher = ASRBatcher(asr) if asr is not None else None
+    tts_lock = threading.Lock()
+
+    @app.post("/v1/audio/speech")
+    async def speech(body: Dict[str, Any]):
+        if tts is None:
+            raise HTTPException(501, "no text-to-speech model loaded (serve with --tts-model / --tts-vocoder)")
+        text = body.get("input")
+        fmt = body.get("response_format", "wav")
+        if not isinstance(text, str) or not text.strip():
+            raise HTTPException(400, "input must be a non-empty string")
+        if fmt not in ("wav", "pcm"):
+            raise HTTPException(400, "response_format must be wav or pcm")
+
+        def run():
+            with tts_lock:  # one synthesis at a time on the model's device
+                return tts.wav_bytes(text, body.get("voice"), int(body.get("seed", 0)))
+        try:
+            data = await asyncio.get_running_loop().run_in_executor(None, run)
+        except ValueError as e:
+            raise HTTPException(400, str(e))
+        if fmt == "pcm":  # raw 16-bit little-endian samples after the 44-byte WAVE header
+            return Response(content=data[44:], media_type="audio/pcm")
+        return Response(content=data, media_type="audio/wav")
 
     async def run(task: str, file: UploadFile, language: Optional[str], response_format: str,
                   temperature: float):
