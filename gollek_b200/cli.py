@@ -1,7 +1,8 @@
 """Command-line interface: ``python -m gollek_b200 <command>``.
 
 Commands follow the reference CLI (ui/gollek-cli/…/cli/commands/RunCommand.java:45-324 and
-siblings: run, chat, batch, list, show, convert, quantize, serve, providers, stats, pull):
+siblings: run, chat, batch, list, show, convert, quantize, serve, providers, stats, pull; plus
+transcribe and speak for audio):
 
   run       one-shot generation            chat      interactive chat loop
   batch     JSONL prompts → JSONL outputs  serve     HTTP server (OpenAI + gollek routes)
@@ -223,6 +224,17 @@ def cmd_transcribe(args):
             print(r["text"])
 
 
+def cmd_speak(args):
+    """Text to speech with a SpeechT5 checkpoint and a HiFi-GAN vocoder: writes a 16-bit WAVE file."""
+    import torch
+    from .models.speecht5 import SpeechSynth
+    dev = args.device or ("cuda" if torch.cuda.is_available() else "cpu")
+    synth = SpeechSynth(args.model, args.vocoder, device=dev, dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
+    with open(args.out, "wb") as f:
+        f.write(synth.wav_bytes(args.text, args.voice, args.seed))
+    print(f"wrote {args.out}")
+
+
 def cmd_bench(args):
     import subprocess
     here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -305,6 +317,15 @@ def build_parser():
     tr.add_argument("--json", action="store_true")
     tr.add_argument("--device", default=None)
     tr.set_defaults(fn=cmd_transcribe)
+    sp = sub.add_parser("speak", help="text to speech (SpeechT5 + HiFi-GAN checkpoints) into a WAV file")
+    sp.add_argument("model")
+    sp.add_argument("text")
+    sp.add_argument("--vocoder", required=True)
+    sp.add_argument("--out", default="speech.wav")
+    sp.add_argument("--voice", default=None, help="speakers/<voice>.npy in the model directory")
+    sp.add_argument("--seed", type=int, default=0)
+    sp.add_argument("--device", default=None)
+    sp.set_defaults(fn=cmd_speak)
     be = sub.add_parser("bench")
     be.add_argument("rest", nargs=argparse.REMAINDER)
     be.set_defaults(fn=cmd_bench)

@@ -125,3 +125,28 @@ def test_speecht5_gpu_bf16_close_to_fp32():
     n = min(a.shape[0], b.shape[0])
     assert n >= 8
     assert float((a[:n] - b[:n]).norm() / a[:n].norm()) < 0.05
+
+
+def test_speak_cli_with_sentencepiece_tokenizer(tmp_path):
+    """``gollek speak``: the default tokenizer (the checkpoint's character SentencePiece model plus the
+    end-of-sequence id) and a WAV file of the synthesized waveform."""
+    import argparse
+    import wave
+
+    import sentencepiece as spm
+    from transformers import SpeechT5HifiGan, SpeechT5HifiGanConfig
+    from gollek_b200 import cli
+    cfg, m = _tiny()
+    m.save_pretrained(str(tmp_path / "tts"))
+    torch.manual_seed(3)
+    SpeechT5HifiGan(SpeechT5HifiGanConfig(upsample_initial_channel=32, model_in_dim=80)).save_pretrained(
+        str(tmp_path / "voc"))
+    corpus = tmp_path / "corpus.txt"
+    corpus.write_text("\n".join(["the quick brown fox jumps over the lazy dog"] * 20))
+    spm.SentencePieceTrainer.train(input=str(corpus), model_prefix=str(tmp_path / "tts" / "spm_char"),
+                                   model_type="char", vocab_size=31, bos_id=0, pad_id=1, eos_id=2, unk_id=3)
+    out = tmp_path / "a.wav"
+    cli.cmd_speak(argparse.Namespace(model=str(tmp_path / "tts"), vocoder=str(tmp_path / "voc"), text="a lazy fox",
+                                     out=str(out), voice=None, seed=0, device="cpu"))
+    with wave.open(str(out)) as w:
+        assert w.getframerate() == 16000 and w.getnframes() > 0 and w.getnframes() % 256 == 0
