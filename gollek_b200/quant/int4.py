@@ -234,7 +234,7 @@ def from_gptq(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
                       zeros.t().to(torch.bfloat16).contiguous(), N, K, group)
 
 
-QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip", "bitsandbytes")
+QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip", "bitsandbytes", "squeezellm")
 
 
 def quantized_checkpoint_getter(ck, quant_config: dict):
@@ -246,6 +246,9 @@ def quantized_checkpoint_getter(ck, quant_config: dict):
     if method == "bitsandbytes":
         from .bnb import bnb_getter
         return bnb_getter(ck)
+    if method == "squeezellm":
+        from .squeezellm import squeezellm_getter
+        return squeezellm_getter(ck)
     if method == "quip":
         from .quip import QuipWeight
         stages, seed = int(quant_config.get("stages", 1)), int(quant_config.get("seed", 0))

@@ -207,3 +207,45 @@ def test_bitsandbytes_checkpoint_loading(tmp_path, double_quant):
     eng = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=8)
     outp = eng.generate([[5, 6, 7, 8]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
     assert len(outp.output_token_ids) == 3
+
+
+def test_squeezellm_dense_and_sparse(tmp_path):
+    """SqueezeLLM: on a heavy-tailed matrix the per-channel k-means codebooks plus exact outliers beat
+    uniform int4; the checkpoint tensors round-trip, and the engine serves such a checkpoint."""
+    from gollek_b200.quant.squeezellm import from_tensors, quantize_squeezellm, to_tensors
+    g = torch.Generator().manual_seed(5)
+    W = torch.distributions.StudentT(3.0).sample((256, 512)) * 0.01
+    q = quantize_squeezellm(W, 4, 0.005)
+    assert q.val.numel() == round(0.005 * W.numel())
+    e = _rel(q.dequantize(), W)
+    assert e < 0.8 * _rel(quantize_rtn(W, 128).dequantize(), W), e
+    t = to_tensors(q)
+    back = from_tensors(t["qweight"], t["lookup_table"], t["dense_ptr"], t["dense_idx"], t["weight_nnz"])
+    assert torch.equal(back.dequantize(), q.dequantize())
+    # a checkpoint served by the engine
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine, load_model_source
+    from gollek_b200.engine.sequence import SamplingParams
+    cfg = preset("tiny-llama", intermediate_size=512, num_hidden_layers=1)
+    w = init_random_weights(cfg, seed=4)
+    out = {}
+    for k, v in w.items():
+        if k.endswith("proj.weight"):
+            for suf, tt in to_tensors(quantize_squeezellm(v, 4, 0.005)).items():
+                out[k[:-7] + "." + suf] = tt
+        else:
+            out[k] = v
+    d = tmp_path / "sq"
+    d.mkdir()
+    save_file(out, str(d / "model.safetensors"))
+    hf = cfg.to_hf()
+    hf["quantization_config"] = {"quant_method": "squeezellm", "wbits": 4}
+    (d / "config.json").write_text(json.dumps(hf))
+    qcfg, get, _ = load_model_source(str(d))
+    k = "model.layers.0.mlp.down_proj.weight"
+    assert get(k).dtype == torch.bfloat16 and _rel(get(k).float(), w[k].float()) < 0.12
+    ec = EngineConfig(device="cpu", dtype="float32", block_size=16, max_num_seqs=2, max_num_batched_tokens=64,
+                      max_model_len=64, use_cuda_graphs=False)
+    o = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=8).generate(
+        [[5, 6, 7]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
+    assert len(o.output_token_ids) == 3
