@@ -109,7 +109,7 @@ def cmd_quantize(args):
         t = args.type.upper()
         G.write_llama_gguf(args.dst, cfg, w, t if t in G.MIXTURES else G.TYPE_BY_NAME[t])
         print(f"wrote {args.dst} ({args.type})")
-    elif args.method in ("awq", "autoround", "quip"):
+    elif args.method in ("awq", "autoround", "quip", "nvfp4", "mxfp4"):
         from .quant.offline import quantize_checkpoint
         calib = None
         if args.calib_file:  # one calibration sequence of token ids per line
@@ -131,12 +131,12 @@ def cmd_dequantize(args):
 
     import torch
     from .loaders.safetensors import SafetensorsCheckpoint, save_sharded
-    from .quant.int4 import QUANT_METHODS, Int4Weight, quantized_checkpoint_getter
+    from .quant.int4 import QUANT_METHODS, Int4Weight, checkpoint_quant_config, quantized_checkpoint_getter
     with open(os.path.join(args.src, "config.json")) as f:
         hf = json.load(f)
-    qc = hf.get("quantization_config")
+    qc = checkpoint_quant_config(args.src)
     if not qc or qc.get("quant_method") not in QUANT_METHODS:
-        raise SystemExit(f"{args.src}: no GPTQ / AWQ / AutoRound / QuIP quantization_config in config.json")
+        raise SystemExit(f"{args.src}: no supported quantization_config in config.json / hf_quant_config.json")
     ck = SafetensorsCheckpoint(args.src)
     get = quantized_checkpoint_getter(ck, qc)
     keys = set(ck.keys())
@@ -146,6 +146,13 @@ def cmd_dequantize(args):
             continue
         if k.endswith(".scale") and k[:-6] + ".weight" in keys:  # AutoRound native scale
             continue
+        if k.endswith((".weight_scale", ".weight_scale_2", ".input_scale")):  # ModelOpt scales
+            continue
+        if k.endswith((".weight_blocks", ".weight_scales")):  # MXFP4: served under <name>.weight
+            if k.endswith("_scales"):
+                continue
+            k = k[:-len("_blocks")]
+            n_q += 1
         if k.endswith(".quip_scales"):
             name = k[:-len(".quip_scales")] + ".weight"
         else:
@@ -153,12 +160,14 @@ def cmd_dequantize(args):
         v = get(name)
         if qc.get("quant_method") == "quip" and k.endswith(".quip_scales"):
             n_q += 1
+        if k.endswith(".weight") and k + "_scale" in keys:  # ModelOpt NVFP4 / FP8 linear
+            n_q += 1
         if isinstance(v, Int4Weight):
             v, n_q = v.dequantize(torch.float32), n_q + 1
         out[name] = v.to(torch.bfloat16) if v.is_floating_point() else v
     os.makedirs(args.dst, exist_ok=True)
     save_sharded(out, args.dst)
-    hf.pop("quantization_config")
+    hf.pop("quantization_config", None)
     hf["torch_dtype"] = "bfloat16"
     with open(os.path.join(args.dst, "config.json"), "w") as f:
         json.dump(hf, f, indent=1)
@@ -283,7 +292,7 @@ def build_parser():
     q.add_argument("src")
     q.add_argument("dst")
     q.add_argument("--type", default="Q4_K", help="GGUF source: target ggml type or mixture")
-    q.add_argument("--method", default="fp8", choices=["fp8", "awq", "autoround", "quip"],
+    q.add_argument("--method", default="fp8", choices=["fp8", "awq", "autoround", "quip", "nvfp4", "mxfp4"],
                    help="safetensors source: block-scaled fp8, AWQ or AutoRound int4 (calibrated), QuIP lattice")
     q.add_argument("--group", type=int, default=128, help="awq / autoround: input columns per scale")
     q.add_argument("--iters", type=int, default=200, help="autoround: signed-gradient steps per linear")

@@ -605,10 +605,9 @@ def load_model_source(source: str, keep_quantized: bool = False):
         with open(os.path.join(d, "config.json")) as fh:
             cfg = ModelConfig.from_hf(json.load(fh))
         ck = SafetensorsCheckpoint(source)
-        with open(os.path.join(d, "config.json")) as fh:
-            qc = json.load(fh).get("quantization_config") or {}
+        from ..quant.int4 import QUANT_METHODS, checkpoint_quant_config, quantized_checkpoint_getter
+        qc = checkpoint_quant_config(d)
         getter = ck.get
-        from ..quant.int4 import QUANT_METHODS, quantized_checkpoint_getter
         if qc.get("quant_method") in QUANT_METHODS:
             getter = quantized_checkpoint_getter(ck, qc)
         return cfg, getter, load_tokenizer(d)

@@ -142,7 +142,7 @@ def save_file(tensors: Dict[str, torch.Tensor], path: str, metadata: Optional[di
         f.write(hb)
         for name in order:
             t = tensors[name].detach().contiguous().cpu()
-            f.write(t.view(torch.uint8).numpy().tobytes() if t.numel() else b"")
+            f.write(t.reshape(-1).view(torch.uint8).numpy().tobytes() if t.numel() else b"")
 
 
 def save_sharded(tensors: Dict[str, torch.Tensor], directory: str, max_shard_bytes: int = 4 << 30) -> None:

@@ -234,15 +234,35 @@ def from_gptq(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
                       zeros.t().to(torch.bfloat16).contiguous(), N, K, group)
 
 
-QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip", "bitsandbytes", "squeezellm")
+QUANT_METHODS = ("awq", "gptq", "auto-round", "autoround", "intel/auto-round", "quip", "bitsandbytes", "squeezellm",
+                 "modelopt", "mxfp4")
+
+
+def checkpoint_quant_config(d: str) -> dict:
+    """The quantization config of checkpoint directory ``d``: config.json's ``quantization_config``,
+    else ModelOpt's hf_quant_config.json (``{"quantization": {"quant_algo": …}}``)."""
+    import json
+    import os
+    with open(os.path.join(d, "config.json")) as fh:
+        qc = json.load(fh).get("quantization_config") or {}
+    mo = os.path.join(d, "hf_quant_config.json")
+    if not qc and os.path.exists(mo):
+        with open(mo) as fh:
+            q = json.load(fh).get("quantization") or {}
+        if q.get("quant_algo"):
+            qc = {"quant_method": "modelopt", **q}
+    return qc
 
 
 def quantized_checkpoint_getter(ck, quant_config: dict):
     """Wrap a checkpoint reader so that ``get("….weight")`` of a quantized linear returns an
     ``Int4Weight`` (or bf16 for act-order GPTQ): GPTQ / AWQ from qweight / qzeros / scales; AutoRound
     from its native weight / scale / zp tensors or from GPTQ-named ones; QuIP (``quant/quip.py``) from
-    its lattice codes, dequantized to bf16 here."""
+    its lattice codes, dequantized to bf16 here; NVFP4 / FP8 ModelOpt and MXFP4 through ``quant/fp4.py``."""
     method = quant_config.get("quant_method")
+    if method in ("modelopt", "mxfp4"):
+        from .fp4 import fp4_getter
+        return fp4_getter(ck, quant_config)
     if method == "bitsandbytes":
         from .bnb import bnb_getter
         return bnb_getter(ck)

@@ -70,7 +70,7 @@ def quantize_checkpoint(src: str, dst: str, method: str, group: int = 128, calib
     from .awq import awq_search, to_awq
     from .int4 import quantize_rtn
     from .quip import quantize_quip
-    if method not in ("awq", "autoround", "quip"):
+    if method not in ("awq", "autoround", "quip", "nvfp4", "mxfp4"):
         raise ValueError(f"unknown method {method!r}")
     with open(os.path.join(src, "config.json")) as f:
         hf = json.load(f)
@@ -123,6 +123,13 @@ def quantize_checkpoint(src: str, dst: str, method: str, group: int = 128, calib
                     out[p + n + ".scale"] = t["scale"]
                     out[p + n + ".zp"] = t["zp"]
                     n_q += 1
+        elif method in ("nvfp4", "mxfp4"):
+            from .fp4 import quantize_mxfp4, quantize_nvfp4, to_tensors as fp4_tensors
+            for n, W in lin.items():
+                q = quantize_nvfp4(W) if method == "nvfp4" else quantize_mxfp4(W)
+                for suf, t in fp4_tensors(q).items():
+                    out[p + n + ".weight" + suf] = t
+                n_q += 1
         else:
             for n, W in lin.items():
                 q = quantize_quip(W, stages=stages, seed=seed)
@@ -141,6 +148,10 @@ def quantize_checkpoint(src: str, dst: str, method: str, group: int = 128, calib
     elif method == "autoround":
         qc = {"quant_method": "auto-round", "bits": 4, "group_size": group, "sym": False, "iters": iters,
               "packing_format": "auto_round"}
+    elif method == "nvfp4":
+        qc = {"quant_method": "modelopt", "quant_algo": "NVFP4", "group_size": 16}
+    elif method == "mxfp4":
+        qc = {"quant_method": "mxfp4", "group_size": 32}
     else:
         qc = {"quant_method": "quip", "stages": stages, "seed": seed, "codebook": "e8-ball10", "group_size": 64}
     hf["quantization_config"] = qc

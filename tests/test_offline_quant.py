@@ -249,3 +249,90 @@ def test_squeezellm_dense_and_sparse(tmp_path):
     o = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=8).generate(
         [[5, 6, 7]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
     assert len(o.output_token_ids) == 3
+
+
+def test_e2m1_rounding_and_fp4_formats():
+    """e2m1: nearest code, ties to the even code, saturation at 6; NVFP4 (e4m3 scale per 16 and a
+    tensor scale) and MXFP4 (power-of-two scale per 32) round-trip through their checkpoint tensors,
+    and the W4A4 oracle matches the dequantized product."""
+    from gollek_b200.quant import fp4 as F
+    x = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.0, -0.3, -5.0, 0.74, 0.76])
+    assert F.decode_e2m1(F.encode_e2m1(x)).tolist() == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 6.0, -0.5, -4.0, 0.5, 1.0]
+    c = torch.arange(16, dtype=torch.uint8)
+    assert torch.equal(F.encode_e2m1(F.decode_e2m1(c))[c != 8], c[c != 8])  # -0 encodes as +0
+    assert torch.equal(F.unpack_nibbles(F.pack_nibbles(c.view(2, 8))), c.view(2, 8))
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(96, 256, generator=g) * 0.02
+    w[:, :16] *= 50.0  # one block of large magnitude per row: the per-block scales absorb it
+    for fmt in ("nvfp4", "mxfp4"):
+        q = F.quantize_nvfp4(w) if fmt == "nvfp4" else F.quantize_mxfp4(w)
+        assert _rel(q.dequantize(), w) < 0.12, (fmt, _rel(q.dequantize(), w))
+        t = F.to_tensors(q)
+        back = (F.from_nvfp4(t[""], t["_scale"], t["_scale_2"]) if fmt == "nvfp4"
+                else F.from_mxfp4(t["_blocks"], t["_scales"]))
+        assert torch.equal(back.dequantize(), q.dequantize())
+        xa = torch.randn(5, 256, generator=g)
+        ref = F.fp4_matmul_reference(xa, q, quantize_activations=False)
+        assert torch.allclose(ref, xa @ q.dequantize().t(), atol=1e-5)
+        assert _rel(F.fp4_matmul_reference(xa, q), xa @ w.t()) < 0.2
+    # every NVFP4 element with a non-zero block is within half an e2m1 step of its scaled value
+    q = F.quantize_nvfp4(w)
+    s = (q.scale * q.global_scale).repeat_interleave(16, 1)
+    assert ((q.dequantize() - w).abs() <= s * 1.0 + 1e-12).all()
+
+
+@pytest.mark.parametrize("method", ["nvfp4", "mxfp4"])
+def test_fp4_checkpoint_serves_and_dequantizes(tmp_path, method):
+    """``gollek quantize --method nvfp4|mxfp4`` writes ModelOpt / MXFP4 tensors that the engine loads
+    and serves, and ``gollek dequantize`` turns back into bf16 close to the original."""
+    import subprocess
+    import sys
+    from gollek_b200.config import EngineConfig
+    from gollek_b200.engine.engine import LLMEngine, load_model_source
+    from gollek_b200.engine.sequence import SamplingParams
+    from gollek_b200.loaders.safetensors import SafetensorsCheckpoint
+    cfg = preset("tiny-llama", intermediate_size=512, num_hidden_layers=1)
+    w = init_random_weights(cfg, seed=6)
+    src, dst, deq = tmp_path / "src", tmp_path / method, tmp_path / "deq"
+    src.mkdir()
+    save_file({k: v.to(torch.bfloat16) for k, v in w.items()}, str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps(cfg.to_hf()))
+    run = lambda *a: subprocess.run([sys.executable, "-m", "gollek_b200", *a], check=True, capture_output=True, text=True)
+    run("quantize", str(src), str(dst), "--method", method)
+    ck = SafetensorsCheckpoint(str(dst))
+    k = "model.layers.0.mlp.down_proj.weight"
+    if method == "nvfp4":
+        assert ck.get(k).dtype == torch.uint8 and ck.get(k + "_scale").dtype == torch.float8_e4m3fn
+    else:
+        assert ck.get(k + "_blocks").shape[-1] == 16 and ck.get(k + "_scales").dtype == torch.uint8
+    qcfg, get, _ = load_model_source(str(dst))
+    assert get(k).dtype == torch.bfloat16 and _rel(get(k).float(), w[k].float()) < 0.12
+    ec = EngineConfig(device="cpu", dtype="float32", block_size=16, max_num_seqs=2, max_num_batched_tokens=64,
+                      max_model_len=64, use_cuda_graphs=False)
+    o = LLMEngine(ec, model_cfg=qcfg, weights=get, num_blocks=8).generate(
+        [[5, 6, 7]], SamplingParams(temperature=0.0, max_tokens=3, ignore_eos=True))[0]
+    assert len(o.output_token_ids) == 3
+    r = run("dequantize", str(dst), str(deq))
+    assert "7 " in r.stdout, r.stdout  # q, k, v, o, gate, up, down
+    back = SafetensorsCheckpoint(str(deq)).get(k)
+    assert back.dtype == torch.bfloat16 and torch.equal(back, get(k))
+
+
+def test_modelopt_hf_quant_config_and_fp8(tmp_path):
+    """A ModelOpt checkpoint described only by hf_quant_config.json; its FP8 linears (e4m3 weight,
+    per-tensor scale) load as bf16."""
+    from gollek_b200.loaders.safetensors import SafetensorsCheckpoint
+    from gollek_b200.quant.int4 import checkpoint_quant_config, quantized_checkpoint_getter
+    w = torch.randn(64, 128) * 0.05
+    s = w.abs().max() / 448.0
+    d = tmp_path / "mo"
+    d.mkdir()
+    save_file({"l.weight": (w / s).to(torch.float8_e4m3fn), "l.weight_scale": s.reshape(()).float(),
+               "n.weight": torch.ones(8)}, str(d / "model.safetensors"))
+    (d / "config.json").write_text(json.dumps({"model_type": "llama"}))
+    (d / "hf_quant_config.json").write_text(json.dumps({"quantization": {"quant_algo": "FP8"}}))
+    qc = checkpoint_quant_config(str(d))
+    assert qc["quant_method"] == "modelopt" and qc["quant_algo"] == "FP8"
+    get = quantized_checkpoint_getter(SafetensorsCheckpoint(str(d)), qc)
+    assert get("l.weight").dtype == torch.bfloat16 and _rel(get("l.weight").float(), w) < 0.05
+    assert torch.equal(get("n.weight"), torch.ones(8))
