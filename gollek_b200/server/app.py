@@ -290,12 +290,16 @@ class RagQueryRequest(BaseModel):
 def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: Optional[List[str]] = None,
                rate: float = 0.0, burst: float = 0.0, request_timeout: float = 600.0,
                engine_builder=None, drain_timeout_s: float = 30.0,
-               routes: Optional[Dict[str, AsyncEngine]] = None, asr=None, tts=None) -> FastAPI:
+               routes: Optional[Dict[str, AsyncEngine]] = None, asr=None, tts=None,
+               providers=None) -> FastAPI:
     """``engine_builder(model) -> LLMEngine`` builds the engine of a hot-swap (default: the running
     engine's configuration with ``model`` replaced). ``asr``: a ``WhisperASR`` behind the
     /v1/audio transcription endpoints; ``tts``: a ``SpeechSynth`` behind /v1/audio/speech."""
     st = ServerState(aengine, model_name, api_keys, rate, burst, request_timeout)
     st.routes.update(routes or {})
+    from .providers import OpenAIHTTPProvider, ProviderRegistry, ProviderRouter, _ClientError
+    st.providers = providers if providers is not None else ProviderRegistry()
+    st.provider_router = ProviderRouter(st.providers)
     from .rag import RagStore
     st.rag = RagStore()
     from .plugins import ServerPlugins, UnsafeContent, redact_pii, split_reasoning
@@ -499,6 +503,10 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                  "max_model_len": st.max_len()}]
         data += [{"id": n, "object": "model", "created": _now(), "owned_by": "gollek-b200",
                   "max_model_len": e.engine.cfg.max_model_len} for n, e in st.routes.items()]
+        local = {d["id"] for d in data}
+        for p in st.providers.all():
+            data += [{"id": m, "object": "model", "created": _now(), "owned_by": p.id}
+                     for m in p.models() if m not in local]
         return {"object": "list", "data": data}
 
     @app.get("/v1/models/{model_id}")
@@ -535,8 +543,31 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         return {"id": cid, "object": "text_completion", "created": _now(), "model": st.model_name, "choices": choices,
                 "usage": {"prompt_tokens": pt, "completion_tokens": ct, "total_tokens": pt + ct}}
 
+    def _remote(model: Optional[str]) -> bool:
+        """A model that no local engine serves but a registered provider does."""
+        return bool(model) and model != st._model_name and model not in st.routes and \
+            any(p.supports(model) for p in st.providers.all())
+
+    async def _forward(route: str, req):
+        body = req.model_dump(exclude_unset=True)
+        if body.get("stream"):
+            d = st.provider_router.route(body["model"], streaming=True)
+            p = st.providers.get(d.provider)
+            if not isinstance(p, OpenAIHTTPProvider):
+                raise HTTPException(400, f"provider {d.provider} does not stream")
+            return StreamingResponse(p.stream(route, body), media_type="text/event-stream")
+        try:
+            out = await asyncio.to_thread(st.provider_router.execute, route, body)
+        except Exception as e:  # every provider failed
+            return error_response("RUNTIME_ENGINE_UNAVAILABLE", str(e))
+        if isinstance(out, _ClientError):
+            return JSONResponse(out.body, status_code=out.status)
+        return out
+
     @app.post("/v1/completions")
     async def completions(req: CompletionRequest):
+        if _remote(getattr(req, "model", None)):
+            return await _forward("completions", req)
         st.route(getattr(req, "model", None))
         if req.n != 1 and not req.use_beam_search:
             raise HTTPException(400, "n > 1 needs use_beam_search")
@@ -587,6 +618,10 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
                             for e in o.logprobs]}
 
     async def _chat(req: ChatRequest, force_stream: bool = False):
+        if _remote(getattr(req, "model", None)):
+            if force_stream:
+                req.stream = True
+            return await _forward("chat/completions", req)
         st.route(getattr(req, "model", None))
         if req.n != 1:
             raise HTTPException(400, "only n=1 is supported")
@@ -984,6 +1019,34 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         eng = await asyncio.to_thread(engine_builder or _default_builder, str(model))
         st.routes[str(name)] = _AE(eng).start()
         return {"name": name, "model": model, "served": [st._model_name] + list(st.routes)}
+
+    @app.get("/v1/admin/providers")
+    async def admin_providers():
+        return {"providers": [p.status() for p in st.providers.all()]}
+
+    @app.post("/v1/admin/providers")
+    async def admin_add_provider(body: Dict[str, Any]):
+        """Register an OpenAI-compatible upstream: {"id", "base_url", "api_key"?, "models"?}."""
+        pid, url = (body or {}).get("id"), (body or {}).get("base_url")
+        if not pid or not url:
+            raise HTTPException(400, "body needs id and base_url")
+        st.providers.register(OpenAIHTTPProvider(str(pid), str(url), str(body.get("api_key", "")),
+                                                 body.get("models"), float(body.get("timeout", 60.0))))
+        return {"registered": pid, "providers": [p.id for p in st.providers.all()]}
+
+    @app.delete("/v1/admin/providers/{pid}")
+    async def admin_remove_provider(pid: str):
+        if not st.providers.unregister(pid):
+            raise HTTPException(404, f"no provider {pid}")
+        return {"removed": pid}
+
+    @app.get("/v1/admin/providers/route")
+    async def admin_route(model: str, stream: bool = False):
+        try:
+            d = st.provider_router.route(model, streaming=stream)
+        except Exception as e:
+            raise HTTPException(404, str(e))
+        return {"provider": d.provider, "score": d.score, "fallbacks": d.fallbacks}
 
     @app.delete("/v1/admin/models/{name}")
     async def admin_remove_model(name: str):
