@@ -144,6 +144,13 @@ class GGUFTokenizer:
     * ``model == "gpt2"``: byte-level BPE. The text is split by the vocabulary's pre-tokenizer
       pattern (``tokenizer.ggml.pre``), each chunk's UTF-8 bytes are mapped to the GPT-2 byte
       alphabet, and ``tokenizer.ggml.merges`` are applied lowest rank first.
+    * ``model == "bert"``: WordPiece. The text is cleaned (control characters dropped, whitespace
+      unified), lower-cased with accents stripped (``lowercase``), CJK ideographs and punctuation
+      become words of their own, and each whitespace-separated word is split greedily into the
+      longest vocabulary pieces from its start; a word with no such split (or longer than 100
+      characters) becomes the unknown token. The vocabulary may be in the ``##`` continuation form
+      (as HF writes it) or in GGUF's phantom-space form (word-initial pieces carry ``▁``, continuation
+      pieces are bare). The ids are wrapped in the classifier / separator tokens.
     Control / user-defined tokens that appear literally in the text are matched as single ids.
     ``add_bos`` follows ``tokenizer.ggml.add_bos_token``; ``tokenizer.chat_template`` (Jinja) is used
     by ``apply_chat_template`` when present.
@@ -154,14 +161,18 @@ class GGUFTokenizer:
 
     def __init__(self, tokens: List[str], scores: Optional[List[float]] = None, bos: int = 1, eos: int = 2,
                  model: str = "llama", merges: Optional[List[str]] = None, token_types: Optional[List[int]] = None,
-                 pre: str = "default", add_bos: Optional[bool] = None, chat_template: Optional[str] = None):
+                 pre: str = "default", add_bos: Optional[bool] = None, chat_template: Optional[str] = None,
+                 add_eos: Optional[bool] = None, unk: Optional[int] = None, lowercase: bool = True):
         self.tokens = tokens
         self.vocab_size = len(tokens)
         self.model = model
         self.scores = scores or [0.0] * len(tokens)
         self.bos, self.eos_token_id = bos, eos
         self.token_types = token_types or [_TT_NORMAL] * len(tokens)
-        self.add_bos = (model == "llama") if add_bos is None else bool(add_bos)
+        self.add_bos = (model in ("llama", "bert")) if add_bos is None else bool(add_bos)
+        self.add_eos = (model == "bert") if add_eos is None else bool(add_eos)
+        self.wordpiece = model == "bert"
+        self.lowercase = lowercase
         self.chat_template = chat_template
         self.index: Dict[str, int] = {}
         for i, t in enumerate(tokens):
@@ -193,6 +204,9 @@ class GGUFTokenizer:
             self._byte_enc = [enc[b] for b in range(256)]
         self._dec = _gpt2_byte_decoder()
         self._cache: Dict[str, List[int]] = {}
+        if self.wordpiece:
+            self.hash_form = any(t.startswith("##") and len(t) > 2 for t in tokens)
+            self.unk = unk if unk is not None else self.index.get("[UNK]", 0)
 
     @staticmethod
     def from_metadata(meta: dict) -> "GGUFTokenizer":
@@ -204,7 +218,9 @@ class GGUFTokenizer:
                              token_types=meta.get("tokenizer.ggml.token_type"),
                              pre=str(meta.get("tokenizer.ggml.pre", "default")),
                              add_bos=meta.get("tokenizer.ggml.add_bos_token"),
-                             chat_template=meta.get("tokenizer.chat_template"))
+                             chat_template=meta.get("tokenizer.chat_template"),
+                             add_eos=meta.get("tokenizer.ggml.add_eos_token"),
+                             unk=meta.get("tokenizer.ggml.unknown_token_id"))
 
     # -- encoding
     def encode(self, text: str, add_special: bool = True) -> List[int]:
@@ -223,11 +239,64 @@ class GGUFTokenizer:
         for chunk, is_special in parts:
             if is_special:
                 ids.append(self.special[chunk])
+            elif self.wordpiece:
+                ids += self._encode_wpm(chunk)
             elif self.byte_level:
                 ids += self._encode_bpe(chunk)
             else:
                 ids += self._encode_spm(chunk, first)
             first = False
+        if add_special and self.add_eos:
+            ids.append(self.eos_token_id)
+        return ids
+
+    @staticmethod
+    def _wpm_words(text: str, lowercase: bool) -> List[str]:
+        import unicodedata
+        out, cur = [], []
+
+        def flush():
+            if cur:
+                out.append("".join(cur))
+                cur.clear()
+        if lowercase:
+            text = "".join(c for c in unicodedata.normalize("NFD", text.lower()) if unicodedata.category(c) != "Mn")
+        for c in text:
+            o = ord(c)
+            cat = unicodedata.category(c)
+            if o == 0 or o == 0xFFFD or (cat.startswith("C") and c not in "\t\n\r"):
+                continue
+            if c.isspace():
+                flush()
+            elif (33 <= o <= 47 or 58 <= o <= 64 or 91 <= o <= 96 or 123 <= o <= 126 or cat.startswith("P")
+                  or 0x4E00 <= o <= 0x9FFF or 0x3400 <= o <= 0x4DBF or 0x20000 <= o <= 0x2A6DF
+                  or 0xF900 <= o <= 0xFAFF or 0x2F800 <= o <= 0x2FA1F):
+                flush()
+                out.append(c)
+            else:
+                cur.append(c)
+        flush()
+        return out
+
+    def _encode_wpm(self, text: str) -> List[int]:
+        ids: List[int] = []
+        for w in self._wpm_words(text, self.lowercase):
+            if len(w) > 100:
+                ids.append(self.unk)
+                continue
+            pieces, start = [], 0
+            while start < len(w):
+                for end in range(len(w), start, -1):
+                    sub = w[start:end]
+                    key = (("##" + sub) if start else sub) if self.hash_form else (sub if start else "▁" + sub)
+                    if key in self.index:
+                        pieces.append(self.index[key])
+                        break
+                else:
+                    pieces = [self.unk]
+                    break
+                start = end
+            ids += pieces
         return ids
 
     def _encode_bpe(self, text: str) -> List[int]:
@@ -335,6 +404,23 @@ class GGUFTokenizer:
 
     def decode(self, ids: List[int]) -> str:
         out = bytearray()
+        if self.wordpiece:
+            words: List[str] = []
+            for i in ids:
+                if not (0 <= i < len(self.tokens)) or self.token_types[i] == _TT_CONTROL:
+                    continue
+                t = self.tokens[i]
+                if self.hash_form:
+                    cont = t.startswith("##")
+                    t = t[2:] if cont else t
+                else:
+                    cont = not t.startswith("▁")
+                    t = t if cont else t[1:]
+                if cont and words:
+                    words[-1] += t
+                else:
+                    words.append(t)
+            return " ".join(words)
         if self.byte_level:
             for i in ids:
                 if 0 <= i < len(self.tokens) and self.token_types[i] != _TT_CONTROL:

@@ -115,3 +115,31 @@ def test_gguf_metadata_tokenizer_and_chat_template(tmp_path):
     assert tok.decode([1, 260]) == "hi"
     text = tok.apply_chat_template([{"role": "user", "content": "yo"}])
     assert text == "<|user|>yo<|end|><|assistant|>"  # the rendered BOS is left to encode()
+
+
+def test_wordpiece_matches_hf_bert_tokenizer():
+    """GGUF ``bert`` vocabularies (phantom-space form, as GGUF stores them) and the ``##`` form both
+    tokenize like HF tokenizers' BERT WordPiece (uncased), with [CLS] / [SEP] around the ids."""
+    from tokenizers import BertWordPieceTokenizer
+    from gollek_b200.utils.tokenizer import GGUFTokenizer
+    words = ["the", "run", "##ning", "##s", "un", "##believ", "##able", "thing", "hello", "world", "na", "##ive",
+             "cafe", "token", "##izer", "a", "b", "c", "x", "##x", "test", "##ed", "中", "文", "don", "'", "t"]
+    punct = list(",.!?-()'\"") + [";", ":"]
+    vocab = ["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]"] + words + [p for p in punct if p not in words]
+    hf = BertWordPieceTokenizer({t: i for i, t in enumerate(vocab)}, lowercase=True)
+    phantom = [t if (t.startswith("[") and t.endswith("]")) else (t[2:] if t.startswith("##") else "▁" + t)
+               for t in vocab]
+    types = [3 if (t.startswith("[") and t.endswith("]")) else 1 for t in vocab]
+    texts = ["Hello, world!", "The running things... Unbelievable!", "naïve Café; TESTED tokenizers",
+             "don't stop", "中文 mixed\twith\ncontrol\x07 chars", "zzz qqq", "x" * 150, "xxxx", "(a) [MASK] b",
+             "  leading and trailing  ", ""]
+    for form in (phantom, vocab):
+        tok = GGUFTokenizer(form, None, bos=2, eos=3, model="bert", token_types=types)
+        for text in texts:
+            assert tok.encode(text) == hf.encode(text).ids, (form is phantom, text)
+        assert tok.decode(tok.encode("the running things")) == "the running things"
+    meta = {"tokenizer.ggml.model": "bert", "tokenizer.ggml.tokens": phantom, "tokenizer.ggml.token_type": types,
+            "tokenizer.ggml.bos_token_id": 2, "tokenizer.ggml.eos_token_id": 3, "tokenizer.ggml.unknown_token_id": 1}
+    t2 = GGUFTokenizer.from_metadata(meta)
+    assert t2.encode("Hello, world!") == hf.encode("Hello, world!").ids
+    assert t2.encode("hello", add_special=False) == [vocab.index("hello")]
