@@ -123,7 +123,9 @@ class GollekClient:
         body = {"model": req.model, "messages": [{"role": "user", "content": req.prompt}],
                 "parameters": req.parameters()}
         j = self._post("/v1/inference/completions", body).json()
-        return GenerationResponse(j["content"], j["model"], Usage(0, j.get("tokensUsed", 0)),
+        usage = (Usage(j["promptTokens"], j["completionTokens"]) if "completionTokens" in j
+                 else Usage(0, j.get("tokensUsed", 0)))  # servers that report only the total
+        return GenerationResponse(j["content"], j["model"], usage,
                                   j.get("finishReason"), j["requestId"])
 
     def complete(self, prompt: str, **kw) -> dict:
@@ -159,6 +161,55 @@ class GollekClient:
     def list_models(self) -> List[str]:
         r = self.http.get(self.base + "/v1/models", timeout=self.timeout)
         return [m["id"] for m in r.json()["data"]]
+
+    def _get(self, path: str, **params):
+        r = self.http.get(self.base + path, params=params or None, timeout=self.timeout)
+        if r.status_code >= 400:
+            raise RuntimeError(f"{path}: HTTP {r.status_code}: {r.text[:500]}")
+        return r.json()
+
+    def submit(self, req: GenerationRequest) -> str:
+        """Queue ``req`` as an asynchronous job; returns its job id."""
+        body = {"model": req.model, "messages": [{"role": "user", "content": req.prompt}],
+                "parameters": req.parameters()}
+        return self._post("/v1/infer/async", body).json()["jobId"]
+
+    def job(self, job_id: str) -> dict:
+        """{jobId, status (PENDING / RUNNING / COMPLETED / FAILED), result, error}."""
+        return self._get(f"/v1/infer/async/{job_id}")
+
+    def wait(self, job_id: str, timeout: float = 600.0, poll: float = 0.05) -> dict:
+        import time
+        t_end = time.monotonic() + timeout
+        while True:
+            j = self.job(job_id)
+            if j["status"] in ("COMPLETED", "FAILED") or time.monotonic() > t_end:
+                return j
+            time.sleep(poll)
+
+    def speech(self, text: str, voice: str = "default", response_format: str = "wav") -> bytes:
+        """Text to speech (WAV bytes, or raw 16-bit PCM with ``response_format="pcm"``)."""
+        return self._post("/v1/audio/speech", {"input": text, "voice": voice,
+                                               "response_format": response_format}).content
+
+    def transcribe(self, audio: bytes, filename: str = "audio.wav", translate: bool = False, **fields) -> dict:
+        """Speech recognition of an audio file's bytes (``translate`` for English translation)."""
+        path = "/v1/audio/translations" if translate else "/v1/audio/transcriptions"
+        r = self.http.post(self.base + path, files={"file": (filename, audio)},
+                           data={k: str(v) for k, v in fields.items()}, timeout=self.timeout)
+        if r.status_code >= 400:
+            raise RuntimeError(f"{path}: HTTP {r.status_code}: {r.text[:500]}")
+        return r.json()
+
+    def providers(self) -> List[dict]:
+        return self._get("/v1/admin/providers")["providers"]
+
+    def add_provider(self, pid: str, base_url: str, api_key: str = "", models: Optional[List[str]] = None) -> dict:
+        """Register an OpenAI-compatible upstream that serves models this server does not."""
+        body = {"id": pid, "base_url": base_url, "api_key": api_key}
+        if models:
+            body["models"] = models
+        return self._post("/v1/admin/providers", body).json()
 
     def health(self) -> bool:
         try:

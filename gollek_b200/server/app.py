@@ -6,7 +6,8 @@ OpenAI surface (runner/safetensor/gollek-safetensor-api/…/OpenAiCompatibleReso
   POST /v1/embeddings. Defaults as the reference: temperature 0.7, top_p 0.95, top_k 50,
   max_tokens 2048 (capped by the model length).
 gollek surface (inference/gollek-api-rest/…/api/rest/InferenceResource.java:46-266):
-  POST /v1/infer/completions → {requestId, content, model, tokensUsed, durationMs, timestamp}
+  POST /v1/infer/completions → {requestId, content, model, tokensUsed, promptTokens, completionTokens,
+  durationMs, timestamp}
   POST /v1/infer/async → {jobId}; GET /v1/infer/async/{jobId}; POST /v1/infer/stream (SSE of
   {index, content, isFinal}); POST /v1/infer/batch; POST /v1/infer/embeddings;
   DELETE /v1/infer/{requestId}. The same routes are served under /v1/inference/* (the path the
@@ -902,6 +903,7 @@ def create_app(aengine: AsyncEngine, model_name: str = "gollek-b200", api_keys: 
         o = await run_full(infer_prompt(req), sp, rid, lora, req.priority, timeout=req.timeout / 1000 if req.timeout else None)
         return {"requestId": rid, "content": o.text or detok(o.output_token_ids), "model": req.model or st.model_name,
                 "tokensUsed": len(o.prompt_token_ids) + len(o.output_token_ids),
+                "promptTokens": len(o.prompt_token_ids), "completionTokens": len(o.output_token_ids),
                 "durationMs": int((time.perf_counter() - t0) * 1e3),
                 "timestamp": datetime.now(timezone.utc).isoformat(), "finishReason": o.finish_reason}
 
