@@ -25,7 +25,7 @@ Codes are packed two per byte, element 2i in the low nibble. Checkpoint tensors 
   ``<name>.weight_scales`` uint8 [N, K / 32] (e8m0).
 
 Loading dequantizes to bf16; the block-scaled FP4 tensor-core GEMM (``tcgen05.mma`` kind::mxf4nvf4)
-is not built, so FP4 checkpoints serve through the bf16 (or, re-quantized at load, the fp8) GEMMs.
+is not built, so FP4 checkpoints serve through the bf16 GEMMs.
 """
 from __future__ import annotations
 
