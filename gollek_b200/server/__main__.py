@@ -31,6 +31,8 @@ def main(argv=None):
     ap.add_argument("--asr-model", default=None, help="Whisper checkpoint directory for /v1/audio/*")
     ap.add_argument("--tts-model", default=None, help="SpeechT5 text-to-speech directory for /v1/audio/speech")
     ap.add_argument("--tts-vocoder", default=None, help="HiFi-GAN vocoder directory for /v1/audio/speech")
+    ap.add_argument("--provider", action="append", default=[], metavar="ID=URL[,KEY]",
+                    help="OpenAI-compatible upstream serving models this server does not (repeatable)")
     args = ap.parse_args(argv)
     import uvicorn
     from ..config import EngineConfig
@@ -59,7 +61,8 @@ def main(argv=None):
         return _serve_tp(args, cfg, keys)
     ae = AsyncEngine(LLMEngine(cfg)).start()
     app = create_app(ae, model_name=args.served_model_name or os.path.basename(args.model.rstrip("/")),
-                     api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg))
+                     api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg),
+                     providers=parse_providers(args.provider))
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     finally:
@@ -74,6 +77,19 @@ def _asr(args, cfg):
     from ..models.whisper import WhisperASR
     dev = str(cfg.device)
     return WhisperASR(args.asr_model, device=dev, dtype=torch.float32 if dev == "cpu" else torch.bfloat16)
+
+
+def parse_providers(specs):
+    """``ID=URL[,KEY]`` strings -> a registry of OpenAI-compatible upstreams."""
+    from .providers import OpenAIHTTPProvider, ProviderRegistry
+    reg = ProviderRegistry()
+    for spec in specs or []:
+        pid, eq, rest = spec.partition("=")
+        if not eq or not pid or not rest:
+            raise SystemExit(f"--provider {spec!r}: expected ID=URL[,KEY]")
+        url, _, key = rest.partition(",")
+        reg.register(OpenAIHTTPProvider(pid, url, key))
+    return reg
 
 
 def _tts(args, cfg):
@@ -118,7 +134,8 @@ def _serve_tp(args, cfg, keys):
         drv = DriverEngine(engine, cp)
         ae = AsyncEngine(drv).start()
         app = create_app(ae, model_name=args.served_model_name or os.path.basename(str(args.model).rstrip("/")),
-                         api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg))
+                         api_keys=keys, rate=args.rate_limit, asr=_asr(args, cfg), tts=_tts(args, cfg),
+                         providers=parse_providers(args.provider))
         try:
             uvicorn.run(app, host=args.host, port=args.port, log_level="info")
         finally:

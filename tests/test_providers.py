@@ -164,3 +164,12 @@ def test_forwarding_streaming_and_failover(client):
             except Exception:
                 pass
         client.delete("/v1/admin/providers/p2")
+
+
+def test_server_provider_flag():
+    from gollek_b200.server.__main__ import parse_providers
+    reg = parse_providers(["a=http://h:1/v1,sk-1", "b=http://h:2/v1"])
+    a, b = reg.get("a"), reg.get("b")
+    assert (a.base, a.key, b.base, b.key) == ("http://h:1/v1", "sk-1", "http://h:2/v1", "")
+    with pytest.raises(SystemExit):
+        parse_providers(["nourl"])
